@@ -1,0 +1,290 @@
+"""Benchmark: int4-g32-a16 GPT-2 124M batch-1 greedy decode (config 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+A step is one whole config-0 generation: prompt [50256], then 100 greedy
+tokens (100 model forwards, each one decode step of the int4-g32-a16
+layers, the int8 per-channel head with its argmax, and the int8 KV cache).
+Weights are random-init (N(0, 0.02), seed 0); no checkpoint is read.
+
+value: generated tokens / device time of the K timed steps (CUDA events on
+the library's stream, L2 flushed by a 256 MiB write between steps, prompt
+and ids resident in HBM). e2e: the same through llmq_generate with host
+prompt and host ids (the copies inside the timed region). roofline: the
+dominant kernel (the fused int8 head GEMV + argmax), timed live with CUDA
+events on its stream, against the measured HBM copy bandwidth.
+cpu_baseline: the CPU oracle (a C restatement of the reference's path) on a
+bounded sample. With N GPUs (torchrun), each rank decodes its own sequence
+(replicas of the batch-1 decode, which does not shard), and value is the
+sum over ranks with the max device time over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+STEPS_PER_GEN = 100
+PROMPT = [50256]
+HEAD_BYTES = 50257 * 768 + 50257 * 3          # int8-ch head: codes + f16 scale + u8 zp per row
+LAYER_BYTES = 12 * (2304 + 768 + 3072 + 768) * 768 * 19 // 32  # int4-g32: 0.59375 B/weight
+TOKEN_BYTES = LAYER_BYTES + HEAD_BYTES         # 89,178,099 per token
+METRIC = "int4-g32-a16 decode tok/s (b=1)"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def cpu_baseline(seconds: float = 20.0):
+    """The CPU oracle's greedy decode of config 0, sampled for about
+    `seconds`: tokens per second over the tokens it finished."""
+    from llm_mojo_b200 import synth
+    from oracle import oracle as O
+
+    t = synth.gpt2_random_init(0)
+    m = O.Model(t)
+    logits = m.forward(PROMPT, 0)
+    n, pos, t0 = 1, 1, time.perf_counter()
+    while time.perf_counter() - t0 < seconds and n < STEPS_PER_GEN:
+        nxt = int(O.lib().oq_argmax(O.ptr(logits), m.V))
+        logits = m.forward([nxt], pos)
+        pos += 1
+        n += 1
+    dt = time.perf_counter() - t0
+    m.close()
+    return {"value": (n - 1) / dt, "unit": "tok/s", "cores": 1, "kind": "port",
+            "sample": f"{n - 1} decode steps of config 0 (after the prompt forward), single thread"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    steps = []
+    for i in range(args.warmup + args.steps):
+        b = cpu_baseline(args.cpu_seconds)
+        if i >= args.warmup:
+            steps.append(b["value"])
+    v = statistics.median(steps)
+    b["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * STEPS_PER_GEN / v,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int16xint4->int32",
+            "data": "synthetic", "config": config_dict(args),
+            "cpu_baseline": b, "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+def config_dict(args):
+    return {"workload": "config 0: GPT-2 124M batch-1 greedy decode, int4-g32-a16 layers + int8-ch head + "
+                        "int8 KV, prompt [50256] then 100 tokens, random-init weights (seed 0)",
+            "global_batch": args.gpus, "seq_len": 101, "parallelism": f"replicas{args.gpus}",
+            "l2": "flushed between steps (256 MiB write)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+
+    from llm_mojo_b200 import build, synth
+    from llm_mojo_b200._lib import check, lib
+    from llm_mojo_b200.model import Model
+    from llm_mojo_b200.tensor import Context
+
+    build.build()
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    model = Model(ctx, synth.gpt2_random_init(0))
+    prompt_dev = torch.tensor(PROMPT, dtype=torch.int32, device="cuda")
+    ids_dev = torch.zeros(STEPS_PER_GEN, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    import ctypes as C
+
+    def gen_async():
+        check(lib().llmq_generate_async(ctx.h, model.h, C.c_void_p(prompt_dev.data_ptr()), len(PROMPT),
+                                        STEPS_PER_GEN, C.c_void_p(ids_dev.data_ptr())), ctx.h)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            gen_async()
+            flush.zero_()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        with Clocks(local) as clk:
+            for s, e in evs:
+                s.record(stream)
+                gen_async()
+                e.record(stream)
+                flush.zero_()
+            stream.synchronize()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        step_ms = [s.elapsed_time(e) for s, e in evs]
+        total_ms = sum(step_ms)
+        ids = ids_dev.cpu().numpy().copy()
+
+        # e2e: the public host-buffer call, copies inside the timed region.
+        e2e_ms = []
+        for _ in range(max(3, args.steps // 2)):
+            flush.zero_()
+            stream.synchronize()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            out = model.generate(PROMPT, STEPS_PER_GEN)
+            e0.record(stream)
+            stream.synchronize()
+            e2e_ms.append(s0.elapsed_time(e0))
+        assert list(out) == list(ids)
+
+        # roofline: the head GEMV + argmax (largest single launch) timed alone.
+        h = torch.randn(768, device="cuda")
+        am = torch.zeros(1, dtype=torch.int32, device="cuda")
+        hs = []
+        for i in range(args.warmup + 20):
+            flush.zero_()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            check(lib().llmq_head_argmax(ctx.h, model.head.h, C.c_void_p(h.data_ptr()), None,
+                                         C.c_void_p(am.data_ptr())), ctx.h)
+            e0.record(stream)
+            if i >= args.warmup:
+                hs.append((s0, e0))
+        stream.synchronize()
+        head_ms = statistics.mean(s.elapsed_time(e) for s, e in hs)
+
+    t_max = total_ms
+    e2e_avg = statistics.mean(e2e_ms)
+    if world > 1:
+        tt = torch.tensor([total_ms, e2e_avg], device="cuda", dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_max, e2e_avg = float(tt[0]), float(tt[1])
+        all_ids = [torch.zeros(STEPS_PER_GEN, dtype=torch.int32, device="cuda") for _ in range(world)]
+        dist.all_gather(all_ids, ids_dev)
+    tokens = world * args.steps * STEPS_PER_GEN
+    value = tokens / (t_max / 1000.0)
+    peak, peak_kind = peaks()
+    achieved = HEAD_BYTES / (head_ms / 1000.0) / 1e9
+    if rank == 0:
+        cpu = None if args.no_cpu_baseline else cpu_baseline(args.cpu_seconds)
+        launches_per_token = model.n_layer * 5 + 2
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": t_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16xint4->int32", "data": "synthetic", "config": config_dict(args),
+            "e2e": {"value": world * STEPS_PER_GEN / (e2e_avg / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * len(PROMPT), "d2h_bytes_per_step": 4 * STEPS_PER_GEN},
+            "roofline": {"bound": "hbm", "kernel": "gemv_a16_kernel<GEN8, PRO_LN, argmax> (int8-ch head 50257x768)",
+                         "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None,
+                         "algorithmic_bytes_per_launch": HEAD_BYTES, "avg_launch_ms": head_ms},
+            "weight_bytes_per_token": TOKEN_BYTES,
+            "effective_weight_gbs": TOKEN_BYTES * STEPS_PER_GEN * args.steps / (total_ms / 1000.0) / 1e9,
+            "gpu_launches": args.steps * (1 + STEPS_PER_GEN * launches_per_token),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "ids_head": [int(i) for i in ids[:8]],
+        }
+        print(json.dumps(line))
+    model.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

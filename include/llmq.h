@@ -1,0 +1,157 @@
+/*
+ * llmq.h -- C ABI of the B200 (sm_100a) quantized-matmul hot path of
+ * llm_mojo (GPT-2 124M inference with pluggable weight formats).
+ *
+ * Plain pointers and sizes only. "dev" pointers are CUDA device memory of
+ * the context's device; "host" pointers are borrowed for the duration of the
+ * call. Every function returns an llmq_status; llmq_last_error() gives the
+ * message of the last failure on a context. Handles are owned by the caller
+ * and released with the matching *_free. One context serves one host thread
+ * and one device; its calls are issued on the context's stream.
+ */
+#ifndef LLMQ_H
+#define LLMQ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int llmq_status;
+#define LLMQ_OK 0
+#define LLMQ_ERR_INVALID 1     /* bad argument or shape (the reference raises or aborts) */
+#define LLMQ_ERR_CUDA 2        /* a CUDA call failed */
+#define LLMQ_ERR_NOMEM 3       /* device or host allocation failed */
+#define LLMQ_ERR_TIMEOUT 4     /* a bounded device-side wait gave up */
+#define LLMQ_ERR_UNSUPPORTED 5 /* format or path not available */
+
+typedef struct llmq_ctx llmq_ctx;
+typedef struct llmq_weight llmq_weight;
+typedef struct llmq_kv llmq_kv;
+typedef struct llmq_model llmq_model;
+
+/* linear() epilogue flags: kernels.mojo:38-48 store_out[RESID, GELU], BIAS. */
+#define LLMQ_BIAS 1
+#define LLMQ_GELU 2
+#define LLMQ_RESID 4
+
+/* KV cache kinds: kvcache.mojo QuantKV[8] (float attention) and
+ * int_attention.mojo IntAttnKV (integer attention). */
+#define LLMQ_KV_QUANT8 1
+#define LLMQ_KV_INTATTN 2
+
+/* ---- context ------------------------------------------------------------ */
+/* No reference counterpart (the reference runs in-process on the CPU). */
+llmq_status llmq_init(int device, llmq_ctx **out);
+llmq_status llmq_destroy(llmq_ctx *ctx);
+const char *llmq_last_error(const llmq_ctx *ctx);
+/* Issue the context's work on `cuda_stream` (a cudaStream_t); NULL restores
+ * the context's own stream. */
+llmq_status llmq_set_stream(llmq_ctx *ctx, void *cuda_stream);
+llmq_status llmq_sync(llmq_ctx *ctx);
+
+/* ---- weight formats ------------------------------------------------------ */
+/* Replaces QuantMatrix.from_f32 (tensor.mojo:333-383): the reference's RTN
+ * affine quantizer, on the host. src is [rows, cols] row-major float32;
+ * reduce_rows=1 stores the transpose (layer matrices, [IN, OUT] -> [OUT, IN]),
+ * 0 stores src as is (wte, [V, C]). group 0 = per channel. a16 with bits 4
+ * and group 32 selects the BLOCKED decode layout (tensor.mojo:277-288,
+ * nibble_at :385-404). codes: n*k*bits/8 bytes, scale (float16 bits) and zp:
+ * n*(k/group) each, n = reduce_rows ? cols : rows, k the other. */
+llmq_status llmq_quantize_affine(const float *src_host, int rows, int cols, int reduce_rows, int bits, int group,
+                                 int sym, int a16, uint8_t *codes_host, uint16_t *scale_host, uint8_t *zp_host);
+
+/* Uploads a QuantMatrix[bits, group, sym, a16] in its stored layout
+ * (tensor.mojo:302-307: codes, float16 scale, u8 zero point per group), as
+ * restore (tensor.mojo:645-656) takes it. rows = outputs, cols = the
+ * reduction axis; group 0 = per channel. */
+llmq_status llmq_weight_create_affine(llmq_ctx *ctx, int bits, int group, int sym, int a16, int rows, int cols,
+                                      const uint8_t *codes_host, const uint16_t *scale_host,
+                                      const uint8_t *zp_host, llmq_weight **out);
+/* WeightMatrix.free (tensor.mojo:658-661). */
+llmq_status llmq_weight_free(llmq_weight *w);
+/* WeightMatrix.nbytes (tensor.mojo:629-632): codes + 3 bytes per group. */
+long long llmq_weight_nbytes(const llmq_weight *w);
+
+/* ---- kernels (device pointers) ------------------------------------------ */
+/* Replaces kernels.linear (kernels.mojo:655-673) for ACT16 formats, i.e.
+ * matmul_rows_a16 (:419-509): out[T, OUT] (+)= act(x[T, IN] @ w^T + b).
+ * T == 1 is the decode path (dot_row_i16 via linear_team, :774-816), T > 1
+ * the tile path (tile_i16, :512-573; rows_i16 for OUT % 32). */
+llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x_dev, const float *bias_dev,
+                        float *out_dev, int T, int IN, int OUT, int flags);
+/* Replaces head (kernels.mojo:676-690) + argmax (gpt2t.mojo:792-797) for one
+ * token: logits[V] = h[C] @ w^T (logits_dev may be NULL) and the first index
+ * of the largest logit into *argmax_dev. */
+llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev,
+                             int *argmax_dev);
+/* Replaces layernorm (kernels.mojo:179-197), eps 1e-5. */
+llmq_status llmq_layernorm(llmq_ctx *ctx, float *out_dev, const float *x_dev, const float *w_dev,
+                           const float *b_dev, int T, int C);
+/* Replaces quantize_rows (kernels.mojo:400-416). */
+llmq_status llmq_quantize_rows(llmq_ctx *ctx, const float *x_dev, int T, int IN, int16_t *xq_dev, float *sx_dev);
+/* The int32 lane sums of dot_row_i16 (tensor.mojo:518-577) for input x[IN]
+ * after quantize_rows: lanes_dev[OUT][units][16], units = IN/256 for the
+ * BLOCKED layout (sums of x*u before the zero point), else IN/group (sums of
+ * x*(u - zp)). For bit-exact parity checks of the integer accumulators. */
+llmq_status llmq_debug_lane_sums(llmq_ctx *ctx, const llmq_weight *w, const float *x_dev, int32_t *lanes_dev);
+
+/* ---- KV cache (kvcache.mojo:31-87 KVCache) ------------------------------ */
+/* KVCache.create. kind LLMQ_KV_QUANT8 or LLMQ_KV_INTATTN. */
+llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int n_head, int head_dim,
+                           llmq_kv **out);
+llmq_status llmq_kv_free(llmq_kv *kv);
+/* KVCache.store for T tokens: the key and value of qkv row t ([T, 3C],
+ * columns C.. and 2C..) at position pos0 + t of `layer`. */
+llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T, const float *qkv_dev);
+/* KVCache.attend (kvcache.mojo:62-79): out[T, C] for T tokens at pos0.. */
+llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out_dev, const float *qkv_dev, int layer, int T,
+                           int pos0);
+/* Copies the cache's storage to the host (codes and scales as the format
+ * lays them out; QuantKV[8]: k, v int8 [L][max_t][H][hd], ks, vs float
+ * [L][max_t][H]). Any pointer may be NULL. For tests. */
+llmq_status llmq_kv_read(llmq_ctx *ctx, const llmq_kv *kv, void *k_host, void *v_host, void *ks_host,
+                         void *vs_host);
+
+/* ---- model (gpt2t.mojo:198-572 Model) ------------------------------------ */
+/* Model[W, E, KV] from 4*n_layer layer matrices (per layer: attn.c_attn,
+ * attn.c_proj, mlp.c_fc, mlp.c_proj, gpt2t.mojo:84-96), the tied wte/head
+ * matrix and the float32 parameters in Model.small order (per layer
+ * ln_1.w, ln_1.b, c_attn.b, c_proj.b, ln_2.w, ln_2.b, c_fc.b, mlp.c_proj.b,
+ * then wpe [1024][768], ln_f.w, ln_f.b; gpt2t.mojo:255-267). The matrices
+ * stay owned by the caller and must outlive the model. */
+llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *mats, const llmq_weight *head,
+                              const float *small_host, int kv_kind, int max_t, llmq_model **out);
+llmq_status llmq_model_free(llmq_model *m);
+/* Model.forward (gpt2t.mojo:329-342): tokens at positions pos0.., logits of
+ * the last token into logits_dev (may be NULL) and its argmax into
+ * *argmax_host (may be NULL). */
+llmq_status llmq_model_forward(llmq_ctx *ctx, llmq_model *m, const int *tokens_host, int T, int pos0,
+                               float *logits_dev, int *argmax_host);
+/* Model.forward_all (gpt2t.mojo:449-459): logits_dev[T, V] for every
+ * position of tokens (from position 0). */
+llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *tokens_host, int T,
+                                   float *logits_dev);
+/* Greedy generate (gpt2t.mojo:942-980, without the stop at EOT): forward
+ * the prompt, then `steps` argmaxes with a decode step between consecutive
+ * ones; ids into out_ids_host[steps]. Each decode step is one CUDA graph
+ * launch. */
+llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, int n_prompt, int steps,
+                          int *out_ids_host);
+/* generate with device-resident prompt and ids, asynchronous on the
+ * context's stream (no host synchronisation): the same steps as
+ * llmq_generate. */
+llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
+                                int *ids_dev);
+/* The cudaStream_t the context issues its work on. */
+void *llmq_stream(const llmq_ctx *ctx);
+/* 1 (default) replays each decode step as a captured CUDA graph; 0 launches
+ * its kernels one by one. */
+llmq_status llmq_model_use_graph(llmq_model *m, int enable);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLMQ_H */

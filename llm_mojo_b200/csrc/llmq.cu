@@ -1,0 +1,809 @@
+// C ABI of the B200 quantized-matmul hot path (include/llmq.h).
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/llmq.h"
+#include "attention.cuh"
+#include "gemv_a16.cuh"
+#include "prefill_a16.cuh"
+
+using namespace llmq;
+
+struct llmq_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  // scratch owned by the context (grown on demand)
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  DecodeState *state = nullptr;  // device, for llmq_head_argmax
+};
+
+struct llmq_weight {
+  llmq_ctx *ctx;
+  int bits, group, sym, a16, blocked;
+  int rows, cols;
+  uint8_t *codes;
+  uint16_t *scale;
+  uint8_t *zp;
+  long long nbytes;
+  WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
+};
+
+struct llmq_kv {
+  llmq_ctx *ctx;
+  int kind;
+  KV8View v8;
+};
+
+struct llmq_model {
+  llmq_ctx *ctx;
+  int n_layer, C, V, max_t, n_head;
+  std::vector<const llmq_weight *> mats;
+  const llmq_weight *head;
+  llmq_kv *kv;
+  float *small;  // device copy of the float32 parameters
+  float *x, *xn, *qkv, *att, *fc, *logits;
+  int *tokens;
+  int *ids;
+  int max_ids;
+  float *part_val;
+  int *part_idx;
+  DecodeState *state;
+  DecodeState *state_host;  // pinned staging
+  int *ids_host;            // pinned staging
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int use_graph = 1;
+  const float *vec(int l, int which) const {
+    static const int mult[8] = {0, 1, 2, 5, 6, 7, 8, 12};
+    return small + (size_t)l * 13 * C + (size_t)mult[which] * C;
+  }
+  const float *wpe() const { return small + (size_t)n_layer * 13 * C; }
+  const float *lnf_w() const { return wpe() + (size_t)1024 * C; }
+  const float *lnf_b() const { return lnf_w() + C; }
+};
+
+namespace {
+
+llmq_status fail(llmq_ctx *ctx, llmq_status st, const std::string &msg) {
+  if (ctx) ctx->err = msg;
+  return st;
+}
+
+#define CK(call)                                                                                 \
+  do {                                                                                           \
+    cudaError_t e_ = (call);                                                                     \
+    if (e_ != cudaSuccess)                                                                       \
+      return fail(ctx, LLMQ_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));     \
+  } while (0)
+
+#define CKL()                                                                                    \
+  do {                                                                                           \
+    cudaError_t e_ = cudaGetLastError();                                                         \
+    if (e_ != cudaSuccess) return fail(ctx, LLMQ_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+constexpr int kR = 16, kP = 3;
+constexpr int kThreads = kR * kP * 4;
+
+template <int FMT>
+int smem_bytes(const WeightView &w) {
+  SmemPlan<FMT> pl(w.cols, w.group, kR);
+  return pl.total;
+}
+
+constexpr int kMaxSmem = 200 * 1024;
+
+template <int FMT, int PRO, bool ARG>
+cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s) {
+  gemv_a16_kernel<FMT, PRO, kR, kP, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
+  return cudaGetLastError();
+}
+
+template <int FMT>
+cudaError_t configure_fmt() {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](const void *k) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  };
+  set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR, kP, true>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR, kP, false>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, true>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, false>);
+  return e;
+}
+
+int fmt_of(const WeightView &w) { return w.blocked ? FMT_BLK4 : (w.bits == 4 ? FMT_GEN4 : FMT_GEN8); }
+
+int gemv_grid(const llmq_ctx *ctx, const WeightView &w) {
+  int tiles = (w.rows + kR - 1) / kR;
+  int cap = ctx->num_sms * 8;
+  return tiles < cap ? tiles : cap;
+}
+
+cudaError_t launch_gemv(const llmq_ctx *ctx, const GemvArgs &a, int pro, bool argmax, cudaStream_t s) {
+  int grid = gemv_grid(ctx, a.w);
+  int fmt = fmt_of(a.w);
+#define DISPATCH(F)                                                             \
+  if (fmt == F) {                                                               \
+    if (pro == PRO_LN)                                                          \
+      return argmax ? launch_gemv_t<F, PRO_LN, true>(a, grid, s) : launch_gemv_t<F, PRO_LN, false>(a, grid, s); \
+    return argmax ? launch_gemv_t<F, PRO_QUANT, true>(a, grid, s) : launch_gemv_t<F, PRO_QUANT, false>(a, grid, s); \
+  }
+  DISPATCH(FMT_BLK4)
+  DISPATCH(FMT_GEN4)
+  DISPATCH(FMT_GEN8)
+#undef DISPATCH
+  return cudaErrorInvalidValue;
+}
+
+bool smem_ok(const WeightView &w) {
+  int fmt = fmt_of(w);
+  int b = fmt == FMT_BLK4 ? smem_bytes<FMT_BLK4>(w) : (fmt == FMT_GEN4 ? smem_bytes<FMT_GEN4>(w) : smem_bytes<FMT_GEN8>(w));
+  return b <= kMaxSmem;
+}
+
+llmq_status ensure_scratch(llmq_ctx *ctx, size_t bytes) {
+  if (ctx->scratch_bytes >= bytes) return LLMQ_OK;
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  ctx->scratch = nullptr;
+  ctx->scratch_bytes = 0;
+  CK(cudaMalloc(&ctx->scratch, bytes));
+  ctx->scratch_bytes = bytes;
+  return LLMQ_OK;
+}
+
+}  // namespace
+
+template <int FMT>
+__global__ void __launch_bounds__(kThreads) lane_sums_kernel(GemvArgs a, int32_t *lanes_out);
+
+namespace {
+// Raises the dynamic shared-memory limit of every kernel once, outside any
+// stream capture.
+cudaError_t configure_kernels() {
+  cudaError_t e = configure_fmt<FMT_BLK4>();
+  if (e == cudaSuccess) e = configure_fmt<FMT_GEN4>();
+  if (e == cudaSuccess) e = configure_fmt<FMT_GEN8>();
+  if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_BLK4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  return e;
+}
+}  // namespace
+
+// Debug: lane sums of one row range. Runs the PRO_QUANT prologue and the
+// integer phase, then copies the lane sums (zero point applied for the
+// grouped layouts) to lanes_out[rows][units][16].
+template <int FMT>
+__global__ void __launch_bounds__(kThreads) lane_sums_kernel(GemvArgs a, int32_t *lanes_out) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  SmemPlan<FMT> pl(a.w.cols, a.w.group, kR);
+  prologue<FMT, PRO_QUANT>(a, smem, pl);
+  const int units = FMT == FMT_BLK4 ? a.w.cols >> 8 : a.w.cols / a.w.group;
+  int *lanes_all = (int *)(smem + pl.lanes);
+  const int *xp32 = (const int *)(smem + pl.xq);
+  const int *xsum = (const int *)(smem + pl.xs);
+  const int t = threadIdx.x, q = t & 3, p = (t >> 2) % kP, r = (t >> 2) / kP;
+  for (int row0 = blockIdx.x * kR; row0 < a.w.rows; row0 += gridDim.x * kR) {
+    for (int i = t; i < kR * units * 16; i += blockDim.x) lanes_all[i] = 0;
+    __syncthreads();
+    const int row = row0 + r;
+    if (row < a.w.rows) int_phase<FMT, kP>(a.w, row, q, p, xp32, lanes_all + r * units * 16);
+    __syncthreads();
+    for (int i = t; i < kR * units * 16; i += blockDim.x) {
+      int rr = row0 + i / (units * 16), u = (i / 16) % units, L = i % 16;
+      if (rr >= a.w.rows) continue;
+      int v = lanes_all[i];
+      if (FMT != FMT_BLK4) {
+        int zp = a.w.zp[(size_t)rr * units + u];
+        v = (int)((unsigned)v - (unsigned)(zp * xsum[u * 16 + L]));
+      }
+      lanes_out[(size_t)rr * units * 16 + u * 16 + L] = v;
+    }
+    __syncthreads();
+  }
+}
+
+extern "C" {
+
+llmq_status llmq_init(int device, llmq_ctx **out) {
+  if (!out) return LLMQ_ERR_INVALID;
+  *out = nullptr;
+  llmq_ctx *ctx = new llmq_ctx();
+  ctx->device = device;
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->state, sizeof(DecodeState));
+  if (e == cudaSuccess) e = cudaMemset(ctx->state, 0, sizeof(DecodeState));
+  if (e == cudaSuccess) e = configure_kernels();
+  if (e != cudaSuccess) {
+    delete ctx;
+    return LLMQ_ERR_CUDA;
+  }
+  ctx->stream = ctx->own;
+  *out = ctx;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_destroy(llmq_ctx *ctx) {
+  if (!ctx) return LLMQ_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  if (ctx->own) cudaStreamSynchronize(ctx->own);
+  if (ctx->scratch) cudaFree(ctx->scratch);
+  if (ctx->state) cudaFree(ctx->state);
+  if (ctx->own) cudaStreamDestroy(ctx->own);
+  delete ctx;
+  return LLMQ_OK;
+}
+
+const char *llmq_last_error(const llmq_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+llmq_status llmq_set_stream(llmq_ctx *ctx, void *s) {
+  if (!ctx) return LLMQ_ERR_INVALID;
+  ctx->stream = s ? (cudaStream_t)s : ctx->own;
+  return LLMQ_OK;
+}
+
+void *llmq_stream(const llmq_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+
+llmq_status llmq_sync(llmq_ctx *ctx) {
+  if (!ctx) return LLMQ_ERR_INVALID;
+  CK(cudaStreamSynchronize(ctx->stream));
+  return LLMQ_OK;
+}
+
+llmq_status llmq_weight_create_affine(llmq_ctx *ctx, int bits, int group, int sym, int a16, int rows, int cols,
+                                      const uint8_t *codes, const uint16_t *scale, const uint8_t *zp,
+                                      llmq_weight **out) {
+  if (!ctx || !out || !codes || !scale || !zp) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  *out = nullptr;
+  int g = group == 0 ? cols : group;
+  if ((bits != 4 && bits != 8) || rows <= 0 || cols <= 0 || group < 0 || cols % g != 0 || g % 32 != 0)
+    return fail(ctx, LLMQ_ERR_INVALID, "group size must divide the reduction axis and be a multiple of 32");
+  int blocked = a16 && bits == 4 && group == 32;
+  if (blocked && cols % 256 != 0) return fail(ctx, LLMQ_ERR_INVALID, "the BLOCKED layout needs cols % 256 == 0");
+  CK(cudaSetDevice(ctx->device));
+  llmq_weight *w = new llmq_weight();
+  w->ctx = ctx;
+  w->bits = bits;
+  w->group = g;
+  w->sym = sym;
+  w->a16 = a16;
+  w->blocked = blocked;
+  w->rows = rows;
+  w->cols = cols;
+  size_t nc = (size_t)rows * cols * bits / 8, ng = (size_t)rows * (cols / g);
+  w->nbytes = (long long)(nc + 3 * ng);
+  cudaError_t e = cudaMalloc(&w->codes, nc);
+  if (e == cudaSuccess) e = cudaMalloc(&w->scale, ng * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&w->zp, ng);
+  if (e == cudaSuccess) e = cudaMemcpy(w->codes, codes, nc, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(w->scale, scale, ng * 2, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(w->zp, zp, ng, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    llmq_weight_free(w);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+  }
+  if (!smem_ok(w->view())) {
+    llmq_weight_free(w);
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "matrix too wide for the one-token kernel's shared memory");
+  }
+  *out = w;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_weight_free(llmq_weight *w) {
+  if (!w) return LLMQ_ERR_INVALID;
+  if (w->codes) cudaFree(w->codes);
+  if (w->scale) cudaFree(w->scale);
+  if (w->zp) cudaFree(w->zp);
+  delete w;
+  return LLMQ_OK;
+}
+
+long long llmq_weight_nbytes(const llmq_weight *w) { return w ? w->nbytes : -1; }
+
+llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
+                        int IN, int OUT, int flags) {
+  if (!ctx || !w || !x || !out || T <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument or T <= 0");
+  if (IN != w->cols || OUT != w->rows) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the matrix");
+  if ((flags & LLMQ_BIAS) && !bias) return fail(ctx, LLMQ_ERR_INVALID, "LLMQ_BIAS without a bias");
+  if (!w->a16) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "llmq_linear takes A16 formats");
+  CK(cudaSetDevice(ctx->device));
+  int epi = (flags & LLMQ_BIAS ? EPI_BIAS : 0) | (flags & LLMQ_GELU ? EPI_GELU : 0) |
+            (flags & LLMQ_RESID ? EPI_RESID : 0);
+  if (T == 1) {
+    GemvArgs a{};
+    a.w = w->view();
+    a.x = x;
+    a.bias = bias;
+    a.out = out;
+    a.epi = epi;
+    CK(launch_gemv(ctx, a, PRO_QUANT, false, ctx->stream));
+    return LLMQ_OK;
+  }
+  size_t need = (size_t)T * IN * 2 + (size_t)T * 4 + 256;
+  llmq_status st = ensure_scratch(ctx, need);
+  if (st != LLMQ_OK) return st;
+  int16_t *xq = (int16_t *)ctx->scratch;
+  float *sx = (float *)((char *)ctx->scratch + (((size_t)T * IN * 2 + 255) / 256) * 256);
+  quantize_rows_kernel<<<T, 256, 0, ctx->stream>>>(x, IN, xq, sx);
+  CKL();
+  int full = OUT / 32;
+  if (full > 0) {
+    dim3 grid(full, (T + 31) / 32);
+    tile_a16_kernel<<<grid, 256, 0, ctx->stream>>>(w->view(), xq, sx, bias, out, T, OUT, epi);
+    CKL();
+  }
+  if (OUT % 32) {
+    int n = T * (OUT - full * 32);
+    rows_a16_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(w->view(), xq, sx, bias, out, T, OUT, full * 32, epi);
+    CKL();
+  }
+  return LLMQ_OK;
+}
+
+llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h, float *logits, int *argmax) {
+  if (!ctx || !w || !h || !argmax) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  if (!w->a16) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "llmq_head_argmax takes A16 formats");
+  CK(cudaSetDevice(ctx->device));
+  int grid = gemv_grid(ctx, w->view());
+  llmq_status st = ensure_scratch(ctx, (size_t)grid * 8 + 256);
+  if (st != LLMQ_OK) return st;
+  GemvArgs a{};
+  a.w = w->view();
+  a.x = h;
+  a.out = logits;
+  a.part_val = (float *)ctx->scratch;
+  a.part_idx = (int *)((char *)ctx->scratch + (size_t)grid * 4);
+  a.state = ctx->state;
+  a.ids = argmax;  // written at state->step, kept at 0 here
+  CK(cudaMemsetAsync(ctx->state, 0, sizeof(DecodeState), ctx->stream));
+  CK(launch_gemv(ctx, a, PRO_QUANT, true, ctx->stream));
+  return LLMQ_OK;
+}
+
+llmq_status llmq_layernorm(llmq_ctx *ctx, float *out, const float *x, const float *w, const float *b, int T, int C) {
+  if (!ctx || !out || !x || !w || !b || T <= 0 || C <= 0 || C % 16) return fail(ctx, LLMQ_ERR_INVALID, "bad argument");
+  CK(cudaSetDevice(ctx->device));
+  layernorm_kernel<<<T, 256, C * 4, ctx->stream>>>(out, x, w, b, C);
+  CKL();
+  return LLMQ_OK;
+}
+
+llmq_status llmq_quantize_rows(llmq_ctx *ctx, const float *x, int T, int IN, int16_t *xq, float *sx) {
+  if (!ctx || !x || !xq || !sx || T <= 0 || IN <= 0) return fail(ctx, LLMQ_ERR_INVALID, "bad argument");
+  CK(cudaSetDevice(ctx->device));
+  quantize_rows_kernel<<<T, 256, 0, ctx->stream>>>(x, IN, xq, sx);
+  CKL();
+  return LLMQ_OK;
+}
+
+llmq_status llmq_debug_lane_sums(llmq_ctx *ctx, const llmq_weight *w, const float *x, int32_t *lanes) {
+  if (!ctx || !w || !x || !lanes) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  CK(cudaSetDevice(ctx->device));
+  GemvArgs a{};
+  a.w = w->view();
+  a.x = x;
+  int grid = gemv_grid(ctx, a.w);
+  int fmt = fmt_of(a.w);
+  if (fmt == FMT_BLK4) {
+    lane_sums_kernel<FMT_BLK4><<<grid, kThreads, smem_bytes<FMT_BLK4>(a.w), ctx->stream>>>(a, lanes);
+  } else if (fmt == FMT_GEN4) {
+    lane_sums_kernel<FMT_GEN4><<<grid, kThreads, smem_bytes<FMT_GEN4>(a.w), ctx->stream>>>(a, lanes);
+  } else {
+    lane_sums_kernel<FMT_GEN8><<<grid, kThreads, smem_bytes<FMT_GEN8>(a.w), ctx->stream>>>(a, lanes);
+  }
+  CKL();
+  return LLMQ_OK;
+}
+
+// ---- KV cache --------------------------------------------------------------
+
+llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int n_head, int head_dim,
+                           llmq_kv **out) {
+  if (!ctx || !out || n_layer <= 0 || max_t <= 0 || n_head <= 0 || head_dim <= 0 || head_dim % 16 || head_dim > 128)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad cache shape");
+  if (kind != LLMQ_KV_QUANT8) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "cache kind not built");
+  *out = nullptr;
+  CK(cudaSetDevice(ctx->device));
+  llmq_kv *c = new llmq_kv();
+  c->ctx = ctx;
+  c->kind = kind;
+  size_t n = (size_t)n_layer * max_t * n_head * head_dim, ns = (size_t)n_layer * max_t * n_head;
+  KV8View &v = c->v8;
+  v.n_layer = n_layer;
+  v.max_t = max_t;
+  v.n_head = n_head;
+  v.head_dim = head_dim;
+  cudaError_t e = cudaMalloc(&v.k, n);
+  if (e == cudaSuccess) e = cudaMalloc(&v.v, n);
+  if (e == cudaSuccess) e = cudaMalloc(&v.ks, ns * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&v.vs, ns * 4);
+  if (e == cudaSuccess) e = cudaMemset(v.k, 0, n);
+  if (e == cudaSuccess) e = cudaMemset(v.v, 0, n);
+  if (e == cudaSuccess) e = cudaMemset(v.ks, 0, ns * 4);
+  if (e == cudaSuccess) e = cudaMemset(v.vs, 0, ns * 4);
+  if (e != cudaSuccess) {
+    llmq_kv_free(c);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("kv alloc: ") + cudaGetErrorString(e));
+  }
+  *out = c;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_kv_free(llmq_kv *c) {
+  if (!c) return LLMQ_ERR_INVALID;
+  if (c->v8.k) cudaFree(c->v8.k);
+  if (c->v8.v) cudaFree(c->v8.v);
+  if (c->v8.ks) cudaFree(c->v8.ks);
+  if (c->v8.vs) cudaFree(c->v8.vs);
+  delete c;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T, const float *qkv) {
+  if (!ctx || !kv || !qkv || T <= 0 || layer < 0 || layer >= kv->v8.n_layer || pos0 < 0 || pos0 + T > kv->v8.max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
+  CK(cudaSetDevice(ctx->device));
+  dim3 grid(kv->v8.n_head, T, 2);
+  kv8_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr);
+  CKL();
+  return LLMQ_OK;
+}
+
+llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *qkv, int layer, int T, int pos0) {
+  if (!ctx || !kv || !qkv || !out || T <= 0 || layer < 0 || layer >= kv->v8.n_layer || pos0 < 0 ||
+      pos0 + T > kv->v8.max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
+  CK(cudaSetDevice(ctx->device));
+  dim3 grid(kv->v8.n_head, T);
+  size_t sm = (size_t)(2 * kv->v8.max_t + kv->v8.head_dim) * 4;
+  kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
+  CKL();
+  return LLMQ_OK;
+}
+
+llmq_status llmq_kv_read(llmq_ctx *ctx, const llmq_kv *kv, void *k, void *v, void *ks, void *vs) {
+  if (!ctx || !kv) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  const KV8View &c = kv->v8;
+  size_t n = (size_t)c.n_layer * c.max_t * c.n_head * c.head_dim, ns = (size_t)c.n_layer * c.max_t * c.n_head;
+  if (k) CK(cudaMemcpy(k, c.k, n, cudaMemcpyDeviceToHost));
+  if (v) CK(cudaMemcpy(v, c.v, n, cudaMemcpyDeviceToHost));
+  if (ks) CK(cudaMemcpy(ks, c.ks, ns * 4, cudaMemcpyDeviceToHost));
+  if (vs) CK(cudaMemcpy(vs, c.vs, ns * 4, cudaMemcpyDeviceToHost));
+  return LLMQ_OK;
+}
+
+}  // extern "C"
+
+// ---- model -----------------------------------------------------------------
+
+namespace {
+
+// One decode step (gpt2t.mojo:350-447): embedding, 12 x (LN1 + QKV, KV store
+// + attention, PROJ + residual, LN2 + FC + GELU, FCPROJ + residual), LN_f +
+// head + argmax. Token, position and step index come from m->state.
+llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
+  llmq_ctx *ctx = m->ctx;
+  const int C = m->C;
+  embed_kernel<<<3, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->state);
+  CKL();
+  size_t att_sm = (size_t)(2 * m->max_t + C / m->n_head) * 4;
+  for (int l = 0; l < m->n_layer; l++) {
+    const llmq_weight *const *w = &m->mats[4 * l];
+    GemvArgs a{};
+    a.w = w[0]->view();
+    a.x = m->x;
+    a.ln_w = m->vec(l, 0);
+    a.ln_b = m->vec(l, 1);
+    a.bias = m->vec(l, 2);
+    a.out = m->qkv;
+    a.epi = EPI_BIAS;
+    CK(launch_gemv(ctx, a, PRO_LN, false, s));
+    kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1);
+    CKL();
+    a = GemvArgs{};
+    a.w = w[1]->view();
+    a.x = m->att;
+    a.bias = m->vec(l, 3);
+    a.out = m->x;
+    a.epi = EPI_BIAS | EPI_RESID;
+    CK(launch_gemv(ctx, a, PRO_QUANT, false, s));
+    a = GemvArgs{};
+    a.w = w[2]->view();
+    a.x = m->x;
+    a.ln_w = m->vec(l, 4);
+    a.ln_b = m->vec(l, 5);
+    a.bias = m->vec(l, 6);
+    a.out = m->fc;
+    a.epi = EPI_BIAS | EPI_GELU;
+    CK(launch_gemv(ctx, a, PRO_LN, false, s));
+    a = GemvArgs{};
+    a.w = w[3]->view();
+    a.x = m->fc;
+    a.bias = m->vec(l, 7);
+    a.out = m->x;
+    a.epi = EPI_BIAS | EPI_RESID;
+    CK(launch_gemv(ctx, a, PRO_QUANT, false, s));
+  }
+  GemvArgs a{};
+  a.w = m->head->view();
+  a.x = m->x;
+  a.ln_w = m->lnf_w();
+  a.ln_b = m->lnf_b();
+  a.out = m->logits;
+  a.part_val = m->part_val;
+  a.part_idx = m->part_idx;
+  a.state = m->state;
+  a.ids = m->ids;
+  CK(launch_gemv(ctx, a, PRO_LN, true, s));
+  return LLMQ_OK;
+}
+
+// Several tokens at positions pos0.. through all layers (gpt2t.mojo:485-571);
+// leaves the hidden states in m->x.
+llmq_status enqueue_blocks(llmq_model *m, int T, int pos0, cudaStream_t s) {
+  llmq_ctx *ctx = m->ctx;
+  const int C = m->C;
+  embed_rows_kernel<<<T, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->tokens, pos0);
+  CKL();
+  llmq_status st;
+  for (int l = 0; l < m->n_layer; l++) {
+    const llmq_weight *const *w = &m->mats[4 * l];
+    layernorm_kernel<<<T, 256, C * 4, s>>>(m->xn, m->x, m->vec(l, 0), m->vec(l, 1), C);
+    CKL();
+    if ((st = llmq_linear(ctx, w[0], m->xn, m->vec(l, 2), m->qkv, T, C, 3 * C, LLMQ_BIAS)) != LLMQ_OK) return st;
+    if ((st = llmq_kv_store(ctx, m->kv, l, pos0, T, m->qkv)) != LLMQ_OK) return st;
+    if ((st = llmq_kv_attend(ctx, m->kv, m->att, m->qkv, l, T, pos0)) != LLMQ_OK) return st;
+    if ((st = llmq_linear(ctx, w[1], m->att, m->vec(l, 3), m->x, T, C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK) return st;
+    layernorm_kernel<<<T, 256, C * 4, s>>>(m->xn, m->x, m->vec(l, 4), m->vec(l, 5), C);
+    CKL();
+    if ((st = llmq_linear(ctx, w[2], m->xn, m->vec(l, 6), m->fc, T, C, 4 * C, LLMQ_BIAS | LLMQ_GELU)) != LLMQ_OK) return st;
+    if ((st = llmq_linear(ctx, w[3], m->fc, m->vec(l, 7), m->x, T, 4 * C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK) return st;
+  }
+  return LLMQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *mats, const llmq_weight *head,
+                              const float *small_host, int kv_kind, int max_t, llmq_model **out) {
+  if (!ctx || !mats || !head || !small_host || !out || n_layer <= 0 || max_t <= 0 || max_t > 1024)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad model arguments");
+  const int C = 768;
+  for (int i = 0; i < 4 * n_layer; i++) {
+    static const int ins[4] = {C, C, C, 4 * C}, outs[4] = {3 * C, C, 4 * C, C};
+    if (!mats[i] || mats[i]->cols != ins[i % 4] || mats[i]->rows != outs[i % 4] || !mats[i]->a16)
+      return fail(ctx, LLMQ_ERR_INVALID, "layer matrix " + std::to_string(i) + " has an unexpected shape or format");
+  }
+  if (head->cols != C || !head->a16) return fail(ctx, LLMQ_ERR_INVALID, "head must be an A16 [V, 768] matrix");
+  *out = nullptr;
+  CK(cudaSetDevice(ctx->device));
+  llmq_model *m = new llmq_model();
+  m->ctx = ctx;
+  m->n_layer = n_layer;
+  m->C = C;
+  m->V = head->rows;
+  m->max_t = max_t;
+  m->n_head = 12;
+  m->mats.assign(mats, mats + 4 * n_layer);
+  m->head = head;
+  m->max_ids = 4096;
+  llmq_status st = llmq_kv_create(ctx, kv_kind, n_layer, max_t, m->n_head, C / m->n_head, &m->kv);
+  if (st != LLMQ_OK) {
+    delete m;
+    return st;
+  }
+  size_t small_n = (size_t)n_layer * 13 * C + (size_t)1024 * C + 2 * C;
+  int grid = gemv_grid(ctx, head->view());
+  cudaError_t e = cudaMalloc(&m->small, small_n * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(m->small, small_host, small_n * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&m->x, (size_t)max_t * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->xn, (size_t)max_t * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->qkv, (size_t)max_t * 3 * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->att, (size_t)max_t * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->fc, (size_t)max_t * 4 * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->logits, (size_t)m->V * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->tokens, (size_t)max_t * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->ids, (size_t)m->max_ids * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->part_val, (size_t)grid * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->part_idx, (size_t)grid * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&m->state, sizeof(DecodeState));
+  if (e == cudaSuccess) e = cudaMemset(m->state, 0, sizeof(DecodeState));
+  if (e == cudaSuccess) e = cudaMallocHost(&m->state_host, sizeof(DecodeState));
+  if (e == cudaSuccess) e = cudaMallocHost(&m->ids_host, (size_t)m->max_ids * 4);
+  if (e != cudaSuccess) {
+    llmq_model_free(m);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("model alloc: ") + cudaGetErrorString(e));
+  }
+  *out = m;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_free(llmq_model *m) {
+  if (!m) return LLMQ_ERR_INVALID;
+  cudaSetDevice(m->ctx->device);
+  if (m->exec) cudaGraphExecDestroy(m->exec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  if (m->kv) llmq_kv_free(m->kv);
+  float *fs[] = {m->small, m->x, m->xn, m->qkv, m->att, m->fc, m->logits, m->part_val};
+  for (float *p : fs)
+    if (p) cudaFree(p);
+  if (m->tokens) cudaFree(m->tokens);
+  if (m->ids) cudaFree(m->ids);
+  if (m->part_idx) cudaFree(m->part_idx);
+  if (m->state) cudaFree(m->state);
+  if (m->state_host) cudaFreeHost(m->state_host);
+  if (m->ids_host) cudaFreeHost(m->ids_host);
+  delete m;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_use_graph(llmq_model *m, int enable) {
+  if (!m) return LLMQ_ERR_INVALID;
+  m->use_graph = enable;
+  return LLMQ_OK;
+}
+
+static llmq_status run_decode_step(llmq_model *m) {
+  llmq_ctx *ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  if (!m->use_graph) return enqueue_decode_step(m, s);
+  if (!m->exec) {
+    CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    llmq_status st = enqueue_decode_step(m, s);
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (st != LLMQ_OK) {
+      if (g) cudaGraphDestroy(g);
+      return st;
+    }
+    CK(e);
+    m->graph = g;
+    CK(cudaGraphInstantiate(&m->exec, g, 0));
+  }
+  CK(cudaGraphLaunch(m->exec, s));
+  return LLMQ_OK;
+}
+
+static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0);
+
+// Prompt through the model; ends with ids[0] = argmax of the last token's
+// logits, state = {token: ids[0], pos: n_prompt, step: 1}.
+static llmq_status run_prompt(llmq_model *m, const int *prompt, int T, int pos0) {
+  llmq_ctx *ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  if (T == 1) {
+    *m->state_host = DecodeState{};
+    m->state_host->token = prompt[0];
+    m->state_host->pos = pos0;
+    CK(cudaMemcpyAsync(m->state, m->state_host, sizeof(DecodeState), cudaMemcpyHostToDevice, s));
+    return run_decode_step(m);
+  }
+  CK(cudaMemcpyAsync(m->tokens, prompt, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+  return run_prompt_tail(m, T, pos0);
+}
+
+// Prefill of the T tokens already in m->tokens, then the head's argmax.
+static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0) {
+  llmq_ctx *ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  llmq_status st = enqueue_blocks(m, T, pos0, s);
+  if (st != LLMQ_OK) return st;
+  *m->state_host = DecodeState{};
+  m->state_host->pos = pos0 + T - 1;
+  CK(cudaMemcpyAsync(m->state, m->state_host, sizeof(DecodeState), cudaMemcpyHostToDevice, s));
+  GemvArgs a{};
+  a.w = m->head->view();
+  a.x = m->x + (size_t)(T - 1) * m->C;
+  a.ln_w = m->lnf_w();
+  a.ln_b = m->lnf_b();
+  a.out = m->logits;
+  a.part_val = m->part_val;
+  a.part_idx = m->part_idx;
+  a.state = m->state;
+  a.ids = m->ids;
+  CK(launch_gemv(ctx, a, PRO_LN, true, s));
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_forward(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T, int pos0, float *logits_dev,
+                               int *argmax_host) {
+  if (!ctx || !m || !tokens || T <= 0 || pos0 < 0 || pos0 + T > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad tokens or positions");
+  for (int i = 0; i < T; i++)
+    if (tokens[i] < 0 || tokens[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  llmq_status st = run_prompt(m, tokens, T, pos0);
+  if (st != LLMQ_OK) return st;
+  cudaStream_t s = ctx->stream;
+  if (logits_dev) CK(cudaMemcpyAsync(logits_dev, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, s));
+  if (argmax_host) {
+    CK(cudaMemcpyAsync(m->ids_host, m->ids, 4, cudaMemcpyDeviceToHost, s));
+  }
+  CK(cudaStreamSynchronize(s));
+  if (argmax_host) *argmax_host = m->ids_host[0];
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T, float *logits_dev) {
+  if (!ctx || !m || !tokens || !logits_dev || T <= 0 || T > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad tokens");
+  for (int i = 0; i < T; i++)
+    if (tokens[i] < 0 || tokens[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  cudaStream_t s = ctx->stream;
+  CK(cudaMemcpyAsync(m->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+  llmq_status st = enqueue_blocks(m, T, 0, s);
+  if (st == LLMQ_OK) {
+    layernorm_kernel<<<T, 256, m->C * 4, s>>>(m->xn, m->x, m->lnf_w(), m->lnf_b(), m->C);
+    st = llmq_linear(ctx, m->head, m->xn, nullptr, logits_dev, T, m->C, m->V, 0);
+  }
+  if (st != LLMQ_OK) return st;
+  CK(cudaStreamSynchronize(s));
+  return LLMQ_OK;
+}
+
+llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n_prompt, int steps, int *out_ids) {
+  if (!ctx || !m || !prompt || !out_ids || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
+      n_prompt + steps - 1 > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
+  for (int i = 0; i < n_prompt; i++)
+    if (prompt[i] < 0 || prompt[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  llmq_status st = run_prompt(m, prompt, n_prompt, 0);
+  if (st != LLMQ_OK) return st;
+  for (int i = 1; i < steps; i++)
+    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  cudaStream_t s = ctx->stream;
+  CK(cudaMemcpyAsync(m->ids_host, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  std::memcpy(out_ids, m->ids_host, (size_t)steps * 4);
+  return LLMQ_OK;
+}
+
+__global__ void init_state_kernel(DecodeState *st, const int *prompt, int n_prompt) {
+  st->token = prompt[0];
+  st->pos = 0;
+  st->step = 0;
+  st->ticket = 0;
+}
+
+llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
+                                int *ids_dev) {
+  if (!ctx || !m || !prompt_dev || !ids_dev || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
+      n_prompt + steps - 1 > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
+  CK(cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->stream;
+  llmq_status st;
+  if (n_prompt == 1) {
+    init_state_kernel<<<1, 1, 0, s>>>(m->state, prompt_dev, 1);
+    CKL();
+    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  } else {
+    CK(cudaMemcpyAsync(m->tokens, prompt_dev, (size_t)n_prompt * 4, cudaMemcpyDeviceToDevice, s));
+    if ((st = run_prompt_tail(m, n_prompt, 0)) != LLMQ_OK) return st;
+  }
+  for (int i = 1; i < steps; i++)
+    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  CK(cudaMemcpyAsync(ids_dev, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToDevice, s));
+  return LLMQ_OK;
+}
+
+}  // extern "C"

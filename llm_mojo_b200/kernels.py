@@ -1,0 +1,110 @@
+"""The kernels layer (kernels.mojo) on device tensors: linear, head with
+greedy argmax, layernorm, quantize_rows, and the KV cache's store/attend.
+
+Arguments are torch CUDA tensors (float32 / int16 / int32, contiguous);
+torch only provides the device memory. Calls are issued on the context's
+stream and synchronised with torch's before and after, so tensors can be
+used directly.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+from ._lib import BIAS, GELU, KV_INTATTN, KV_QUANT8, RESID, check, lib
+from .tensor import Context, QuantMatrix
+
+
+def _p(t):
+    if t is None:
+        return None
+    assert t.is_cuda and t.is_contiguous()
+    return C.c_void_p(t.data_ptr())
+
+
+def _pre(ctx: Context):
+    import torch
+
+    torch.cuda.current_stream().synchronize()
+
+
+def linear(ctx: Context, out, x, w: QuantMatrix, b, T: int, IN: int, OUT: int, resid=False, gelu=False):
+    """out[T, OUT] (+)= act(x[T, IN] @ w^T + b) (kernels.mojo:655-673)."""
+    _pre(ctx)
+    flags = (BIAS if b is not None else 0) | (GELU if gelu else 0) | (RESID if resid else 0)
+    check(lib().llmq_linear(ctx.h, w.h, _p(x), _p(b), _p(out), T, IN, OUT, flags), ctx.h)
+    ctx.sync()
+
+
+def head_argmax(ctx: Context, w: QuantMatrix, h, logits, argmax):
+    """logits[V] = h[C] @ w^T and the greedy argmax (kernels.mojo:676-690,
+    gpt2t.mojo:792-797); argmax is a 1-element int32 device tensor."""
+    _pre(ctx)
+    check(lib().llmq_head_argmax(ctx.h, w.h, _p(h), _p(logits), _p(argmax)), ctx.h)
+    ctx.sync()
+
+
+def layernorm(ctx: Context, out, x, w, b, T: int, C_: int):
+    _pre(ctx)
+    check(lib().llmq_layernorm(ctx.h, _p(out), _p(x), _p(w), _p(b), T, C_), ctx.h)
+    ctx.sync()
+
+
+def quantize_rows(ctx: Context, x, T: int, IN: int, xq, sx):
+    _pre(ctx)
+    check(lib().llmq_quantize_rows(ctx.h, _p(x), T, IN, _p(xq), _p(sx)), ctx.h)
+    ctx.sync()
+
+
+def lane_sums(ctx: Context, w: QuantMatrix, x, lanes):
+    """int32 lane sums of dot_row_i16 for every row, [OUT][units][16]."""
+    _pre(ctx)
+    check(lib().llmq_debug_lane_sums(ctx.h, w.h, _p(x), _p(lanes)), ctx.h)
+    ctx.sync()
+
+
+class KVCache:
+    """KVCache (kvcache.mojo:31-87): QuantKV[8] ('int8') or IntAttnKV
+    ('intattn')."""
+
+    def __init__(self, ctx: Context, kind: str, n_layer: int, max_t: int, n_head: int, head_dim: int):
+        self.ctx = ctx
+        self.kind = {"int8": KV_QUANT8, "intattn": KV_INTATTN}[kind]
+        self.shape = (n_layer, max_t, n_head, head_dim)
+        h = C.c_void_p()
+        check(lib().llmq_kv_create(ctx.h, self.kind, n_layer, max_t, n_head, head_dim, C.byref(h)), ctx.h)
+        self.h = h
+
+    def store(self, layer: int, pos0: int, T: int, qkv):
+        _pre(self.ctx)
+        check(lib().llmq_kv_store(self.ctx.h, self.h, layer, pos0, T, _p(qkv)), self.ctx.h)
+        self.ctx.sync()
+
+    def attend(self, out, qkv, layer: int, T: int, pos0: int):
+        _pre(self.ctx)
+        check(lib().llmq_kv_attend(self.ctx.h, self.h, _p(out), _p(qkv), layer, T, pos0), self.ctx.h)
+        self.ctx.sync()
+
+    def read(self):
+        """(k, v, ks, vs) host copies of the storage."""
+        import numpy as np
+
+        L, T, H, D = self.shape
+        k = np.zeros(L * T * H * D, dtype=np.int8)
+        v = np.zeros_like(k)
+        ks = np.zeros(L * T * H, dtype=np.float32)
+        vs = np.zeros_like(ks)
+        ptr = lambda a: a.ctypes.data_as(C.c_void_p)  # noqa: E731
+        check(lib().llmq_kv_read(self.ctx.h, self.h, ptr(k), ptr(v), ptr(ks), ptr(vs)), self.ctx.h)
+        return k, v, ks, vs
+
+    def free(self):
+        if self.h:
+            lib().llmq_kv_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,86 @@
+"""GPT-2 124M on the device, mirroring the reference's Model[W, E, KV]
+(gpt2t.mojo:198-572): load_model's conversion of the layer matrices and the
+tied wte/head, forward / forward_all, and greedy generate.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import synth
+from ._lib import KV_INTATTN, KV_QUANT8, check, lib
+from .tensor import Context, QuantMatrix, parse_dtype
+
+# HEAD8_A16 (gpt2t.mojo:1231-1235): int8 per vocabulary row, integer path.
+HEAD8_A16 = (8, 0, False, True)
+
+
+class Model:
+    """Model[W, E, KV] with an A16 layer format W (e.g. 'int4-g32-a16'), the
+    int8 head (head='int8') or the layer format (head='same'), and a
+    QuantKV[8] ('int8') or IntAttnKV ('intattn') cache."""
+
+    def __init__(self, ctx: Context, tensors: dict, dtype: str = "int4-g32-a16", head: str = "int8",
+                 kv: str = "int8", n_layer: int = synth.N_LAYER, max_t: int = synth.MAX_T):
+        bits, group, sym, a16 = parse_dtype(dtype)
+        if not a16:
+            raise ValueError("the device model runs the -a16 formats")
+        self.ctx, self.dtype, self.n_layer = ctx, dtype, n_layer
+        self.mats = [QuantMatrix.from_f32(ctx, tensors[f"h.{l}.{name}"], bits, group, sym, a16, True)
+                     for l in range(n_layer) for name in synth.MAT_NAMES]
+        hfmt = HEAD8_A16 if head == "int8" else (bits, group, sym, a16)
+        self.head = QuantMatrix.from_f32(ctx, tensors["wte.weight"], *hfmt, False)
+        self.small = synth.small_floats(tensors, n_layer)
+        arr = (C.c_void_p * len(self.mats))(*[m.h.value for m in self.mats])
+        h = C.c_void_p()
+        kind = {"int8": KV_QUANT8, "intattn": KV_INTATTN}[kv]
+        check(lib().llmq_model_create(ctx.h, n_layer, C.cast(arr, C.c_void_p), self.head.h,
+                                      self.small.ctypes.data_as(C.c_void_p), kind, max_t, C.byref(h)), ctx.h)
+        self.h = h
+        self.V = self.head.rows
+
+    def weight_bytes(self) -> int:
+        """Model.weight_bytes (gpt2t.mojo:312-319)."""
+        return self.head.nbytes() + sum(m.nbytes() for m in self.mats) + self.small.size * 4
+
+    def use_graph(self, enable: bool):
+        check(lib().llmq_model_use_graph(self.h, int(enable)), self.ctx.h)
+
+    def forward(self, tokens, pos0: int, logits=None) -> int:
+        """Runs tokens at positions pos0..; returns the last token's argmax and
+        writes its logits into `logits` (a float32 CUDA tensor [V]) if given."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = C.c_int(0)
+        lp = C.c_void_p(logits.data_ptr()) if logits is not None else None
+        check(lib().llmq_model_forward(self.ctx.h, self.h, t.ctypes.data_as(C.c_void_p), t.size, pos0, lp,
+                                       C.byref(out)), self.ctx.h)
+        return out.value
+
+    def forward_all(self, tokens, logits) -> None:
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(lib().llmq_model_forward_all(self.ctx.h, self.h, t.ctypes.data_as(C.c_void_p), t.size,
+                                           C.c_void_p(logits.data_ptr())), self.ctx.h)
+
+    def generate(self, prompt, steps: int) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(steps, dtype=np.int32)
+        check(lib().llmq_generate(self.ctx.h, self.h, p.ctypes.data_as(C.c_void_p), p.size, steps,
+                                  out.ctypes.data_as(C.c_void_p)), self.ctx.h)
+        return out
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().llmq_model_free(self.h)
+            self.h = None
+        for m in getattr(self, "mats", []):
+            m.free()
+        if getattr(self, "head", None) is not None:
+            self.head.free()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1,0 +1,255 @@
+"""GPU kernels against the CPU oracle, through the C ABI.
+
+Integer accumulators must be bit-exact, and so must every float output:
+the kernels follow the reference's float32 operation order (lane chains,
+halving-tree sums, fma where the reference calls .fma) and the oracle does
+too, so the tolerance is zero. Shapes are config 0's (2304x768, 768x768,
+3072x768, 768x3072, 50257x768) plus odd ones that exercise the tails.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+FORMATS = ["int4-g32-a16", "int4-g32-sym-a16", "int4-g64-a16", "int4-g128-a16", "int4-ch-a16", "int8-ch-a16",
+           "int8-g32-a16", "int4-ch-sym-a16"]
+
+
+@pytest.fixture(scope="module")
+def torch():
+    import torch
+
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return torch
+
+
+@pytest.fixture(scope="module")
+def ctx(torch):
+    from llm_mojo_b200 import build
+    from llm_mojo_b200.tensor import Context
+
+    build.build()
+    return Context(0)
+
+
+def make_weights(fmt, IN, OUT, seed):
+    from llm_mojo_b200.tensor import parse_dtype
+
+    bits, group, sym, a16 = parse_dtype(fmt)
+    rng = np.random.default_rng(seed)
+    src = (rng.standard_normal((IN, OUT), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    return src, (bits, group, sym, a16)
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+@pytest.mark.parametrize("IN,OUT", [(768, 2304), (3072, 768), (768, 70)])
+def test_decode_gemv_bit_exact(torch, ctx, fmt, IN, OUT):
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix
+
+    src, (bits, group, sym, a16) = make_weights(fmt, IN, OUT, IN + OUT)
+    ow = O.QuantMatrix(src, bits, group, sym, a16, True)
+    gw = QuantMatrix.from_f32(ctx, src, bits, group, sym, a16, True)
+    rng = np.random.default_rng(1)
+    for big, flags in [(False, dict()), (False, dict(gelu=True)), (True, dict(resid=True))]:
+        x = rng.standard_normal((1, IN)).astype(np.float32)
+        if big:  # every activation near +-max: the largest int32 lane sums
+            x = (rng.uniform(0.9, 1.0, (1, IN)) * np.where(np.arange(IN) % 2 == 0, 1, -1)).astype(np.float32)
+        b = rng.standard_normal(OUT).astype(np.float32)
+        resid = rng.standard_normal((1, OUT)).astype(np.float32) if flags.get("resid") else None
+        want = O.matmul_rows_a16(x, ow, b, resid_into=resid, gelu=flags.get("gelu", False))
+        out = dev(torch, resid if resid is not None else np.zeros((1, OUT), np.float32))
+        kernels.linear(ctx, out, dev(torch, x), gw, dev(torch, b), 1, IN, OUT, **flags)
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), \
+            f"max diff {np.abs(got - want).max()} at {np.argmax(np.abs(got - want))}"
+    gw.free()
+
+
+@pytest.mark.parametrize("fmt", ["int4-g32-a16", "int4-g64-a16", "int8-ch-a16", "int4-ch-sym-a16"])
+def test_lane_sums_bit_exact(torch, ctx, fmt):
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix
+
+    IN, OUT = 3072, 96
+    src, (bits, group, sym, a16) = make_weights(fmt, IN, OUT, 11)
+    ow = O.QuantMatrix(src, bits, group, sym, a16, True)
+    gw = QuantMatrix.from_f32(ctx, src, bits, group, sym, a16, True)
+    x = (np.random.default_rng(2).uniform(0.9, 1.0, (1, IN)) * np.where(np.arange(IN) % 3 == 0, 1, -1)).astype(
+        np.float32)
+    xq, sx = O.quantize_rows(x)
+    if ow.blocked:
+        x1, xs = O.permute_x_i16(xq[0])
+    else:
+        x1, xs = xq[0], None
+    units = IN // 256 if ow.blocked else IN // ow.group
+    lanes = torch.zeros((OUT, units, 16), dtype=torch.int32, device="cuda")
+    kernels.lane_sums(ctx, gw, dev(torch, x[0]), lanes)
+    got = lanes.cpu().numpy()
+    for r in range(OUT):
+        assert np.array_equal(got[r], O.lane_sums(ow, r, x1, xs)), f"row {r}"
+    gw.free()
+
+
+@pytest.mark.parametrize("fmt", ["int4-g32-a16", "int8-ch-a16", "int4-g128-a16"])
+@pytest.mark.parametrize("T,IN,OUT", [(3, 768, 64), (4, 768, 70), (9, 3072, 40), (5, 768, 2304), (476, 768, 768)])
+def test_prefill_linear_bit_exact(torch, ctx, fmt, T, IN, OUT):
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix
+
+    src, (bits, group, sym, a16) = make_weights(fmt, IN, OUT, T * 7 + OUT)
+    ow = O.QuantMatrix(src, bits, group, sym, a16, True)
+    gw = QuantMatrix.from_f32(ctx, src, bits, group, sym, a16, True)
+    rng = np.random.default_rng(T)
+    x = rng.standard_normal((T, IN)).astype(np.float32)
+    x[0] = (rng.uniform(0.9, 1.0, IN) * np.where(np.arange(IN) % 2 == 0, 1, -1)).astype(np.float32)
+    b = rng.standard_normal(OUT).astype(np.float32)
+    want = O.matmul_rows_a16(x, ow, b, gelu=True)
+    out = torch.zeros((T, OUT), dtype=torch.float32, device="cuda")
+    kernels.linear(ctx, out, dev(torch, x), gw, dev(torch, b), T, IN, OUT, gelu=True)
+    got = out.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"max diff {np.abs(got - want).max()}"
+    gw.free()
+
+
+def test_layernorm_and_quantize_rows_bit_exact(torch, ctx):
+    from llm_mojo_b200 import kernels
+
+    rng = np.random.default_rng(4)
+    T, Cn = 7, 768
+    x = (rng.standard_normal((T, Cn)) * 3).astype(np.float32)
+    w = rng.standard_normal(Cn).astype(np.float32)
+    b = rng.standard_normal(Cn).astype(np.float32)
+    out = torch.zeros((T, Cn), dtype=torch.float32, device="cuda")
+    kernels.layernorm(ctx, out, dev(torch, x), dev(torch, w), dev(torch, b), T, Cn)
+    assert np.array_equal(out.cpu().numpy(), O.layernorm(x, w, b))
+    xq = torch.zeros((T, Cn), dtype=torch.int16, device="cuda")
+    sx = torch.zeros(T, dtype=torch.float32, device="cuda")
+    kernels.quantize_rows(ctx, dev(torch, x), T, Cn, xq, sx)
+    wq, ws = O.quantize_rows(x)
+    assert np.array_equal(xq.cpu().numpy(), wq)
+    assert np.array_equal(sx.cpu().numpy(), ws)
+
+
+def test_head_argmax_matches_oracle(torch, ctx, gpt2_tensors):
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix
+
+    wte = gpt2_tensors["wte.weight"]
+    ow = O.QuantMatrix(wte, 8, 0, False, True, False)
+    gw = QuantMatrix.from_f32(ctx, wte, 8, 0, False, True, False)
+    rng = np.random.default_rng(9)
+    for trial in range(3):
+        h = rng.standard_normal((1, 768)).astype(np.float32)
+        want = O.matmul_rows_a16(h, ow, None)[0]
+        logits = torch.zeros(50257, dtype=torch.float32, device="cuda")
+        am = torch.zeros(1, dtype=torch.int32, device="cuda")
+        kernels.head_argmax(ctx, gw, dev(torch, h[0]), logits, am)
+        got = logits.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert int(am.item()) == O.lib().oq_argmax(O.ptr(want), 50257)
+    gw.free()
+
+
+@pytest.mark.parametrize("npos0,T", [(0, 1), (0, 5), (15, 1), (16, 1), (99, 1), (200, 7), (1000, 3)])
+def test_quant8_attention_bit_exact(torch, ctx, npos0, T):
+    """QuantKV[8] store + attend_float_one, the context grid of the
+    reference's tests/int_attention_check.mojo."""
+    from llm_mojo_b200.kernels import KVCache
+
+    NH, HS, Cn, MAXT = 12, 64, 768, 1024
+    rng = np.random.default_rng(npos0 * 10 + T)
+    n = npos0 + T
+    qkv_all = (rng.standard_normal((n, 3 * Cn)) * 2).astype(np.float32)
+    kv = KVCache(ctx, "int8", 1, MAXT, NH, HS)
+    oc = O.lib().oq_qkv8_new(1, MAXT, NH, HS)
+    try:
+        if npos0:
+            kv.store(0, 0, npos0, dev(torch, qkv_all[:npos0]))
+        for p in range(n):
+            row = qkv_all[p]
+            O.lib().oq_qkv8_store(oc, 0, p, O.ptr(np.ascontiguousarray(row[Cn:2 * Cn])),
+                                  O.ptr(np.ascontiguousarray(row[2 * Cn:])))
+        q = np.ascontiguousarray(qkv_all[npos0:])
+        kv.store(0, npos0, T, dev(torch, q))
+        out = torch.zeros((T, Cn), dtype=torch.float32, device="cuda")
+        kv.attend(out, dev(torch, q), 0, T, npos0)
+        want = np.zeros((T, Cn), dtype=np.float32)
+        for t in range(T):
+            for h in range(NH):
+                O.lib().oq_qkv8_attend_one(oc, O.ptr(want), O.ptr(q), 0, t, h, npos0)
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"max diff {np.abs(got - want).max()}"
+        k, v, ks, vs = kv.read()
+        import ctypes as C
+
+        ok = np.ctypeslib.as_array(C.cast(O.lib().oq_qkv8_k(oc), C.POINTER(C.c_int8)), shape=(MAXT * NH * HS,))
+        oks = np.ctypeslib.as_array(C.cast(O.lib().oq_qkv8_ks(oc), C.POINTER(C.c_float)), shape=(MAXT * NH,))
+        assert np.array_equal(k[: n * NH * HS], ok[: n * NH * HS])
+        assert np.array_equal(ks[: n * NH], oks[: n * NH])
+    finally:
+        O.lib().oq_qkv8_free(oc)
+        kv.free()
+
+
+@pytest.fixture(scope="module")
+def gpu_model(torch, ctx, gpt2_tensors):
+    from llm_mojo_b200.model import Model
+
+    m = Model(ctx, gpt2_tensors)
+    yield m
+    m.free()
+
+
+def test_generate_100_greedy_ids_match_oracle(gpu_model, oracle_a16):
+    """Config 0: prompt [50256], 100 greedy tokens, int4-g32-a16 + int8 head +
+    int8 KV: the ids must be identical."""
+    want = oracle_a16.generate([50256], 100)
+    got = gpu_model.generate([50256], 100)
+    assert list(got) == list(want)
+    got2 = gpu_model.generate([50256], 100)  # replays the captured graph
+    assert list(got2) == list(want)
+
+
+def test_forward_logits_bit_exact(torch, gpu_model, oracle_a16, golden):
+    logits = torch.zeros(50257, dtype=torch.float32, device="cuda")
+    prompt = golden["prompt24"]
+    am = gpu_model.forward(prompt, 0, logits)
+    want = oracle_a16.forward(prompt, 0)
+    got = logits.cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"max diff {np.abs(got - want).max()}"
+    assert am == int(np.argmax(want))
+    # one decode step after the prompt
+    am = gpu_model.forward([am], len(prompt), logits)
+    want = oracle_a16.forward([int(np.argmax(want))], len(prompt))
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_prompt_then_generate_matches_oracle(gpu_model, oracle_a16, golden):
+    prompt = golden["prompt24"]
+    assert list(gpu_model.generate(prompt, 20)) == list(oracle_a16.generate(prompt, 20))
+
+
+def test_forward_all_bit_exact(torch, gpu_model, oracle_a16, golden):
+    toks = golden["prompt24"][:16]
+    logits = torch.zeros((16, 50257), dtype=torch.float32, device="cuda")
+    gpu_model.forward_all(toks, logits)
+    want = oracle_a16.forward_all(toks)
+    assert np.array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_graph_and_eager_steps_agree(gpu_model):
+    gpu_model.use_graph(False)
+    try:
+        eager = gpu_model.generate([50256], 12)
+    finally:
+        gpu_model.use_graph(True)
+    assert list(eager) == list(gpu_model.generate([50256], 12))
