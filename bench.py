@@ -38,7 +38,8 @@ sys.path.insert(0, ROOT)
 STEPS_PER_GEN = 100
 PROMPT = [50256]
 HEAD_BYTES = 50257 * 768 + 50257 * 3          # int8-ch head: codes + f16 scale + u8 zp per row
-LAYER_BYTES = 12 * (2304 + 768 + 3072 + 768) * 768 * 19 // 32  # int4-g32: 0.59375 B/weight
+LAYER_WEIGHTS = 12 * (768 * (2304 + 768 + 3072) + 3072 * 768)  # 84,934,656
+LAYER_BYTES = LAYER_WEIGHTS * 19 // 32         # int4-g32: 0.59375 B/weight = 50,429,952
 TOKEN_BYTES = LAYER_BYTES + HEAD_BYTES         # 89,178,099 per token
 METRIC = "int4-g32-a16 decode tok/s (b=1)"
 

@@ -144,11 +144,23 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, 
  * llmq_generate. */
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
                                 int *ids_dev);
+/* Waits for the context's stream and reports a bounded device-side wait of
+ * the model's persistent kernel that gave up (LLMQ_ERR_TIMEOUT). */
+llmq_status llmq_model_check(llmq_ctx *ctx, llmq_model *m);
 /* The cudaStream_t the context issues its work on. */
 void *llmq_stream(const llmq_ctx *ctx);
-/* 1 (default) replays each decode step as a captured CUDA graph; 0 launches
- * its kernels one by one. */
-llmq_status llmq_model_use_graph(llmq_model *m, int enable);
+/* How decode steps run (replacing the reference's per-token thread team,
+ * team.mojo:36-82, and gpt2t.mojo:350-447's single parallel region):
+ * LLMQ_MODE_PERSISTENT (default when the formats allow it: int4-g32 A16
+ * layers, per-channel int8 A16 head, QuantKV[8]) runs a whole generation as
+ * one persistent kernel; LLMQ_MODE_GRAPH replays each step as a captured
+ * CUDA graph of one-token kernels; LLMQ_MODE_EAGER launches those kernels
+ * one by one. Returns LLMQ_ERR_UNSUPPORTED if the model cannot run `mode`. */
+#define LLMQ_MODE_EAGER 0
+#define LLMQ_MODE_GRAPH 1
+#define LLMQ_MODE_PERSISTENT 2
+llmq_status llmq_model_set_mode(llmq_model *m, int mode);
+int llmq_model_mode(const llmq_model *m);
 
 #ifdef __cplusplus
 }

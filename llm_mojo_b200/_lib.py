@@ -16,6 +16,7 @@ LIB_PATH = os.path.join(HERE, "libllmq.so")
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
 BIAS, GELU, RESID = 1, 2, 4
 KV_QUANT8, KV_INTATTN = 1, 2
+MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT = 0, 1, 2
 
 
 class LlmqError(RuntimeError):
@@ -52,9 +53,11 @@ SIGNATURES = {
     "llmq_model_forward": (I, [P, P, P, I, I, P, P]),
     "llmq_model_forward_all": (I, [P, P, P, I, P]),
     "llmq_generate": (I, [P, P, P, I, I, P]),
-    "llmq_model_use_graph": (I, [P, I]),
+    "llmq_model_set_mode": (I, [P, I]),
+    "llmq_model_mode": (I, [P]),
     "llmq_generate_async": (I, [P, P, P, I, I, P]),
     "llmq_stream": (P, [P]),
+    "llmq_model_check": (I, [P, P]),
 }
 
 _lib = None

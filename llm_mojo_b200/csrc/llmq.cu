@@ -7,6 +7,7 @@
 #include "../../include/llmq.h"
 #include "attention.cuh"
 #include "gemv_a16.cuh"
+#include "mega.cuh"
 #include "prefill_a16.cuh"
 
 using namespace llmq;
@@ -58,7 +59,16 @@ struct llmq_model {
   int *ids_host;            // pinned staging
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
-  int use_graph = 1;
+  int mode = LLMQ_MODE_GRAPH;
+  // persistent decode kernel (mega.cuh)
+  bool mega_ok = false;
+  int mega_grid = 0, mega_nchunks = 0;
+  uint8_t *mega_stream = nullptr;
+  long long *mega_base = nullptr;
+  MkChunk *mega_chunks = nullptr;
+  unsigned long long *mega_ll = nullptr;
+  int *mega_err = nullptr;
+  unsigned mega_flag = 1;
   const float *vec(int l, int which) const {
     static const int mult[8] = {0, 1, 2, 5, 6, 7, 8, 12};
     return small + (size_t)l * 13 * C + (size_t)mult[which] * C;
@@ -173,6 +183,8 @@ cudaError_t configure_kernels() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_BLK4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)mega_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MkSmem));
   return e;
 }
 }  // namespace
@@ -490,6 +502,161 @@ llmq_status llmq_kv_read(llmq_ctx *ctx, const llmq_kv *kv, void *k, void *v, voi
 
 namespace {
 
+struct CopyDesc {
+  const uint8_t *src;
+  long long dst;
+  long long bytes;
+};
+
+// Byte gather used once per model to build the per-CTA weight streams.
+__global__ void gather_kernel(const CopyDesc *d, uint8_t *dst) {
+  const CopyDesc c = d[blockIdx.x];
+  for (long long i = threadIdx.x; i < c.bytes; i += blockDim.x) dst[c.dst + i] = c.src[i];
+}
+
+inline long long align16(long long x) { return (x + 15) & ~15LL; }
+
+// Builds the persistent kernel's per-CTA weight streams (mega.cuh): CTA c
+// gets rows [rows*c/G, rows*(c+1)/G) of every layer matrix, in use order,
+// then its share of the head in 32-row tiles. Returns LLMQ_OK without
+// enabling the kernel when the formats are not the ones it runs.
+llmq_status mega_setup(llmq_model *m) {
+  llmq_ctx *ctx = m->ctx;
+  m->mega_ok = false;
+  if (m->kv->kind != LLMQ_KV_QUANT8 || m->n_head != 12 || m->C != 768 || m->kv->v8.head_dim != 64) return LLMQ_OK;
+  for (const llmq_weight *w : m->mats)
+    if (!w->blocked) return LLMQ_OK;
+  const llmq_weight *hd = m->head;
+  if (hd->bits != 8 || hd->group != hd->cols || hd->blocked || !hd->a16) return LLMQ_OK;
+  int occ = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, mega_decode_kernel, MK_THREADS, sizeof(MkSmem)));
+  if (occ < 1) return LLMQ_OK;
+  const int G = ctx->num_sms;
+  int max_tiles = 0;
+  for (int c = 0; c < G; c++) {
+    int h0 = (int)((long long)m->V * c / G), h1 = (int)((long long)m->V * (c + 1) / G);
+    int t = (h1 - h0 + MK_HEAD_TILE - 1) / MK_HEAD_TILE;
+    if (t > max_tiles) max_tiles = t;
+  }
+  const int nch = 4 * m->n_layer + max_tiles;
+  if (nch > MK_MAX_CHUNKS) return LLMQ_OK;
+  std::vector<MkChunk> chunks((size_t)G * nch);
+  std::vector<long long> base(G);
+  std::vector<CopyDesc> copies;
+  long long total = 0;
+  for (int c = 0; c < G; c++) {
+    base[c] = total;
+    long long off = 0;
+    int k = 0;
+    auto add = [&](int kind, int layer, const llmq_weight *w, int r0, int r1) -> bool {
+      int n = r1 - r0, gpr = w->cols / w->group;
+      long long row_bytes = (long long)w->cols * w->bits / 8;
+      long long codes = n * row_bytes, sc = (long long)n * gpr * 2, zpb = (long long)n * gpr;
+      MkChunk ch{};
+      ch.kind = kind;
+      ch.layer = layer;
+      ch.r0 = r0;
+      ch.r1 = r1;
+      ch.off = (int)off;
+      ch.scale_off = (int)align16(codes);
+      ch.zp_off = (int)(ch.scale_off + align16(sc));
+      ch.bytes = (int)(ch.zp_off + align16(zpb));
+      if (ch.bytes == 0) ch.bytes = 16;
+      if (ch.bytes > MK_SLOT || (kind != PH_HEAD && n > 64)) return false;
+      if (n > 0) {
+        copies.push_back({w->codes + r0 * row_bytes, total + off, codes});
+        copies.push_back({(const uint8_t *)w->scale + (long long)r0 * gpr * 2, total + off + ch.scale_off, sc});
+        copies.push_back({w->zp + (long long)r0 * gpr, total + off + ch.zp_off, zpb});
+      }
+      chunks[(size_t)c * nch + k++] = ch;
+      off += ch.bytes;
+      return true;
+    };
+    for (int l = 0; l < m->n_layer; l++)
+      for (int j = 0; j < 4; j++) {
+        const llmq_weight *w = m->mats[4 * l + j];
+        int r0 = (int)((long long)w->rows * c / G), r1 = (int)((long long)w->rows * (c + 1) / G);
+        if (!add(j, l, w, r0, r1)) return LLMQ_OK;
+      }
+    int h0 = (int)((long long)m->V * c / G), h1 = (int)((long long)m->V * (c + 1) / G);
+    for (int t = 0; t < max_tiles; t++) {
+      int r0 = h0 + t * MK_HEAD_TILE;
+      if (r0 > h1) r0 = h1;
+      int r1 = r0 + MK_HEAD_TILE < h1 ? r0 + MK_HEAD_TILE : h1;
+      if (!add(PH_HEAD, -1, hd, r0, r1)) return LLMQ_OK;
+    }
+    total += align16(off);
+  }
+  CK(cudaMalloc(&m->mega_stream, total + 16));
+  CK(cudaMalloc(&m->mega_base, sizeof(long long) * G));
+  CK(cudaMalloc(&m->mega_chunks, sizeof(MkChunk) * chunks.size()));
+  CK(cudaMemcpy(m->mega_base, base.data(), sizeof(long long) * G, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(m->mega_chunks, chunks.data(), sizeof(MkChunk) * chunks.size(), cudaMemcpyHostToDevice));
+  CopyDesc *dd = nullptr;
+  CK(cudaMalloc(&dd, sizeof(CopyDesc) * copies.size()));
+  CK(cudaMemcpy(dd, copies.data(), sizeof(CopyDesc) * copies.size(), cudaMemcpyHostToDevice));
+  gather_kernel<<<(unsigned)copies.size(), 256, 0, ctx->stream>>>(dd, m->mega_stream);
+  CKL();
+  CK(cudaStreamSynchronize(ctx->stream));
+  cudaFree(dd);
+  MkLL ll(m->C, m->n_layer, G);
+  CK(cudaMalloc(&m->mega_ll, sizeof(unsigned long long) * ll.total()));
+  CK(cudaMemset(m->mega_ll, 0, sizeof(unsigned long long) * ll.total()));
+  CK(cudaMalloc(&m->mega_err, sizeof(int)));
+  CK(cudaMemset(m->mega_err, 0, sizeof(int)));
+  m->mega_grid = G;
+  m->mega_nchunks = nch;
+  m->mega_flag = 1;
+  m->mega_ok = true;
+  m->mode = LLMQ_MODE_PERSISTENT;
+  return LLMQ_OK;
+}
+
+// One cooperative launch: `steps` greedy steps from *first_token at pos0.
+llmq_status run_mega(llmq_model *m, const int *first_token, int pos0, int steps, int *ids, float *logits) {
+  llmq_ctx *ctx = m->ctx;
+  MegaArgs a{};
+  a.stream = m->mega_stream;
+  a.stream_base = m->mega_base;
+  a.chunks = m->mega_chunks;
+  a.nchunks = m->mega_nchunks;
+  a.n_layer = m->n_layer;
+  a.C = m->C;
+  a.V = m->V;
+  a.n_head = m->n_head;
+  a.small = m->small;
+  a.head = m->head->view();
+  a.kv = m->kv->v8;
+  a.ll = m->mega_ll;
+  a.logits = logits;
+  a.ids = ids;
+  a.first_token = first_token;
+  a.pos0 = pos0;
+  a.steps = steps;
+  a.flag0 = m->mega_flag;
+  a.err = m->mega_err;
+  a.timeout_cycles = 4000000000LL;  // ~2 s at 2 GHz per wait
+  m->mega_flag += (unsigned)steps;
+  void *args[] = {&a};
+  CK(cudaLaunchCooperativeKernel((const void *)mega_decode_kernel, m->mega_grid, MK_THREADS, args, sizeof(MkSmem),
+                                 ctx->stream));
+  return LLMQ_OK;
+}
+
+// After a synchronisation: turns a recorded device-side timeout into a status.
+llmq_status mega_check(llmq_model *m) {
+  llmq_ctx *ctx = m->ctx;
+  if (!m->mega_ok) return LLMQ_OK;
+  int code = 0;
+  CK(cudaMemcpy(&code, m->mega_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code) {
+    cudaMemset(m->mega_err, 0, sizeof(int));
+    return fail(ctx, LLMQ_ERR_TIMEOUT, "persistent decode kernel: a bounded wait gave up (code " +
+                                           std::to_string(code) + ")");
+  }
+  return LLMQ_OK;
+}
+
 // One decode step (gpt2t.mojo:350-447): embedding, 12 x (LN1 + QKV, KV store
 // + attention, PROJ + residual, LN2 + FC + GELU, FCPROJ + residual), LN_f +
 // head + argmax. Token, position and step index come from m->state.
@@ -628,6 +795,10 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
     llmq_model_free(m);
     return fail(ctx, LLMQ_ERR_CUDA, std::string("model alloc: ") + cudaGetErrorString(e));
   }
+  if ((st = mega_setup(m)) != LLMQ_OK) {
+    llmq_model_free(m);
+    return st;
+  }
   *out = m;
   return LLMQ_OK;
 }
@@ -647,20 +818,32 @@ llmq_status llmq_model_free(llmq_model *m) {
   if (m->state) cudaFree(m->state);
   if (m->state_host) cudaFreeHost(m->state_host);
   if (m->ids_host) cudaFreeHost(m->ids_host);
+  if (m->mega_stream) cudaFree(m->mega_stream);
+  if (m->mega_base) cudaFree(m->mega_base);
+  if (m->mega_chunks) cudaFree(m->mega_chunks);
+  if (m->mega_ll) cudaFree(m->mega_ll);
+  if (m->mega_err) cudaFree(m->mega_err);
   delete m;
   return LLMQ_OK;
 }
 
-llmq_status llmq_model_use_graph(llmq_model *m, int enable) {
+llmq_status llmq_model_set_mode(llmq_model *m, int mode) {
   if (!m) return LLMQ_ERR_INVALID;
-  m->use_graph = enable;
+  if (mode != LLMQ_MODE_EAGER && mode != LLMQ_MODE_GRAPH && mode != LLMQ_MODE_PERSISTENT)
+    return fail(m->ctx, LLMQ_ERR_INVALID, "unknown mode");
+  if (mode == LLMQ_MODE_PERSISTENT && !m->mega_ok)
+    return fail(m->ctx, LLMQ_ERR_UNSUPPORTED, "the persistent decode kernel runs int4-g32 A16 layers, a per-channel "
+                                              "int8 A16 head and the QuantKV[8] cache");
+  m->mode = mode;
   return LLMQ_OK;
 }
+
+int llmq_model_mode(const llmq_model *m) { return m ? m->mode : -1; }
 
 static llmq_status run_decode_step(llmq_model *m) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
-  if (!m->use_graph) return enqueue_decode_step(m, s);
+  if (m->mode == LLMQ_MODE_EAGER) return enqueue_decode_step(m, s);
   if (!m->exec) {
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     llmq_status st = enqueue_decode_step(m, s);
@@ -678,25 +861,15 @@ static llmq_status run_decode_step(llmq_model *m) {
   return LLMQ_OK;
 }
 
-static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0);
-
-// Prompt through the model; ends with ids[0] = argmax of the last token's
-// logits, state = {token: ids[0], pos: n_prompt, step: 1}.
-static llmq_status run_prompt(llmq_model *m, const int *prompt, int T, int pos0) {
-  llmq_ctx *ctx = m->ctx;
-  cudaStream_t s = ctx->stream;
-  if (T == 1) {
-    *m->state_host = DecodeState{};
-    m->state_host->token = prompt[0];
-    m->state_host->pos = pos0;
-    CK(cudaMemcpyAsync(m->state, m->state_host, sizeof(DecodeState), cudaMemcpyHostToDevice, s));
-    return run_decode_step(m);
-  }
-  CK(cudaMemcpyAsync(m->tokens, prompt, (size_t)T * 4, cudaMemcpyHostToDevice, s));
-  return run_prompt_tail(m, T, pos0);
+__global__ void init_state_kernel(DecodeState *st, const int *tokens, int pos0) {
+  st->token = tokens[0];
+  st->pos = pos0;
+  st->step = 0;
+  st->ticket = 0;
 }
 
-// Prefill of the T tokens already in m->tokens, then the head's argmax.
+// Prefill of the T tokens in m->tokens at positions pos0.., then the head's
+// argmax: ids[0], state = {token: ids[0], pos: pos0 + T, step: 1}.
 static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
@@ -719,22 +892,52 @@ static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0) {
   return LLMQ_OK;
 }
 
+// `steps` greedy steps from the T tokens in m->tokens at positions pos0..:
+// ids into m->ids[0, steps), the last step's logits into m->logits (always
+// in the graph and eager modes; with want_logits in the persistent mode).
+// Asynchronous on the context's stream.
+static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits) {
+  llmq_ctx *ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok;
+  llmq_status st;
+  if (T == 1) {
+    if (pers) return run_mega(m, m->tokens, pos0, steps, m->ids, want_logits ? m->logits : nullptr);
+    init_state_kernel<<<1, 1, 0, s>>>(m->state, m->tokens, pos0);
+    CKL();
+    for (int i = 0; i < steps; i++)
+      if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+    return LLMQ_OK;
+  }
+  if ((st = run_prompt_tail(m, T, pos0)) != LLMQ_OK) return st;
+  if (steps == 1) return LLMQ_OK;
+  if (pers) return run_mega(m, &m->state->token, pos0 + T, steps - 1, m->ids + 1, want_logits ? m->logits : nullptr);
+  for (int i = 1; i < steps; i++)
+    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  return LLMQ_OK;
+}
+
+static llmq_status check_tokens(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T) {
+  for (int i = 0; i < T; i++)
+    if (tokens[i] < 0 || tokens[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
+  return LLMQ_OK;
+}
+
 llmq_status llmq_model_forward(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T, int pos0, float *logits_dev,
                                int *argmax_host) {
   if (!ctx || !m || !tokens || T <= 0 || pos0 < 0 || pos0 + T > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad tokens or positions");
-  for (int i = 0; i < T; i++)
-    if (tokens[i] < 0 || tokens[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
-  CK(cudaSetDevice(ctx->device));
-  CK(cudaStreamSynchronize(ctx->stream));
-  llmq_status st = run_prompt(m, tokens, T, pos0);
+  llmq_status st = check_tokens(ctx, m, tokens, T);
   if (st != LLMQ_OK) return st;
+  CK(cudaSetDevice(ctx->device));
   cudaStream_t s = ctx->stream;
-  if (logits_dev) CK(cudaMemcpyAsync(logits_dev, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, s));
-  if (argmax_host) {
-    CK(cudaMemcpyAsync(m->ids_host, m->ids, 4, cudaMemcpyDeviceToHost, s));
-  }
   CK(cudaStreamSynchronize(s));
+  CK(cudaMemcpyAsync(m->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, s));
+  if ((st = run_generation(m, T, pos0, 1, logits_dev != nullptr)) != LLMQ_OK) return st;
+  if (logits_dev) CK(cudaMemcpyAsync(logits_dev, m->logits, (size_t)m->V * 4, cudaMemcpyDeviceToDevice, s));
+  CK(cudaMemcpyAsync(m->ids_host, m->ids, 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if ((st = mega_check(m)) != LLMQ_OK) return st;
   if (argmax_host) *argmax_host = m->ids_host[0];
   return LLMQ_OK;
 }
@@ -762,26 +965,18 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n
   if (!ctx || !m || !prompt || !out_ids || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
       n_prompt + steps - 1 > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
-  for (int i = 0; i < n_prompt; i++)
-    if (prompt[i] < 0 || prompt[i] >= m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
-  CK(cudaSetDevice(ctx->device));
-  CK(cudaStreamSynchronize(ctx->stream));
-  llmq_status st = run_prompt(m, prompt, n_prompt, 0);
+  llmq_status st = check_tokens(ctx, m, prompt, n_prompt);
   if (st != LLMQ_OK) return st;
-  for (int i = 1; i < steps; i++)
-    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  CK(cudaSetDevice(ctx->device));
   cudaStream_t s = ctx->stream;
+  CK(cudaStreamSynchronize(s));
+  CK(cudaMemcpyAsync(m->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, s));
+  if ((st = run_generation(m, n_prompt, 0, steps, false)) != LLMQ_OK) return st;
   CK(cudaMemcpyAsync(m->ids_host, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, s));
   CK(cudaStreamSynchronize(s));
+  if ((st = mega_check(m)) != LLMQ_OK) return st;
   std::memcpy(out_ids, m->ids_host, (size_t)steps * 4);
   return LLMQ_OK;
-}
-
-__global__ void init_state_kernel(DecodeState *st, const int *prompt, int n_prompt) {
-  st->token = prompt[0];
-  st->pos = 0;
-  st->step = 0;
-  st->ticket = 0;
 }
 
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
@@ -791,19 +986,17 @@ llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
   CK(cudaSetDevice(ctx->device));
   cudaStream_t s = ctx->stream;
-  llmq_status st;
-  if (n_prompt == 1) {
-    init_state_kernel<<<1, 1, 0, s>>>(m->state, prompt_dev, 1);
-    CKL();
-    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
-  } else {
-    CK(cudaMemcpyAsync(m->tokens, prompt_dev, (size_t)n_prompt * 4, cudaMemcpyDeviceToDevice, s));
-    if ((st = run_prompt_tail(m, n_prompt, 0)) != LLMQ_OK) return st;
-  }
-  for (int i = 1; i < steps; i++)
-    if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+  CK(cudaMemcpyAsync(m->tokens, prompt_dev, (size_t)n_prompt * 4, cudaMemcpyDeviceToDevice, s));
+  llmq_status st = run_generation(m, n_prompt, 0, steps, false);
+  if (st != LLMQ_OK) return st;
   CK(cudaMemcpyAsync(ids_dev, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToDevice, s));
   return LLMQ_OK;
+}
+
+llmq_status llmq_model_check(llmq_ctx *ctx, llmq_model *m) {
+  if (!ctx || !m) return LLMQ_ERR_INVALID;
+  CK(cudaStreamSynchronize(ctx->stream));
+  return mega_check(m);
 }
 
 }  // extern "C"

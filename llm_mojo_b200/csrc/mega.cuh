@@ -1,0 +1,785 @@
+// Persistent decode kernel: a whole greedy generation (many tokens) in one
+// cooperative launch on sm_100a, one CTA per SM.
+//
+// Why: a decode step is ~60 dependent operations (per layer: LayerNorm +
+// QKV GEMV, KV store + attention, PROJ GEMV, LayerNorm + FC GEMV, FCPROJ
+// GEMV; then LN_f + head GEMV + argmax), each of which needs the whole
+// previous activation vector (LayerNorm and the int16 quantization of every
+// matmul input take a max or sums over all of it). Launched one by one, each
+// costs a launch and a cold start; here every CTA stays resident and
+//   - streams its own slice of every weight matrix, in the order it will use
+//     them, from a per-CTA packed copy in HBM into a shared-memory ring with
+//     cp.async.bulk (a producer warp, mbarrier completion), running ahead of
+//     the computation across layers and tokens, so weights never sit on the
+//     critical path;
+//   - exchanges activations through global buffers of 8-byte words that
+//     hold a float and a 32-bit flag (the token's sequence number): a writer
+//     publishes a value and its flag with one single-copy-atomic store, and a
+//     reader spins on the words it needs until their flags match. This is
+//     both the data transfer and the synchronisation; there is no separate
+//     grid barrier.
+// Every spin (ring slots, flags) is bounded by a cycle budget; on timeout
+// the kernel records an error code, waits (bounded) for its own bulk copies
+// in flight, and returns.
+//
+// The arithmetic of each phase is that of the one-token kernels
+// (gemv_a16.cuh, attention.cuh): bit-identical to the reference's.
+#pragma once
+
+#include "attention.cuh"
+#include "gemv_a16.cuh"
+
+namespace llmq {
+
+constexpr int MK_CONSUMERS = 256;
+constexpr int MK_THREADS = MK_CONSUMERS + 32;  // + producer warp
+constexpr int MK_NSLOT = 7;
+constexpr int MK_SLOT = 24704;  // bytes per ring slot: one chunk (largest: 32 head rows)
+constexpr int MK_HEAD_TILE = 32;
+constexpr int MK_LANES = 4096;  // int32 lane sums held at once
+constexpr int MK_MAX_CHUNKS = 64;  // chunks per CTA per token
+
+enum { PH_QKV = 0, PH_PROJ = 1, PH_FC = 2, PH_FCPROJ = 3, PH_HEAD = 4 };
+
+// One chunk of a CTA's weight stream: rows [r0, r1) of one matrix, as codes
+// (rows * row_bytes), then float16 scales, then zero points, each padded to
+// 16 bytes.
+struct MkChunk {
+  int kind, layer, r0, r1;
+  int off, bytes, scale_off, zp_off;
+};
+
+struct MegaArgs {
+  const uint8_t *stream;         // packed weight streams of all CTAs
+  const long long *stream_base;  // [grid] offset of CTA c's stream
+  const MkChunk *chunks;         // [grid][nchunks]
+  int nchunks;                   // chunks per CTA per token
+  int n_layer, C, V, n_head;
+  const float *small;            // float32 parameters in Model.small order
+  WeightView head;               // the tied wte / head in its stored layout (embedding lookups)
+  KV8View kv;
+  unsigned long long *ll;        // exchange buffers (see MkLL)
+  float *logits;                 // [V] last step's logits, or null
+  int *ids;                      // [steps] produced ids
+  const int *first_token;        // device: the token of the first step
+  int pos0;                      // its position
+  int steps;
+  unsigned flag0;                // flag of the first step (steps use flag0, flag0 + 1, ...)
+  int *err;                      // device error word (0 = ok)
+  long long timeout_cycles;
+};
+
+// Offsets (in 8-byte words) of the exchange buffers inside MegaArgs::ll.
+struct MkLL {
+  int C, L, grid;
+  __host__ __device__ MkLL(int c, int l, int g) : C(c), L(l), grid(g) {}
+  __host__ __device__ long long qkv(int l) const { return (long long)l * 9 * C; }          // 3C
+  __host__ __device__ long long att(int l) const { return (long long)l * 9 * C + 3 * C; }  // C
+  __host__ __device__ long long xmid(int l) const { return (long long)l * 9 * C + 4 * C; } // C
+  __host__ __device__ long long fc(int l) const { return (long long)l * 9 * C + 5 * C; }   // 4C
+  __host__ __device__ long long xout(int l) const { return (long long)L * 9 * C + (long long)l * C; }
+  __host__ __device__ long long part() const { return (long long)L * 10 * C; }           // 2 * grid
+  __host__ __device__ long long total() const { return part() + 2LL * grid; }
+};
+
+// --- PTX helpers -------------------------------------------------------------
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(unsigned long long *b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long *b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *b, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, unsigned long long *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_CONSUMERS) : "memory"); }
+
+__device__ __forceinline__ unsigned long long ll_pack(float v, unsigned flag) {
+  return ((unsigned long long)flag << 32) | (unsigned long long)__float_as_uint(v);
+}
+
+// --- shared memory ---------------------------------------------------------
+
+struct MkSmem {
+  unsigned long long full[MK_NSLOT], empty[MK_NSLOT];
+  volatile int abort;        // set by a consumer that timed out
+  int token;
+  float red[64];
+  float xfull[768];          // the residual stream x of this token (all 768)
+  float xf[3072];            // the current matmul input (after LayerNorm)
+  int16_t xq[3072];          // its int16 codes (permuted for BLOCKED)
+  int xs[192];               // BLOCKED lane sums (as float) / per-channel pair sums (int)
+  int lanes[MK_LANES];       // int32 lane sums of the current rows
+  float att_sc[1024];        // attention scores / exponentials
+  float att_ps[1024];        // p * vs
+  float att_q[64];
+  int8_t att_k[64], att_v[64];
+  float best_v[8];
+  int best_i[8];
+  float bias[64];            // the current phase's biases for this CTA's rows
+  MkChunk chunks[MK_MAX_CHUNKS];
+  alignas(128) uint8_t ring[MK_NSLOT][MK_SLOT];
+};
+
+// Bounded spin helper: returns false (and records the error) once the
+// budget is spent.
+__device__ __forceinline__ bool mk_alive(const MegaArgs &a, MkSmem &sm, long long t0, int code) {
+  if (sm.abort) return false;
+  if (clock64() - t0 > a.timeout_cycles) {
+    sm.abort = 1;
+    atomicCAS(a.err, 0, code);
+    return false;
+  }
+  return true;
+}
+
+// Reads n exchange words with flag `flag` into dst (all consumer threads).
+__device__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsigned long long *src, int n, unsigned flag,
+                        float *dst, int code) {
+  long long t0 = clock64();
+  for (int base = threadIdx.x; base < n; base += MK_CONSUMERS * 4) {
+    unsigned pending = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      if (base + j * MK_CONSUMERS < n) pending |= 1u << j;
+    while (pending) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (pending & (1u << j)) {
+          int i = base + j * MK_CONSUMERS;
+          unsigned long long v = ld_relaxed_u64(src + i);
+          if ((unsigned)(v >> 32) == flag) {
+            dst[i] = __uint_as_float((unsigned)v);
+            pending &= ~(1u << j);
+          }
+        }
+      }
+      if (pending && !mk_alive(a, sm, t0, code)) break;
+    }
+  }
+  consumers_sync();
+  return !sm.abort;
+}
+
+// LayerNorm parameters of this thread's 3 elements (C = 768), loaded ahead of
+// the wait for the activations so that their latency overlaps it.
+struct LnParams {
+  float w[3], b[3];
+};
+__device__ __forceinline__ LnParams ln_load(const float *w, const float *b) {
+  LnParams p;
+#pragma unroll
+  for (int j = 0; j < 3; j++) {
+    p.w[j] = __ldg(w + threadIdx.x + j * MK_CONSUMERS);
+    p.b[j] = __ldg(b + threadIdx.x + j * MK_CONSUMERS);
+  }
+  return p;
+}
+
+// LayerNorm of sm.xf[0..768) in place (kernels.mojo:179-197).
+__device__ void mk_layernorm(MkSmem &sm, const LnParams &pr) {
+  const int C = 768;
+  if (threadIdx.x < 32) {
+    int l = threadIdx.x & 15;
+    float s = 0.0f;
+    for (int i = 0; i < C; i += 16) s = s + sm.xf[i + l];
+    float mean = tree16_warp(s) / (float)C;
+    float sq = 0.0f;
+    for (int i = 0; i < C; i += 16) {
+      float d = sm.xf[i + l] - mean;
+      sq = sq + d * d;
+    }
+    float var = tree16_warp(sq) / (float)C;
+    if (threadIdx.x == 0) {
+      sm.red[40] = mean;
+      sm.red[41] = 1.0f / sqrtf(var + 1e-5f);
+    }
+  }
+  consumers_sync();
+  float mean = sm.red[40], rstd = sm.red[41];
+#pragma unroll
+  for (int j = 0; j < 3; j++) {
+    int i = threadIdx.x + j * MK_CONSUMERS;
+    float n = (sm.xf[i] - mean) * rstd;
+    sm.xf[i] = n * pr.w[j] + pr.b[j];
+  }
+  consumers_sync();
+}
+
+// quantize_rows of sm.xf[0..IN) into sm.xq (BLOCKED lane order and lane
+// sums when blocked, natural order and per-lane pair sums otherwise).
+// Returns sx.
+__device__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < IN; i += MK_CONSUMERS) mx = fmaxf(mx, fabsf(sm.xf[i]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = mx;
+  consumers_sync();
+  mx = sm.red[0];
+#pragma unroll
+  for (int w = 1; w < MK_CONSUMERS / 32; w++) mx = fmaxf(mx, sm.red[w]);
+  float s = mx / 32767.0f;
+  if (s == 0.0f) s = 1.0f;
+  float inv = 1.0f / s;
+  if (blocked) {
+    for (int col = threadIdx.x; col < IN; col += MK_CONSUMERS) {
+      int blk = col >> 8, w = col & 255, e = w & 31, p = e >> 1;
+      int lane = (w >> 5) + 8 * (p >> 3);
+      sm.xq[blk * 256 + (p & 7) * 32 + 2 * lane + (e & 1)] = (int16_t)roundf(sm.xf[col] * inv);
+    }
+    for (int i = threadIdx.x; i < IN / 16; i += MK_CONSUMERS) {
+      int blk = i >> 4, lane = i & 15;
+      int base = blk * 256 + (lane & 7) * 32 + (lane >> 3) * 16;
+      int sum = 0;
+      for (int e = 0; e < 16; e++) sum += (int)roundf(sm.xf[base + e] * inv);
+      ((float *)sm.xs)[i] = (float)sum;
+    }
+  } else {
+    for (int i = threadIdx.x; i < IN; i += MK_CONSUMERS) sm.xq[i] = (int16_t)roundf(sm.xf[i] * inv);
+    consumers_sync();
+    // per-channel rows (one group): sums of each lane's pairs over the row.
+    if (threadIdx.x < 16) {
+      int L = threadIdx.x, sum = 0;
+      for (int k0 = 0; k0 < IN; k0 += 32) sum += (int)sm.xq[k0 + 2 * L] + (int)sm.xq[k0 + 2 * L + 1];
+      sm.xs[L] = sum;
+    }
+  }
+  consumers_sync();
+  return s;
+}
+
+// BLOCKED int4-g32 rows [0, R) of the chunk in `slot` against sm.xq: the
+// float results of dot_row_i16 for each row, delivered to `emit(r, dot)` by
+// the thread with q == 0 of the row.
+template <typename Emit>
+__device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit) {
+  const int R = ch.r1 - ch.r0, nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
+  const int *xp32 = (const int *)sm.xq;
+  const float *xs = (const float *)sm.xs;
+  const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
+  const uint8_t *zpp = slot + ch.zp_off;
+  // rows per pass: as many as lanes[] holds, at most 64 (one float pass)
+  const int pass = MK_LANES / (nblk * 16) < 64 ? MK_LANES / (nblk * 16) : 64;
+  for (int rbase = 0; rbase < R; rbase += pass) {
+    const int rows = R - rbase < pass ? R - rbase : pass;
+    // integer phase: items (row, block, q)
+    const int items = rows * nblk * 4;
+    for (int it = threadIdx.x; it < items; it += MK_CONSUMERS) {
+      int q = it & 3, rb = it >> 2, b = rb % nblk, r = rb / nblk;
+      const uint32_t *wp = (const uint32_t *)(slot + (size_t)(rbase + r) * row_bytes + b * 128) + q;
+      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+      const int rot = rb & 7;
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        int s = (j + rot) & 7;
+        uint32_t wv = wp[4 * s];
+        uint32_t lo = wv & 0x0F0F0F0Fu, hi = (wv >> 4) & 0x0F0F0F0Fu;
+        const int *xv = xp32 + b * 128 + s * 16;
+        int2 x01 = *(const int2 *)(xv + 2 * q);
+        int2 x89 = *(const int2 *)(xv + 2 * q + 8);
+        a0 = dp2a_lo_su(x01.x, lo, a0);
+        a1 = dp2a_hi_su(x01.y, lo, a1);
+        a2 = dp2a_lo_su(x89.x, hi, a2);
+        a3 = dp2a_hi_su(x89.y, hi, a3);
+      }
+      int *ln = sm.lanes + (r * nblk + b) * 16;
+      ln[2 * q] = a0;
+      ln[2 * q + 1] = a1;
+      ln[2 * q + 8] = a2;
+      ln[2 * q + 9] = a3;
+    }
+    consumers_sync();
+    // float phase: thread (row, q), 64 rows per pass.
+    {
+      const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
+      const int rr = r < rows ? r : 0;
+      float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int b = 0; b < nblk; b++) {
+        int g0 = (rbase + rr) * gpr + b * 8;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          int L = (j < 2) ? (2 * q + j) : (2 * q + 8 + (j - 2));
+          float zp = (float)zpp[g0 + (L & 7)];
+          float sc = half_bits_to_float(scl[g0 + (L & 7)]);
+          f[j] = fmaf((float)sm.lanes[(rr * nblk + b) * 16 + L] - zp * xs[b * 16 + L], sc, f[j]);
+        }
+      }
+      float a0 = f[0] + f[2], a1 = f[1] + f[3];
+      a0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 2);
+      a1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 2);
+      float c0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 1);
+      float c1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+      float dot = c0 + c1;
+      if (q == 0 && r < rows) emit(rbase + r, dot);
+    }
+    consumers_sync();
+  }
+}
+
+// Per-channel int8 rows (the head) of the chunk in `slot`.
+template <typename Emit>
+__device__ void mk_rows_ch8(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit) {
+  const int R = ch.r1 - ch.r0, nch = IN >> 5;
+  const int *xp32 = (const int *)sm.xq;
+  const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
+  const uint8_t *zpp = slot + ch.zp_off;
+  // integer phase: items (row, q, part), 2 parts of nch/2 chunks
+  {
+    const int q = threadIdx.x & 3, r = (threadIdx.x >> 2) & 31, p = threadIdx.x >> 7;
+    int a[4] = {0, 0, 0, 0};
+    if (r < R) {
+      const uint8_t *rp = slot + (size_t)r * IN;
+      const int c0 = p * (nch / 2), c1 = (p + 1) * (nch / 2);
+      for (int cc = c0; cc < c1; cc++) {
+        int c = c0 + ((cc - c0 + r) % (c1 - c0));
+        uint2 v = *(const uint2 *)(rp + c * 32 + 8 * q);
+        int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
+        a[0] = dp2a_lo_su(xv.x, v.x, a[0]);
+        a[1] = dp2a_hi_su(xv.y, v.x, a[1]);
+        a[2] = dp2a_lo_su(xv.z, v.y, a[2]);
+        a[3] = dp2a_hi_su(xv.w, v.y, a[3]);
+      }
+    }
+    int *ln = sm.lanes + (p * 32 + r) * 16 + 4 * q;
+#pragma unroll
+    for (int j = 0; j < 4; j++) ln[j] = a[j];
+  }
+  consumers_sync();
+  if (threadIdx.x < 128) {
+    const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
+    const int rr = r < R ? r : 0;
+    int zp = zpp[rr];
+    float sc = half_bits_to_float(scl[rr]);
+    float f[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int L = 4 * q + j;
+      int acc = sm.lanes[rr * 16 + L] + sm.lanes[(32 + rr) * 16 + L];
+      acc = (int)((unsigned)acc - (unsigned)(zp * sm.xs[L]));
+      f[j] = fmaf((float)acc, sc, 0.0f);
+    }
+    // halving tree (lanes 4q..4q+3 in thread q of 4)
+    float b[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) b[j] = f[j] + __shfl_xor_sync(0xffffffffu, f[j], 2);
+#pragma unroll
+    for (int j = 0; j < 4; j++) b[j] = b[j] + __shfl_xor_sync(0xffffffffu, b[j], 1);
+    float dot = (b[0] + b[2]) + (b[1] + b[3]);
+    if (q == 0 && r < R) emit(r, dot);
+  }
+  consumers_sync();
+}
+
+// Attention phase of head h (QuantKV[8]): store the token's key and value,
+// then attend over positions 0..pos (attend_float_one, kvcache.mojo:113-150).
+// Returns false on timeout.
+__device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int l, int h, int pos, unsigned flag) {
+  const int HS = a.kv.head_dim, C = a.C;
+  const int tid = threadIdx.x;
+  // poll q, k, v of head h (3 x 64 words)
+  {
+    long long t0 = clock64();
+    if (tid < 3 * HS) {
+      int which = tid / HS, d = tid % HS;
+      const unsigned long long *src = a.ll + ll.qkv(l) + which * C + h * HS + d;
+      unsigned long long v;
+      while (true) {
+        v = ld_relaxed_u64(src);
+        if ((unsigned)(v >> 32) == flag) break;
+        if (!mk_alive(a, sm, t0, 2)) break;
+      }
+      float x = __uint_as_float((unsigned)v);
+      if (which == 0) sm.att_q[d] = x;
+      else sm.xf[(which - 1) * 64 + d] = x;
+    }
+    consumers_sync();
+    if (sm.abort) return false;
+  }
+  // store: per-head int8 quantization of k and v (QuantKV.quantize).
+  const size_t sl = ((size_t)l * a.kv.max_t + pos) * a.kv.n_head + h;
+  if (tid < 64) {
+    for (int which = 0; which < 2; which++) {
+      float x = sm.xf[which * 64 + tid];
+      float m = fabsf(x);
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if ((tid & 31) == 0) sm.red[48 + which * 2 + (tid >> 5)] = m;
+    }
+  }
+  consumers_sync();
+  if (tid < 64) {
+    for (int which = 0; which < 2; which++) {
+      float m = fmaxf(sm.red[48 + which * 2], sm.red[49 + which * 2]);
+      float s = m / 127.0f;
+      if (s == 0.0f) s = 1.0f;
+      float inv = 1.0f / s;
+      int8_t code = (int8_t)roundf(sm.xf[which * 64 + tid] * inv);
+      if (which == 0) {
+        sm.att_k[tid] = code;
+        a.kv.k[sl * HS + tid] = code;
+        if (tid == 0) a.kv.ks[sl] = s;
+      } else {
+        sm.att_v[tid] = code;
+        a.kv.v[sl * HS + tid] = code;
+        if (tid == 0) a.kv.vs[sl] = s;
+      }
+    }
+  }
+  consumers_sync();
+  const int npos = pos + 1;
+  const float scale = 1.0f / sqrtf((float)HS);
+  float mx = -__int_as_float(0x7f800000);
+  for (int s = tid; s < npos; s += MK_CONSUMERS) {
+    size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
+    const int8_t *kp = (s == pos) ? sm.att_k : a.kv.k + ss * HS;
+    float ksc = (s == pos) ? a.kv.ks[ss] : a.kv.ks[ss];
+    float d[16];
+#pragma unroll
+    for (int k = 0; k < 16; k++) d[k] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 64; i += 16) {
+      int4 kv4 = *(const int4 *)(kp + i);
+      const int8_t *kb = (const int8_t *)&kv4;
+#pragma unroll
+      for (int k = 0; k < 16; k++) d[k] = d[k] + sm.att_q[i + k] * (float)kb[k];
+    }
+#pragma unroll
+    for (int k = 0; k < 8; k++) d[k] = d[k] + d[k + 8];
+#pragma unroll
+    for (int k = 0; k < 4; k++) d[k] = d[k] + d[k + 4];
+    d[0] = d[0] + d[2];
+    d[1] = d[1] + d[3];
+    float v = ((d[0] + d[1]) * ksc) * scale;
+    sm.att_sc[s] = v;
+    mx = fmaxf(mx, v);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((tid & 31) == 0) sm.red[tid >> 5] = mx;
+  consumers_sync();
+  mx = sm.red[0];
+#pragma unroll
+  for (int w = 1; w < MK_CONSUMERS / 32; w++) mx = fmaxf(mx, sm.red[w]);
+  for (int s = tid; s < npos; s += MK_CONSUMERS) sm.att_sc[s] = lm_expf(sm.att_sc[s] - mx);
+  consumers_sync();
+  if (tid == 0) {
+    float total = 0.0f;
+    for (int s = 0; s < npos; s++) total += sm.att_sc[s];
+    sm.red[36] = total;
+  }
+  consumers_sync();
+  const float total = sm.red[36];
+  for (int s = tid; s < npos; s += MK_CONSUMERS) {
+    size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
+    float p = sm.att_sc[s] / total;
+    sm.att_ps[s] = p * a.kv.vs[ss];
+  }
+  consumers_sync();
+  if (tid < HS) {
+    const int d = tid;
+    const size_t stride = (size_t)a.kv.n_head * HS;
+    const int8_t *vp = a.kv.v + ((size_t)l * a.kv.max_t * a.kv.n_head + h) * HS + d;
+    float acc = 0.0f;
+    int s = 0;
+    for (; s + 4 <= pos; s += 4) {
+      float v0 = (float)vp[(size_t)s * stride], v1 = (float)vp[(size_t)(s + 1) * stride];
+      float v2 = (float)vp[(size_t)(s + 2) * stride], v3 = (float)vp[(size_t)(s + 3) * stride];
+      acc = fmaf(sm.att_ps[s], v0, acc);
+      acc = fmaf(sm.att_ps[s + 1], v1, acc);
+      acc = fmaf(sm.att_ps[s + 2], v2, acc);
+      acc = fmaf(sm.att_ps[s + 3], v3, acc);
+    }
+    for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride], acc);
+    acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
+    st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
+  }
+  return true;
+}
+
+// Loads the biases of rows [r0, r0 + n) into sm.bias (n <= 64).
+__device__ __forceinline__ void mk_bias_load(MkSmem &sm, const float *bias, int r0, int n) {
+  if (threadIdx.x < n) sm.bias[threadIdx.x] = __ldg(bias + r0 + threadIdx.x);
+}
+
+__global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  MkSmem &sm = *reinterpret_cast<MkSmem *>(smem_raw);
+  const int tid = threadIdx.x;
+  const int cta = blockIdx.x, grid = gridDim.x;
+  const MkLL ll(a.C, a.n_layer, grid);
+  const uint8_t *stream = a.stream + a.stream_base[cta];
+  const long long total_chunks = (long long)a.nchunks * a.steps;
+
+  for (int i = tid; i < a.nchunks; i += MK_THREADS) sm.chunks[i] = a.chunks[(size_t)cta * a.nchunks + i];
+  if (tid == 0) {
+    for (int i = 0; i < MK_NSLOT; i++) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], 1);
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  if (tid >= MK_CONSUMERS) {
+    // ---------------- producer warp ----------------
+    if (tid != MK_CONSUMERS) return;
+    long long issued = 0;
+    for (long long seq = 0; seq < total_chunks; seq++) {
+      const int slot = (int)(seq % MK_NSLOT);
+      if (seq >= MK_NSLOT) {
+        const unsigned par = (unsigned)(((seq / MK_NSLOT) - 1) & 1);
+        long long t0 = clock64();
+        bool ok = true;
+        while (!mbar_try_wait(&sm.empty[slot], par)) {
+          if (sm.abort || clock64() - t0 > a.timeout_cycles) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+      }
+      const MkChunk &ch = sm.chunks[seq % a.nchunks];
+      mbar_expect_tx(&sm.full[slot], (unsigned)ch.bytes);
+      bulk_g2s(sm.ring[slot], stream + ch.off, (unsigned)ch.bytes, &sm.full[slot]);
+      issued = seq + 1;
+    }
+    // On abort, wait (bounded) for every copy still in flight into the ring.
+    if (sm.abort) {
+      for (long long seq = issued > MK_NSLOT ? issued - MK_NSLOT : 0; seq < issued; seq++) {
+        const int slot = (int)(seq % MK_NSLOT);
+        const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
+        long long t1 = clock64();
+        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int C = a.C, C4 = 4 * C;
+  long long seq = 0;
+  auto slot_wait = [&](int &slot) -> bool {
+    slot = (int)(seq % MK_NSLOT);
+    const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
+    long long t0 = clock64();
+    while (!mbar_try_wait(&sm.full[slot], par)) {
+      if (!mk_alive(a, sm, t0, 1)) return false;
+    }
+    return true;
+  };
+  auto slot_release = [&](int slot) {
+    consumers_sync();
+    if (tid == 0) mbar_arrive(&sm.empty[slot]);
+    seq++;
+  };
+
+  if (tid == 0) {
+    int t0 = *a.first_token;
+    if (t0 < 0 || t0 >= a.V) {
+      atomicCAS(a.err, 0, 9);
+      t0 = 0;
+    }
+    sm.token = t0;
+  }
+  consumers_sync();
+  int token = sm.token;
+  const float *wpe = a.small + (size_t)a.n_layer * 13 * C;
+  const float *lnf = wpe + (size_t)1024 * C;
+
+  for (int step = 0; step < a.steps; step++) {
+    const unsigned flag = a.flag0 + (unsigned)step;
+    const int pos = a.pos0 + step;
+    // embedding of the token (every CTA, the whole row)
+    {
+      const int gpr = a.head.cols / a.head.group;
+      for (int i = tid; i < C; i += MK_CONSUMERS) {
+        size_t gi = (size_t)token * gpr + i / a.head.group;
+        float s = half_bits_to_float(a.head.scale[gi]);
+        float v = (float)(code_at(a.head, token, i) - (int)a.head.zp[gi]) * s;
+        sm.xfull[i] = v + wpe[(size_t)pos * C + i];
+      }
+      consumers_sync();
+    }
+    int ci = 0;  // chunk index within the token
+    for (int l = 0; l < a.n_layer; l++) {
+      const float *vec = a.small + (size_t)l * 13 * C;
+      // ---- A: LN1 + QKV ----
+      {
+        const MkChunk ch = sm.chunks[ci++];
+        LnParams lp = ln_load(vec, vec + C);
+        mk_bias_load(sm, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
+        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) return;
+        for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
+        consumers_sync();
+        mk_layernorm(sm, lp);
+        const float sx = mk_quantize(sm, C, true);
+        int slot;
+        if (!slot_wait(slot)) return;
+        unsigned long long *dst = a.ll + ll.qkv(l);
+        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
+          float v = dot * sx + sm.bias[r];
+          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
+        });
+        slot_release(slot);
+      }
+      // ---- B: KV store + attention (CTA h for head h) ----
+      if (cta < a.n_head) {
+        if (!mk_attention(a, sm, ll, l, cta, pos, flag)) return;
+      }
+      // ---- C: PROJ + residual ----
+      {
+        const MkChunk ch = sm.chunks[ci++];
+        mk_bias_load(sm, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
+        if (!mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4)) return;
+        const float sx = mk_quantize(sm, C, true);
+        int slot;
+        if (!slot_wait(slot)) return;
+        unsigned long long *dst = a.ll + ll.xmid(l);
+        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
+          float v = dot * sx + sm.bias[r];
+          v += sm.xfull[ch.r0 + r];
+          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
+        });
+        slot_release(slot);
+      }
+      // ---- D: LN2 + FC + GELU ----
+      {
+        const MkChunk ch = sm.chunks[ci++];
+        LnParams lp = ln_load(vec + 6 * C, vec + 7 * C);
+        mk_bias_load(sm, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
+        if (!mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5)) return;
+        for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
+        consumers_sync();
+        mk_layernorm(sm, lp);
+        const float sx = mk_quantize(sm, C, true);
+        int slot;
+        if (!slot_wait(slot)) return;
+        unsigned long long *dst = a.ll + ll.fc(l);
+        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
+          float v = dot * sx + sm.bias[r];
+          v = gelu(v);
+          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
+        });
+        slot_release(slot);
+      }
+      // ---- E: FCPROJ + residual ----
+      {
+        const MkChunk ch = sm.chunks[ci++];
+        mk_bias_load(sm, vec + 12 * C, ch.r0, ch.r1 - ch.r0);
+        if (!mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6)) return;
+        const float sx = mk_quantize(sm, C4, true);
+        int slot;
+        if (!slot_wait(slot)) return;
+        unsigned long long *dst = a.ll + ll.xout(l);
+        mk_rows_blk4(sm, sm.ring[slot], ch, C4, [&](int r, float dot) {
+          float v = dot * sx + sm.bias[r];
+          v += sm.xfull[ch.r0 + r];
+          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
+        });
+        slot_release(slot);
+      }
+    }
+    // ---- H: LN_f + head + argmax ----
+    LnParams lp = ln_load(lnf, lnf + C);
+    if (!mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7)) return;
+    mk_layernorm(sm, lp);
+    const float sx = mk_quantize(sm, C, false);
+    float bv = -__int_as_float(0x7f800000);
+    int bi = 0x7fffffff;
+    for (; ci < a.nchunks; ci++) {
+      int slot;
+      if (!slot_wait(slot)) return;
+      const MkChunk ch = sm.chunks[ci];
+      mk_rows_ch8(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
+        int o = ch.r0 + r;
+        float v = dot * sx;
+        if (a.logits) a.logits[o] = v;
+        if (better(v, o, bv, bi)) {
+          bv = v;
+          bi = o;
+        }
+      });
+      slot_release(slot);
+    }
+    // CTA argmax
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((tid & 31) == 0) {
+      sm.best_v[tid >> 5] = bv;
+      sm.best_i[tid >> 5] = bi;
+    }
+    consumers_sync();
+    if (tid == 0) {
+      for (int w = 1; w < MK_CONSUMERS / 32; w++)
+        if (better(sm.best_v[w], sm.best_i[w], bv, bi)) {
+          bv = sm.best_v[w];
+          bi = sm.best_i[w];
+        }
+      st_relaxed_u64(a.ll + ll.part() + 2 * cta, ll_pack(bv, flag));
+      st_relaxed_u64(a.ll + ll.part() + 2 * cta + 1, ((unsigned long long)flag << 32) | (unsigned)bi);
+    }
+    // ---- I: global argmax (every CTA) ----
+    if (!mk_poll(a, sm, a.ll + ll.part(), 2 * grid, flag, sm.xf, 8)) return;
+    if (tid < 32) {
+      float v = -__int_as_float(0x7f800000);
+      int i = 0x7fffffff;
+      for (int c = tid; c < grid; c += 32) {
+        float cv = sm.xf[2 * c];
+        int cidx = __float_as_int(sm.xf[2 * c + 1]);
+        if (better(cv, cidx, v, i)) {
+          v = cv;
+          i = cidx;
+        }
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        if (better(ov, oi, v, i)) {
+          v = ov;
+          i = oi;
+        }
+      }
+      if (tid == 0) {
+        if (i == 0x7fffffff) i = 0;  // every logit NaN: the scan keeps index 0
+        sm.token = i;
+        if (cta == 0) a.ids[step] = i;
+      }
+    }
+    consumers_sync();
+    token = sm.token;
+  }
+}
+
+}  // namespace llmq

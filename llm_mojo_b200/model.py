@@ -10,7 +10,7 @@ import ctypes as C
 import numpy as np
 
 from . import synth
-from ._lib import KV_INTATTN, KV_QUANT8, check, lib
+from ._lib import KV_INTATTN, KV_QUANT8, MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT, check, lib
 from .tensor import Context, QuantMatrix, parse_dtype
 
 # HEAD8_A16 (gpt2t.mojo:1231-1235): int8 per vocabulary row, integer path.
@@ -45,8 +45,16 @@ class Model:
         """Model.weight_bytes (gpt2t.mojo:312-319)."""
         return self.head.nbytes() + sum(m.nbytes() for m in self.mats) + self.small.size * 4
 
-    def use_graph(self, enable: bool):
-        check(lib().llmq_model_use_graph(self.h, int(enable)), self.ctx.h)
+    MODES = {"eager": MODE_EAGER, "graph": MODE_GRAPH, "persistent": MODE_PERSISTENT}
+
+    def set_mode(self, mode: str):
+        """'persistent' (one kernel per generation), 'graph' (a CUDA graph per
+        decode step) or 'eager' (one launch per operation)."""
+        check(lib().llmq_model_set_mode(self.h, self.MODES[mode]), self.ctx.h)
+
+    def mode(self) -> str:
+        m = lib().llmq_model_mode(self.h)
+        return {v: k for k, v in self.MODES.items()}[m]
 
     def forward(self, tokens, pos0: int, logits=None) -> int:
         """Runs tokens at positions pos0..; returns the last token's argmax and

@@ -246,10 +246,15 @@ def test_forward_all_bit_exact(torch, gpu_model, oracle_a16, golden):
     assert np.array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
-def test_graph_and_eager_steps_agree(gpu_model):
-    gpu_model.use_graph(False)
+@pytest.mark.parametrize("mode", ["eager", "graph", "persistent"])
+def test_decode_modes_agree_with_oracle(gpu_model, oracle_a16, mode):
+    """The three ways a decode step runs give the oracle's ids (and the
+    persistent kernel is the default for these formats)."""
+    assert gpu_model.mode() == "persistent"
+    want = oracle_a16.generate([50256], 24)
+    gpu_model.set_mode(mode)
     try:
-        eager = gpu_model.generate([50256], 12)
+        got = gpu_model.generate([50256], 24)
     finally:
-        gpu_model.use_graph(True)
-    assert list(eager) == list(gpu_model.generate([50256], 12))
+        gpu_model.set_mode("persistent")
+    assert list(got) == list(want)
