@@ -130,20 +130,21 @@ struct MkSmem {
   unsigned long long full[MK_NSLOT], empty[MK_NSLOT];
   volatile int abort;        // set by a consumer that timed out
   int token;
-  float red[64];
-  float xfull[768];          // the residual stream x of this token (all 768)
-  float xf[3072];            // the current matmul input (after LayerNorm)
-  int16_t xq[3072];          // its int16 codes (permuted for BLOCKED)
-  int xs[192];               // BLOCKED lane sums (as float) / per-channel pair sums (int)
-  int lanes[MK_LANES];       // int32 lane sums of the current rows
-  float att_sc[1024];        // attention scores / exponentials
-  float att_ps[1024];        // p * vs
-  float att_q[64];
-  int8_t att_k[64], att_v[64];
-  float best_v[8];
-  int best_i[8];
-  float bias[64];            // the current phase's biases for this CTA's rows
-  MkChunk chunks[MK_MAX_CHUNKS];
+  alignas(16) float red[64];
+  alignas(16) float xfull[768];     // the residual stream x of this token (all 768)
+  alignas(16) float xf[3072];       // the current matmul input (after LayerNorm)
+  alignas(16) int16_t xq[3072];     // its int16 codes (permuted for BLOCKED)
+  alignas(16) int xs[192];          // BLOCKED lane sums (as float) / per-channel pair sums (int)
+  alignas(16) int lanes[MK_LANES];  // int32 lane sums of the current rows
+  alignas(16) float att_sc[1024];   // attention scores / exponentials
+  alignas(16) float att_ps[1024];   // p * vs
+  alignas(16) float att_q[64];
+  alignas(16) int8_t att_k[64];
+  alignas(16) int8_t att_v[64];
+  alignas(16) float best_v[8];
+  alignas(16) int best_i[8];
+  alignas(16) float bias[64];       // the current phase's biases for this CTA's rows
+  alignas(16) MkChunk chunks[MK_MAX_CHUNKS];
   alignas(128) uint8_t ring[MK_NSLOT][MK_SLOT];
 };
 
