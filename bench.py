@@ -160,6 +160,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="after the timed region, run one generation with the persistent kernel's per-phase "
+                         "timers and print them (microseconds per token) to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
@@ -246,6 +249,19 @@ def main():
                 hs.append((s0, e0))
         stream.synchronize()
         head_ms = statistics.mean(s.elapsed_time(e) for s, e in hs)
+
+    if args.profile:
+        model.profile(True)
+        model.generate(PROMPT, STEPS_PER_GEN)
+        mhz = torch.cuda.get_device_properties(local).clock_rate / 1000.0 if hasattr(
+            torch.cuda.get_device_properties(local), "clock_rate") else 1965.0
+        for i, d in enumerate(model.profile_read()):
+            steps = max(1, d.pop("steps"))
+            us = {k: v / steps / mhz for k, v in d.items()}
+            tot = sum(v for k, v in us.items() if k != "ring waits")
+            print(f"[profile] CTA {'0' if i == 0 else 'grid/2'}: {tot:.1f} us/token at {mhz:.0f} MHz: " +
+                  ", ".join(f"{k} {v:.2f}" for k, v in us.items()), file=sys.stderr)
+        model.profile(False)
 
     t_max = total_ms
     e2e_avg = statistics.mean(e2e_ms)

@@ -144,6 +144,17 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, 
  * llmq_generate. */
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
                                 int *ids_dev);
+/* Per-operation timers of the persistent decode kernel, as the reference's
+ * --profile (gpt2t.mojo:121-142, print_profile :461-483): with profiling on,
+ * CTA 0 (which also runs head 0's attention) and CTA grid/2 add the SM
+ * cycles of each phase of every step to 2 x 20 counters, in this order:
+ * embed, QKV wait, QKV (LN1 + quantize + GEMV), attention (KV store +
+ * attend), PROJ wait, PROJ, FC wait, FC (LN2 + GEMV + GELU), FCPROJ wait,
+ * FCPROJ, head wait, head (LN_f + GEMV), argmax, ring-slot waits (also
+ * inside the phases), steps, then inside the phases: LayerNorm, quantize,
+ * integer dots, float epilogue. profile_read copies them (n >= 40). */
+llmq_status llmq_model_profile(llmq_ctx *ctx, llmq_model *m, int enable);
+llmq_status llmq_model_profile_read(llmq_ctx *ctx, llmq_model *m, long long *cycles_host, int n, int reset);
 /* Waits for the context's stream and reports a bounded device-side wait of
  * the model's persistent kernel that gave up (LLMQ_ERR_TIMEOUT). */
 llmq_status llmq_model_check(llmq_ctx *ctx, llmq_model *m);

@@ -58,6 +58,8 @@ SIGNATURES = {
     "llmq_generate_async": (I, [P, P, P, I, I, P]),
     "llmq_stream": (P, [P]),
     "llmq_model_check": (I, [P, P]),
+    "llmq_model_profile": (I, [P, P, I]),
+    "llmq_model_profile_read": (I, [P, P, P, I, I]),
 }
 
 _lib = None

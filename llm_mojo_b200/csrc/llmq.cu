@@ -69,6 +69,7 @@ struct llmq_model {
   unsigned long long *mega_ll = nullptr;
   int *mega_err = nullptr;
   unsigned mega_flag = 1;
+  long long *prof = nullptr;  // [2][MK_PROF] when profiling
   const float *vec(int l, int which) const {
     static const int mult[8] = {0, 1, 2, 5, 6, 7, 8, 12};
     return small + (size_t)l * 13 * C + (size_t)mult[which] * C;
@@ -636,6 +637,7 @@ llmq_status run_mega(llmq_model *m, const int *first_token, int pos0, int steps,
   a.flag0 = m->mega_flag;
   a.err = m->mega_err;
   a.timeout_cycles = 4000000000LL;  // ~2 s at 2 GHz per wait
+  a.prof = m->prof;
   m->mega_flag += (unsigned)steps;
   void *args[] = {&a};
   CK(cudaLaunchCooperativeKernel((const void *)mega_decode_kernel, m->mega_grid, MK_THREADS, args, sizeof(MkSmem),
@@ -823,6 +825,7 @@ llmq_status llmq_model_free(llmq_model *m) {
   if (m->mega_chunks) cudaFree(m->mega_chunks);
   if (m->mega_ll) cudaFree(m->mega_ll);
   if (m->mega_err) cudaFree(m->mega_err);
+  if (m->prof) cudaFree(m->prof);
   delete m;
   return LLMQ_OK;
 }
@@ -990,6 +993,29 @@ llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_
   llmq_status st = run_generation(m, n_prompt, 0, steps, false);
   if (st != LLMQ_OK) return st;
   CK(cudaMemcpyAsync(ids_dev, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToDevice, s));
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_profile(llmq_ctx *ctx, llmq_model *m, int enable) {
+  if (!ctx || !m) return LLMQ_ERR_INVALID;
+  CK(cudaSetDevice(ctx->device));
+  if (enable && !m->prof) {
+    CK(cudaMalloc(&m->prof, sizeof(long long) * 2 * MK_PROF));
+    CK(cudaMemset(m->prof, 0, sizeof(long long) * 2 * MK_PROF));
+  } else if (!enable && m->prof) {
+    CK(cudaStreamSynchronize(ctx->stream));
+    cudaFree(m->prof);
+    m->prof = nullptr;
+  }
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_profile_read(llmq_ctx *ctx, llmq_model *m, long long *cycles_host, int n, int reset) {
+  if (!ctx || !m || !cycles_host || n < 2 * MK_PROF) return fail(ctx, LLMQ_ERR_INVALID, "need 40 entries");
+  if (!m->prof) return fail(ctx, LLMQ_ERR_INVALID, "profiling is off");
+  CK(cudaStreamSynchronize(ctx->stream));
+  CK(cudaMemcpy(cycles_host, m->prof, sizeof(long long) * 2 * MK_PROF, cudaMemcpyDeviceToHost));
+  if (reset) CK(cudaMemset(m->prof, 0, sizeof(long long) * 2 * MK_PROF));
   return LLMQ_OK;
 }
 

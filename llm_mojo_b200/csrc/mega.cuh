@@ -34,8 +34,9 @@ namespace llmq {
 constexpr int MK_CONSUMERS = 256;
 constexpr int MK_THREADS = MK_CONSUMERS + 32;  // + producer warp
 constexpr int MK_NSLOT = 7;
-constexpr int MK_SLOT = 24704;  // bytes per ring slot: one chunk (largest: 32 head rows)
-constexpr int MK_HEAD_TILE = 32;
+constexpr int MK_SLOT = 18512;  // bytes per ring slot: one chunk (largest: 24 head rows)
+constexpr int MK_HEAD_TILE = 24;
+constexpr int MK_KV_STAGE = 256;  // cache positions an attention CTA stages in shared memory
 constexpr int MK_LANES = 4096;  // int32 lane sums held at once
 constexpr int MK_MAX_CHUNKS = 64;  // chunks per CTA per token
 
@@ -67,7 +68,27 @@ struct MegaArgs {
   unsigned flag0;                // flag of the first step (steps use flag0, flag0 + 1, ...)
   int *err;                      // device error word (0 = ok)
   long long timeout_cycles;
+  long long *prof;               // [2][MK_PROF] cycles per category (CTA 0 and CTA grid/2), or null
 };
+
+// Profiling categories (the reference's --profile timers, gpt2t.mojo:121-142,
+// split into the time spent waiting for the previous phase's activations and
+// the time spent computing).
+enum {
+  PF_EMBED = 0, PF_QKV_WAIT, PF_QKV, PF_ATTN, PF_PROJ_WAIT, PF_PROJ, PF_FC_WAIT, PF_FC, PF_FCPROJ_WAIT, PF_FCPROJ,
+  PF_HEAD_WAIT, PF_HEAD, PF_ARGMAX, PF_RING_WAIT, PF_STEPS,
+  // sub-phase timers (also counted in the phases above)
+  PF_LN, PF_QUANT, PF_INT, PF_FLOAT, MK_PROF = 20
+};
+
+// Adds the cycles since *t to acc[k] and restarts *t (when acc is not null).
+__device__ __forceinline__ void sub_tick(long long *acc, int k, long long &t) {
+  if (acc) {
+    long long n = clock64();
+    acc[k] += n - t;
+    t = n;
+  }
+}
 
 // Offsets (in 8-byte words) of the exchange buffers inside MegaArgs::ll.
 struct MkLL {
@@ -118,6 +139,13 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long *p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_CONSUMERS) : "memory"); }
 
 __device__ __forceinline__ unsigned long long ll_pack(float v, unsigned flag) {
@@ -141,6 +169,10 @@ struct MkSmem {
   alignas(16) float att_q[64];
   alignas(16) int8_t att_k[64];
   alignas(16) int8_t att_v[64];
+  alignas(16) int8_t kst[MK_KV_STAGE][64];  // staged key codes of positions [0, pos)
+  alignas(16) int8_t vst[MK_KV_STAGE][64];  // staged value codes
+  alignas(16) float kss[MK_KV_STAGE];       // their scales
+  alignas(16) float vss[MK_KV_STAGE];
   alignas(16) float best_v[8];
   alignas(16) int best_i[8];
   alignas(16) float bias[64];       // the current phase's biases for this CTA's rows
@@ -204,8 +236,9 @@ __device__ __forceinline__ LnParams ln_load(const float *w, const float *b) {
 }
 
 // LayerNorm of sm.xf[0..768) in place (kernels.mojo:179-197).
-__device__ void mk_layernorm(MkSmem &sm, const LnParams &pr) {
+__device__ void mk_layernorm(MkSmem &sm, const LnParams &pr, long long *pacc = nullptr) {
   const int C = 768;
+  long long t0 = clock64();
   if (threadIdx.x < 32) {
     int l = threadIdx.x & 15;
     float s = 0.0f;
@@ -231,12 +264,14 @@ __device__ void mk_layernorm(MkSmem &sm, const LnParams &pr) {
     sm.xf[i] = n * pr.w[j] + pr.b[j];
   }
   consumers_sync();
+  sub_tick(pacc, PF_LN, t0);
 }
 
 // quantize_rows of sm.xf[0..IN) into sm.xq (BLOCKED lane order and lane
 // sums when blocked, natural order and per-lane pair sums otherwise).
 // Returns sx.
-__device__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
+__device__ float mk_quantize(MkSmem &sm, int IN, bool blocked, long long *pacc = nullptr) {
+  long long t0 = clock64();
   float mx = 0.0f;
   for (int i = threadIdx.x; i < IN; i += MK_CONSUMERS) mx = fmaxf(mx, fabsf(sm.xf[i]));
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -254,11 +289,16 @@ __device__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
       int lane = (w >> 5) + 8 * (p >> 3);
       sm.xq[blk * 256 + (p & 7) * 32 + 2 * lane + (e & 1)] = (int16_t)roundf(sm.xf[col] * inv);
     }
+    consumers_sync();
+    // lane L of block blk: the 8 code pairs at blk*128 + s*16 + L
+    const int *xp32 = (const int *)sm.xq;
     for (int i = threadIdx.x; i < IN / 16; i += MK_CONSUMERS) {
-      int blk = i >> 4, lane = i & 15;
-      int base = blk * 256 + (lane & 7) * 32 + (lane >> 3) * 16;
-      int sum = 0;
-      for (int e = 0; e < 16; e++) sum += (int)roundf(sm.xf[base + e] * inv);
+      int blk = i >> 4, lane = i & 15, sum = 0;
+#pragma unroll
+      for (int st = 0; st < 8; st++) {
+        int pr = xp32[blk * 128 + st * 16 + lane];
+        sum += (int)(int16_t)(pr & 0xFFFF) + (pr >> 16);
+      }
       ((float *)sm.xs)[i] = (float)sum;
     }
   } else {
@@ -272,6 +312,7 @@ __device__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
     }
   }
   consumers_sync();
+  sub_tick(pacc, PF_QUANT, t0);
   return s;
 }
 
@@ -279,7 +320,9 @@ __device__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
 // float results of dot_row_i16 for each row, delivered to `emit(r, dot)` by
 // the thread with q == 0 of the row.
 template <typename Emit>
-__device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit) {
+__device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit,
+                             long long *pacc = nullptr) {
+  long long t0 = clock64();
   const int R = ch.r1 - ch.r0, nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
   const int *xp32 = (const int *)sm.xq;
   const float *xs = (const float *)sm.xs;
@@ -316,6 +359,7 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
       ln[2 * q + 9] = a3;
     }
     consumers_sync();
+    sub_tick(pacc, PF_INT, t0);
     // float phase: thread (row, q), 64 rows per pass.
     {
       const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
@@ -327,7 +371,7 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
         for (int j = 0; j < 4; j++) {
           int L = (j < 2) ? (2 * q + j) : (2 * q + 8 + (j - 2));
           float zp = (float)zpp[g0 + (L & 7)];
-          float sc = half_bits_to_float(scl[g0 + (L & 7)]);
+          float sc = __half2float(__ushort_as_half(scl[g0 + (L & 7)]));
           f[j] = fmaf((float)sm.lanes[(rr * nblk + b) * 16 + L] - zp * xs[b * 16 + L], sc, f[j]);
         }
       }
@@ -340,6 +384,7 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
       if (q == 0 && r < rows) emit(rbase + r, dot);
     }
     consumers_sync();
+    sub_tick(pacc, PF_FLOAT, t0);
   }
 }
 
@@ -376,7 +421,7 @@ __device__ void mk_rows_ch8(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, 
     const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
     const int rr = r < R ? r : 0;
     int zp = zpp[rr];
-    float sc = half_bits_to_float(scl[rr]);
+    float sc = __half2float(__ushort_as_half(scl[rr]));
     float f[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -395,6 +440,32 @@ __device__ void mk_rows_ch8(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, 
     if (q == 0 && r < R) emit(r, dot);
   }
   consumers_sync();
+}
+
+// Starts copying this head's cached keys, values and their scales for
+// positions [0, pos) into shared memory (pos <= MK_KV_STAGE); mk_attention
+// waits for them. Issued early so that the copies overlap the QKV phase.
+__device__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l, int h, int pos) {
+  if (pos > MK_KV_STAGE) return;
+  const size_t row0 = ((size_t)l * a.kv.max_t) * a.kv.n_head + h;  // slot of position 0
+  const size_t stride = a.kv.n_head;
+  for (int i = threadIdx.x; i < pos * 8; i += MK_CONSUMERS) {
+    int s = i >> 3, part = i & 7;  // parts 0-3: key, 4-7: value (16 bytes each)
+    size_t slot = row0 + s * stride;
+    if (part < 4)
+      cp_async16(&sm.kst[s][part * 16], a.kv.k + slot * 64 + part * 16);
+    else
+      cp_async16(&sm.vst[s][(part - 4) * 16], a.kv.v + slot * 64 + (part - 4) * 16);
+  }
+  for (int i = threadIdx.x; i < pos * 2; i += MK_CONSUMERS) {
+    int s = i >> 1;
+    size_t slot = row0 + s * stride;
+    if (i & 1)
+      cp_async4(&sm.vss[s], a.kv.vs + slot);
+    else
+      cp_async4(&sm.kss[s], a.kv.ks + slot);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 // Attention phase of head h (QuantKV[8]): store the token's key and value,
@@ -451,14 +522,16 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
       }
     }
   }
+  const bool staged = pos <= MK_KV_STAGE;
+  cp_async_wait_all();
   consumers_sync();
   const int npos = pos + 1;
   const float scale = 1.0f / sqrtf((float)HS);
   float mx = -__int_as_float(0x7f800000);
   for (int s = tid; s < npos; s += MK_CONSUMERS) {
     size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
-    const int8_t *kp = (s == pos) ? sm.att_k : a.kv.k + ss * HS;
-    float ksc = (s == pos) ? a.kv.ks[ss] : a.kv.ks[ss];
+    const int8_t *kp = (s == pos) ? sm.att_k : (staged ? sm.kst[s] : a.kv.k + ss * HS);
+    float ksc = (s == pos || !staged) ? a.kv.ks[ss] : sm.kss[s];
     float d[16];
 #pragma unroll
     for (int k = 0; k < 16; k++) d[k] = 0.0f;
@@ -497,10 +570,17 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
   for (int s = tid; s < npos; s += MK_CONSUMERS) {
     size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
     float p = sm.att_sc[s] / total;
-    sm.att_ps[s] = p * a.kv.vs[ss];
+    sm.att_ps[s] = p * ((s == pos || !staged) ? a.kv.vs[ss] : sm.vss[s]);
   }
   consumers_sync();
-  if (tid < HS) {
+  if (tid < HS && staged) {
+    const int d = tid;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
+    acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
+    st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
+  } else if (tid < HS) {
     const int d = tid;
     const size_t stride = (size_t)a.kv.n_head * HS;
     const int8_t *vp = a.kv.v + ((size_t)l * a.kv.max_t * a.kv.n_head + h) * HS + d;
@@ -585,6 +665,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   // ---------------- consumers ----------------
   const int C = a.C, C4 = 4 * C;
   long long seq = 0;
+  // profiling (thread 0 of CTAs 0 and grid/2)
+  const bool prof_on = a.prof && tid == 0 && (cta == 0 || cta == grid / 2);
+  long long pacc[MK_PROF];
+  for (int k = 0; k < MK_PROF; k++) pacc[k] = 0;
+  long long tlast = clock64();
+  long long *pp = prof_on ? pacc : nullptr;
+  auto tick = [&](int k) {
+    if (prof_on) {
+      long long t = clock64();
+      pacc[k] += t - tlast;
+      tlast = t;
+    }
+  };
   auto slot_wait = [&](int &slot) -> bool {
     slot = (int)(seq % MK_NSLOT);
     const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
@@ -592,6 +685,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     while (!mbar_try_wait(&sm.full[slot], par)) {
       if (!mk_alive(a, sm, t0, 1)) return false;
     }
+    if (prof_on) pacc[PF_RING_WAIT] += clock64() - t0;
     return true;
   };
   auto slot_release = [&](int slot) {
@@ -626,39 +720,45 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         sm.xfull[i] = v + wpe[(size_t)pos * C + i];
       }
       consumers_sync();
+      tick(PF_EMBED);
     }
     int ci = 0;  // chunk index within the token
     for (int l = 0; l < a.n_layer; l++) {
       const float *vec = a.small + (size_t)l * 13 * C;
       // ---- A: LN1 + QKV ----
       {
+        if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
         const MkChunk ch = sm.chunks[ci++];
         LnParams lp = ln_load(vec, vec + C);
         mk_bias_load(sm, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
         if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) return;
+        tick(PF_QKV_WAIT);
         for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
         consumers_sync();
-        mk_layernorm(sm, lp);
-        const float sx = mk_quantize(sm, C, true);
+        mk_layernorm(sm, lp, pp);
+        const float sx = mk_quantize(sm, C, true, pp);
         int slot;
         if (!slot_wait(slot)) return;
         unsigned long long *dst = a.ll + ll.qkv(l);
         mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
           float v = dot * sx + sm.bias[r];
           st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        });
+        }, pp);
         slot_release(slot);
+        tick(PF_QKV);
       }
       // ---- B: KV store + attention (CTA h for head h) ----
       if (cta < a.n_head) {
         if (!mk_attention(a, sm, ll, l, cta, pos, flag)) return;
+        tick(PF_ATTN);
       }
       // ---- C: PROJ + residual ----
       {
         const MkChunk ch = sm.chunks[ci++];
         mk_bias_load(sm, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
         if (!mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4)) return;
-        const float sx = mk_quantize(sm, C, true);
+        tick(PF_PROJ_WAIT);
+        const float sx = mk_quantize(sm, C, true, pp);
         int slot;
         if (!slot_wait(slot)) return;
         unsigned long long *dst = a.ll + ll.xmid(l);
@@ -666,8 +766,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
           float v = dot * sx + sm.bias[r];
           v += sm.xfull[ch.r0 + r];
           st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        });
+        }, pp);
         slot_release(slot);
+        tick(PF_PROJ);
       }
       // ---- D: LN2 + FC + GELU ----
       {
@@ -675,10 +776,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         LnParams lp = ln_load(vec + 6 * C, vec + 7 * C);
         mk_bias_load(sm, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
         if (!mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5)) return;
+        tick(PF_FC_WAIT);
         for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
         consumers_sync();
-        mk_layernorm(sm, lp);
-        const float sx = mk_quantize(sm, C, true);
+        mk_layernorm(sm, lp, pp);
+        const float sx = mk_quantize(sm, C, true, pp);
         int slot;
         if (!slot_wait(slot)) return;
         unsigned long long *dst = a.ll + ll.fc(l);
@@ -686,15 +788,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
           float v = dot * sx + sm.bias[r];
           v = gelu(v);
           st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        });
+        }, pp);
         slot_release(slot);
+        tick(PF_FC);
       }
       // ---- E: FCPROJ + residual ----
       {
         const MkChunk ch = sm.chunks[ci++];
         mk_bias_load(sm, vec + 12 * C, ch.r0, ch.r1 - ch.r0);
         if (!mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6)) return;
-        const float sx = mk_quantize(sm, C4, true);
+        tick(PF_FCPROJ_WAIT);
+        const float sx = mk_quantize(sm, C4, true, pp);
         int slot;
         if (!slot_wait(slot)) return;
         unsigned long long *dst = a.ll + ll.xout(l);
@@ -702,15 +806,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
           float v = dot * sx + sm.bias[r];
           v += sm.xfull[ch.r0 + r];
           st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        });
+        }, pp);
         slot_release(slot);
+        tick(PF_FCPROJ);
       }
     }
     // ---- H: LN_f + head + argmax ----
     LnParams lp = ln_load(lnf, lnf + C);
     if (!mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7)) return;
-    mk_layernorm(sm, lp);
-    const float sx = mk_quantize(sm, C, false);
+    tick(PF_HEAD_WAIT);
+    mk_layernorm(sm, lp, pp);
+    const float sx = mk_quantize(sm, C, false, pp);
     float bv = -__int_as_float(0x7f800000);
     int bi = 0x7fffffff;
     for (; ci < a.nchunks; ci++) {
@@ -728,6 +834,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       });
       slot_release(slot);
     }
+    tick(PF_HEAD);
     // CTA argmax
     for (int o = 16; o > 0; o >>= 1) {
       float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -780,6 +887,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     }
     consumers_sync();
     token = sm.token;
+    tick(PF_ARGMAX);
+    if (prof_on) pacc[PF_STEPS] += 1;
+  }
+  if (prof_on) {
+    long long *dst = a.prof + (cta == 0 ? 0 : MK_PROF);
+    for (int k = 0; k < MK_PROF; k++) dst[k] += pacc[k];
   }
 }
 

@@ -56,6 +56,21 @@ class Model:
         m = lib().llmq_model_mode(self.h)
         return {v: k for k, v in self.MODES.items()}[m]
 
+    PROFILE_NAMES = ("embed", "qkv wait", "qkv", "attention", "proj wait", "proj", "fc wait", "fc",
+                     "fcproj wait", "fcproj", "head wait", "head", "argmax", "ring waits", "steps",
+                     "in: layernorm", "in: quantize", "in: int dots", "in: float epilogue")
+
+    def profile(self, enable: bool = True):
+        """Per-phase cycle counters of the persistent kernel (--profile)."""
+        check(lib().llmq_model_profile(self.ctx.h, self.h, int(enable)), self.ctx.h)
+
+    def profile_read(self, reset: bool = True) -> list[dict]:
+        """Counters of CTA 0 and CTA grid/2: {category: cycles}."""
+        n = len(self.PROFILE_NAMES) + 1
+        buf = (C.c_longlong * (2 * n))()
+        check(lib().llmq_model_profile_read(self.ctx.h, self.h, buf, 2 * n, int(reset)), self.ctx.h)
+        return [dict(zip(self.PROFILE_NAMES, buf[n * i:n * i + n - 1])) for i in range(2)]
+
     def forward(self, tokens, pos0: int, logits=None) -> int:
         """Runs tokens at positions pos0..; returns the last token's argmax and
         writes its logits into `logits` (a float32 CUDA tensor [V]) if given."""
