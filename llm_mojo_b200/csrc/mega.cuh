@@ -192,29 +192,30 @@ __device__ __forceinline__ bool mk_alive(const MegaArgs &a, MkSmem &sm, long lon
   return true;
 }
 
-// Reads n exchange words with flag `flag` into dst (all consumer threads).
+// Reads n <= MK_POLL * MK_CONSUMERS exchange words with flag `flag` into dst
+// (all consumer threads). Each round issues every pending load of the
+// thread before checking any, so a round costs one memory round trip.
+constexpr int MK_POLL = 12;
 __device__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsigned long long *src, int n, unsigned flag,
                         float *dst, int code) {
   long long t0 = clock64();
-  for (int base = threadIdx.x; base < n; base += MK_CONSUMERS * 4) {
-    unsigned pending = 0;
+  const int tid = threadIdx.x;
+  unsigned pending = 0;
 #pragma unroll
-    for (int j = 0; j < 4; j++)
-      if (base + j * MK_CONSUMERS < n) pending |= 1u << j;
-    while (pending) {
+  for (int k = 0; k < MK_POLL; k++)
+    if (tid + k * MK_CONSUMERS < n) pending |= 1u << k;
+  while (pending) {
+    unsigned long long v[MK_POLL];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        if (pending & (1u << j)) {
-          int i = base + j * MK_CONSUMERS;
-          unsigned long long v = ld_relaxed_u64(src + i);
-          if ((unsigned)(v >> 32) == flag) {
-            dst[i] = __uint_as_float((unsigned)v);
-            pending &= ~(1u << j);
-          }
-        }
+    for (int k = 0; k < MK_POLL; k++)
+      if (pending & (1u << k)) v[k] = ld_relaxed_u64(src + tid + k * MK_CONSUMERS);
+#pragma unroll
+    for (int k = 0; k < MK_POLL; k++)
+      if ((pending & (1u << k)) && (unsigned)(v[k] >> 32) == flag) {
+        dst[tid + k * MK_CONSUMERS] = __uint_as_float((unsigned)v[k]);
+        pending &= ~(1u << k);
       }
-      if (pending && !mk_alive(a, sm, t0, code)) break;
-    }
+    if (pending && !mk_alive(a, sm, t0, code)) break;
   }
   consumers_sync();
   return !sm.abort;
@@ -240,14 +241,29 @@ __device__ void mk_layernorm(MkSmem &sm, const LnParams &pr, long long *pacc = n
   const int C = 768;
   long long t0 = clock64();
   if (threadIdx.x < 32) {
-    int l = threadIdx.x & 15;
+    // lane l's 48 values in registers, then the two sequential sums
+    const int l = threadIdx.x & 15;
     float s = 0.0f;
-    for (int i = 0; i < C; i += 16) s = s + sm.xf[i + l];
+#pragma unroll
+    for (int k0 = 0; k0 < 48; k0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) v[k] = sm.xf[16 * (k0 + k) + l];
+#pragma unroll
+      for (int k = 0; k < 16; k++) s = s + v[k];
+    }
     float mean = tree16_warp(s) / (float)C;
     float sq = 0.0f;
-    for (int i = 0; i < C; i += 16) {
-      float d = sm.xf[i + l] - mean;
-      sq = sq + d * d;
+#pragma unroll
+    for (int k0 = 0; k0 < 48; k0 += 16) {
+      float v[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) v[k] = sm.xf[16 * (k0 + k) + l];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        float d = v[k] - mean;
+        sq = sq + d * d;
+      }
     }
     float var = tree16_warp(sq) / (float)C;
     if (threadIdx.x == 0) {
@@ -364,16 +380,23 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
     {
       const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
       const int rr = r < rows ? r : 0;
+      // lanes 2q, 2q+1 (groups 2q, 2q+1, first halves) and 2q+8, 2q+9
+      // (the same groups' second halves)
       float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int b = 0; b < nblk; b++) {
-        int g0 = (rbase + rr) * gpr + b * 8;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-          int L = (j < 2) ? (2 * q + j) : (2 * q + 8 + (j - 2));
-          float zp = (float)zpp[g0 + (L & 7)];
-          float sc = __half2float(__ushort_as_half(scl[g0 + (L & 7)]));
-          f[j] = fmaf((float)sm.lanes[(rr * nblk + b) * 16 + L] - zp * xs[b * 16 + L], sc, f[j]);
-        }
+        const int g0 = (rbase + rr) * gpr + b * 8 + 2 * q;
+        const unsigned zp2 = *(const uint16_t *)(zpp + g0);
+        const __half2 sc2 = *(const __half2 *)(scl + g0);
+        const float zp0 = (float)(zp2 & 0xFF), zp1 = (float)(zp2 >> 8);
+        const float sc0 = __low2float(sc2), sc1 = __high2float(sc2);
+        const int2 la = *(const int2 *)(sm.lanes + (rr * nblk + b) * 16 + 2 * q);
+        const int2 lb = *(const int2 *)(sm.lanes + (rr * nblk + b) * 16 + 2 * q + 8);
+        const float2 xa = *(const float2 *)(xs + b * 16 + 2 * q);
+        const float2 xb = *(const float2 *)(xs + b * 16 + 2 * q + 8);
+        f[0] = fmaf((float)la.x - zp0 * xa.x, sc0, f[0]);
+        f[1] = fmaf((float)la.y - zp1 * xa.y, sc1, f[1]);
+        f[2] = fmaf((float)lb.x - zp0 * xb.x, sc0, f[2]);
+        f[3] = fmaf((float)lb.y - zp1 * xb.y, sc1, f[3]);
       }
       float a0 = f[0] + f[2], a1 = f[1] + f[3];
       a0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 2);
@@ -561,8 +584,17 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
   for (int s = tid; s < npos; s += MK_CONSUMERS) sm.att_sc[s] = lm_expf(sm.att_sc[s] - mx);
   consumers_sync();
   if (tid == 0) {
+    // sequential sum in position order, 16 values loaded ahead at a time
     float total = 0.0f;
-    for (int s = 0; s < npos; s++) total += sm.att_sc[s];
+    int s = 0;
+    for (; s + 16 <= npos; s += 16) {
+      float e[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) e[k] = sm.att_sc[s + k];
+#pragma unroll
+      for (int k = 0; k < 16; k++) total += e[k];
+    }
+    for (; s < npos; s++) total += sm.att_sc[s];
     sm.red[36] = total;
   }
   consumers_sync();
@@ -576,8 +608,18 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
   if (tid < HS && staged) {
     const int d = tid;
     float acc = 0.0f;
-#pragma unroll 8
-    for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
+    int s = 0;
+    for (; s + 16 <= pos; s += 16) {
+      float pv[16], vv[16];
+#pragma unroll
+      for (int k = 0; k < 16; k++) {
+        pv[k] = sm.att_ps[s + k];
+        vv[k] = (float)sm.vst[s + k][d];
+      }
+#pragma unroll
+      for (int k = 0; k < 16; k++) acc = fmaf(pv[k], vv[k], acc);
+    }
+    for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
     acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
     st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
   } else if (tid < HS) {
