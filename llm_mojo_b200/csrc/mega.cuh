@@ -9,9 +9,10 @@
 // costs a launch and a cold start; here every CTA stays resident and
 //   - streams its own slice of every weight matrix, in the order it will use
 //     them, from a per-CTA packed copy in HBM into a shared-memory ring with
-//     cp.async.bulk (a producer warp, mbarrier completion), running ahead of
-//     the computation across layers and tokens, so weights never sit on the
-//     critical path;
+//     cp.async.bulk (mbarrier completion): the thread that releases a slot
+//     issues the copy of the chunk MK_NSLOT ahead into it, so the ring runs
+//     ahead of the computation across layers and tokens and weights never sit
+//     on the critical path;
 //   - exchanges activations through global buffers of 8-byte words that
 //     hold a float and a 32-bit flag (the token's sequence number): a writer
 //     publishes a value and its flag with one single-copy-atomic store, and a
@@ -32,7 +33,7 @@
 namespace llmq {
 
 constexpr int MK_CONSUMERS = 256;
-constexpr int MK_THREADS = MK_CONSUMERS + 32;  // + producer warp
+constexpr int MK_THREADS = MK_CONSUMERS;  // all threads compute; thread 0 also issues the ring's copies
 constexpr int MK_NSLOT = 7;
 constexpr int MK_SLOT = 18512;  // bytes per ring slot: one chunk (largest: 24 head rows)
 constexpr int MK_HEAD_TILE = 24;
@@ -155,7 +156,7 @@ __device__ __forceinline__ unsigned long long ll_pack(float v, unsigned flag) {
 // --- shared memory ---------------------------------------------------------
 
 struct MkSmem {
-  unsigned long long full[MK_NSLOT], empty[MK_NSLOT];
+  unsigned long long full[MK_NSLOT];
   volatile int abort;        // set by a consumer that timed out
   int token;
   alignas(16) float red[64];
@@ -659,50 +660,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
 
   for (int i = tid; i < a.nchunks; i += MK_THREADS) sm.chunks[i] = a.chunks[(size_t)cta * a.nchunks + i];
   if (tid == 0) {
-    for (int i = 0; i < MK_NSLOT; i++) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], 1);
-    }
+    for (int i = 0; i < MK_NSLOT; i++) mbar_init(&sm.full[i], 1);
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-
-  if (tid >= MK_CONSUMERS) {
-    // ---------------- producer warp ----------------
-    if (tid != MK_CONSUMERS) return;
-    long long issued = 0;
-    for (long long seq = 0; seq < total_chunks; seq++) {
-      const int slot = (int)(seq % MK_NSLOT);
-      if (seq >= MK_NSLOT) {
-        const unsigned par = (unsigned)(((seq / MK_NSLOT) - 1) & 1);
-        long long t0 = clock64();
-        bool ok = true;
-        while (!mbar_try_wait(&sm.empty[slot], par)) {
-          if (sm.abort || clock64() - t0 > a.timeout_cycles) {
-            ok = false;
-            break;
-          }
-        }
-        if (!ok) break;
-      }
-      const MkChunk &ch = sm.chunks[seq % a.nchunks];
-      mbar_expect_tx(&sm.full[slot], (unsigned)ch.bytes);
-      bulk_g2s(sm.ring[slot], stream + ch.off, (unsigned)ch.bytes, &sm.full[slot]);
-      issued = seq + 1;
-    }
-    // On abort, wait (bounded) for every copy still in flight into the ring.
-    if (sm.abort) {
-      for (long long seq = issued > MK_NSLOT ? issued - MK_NSLOT : 0; seq < issued; seq++) {
-        const int slot = (int)(seq % MK_NSLOT);
-        const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
-        long long t1 = clock64();
-        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
-        }
-      }
-    }
-    return;
-  }
+  // Chunk `q` of the whole generation into its ring slot (thread 0).
+  auto issue = [&](long long q) {
+    const int slot = (int)(q % MK_NSLOT);
+    const MkChunk &ch = sm.chunks[q % a.nchunks];
+    mbar_expect_tx(&sm.full[slot], (unsigned)ch.bytes);
+    bulk_g2s(sm.ring[slot], stream + ch.off, (unsigned)ch.bytes, &sm.full[slot]);
+  };
+  if (tid == 0)
+    for (long long q = 0; q < MK_NSLOT && q < total_chunks; q++) issue(q);
 
   // ---------------- consumers ----------------
   const int C = a.C, C4 = 4 * C;
@@ -730,9 +701,23 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     if (prof_on) pacc[PF_RING_WAIT] += clock64() - t0;
     return true;
   };
+  // On a timeout every thread leaves; first each waits for its own cp.async
+  // copies, and thread 0 (bounded) for the ring's bulk copies in flight.
+  auto drain = [&]() {
+    cp_async_wait_all();
+    if (tid == 0) {
+      for (long long q = seq; q < seq + MK_NSLOT && q < total_chunks; q++) {
+        const int slot = (int)(q % MK_NSLOT);
+        const unsigned par = (unsigned)((q / MK_NSLOT) & 1);
+        long long t1 = clock64();
+        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        }
+      }
+    }
+  };
   auto slot_release = [&](int slot) {
-    consumers_sync();
-    if (tid == 0) mbar_arrive(&sm.empty[slot]);
+    consumers_sync();  // every thread is done with the slot
+    if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
     seq++;
   };
 
@@ -773,14 +758,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         const MkChunk ch = sm.chunks[ci++];
         LnParams lp = ln_load(vec, vec + C);
         mk_bias_load(sm, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
-        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) return;
+        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
+          drain();
+          return;
+        }
         tick(PF_QKV_WAIT);
         for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
         consumers_sync();
         mk_layernorm(sm, lp, pp);
         const float sx = mk_quantize(sm, C, true, pp);
         int slot;
-        if (!slot_wait(slot)) return;
+        if (!slot_wait(slot)) {
+          drain();
+          return;
+        }
         unsigned long long *dst = a.ll + ll.qkv(l);
         mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
           float v = dot * sx + sm.bias[r];
@@ -791,18 +782,27 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       }
       // ---- B: KV store + attention (CTA h for head h) ----
       if (cta < a.n_head) {
-        if (!mk_attention(a, sm, ll, l, cta, pos, flag)) return;
+        if (!mk_attention(a, sm, ll, l, cta, pos, flag)) {
+          drain();
+          return;
+        }
         tick(PF_ATTN);
       }
       // ---- C: PROJ + residual ----
       {
         const MkChunk ch = sm.chunks[ci++];
         mk_bias_load(sm, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4)) return;
+        if (!mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4)) {
+          drain();
+          return;
+        }
         tick(PF_PROJ_WAIT);
         const float sx = mk_quantize(sm, C, true, pp);
         int slot;
-        if (!slot_wait(slot)) return;
+        if (!slot_wait(slot)) {
+          drain();
+          return;
+        }
         unsigned long long *dst = a.ll + ll.xmid(l);
         mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
           float v = dot * sx + sm.bias[r];
@@ -817,14 +817,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         const MkChunk ch = sm.chunks[ci++];
         LnParams lp = ln_load(vec + 6 * C, vec + 7 * C);
         mk_bias_load(sm, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5)) return;
+        if (!mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5)) {
+          drain();
+          return;
+        }
         tick(PF_FC_WAIT);
         for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
         consumers_sync();
         mk_layernorm(sm, lp, pp);
         const float sx = mk_quantize(sm, C, true, pp);
         int slot;
-        if (!slot_wait(slot)) return;
+        if (!slot_wait(slot)) {
+          drain();
+          return;
+        }
         unsigned long long *dst = a.ll + ll.fc(l);
         mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
           float v = dot * sx + sm.bias[r];
@@ -838,11 +844,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       {
         const MkChunk ch = sm.chunks[ci++];
         mk_bias_load(sm, vec + 12 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6)) return;
+        if (!mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6)) {
+          drain();
+          return;
+        }
         tick(PF_FCPROJ_WAIT);
         const float sx = mk_quantize(sm, C4, true, pp);
         int slot;
-        if (!slot_wait(slot)) return;
+        if (!slot_wait(slot)) {
+          drain();
+          return;
+        }
         unsigned long long *dst = a.ll + ll.xout(l);
         mk_rows_blk4(sm, sm.ring[slot], ch, C4, [&](int r, float dot) {
           float v = dot * sx + sm.bias[r];
@@ -855,7 +867,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     }
     // ---- H: LN_f + head + argmax ----
     LnParams lp = ln_load(lnf, lnf + C);
-    if (!mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7)) return;
+    if (!mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7)) {
+          drain();
+          return;
+        }
     tick(PF_HEAD_WAIT);
     mk_layernorm(sm, lp, pp);
     const float sx = mk_quantize(sm, C, false, pp);
@@ -863,7 +878,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     int bi = 0x7fffffff;
     for (; ci < a.nchunks; ci++) {
       int slot;
-      if (!slot_wait(slot)) return;
+      if (!slot_wait(slot)) {
+          drain();
+          return;
+        }
       const MkChunk ch = sm.chunks[ci];
       mk_rows_ch8(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
         int o = ch.r0 + r;
@@ -901,7 +919,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       st_relaxed_u64(a.ll + ll.part() + 2 * cta + 1, ((unsigned long long)flag << 32) | (unsigned)bi);
     }
     // ---- I: global argmax (every CTA) ----
-    if (!mk_poll(a, sm, a.ll + ll.part(), 2 * grid, flag, sm.xf, 8)) return;
+    if (!mk_poll(a, sm, a.ll + ll.part(), 2 * grid, flag, sm.xf, 8)) {
+          drain();
+          return;
+        }
     if (tid < 32) {
       float v = -__int_as_float(0x7f800000);
       int i = 0x7fffffff;
