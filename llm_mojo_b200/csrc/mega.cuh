@@ -14,14 +14,18 @@
 //     ahead of the computation across layers and tokens and weights never sit
 //     on the critical path;
 //   - exchanges activations through global buffers of 8-byte words that
-//     hold a float and a 32-bit flag (the token's sequence number): a writer
+//     hold a float and a 32-bit flag (the step's sequence number): a writer
 //     publishes a value and its flag with one single-copy-atomic store, and a
 //     reader spins on the words it needs until their flags match. This is
 //     both the data transfer and the synchronisation; there is no separate
 //     grid barrier.
 // Every spin (ring slots, flags) is bounded by a cycle budget; on timeout
-// the kernel records an error code, waits (bounded) for its own bulk copies
-// in flight, and returns.
+// the kernel records an error code, waits (bounded) for its own copies in
+// flight, and returns.
+//
+// The phase helpers are deliberately not inlined: one copy of each keeps
+// the kernel's code small enough to stay in the SMs' instruction caches
+// while it loops over layers and tokens.
 //
 // The arithmetic of each phase is that of the one-token kernels
 // (gemv_a16.cuh, attention.cuh): bit-identical to the reference's.
@@ -32,14 +36,14 @@
 
 namespace llmq {
 
-constexpr int MK_CONSUMERS = 256;
-constexpr int MK_THREADS = MK_CONSUMERS;  // all threads compute; thread 0 also issues the ring's copies
+constexpr int MK_THREADS = 256;
 constexpr int MK_NSLOT = 7;
-constexpr int MK_SLOT = 18512;  // bytes per ring slot: one chunk (largest: 24 head rows)
+constexpr int MK_SLOT = 18512;     // bytes per ring slot: one chunk (largest: 24 head rows)
 constexpr int MK_HEAD_TILE = 24;
-constexpr int MK_KV_STAGE = 256;  // cache positions an attention CTA stages in shared memory
-constexpr int MK_LANES = 4096;  // int32 lane sums held at once
+constexpr int MK_KV_STAGE = 256;   // cache positions an attention CTA stages in shared memory
+constexpr int MK_LANES = 4096;     // int32 lane sums held at once
 constexpr int MK_MAX_CHUNKS = 64;  // chunks per CTA per token
+constexpr int MK_POLL = 12;        // exchange words a thread polls at once (n <= 3072)
 
 enum { PH_QKV = 0, PH_PROJ = 1, PH_FC = 2, PH_FCPROJ = 3, PH_HEAD = 4 };
 
@@ -82,7 +86,7 @@ enum {
   PF_LN, PF_QUANT, PF_INT, PF_FLOAT, MK_PROF = 20
 };
 
-// Adds the cycles since *t to acc[k] and restarts *t (when acc is not null).
+// Adds the cycles since t to acc[k] and restarts t (when acc is not null).
 __device__ __forceinline__ void sub_tick(long long *acc, int k, long long &t) {
   if (acc) {
     long long n = clock64();
@@ -114,9 +118,6 @@ __device__ __forceinline__ void mbar_init(unsigned long long *b, unsigned count)
 __device__ __forceinline__ void mbar_expect_tx(unsigned long long *b, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(unsigned long long *b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long *b, unsigned parity) {
   unsigned ok;
   asm volatile(
@@ -146,8 +147,9 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_CONSUMERS) : "memory"); }
+__device__ __forceinline__ void cta_sync() { asm volatile("bar.sync 1, %0;" ::"n"(MK_THREADS) : "memory"); }
 
 __device__ __forceinline__ unsigned long long ll_pack(float v, unsigned flag) {
   return ((unsigned long long)flag << 32) | (unsigned long long)__float_as_uint(v);
@@ -157,7 +159,7 @@ __device__ __forceinline__ unsigned long long ll_pack(float v, unsigned flag) {
 
 struct MkSmem {
   unsigned long long full[MK_NSLOT];
-  volatile int abort;        // set by a consumer that timed out
+  volatile int abort;               // set by a thread whose wait timed out
   int token;
   alignas(16) float red[64];
   alignas(16) float xfull[768];     // the residual stream x of this token (all 768)
@@ -165,6 +167,9 @@ struct MkSmem {
   alignas(16) int16_t xq[3072];     // its int16 codes (permuted for BLOCKED)
   alignas(16) int xs[192];          // BLOCKED lane sums (as float) / per-channel pair sums (int)
   alignas(16) int lanes[MK_LANES];  // int32 lane sums of the current rows
+  alignas(16) float lnw[768];       // the next LayerNorm's weight and bias
+  alignas(16) float lnb[768];
+  alignas(16) float bias[64];       // the current phase's biases for this CTA's rows
   alignas(16) float att_sc[1024];   // attention scores / exponentials
   alignas(16) float att_ps[1024];   // p * vs
   alignas(16) float att_q[64];
@@ -176,13 +181,14 @@ struct MkSmem {
   alignas(16) float vss[MK_KV_STAGE];
   alignas(16) float best_v[8];
   alignas(16) int best_i[8];
-  alignas(16) float bias[64];       // the current phase's biases for this CTA's rows
+  alignas(16) float thr_v[MK_THREADS];  // per-thread argmax candidates of the head phase
+  alignas(16) int thr_i[MK_THREADS];
   alignas(16) MkChunk chunks[MK_MAX_CHUNKS];
   alignas(128) uint8_t ring[MK_NSLOT][MK_SLOT];
 };
 
-// Bounded spin helper: returns false (and records the error) once the
-// budget is spent.
+// Bounded spin helper: false (and the error recorded) once the budget is
+// spent or another thread has given up.
 __device__ __forceinline__ bool mk_alive(const MegaArgs &a, MkSmem &sm, long long t0, int code) {
   if (sm.abort) return false;
   if (clock64() - t0 > a.timeout_cycles) {
@@ -193,56 +199,56 @@ __device__ __forceinline__ bool mk_alive(const MegaArgs &a, MkSmem &sm, long lon
   return true;
 }
 
-// Reads n <= MK_POLL * MK_CONSUMERS exchange words with flag `flag` into dst
-// (all consumer threads). Each round issues every pending load of the
-// thread before checking any, so a round costs one memory round trip.
-constexpr int MK_POLL = 12;
-__device__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsigned long long *src, int n, unsigned flag,
-                        float *dst, int code) {
+// Reads n <= MK_POLL * MK_THREADS exchange words with flag `flag` into dst
+// (all threads). Each round issues every pending load of the thread before
+// checking any, so a round costs one memory round trip.
+__device__ __noinline__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsigned long long *src, int n,
+                                     unsigned flag, float *dst, int code) {
   long long t0 = clock64();
   const int tid = threadIdx.x;
   unsigned pending = 0;
 #pragma unroll
   for (int k = 0; k < MK_POLL; k++)
-    if (tid + k * MK_CONSUMERS < n) pending |= 1u << k;
+    if (tid + k * MK_THREADS < n) pending |= 1u << k;
   while (pending) {
     unsigned long long v[MK_POLL];
 #pragma unroll
     for (int k = 0; k < MK_POLL; k++)
-      if (pending & (1u << k)) v[k] = ld_relaxed_u64(src + tid + k * MK_CONSUMERS);
+      if (pending & (1u << k)) v[k] = ld_relaxed_u64(src + tid + k * MK_THREADS);
 #pragma unroll
     for (int k = 0; k < MK_POLL; k++)
       if ((pending & (1u << k)) && (unsigned)(v[k] >> 32) == flag) {
-        dst[tid + k * MK_CONSUMERS] = __uint_as_float((unsigned)v[k]);
+        dst[tid + k * MK_THREADS] = __uint_as_float((unsigned)v[k]);
         pending &= ~(1u << k);
       }
     if (pending && !mk_alive(a, sm, t0, code)) break;
   }
-  consumers_sync();
+  cta_sync();
   return !sm.abort;
 }
 
-// LayerNorm parameters of this thread's 3 elements (C = 768), loaded ahead of
-// the wait for the activations so that their latency overlaps it.
-struct LnParams {
-  float w[3], b[3];
-};
-__device__ __forceinline__ LnParams ln_load(const float *w, const float *b) {
-  LnParams p;
-#pragma unroll
-  for (int j = 0; j < 3; j++) {
-    p.w[j] = __ldg(w + threadIdx.x + j * MK_CONSUMERS);
-    p.b[j] = __ldg(b + threadIdx.x + j * MK_CONSUMERS);
+// Starts copying a LayerNorm's weight and bias (768 each) and this CTA's
+// biases of rows [r0, r0 + n) into shared memory; waited for before use
+// (cp_async_wait_all). Issued before the wait for the activations.
+__device__ __forceinline__ void mk_params_load(MkSmem &sm, const float *lnw, const float *lnb, const float *bias,
+                                               int r0, int n) {
+  const int tid = threadIdx.x;
+  if (lnw && tid < 192) {
+    cp_async16(&sm.lnw[tid * 4], lnw + tid * 4);
+    cp_async16(&sm.lnb[tid * 4], lnb + tid * 4);
   }
-  return p;
+  if (bias && tid < n) cp_async4(&sm.bias[tid], bias + r0 + tid);
+  cp_async_commit();
 }
 
-// LayerNorm of sm.xf[0..768) in place (kernels.mojo:179-197).
-__device__ void mk_layernorm(MkSmem &sm, const LnParams &pr, long long *pacc = nullptr) {
+// LayerNorm of sm.xf[0..768) in place with sm.lnw / sm.lnb
+// (kernels.mojo:179-197): 16 lane sums, each sequential over the row's
+// 16-float chunks, reduced by the halving tree.
+__device__ __noinline__ void mk_layernorm(MkSmem &sm) {
   const int C = 768;
-  long long t0 = clock64();
+  cp_async_wait_all();
+  cta_sync();
   if (threadIdx.x < 32) {
-    // lane l's 48 values in registers, then the two sequential sums
     const int l = threadIdx.x & 15;
     float s = 0.0f;
 #pragma unroll
@@ -272,44 +278,41 @@ __device__ void mk_layernorm(MkSmem &sm, const LnParams &pr, long long *pacc = n
       sm.red[41] = 1.0f / sqrtf(var + 1e-5f);
     }
   }
-  consumers_sync();
-  float mean = sm.red[40], rstd = sm.red[41];
-#pragma unroll
-  for (int j = 0; j < 3; j++) {
-    int i = threadIdx.x + j * MK_CONSUMERS;
+  cta_sync();
+  const float mean = sm.red[40], rstd = sm.red[41];
+  for (int i = threadIdx.x; i < C; i += MK_THREADS) {
     float n = (sm.xf[i] - mean) * rstd;
-    sm.xf[i] = n * pr.w[j] + pr.b[j];
+    sm.xf[i] = n * sm.lnw[i] + sm.lnb[i];
   }
-  consumers_sync();
-  sub_tick(pacc, PF_LN, t0);
+  cta_sync();
 }
 
-// quantize_rows of sm.xf[0..IN) into sm.xq (BLOCKED lane order and lane
-// sums when blocked, natural order and per-lane pair sums otherwise).
+// quantize_rows of sm.xf[0..IN) into sm.xq (kernels.mojo:400-416): the
+// BLOCKED lane order and lane sums when blocked (permute_x_i16,
+// tensor.mojo:498-516), natural order and per-lane pair sums otherwise.
 // Returns sx.
-__device__ float mk_quantize(MkSmem &sm, int IN, bool blocked, long long *pacc = nullptr) {
-  long long t0 = clock64();
+__device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
   float mx = 0.0f;
-  for (int i = threadIdx.x; i < IN; i += MK_CONSUMERS) mx = fmaxf(mx, fabsf(sm.xf[i]));
+  for (int i = threadIdx.x; i < IN; i += MK_THREADS) mx = fmaxf(mx, fabsf(sm.xf[i]));
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = mx;
-  consumers_sync();
+  cta_sync();
   mx = sm.red[0];
 #pragma unroll
-  for (int w = 1; w < MK_CONSUMERS / 32; w++) mx = fmaxf(mx, sm.red[w]);
+  for (int w = 1; w < MK_THREADS / 32; w++) mx = fmaxf(mx, sm.red[w]);
   float s = mx / 32767.0f;
   if (s == 0.0f) s = 1.0f;
-  float inv = 1.0f / s;
+  const float inv = 1.0f / s;
   if (blocked) {
-    for (int col = threadIdx.x; col < IN; col += MK_CONSUMERS) {
+    for (int col = threadIdx.x; col < IN; col += MK_THREADS) {
       int blk = col >> 8, w = col & 255, e = w & 31, p = e >> 1;
       int lane = (w >> 5) + 8 * (p >> 3);
       sm.xq[blk * 256 + (p & 7) * 32 + 2 * lane + (e & 1)] = (int16_t)roundf(sm.xf[col] * inv);
     }
-    consumers_sync();
+    cta_sync();
     // lane L of block blk: the 8 code pairs at blk*128 + s*16 + L
     const int *xp32 = (const int *)sm.xq;
-    for (int i = threadIdx.x; i < IN / 16; i += MK_CONSUMERS) {
+    for (int i = threadIdx.x; i < IN / 16; i += MK_THREADS) {
       int blk = i >> 4, lane = i & 15, sum = 0;
 #pragma unroll
       for (int st = 0; st < 8; st++) {
@@ -319,39 +322,40 @@ __device__ float mk_quantize(MkSmem &sm, int IN, bool blocked, long long *pacc =
       ((float *)sm.xs)[i] = (float)sum;
     }
   } else {
-    for (int i = threadIdx.x; i < IN; i += MK_CONSUMERS) sm.xq[i] = (int16_t)roundf(sm.xf[i] * inv);
-    consumers_sync();
-    // per-channel rows (one group): sums of each lane's pairs over the row.
+    for (int i = threadIdx.x; i < IN; i += MK_THREADS) sm.xq[i] = (int16_t)roundf(sm.xf[i] * inv);
+    cta_sync();
     if (threadIdx.x < 16) {
       int L = threadIdx.x, sum = 0;
       for (int k0 = 0; k0 < IN; k0 += 32) sum += (int)sm.xq[k0 + 2 * L] + (int)sm.xq[k0 + 2 * L + 1];
       sm.xs[L] = sum;
     }
   }
-  consumers_sync();
-  sub_tick(pacc, PF_QUANT, t0);
+  cta_sync();
   return s;
 }
 
-// BLOCKED int4-g32 rows [0, R) of the chunk in `slot` against sm.xq: the
-// float results of dot_row_i16 for each row, delivered to `emit(r, dot)` by
-// the thread with q == 0 of the row.
-template <typename Emit>
-__device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit,
-                             long long *pacc = nullptr) {
+// Epilogue flags of mk_gemv_blk4 (store_out, kernels.mojo:38-48).
+enum { MK_GELU = 1, MK_RESID = 2 };
+
+// BLOCKED int4-g32 rows of the chunk in `slot` against sm.xq (dot_row_i16,
+// tensor.mojo:522-540), then v = dot * sx + bias (+ GELU) (+ sm.xfull[o]),
+// published as exchange words out[o] with `flag`.
+__device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, float sx,
+                                          int epi, unsigned long long *out, unsigned flag, long long *pacc) {
   long long t0 = clock64();
   const int R = ch.r1 - ch.r0, nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
   const int *xp32 = (const int *)sm.xq;
   const float *xs = (const float *)sm.xs;
   const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
   const uint8_t *zpp = slot + ch.zp_off;
-  // rows per pass: as many as lanes[] holds, at most 64 (one float pass)
   const int pass = MK_LANES / (nblk * 16) < 64 ? MK_LANES / (nblk * 16) : 64;
   for (int rbase = 0; rbase < R; rbase += pass) {
     const int rows = R - rbase < pass ? R - rbase : pass;
-    // integer phase: items (row, block, q)
+    // integer phase: items (row, block, q); the steps of a block are visited
+    // in an order rotated by the item so that a warp's shared-memory reads
+    // fall in different banks.
     const int items = rows * nblk * 4;
-    for (int it = threadIdx.x; it < items; it += MK_CONSUMERS) {
+    for (int it = threadIdx.x; it < items; it += MK_THREADS) {
       int q = it & 3, rb = it >> 2, b = rb % nblk, r = rb / nblk;
       const uint32_t *wp = (const uint32_t *)(slot + (size_t)(rbase + r) * row_bytes + b * 128) + q;
       int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
@@ -375,14 +379,13 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
       ln[2 * q + 8] = a2;
       ln[2 * q + 9] = a3;
     }
-    consumers_sync();
+    cta_sync();
     sub_tick(pacc, PF_INT, t0);
-    // float phase: thread (row, q), 64 rows per pass.
+    // float phase: thread (row, q), 64 rows per pass; lanes 2q, 2q+1 (groups
+    // 2q, 2q+1, first halves) and 2q+8, 2q+9 (their second halves).
     {
       const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
       const int rr = r < rows ? r : 0;
-      // lanes 2q, 2q+1 (groups 2q, 2q+1, first halves) and 2q+8, 2q+9
-      // (the same groups' second halves)
       float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
       for (int b = 0; b < nblk; b++) {
         const int g0 = (rbase + rr) * gpr + b * 8 + 2 * q;
@@ -405,47 +408,55 @@ __device__ void mk_rows_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch,
       float c0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 1);
       float c1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
       float dot = c0 + c1;
-      if (q == 0 && r < rows) emit(rbase + r, dot);
+      if (q == 0 && r < rows) {
+        const int rl = rbase + r, o = ch.r0 + rl;
+        float v = dot * sx + sm.bias[rl];
+        if (epi & MK_GELU) v = gelu(v);
+        if (epi & MK_RESID) v += sm.xfull[o];
+        st_relaxed_u64(out + o, ll_pack(v, flag));
+      }
     }
-    consumers_sync();
+    cta_sync();
     sub_tick(pacc, PF_FLOAT, t0);
   }
 }
 
-// Per-channel int8 rows (the head) of the chunk in `slot`.
-template <typename Emit>
-__device__ void mk_rows_ch8(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, Emit emit) {
+// Per-channel int8 head rows of the chunk in `slot` (dot_row_i16 per
+// channel, tensor.mojo:541-566): logit = dot * sx, written to logits (if
+// any) and folded into this thread's argmax candidate (sm.thr_v / thr_i).
+__device__ __noinline__ void mk_head_tile(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, float sx,
+                                          float *logits) {
   const int R = ch.r1 - ch.r0, nch = IN >> 5;
   const int *xp32 = (const int *)sm.xq;
   const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
   const uint8_t *zpp = slot + ch.zp_off;
-  // integer phase: items (row, q, part), 2 parts of nch/2 chunks
+  // integer phase: items (row, q, part), 2 parts of nch/2 chunks, R <= 32
   {
     const int q = threadIdx.x & 3, r = (threadIdx.x >> 2) & 31, p = threadIdx.x >> 7;
-    int a[4] = {0, 0, 0, 0};
+    int acc[4] = {0, 0, 0, 0};
     if (r < R) {
       const uint8_t *rp = slot + (size_t)r * IN;
-      const int c0 = p * (nch / 2), c1 = (p + 1) * (nch / 2);
-      for (int cc = c0; cc < c1; cc++) {
-        int c = c0 + ((cc - c0 + r) % (c1 - c0));
+      const int c0 = p * (nch / 2), c1 = (p + 1) * (nch / 2), span = c1 - c0;
+      for (int cc = 0; cc < span; cc++) {
+        int c = c0 + (cc + r) % span;
         uint2 v = *(const uint2 *)(rp + c * 32 + 8 * q);
         int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
-        a[0] = dp2a_lo_su(xv.x, v.x, a[0]);
-        a[1] = dp2a_hi_su(xv.y, v.x, a[1]);
-        a[2] = dp2a_lo_su(xv.z, v.y, a[2]);
-        a[3] = dp2a_hi_su(xv.w, v.y, a[3]);
+        acc[0] = dp2a_lo_su(xv.x, v.x, acc[0]);
+        acc[1] = dp2a_hi_su(xv.y, v.x, acc[1]);
+        acc[2] = dp2a_lo_su(xv.z, v.y, acc[2]);
+        acc[3] = dp2a_hi_su(xv.w, v.y, acc[3]);
       }
     }
     int *ln = sm.lanes + (p * 32 + r) * 16 + 4 * q;
 #pragma unroll
-    for (int j = 0; j < 4; j++) ln[j] = a[j];
+    for (int j = 0; j < 4; j++) ln[j] = acc[j];
   }
-  consumers_sync();
+  cta_sync();
   if (threadIdx.x < 128) {
     const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
     const int rr = r < R ? r : 0;
-    int zp = zpp[rr];
-    float sc = __half2float(__ushort_as_half(scl[rr]));
+    const int zp = zpp[rr];
+    const float sc = __half2float(__ushort_as_half(scl[rr]));
     float f[4];
 #pragma unroll
     for (int j = 0; j < 4; j++) {
@@ -460,20 +471,29 @@ __device__ void mk_rows_ch8(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, 
     for (int j = 0; j < 4; j++) b[j] = f[j] + __shfl_xor_sync(0xffffffffu, f[j], 2);
 #pragma unroll
     for (int j = 0; j < 4; j++) b[j] = b[j] + __shfl_xor_sync(0xffffffffu, b[j], 1);
-    float dot = (b[0] + b[2]) + (b[1] + b[3]);
-    if (q == 0 && r < R) emit(r, dot);
+    const float dot = (b[0] + b[2]) + (b[1] + b[3]);
+    if (q == 0 && r < R) {
+      const int o = ch.r0 + r;
+      const float v = dot * sx;
+      if (logits) logits[o] = v;
+      const int t = threadIdx.x;
+      if (better(v, o, sm.thr_v[t], sm.thr_i[t])) {
+        sm.thr_v[t] = v;
+        sm.thr_i[t] = o;
+      }
+    }
   }
-  consumers_sync();
+  cta_sync();
 }
 
 // Starts copying this head's cached keys, values and their scales for
 // positions [0, pos) into shared memory (pos <= MK_KV_STAGE); mk_attention
 // waits for them. Issued early so that the copies overlap the QKV phase.
-__device__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l, int h, int pos) {
+__device__ __noinline__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l, int h, int pos) {
   if (pos > MK_KV_STAGE) return;
   const size_t row0 = ((size_t)l * a.kv.max_t) * a.kv.n_head + h;  // slot of position 0
   const size_t stride = a.kv.n_head;
-  for (int i = threadIdx.x; i < pos * 8; i += MK_CONSUMERS) {
+  for (int i = threadIdx.x; i < pos * 8; i += MK_THREADS) {
     int s = i >> 3, part = i & 7;  // parts 0-3: key, 4-7: value (16 bytes each)
     size_t slot = row0 + s * stride;
     if (part < 4)
@@ -481,7 +501,7 @@ __device__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l, int h, int 
     else
       cp_async16(&sm.vst[s][(part - 4) * 16], a.kv.v + slot * 64 + (part - 4) * 16);
   }
-  for (int i = threadIdx.x; i < pos * 2; i += MK_CONSUMERS) {
+  for (int i = threadIdx.x; i < pos * 2; i += MK_THREADS) {
     int s = i >> 1;
     size_t slot = row0 + s * stride;
     if (i & 1)
@@ -489,13 +509,15 @@ __device__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l, int h, int 
     else
       cp_async4(&sm.kss[s], a.kv.ks + slot);
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
+  cp_async_commit();
 }
 
-// Attention phase of head h (QuantKV[8]): store the token's key and value,
-// then attend over positions 0..pos (attend_float_one, kvcache.mojo:113-150).
+// Attention phase of head h (QuantKV[8]): store the token's key and value
+// (QuantKV.store, kvcache.mojo:333-342), then attend over positions 0..pos
+// (attend_float_one, kvcache.mojo:113-150) and publish att[h*64 .. +64).
 // Returns false on timeout.
-__device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int l, int h, int pos, unsigned flag) {
+__device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int l, int h, int pos,
+                                          unsigned flag) {
   const int HS = a.kv.head_dim, C = a.C;
   const int tid = threadIdx.x;
   // poll q, k, v of head h (3 x 64 words)
@@ -511,23 +533,24 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
         if (!mk_alive(a, sm, t0, 2)) break;
       }
       float x = __uint_as_float((unsigned)v);
-      if (which == 0) sm.att_q[d] = x;
-      else sm.xf[(which - 1) * 64 + d] = x;
+      if (which == 0)
+        sm.att_q[d] = x;
+      else
+        sm.xf[(which - 1) * 64 + d] = x;
     }
-    consumers_sync();
+    cta_sync();
     if (sm.abort) return false;
   }
   // store: per-head int8 quantization of k and v (QuantKV.quantize).
   const size_t sl = ((size_t)l * a.kv.max_t + pos) * a.kv.n_head + h;
   if (tid < 64) {
     for (int which = 0; which < 2; which++) {
-      float x = sm.xf[which * 64 + tid];
-      float m = fabsf(x);
+      float m = fabsf(sm.xf[which * 64 + tid]);
       for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
       if ((tid & 31) == 0) sm.red[48 + which * 2 + (tid >> 5)] = m;
     }
   }
-  consumers_sync();
+  cta_sync();
   if (tid < 64) {
     for (int which = 0; which < 2; which++) {
       float m = fmaxf(sm.red[48 + which * 2], sm.red[49 + which * 2]);
@@ -548,11 +571,11 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
   }
   const bool staged = pos <= MK_KV_STAGE;
   cp_async_wait_all();
-  consumers_sync();
+  cta_sync();
   const int npos = pos + 1;
   const float scale = 1.0f / sqrtf((float)HS);
   float mx = -__int_as_float(0x7f800000);
-  for (int s = tid; s < npos; s += MK_CONSUMERS) {
+  for (int s = tid; s < npos; s += MK_THREADS) {
     size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
     const int8_t *kp = (s == pos) ? sm.att_k : (staged ? sm.kst[s] : a.kv.k + ss * HS);
     float ksc = (s == pos || !staged) ? a.kv.ks[ss] : sm.kss[s];
@@ -578,12 +601,12 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((tid & 31) == 0) sm.red[tid >> 5] = mx;
-  consumers_sync();
+  cta_sync();
   mx = sm.red[0];
 #pragma unroll
-  for (int w = 1; w < MK_CONSUMERS / 32; w++) mx = fmaxf(mx, sm.red[w]);
-  for (int s = tid; s < npos; s += MK_CONSUMERS) sm.att_sc[s] = lm_expf(sm.att_sc[s] - mx);
-  consumers_sync();
+  for (int w = 1; w < MK_THREADS / 32; w++) mx = fmaxf(mx, sm.red[w]);
+  for (int s = tid; s < npos; s += MK_THREADS) sm.att_sc[s] = lm_expf(sm.att_sc[s] - mx);
+  cta_sync();
   if (tid == 0) {
     // sequential sum in position order, 16 values loaded ahead at a time
     float total = 0.0f;
@@ -598,55 +621,112 @@ __device__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int 
     for (; s < npos; s++) total += sm.att_sc[s];
     sm.red[36] = total;
   }
-  consumers_sync();
+  cta_sync();
   const float total = sm.red[36];
-  for (int s = tid; s < npos; s += MK_CONSUMERS) {
+  for (int s = tid; s < npos; s += MK_THREADS) {
     size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
     float p = sm.att_sc[s] / total;
     sm.att_ps[s] = p * ((s == pos || !staged) ? a.kv.vs[ss] : sm.vss[s]);
   }
-  consumers_sync();
-  if (tid < HS && staged) {
+  cta_sync();
+  if (tid < HS) {
+    // acc = fma(p * vs, v, acc) over positions in order
     const int d = tid;
     float acc = 0.0f;
-    int s = 0;
-    for (; s + 16 <= pos; s += 16) {
-      float pv[16], vv[16];
+    if (staged) {
+      int s = 0;
+      for (; s + 16 <= pos; s += 16) {
+        float pv[16], vv[16];
 #pragma unroll
-      for (int k = 0; k < 16; k++) {
-        pv[k] = sm.att_ps[s + k];
-        vv[k] = (float)sm.vst[s + k][d];
+        for (int k = 0; k < 16; k++) {
+          pv[k] = sm.att_ps[s + k];
+          vv[k] = (float)sm.vst[s + k][d];
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc = fmaf(pv[k], vv[k], acc);
       }
-#pragma unroll
-      for (int k = 0; k < 16; k++) acc = fmaf(pv[k], vv[k], acc);
+      for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
+    } else {
+      const size_t stride = (size_t)a.kv.n_head * HS;
+      const int8_t *vp = a.kv.v + ((size_t)l * a.kv.max_t * a.kv.n_head + h) * HS + d;
+      for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride], acc);
     }
-    for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
-    acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
-    st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
-  } else if (tid < HS) {
-    const int d = tid;
-    const size_t stride = (size_t)a.kv.n_head * HS;
-    const int8_t *vp = a.kv.v + ((size_t)l * a.kv.max_t * a.kv.n_head + h) * HS + d;
-    float acc = 0.0f;
-    int s = 0;
-    for (; s + 4 <= pos; s += 4) {
-      float v0 = (float)vp[(size_t)s * stride], v1 = (float)vp[(size_t)(s + 1) * stride];
-      float v2 = (float)vp[(size_t)(s + 2) * stride], v3 = (float)vp[(size_t)(s + 3) * stride];
-      acc = fmaf(sm.att_ps[s], v0, acc);
-      acc = fmaf(sm.att_ps[s + 1], v1, acc);
-      acc = fmaf(sm.att_ps[s + 2], v2, acc);
-      acc = fmaf(sm.att_ps[s + 3], v3, acc);
-    }
-    for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride], acc);
     acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
     st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
   }
   return true;
 }
 
-// Loads the biases of rows [r0, r0 + n) into sm.bias (n <= 64).
-__device__ __forceinline__ void mk_bias_load(MkSmem &sm, const float *bias, int r0, int n) {
-  if (threadIdx.x < n) sm.bias[threadIdx.x] = __ldg(bias + r0 + threadIdx.x);
+// Embedding of `token` at `pos` (gpt2t.mojo:378-385) into sm.xfull.
+__device__ __noinline__ void mk_embed(const MegaArgs &a, MkSmem &sm, int token, int pos) {
+  const int C = a.C, gpr = a.head.cols / a.head.group;
+  const float *wpe = a.small + (size_t)a.n_layer * 13 * C;
+  for (int i = threadIdx.x; i < C; i += MK_THREADS) {
+    size_t gi = (size_t)token * gpr + i / a.head.group;
+    float s = __half2float(__ushort_as_half(a.head.scale[gi]));
+    float v = (float)(code_at(a.head, token, i) - (int)a.head.zp[gi]) * s;
+    sm.xfull[i] = v + wpe[(size_t)pos * C + i];
+  }
+  cta_sync();
+}
+
+// The greedy argmax over all CTAs' candidates (gpt2t.mojo:792-797) after
+// the head phase; the winner goes to sm.token (and ids[step] from CTA 0).
+// Returns false on timeout.
+__device__ __noinline__ bool mk_argmax(const MegaArgs &a, MkSmem &sm, const MkLL &ll, unsigned flag, int step) {
+  const int tid = threadIdx.x, cta = blockIdx.x, grid = gridDim.x;
+  float bv = sm.thr_v[tid];
+  int bi = sm.thr_i[tid];
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if ((tid & 31) == 0) {
+    sm.best_v[tid >> 5] = bv;
+    sm.best_i[tid >> 5] = bi;
+  }
+  cta_sync();
+  if (tid == 0) {
+    for (int w = 1; w < MK_THREADS / 32; w++)
+      if (better(sm.best_v[w], sm.best_i[w], bv, bi)) {
+        bv = sm.best_v[w];
+        bi = sm.best_i[w];
+      }
+    st_relaxed_u64(a.ll + ll.part() + 2 * cta, ll_pack(bv, flag));
+    st_relaxed_u64(a.ll + ll.part() + 2 * cta + 1, ((unsigned long long)flag << 32) | (unsigned)bi);
+  }
+  if (!mk_poll(a, sm, a.ll + ll.part(), 2 * grid, flag, sm.xf, 8)) return false;
+  if (tid < 32) {
+    float v = -__int_as_float(0x7f800000);
+    int i = 0x7fffffff;
+    for (int c = tid; c < grid; c += 32) {
+      float cv = sm.xf[2 * c];
+      int cidx = __float_as_int(sm.xf[2 * c + 1]);
+      if (better(cv, cidx, v, i)) {
+        v = cv;
+        i = cidx;
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (better(ov, oi, v, i)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    if (tid == 0) {
+      if (i == 0x7fffffff) i = 0;  // every logit NaN: the scan keeps index 0
+      sm.token = i;
+      if (cta == 0) a.ids[step] = i;
+    }
+  }
+  cta_sync();
+  return true;
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) {
@@ -657,15 +737,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   const MkLL ll(a.C, a.n_layer, grid);
   const uint8_t *stream = a.stream + a.stream_base[cta];
   const long long total_chunks = (long long)a.nchunks * a.steps;
+  const int C = a.C, C4 = 4 * C;
 
   for (int i = tid; i < a.nchunks; i += MK_THREADS) sm.chunks[i] = a.chunks[(size_t)cta * a.nchunks + i];
   if (tid == 0) {
     for (int i = 0; i < MK_NSLOT; i++) mbar_init(&sm.full[i], 1);
     sm.abort = 0;
+    int t0 = *a.first_token;
+    if (t0 < 0 || t0 >= a.V) {
+      atomicCAS(a.err, 0, 9);
+      t0 = 0;
+    }
+    sm.token = t0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  // Chunk `q` of the whole generation into its ring slot (thread 0).
+
+  long long seq = 0;  // chunks consumed
+  // Chunk q of the whole generation into its ring slot (thread 0).
   auto issue = [&](long long q) {
     const int slot = (int)(q % MK_NSLOT);
     const MkChunk &ch = sm.chunks[q % a.nchunks];
@@ -675,15 +764,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   if (tid == 0)
     for (long long q = 0; q < MK_NSLOT && q < total_chunks; q++) issue(q);
 
-  // ---------------- consumers ----------------
-  const int C = a.C, C4 = 4 * C;
-  long long seq = 0;
   // profiling (thread 0 of CTAs 0 and grid/2)
   const bool prof_on = a.prof && tid == 0 && (cta == 0 || cta == grid / 2);
   long long pacc[MK_PROF];
   for (int k = 0; k < MK_PROF; k++) pacc[k] = 0;
-  long long tlast = clock64();
   long long *pp = prof_on ? pacc : nullptr;
+  long long tlast = clock64();
   auto tick = [&](int k) {
     if (prof_on) {
       long long t = clock64();
@@ -691,19 +777,136 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       tlast = t;
     }
   };
-  auto slot_wait = [&](int &slot) -> bool {
-    slot = (int)(seq % MK_NSLOT);
+  auto slot_wait = [&]() -> int {  // slot of chunk `seq`, or -1 on timeout
+    const int slot = (int)(seq % MK_NSLOT);
     const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
     long long t0 = clock64();
     while (!mbar_try_wait(&sm.full[slot], par)) {
-      if (!mk_alive(a, sm, t0, 1)) return false;
+      if (!mk_alive(a, sm, t0, 1)) return -1;
     }
     if (prof_on) pacc[PF_RING_WAIT] += clock64() - t0;
+    return slot;
+  };
+  auto slot_release = [&]() {
+    cta_sync();  // every thread is done with the slot
+    if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
+    seq++;
+  };
+  // One GEMV phase: wait for its weights, compute, publish, release.
+  auto gemv = [&](const MkChunk &ch, int IN, float sx, int epi, unsigned long long *out, unsigned flag) -> bool {
+    const int slot = slot_wait();
+    if (slot < 0) return false;
+    mk_gemv_blk4(sm, sm.ring[slot], ch, IN, sx, epi, out, flag, pp);
+    slot_release();
     return true;
   };
-  // On a timeout every thread leaves; first each waits for its own cp.async
-  // copies, and thread 0 (bounded) for the ring's bulk copies in flight.
-  auto drain = [&]() {
+
+  const float *lnf = a.small + (size_t)a.n_layer * 13 * C + (size_t)1024 * C;
+  bool ok = true;
+  for (int step = 0; ok && step < a.steps; step++) {
+    const unsigned flag = a.flag0 + (unsigned)step;
+    const int pos = a.pos0 + step;
+    mk_embed(a, sm, sm.token, pos);
+    tick(PF_EMBED);
+    int ci = 0;  // chunk index within the token
+    for (int l = 0; ok && l < a.n_layer; l++) {
+      const float *vec = a.small + (size_t)l * 13 * C;
+      // ---- A: LN1 + QKV ----
+      {
+        if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
+        const MkChunk &ch = sm.chunks[ci++];
+        mk_params_load(sm, vec, vec + C, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
+        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
+          ok = false;
+          break;
+        }
+        tick(PF_QKV_WAIT);
+        for (int i = tid; i < C; i += MK_THREADS) sm.xf[i] = sm.xfull[i];
+        long long t0 = clock64();
+        mk_layernorm(sm);
+        sub_tick(pp, PF_LN, t0);
+        const float sx = mk_quantize(sm, C, true);
+        sub_tick(pp, PF_QUANT, t0);
+        if (!(ok = gemv(ch, C, sx, 0, a.ll + ll.qkv(l), flag))) break;
+        tick(PF_QKV);
+      }
+      // ---- B: KV store + attention (CTA h for head h) ----
+      if (cta < a.n_head) {
+        if (!(ok = mk_attention(a, sm, ll, l, cta, pos, flag))) break;
+        tick(PF_ATTN);
+      }
+      // ---- C: PROJ + residual ----
+      {
+        const MkChunk &ch = sm.chunks[ci++];
+        mk_params_load(sm, nullptr, nullptr, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
+        if (!(ok = mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4))) break;
+        tick(PF_PROJ_WAIT);
+        long long t0 = clock64();
+        cp_async_wait_all();
+        const float sx = mk_quantize(sm, C, true);
+        sub_tick(pp, PF_QUANT, t0);
+        if (!(ok = gemv(ch, C, sx, MK_RESID, a.ll + ll.xmid(l), flag))) break;
+        tick(PF_PROJ);
+      }
+      // ---- D: LN2 + FC + GELU ----
+      {
+        const MkChunk &ch = sm.chunks[ci++];
+        mk_params_load(sm, vec + 6 * C, vec + 7 * C, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
+        if (!(ok = mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5))) break;
+        tick(PF_FC_WAIT);
+        for (int i = tid; i < C; i += MK_THREADS) sm.xf[i] = sm.xfull[i];
+        long long t0 = clock64();
+        mk_layernorm(sm);
+        sub_tick(pp, PF_LN, t0);
+        const float sx = mk_quantize(sm, C, true);
+        sub_tick(pp, PF_QUANT, t0);
+        if (!(ok = gemv(ch, C, sx, MK_GELU, a.ll + ll.fc(l), flag))) break;
+        tick(PF_FC);
+      }
+      // ---- E: FCPROJ + residual ----
+      {
+        const MkChunk &ch = sm.chunks[ci++];
+        mk_params_load(sm, nullptr, nullptr, vec + 12 * C, ch.r0, ch.r1 - ch.r0);
+        if (!(ok = mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6))) break;
+        tick(PF_FCPROJ_WAIT);
+        long long t0 = clock64();
+        cp_async_wait_all();
+        const float sx = mk_quantize(sm, C4, true);
+        sub_tick(pp, PF_QUANT, t0);
+        if (!(ok = gemv(ch, C4, sx, MK_RESID, a.ll + ll.xout(l), flag))) break;
+        tick(PF_FCPROJ);
+      }
+    }
+    if (!ok) break;
+    // ---- H: LN_f + head + argmax ----
+    mk_params_load(sm, lnf, lnf + C, nullptr, 0, 0);
+    if (!(ok = mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7))) break;
+    tick(PF_HEAD_WAIT);
+    mk_layernorm(sm);
+    const float sx = mk_quantize(sm, C, false);
+    sm.thr_v[tid] = -__int_as_float(0x7f800000);
+    sm.thr_i[tid] = 0x7fffffff;
+    for (; ci < a.nchunks; ci++) {
+      const int slot = slot_wait();
+      if (slot < 0) {
+        ok = false;
+        break;
+      }
+      mk_head_tile(sm, sm.ring[slot], sm.chunks[ci], C, sx, a.logits);
+      slot_release();
+    }
+    if (!ok) break;
+    tick(PF_HEAD);
+    // ---- I: global argmax (every CTA) ----
+    if (!(ok = mk_argmax(a, sm, ll, flag, step))) break;
+    tick(PF_ARGMAX);
+    if (prof_on) pacc[PF_STEPS] += 1;
+  }
+
+  if (!ok) {
+    // On a timeout every thread leaves; first each waits for its own
+    // cp.async copies, and thread 0 (bounded) for the ring's bulk copies in
+    // flight.
     cp_async_wait_all();
     if (tid == 0) {
       for (long long q = seq; q < seq + MK_NSLOT && q < total_chunks; q++) {
@@ -714,244 +917,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         }
       }
     }
-  };
-  auto slot_release = [&](int slot) {
-    consumers_sync();  // every thread is done with the slot
-    if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
-    seq++;
-  };
-
-  if (tid == 0) {
-    int t0 = *a.first_token;
-    if (t0 < 0 || t0 >= a.V) {
-      atomicCAS(a.err, 0, 9);
-      t0 = 0;
-    }
-    sm.token = t0;
-  }
-  consumers_sync();
-  int token = sm.token;
-  const float *wpe = a.small + (size_t)a.n_layer * 13 * C;
-  const float *lnf = wpe + (size_t)1024 * C;
-
-  for (int step = 0; step < a.steps; step++) {
-    const unsigned flag = a.flag0 + (unsigned)step;
-    const int pos = a.pos0 + step;
-    // embedding of the token (every CTA, the whole row)
-    {
-      const int gpr = a.head.cols / a.head.group;
-      for (int i = tid; i < C; i += MK_CONSUMERS) {
-        size_t gi = (size_t)token * gpr + i / a.head.group;
-        float s = half_bits_to_float(a.head.scale[gi]);
-        float v = (float)(code_at(a.head, token, i) - (int)a.head.zp[gi]) * s;
-        sm.xfull[i] = v + wpe[(size_t)pos * C + i];
-      }
-      consumers_sync();
-      tick(PF_EMBED);
-    }
-    int ci = 0;  // chunk index within the token
-    for (int l = 0; l < a.n_layer; l++) {
-      const float *vec = a.small + (size_t)l * 13 * C;
-      // ---- A: LN1 + QKV ----
-      {
-        if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
-        const MkChunk ch = sm.chunks[ci++];
-        LnParams lp = ln_load(vec, vec + C);
-        mk_bias_load(sm, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
-        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
-          drain();
-          return;
-        }
-        tick(PF_QKV_WAIT);
-        for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
-        consumers_sync();
-        mk_layernorm(sm, lp, pp);
-        const float sx = mk_quantize(sm, C, true, pp);
-        int slot;
-        if (!slot_wait(slot)) {
-          drain();
-          return;
-        }
-        unsigned long long *dst = a.ll + ll.qkv(l);
-        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
-          float v = dot * sx + sm.bias[r];
-          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        }, pp);
-        slot_release(slot);
-        tick(PF_QKV);
-      }
-      // ---- B: KV store + attention (CTA h for head h) ----
-      if (cta < a.n_head) {
-        if (!mk_attention(a, sm, ll, l, cta, pos, flag)) {
-          drain();
-          return;
-        }
-        tick(PF_ATTN);
-      }
-      // ---- C: PROJ + residual ----
-      {
-        const MkChunk ch = sm.chunks[ci++];
-        mk_bias_load(sm, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4)) {
-          drain();
-          return;
-        }
-        tick(PF_PROJ_WAIT);
-        const float sx = mk_quantize(sm, C, true, pp);
-        int slot;
-        if (!slot_wait(slot)) {
-          drain();
-          return;
-        }
-        unsigned long long *dst = a.ll + ll.xmid(l);
-        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
-          float v = dot * sx + sm.bias[r];
-          v += sm.xfull[ch.r0 + r];
-          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        }, pp);
-        slot_release(slot);
-        tick(PF_PROJ);
-      }
-      // ---- D: LN2 + FC + GELU ----
-      {
-        const MkChunk ch = sm.chunks[ci++];
-        LnParams lp = ln_load(vec + 6 * C, vec + 7 * C);
-        mk_bias_load(sm, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5)) {
-          drain();
-          return;
-        }
-        tick(PF_FC_WAIT);
-        for (int i = tid; i < C; i += MK_CONSUMERS) sm.xf[i] = sm.xfull[i];
-        consumers_sync();
-        mk_layernorm(sm, lp, pp);
-        const float sx = mk_quantize(sm, C, true, pp);
-        int slot;
-        if (!slot_wait(slot)) {
-          drain();
-          return;
-        }
-        unsigned long long *dst = a.ll + ll.fc(l);
-        mk_rows_blk4(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
-          float v = dot * sx + sm.bias[r];
-          v = gelu(v);
-          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        }, pp);
-        slot_release(slot);
-        tick(PF_FC);
-      }
-      // ---- E: FCPROJ + residual ----
-      {
-        const MkChunk ch = sm.chunks[ci++];
-        mk_bias_load(sm, vec + 12 * C, ch.r0, ch.r1 - ch.r0);
-        if (!mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6)) {
-          drain();
-          return;
-        }
-        tick(PF_FCPROJ_WAIT);
-        const float sx = mk_quantize(sm, C4, true, pp);
-        int slot;
-        if (!slot_wait(slot)) {
-          drain();
-          return;
-        }
-        unsigned long long *dst = a.ll + ll.xout(l);
-        mk_rows_blk4(sm, sm.ring[slot], ch, C4, [&](int r, float dot) {
-          float v = dot * sx + sm.bias[r];
-          v += sm.xfull[ch.r0 + r];
-          st_relaxed_u64(dst + ch.r0 + r, ll_pack(v, flag));
-        }, pp);
-        slot_release(slot);
-        tick(PF_FCPROJ);
-      }
-    }
-    // ---- H: LN_f + head + argmax ----
-    LnParams lp = ln_load(lnf, lnf + C);
-    if (!mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7)) {
-          drain();
-          return;
-        }
-    tick(PF_HEAD_WAIT);
-    mk_layernorm(sm, lp, pp);
-    const float sx = mk_quantize(sm, C, false, pp);
-    float bv = -__int_as_float(0x7f800000);
-    int bi = 0x7fffffff;
-    for (; ci < a.nchunks; ci++) {
-      int slot;
-      if (!slot_wait(slot)) {
-          drain();
-          return;
-        }
-      const MkChunk ch = sm.chunks[ci];
-      mk_rows_ch8(sm, sm.ring[slot], ch, C, [&](int r, float dot) {
-        int o = ch.r0 + r;
-        float v = dot * sx;
-        if (a.logits) a.logits[o] = v;
-        if (better(v, o, bv, bi)) {
-          bv = v;
-          bi = o;
-        }
-      });
-      slot_release(slot);
-    }
-    tick(PF_HEAD);
-    // CTA argmax
-    for (int o = 16; o > 0; o >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (better(ov, oi, bv, bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if ((tid & 31) == 0) {
-      sm.best_v[tid >> 5] = bv;
-      sm.best_i[tid >> 5] = bi;
-    }
-    consumers_sync();
-    if (tid == 0) {
-      for (int w = 1; w < MK_CONSUMERS / 32; w++)
-        if (better(sm.best_v[w], sm.best_i[w], bv, bi)) {
-          bv = sm.best_v[w];
-          bi = sm.best_i[w];
-        }
-      st_relaxed_u64(a.ll + ll.part() + 2 * cta, ll_pack(bv, flag));
-      st_relaxed_u64(a.ll + ll.part() + 2 * cta + 1, ((unsigned long long)flag << 32) | (unsigned)bi);
-    }
-    // ---- I: global argmax (every CTA) ----
-    if (!mk_poll(a, sm, a.ll + ll.part(), 2 * grid, flag, sm.xf, 8)) {
-          drain();
-          return;
-        }
-    if (tid < 32) {
-      float v = -__int_as_float(0x7f800000);
-      int i = 0x7fffffff;
-      for (int c = tid; c < grid; c += 32) {
-        float cv = sm.xf[2 * c];
-        int cidx = __float_as_int(sm.xf[2 * c + 1]);
-        if (better(cv, cidx, v, i)) {
-          v = cv;
-          i = cidx;
-        }
-      }
-      for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        int oi = __shfl_xor_sync(0xffffffffu, i, o);
-        if (better(ov, oi, v, i)) {
-          v = ov;
-          i = oi;
-        }
-      }
-      if (tid == 0) {
-        if (i == 0x7fffffff) i = 0;  // every logit NaN: the scan keeps index 0
-        sm.token = i;
-        if (cta == 0) a.ids[step] = i;
-      }
-    }
-    consumers_sync();
-    token = sm.token;
-    tick(PF_ARGMAX);
-    if (prof_on) pacc[PF_STEPS] += 1;
+    return;
   }
   if (prof_on) {
     long long *dst = a.prof + (cta == 0 ? 0 : MK_PROF);
