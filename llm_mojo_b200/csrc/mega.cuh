@@ -223,6 +223,7 @@ __device__ __noinline__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsign
       }
     if (pending && !mk_alive(a, sm, t0, code)) break;
   }
+  cp_async_wait_all();  // parameters prefetched before the wait are then visible after the barrier
   cta_sync();
   return !sm.abort;
 }
@@ -241,13 +242,13 @@ __device__ __forceinline__ void mk_params_load(MkSmem &sm, const float *lnw, con
   cp_async_commit();
 }
 
-// LayerNorm of sm.xf[0..768) in place with sm.lnw / sm.lnb
+// LayerNorm of src[0..768) into sm.xf with sm.lnw / sm.lnb
 // (kernels.mojo:179-197): 16 lane sums, each sequential over the row's
-// 16-float chunks, reduced by the halving tree.
-__device__ __noinline__ void mk_layernorm(MkSmem &sm) {
+// 16-float chunks, reduced by the halving tree. The parameters were
+// prefetched and the row published by the preceding mk_poll barrier.
+// Returns this thread's max |output| (for mk_quantize).
+__device__ __noinline__ float mk_layernorm(MkSmem &sm, const float *src) {
   const int C = 768;
-  cp_async_wait_all();
-  cta_sync();
   if (threadIdx.x < 32) {
     const int l = threadIdx.x & 15;
     float s = 0.0f;
@@ -255,7 +256,7 @@ __device__ __noinline__ void mk_layernorm(MkSmem &sm) {
     for (int k0 = 0; k0 < 48; k0 += 16) {
       float v[16];
 #pragma unroll
-      for (int k = 0; k < 16; k++) v[k] = sm.xf[16 * (k0 + k) + l];
+      for (int k = 0; k < 16; k++) v[k] = src[16 * (k0 + k) + l];
 #pragma unroll
       for (int k = 0; k < 16; k++) s = s + v[k];
     }
@@ -265,7 +266,7 @@ __device__ __noinline__ void mk_layernorm(MkSmem &sm) {
     for (int k0 = 0; k0 < 48; k0 += 16) {
       float v[16];
 #pragma unroll
-      for (int k = 0; k < 16; k++) v[k] = sm.xf[16 * (k0 + k) + l];
+      for (int k = 0; k < 16; k++) v[k] = src[16 * (k0 + k) + l];
 #pragma unroll
       for (int k = 0; k < 16; k++) {
         float d = v[k] - mean;
@@ -280,20 +281,29 @@ __device__ __noinline__ void mk_layernorm(MkSmem &sm) {
   }
   cta_sync();
   const float mean = sm.red[40], rstd = sm.red[41];
+  float mx = 0.0f;
   for (int i = threadIdx.x; i < C; i += MK_THREADS) {
-    float n = (sm.xf[i] - mean) * rstd;
-    sm.xf[i] = n * sm.lnw[i] + sm.lnb[i];
+    float n = (src[i] - mean) * rstd;
+    float o = n * sm.lnw[i] + sm.lnb[i];
+    sm.xf[i] = o;
+    mx = fmaxf(mx, fabsf(o));
   }
-  cta_sync();
+  return mx;
 }
 
-// quantize_rows of sm.xf[0..IN) into sm.xq (kernels.mojo:400-416): the
+// This thread's max |sm.xf[i]| over its elements of [0, IN).
+__device__ __forceinline__ float mk_local_max(const MkSmem &sm, int IN) {
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < IN; i += MK_THREADS) mx = fmaxf(mx, fabsf(sm.xf[i]));
+  return mx;
+}
+
+// quantize_rows of sm.xf[0..IN) into sm.xq (kernels.mojo:400-416), given
+// each thread's max |x| of its elements (mk_local_max or mk_layernorm): the
 // BLOCKED lane order and lane sums when blocked (permute_x_i16,
 // tensor.mojo:498-516), natural order and per-lane pair sums otherwise.
 // Returns sx.
-__device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
-  float mx = 0.0f;
-  for (int i = threadIdx.x; i < IN; i += MK_THREADS) mx = fmaxf(mx, fabsf(sm.xf[i]));
+__device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked, float mx) {
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = mx;
   cta_sync();
@@ -304,20 +314,19 @@ __device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked) {
   if (s == 0.0f) s = 1.0f;
   const float inv = 1.0f / s;
   if (blocked) {
-    for (int col = threadIdx.x; col < IN; col += MK_THREADS) {
-      int blk = col >> 8, w = col & 255, e = w & 31, p = e >> 1;
-      int lane = (w >> 5) + 8 * (p >> 3);
-      sm.xq[blk * 256 + (p & 7) * 32 + 2 * lane + (e & 1)] = (int16_t)roundf(sm.xf[col] * inv);
-    }
-    cta_sync();
-    // lane L of block blk: the 8 code pairs at blk*128 + s*16 + L
-    const int *xp32 = (const int *)sm.xq;
+    // Thread (blk, L) owns lane L of 256-block blk: the 16 columns
+    // blk*256 + (L%8)*32 + (L/8)*16 + e. Column e sits at step (e/2)%8, half
+    // e%2 of the lane's pair; the lane sum is their total.
+    int *xp32 = (int *)sm.xq;
     for (int i = threadIdx.x; i < IN / 16; i += MK_THREADS) {
-      int blk = i >> 4, lane = i & 15, sum = 0;
+      const int blk = i >> 4, L = i & 15;
+      const float *src = sm.xf + blk * 256 + (L & 7) * 32 + (L >> 3) * 16;
+      int sum = 0;
 #pragma unroll
       for (int st = 0; st < 8; st++) {
-        int pr = xp32[blk * 128 + st * 16 + lane];
-        sum += (int)(int16_t)(pr & 0xFFFF) + (pr >> 16);
+        int c0 = (int)roundf(src[2 * st] * inv), c1 = (int)roundf(src[2 * st + 1] * inv);
+        sum += c0 + c1;
+        xp32[blk * 128 + st * 16 + L] = (c0 & 0xFFFF) | (c1 << 16);
       }
       ((float *)sm.xs)[i] = (float)sum;
     }
@@ -787,8 +796,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     if (prof_on) pacc[PF_RING_WAIT] += clock64() - t0;
     return slot;
   };
+  // Called after the barrier that ends the use of the slot (the last one in
+  // mk_gemv_blk4 / mk_head_tile).
   auto slot_release = [&]() {
-    cta_sync();  // every thread is done with the slot
     if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
     seq++;
   };
@@ -816,16 +826,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
         const MkChunk &ch = sm.chunks[ci++];
         mk_params_load(sm, vec, vec + C, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
-        if (l > 0 && !mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
+        if (l == 0) {  // x is this CTA's embedding; only the parameters to wait for
+          cp_async_wait_all();
+          cta_sync();
+        } else if (!mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
           ok = false;
           break;
         }
         tick(PF_QKV_WAIT);
-        for (int i = tid; i < C; i += MK_THREADS) sm.xf[i] = sm.xfull[i];
         long long t0 = clock64();
-        mk_layernorm(sm);
+        const float lmx = mk_layernorm(sm, sm.xfull);
         sub_tick(pp, PF_LN, t0);
-        const float sx = mk_quantize(sm, C, true);
+        const float sx = mk_quantize(sm, C, true, lmx);
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, 0, a.ll + ll.qkv(l), flag))) break;
         tick(PF_QKV);
@@ -842,8 +854,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         if (!(ok = mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4))) break;
         tick(PF_PROJ_WAIT);
         long long t0 = clock64();
-        cp_async_wait_all();
-        const float sx = mk_quantize(sm, C, true);
+        const float sx = mk_quantize(sm, C, true, mk_local_max(sm, C));
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, MK_RESID, a.ll + ll.xmid(l), flag))) break;
         tick(PF_PROJ);
@@ -854,11 +865,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         mk_params_load(sm, vec + 6 * C, vec + 7 * C, vec + 8 * C, ch.r0, ch.r1 - ch.r0);
         if (!(ok = mk_poll(a, sm, a.ll + ll.xmid(l), C, flag, sm.xfull, 5))) break;
         tick(PF_FC_WAIT);
-        for (int i = tid; i < C; i += MK_THREADS) sm.xf[i] = sm.xfull[i];
         long long t0 = clock64();
-        mk_layernorm(sm);
+        const float lmx = mk_layernorm(sm, sm.xfull);
         sub_tick(pp, PF_LN, t0);
-        const float sx = mk_quantize(sm, C, true);
+        const float sx = mk_quantize(sm, C, true, lmx);
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, MK_GELU, a.ll + ll.fc(l), flag))) break;
         tick(PF_FC);
@@ -870,8 +880,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         if (!(ok = mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6))) break;
         tick(PF_FCPROJ_WAIT);
         long long t0 = clock64();
-        cp_async_wait_all();
-        const float sx = mk_quantize(sm, C4, true);
+        const float sx = mk_quantize(sm, C4, true, mk_local_max(sm, C4));
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C4, sx, MK_RESID, a.ll + ll.xout(l), flag))) break;
         tick(PF_FCPROJ);
@@ -882,8 +891,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     mk_params_load(sm, lnf, lnf + C, nullptr, 0, 0);
     if (!(ok = mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7))) break;
     tick(PF_HEAD_WAIT);
-    mk_layernorm(sm);
-    const float sx = mk_quantize(sm, C, false);
+    const float sx = mk_quantize(sm, C, false, mk_layernorm(sm, sm.xf));
     sm.thr_v[tid] = -__int_as_float(0x7f800000);
     sm.thr_i[tid] = 0x7fffffff;
     for (; ci < a.nchunks; ci++) {
