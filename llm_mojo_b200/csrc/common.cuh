@@ -110,6 +110,17 @@ LLMQ_HD float gelu(float r) {
   return (0.5f * r) * (1.0f + lm_tanhf(s * inner));
 }
 
+// round(x), halfway cases away from zero (Mojo's `round`), as an int, for
+// |x| < 2^31: the nearest-even integer from one rounding instruction, then
+// exact ties moved away from zero (x - rint(x) is exact here, and x +- 0.5
+// is an exact integer at a tie).
+__device__ __forceinline__ int round_away(float x) {
+  float r = rintf(x);
+  float d = x - r;
+  if (fabsf(d) == 0.5f) r = x + copysignf(0.5f, x);
+  return (int)r;
+}
+
 // s16 x u8 pair products: c + a.lo16*b.byte0 + a.hi16*b.byte1 (lo) or with
 // bytes 2 and 3 (hi). Exact int32 arithmetic (wraps mod 2^32).
 __device__ __forceinline__ int dp2a_lo_su(int a, unsigned b, int c) {

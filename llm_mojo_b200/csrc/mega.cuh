@@ -44,6 +44,9 @@ constexpr int MK_KV_STAGE = 256;   // cache positions an attention CTA stages in
 constexpr int MK_LANES = 4096;     // int32 lane sums held at once
 constexpr int MK_MAX_CHUNKS = 64;  // chunks per CTA per token
 constexpr int MK_POLL = 12;        // exchange words a thread polls at once (n <= 3072)
+#ifndef MK_BACKOFF_NS
+#define MK_BACKOFF_NS 200           // pause between unsuccessful poll rounds
+#endif
 
 enum { PH_QKV = 0, PH_PROJ = 1, PH_FC = 2, PH_FCPROJ = 3, PH_HEAD = 4 };
 
@@ -221,7 +224,10 @@ __device__ __noinline__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsign
         dst[tid + k * MK_THREADS] = __uint_as_float((unsigned)v[k]);
         pending &= ~(1u << k);
       }
-    if (pending && !mk_alive(a, sm, t0, code)) break;
+    if (pending) {
+      if (!mk_alive(a, sm, t0, code)) break;
+      __nanosleep(MK_BACKOFF_NS);  // spaces the rounds: less load on the L2 lines being polled
+    }
   }
   cp_async_wait_all();  // parameters prefetched before the wait are then visible after the barrier
   cta_sync();
@@ -313,10 +319,10 @@ __device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked, floa
   float s = mx / 32767.0f;
   if (s == 0.0f) s = 1.0f;
   const float inv = 1.0f / s;
-  if (blocked) {
+  if (blocked && IN > 768) {
     // Thread (blk, L) owns lane L of 256-block blk: the 16 columns
-    // blk*256 + (L%8)*32 + (L/8)*16 + e. Column e sits at step (e/2)%8, half
-    // e%2 of the lane's pair; the lane sum is their total.
+    // blk*256 + (L%8)*32 + (L/8)*16 + e. Column e sits at step e/2, half e%2
+    // of the lane's pair; the lane sum is their total.
     int *xp32 = (int *)sm.xq;
     for (int i = threadIdx.x; i < IN / 16; i += MK_THREADS) {
       const int blk = i >> 4, L = i & 15;
@@ -324,14 +330,32 @@ __device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked, floa
       int sum = 0;
 #pragma unroll
       for (int st = 0; st < 8; st++) {
-        int c0 = (int)roundf(src[2 * st] * inv), c1 = (int)roundf(src[2 * st + 1] * inv);
+        int c0 = round_away(src[2 * st] * inv), c1 = round_away(src[2 * st + 1] * inv);
         sum += c0 + c1;
         xp32[blk * 128 + st * 16 + L] = (c0 & 0xFFFF) | (c1 << 16);
       }
       ((float *)sm.xs)[i] = (float)sum;
     }
+  } else if (blocked) {
+    // Element i = (blk, L, e): lane L of 256-block blk holds the 16 columns
+    // blk*256 + (L%8)*32 + (L/8)*16 + e; column e sits at step e/2, half e%2
+    // of the lane's pair. A half-warp holds one lane's 16 columns: the pair
+    // comes from the neighbouring thread and the lane sum from 4 shuffles.
+    int *xp32 = (int *)sm.xq;
+    for (int i = threadIdx.x; i < IN; i += MK_THREADS) {
+      const int e = i & 15, L = (i >> 4) & 15, blk = i >> 8;
+      const int c = round_away(sm.xf[blk * 256 + (L & 7) * 32 + (L >> 3) * 16 + e] * inv);
+      const int nb = __shfl_xor_sync(0xffffffffu, c, 1);
+      if ((e & 1) == 0) xp32[blk * 128 + (e >> 1) * 16 + L] = (c & 0xFFFF) | (nb << 16);
+      int sum = c;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      if (e == 0) ((float *)sm.xs)[blk * 16 + L] = (float)sum;
+    }
   } else {
-    for (int i = threadIdx.x; i < IN; i += MK_THREADS) sm.xq[i] = (int16_t)roundf(sm.xf[i] * inv);
+    for (int i = threadIdx.x; i < IN; i += MK_THREADS) sm.xq[i] = (int16_t)round_away(sm.xf[i] * inv);
     cta_sync();
     if (threadIdx.x < 16) {
       int L = threadIdx.x, sum = 0;
@@ -390,36 +414,28 @@ __device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const
     }
     cta_sync();
     sub_tick(pacc, PF_INT, t0);
-    // float phase: thread (row, q), 64 rows per pass; lanes 2q, 2q+1 (groups
-    // 2q, 2q+1, first halves) and 2q+8, 2q+9 (their second halves).
-    {
-      const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
+    // float phase: 16 threads per row, thread L carries lane L's chain over
+    // the row's blocks; the 16 lanes then add as a halving tree (xor 8, 4,
+    // 2, 1 within the half-warp).
+    for (int r0 = 0; r0 < rows; r0 += MK_THREADS / 16) {
+      const int L = threadIdx.x & 15, r = r0 + (threadIdx.x >> 4);
       const int rr = r < rows ? r : 0;
-      float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint8_t *zrow = zpp + (rbase + rr) * gpr + (L & 7);
+      const uint16_t *srow = scl + (rbase + rr) * gpr + (L & 7);
+      const int *lrow = sm.lanes + rr * nblk * 16 + L;
+      float f = 0.0f;
       for (int b = 0; b < nblk; b++) {
-        const int g0 = (rbase + rr) * gpr + b * 8 + 2 * q;
-        const unsigned zp2 = *(const uint16_t *)(zpp + g0);
-        const __half2 sc2 = *(const __half2 *)(scl + g0);
-        const float zp0 = (float)(zp2 & 0xFF), zp1 = (float)(zp2 >> 8);
-        const float sc0 = __low2float(sc2), sc1 = __high2float(sc2);
-        const int2 la = *(const int2 *)(sm.lanes + (rr * nblk + b) * 16 + 2 * q);
-        const int2 lb = *(const int2 *)(sm.lanes + (rr * nblk + b) * 16 + 2 * q + 8);
-        const float2 xa = *(const float2 *)(xs + b * 16 + 2 * q);
-        const float2 xb = *(const float2 *)(xs + b * 16 + 2 * q + 8);
-        f[0] = fmaf((float)la.x - zp0 * xa.x, sc0, f[0]);
-        f[1] = fmaf((float)la.y - zp1 * xa.y, sc1, f[1]);
-        f[2] = fmaf((float)lb.x - zp0 * xb.x, sc0, f[2]);
-        f[3] = fmaf((float)lb.y - zp1 * xb.y, sc1, f[3]);
+        const float zp = (float)zrow[b * 8];
+        const float sc = __half2float(__ushort_as_half(srow[b * 8]));
+        f = fmaf((float)lrow[b * 16] - zp * xs[b * 16 + L], sc, f);
       }
-      float a0 = f[0] + f[2], a1 = f[1] + f[3];
-      a0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 2);
-      a1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 2);
-      float c0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 1);
-      float c1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
-      float dot = c0 + c1;
-      if (q == 0 && r < rows) {
+      f = f + __shfl_xor_sync(0xffffffffu, f, 8);
+      f = f + __shfl_xor_sync(0xffffffffu, f, 4);
+      f = f + __shfl_xor_sync(0xffffffffu, f, 2);
+      f = f + __shfl_xor_sync(0xffffffffu, f, 1);
+      if (L == 0 && r < rows) {
         const int rl = rbase + r, o = ch.r0 + rl;
-        float v = dot * sx + sm.bias[rl];
+        float v = f * sx + sm.bias[rl];
         if (epi & MK_GELU) v = gelu(v);
         if (epi & MK_RESID) v += sm.xfull[o];
         st_relaxed_u64(out + o, ll_pack(v, flag));
@@ -540,6 +556,7 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
         v = ld_relaxed_u64(src);
         if ((unsigned)(v >> 32) == flag) break;
         if (!mk_alive(a, sm, t0, 2)) break;
+        __nanosleep(MK_BACKOFF_NS);
       }
       float x = __uint_as_float((unsigned)v);
       if (which == 0)
