@@ -145,6 +145,88 @@ def run_reference(args):
     return 0
 
 
+SWEEP_SHAPES = [(2304, 768), (768, 768), (3072, 768), (768, 3072), (50257, 768)]  # (out, in)
+SWEEP_AFFINE = ["int8-g32", "int8-g64", "int8-g128", "int8-ch", "int4-g32", "int4-g64", "int4-g128", "int4-ch"]
+
+
+def run_sweep(args):
+    """Config 1: x ~ N(0,1) (seed 1), W ~ N(0, 0.02) quantized per format;
+    GB/s of packed weight bytes per one-token GEMV, L2 flushed before each
+    timed launch, median of args.steps launches."""
+    import ctypes as C
+
+    import torch
+
+    from llm_mojo_b200 import build
+    from llm_mojo_b200 import gguf_blocks as G
+    from llm_mojo_b200._lib import BIAS, check, lib
+    from llm_mojo_b200.tensor import Context, DenseMatrix, GGUFMatrix, QuantMatrix, parse_dtype
+
+    build.build()
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    peak, peak_kind = peaks()
+    rng = np.random.default_rng(1)
+    for out_, in_ in SWEEP_SHAPES:
+        src = (np.random.default_rng(out_ * 7 + in_).standard_normal((in_, out_), dtype=np.float32) *
+               np.float32(0.02)).astype(np.float32)  # [IN, OUT] (Hugging Face layout)
+        x = torch.from_numpy(rng.standard_normal(in_).astype(np.float32)).cuda()
+        b = torch.zeros(out_, dtype=torch.float32, device="cuda")
+        y = torch.zeros(out_, dtype=torch.float32, device="cuda")
+        cases = []
+        for f in SWEEP_AFFINE:
+            bits, group, sym, _ = parse_dtype(f)
+            cases.append((f + "-a16", lambda bits=bits, group=group, sym=sym:
+                          QuantMatrix.from_f32(ctx, src, bits, group, sym, True, True)))
+            cases.append((f, lambda bits=bits, group=group, sym=sym:
+                          QuantMatrix.from_f32(ctx, src, bits, group, sym, False, True)))
+        for t in (G.Q4_0, G.Q4_1, G.Q8_0, G.Q4_K, G.Q5_K, G.Q6_K):
+            cases.append((G.NAMES[t], lambda t=t: GGUFMatrix(ctx, t, G.quantize(np.ascontiguousarray(src.T), t),
+                                                            out_, in_)))
+        for dt in ("f32", "f16", "bf16"):
+            # layer matrices stay [IN, OUT]; the head is wte [V, C]
+            cases.append((dt, lambda dt=dt: DenseMatrix(ctx, dt, src if out_ != 50257 else np.ascontiguousarray(src.T))))
+        for name, make in cases:
+            try:
+                w = make()
+            except Exception as e:  # a format the shape does not divide into
+                print(json.dumps({"workload": "config 1 GEMV sweep", "format": name, "shape": [out_, in_],
+                                  "skipped": str(e)[:80]}))
+                continue
+            is_head = out_ == 50257
+            def launch():
+                if is_head:
+                    check(lib().llmq_head(ctx.h, w.h, C.c_void_p(x.data_ptr()), C.c_void_p(y.data_ptr()), 1, in_,
+                                          out_), ctx.h)
+                else:
+                    check(lib().llmq_linear(ctx.h, w.h, C.c_void_p(x.data_ptr()), C.c_void_p(b.data_ptr()),
+                                            C.c_void_p(y.data_ptr()), 1, in_, out_, BIAS), ctx.h)
+            times = []
+            with torch.cuda.stream(stream):
+                for i in range(args.warmup + args.steps):
+                    flush.zero_()
+                    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s0.record(stream)
+                    launch()
+                    e0.record(stream)
+                    if i >= args.warmup:
+                        times.append((s0, e0))
+                stream.synchronize()
+            ms = statistics.median(s0.elapsed_time(e0) for s0, e0 in times)
+            nbytes = w.nbytes()
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            print(json.dumps({"workload": "config 1 GEMV sweep", "format": name, "shape": [out_, in_],
+                              "weight_bytes": nbytes, "us": round(ms * 1000, 2), "GB/s": round(gbs, 1),
+                              "frac_of_hbm": round(gbs / peak, 4), "peak_kind": peak_kind,
+                              "l2": "flushed before each launch"}))
+            w.free()
+    ctx.close()
+    return 0
+
+
 def config_dict(args):
     return {"workload": "config 0: GPT-2 124M batch-1 greedy decode, int4-g32-a16 layers + int8-ch head + "
                         "int8 KV, prompt [50256] then 100 tokens, random-init weights (seed 0)",
@@ -160,12 +242,17 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="decode", choices=["decode", "sweep"],
+                    help="decode: config 0 (the default bench line); sweep: config 1, the one-token GEMV of every "
+                         "format at every shape, one JSON line each")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "sweep":
+        return run_sweep(args)
 
     import torch
     import torch.distributed as dist

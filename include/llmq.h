@@ -69,18 +69,45 @@ llmq_status llmq_quantize_affine(const float *src_host, int rows, int cols, int 
 llmq_status llmq_weight_create_affine(llmq_ctx *ctx, int bits, int group, int sym, int a16, int rows, int cols,
                                       const uint8_t *codes_host, const uint16_t *scale_host,
                                       const uint8_t *zp_host, llmq_weight **out);
+/* Uploads a GGUFMatrix (gguf.mojo:344-512): `rows` rows of `cols` values in
+ * ggml block type ggml_type (0 F32, 1 F16, 2 Q4_0, 3 Q4_1, 8 Q8_0, 12 Q4_K,
+ * 13 Q5_K, 14 Q6_K), as stored in the file: rows * (cols / block) blocks. */
+llmq_status llmq_weight_create_gguf(llmq_ctx *ctx, int ggml_type, const void *blocks_host, int rows, int cols,
+                                    llmq_weight **out);
+/* Uploads a DenseMatrix[dtype] (tensor.mojo:150-227), [rows, cols] row-major
+ * as the reference stores it ([IN, OUT] layer matrices, [V, C] wte). */
+#define LLMQ_DENSE_F32 0
+#define LLMQ_DENSE_F16 1
+#define LLMQ_DENSE_BF16 2
+llmq_status llmq_weight_create_dense(llmq_ctx *ctx, int dtype, const void *data_host, int rows, int cols,
+                                     llmq_weight **out);
 /* WeightMatrix.free (tensor.mojo:658-661). */
 llmq_status llmq_weight_free(llmq_weight *w);
 /* WeightMatrix.nbytes (tensor.mojo:629-632): codes + 3 bytes per group. */
 long long llmq_weight_nbytes(const llmq_weight *w);
 
 /* ---- kernels (device pointers) ------------------------------------------ */
-/* Replaces kernels.linear (kernels.mojo:655-673) for ACT16 formats, i.e.
- * matmul_rows_a16 (:419-509): out[T, OUT] (+)= act(x[T, IN] @ w^T + b).
- * T == 1 is the decode path (dot_row_i16 via linear_team, :774-816), T > 1
- * the tile path (tile_i16, :512-573; rows_i16 for OUT % 32). */
+/* Replaces kernels.linear (kernels.mojo:655-673): out[T, OUT] (+)=
+ * act(x[T, IN] @ w + b), with the kernel for w's format:
+ *  - ACT16 affine: matmul_rows_a16 (:419-509); T == 1 is the decode path
+ *    (dot_row_i16 via linear_team, :774-816), T > 1 the tile path (tile_i16,
+ *    :512-573; rows_i16 for OUT % 32);
+ *  - other affine and GGUF formats: matmul_rows (:285-349), one token;
+ *  - dense [IN, OUT]: gemv (:132-176) split in llmq_set_dense_parts parts,
+ *    one token.
+ * Unbuilt combinations return LLMQ_ERR_UNSUPPORTED. */
 llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x_dev, const float *bias_dev,
                         float *out_dev, int T, int IN, int OUT, int flags);
+/* Replaces head (kernels.mojo:676-690): logits[T, V] = h[T, C] @ w[V, C]^T
+ * with the head kernel for w's format (head_i16 for GGUF Q8_0 / Q6_K,
+ * matmul_rows_a16 for ACT16, lm_head / lm_head_rows for dense,
+ * matmul_rows otherwise). */
+llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev, int T, int C,
+                      int V);
+/* The number of parts the dense gemv splits its reduction into (the
+ * reference's thread count, kernels.mojo:141-142 / :828-834; default 4).
+ * Results depend on it, as the reference's do. */
+llmq_status llmq_set_dense_parts(llmq_ctx *ctx, int nparts);
 /* Replaces head (kernels.mojo:676-690) + argmax (gpt2t.mojo:792-797) for one
  * token: logits[V] = h[C] @ w^T (logits_dev may be NULL) and the first index
  * of the largest logit into *argmax_dev. */

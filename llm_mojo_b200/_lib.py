@@ -37,6 +37,10 @@ SIGNATURES = {
     "llmq_quantize_affine": (I, [P, I, I, I, I, I, I, I, P, P, P]),
     "llmq_weight_create_affine": (I, [P, I, I, I, I, I, I, P, P, P, PP]),
     "llmq_weight_free": (I, [P]),
+    "llmq_weight_create_gguf": (I, [P, I, P, I, I, PP]),
+    "llmq_weight_create_dense": (I, [P, I, P, I, I, PP]),
+    "llmq_head": (I, [P, P, P, P, I, I, I]),
+    "llmq_set_dense_parts": (I, [P, I]),
     "llmq_weight_nbytes": (LL, [P]),
     "llmq_linear": (I, [P, P, P, P, P, I, I, I, I]),
     "llmq_head_argmax": (I, [P, P, P, P, P]),

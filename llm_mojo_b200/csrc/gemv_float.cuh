@@ -1,0 +1,376 @@
+// One-token matmuls with float32 arithmetic (sm_100a): dequantize-and-dot
+// for the GGUF block formats and dense rows, the affine W4A32 / W8A32 path,
+// and the dense [IN, OUT] split-K GEMV; plus the integer GGUF head.
+//
+// Reference order: every output is the reference's 16 float32 lane chains,
+// acc[l] = fma(w, x, acc[l]) over the row in its put order (gguf.mojo:
+// 166-297 each_block/dequant_q*, tensor.mojo:431-476 row_op,
+// tensor.mojo:206-210 DenseMatrix.dot_row), added by the halving tree. Here
+// 16 threads share a row, thread l carrying lane l's chain; the tree is four
+// xor shuffles. Rows of the GGUF and dense-row formats are staged through
+// shared memory: a tile of rows (contiguous bytes) per cp.async.bulk copy,
+// two stages, mbarrier completion.
+#pragma once
+
+#include "common.cuh"
+#include "gemv_a16.cuh"
+
+namespace llmq {
+
+enum {
+  RT_F32 = 0, RT_F16 = 1, RT_Q4_0 = 2, RT_Q4_1 = 3, RT_Q8_0 = 8, RT_Q4_K = 12, RT_Q5_K = 13, RT_Q6_K = 14,
+  RT_BF16 = 30  // dense bfloat16 rows (not a GGUF type)
+};
+
+__host__ __device__ inline int rt_block_size(int t) {
+  return (t == RT_F32 || t == RT_F16 || t == RT_BF16) ? 16 : (t == RT_Q4_0 || t == RT_Q4_1 || t == RT_Q8_0) ? 32 : 256;
+}
+__host__ __device__ inline int rt_block_bytes(int t) {
+  switch (t) {
+    case RT_F32: return 64;
+    case RT_F16: return 32;
+    case RT_BF16: return 32;
+    case RT_Q4_0: return 18;
+    case RT_Q4_1: return 20;
+    case RT_Q8_0: return 34;
+    case RT_Q4_K: return 144;
+    case RT_Q5_K: return 176;
+    case RT_Q6_K: return 210;
+  }
+  return 0;
+}
+
+struct RowMat {
+  const uint8_t *data;  // rows * row_bytes
+  int rows, cols, type;
+  long long row_bytes;
+};
+
+__device__ __forceinline__ float ld_f16(const uint8_t *p) {
+  return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
+}
+
+// k_scale_min (gguf.mojo:205-221).
+__device__ __forceinline__ void k_sm(const uint8_t *q, int j, int &sc, int &m) {
+  if (j < 4) {
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+// Lane L's chain over one block of type T at b (in shared memory); x is the
+// block's slice of the input.
+template <int T>
+__device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, int L, float acc) {
+  if (T == RT_Q4_0) {
+    const float d = ld_f16(b);
+    const int q = b[2 + L];
+    acc = fmaf(((float)(q & 0xF) - 8.0f) * d, x[L], acc);
+    acc = fmaf(((float)(q >> 4) - 8.0f) * d, x[16 + L], acc);
+  } else if (T == RT_Q4_1) {
+    const float d = ld_f16(b), m = ld_f16(b + 2);
+    const int q = b[4 + L];
+    acc = fmaf(d * (float)(q & 0xF) + m, x[L], acc);
+    acc = fmaf(d * (float)(q >> 4) + m, x[16 + L], acc);
+  } else if (T == RT_Q8_0) {
+    const float d = ld_f16(b);
+    acc = fmaf(d * (float)(int8_t)b[2 + L], x[L], acc);
+    acc = fmaf(d * (float)(int8_t)b[18 + L], x[16 + L], acc);
+  } else if (T == RT_Q4_K || T == RT_Q5_K) {
+    const float d = ld_f16(b), dmin = ld_f16(b + 2);
+    const uint8_t *sc = b + 4;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      int s1, m1i, s2, m2i;
+      k_sm(sc, 2 * j, s1, m1i);
+      k_sm(sc, 2 * j + 1, s2, m2i);
+      const float d1 = d * (float)s1, m1 = dmin * (float)m1i, d2 = d * (float)s2, m2 = dmin * (float)m2i;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        int lo, hi;
+        if (T == RT_Q4_K) {
+          const int q = b[16 + 32 * j + 16 * h + L];
+          lo = q & 0xF;
+          hi = q >> 4;
+        } else {
+          const int qh = b[16 + 16 * h + L], q = b[48 + 32 * j + 16 * h + L];
+          lo = (q & 0xF) | (((qh >> (2 * j)) & 1) << 4);
+          hi = (q >> 4) | (((qh >> (2 * j + 1)) & 1) << 4);
+        }
+        acc = fmaf(d1 * (float)lo - m1, x[64 * j + 16 * h + L], acc);
+        acc = fmaf(d2 * (float)hi - m2, x[64 * j + 32 + 16 * h + L], acc);
+      }
+    }
+  } else if (T == RT_Q6_K) {
+    const float d = ld_f16(b + 208);
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int lo0 = b[64 * n + 16 * h + L], lo1 = b[64 * n + 32 + 16 * h + L], hi = b[128 + 32 * n + 16 * h + L];
+        const int base = 128 * n + 16 * h;
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+          const float ds = d * (float)(int8_t)b[192 + 8 * n + h + 2 * k];
+          int q;
+          if (k == 0) q = (lo0 & 0xF) | ((hi & 3) << 4);
+          else if (k == 1) q = (lo1 & 0xF) | (((hi >> 2) & 3) << 4);
+          else if (k == 2) q = (lo0 >> 4) | (((hi >> 4) & 3) << 4);
+          else q = (lo1 >> 4) | (((hi >> 6) & 3) << 4);
+          acc = fmaf(ds * ((float)q - 32.0f), x[base + 32 * k + L], acc);
+        }
+      }
+    }
+  } else if (T == RT_F32) {
+    acc = fmaf(((const float *)b)[L], x[L], acc);
+  } else if (T == RT_F16) {
+    acc = fmaf(__half2float(((const __half *)b)[L]), x[L], acc);
+  } else if (T == RT_BF16) {
+    acc = fmaf(__uint_as_float((unsigned)((const uint16_t *)b)[L] << 16), x[L], acc);
+  }
+  return acc;
+}
+
+constexpr int RF_THREADS = 256;
+constexpr int RF_TILE_BYTES = 32 * 1024;  // bytes of rows per stage
+
+struct RowGemvArgs {
+  RowMat w;
+  const float *x;     // [cols]
+  const float *bias;  // [rows] or null
+  float *out;         // [rows]
+  int epi;            // EPI_BIAS / EPI_GELU / EPI_RESID
+};
+
+__device__ __forceinline__ unsigned rf_smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+
+// Row-major float GEMV: CTA tiles of R rows (R * row_bytes <= RF_TILE_BYTES,
+// R <= 16), two shared-memory stages filled by cp.async.bulk.
+template <int T>
+__global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int cols = a.w.cols, rb = (int)a.w.row_bytes;
+  const int R = min(16, max(1, (RF_TILE_BYTES - 32) / rb));
+  float *xs = (float *)smem;                                         // [cols]
+  unsigned long long *bar = (unsigned long long *)(smem + cols * 4);  // [2]
+  uint8_t *stage[2] = {smem + cols * 4 + 128, smem + cols * 4 + 128 + RF_TILE_BYTES};
+  const int ntiles = (a.w.rows + R - 1) / R;
+  for (int i = threadIdx.x; i < cols; i += RF_THREADS) xs[i] = a.x[i];
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rf_smem_u32(&bar[0])));
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rf_smem_u32(&bar[1])));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  // Rows [r0, r0 + n) start at byte r0 * rb, which need not be 16-byte
+  // aligned (Q6_K rows are 630 bytes for 768 columns): copy the aligned
+  // superset [floor16(r0 * rb), ceil16((r0 + n) * rb)) and read the rows at
+  // the offset. The matrix buffer has 32 bytes of padding after its end.
+  auto issue = [&](int tile, int s) {
+    const int r0 = tile * R, n = min(R, a.w.rows - r0);
+    const long long start = (long long)r0 * rb, lo = start & ~15LL, hi = (start + (long long)n * rb + 15) & ~15LL;
+    const unsigned bytes = (unsigned)(hi - lo);
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(rf_smem_u32(&bar[s])), "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            rf_smem_u32(stage[s])),
+        "l"(a.w.data + lo), "r"(bytes), "r"(rf_smem_u32(&bar[s]))
+        : "memory");
+  };
+  int it = 0;
+  if (threadIdx.x == 0 && (int)blockIdx.x < ntiles) issue(blockIdx.x, 0);
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, it++) {
+    const int s = it & 1;
+    const int next = tile + gridDim.x;
+    if (threadIdx.x == 0 && next < ntiles) issue(next, s ^ 1);
+    // wait for this tile (phase it / 2 of stage s)
+    {
+      const unsigned par = (unsigned)((it >> 1) & 1);
+      unsigned ok = 0;
+      long long t0 = clock64();
+      while (!ok) {
+        asm volatile(
+            "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(rf_smem_u32(&bar[s])), "r"(par)
+            : "memory");
+        if (!ok && clock64() - t0 > 4000000000LL) return;  // a copy never landed: give up (bounded)
+      }
+    }
+    const int r0 = tile * R, n = min(R, a.w.rows - r0);
+    const int shift = (int)(((long long)r0 * rb) & 15);
+    const int L = threadIdx.x & 15, g = threadIdx.x >> 4;
+    for (int rr = g; rr < 16; rr += RF_THREADS / 16) {  // rows of the tile handled by this half-warp
+      const bool live = rr < n;
+      const uint8_t *row = stage[s] + shift + (size_t)(live ? rr : 0) * rb;
+      float acc = 0.0f;
+      const int bs = rt_block_size(T), bb = rt_block_bytes(T);
+      for (int blk = 0; blk < cols / bs; blk++) acc = block_lane<T>(row + blk * bb, xs + blk * bs, L, acc);
+      acc = acc + __shfl_xor_sync(0xffffffffu, acc, 8);
+      acc = acc + __shfl_xor_sync(0xffffffffu, acc, 4);
+      acc = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+      if (live && L == 0) {
+        const int o = r0 + rr;
+        float v = acc;
+        if (a.epi & EPI_BIAS) v += a.bias[o];
+        if (a.epi & EPI_GELU) v = gelu(v);
+        if (a.epi & EPI_RESID) v += a.out[o];
+        a.out[o] = v;
+      }
+    }
+    __syncthreads();  // the stage is free for the tile after next
+  }
+}
+
+// Affine W4A32 / W8A32 rows (QuantMatrix.dot_row, tensor.mojo:431-482, natural
+// layout): per group, lane chains accg = fma(u - zp, x, accg) over the group's
+// 32-chunks (low half, then high half of each), then acc = fma(accg, s, acc).
+struct AffFloatArgs {
+  WeightView w;
+  const float *x;
+  const float *bias;
+  float *out;
+  int epi;
+};
+
+template <int BITS>
+__global__ void __launch_bounds__(256) affine_float_gemv_kernel(AffFloatArgs a) {
+  extern __shared__ __align__(16) float xsh[];
+  const int cols = a.w.cols, G = a.w.group, gpr = cols / G;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) xsh[i] = a.x[i];
+  __syncthreads();
+  const int L = threadIdx.x & 15;
+  for (int row = blockIdx.x * 16 + (threadIdx.x >> 4); row < a.w.rows; row += gridDim.x * 16) {
+    const uint8_t *p = a.w.codes + (size_t)row * cols * BITS / 8;
+    float acc = 0.0f;
+    for (int g = 0; g < gpr; g++) {
+      const float s = __half2float(__ushort_as_half(a.w.scale[(size_t)row * gpr + g]));
+      const float zp = (float)a.w.zp[(size_t)row * gpr + g];
+      float accg = 0.0f;
+      for (int c = 0; c < G / 32; c++) {
+        const int k0 = g * G + 32 * c;
+        float v0, v1;
+        if (BITS == 4) {
+          const int b = __ldg(p + k0 / 2 + L);
+          v0 = (float)(b & 0xF) - zp;
+          v1 = (float)(b >> 4) - zp;
+        } else {
+          v0 = (float)__ldg(p + k0 + L) - zp;
+          v1 = (float)__ldg(p + k0 + 16 + L) - zp;
+        }
+        accg = fmaf(v0, xsh[k0 + L], accg);
+        accg = fmaf(v1, xsh[k0 + 16 + L], accg);
+      }
+      acc = fmaf(accg, s, acc);
+    }
+    acc = acc + __shfl_xor_sync(0xffffffffu, acc, 8);
+    acc = acc + __shfl_xor_sync(0xffffffffu, acc, 4);
+    acc = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
+    acc = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
+    if (L == 0) {
+      float v = acc;
+      if (a.epi & EPI_BIAS) v += a.bias[row];
+      if (a.epi & EPI_GELU) v = gelu(v);
+      if (a.epi & EPI_RESID) v += a.out[row];
+      a.out[row] = v;
+    }
+  }
+}
+
+// Dense [IN, OUT] split-K GEMV (kernels.mojo:132-176 gemv, :828-865
+// linear_team): part p accumulates rows [p*rows, min(IN, (p+1)*rows)),
+// rows = ceil(IN / nparts), as one sequential fma chain per output; the
+// parts are added in order after the bias. Stage 1: thread per (part,
+// output) into scratch; stage 2: thread per output.
+template <int DT>
+__global__ void dense_gemv_parts_kernel(const void *w, const float *x, int IN, int OUT, int nparts, float *scratch) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x, p = blockIdx.y;
+  if (j >= OUT) return;
+  const int rows = (IN + nparts - 1) / nparts;
+  const int i0 = p * rows, i1 = min(IN, i0 + rows);
+  float acc = 0.0f;
+  for (int i = i0; i < i1; i++) {
+    float wv;
+    if (DT == 0) wv = __ldg((const float *)w + (size_t)i * OUT + j);
+    else if (DT == 1) wv = __half2float(((const __half *)w)[(size_t)i * OUT + j]);
+    else wv = __uint_as_float((unsigned)__ldg((const uint16_t *)w + (size_t)i * OUT + j) << 16);
+    acc = fmaf(x[i], wv, acc);
+  }
+  scratch[(size_t)p * OUT + j] = acc;
+}
+
+__global__ void dense_gemv_combine_kernel(const float *scratch, const float *bias, float *out, int OUT, int nparts,
+                                          int epi) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= OUT) return;
+  float r = (epi & EPI_BIAS) ? bias[j] : 0.0f;
+  for (int p = 0; p < nparts; p++) r += scratch[(size_t)p * OUT + j];
+  if (epi & EPI_GELU) r = gelu(r);
+  if (epi & EPI_RESID) r += out[j];
+  out[j] = r;
+}
+
+// The GGUF integer head (gguf.mojo:456-505, kernels.mojo:693-736) for one
+// token: x quantized to int16 (quantize_rows), weights as int16
+// ((q - 32) * scale for Q6_K, q for Q8_0), int32 lane sums (lane i: pair
+// 2i, 2i+1 of each 32 weights) per block (Q8_0) or superblock (Q6_K), then
+// accf = fma(f32(acc), d, accf) and the halving tree; logit = dot * sx.
+template <int T>
+__global__ void __launch_bounds__(256) gguf_head_i16_kernel(RowMat w, const float *h, float *logits) {
+  __shared__ __align__(16) int16_t xq[4096];
+  __shared__ float red[64];
+  const int cols = w.cols;
+  float mx = 0.0f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) mx = fmaxf(mx, fabsf(h[i]));
+  mx = block_max(mx, red);
+  float s = mx / 32767.0f;
+  if (s == 0.0f) s = 1.0f;
+  const float inv = 1.0f / s;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) xq[i] = (int16_t)round_away(h[i] * inv);
+  __syncthreads();
+  const int L = threadIdx.x & 15;
+  for (int row = blockIdx.x * 16 + (threadIdx.x >> 4); row < w.rows; row += gridDim.x * 16) {
+    const uint8_t *p = w.data + (size_t)row * w.row_bytes;
+    float accf = 0.0f;
+    if (T == RT_Q8_0) {
+      for (int blk = 0; blk < cols / 32; blk++) {
+        const uint8_t *b = p + blk * 34;
+        const int acc = (int)xq[blk * 32 + 2 * L] * (int)(int8_t)b[2 + 2 * L] +
+                        (int)xq[blk * 32 + 2 * L + 1] * (int)(int8_t)b[3 + 2 * L];
+        accf = fmaf((float)acc, ld_f16(b), accf);
+      }
+    } else {
+      for (int sb = 0; sb < cols / 256; sb++) {
+        const uint8_t *b = p + sb * 210;
+        int acc = 0;
+#pragma unroll
+        for (int n = 0; n < 2; n++)
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const uint8_t *Lb = b + 64 * n + ((k & 1) ? 32 : 0);
+            const uint8_t *Hb = b + 128 + 32 * n;
+            const int sc = (int8_t)b[192 + 8 * n + 2 * k + (L >= 8 ? 1 : 0)];
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+              const int j = 2 * L + e;
+              const int q = ((k >= 2) ? (Lb[j] >> 4) : (Lb[j] & 0xF)) | (((Hb[j] >> (2 * k)) & 3) << 4);
+              acc += (int)xq[sb * 256 + 128 * n + 32 * k + j] * ((q - 32) * sc);
+            }
+          }
+        accf = fmaf((float)acc, ld_f16(b + 208), accf);
+      }
+    }
+    accf = accf + __shfl_xor_sync(0xffffffffu, accf, 8);
+    accf = accf + __shfl_xor_sync(0xffffffffu, accf, 4);
+    accf = accf + __shfl_xor_sync(0xffffffffu, accf, 2);
+    accf = accf + __shfl_xor_sync(0xffffffffu, accf, 1);
+    if (L == 0) logits[row] = accf * s;
+  }
+}
+
+}  // namespace llmq

@@ -1,4 +1,5 @@
 // C ABI of the B200 quantized-matmul hot path (include/llmq.h).
+#include <algorithm>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -7,6 +8,7 @@
 #include "../../include/llmq.h"
 #include "attention.cuh"
 #include "gemv_a16.cuh"
+#include "gemv_float.cuh"
 #include "mega.cuh"
 #include "prefill_a16.cuh"
 
@@ -22,17 +24,24 @@ struct llmq_ctx {
   void *scratch = nullptr;
   size_t scratch_bytes = 0;
   DecodeState *state = nullptr;  // device, for llmq_head_argmax
+  int dense_parts = 4;           // gemv's parts: the reference team of 4 threads (gpt2t.mojo:281 on 4 cores)
 };
+
+enum { WK_AFFINE = 0, WK_GGUF = 1, WK_DENSE = 2 };
 
 struct llmq_weight {
   llmq_ctx *ctx;
-  int bits, group, sym, a16, blocked;
-  int rows, cols;
-  uint8_t *codes;
-  uint16_t *scale;
-  uint8_t *zp;
-  long long nbytes;
+  int kind = WK_AFFINE;
+  int bits = 0, group = 0, sym = 0, a16 = 0, blocked = 0;
+  int rows = 0, cols = 0;
+  uint8_t *codes = nullptr;  // affine codes; GGUF blocks; dense values
+  uint16_t *scale = nullptr;
+  uint8_t *zp = nullptr;
+  int rtype = 0;             // GGUF / dense: the RT_* row type
+  long long row_bytes = 0;
+  long long nbytes = 0;
   WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
+  RowMat rowmat() const { return RowMat{codes, rows, cols, rtype, row_bytes}; }
 };
 
 struct llmq_kv {
@@ -186,6 +195,19 @@ cudaError_t configure_kernels() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)mega_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MkSmem));
+  const int rsm = 4096 * 4 + 128 + 2 * RF_TILE_BYTES;
+  auto rs = [&](const void *k) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rsm);
+  };
+  rs((const void *)row_gemv_kernel<RT_F32>);
+  rs((const void *)row_gemv_kernel<RT_F16>);
+  rs((const void *)row_gemv_kernel<RT_BF16>);
+  rs((const void *)row_gemv_kernel<RT_Q4_0>);
+  rs((const void *)row_gemv_kernel<RT_Q4_1>);
+  rs((const void *)row_gemv_kernel<RT_Q8_0>);
+  rs((const void *)row_gemv_kernel<RT_Q4_K>);
+  rs((const void *)row_gemv_kernel<RT_Q5_K>);
+  rs((const void *)row_gemv_kernel<RT_Q6_K>);
   return e;
 }
 }  // namespace
@@ -312,6 +334,65 @@ llmq_status llmq_weight_create_affine(llmq_ctx *ctx, int bits, int group, int sy
   return LLMQ_OK;
 }
 
+llmq_status llmq_weight_create_gguf(llmq_ctx *ctx, int ggml_type, const void *blocks, int rows, int cols,
+                                    llmq_weight **out) {
+  if (!ctx || !out || !blocks || rows <= 0 || cols <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  *out = nullptr;
+  static const int types[] = {RT_F32, RT_F16, RT_Q4_0, RT_Q4_1, RT_Q8_0, RT_Q4_K, RT_Q5_K, RT_Q6_K};
+  bool known = false;
+  for (int t : types) known |= t == ggml_type;
+  if (!known) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "GGUF type " + std::to_string(ggml_type) + " not supported");
+  const int bs = (ggml_type == RT_F32 || ggml_type == RT_F16) ? 1 : rt_block_size(ggml_type);
+  const int bb = (ggml_type == RT_F32) ? 4 : (ggml_type == RT_F16) ? 2 : rt_block_bytes(ggml_type);
+  if (cols % 16 != 0 || cols % bs != 0 || cols > 4096)
+    return fail(ctx, LLMQ_ERR_INVALID, "columns must be a multiple of the block size (and of 16, at most 4096)");
+  CK(cudaSetDevice(ctx->device));
+  llmq_weight *w = new llmq_weight();
+  w->ctx = ctx;
+  w->kind = WK_GGUF;
+  w->rtype = ggml_type;
+  w->rows = rows;
+  w->cols = cols;
+  w->row_bytes = (long long)(cols / bs) * bb;
+  w->nbytes = w->row_bytes * rows;
+  cudaError_t e = cudaMalloc(&w->codes, w->nbytes + 32);  // padding: tiles are copied as 16-byte aligned supersets
+  if (e == cudaSuccess) e = cudaMemset(w->codes + w->nbytes, 0, 32);
+  if (e == cudaSuccess) e = cudaMemcpy(w->codes, blocks, w->nbytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    llmq_weight_free(w);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+  }
+  *out = w;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_weight_create_dense(llmq_ctx *ctx, int dtype, const void *data, int rows, int cols,
+                                     llmq_weight **out) {
+  if (!ctx || !out || !data || rows <= 0 || cols <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  if (dtype != LLMQ_DENSE_F32 && dtype != LLMQ_DENSE_F16 && dtype != LLMQ_DENSE_BF16)
+    return fail(ctx, LLMQ_ERR_INVALID, "dtype must be LLMQ_DENSE_F32, _F16 or _BF16");
+  if (cols % 16 != 0) return fail(ctx, LLMQ_ERR_INVALID, "columns must be a multiple of 16");
+  *out = nullptr;
+  CK(cudaSetDevice(ctx->device));
+  llmq_weight *w = new llmq_weight();
+  w->ctx = ctx;
+  w->kind = WK_DENSE;
+  w->rtype = dtype == LLMQ_DENSE_F32 ? RT_F32 : dtype == LLMQ_DENSE_F16 ? RT_F16 : RT_BF16;
+  w->rows = rows;
+  w->cols = cols;
+  w->row_bytes = (long long)cols * (dtype == LLMQ_DENSE_F32 ? 4 : 2);
+  w->nbytes = w->row_bytes * rows;
+  cudaError_t e = cudaMalloc(&w->codes, w->nbytes + 32);
+  if (e == cudaSuccess) e = cudaMemset(w->codes + w->nbytes, 0, 32);
+  if (e == cudaSuccess) e = cudaMemcpy(w->codes, data, w->nbytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    llmq_weight_free(w);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("weight upload: ") + cudaGetErrorString(e));
+  }
+  *out = w;
+  return LLMQ_OK;
+}
+
 llmq_status llmq_weight_free(llmq_weight *w) {
   if (!w) return LLMQ_ERR_INVALID;
   if (w->codes) cudaFree(w->codes);
@@ -323,15 +404,86 @@ llmq_status llmq_weight_free(llmq_weight *w) {
 
 long long llmq_weight_nbytes(const llmq_weight *w) { return w ? w->nbytes : -1; }
 
+}  // extern "C"
+
+namespace {
+template <int T>
+cudaError_t launch_row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
+  const int rb = (int)a.w.row_bytes;
+  const int R = std::min(16, std::max(1, (RF_TILE_BYTES - 32) / rb));
+  const int ntiles = (a.w.rows + R - 1) / R;
+  const int grid = std::min(ntiles, ctx->num_sms * 2);
+  const int sm = a.w.cols * 4 + 128 + 2 * RF_TILE_BYTES;
+  row_gemv_kernel<T><<<grid, RF_THREADS, sm, ctx->stream>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
+  switch (a.w.type) {
+    case RT_F32: return launch_row_gemv<RT_F32>(ctx, a);
+    case RT_F16: return launch_row_gemv<RT_F16>(ctx, a);
+    case RT_BF16: return launch_row_gemv<RT_BF16>(ctx, a);
+    case RT_Q4_0: return launch_row_gemv<RT_Q4_0>(ctx, a);
+    case RT_Q4_1: return launch_row_gemv<RT_Q4_1>(ctx, a);
+    case RT_Q8_0: return launch_row_gemv<RT_Q8_0>(ctx, a);
+    case RT_Q4_K: return launch_row_gemv<RT_Q4_K>(ctx, a);
+    case RT_Q5_K: return launch_row_gemv<RT_Q5_K>(ctx, a);
+    case RT_Q6_K: return launch_row_gemv<RT_Q6_K>(ctx, a);
+  }
+  return cudaErrorInvalidValue;
+}
+}  // namespace
+
+extern "C" {
+
+llmq_status llmq_set_dense_parts(llmq_ctx *ctx, int nparts) {
+  if (!ctx || nparts <= 0 || nparts > 256) return fail(ctx, LLMQ_ERR_INVALID, "parts must be in [1, 256]");
+  ctx->dense_parts = nparts;
+  return LLMQ_OK;
+}
+
 llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
                         int IN, int OUT, int flags) {
   if (!ctx || !w || !x || !out || T <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument or T <= 0");
-  if (IN != w->cols || OUT != w->rows) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the matrix");
   if ((flags & LLMQ_BIAS) && !bias) return fail(ctx, LLMQ_ERR_INVALID, "LLMQ_BIAS without a bias");
-  if (!w->a16) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "llmq_linear takes A16 formats");
   CK(cudaSetDevice(ctx->device));
   int epi = (flags & LLMQ_BIAS ? EPI_BIAS : 0) | (flags & LLMQ_GELU ? EPI_GELU : 0) |
             (flags & LLMQ_RESID ? EPI_RESID : 0);
+  if (w->kind == WK_DENSE) {
+    // DenseMatrix layer matrices are [IN, OUT] (tensor.mojo:150-227).
+    if (IN != w->rows || OUT != w->cols) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the [IN, OUT] matrix");
+    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "dense matmuls with T > 1 are not built");
+    const int np = ctx->dense_parts;
+    llmq_status st = ensure_scratch(ctx, (size_t)np * OUT * 4);
+    if (st != LLMQ_OK) return st;
+    float *scratch = (float *)ctx->scratch;
+    dim3 grid((OUT + 255) / 256, np);
+    if (w->rtype == RT_F32) dense_gemv_parts_kernel<0><<<grid, 256, 0, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+    else if (w->rtype == RT_F16) dense_gemv_parts_kernel<1><<<grid, 256, 0, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+    else dense_gemv_parts_kernel<2><<<grid, 256, 0, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+    CKL();
+    dense_gemv_combine_kernel<<<(OUT + 255) / 256, 256, 0, ctx->stream>>>(scratch, bias, out, OUT, np, epi);
+    CKL();
+    return LLMQ_OK;
+  }
+  if (IN != w->cols || OUT != w->rows) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the matrix");
+  if (w->kind == WK_GGUF || (w->kind == WK_AFFINE && !w->a16)) {
+    // matmul_rows (kernels.mojo:285-349) for one token: dot_row per output.
+    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation matmuls with T > 1 are not built");
+    if (w->kind == WK_GGUF) {
+      RowGemvArgs a{w->rowmat(), x, bias, out, epi};
+      CK(row_gemv(ctx, a));
+    } else {
+      AffFloatArgs a{w->view(), x, bias, out, epi};
+      const int grid = std::min((w->rows + 15) / 16, ctx->num_sms * 4);
+      if (w->bits == 4)
+        affine_float_gemv_kernel<4><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
+      else
+        affine_float_gemv_kernel<8><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
+      CKL();
+    }
+    return LLMQ_OK;
+  }
   if (T == 1) {
     GemvArgs a{};
     a.w = w->view();
@@ -359,6 +511,38 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     int n = T * (OUT - full * 32);
     rows_a16_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(w->view(), xq, sx, bias, out, T, OUT, full * 32, epi);
     CKL();
+  }
+  return LLMQ_OK;
+}
+
+llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float *logits, int T, int C, int V) {
+  if (!ctx || !w || !h || !logits || T <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument or T <= 0");
+  if (w->rows != V || w->cols != C) return fail(ctx, LLMQ_ERR_INVALID, "the head must be [V, C]");
+  CK(cudaSetDevice(ctx->device));
+  if (w->kind == WK_GGUF && (w->rtype == RT_Q8_0 || w->rtype == RT_Q6_K)) {
+    // head_i16: the same arithmetic for one token and for several.
+    const int grid = std::min((V + 15) / 16, ctx->num_sms * 4);
+    for (int t = 0; t < T; t++) {
+      if (w->rtype == RT_Q8_0)
+        gguf_head_i16_kernel<RT_Q8_0><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h + (size_t)t * C, logits + (size_t)t * V);
+      else
+        gguf_head_i16_kernel<RT_Q6_K><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h + (size_t)t * C, logits + (size_t)t * V);
+      CKL();
+    }
+    return LLMQ_OK;
+  }
+  if (w->kind == WK_AFFINE && w->a16) return llmq_linear(ctx, w, h, nullptr, logits, T, C, V, 0);
+  // lm_head / lm_head_rows (dense, kernels.mojo:213-271) and matmul_rows
+  // (OUT_MAJOR formats) for one token: a 16-lane dot per vocabulary row;
+  // lm_head_rows gives every token the same arithmetic as lm_head.
+  for (int t = 0; t < T; t++) {
+    if (w->kind == WK_DENSE) {
+      RowGemvArgs a{w->rowmat(), h + (size_t)t * C, nullptr, logits + (size_t)t * V, 0};
+      CK(row_gemv(ctx, a));
+    } else {
+      llmq_status st = llmq_linear(ctx, w, h + (size_t)t * C, nullptr, logits + (size_t)t * V, 1, C, V, 0);
+      if (st != LLMQ_OK) return st;
+    }
   }
   return LLMQ_OK;
 }

@@ -36,6 +36,18 @@ def linear(ctx: Context, out, x, w: QuantMatrix, b, T: int, IN: int, OUT: int, r
     ctx.sync()
 
 
+def head(ctx: Context, logits, h, w, T: int, V: int, C_: int):
+    """logits[T, V] = h[T, C] @ w[V, C]^T with the head kernel of w's format
+    (kernels.mojo:676-690)."""
+    _pre(ctx)
+    check(lib().llmq_head(ctx.h, w.h, _p(h), _p(logits), T, C_, V), ctx.h)
+    ctx.sync()
+
+
+def set_dense_parts(ctx: Context, nparts: int):
+    check(lib().llmq_set_dense_parts(ctx.h, nparts), ctx.h)
+
+
 def head_argmax(ctx: Context, w: QuantMatrix, h, logits, argmax):
     """logits[V] = h[C] @ w^T and the greedy argmax (kernels.mojo:676-690,
     gpt2t.mojo:792-797); argmax is a 1-element int32 device tensor."""

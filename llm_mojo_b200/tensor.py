@@ -120,3 +120,78 @@ class QuantMatrix:
             self.free()
         except Exception:
             pass
+
+
+class GGUFMatrix:
+    """GGUFMatrix (gguf.mojo:344-512): rows of ggml blocks used as stored."""
+
+    def __init__(self, ctx: Context, ggml_type: int, blocks: np.ndarray, rows: int, cols: int):
+        self.ctx, self.kind, self.rows, self.cols = ctx, ggml_type, rows, cols
+        self.blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+        h = C.c_void_p()
+        check(lib().llmq_weight_create_gguf(ctx.h, ggml_type, _ptr(self.blocks), rows, cols, C.byref(h)), ctx.h)
+        self.h = h
+
+    @staticmethod
+    def name() -> str:
+        return "gguf"
+
+    def has_i16(self) -> bool:
+        """GGUFMatrix.has_i16 (gguf.mojo:456-457): Q6_K and Q8_0."""
+        return self.kind in (14, 8)
+
+    def nbytes(self) -> int:
+        return int(lib().llmq_weight_nbytes(self.h))
+
+    def free(self):
+        if self.h:
+            lib().llmq_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class DenseMatrix:
+    """DenseMatrix[dtype] (tensor.mojo:150-227): f32 / f16 / bf16 values,
+    [rows, cols] as given ([IN, OUT] layer matrices, [V, C] wte)."""
+
+    DTYPES = {"f32": 0, "f16": 1, "bf16": 2}
+
+    def __init__(self, ctx: Context, dtype: str, src: np.ndarray):
+        src = np.ascontiguousarray(src, dtype=np.float32)
+        self.ctx, self.dtype = ctx, dtype
+        self.rows, self.cols = src.shape
+        if dtype == "f32":
+            data = src
+        elif dtype == "f16":
+            data = src.astype(np.float16)
+        else:  # bfloat16: round to nearest even, as .cast[bfloat16]()
+            b = src.view(np.uint32).astype(np.uint64)
+            b = (b + 0x7FFF + ((b >> 16) & 1)) >> 16
+            data = b.astype(np.uint16)
+        self.data = np.ascontiguousarray(data)
+        h = C.c_void_p()
+        check(lib().llmq_weight_create_dense(ctx.h, self.DTYPES[dtype], _ptr(self.data), self.rows, self.cols,
+                                             C.byref(h)), ctx.h)
+        self.h = h
+
+    def name(self) -> str:
+        return self.dtype
+
+    def nbytes(self) -> int:
+        return int(lib().llmq_weight_nbytes(self.h))
+
+    def free(self):
+        if self.h:
+            lib().llmq_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -965,3 +965,270 @@ OQ_EXPORT void oq_generate(oq_model *m, const int32_t *prompt, int n_prompt, int
   }
   free(logits);
 }
+
+/* ------------------------------------------------------------------------ */
+/* GGUF block formats (gguf.mojo:139-512)                                    */
+/* ------------------------------------------------------------------------ */
+
+enum { GG_F32 = 0, GG_F16 = 1, GG_Q4_0 = 2, GG_Q4_1 = 3, GG_Q8_0 = 8, GG_Q4_K = 12, GG_Q5_K = 13, GG_Q6_K = 14 };
+
+OQ_EXPORT int oq_gguf_block_size(int t) {
+  if (t == GG_F32 || t == GG_F16) return 1;
+  if (t == GG_Q4_0 || t == GG_Q4_1 || t == GG_Q8_0) return 32;
+  return 256;
+}
+
+OQ_EXPORT int oq_gguf_block_bytes(int t) {
+  switch (t) {
+    case GG_F32: return 4;
+    case GG_F16: return 2;
+    case GG_Q4_0: return 18;
+    case GG_Q4_1: return 20;
+    case GG_Q8_0: return 34;
+    case GG_Q4_K: return 144;
+    case GG_Q5_K: return 176;
+    case GG_Q6_K: return 210;
+  }
+  return 0;
+}
+
+static inline float f16_at(const uint8_t *p) { return f16_to_f32((uint16_t)(p[0] | (p[1] << 8))); }
+
+/* `put` (gguf.mojo:166-175): store v[16] at dst+off, or with dot fold
+ * acc[l] = fma(v[l], x[off+l], acc[l]). */
+static inline void put(int dot, float *dst, const float *x, float *acc, int off, const float *v) {
+  for (int l = 0; l < 16; l++) {
+    if (dot)
+      acc[l] = fmaf(v[l], x[off + l], acc[l]);
+    else
+      dst[off + l] = v[l];
+  }
+}
+
+/* k_scale_min (gguf.mojo:205-221). */
+static inline void k_scale_min(const uint8_t *q, int j, int *sc, int *m) {
+  if (j < 4) {
+    *sc = q[j] & 63;
+    *m = q[j + 4] & 63;
+  } else {
+    *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+/* One block at b of type t (dequant_q* in gguf.mojo:178-297), dot or store. */
+static void gguf_block(int t, const uint8_t *b, float *dst, const float *x, float *acc, int dot) {
+  float v[16];
+  if (t == GG_Q4_0) {
+    float d = f16_at(b);
+    const uint8_t *q = b + 2;
+    for (int l = 0; l < 16; l++) v[l] = ((float)(q[l] & 0xF) - 8.0f) * d;
+    put(dot, dst, x, acc, 0, v);
+    for (int l = 0; l < 16; l++) v[l] = ((float)(q[l] >> 4) - 8.0f) * d;
+    put(dot, dst, x, acc, 16, v);
+  } else if (t == GG_Q4_1) {
+    float d = f16_at(b), m = f16_at(b + 2);
+    const uint8_t *q = b + 4;
+    for (int l = 0; l < 16; l++) v[l] = d * (float)(q[l] & 0xF) + m;
+    put(dot, dst, x, acc, 0, v);
+    for (int l = 0; l < 16; l++) v[l] = d * (float)(q[l] >> 4) + m;
+    put(dot, dst, x, acc, 16, v);
+  } else if (t == GG_Q8_0) {
+    float d = f16_at(b);
+    for (int h = 0; h < 2; h++) {
+      for (int l = 0; l < 16; l++) v[l] = d * (float)(int8_t)b[2 + 16 * h + l];
+      put(dot, dst, x, acc, 16 * h, v);
+    }
+  } else if (t == GG_Q4_K || t == GG_Q5_K) {
+    float d = f16_at(b), dmin = f16_at(b + 2);
+    const uint8_t *scales = b + 4;
+    for (int j = 0; j < 4; j++) {
+      int sc1, m1i, sc2, m2i;
+      k_scale_min(scales, 2 * j, &sc1, &m1i);
+      k_scale_min(scales, 2 * j + 1, &sc2, &m2i);
+      float d1 = d * (float)sc1, m1 = dmin * (float)m1i;
+      float d2 = d * (float)sc2, m2 = dmin * (float)m2i;
+      for (int h = 0; h < 2; h++) {
+        if (t == GG_Q4_K) {
+          const uint8_t *q = b + 16 + 32 * j + 16 * h;
+          for (int l = 0; l < 16; l++) v[l] = d1 * (float)(q[l] & 0xF) - m1;
+          put(dot, dst, x, acc, 64 * j + 16 * h, v);
+          for (int l = 0; l < 16; l++) v[l] = d2 * (float)(q[l] >> 4) - m2;
+          put(dot, dst, x, acc, 64 * j + 32 + 16 * h, v);
+        } else {
+          const uint8_t *qh = b + 16 + 16 * h;
+          const uint8_t *q = b + 48 + 32 * j + 16 * h;
+          for (int l = 0; l < 16; l++) {
+            int lo = (q[l] & 0xF) | (((qh[l] >> (2 * j)) & 1) << 4);
+            v[l] = d1 * (float)lo - m1;
+          }
+          put(dot, dst, x, acc, 64 * j + 16 * h, v);
+          for (int l = 0; l < 16; l++) {
+            int hi = (q[l] >> 4) | (((qh[l] >> (2 * j + 1)) & 1) << 4);
+            v[l] = d2 * (float)hi - m2;
+          }
+          put(dot, dst, x, acc, 64 * j + 32 + 16 * h, v);
+        }
+      }
+    }
+  } else if (t == GG_Q6_K) {
+    float d = f16_at(b + 208);
+    for (int n = 0; n < 2; n++) {
+      int ql = 64 * n, qhoff = 128 + 32 * n, sc = 192 + 8 * n;
+      for (int h = 0; h < 2; h++) {
+        const uint8_t *lo0 = b + ql + 16 * h, *lo1 = b + ql + 32 + 16 * h, *hi = b + qhoff + 16 * h;
+        int base = 128 * n + 16 * h;
+        for (int k = 0; k < 4; k++) {
+          float s = (float)(int8_t)b[sc + h + 2 * k];
+          float ds = d * s;
+          for (int l = 0; l < 16; l++) {
+            int q;
+            if (k == 0) q = (lo0[l] & 0xF) | ((hi[l] & 3) << 4);
+            else if (k == 1) q = (lo1[l] & 0xF) | (((hi[l] >> 2) & 3) << 4);
+            else if (k == 2) q = (lo0[l] >> 4) | (((hi[l] >> 4) & 3) << 4);
+            else q = (lo1[l] >> 4) | (((hi[l] >> 6) & 3) << 4);
+            v[l] = ds * ((float)q - 32.0f);
+          }
+          put(dot, dst, x, acc, base + 32 * k, v);
+        }
+      }
+    }
+  }
+}
+
+/* GGUFMatrix.each_block (gguf.mojo:388-417) over one row. */
+static void gguf_row(int t, const uint8_t *row, int cols, float *dst, const float *x, float *acc, int dot) {
+  for (int l = 0; l < 16; l++) acc[l] = 0.0f;
+  if (t == GG_F32 || t == GG_F16) {
+    float v[16];
+    for (int i = 0; i < cols; i += 16) {
+      for (int l = 0; l < 16; l++) {
+        float w;
+        if (t == GG_F32)
+          memcpy(&w, row + 4 * (i + l), 4);
+        else
+          w = f16_at(row + 2 * (i + l));
+        v[l] = w;
+      }
+      put(dot, dst + i, x + i, acc, 0, v);
+    }
+    return;
+  }
+  int bs = oq_gguf_block_size(t), bb = oq_gguf_block_bytes(t);
+  for (int blk = 0; blk < cols / bs; blk++)
+    gguf_block(t, row + (long)blk * bb, dst ? dst + blk * bs : NULL, x ? x + blk * bs : NULL, acc, dot);
+}
+
+OQ_EXPORT void oq_gguf_dequant_row(int t, const uint8_t *row, int cols, float *dst) {
+  float acc[16];
+  gguf_row(t, row, cols, dst, NULL, acc, 0);
+}
+
+/* GGUFMatrix.dot_row (gguf.mojo:384-386). */
+OQ_EXPORT float oq_gguf_dot_row(int t, const uint8_t *row, int cols, const float *x) {
+  float acc[16];
+  gguf_row(t, row, cols, NULL, x, acc, 1);
+  return tree16(acc);
+}
+
+/* Q6_K weights of superblock b as int16 (q - 32) * scale, 32 at a time
+ * (q6_k_i16, gguf.mojo:322-336): weights 128n + 32k + j. */
+static void q6k_i16(const uint8_t *b, int n, int k, int16_t *out) {
+  const uint8_t *L = b + 64 * n + ((k & 1) ? 32 : 0);
+  const uint8_t *H = b + 128 + 32 * n;
+  for (int j = 0; j < 32; j++) {
+    int q = ((k >= 2) ? (L[j] >> 4) : (L[j] & 0xF)) | (((H[j] >> (2 * k)) & 3) << 4);
+    int s = (int8_t)b[192 + 8 * n + 2 * k + (j >= 16 ? 1 : 0)];
+    out[j] = (int16_t)((q - 32) * s);
+  }
+}
+
+/* GGUFMatrix.dot_row_i16 (gguf.mojo:462-487) for Q8_0 and Q6_K. */
+OQ_EXPORT float oq_gguf_dot_row_i16(int t, const uint8_t *row, int cols, const int16_t *xq) {
+  float accf[16];
+  for (int l = 0; l < 16; l++) accf[l] = 0.0f;
+  if (t == GG_Q8_0) {
+    for (int blk = 0; blk < cols / 32; blk++) {
+      const uint8_t *b = row + blk * 34;
+      int16_t w[32];
+      for (int j = 0; j < 32; j++) w[j] = (int8_t)b[2 + j];
+      int32_t acc[16] = {0};
+      dot_pairs(acc, xq + blk * 32, w);
+      float d = f16_at(b);
+      for (int l = 0; l < 16; l++) accf[l] = fmaf((float)acc[l], d, accf[l]);
+    }
+    return tree16(accf);
+  }
+  for (int sb = 0; sb < cols / 256; sb++) {
+    const uint8_t *b = row + sb * 210;
+    int32_t acc[16] = {0};
+    for (int n = 0; n < 2; n++)
+      for (int k = 0; k < 4; k++) {
+        int16_t w[32];
+        q6k_i16(b, n, k, w);
+        dot_pairs(acc, xq + sb * 256 + 128 * n + 32 * k, w);
+      }
+    float d = f16_at(b + 208);
+    for (int l = 0; l < 16; l++) accf[l] = fmaf((float)acc[l], d, accf[l]);
+  }
+  return tree16(accf);
+}
+
+/* head_i16 for one token (kernels.mojo:693-736, T == 1): logits[v] =
+ * dot_row_i16(v, xq) * sx. */
+OQ_EXPORT void oq_gguf_head_i16(int t, const uint8_t *w, int V, int C, const float *h, float *logits) {
+  int16_t *xq = (int16_t *)malloc(sizeof(int16_t) * C);
+  float sx;
+  oq_quantize_rows(h, 1, C, xq, &sx);
+  long rb = (long)(C / oq_gguf_block_size(t)) * oq_gguf_block_bytes(t);
+  for (int v = 0; v < V; v++) logits[v] = oq_gguf_dot_row_i16(t, w + v * rb, C, xq) * sx;
+  free(xq);
+}
+
+/* ------------------------------------------------------------------------ */
+/* Dense float formats (tensor.mojo:150-227, kernels.mojo:132-176, 213-227)  */
+/* ------------------------------------------------------------------------ */
+
+enum { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2 };
+
+static inline float dense_at(int dt, const void *w, long i) {
+  if (dt == DT_F32) return ((const float *)w)[i];
+  uint16_t u = ((const uint16_t *)w)[i];
+  if (dt == DT_F16) return f16_to_f32(u);
+  uint32_t b = (uint32_t)u << 16;
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+
+/* DenseMatrix.dot_row / lm_head (tensor.mojo:206-210, kernels.mojo:213-227):
+ * 16 lane fma chains over the row, halving tree. w is [rows, cols]. */
+OQ_EXPORT float oq_dense_dot_row(int dt, const void *w, int row, int cols, const float *x) {
+  float d[16];
+  for (int l = 0; l < 16; l++) d[l] = 0.0f;
+  for (int i = 0; i < cols; i += 16)
+    for (int l = 0; l < 16; l++) d[l] = fmaf(x[i + l], dense_at(dt, w, (long)row * cols + i + l), d[l]);
+  return tree16(d);
+}
+
+/* gemv (kernels.mojo:132-176) with `nparts` parts: out[OUT] (+)= act(x[IN]
+ * @ w[IN, OUT] + b). Part p accumulates rows [p*rows, min(IN, (p+1)*rows)),
+ * rows = ceil(IN / nparts), each output a sequential fma chain; the parts
+ * are then added in order after the bias. */
+OQ_EXPORT void oq_dense_gemv(int dt, const void *w, const float *x, const float *b, float *out, int IN, int OUT,
+                             int nparts, int resid, int gelu) {
+  int rows = (IN + nparts - 1) / nparts;
+  float *scratch = (float *)calloc((size_t)nparts * OUT, sizeof(float));
+  for (int p = 0; p < nparts; p++) {
+    float *acc = scratch + (size_t)p * OUT;
+    int end = (p + 1) * rows < IN ? (p + 1) * rows : IN;
+    for (int i = p * rows; i < end; i++)
+      for (int j = 0; j < OUT; j++) acc[j] = fmaf(x[i], dense_at(dt, w, (long)i * OUT + j), acc[j]);
+  }
+  for (int j = 0; j < OUT; j++) {
+    float r = b ? b[j] : 0.0f;
+    for (int p = 0; p < nparts; p++) r += scratch[(size_t)p * OUT + j];
+    finish(out, j, r, resid, gelu);
+  }
+  free(scratch);
+}

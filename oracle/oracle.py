@@ -77,11 +77,23 @@ def _declare(L):
         "oq_model_forward_all": (V, [P, P, I, P]),
         "oq_argmax": (I, [P, I]),
         "oq_generate": (V, [P, P, I, I, P]),
+        "oq_gguf_block_size": (I, [I]), "oq_gguf_block_bytes": (I, [I]),
+        "oq_gguf_dequant_row": (V, [I, P, I, P]),
+        "oq_gguf_dot_row": (F, [I, P, I, P]),
+        "oq_gguf_dot_row_i16": (F, [I, P, I, P]),
+        "oq_gguf_head_i16": (V, [I, P, I, I, P, P]),
+        "oq_dense_dot_row": (F, [I, P, I, I, P]),
+        "oq_dense_gemv": (V, [I, P, P, P, P, I, I, I, I, I]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
         f.restype = res
         f.argtypes = args
+
+
+def oq_gelu_np(v: float) -> np.float32:
+    """The oracle's GELU of one float32 value."""
+    return np.float32(lib().oq_gelu(float(np.float32(v))))
 
 
 def ptr(a: np.ndarray):
