@@ -11,10 +11,11 @@ value: generated tokens / device time of the K timed steps (CUDA events on
 the library's stream, L2 flushed by a 256 MiB write between steps, prompt
 and ids resident in HBM). e2e: the same through llmq_generate with host
 prompt and host ids (the copies inside the timed region). roofline: the
-dominant kernel (the fused int8 head GEMV + argmax), timed live with CUDA
-events on its stream, against the measured HBM copy bandwidth.
-cpu_baseline: the CPU oracle (a C restatement of the reference's path) on a
-bounded sample. With N GPUs (torchrun), each rank decodes its own sequence
+dominant kernel (the persistent decode kernel, one launch per generation),
+timed live with CUDA events on its stream, against the measured HBM copy
+bandwidth. cpu_baseline: the CPU oracle (a C restatement of the reference's
+path: a thread team of one thread per physical core, VNNI integer dots) on
+a bounded sample. With N GPUs (torchrun), each rank decodes its own sequence
 (replicas of the batch-1 decode, which does not shard), and value is the
 sum over ranks with the max device time over ranks.
 """
@@ -65,7 +66,7 @@ class Clocks:
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -121,8 +122,12 @@ def cpu_baseline(seconds: float = 20.0):
         n += 1
     dt = time.perf_counter() - t0
     m.close()
-    return {"value": (n - 1) / dt, "unit": "tok/s", "cores": 1, "kind": "port",
-            "sample": f"{n - 1} decode steps of config 0 (after the prompt forward), single thread"}
+    threads = int(O.lib().oq_threads())
+    vnni = bool(O.lib().oq_set_vnni(1))
+    return {"value": (n - 1) / dt, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{n - 1} decode steps of config 0 (after the prompt forward), {threads}-thread team "
+                      f"(one per physical core), {'AVX-512 VNNI' if vnni else 'scalar'} integer dots, "
+                      f"{os.cpu_count()} logical CPUs"}
 
 
 def run_reference(args):
@@ -321,22 +326,6 @@ def main():
             e2e_ms.append(s0.elapsed_time(e0))
         assert list(out) == list(ids)
 
-        # roofline: the head GEMV + argmax (largest single launch) timed alone.
-        h = torch.randn(768, device="cuda")
-        am = torch.zeros(1, dtype=torch.int32, device="cuda")
-        hs = []
-        for i in range(args.warmup + 20):
-            flush.zero_()
-            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            check(lib().llmq_head_argmax(ctx.h, model.head.h, C.c_void_p(h.data_ptr()), None,
-                                         C.c_void_p(am.data_ptr())), ctx.h)
-            e0.record(stream)
-            if i >= args.warmup:
-                hs.append((s0, e0))
-        stream.synchronize()
-        head_ms = statistics.mean(s.elapsed_time(e) for s, e in hs)
-
     if args.profile:
         model.profile(True)
         model.generate(PROMPT, STEPS_PER_GEN)
@@ -361,7 +350,13 @@ def main():
     tokens = world * args.steps * STEPS_PER_GEN
     value = tokens / (t_max / 1000.0)
     peak, peak_kind = peaks()
-    achieved = HEAD_BYTES / (head_ms / 1000.0) / 1e9
+    # roofline: the step is one launch of the persistent decode kernel (the
+    # dominant, and only, kernel of the timed region); its algorithmic bytes
+    # are the weights of every token plus the KV cache each token reads.
+    kv_bytes = 19584 * sum(p + 1 for p in range(STEPS_PER_GEN))
+    launch_bytes = STEPS_PER_GEN * TOKEN_BYTES + kv_bytes
+    launch_ms = total_ms / args.steps
+    achieved = launch_bytes / (launch_ms / 1000.0) / 1e9
     if rank == 0:
         cpu = None if args.no_cpu_baseline else cpu_baseline(args.cpu_seconds)
         launches_per_token = model.n_layer * 5 + 2
@@ -371,13 +366,15 @@ def main():
             "vs_baseline": None, "dtype": "int16xint4->int32", "data": "synthetic", "config": config_dict(args),
             "e2e": {"value": world * STEPS_PER_GEN / (e2e_avg / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 4 * len(PROMPT), "d2h_bytes_per_step": 4 * STEPS_PER_GEN},
-            "roofline": {"bound": "hbm", "kernel": "gemv_a16_kernel<GEN8, PRO_LN, argmax> (int8-ch head 50257x768)",
+            "roofline": {"bound": "hbm", "kernel": "mega_decode_kernel (one launch = the 100-token generation)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": None,
-                         "algorithmic_bytes_per_launch": HEAD_BYTES, "avg_launch_ms": head_ms},
+                         "algorithmic_bytes_per_launch": launch_bytes, "avg_launch_ms": launch_ms},
             "weight_bytes_per_token": TOKEN_BYTES,
             "effective_weight_gbs": TOKEN_BYTES * STEPS_PER_GEN * args.steps / (total_ms / 1000.0) / 1e9,
-            "gpu_launches": args.steps * (1 + STEPS_PER_GEN * launches_per_token),
+            "gpu_launches": args.steps * (1 if model.mode() == "persistent" else
+                                          1 + STEPS_PER_GEN * launches_per_token),
+            "decode_mode": model.mode(),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "ids_head": [int(i) for i in ids[:8]],

@@ -151,7 +151,7 @@ __device__ __forceinline__ unsigned rf_smem_u32(const void *p) { return (unsigne
 // R <= 16), two shared-memory stages filled by cp.async.bulk.
 template <int T>
 __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(16) unsigned char smem[];
   const int cols = a.w.cols, rb = (int)a.w.row_bytes;
   const int R = min(16, max(1, (RF_TILE_BYTES - 32) / rb));
   float *xs = (float *)smem;                                         // [cols]

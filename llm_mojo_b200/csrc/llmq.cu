@@ -371,7 +371,6 @@ llmq_status llmq_weight_create_dense(llmq_ctx *ctx, int dtype, const void *data,
   if (!ctx || !out || !data || rows <= 0 || cols <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
   if (dtype != LLMQ_DENSE_F32 && dtype != LLMQ_DENSE_F16 && dtype != LLMQ_DENSE_BF16)
     return fail(ctx, LLMQ_ERR_INVALID, "dtype must be LLMQ_DENSE_F32, _F16 or _BF16");
-  if (cols % 16 != 0) return fail(ctx, LLMQ_ERR_INVALID, "columns must be a multiple of 16");
   *out = nullptr;
   CK(cudaSetDevice(ctx->device));
   llmq_weight *w = new llmq_weight();
@@ -518,6 +517,8 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
 llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float *logits, int T, int C, int V) {
   if (!ctx || !w || !h || !logits || T <= 0) return fail(ctx, LLMQ_ERR_INVALID, "null argument or T <= 0");
   if (w->rows != V || w->cols != C) return fail(ctx, LLMQ_ERR_INVALID, "the head must be [V, C]");
+  if (w->kind == WK_DENSE && (C % 16 != 0 || C > 4096))
+    return fail(ctx, LLMQ_ERR_INVALID, "a dense head needs C a multiple of 16, at most 4096");
   CK(cudaSetDevice(ctx->device));
   if (w->kind == WK_GGUF && (w->rtype == RT_Q8_0 || w->rtype == RT_Q6_K)) {
     // head_i16: the same arithmetic for one token and for several.

@@ -756,7 +756,7 @@ __device__ __noinline__ bool mk_argmax(const MegaArgs &a, MkSmem &sm, const MkLL
 }
 
 __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
   MkSmem &sm = *reinterpret_cast<MkSmem *>(smem_raw);
   const int tid = threadIdx.x;
   const int cta = blockIdx.x, grid = gridDim.x;

@@ -17,10 +17,16 @@
  * (lm_expf, lm_tanhf below: Cody-Waite reduction plus Taylor polynomials,
  * from IEEE add/mul/fma/div only) and uses the same definition on the GPU.
  */
+#include <immintrin.h>
 #include <math.h>
+#include <pthread.h>
+#include <sched.h>
+#include <stdatomic.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
+#include <unistd.h>
 
 #define OQ_EXPORT __attribute__((visibility("default")))
 
@@ -325,6 +331,153 @@ static inline void codes_i16(const oq_qmat *w, const uint8_t *p, int k0, int zp,
   }
 }
 
+/* ------------------------------------------------------------------------ */
+/* The thread team (team.mojo:36-82): persistent workers meeting at a       */
+/* spin-then-yield barrier; work split into contiguous ranges (split).      */
+/* Results never depend on the split: every output is computed whole by     */
+/* one thread.                                                               */
+/* ------------------------------------------------------------------------ */
+
+typedef void (*oq_range_fn)(void *arg, int begin, int end);
+
+static struct {
+  int nt;
+  pthread_t th[256];
+  _Atomic long gen;
+  _Atomic int done;
+  oq_range_fn fn;
+  void *arg;
+  int n;
+} team;
+
+static void team_wait_gen(long g) {
+  int spins = 0;
+  while (atomic_load_explicit(&team.gen, memory_order_acquire) == g) {
+    if (spins < 1000) {
+      _mm_pause();
+      spins++;
+    } else {
+      sched_yield();
+    }
+  }
+}
+
+static void *team_worker(void *p) {
+  int tid = (int)(long)p;
+  long g = 0;
+  for (;;) {
+    team_wait_gen(g);
+    g = atomic_load_explicit(&team.gen, memory_order_acquire);
+    int per = (team.n + team.nt - 1) / team.nt;
+    int b = tid * per < team.n ? tid * per : team.n, e = (tid + 1) * per < team.n ? (tid + 1) * per : team.n;
+    if (b < e) team.fn(team.arg, b, e);
+    atomic_fetch_add_explicit(&team.done, 1, memory_order_acq_rel);
+  }
+  return NULL;
+}
+
+/* Hardware threads per core, from cpu0's sibling list ("0,8" or "0-1"). */
+static int threads_per_core(void) {
+  FILE *f = fopen("/sys/devices/system/cpu/cpu0/topology/thread_siblings_list", "r");
+  if (!f) return 2;
+  char buf[64] = {0};
+  int n = 1;
+  if (fgets(buf, sizeof(buf), f)) {
+    int a, b;
+    if (sscanf(buf, "%d-%d", &a, &b) == 2)
+      n = b - a + 1;
+    else
+      for (const char *c = buf; *c; c++) n += *c == ',';
+  }
+  fclose(f);
+  return n < 1 ? 1 : n;
+}
+
+/* Threads: OQ_THREADS, else one per physical core (gpt2t.mojo:281 takes half
+ * the logical CPUs, i.e. one per core on a two-way SMT machine), at most
+ * 256. */
+OQ_EXPORT int oq_threads(void) {
+  if (team.nt) return team.nt;
+  const char *env = getenv("OQ_THREADS");
+  int n = env ? atoi(env) : (int)(sysconf(_SC_NPROCESSORS_ONLN) / threads_per_core());
+  if (n < 1) n = 1;
+  if (n > 256) n = 256;
+  team.nt = n;
+  for (int i = 1; i < n; i++) pthread_create(&team.th[i], NULL, team_worker, (void *)(long)i);
+  return n;
+}
+
+/* Runs fn over [0, n) split into nt contiguous ranges; thread 0 is the
+ * caller. */
+static void parallel_for(int n, oq_range_fn fn, void *arg) {
+  int nt = oq_threads();
+  if (nt == 1 || n < 2) {
+    fn(arg, 0, n);
+    return;
+  }
+  team.fn = fn;
+  team.arg = arg;
+  team.n = n;
+  atomic_store_explicit(&team.done, 0, memory_order_release);
+  atomic_fetch_add_explicit(&team.gen, 1, memory_order_acq_rel);
+  int per = (n + nt - 1) / nt;
+  fn(arg, 0, per < n ? per : n);
+  int spins = 0;
+  while (atomic_load_explicit(&team.done, memory_order_acquire) != nt - 1) {
+    if (spins < 1000) {
+      _mm_pause();
+      spins++;
+    } else {
+      sched_yield();
+    }
+  }
+}
+
+/* VPDPWSSD (tensor.mojo:34-46 dot_pairs with AVX-512 VNNI): the BLOCKED and
+ * per-channel int8 integer dots, selected at run time. */
+static int vnni_state = -1;
+
+static int have_vnni(void) {
+  if (vnni_state < 0) vnni_state = __builtin_cpu_supports("avx512vnni") && __builtin_cpu_supports("avx512bw") ? 1 : 0;
+  return vnni_state;
+}
+
+/* Enables (1) or disables (0) the VNNI dots where the CPU has them; returns
+ * whether they are in use afterwards. Lets a test compare both paths. */
+OQ_EXPORT int oq_set_vnni(int on) {
+  vnni_state = -1;
+  if (on && have_vnni()) return 1;
+  vnni_state = 0;
+  return 0;
+}
+
+__attribute__((target("avx512f,avx512bw,avx512vnni"))) static void blk4_lanes_vnni(const uint8_t *p, const int16_t *xq,
+                                                                                   int nblk, int32_t *lanes) {
+  const __m128i mask = _mm_set1_epi8(0x0F);
+  for (int blk = 0; blk < nblk; blk++) {
+    __m512i acc = _mm512_setzero_si512();
+    for (int step = 0; step < 8; step++) {
+      __m128i b = _mm_loadu_si128((const __m128i *)(p + blk * 128 + step * 16));
+      __m128i lo = _mm_and_si128(b, mask), hi = _mm_and_si128(_mm_srli_epi16(b, 4), mask);
+      __m512i u = _mm512_cvtepu8_epi16(_mm256_set_m128i(hi, lo));
+      __m512i x = _mm512_loadu_si512((const void *)(xq + blk * 256 + step * 32));
+      acc = _mm512_dpwssd_epi32(acc, x, u);
+    }
+    _mm512_storeu_si512((void *)(lanes + blk * 16), acc);
+  }
+}
+
+__attribute__((target("avx512f,avx512bw,avx512vnni"))) static void ch8_lanes_vnni(const uint8_t *p, const int16_t *xq,
+                                                                                  int cols, int zp, int32_t *lanes) {
+  __m512i acc = _mm512_setzero_si512();
+  const __m512i z = _mm512_set1_epi16((short)zp);
+  for (int k = 0; k < cols; k += 32) {
+    __m512i u = _mm512_sub_epi16(_mm512_cvtepu8_epi16(_mm256_loadu_si256((const __m256i *)(p + k))), z);
+    acc = _mm512_dpwssd_epi32(acc, _mm512_loadu_si512((const void *)(xq + k)), u);
+  }
+  _mm512_storeu_si512((void *)lanes, acc);
+}
+
 /* dot_row_i16 (tensor.mojo:518-577). If lanes != NULL it also receives the
  * int32 lane sums: BLOCKED [cols/256][16] (before the zero point), otherwise
  * [groups][16]. */
@@ -335,16 +488,23 @@ OQ_EXPORT float oq_dot_row_i16_lanes(const oq_qmat *w, int row, const int16_t *x
   float accf[16];
   for (int l = 0; l < 16; l++) accf[l] = 0.0f;
   if (w->blocked) {
+    int32_t vl[12 * 16];
+    const int vnni = have_vnni() && w->cols / 256 <= 12;
+    if (vnni) blk4_lanes_vnni(p, xq, w->cols / 256, vl);
     for (int blk = 0; blk < w->cols / 256; blk++) {
       int32_t acc[16] = {0};
-      for (int step = 0; step < 8; step++) {
-        const uint8_t *b = p + blk * 128 + step * 16;
-        int16_t u[32];
-        for (int j = 0; j < 16; j++) {
-          u[j] = b[j] & 0xF;
-          u[j + 16] = b[j] >> 4;
+      if (vnni) {
+        memcpy(acc, vl + blk * 16, sizeof(acc));
+      } else {
+        for (int step = 0; step < 8; step++) {
+          const uint8_t *b = p + blk * 128 + step * 16;
+          int16_t u[32];
+          for (int j = 0; j < 16; j++) {
+            u[j] = b[j] & 0xF;
+            u[j + 16] = b[j] >> 4;
+          }
+          dot_pairs(acc, xq + blk * 256 + step * 32, u);
         }
-        dot_pairs(acc, xq + blk * 256 + step * 32, u);
       }
       long g0 = (long)row * gpr + blk * 8;
       for (int l = 0; l < 16; l++) {
@@ -360,11 +520,15 @@ OQ_EXPORT float oq_dot_row_i16_lanes(const oq_qmat *w, int row, const int16_t *x
   for (int g = 0; g < gpr; g++) {
     int zp = w->zp[(long)row * gpr + g];
     int32_t acc[16] = {0};
-    for (int c = 0; c < w->group / 32; c++) {
-      int k0 = g * w->group + 32 * c;
-      int16_t u[32];
-      codes_i16(w, p, k0, zp, u);
-      dot_pairs(acc, xq + k0, u);
+    if (w->bits == 8 && gpr == 1 && have_vnni()) {
+      ch8_lanes_vnni(p, xq, w->cols, zp, acc);
+    } else {
+      for (int c = 0; c < w->group / 32; c++) {
+        int k0 = g * w->group + 32 * c;
+        int16_t u[32];
+        codes_i16(w, p, k0, zp, u);
+        dot_pairs(acc, xq + k0, u);
+      }
     }
     float s = f16_to_f32(w->scale[(long)row * gpr + g]);
     for (int l = 0; l < 16; l++) {
@@ -405,6 +569,22 @@ static float dot1_i16(const int16_t *wq, const float *ws, const int16_t *xq, int
   return tree16(accf);
 }
 
+/* Rows [o0, o1) of the one-token path: dot_row_i16 * sx + b, finish. */
+static void rows_i16_range(void *arg, int o0, int o1) {
+  struct {
+    const oq_qmat *w;
+    const int16_t *x1;
+    const float *xs, *b;
+    float *out, s;
+    int resid, gelu;
+  } *j = arg;
+  for (int o = o0; o < o1; o++) {
+    float r = oq_dot_row_i16(j->w, o, j->x1, j->xs) * j->s;
+    if (j->b) r += j->b[o];
+    finish(j->out, o, r, j->resid, j->gelu);
+  }
+}
+
 /* matmul_rows_a16 (kernels.mojo:419-509) with tile_i16 (:512-573) and
  * rows_i16 (:576-614). b may be NULL (BIAS=False). out[T, OUT]. */
 OQ_EXPORT void oq_matmul_rows_a16(float *out, const float *x, const oq_qmat *w, const float *b, int T, int IN,
@@ -420,11 +600,14 @@ OQ_EXPORT void oq_matmul_rows_a16(float *out, const float *x, const oq_qmat *w, 
       oq_permute_x_i16(xq, IN, xp, xs);
       x1 = xp;
     }
-    for (int o = 0; o < OUT; o++) {
-      float r = oq_dot_row_i16(w, o, x1, xs) * sx[0];
-      if (b) r += b[o];
-      finish(out, o, r, resid, gelu);
-    }
+    struct {
+      const oq_qmat *w;
+      const int16_t *x1;
+      const float *xs, *b;
+      float *out, s;
+      int resid, gelu;
+    } job = {w, x1, xs, b, out, sx[0], resid, gelu};
+    parallel_for(OUT, (oq_range_fn)rows_i16_range, &job);
     free(xp);
     free(xs);
   } else {
@@ -891,14 +1074,29 @@ static void kv_store(oq_model *m, int l, int pos, const float *row) {
     oq_intkv_store(m->ikv, l, pos, row + m->C, row + 2 * m->C);
 }
 
-static void attend(oq_model *m, int l, int T, int pos0) {
-  for (int i = 0; i < m->n_head * T; i++) {
+struct attend_job {
+  oq_model *m;
+  int l, pos0;
+};
+
+/* (t, h) pairs [i0, i1): each writes its own head slice of att. */
+static void attend_range(void *arg, int i0, int i1) {
+  struct attend_job *j = arg;
+  oq_model *m = j->m;
+  for (int i = i0; i < i1; i++) {
     int t = i / m->n_head, h = i % m->n_head;
     if (m->kv_kind == OQ_KV_QUANT8)
-      oq_qkv8_attend_one(m->kv8, m->att, m->qkv, l, t, h, pos0);
+      oq_qkv8_attend_one(m->kv8, m->att, m->qkv, j->l, t, h, j->pos0);
     else
-      oq_intkv_attend_one(m->ikv, m->att, m->qkv, l, t, h, pos0);
+      oq_intkv_attend_one(m->ikv, m->att, m->qkv, j->l, t, h, j->pos0);
   }
+}
+
+/* The (token, head) attention units split over the team, as
+ * gpt2t.mojo:395-420 splits heads over threads. */
+static void attend(oq_model *m, int l, int T, int pos0) {
+  struct attend_job j = {m, l, pos0};
+  parallel_for(m->n_head * T, attend_range, &j);
 }
 
 /* blocks (gpt2t.mojo:485-571): embeddings of tokens at pos0.., all layers;

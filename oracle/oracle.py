@@ -84,6 +84,7 @@ def _declare(L):
         "oq_gguf_head_i16": (V, [I, P, I, I, P, P]),
         "oq_dense_dot_row": (F, [I, P, I, I, P]),
         "oq_dense_gemv": (V, [I, P, P, P, P, I, I, I, I, I]),
+        "oq_threads": (I, []), "oq_set_vnni": (I, [I]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

@@ -128,3 +128,22 @@ def test_model_a16_all_positions(golden, oracle_a16):
     for r in range(16):
         ids, vals = golden["a16_all16_top_ids"][r], golden["a16_all16_top_vals"][r]
         assert np.max(np.abs(lg[r][ids] - vals)) <= 1e-2 * mx
+
+
+@pytest.mark.parametrize("bits,group", [(4, 32), (8, 0)])
+def test_vnni_dots_match_scalar(bits, group):
+    """The VNNI integer dots (used where the CPU has AVX-512 VNNI) give the
+    scalar lane sums exactly."""
+    if not O.lib().oq_set_vnni(1):
+        pytest.skip("no AVX-512 VNNI on this CPU")
+    rng = np.random.default_rng(3)
+    w = O.QuantMatrix(rng.normal(0, 0.02, (768, 96)).astype(np.float32), bits, group, False, True, True)
+    xq = rng.integers(-32767, 32768, 768, dtype=np.int16)
+    x1, xs = O.permute_x_i16(xq) if w.blocked else (xq, None)
+    try:
+        fast = [O.lane_sums(w, r, x1, xs) for r in range(w.rows)]
+        O.lib().oq_set_vnni(0)
+        slow = [O.lane_sums(w, r, x1, xs) for r in range(w.rows)]
+    finally:
+        O.lib().oq_set_vnni(1)
+    assert all(np.array_equal(a, b) for a, b in zip(fast, slow))
