@@ -113,6 +113,20 @@ llmq_status llmq_set_dense_parts(llmq_ctx *ctx, int nparts);
  * of the largest logit into *argmax_dev. */
 llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev,
                              int *argmax_dev);
+/* No counterpart in the reference: llmq_head_argmax without any device
+ * allocation, for callers that cannot allocate while they run (a serving
+ * process whose pool holds the device's memory, or a host that must not meet
+ * the device-wide synchronisation of cudaMalloc / cudaFree). Same arguments
+ * and results as llmq_head_argmax. Its scratch is a fixed 16 KiB device
+ * array, one per device, with room for LLMQ_NOALLOC_MAX_PARTS per-CTA
+ * partials; a weight whose gemv grid needs more returns LLMQ_ERR_INVALID
+ * (on B200 the grid is at most 8 CTAs per SM, 1184). The first call on each
+ * device looks up the array's address and should come before any stream
+ * capture. Calls on one device that overlap in time (other streams, other
+ * contexts, other host threads) race on the array: order them. */
+#define LLMQ_NOALLOC_MAX_PARTS 1920
+llmq_status llmq_head_argmax_noalloc(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev,
+                                     int *argmax_dev);
 /* Replaces layernorm (kernels.mojo:179-197), eps 1e-5. */
 llmq_status llmq_layernorm(llmq_ctx *ctx, float *out_dev, const float *x_dev, const float *w_dev,
                            const float *b_dev, int T, int C);

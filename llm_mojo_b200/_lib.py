@@ -44,6 +44,7 @@ SIGNATURES = {
     "llmq_weight_nbytes": (LL, [P]),
     "llmq_linear": (I, [P, P, P, P, P, I, I, I, I]),
     "llmq_head_argmax": (I, [P, P, P, P, P]),
+    "llmq_head_argmax_noalloc": (I, [P, P, P, P, P]),
     "llmq_layernorm": (I, [P, P, P, P, P, I, I]),
     "llmq_quantize_rows": (I, [P, P, I, I, P, P]),
     "llmq_debug_lane_sums": (I, [P, P, P, P]),

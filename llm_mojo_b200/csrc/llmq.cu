@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -564,6 +565,82 @@ llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h
   a.state = ctx->state;
   a.ids = argmax;  // written at state->step, kept at 0 here
   CK(cudaMemsetAsync(ctx->state, 0, sizeof(DecodeState), ctx->stream));
+  CK(launch_gemv(ctx, a, PRO_QUANT, true, ctx->stream));
+  return LLMQ_OK;
+}
+
+// ---------------------------------------------------------------------------
+// llmq_head_argmax_noalloc: the head GEMV + greedy argmax of llmq_head_argmax
+// with its scratch in a fixed device array instead of the context's
+// cudaMalloc'd buffer. It is for callers that cannot allocate device memory
+// while they run: a serving process whose memory pool has reserved the
+// device's HBM up front, and hosts that must not meet the device-wide
+// synchronisation of cudaMalloc / cudaFree between two launches. The
+// existing entry point grows ctx->scratch on demand and is unchanged.
+//
+// The array holds one DecodeState (the CTA ticket and the id slot, which must
+// start at zero and are cleared by a cudaMemsetAsync before every launch) and
+// one (value, index) partial per CTA of the gemv grid, at most
+// LLMQ_NOALLOC_MAX_PARTS of them (16 KiB in all). One array exists per device:
+// calls on the same device that overlap in time (two streams, two contexts,
+// two host threads) race on it and must be ordered by the caller.
+// ---------------------------------------------------------------------------
+constexpr int kNoallocMaxParts = 1920;
+constexpr size_t kNoallocStateBytes = 256;
+constexpr size_t kNoallocBytes = kNoallocStateBytes + (size_t)kNoallocMaxParts * 8;  // 15,616 B
+static_assert(sizeof(DecodeState) <= kNoallocStateBytes, "DecodeState fits its slot");
+static_assert(LLMQ_NOALLOC_MAX_PARTS == kNoallocMaxParts, "header limit matches the array");
+
+static __device__ __align__(256) unsigned char g_head_argmax_scratch[kNoallocBytes];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+// The device address of g_head_argmax_scratch on ctx's device, looked up once
+// per device with that device current. The lookup may load the module on the
+// device, so the first call should come before any stream capture.
+llmq_status noalloc_scratch(llmq_ctx *ctx, unsigned char **out) {
+  if (ctx->device < 0 || ctx->device >= kNoallocMaxDevices)
+    return fail(ctx, LLMQ_ERR_INVALID, "llmq_head_argmax_noalloc: device index beyond 63");
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[ctx->device]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_head_argmax_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(ctx, LLMQ_ERR_CUDA,
+                  std::string("llmq_head_argmax_noalloc: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    g_noalloc_ptr[ctx->device] = ptr;
+  }
+  *out = (unsigned char *)g_noalloc_ptr[ctx->device];
+  return LLMQ_OK;
+}
+}  // namespace
+
+llmq_status llmq_head_argmax_noalloc(llmq_ctx *ctx, const llmq_weight *w, const float *h, float *logits,
+                                     int *argmax) {
+  if (!ctx || !w || !h || !argmax) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  if (w->kind != WK_AFFINE || !w->a16)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "llmq_head_argmax_noalloc takes A16 formats");
+  CK(cudaSetDevice(ctx->device));
+  int grid = gemv_grid(ctx, w->view());
+  if (grid > kNoallocMaxParts)
+    return fail(ctx, LLMQ_ERR_INVALID,
+                "llmq_head_argmax_noalloc: the gemv grid needs " + std::to_string(grid) +
+                    " partials, beyond the fixed scratch's " + std::to_string(kNoallocMaxParts));
+  unsigned char *scratch = nullptr;
+  llmq_status st = noalloc_scratch(ctx, &scratch);
+  if (st != LLMQ_OK) return st;
+  GemvArgs a{};
+  a.w = w->view();
+  a.x = h;
+  a.out = logits;
+  a.state = (DecodeState *)scratch;
+  a.part_val = (float *)(scratch + kNoallocStateBytes);
+  a.part_idx = (int *)(scratch + kNoallocStateBytes + (size_t)kNoallocMaxParts * 4);
+  a.ids = argmax;  // written at state->step, which the memset sets to 0
+  CK(cudaMemsetAsync(scratch, 0, sizeof(DecodeState), ctx->stream));
   CK(launch_gemv(ctx, a, PRO_QUANT, true, ctx->stream));
   return LLMQ_OK;
 }
