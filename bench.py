@@ -43,6 +43,10 @@ LAYER_WEIGHTS = 12 * (768 * (2304 + 768 + 3072) + 3072 * 768)  # 84,934,656
 LAYER_BYTES = LAYER_WEIGHTS * 19 // 32         # int4-g32: 0.59375 B/weight = 50,429,952
 TOKEN_BYTES = LAYER_BYTES + HEAD_BYTES         # 89,178,099 per token
 METRIC = "int4-g32-a16 decode tok/s (b=1)"
+# DRAM bytes (read + write) of one persistent-kernel launch of this workload,
+# from one ncu capture (profiles/mega_decode_kernel.txt): below the
+# algorithmic bytes because the weight stream stays in L2 across tokens.
+MEGA_TRAFFIC_BYTES = 4_262_806_528
 
 
 def peaks():
@@ -70,6 +74,10 @@ class Clocks:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)  # the sampler is running before the timed region starts
+            self.lines.clear()
         except Exception:
             self.proc = None
         return self
@@ -368,7 +376,10 @@ def main():
                     "h2d_bytes_per_step": 4 * len(PROMPT), "d2h_bytes_per_step": 4 * STEPS_PER_GEN},
             "roofline": {"bound": "hbm", "kernel": "mega_decode_kernel (one launch = the 100-token generation)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None,
+                         "frac": achieved / peak,
+                         "traffic": MEGA_TRAFFIC_BYTES if model.mode() == "persistent" else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch "
+                                           "(profiles/mega_decode_kernel.txt)",
                          "algorithmic_bytes_per_launch": launch_bytes, "avg_launch_ms": launch_ms},
             "weight_bytes_per_token": TOKEN_BYTES,
             "effective_weight_gbs": TOKEN_BYTES * STEPS_PER_GEN * args.steps / (total_ms / 1000.0) / 1e9,
