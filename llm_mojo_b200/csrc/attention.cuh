@@ -1,5 +1,9 @@
 // KV caches and attention (kvcache.mojo, int_attention.mojo) on sm_100a.
 //
+// IntAttnKV (int_attention.mojo:62-280): int8 K in [layer*head][pos/16]
+// [d/2][16][2] and V in [layer*head][pos/2][d][2] with int32 Q24 scales;
+// scores, softmax and value sums in integer fixed point (see ia_attend_kernel).
+//
 // QuantKV[8] (kvcache.mojo:248-385): int8 codes [layer][pos][head][64] with a
 // float32 scale per (layer, pos, head) for keys and for values; attention in
 // float32 through score/add_value (attend_float_one, kvcache.mojo:113-150).
@@ -143,6 +147,249 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c, float *out, 
     }
     for (; s < npos; s++) acc = fmaf(ps[s], (float)vp[(size_t)s * stride], acc);
     out[(size_t)t * C + h * HS + d] = acc;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// IntAttnKV (int_attention.mojo:62-280, intmath.mojo:48-123)
+// ---------------------------------------------------------------------------
+
+constexpr int IA_KS = 24;  // K/V scale fraction bits
+constexpr int IA_SF = 16;  // score fraction bits
+constexpr int IA_PB = 16;  // positions per K block
+
+struct IAView {
+  int8_t *k, *v;
+  int32_t *kq, *vq;  // [layer][head][max_t] scales in Q24
+  int n_layer, max_t, n_head, head_dim;
+};
+
+__device__ __forceinline__ size_t ia_lh(const IAView &c, int layer, int head) {
+  return (size_t)layer * c.n_head + head;
+}
+
+// Byte offset of key (pos, d): blocks of 16 positions, d in pairs, the 16
+// positions of a block interleaved per pair (the VNNI layout of the reference).
+__device__ __forceinline__ size_t ia_k_at(const IAView &c, int layer, int head, int pos, int d) {
+  size_t blk = ia_lh(c, layer, head) * (c.max_t / IA_PB) + pos / IA_PB;
+  return ((blk * (c.head_dim / 2) + d / 2) * IA_PB + pos % IA_PB) * 2 + d % 2;
+}
+
+// Byte offset of value (pos, d): positions in pairs, the pair's two values of
+// dimension d adjacent.
+__device__ __forceinline__ size_t ia_v_at(const IAView &c, int layer, int head, int pos, int d) {
+  size_t pair = ia_lh(c, layer, head) * (c.max_t / 2) + pos / 2;
+  return (pair * c.head_dim + d) * 2 + pos % 2;
+}
+
+// Block-wide reductions over blockDim.x threads (a multiple of 32); red holds
+// 32 slots. Every thread gets the result.
+__device__ __forceinline__ float ia_block_max_f(float v, float *red) {
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = fmaxf(m, red[w]);
+  return m;
+}
+
+__device__ __forceinline__ long long ia_block_max_ll(long long v, long long *red) {
+  for (int o = 16; o > 0; o >>= 1) {
+    long long u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = u > v ? u : v;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long m = red[0];
+  for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = red[w] > m ? red[w] : m;
+  return m;
+}
+
+__device__ __forceinline__ long long ia_block_sum_ll(long long v, long long *red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  long long t = 0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += red[w];
+  return t;
+}
+
+// quantize_head (int_attention.mojo:140-168) of one head's key or value by
+// the block's threads [0, head_dim): int8 codes round(x / s), s = max|x| / 127
+// (1 if zero), the scale kept as round(s * 2^24).
+__device__ __forceinline__ void ia_quantize_head(const IAView &c, float x, bool act, int layer, int h, int pos,
+                                                 int which, float *red) {
+  float mx = ia_block_max_f(act ? fabsf(x) : 0.0f, red);
+  float s = mx / 127.0f;
+  if (s == 0.0f) s = 1.0f;
+  float inv = 1.0f / s;
+  int d = threadIdx.x;
+  if (act) {
+    int8_t code = (int8_t)roundf(x * inv);
+    if (which == 0)
+      c.k[ia_k_at(c, layer, h, pos, d)] = code;
+    else
+      c.v[ia_v_at(c, layer, h, pos, d)] = code;
+  }
+  if (threadIdx.x == 0) {
+    int32_t q = (int32_t)llround((double)s * (double)(1 << IA_KS));
+    (which == 0 ? c.kq : c.vq)[ia_lh(c, layer, h) * c.max_t + pos] = q;
+  }
+}
+
+// IntAttnKV.store of T tokens at pos0.. (int_attention.mojo:119-138).
+// grid (n_head, T, 2), block >= head_dim.
+__global__ void ia_store_kernel(IAView c, const float *qkv, int layer, int pos0) {
+  __shared__ float red[32];
+  int h = blockIdx.x, t = blockIdx.y, which = blockIdx.z;
+  int HS = c.head_dim, C = c.n_head * HS;
+  int d = threadIdx.x;
+  bool act = d < HS;
+  float x = act ? qkv[(size_t)t * 3 * C + (1 + which) * C + h * HS + d] : 0.0f;
+  ia_quantize_head(c, x, act, layer, h, pos0 + t, which, red);
+}
+
+// exp2_neg (intmath.mojo:53-65): 2^(-d * mult / 2^40) in Q30 by a cubic in
+// the fraction and a shift by the integer part.
+__device__ __forceinline__ long long ia_exp2_neg(long long d, long long mult) {
+  const long long DCAP = 1LL << 31;
+  long long y = ((d < DCAP ? d : DCAP) * mult) >> 24;
+  long long q = y >> 16;
+  long long r = y & ((1 << 16) - 1);
+  long long p = -42480028LL;
+  p = ((p * r) >> 16) + 248207216LL;
+  p = ((p * r) >> 16) + (-742598100LL);
+  p = ((p * r) >> 16) + 1073741824LL;
+  return q >= 31 ? 0 : p >> (q < 63 ? q : 63);
+}
+
+// IntAttnKV.attend_one (int_attention.mojo:170-269) for token t (position
+// pos0 + t, or *pos_dev + t) and head h; grid (n_head, T), 256 threads.
+//   1. q as int16: sq = max|q| / 32767, qi = round(q / sq); qm = round(sq /
+//      sqrt(hd) * 2^40).
+//   2. scores over the 16-rounded positions: int32 dot of qi with the int8 key
+//      (dp2a), t = (dot * kq + 2^23) >> 24, S = (t * qm + 2^23) >> 24.
+//   3. masked_exp over the npos valid scores: e in Q30, total in int64.
+//   4. weights w = min((e * r16 + 2^30) >> 31, 32767), r16 = (vq * (2^47 /
+//      vmax)) >> 31; values summed as int32 per 128 pairs of positions and
+//      flushed to float in order; out = acc * vmax * 2^15 / (2^24 * total).
+// Integer sums are exact (mod 2^32 as the reference's), so their order is
+// free; the float flushes keep the reference's order. With store != 0 the CTA
+// first stores this token's key and value for its head (decode, T == 1).
+// Shared memory: max_t * 4 (scores, then e) + (max_t + 2) * 2 (weights) bytes.
+__global__ void __launch_bounds__(256) ia_attend_kernel(IAView c, float *out, const float *qkv, int layer, int pos0,
+                                                        const int *pos_dev, int store, long long mult) {
+  extern __shared__ __align__(16) unsigned char ia_sm[];
+  __shared__ long long redl[32];
+  __shared__ float redf[32];
+  __shared__ int32_t qpair[64];       // qi as int16 pairs (head_dim <= 128)
+  __shared__ int32_t part[4 * 128];   // value partials [part][d]
+  const int h = blockIdx.x, t = blockIdx.y;
+  const int HS = c.head_dim, C = c.n_head * HS;
+  const int P0 = pos_dev ? *pos_dev : pos0;
+  const int npos = P0 + t + 1;
+  const int nr = (npos + IA_PB - 1) / IA_PB * IA_PB;
+  int32_t *sc = (int32_t *)ia_sm;                          // [max_t]
+  int16_t *w = (int16_t *)(ia_sm + (size_t)c.max_t * 4);   // [max_t + 2]
+  const int tid = threadIdx.x;
+
+  if (store) {
+    int pos = P0 + t;
+    for (int which = 0; which < 2; which++) {
+      bool act = tid < HS;
+      float x = act ? qkv[(size_t)t * 3 * C + (1 + which) * C + h * HS + tid] : 0.0f;
+      ia_quantize_head(c, x, act, layer, h, pos, which, redf);
+    }
+    __syncthreads();
+  }
+
+  // 1. the query as int16
+  const float *q = qkv + (size_t)t * 3 * C + h * HS;
+  float qv = tid < HS ? q[tid] : 0.0f;
+  float mq = ia_block_max_f(fabsf(qv), redf);
+  float sq = mq / 32767.0f;
+  if (sq == 0.0f) sq = 1.0f;
+  float invq = 1.0f / sq;
+  int16_t qi = (int16_t)roundf(qv * invq);
+  int16_t qi_next = (int16_t)__shfl_down_sync(0xffffffffu, (int)qi, 1);
+  if (tid < HS && (tid & 1) == 0) qpair[tid / 2] = (int32_t)(uint16_t)qi | ((int32_t)qi_next << 16);
+  const long long qm = llround((double)sq / sqrt((double)HS) * (double)(1LL << (IA_SF + IA_KS)));
+  __syncthreads();
+
+  // 2. scores of positions [0, nr)
+  const int32_t *ks = c.kq + ia_lh(c, layer, h) * c.max_t;
+  long long smax = LLONG_MIN;
+  for (int pos = tid; pos < nr; pos += blockDim.x) {
+    const uint16_t *kp = (const uint16_t *)(c.k + ia_k_at(c, layer, h, pos, 0));
+    int acc = 0;
+    for (int j = 0; j < HS / 2; j++) acc = __dp2a_lo(qpair[j], (int)kp[(size_t)j * IA_PB], acc);
+    long long t1 = ((long long)acc * (long long)ks[pos] + (1LL << (IA_KS - 1))) >> IA_KS;
+    long long sfix = (t1 * qm + (1LL << (IA_KS - 1))) >> IA_KS;
+    sc[pos] = (int32_t)sfix;
+    if (pos < npos && (long long)(int32_t)sfix > smax) smax = (int32_t)sfix;
+  }
+  const long long m = ia_block_max_ll(smax, redl);
+
+  // 3. masked_exp: e in Q30 over the valid positions, total in int64
+  long long part_total = 0;
+  for (int pos = tid; pos < nr; pos += blockDim.x) {
+    long long ev = pos < npos ? ia_exp2_neg(m - (long long)sc[pos], mult) : 0;
+    sc[pos] = (int32_t)ev;
+    part_total += ev;
+  }
+  const long long total = ia_block_sum_ll(part_total, redl);
+
+  // 4. value weights and sums
+  const int32_t *vs = c.vq + ia_lh(c, layer, h) * c.max_t;
+  long long vm = 0;
+  for (int pos = tid; pos < npos; pos += blockDim.x) vm = (long long)vs[pos] > vm ? (long long)vs[pos] : vm;
+  const long long vmax = ia_block_max_ll(vm, redl);
+  float *o = out + (size_t)t * C + h * HS;
+  if (vmax == 0 || total == 0) {
+    for (int d = tid; d < HS; d += blockDim.x) o[d] = 0.0f;
+    return;
+  }
+  const long long inv47 = (1LL << 47) / vmax;
+  for (int pos = tid; pos < nr + 2; pos += blockDim.x) {
+    long long ww = 0;
+    if (pos < nr) {
+      long long ee = sc[pos];
+      long long r16 = pos < npos ? ((long long)vs[pos] * inv47) >> 31 : 0;
+      ww = (ee * r16 + (1LL << 30)) >> 31;
+      if (ww > 32767) ww = 32767;
+      if (ee == 0) ww = 0;
+    }
+    w[pos] = (int16_t)ww;
+  }
+  __syncthreads();
+  const int nparts = blockDim.x / HS;  // threads per dimension
+  const int d = tid % HS, pidx = tid / HS;
+  const int npairs = (npos + 1) / 2;
+  float accf = 0.0f;
+  const uint16_t *vbase = (const uint16_t *)(c.v + ia_v_at(c, layer, h, 0, 0));
+  for (int seg = 0; seg < npairs; seg += 128) {
+    int end = npairs < seg + 128 ? npairs : seg + 128;
+    int acc = 0;
+    if (pidx < nparts)
+      for (int pp = seg + pidx; pp < end; pp += nparts) {
+        int wp = (int)(uint16_t)w[2 * pp] | ((int)w[2 * pp + 1] << 16);
+        acc = __dp2a_lo(wp, (int)vbase[(size_t)pp * HS + d], acc);
+      }
+    if (pidx < nparts) part[pidx * HS + d] = acc;
+    __syncthreads();
+    if (pidx == 0) {
+      unsigned sum = 0;
+      for (int p = 0; p < nparts; p++) sum += (unsigned)part[p * HS + d];
+      accf += (float)(int32_t)sum;
+    }
+    __syncthreads();
+  }
+  if (pidx == 0) {
+    float fs = (float)((double)vmax * (double)(1 << 15) / ((double)(1 << IA_KS) * (double)total));
+    o[d] = accf * fs;
   }
 }
 

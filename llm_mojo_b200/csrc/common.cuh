@@ -8,6 +8,7 @@
 // wherever they run.
 #pragma once
 
+#include <climits>
 #include <cstdint>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>

@@ -48,7 +48,9 @@ struct llmq_weight {
 struct llmq_kv {
   llmq_ctx *ctx;
   int kind;
-  KV8View v8;
+  int n_layer, max_t, n_head, head_dim;
+  KV8View v8{};  // LLMQ_KV_QUANT8
+  IAView ia{};   // LLMQ_KV_INTATTN
 };
 
 struct llmq_model {
@@ -686,26 +688,34 @@ llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int 
                            llmq_kv **out) {
   if (!ctx || !out || n_layer <= 0 || max_t <= 0 || n_head <= 0 || head_dim <= 0 || head_dim % 16 || head_dim > 128)
     return fail(ctx, LLMQ_ERR_INVALID, "bad cache shape");
-  if (kind != LLMQ_KV_QUANT8) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "cache kind not built");
+  if (kind != LLMQ_KV_QUANT8 && kind != LLMQ_KV_INTATTN) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "unknown cache kind");
+  // IntAttnKV keeps keys in blocks of 16 positions and pairs of dimensions
+  // (int_attention.mojo:283-284 aborts on other shapes).
+  if (kind == LLMQ_KV_INTATTN && (max_t % IA_PB || head_dim % 32))
+    return fail(ctx, LLMQ_ERR_INVALID, "IntAttnKV needs max_t % 16 == 0 and head_dim % 32 == 0");
   *out = nullptr;
   CK(cudaSetDevice(ctx->device));
   llmq_kv *c = new llmq_kv();
   c->ctx = ctx;
   c->kind = kind;
+  c->n_layer = n_layer;
+  c->max_t = max_t;
+  c->n_head = n_head;
+  c->head_dim = head_dim;
   size_t n = (size_t)n_layer * max_t * n_head * head_dim, ns = (size_t)n_layer * max_t * n_head;
-  KV8View &v = c->v8;
-  v.n_layer = n_layer;
-  v.max_t = max_t;
-  v.n_head = n_head;
-  v.head_dim = head_dim;
-  cudaError_t e = cudaMalloc(&v.k, n);
-  if (e == cudaSuccess) e = cudaMalloc(&v.v, n);
-  if (e == cudaSuccess) e = cudaMalloc(&v.ks, ns * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&v.vs, ns * 4);
-  if (e == cudaSuccess) e = cudaMemset(v.k, 0, n);
-  if (e == cudaSuccess) e = cudaMemset(v.v, 0, n);
-  if (e == cudaSuccess) e = cudaMemset(v.ks, 0, ns * 4);
-  if (e == cudaSuccess) e = cudaMemset(v.vs, 0, ns * 4);
+  void *k = nullptr, *v = nullptr, *ks = nullptr, *vs = nullptr;
+  cudaError_t e = cudaMalloc(&k, n);
+  if (e == cudaSuccess) e = cudaMalloc(&v, n);
+  if (e == cudaSuccess) e = cudaMalloc(&ks, ns * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&vs, ns * 4);
+  if (e == cudaSuccess) e = cudaMemset(k, 0, n);
+  if (e == cudaSuccess) e = cudaMemset(v, 0, n);
+  if (e == cudaSuccess) e = cudaMemset(ks, 0, ns * 4);
+  if (e == cudaSuccess) e = cudaMemset(vs, 0, ns * 4);
+  if (kind == LLMQ_KV_QUANT8)
+    c->v8 = KV8View{(int8_t *)k, (int8_t *)v, (float *)ks, (float *)vs, n_layer, max_t, n_head, head_dim};
+  else
+    c->ia = IAView{(int8_t *)k, (int8_t *)v, (int32_t *)ks, (int32_t *)vs, n_layer, max_t, n_head, head_dim};
   if (e != cudaSuccess) {
     llmq_kv_free(c);
     return fail(ctx, LLMQ_ERR_CUDA, std::string("kv alloc: ") + cudaGetErrorString(e));
@@ -716,32 +726,46 @@ llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int 
 
 llmq_status llmq_kv_free(llmq_kv *c) {
   if (!c) return LLMQ_ERR_INVALID;
-  if (c->v8.k) cudaFree(c->v8.k);
-  if (c->v8.v) cudaFree(c->v8.v);
-  if (c->v8.ks) cudaFree(c->v8.ks);
-  if (c->v8.vs) cudaFree(c->v8.vs);
+  void *bufs[8] = {c->v8.k, c->v8.v, c->v8.ks, c->v8.vs, c->ia.k, c->ia.v, c->ia.kq, c->ia.vq};
+  for (void *b : bufs)
+    if (b) cudaFree(b);
   delete c;
   return LLMQ_OK;
 }
 
+namespace {
+// exp_multiplier (intmath.mojo:48-50) of the score scale 2^-16.
+long long ia_mult() { return (long long)(1.0 / (double)(1 << IA_SF) * 1.4426950408889634 * (double)(1LL << 40) + 0.5); }
+
+size_t ia_attend_smem(const llmq_kv *kv) { return (size_t)kv->max_t * 4 + (size_t)(kv->max_t + 2) * 2; }
+}  // namespace
+
 llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T, const float *qkv) {
-  if (!ctx || !kv || !qkv || T <= 0 || layer < 0 || layer >= kv->v8.n_layer || pos0 < 0 || pos0 + T > kv->v8.max_t)
+  if (!ctx || !kv || !qkv || T <= 0 || layer < 0 || layer >= kv->n_layer || pos0 < 0 || pos0 + T > kv->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
   CK(cudaSetDevice(ctx->device));
-  dim3 grid(kv->v8.n_head, T, 2);
-  kv8_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr);
+  dim3 grid(kv->n_head, T, 2);
+  if (kv->kind == LLMQ_KV_QUANT8)
+    kv8_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr);
+  else
+    ia_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->ia, qkv, layer, pos0);
   CKL();
   return LLMQ_OK;
 }
 
 llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *qkv, int layer, int T, int pos0) {
-  if (!ctx || !kv || !qkv || !out || T <= 0 || layer < 0 || layer >= kv->v8.n_layer || pos0 < 0 ||
-      pos0 + T > kv->v8.max_t)
+  if (!ctx || !kv || !qkv || !out || T <= 0 || layer < 0 || layer >= kv->n_layer || pos0 < 0 ||
+      pos0 + T > kv->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
   CK(cudaSetDevice(ctx->device));
-  dim3 grid(kv->v8.n_head, T);
-  size_t sm = (size_t)(2 * kv->v8.max_t + kv->v8.head_dim) * 4;
-  kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
+  dim3 grid(kv->n_head, T);
+  if (kv->kind == LLMQ_KV_QUANT8) {
+    size_t sm = (size_t)(2 * kv->max_t + kv->head_dim) * 4;
+    kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
+  } else {
+    ia_attend_kernel<<<grid, 256, ia_attend_smem(kv), ctx->stream>>>(kv->ia, out, qkv, layer, pos0, nullptr, 0,
+                                                                     ia_mult());
+  }
   CKL();
   return LLMQ_OK;
 }
@@ -750,12 +774,15 @@ llmq_status llmq_kv_read(llmq_ctx *ctx, const llmq_kv *kv, void *k, void *v, voi
   if (!ctx || !kv) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
   CK(cudaSetDevice(ctx->device));
   CK(cudaStreamSynchronize(ctx->stream));
-  const KV8View &c = kv->v8;
-  size_t n = (size_t)c.n_layer * c.max_t * c.n_head * c.head_dim, ns = (size_t)c.n_layer * c.max_t * c.n_head;
-  if (k) CK(cudaMemcpy(k, c.k, n, cudaMemcpyDeviceToHost));
-  if (v) CK(cudaMemcpy(v, c.v, n, cudaMemcpyDeviceToHost));
-  if (ks) CK(cudaMemcpy(ks, c.ks, ns * 4, cudaMemcpyDeviceToHost));
-  if (vs) CK(cudaMemcpy(vs, c.vs, ns * 4, cudaMemcpyDeviceToHost));
+  size_t n = (size_t)kv->n_layer * kv->max_t * kv->n_head * kv->head_dim;
+  size_t ns = (size_t)kv->n_layer * kv->max_t * kv->n_head;
+  const bool q8 = kv->kind == LLMQ_KV_QUANT8;
+  const void *src[4] = {q8 ? (const void *)kv->v8.k : kv->ia.k, q8 ? (const void *)kv->v8.v : kv->ia.v,
+                        q8 ? (const void *)kv->v8.ks : kv->ia.kq, q8 ? (const void *)kv->v8.vs : kv->ia.vq};
+  void *dst[4] = {k, v, ks, vs};
+  size_t bytes[4] = {n, n, ns * 4, ns * 4};
+  for (int i = 0; i < 4; i++)
+    if (dst[i]) CK(cudaMemcpy(dst[i], src[i], bytes[i], cudaMemcpyDeviceToHost));
   return LLMQ_OK;
 }
 
@@ -941,7 +968,11 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
     a.out = m->qkv;
     a.epi = EPI_BIAS;
     CK(launch_gemv(ctx, a, PRO_LN, false, s));
-    kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1);
+    if (m->kv->kind == LLMQ_KV_QUANT8)
+      kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1);
+    else
+      ia_attend_kernel<<<dim3(m->n_head, 1), 256, ia_attend_smem(m->kv), s>>>(m->kv->ia, m->att, m->qkv, l, 0,
+                                                                               &m->state->pos, 1, ia_mult());
     CKL();
     a = GemvArgs{};
     a.w = w[1]->view();
