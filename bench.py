@@ -162,6 +162,58 @@ SWEEP_SHAPES = [(2304, 768), (768, 768), (3072, 768), (768, 3072), (50257, 768)]
 SWEEP_AFFINE = ["int8-g32", "int8-g64", "int8-g128", "int8-ch", "int4-g32", "int4-g64", "int4-g128", "int4-ch"]
 
 
+PREFILL_T = 476
+PREFILL_FORMATS = ["int8-ch-a16", "int4-g32-a16"]
+PREFILL_INT_OPS = 2 * PREFILL_T * LAYER_WEIGHTS  # 80.86 G int-ops of the layer GEMMs (head: last token only)
+
+
+def run_prefill(args):
+    """Config 2: 476 ids ~ U[0, 50257) (seed 2), batch 1, one forward of the
+    whole prompt (embedding, 12 layers of prefill GEMMs and attention, the
+    last token's head + argmax), L2 flushed before each step. Device time by
+    CUDA events around llmq_model_forward on the library's stream (the call
+    copies the 1.9 KB of ids in and the argmax out); one JSON line per format."""
+    import torch
+
+    from llm_mojo_b200 import build, synth
+    from llm_mojo_b200.model import Model
+    from llm_mojo_b200.tensor import Context
+
+    build.build()
+    torch.cuda.set_device(0)
+    ctx = Context(0)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    tensors = synth.gpt2_random_init(0)
+    ids = synth.uniform_ids(PREFILL_T, 2)
+    for fmt in PREFILL_FORMATS:
+        model = Model(ctx, tensors, dtype=fmt)
+        times, walls = [], []
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup + args.steps):
+                flush.zero_()
+                s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s0.record(stream)
+                t0 = time.perf_counter()
+                model.forward(ids, 0)
+                walls.append(time.perf_counter() - t0)
+                e0.record(stream)
+                if i >= args.warmup:
+                    times.append((s0, e0))
+            stream.synchronize()
+        ms = statistics.median(s0.elapsed_time(e0) for s0, e0 in times)
+        wall = statistics.median(walls[args.warmup:])
+        print(json.dumps({"workload": "config 2 prefill", "format": fmt, "tokens": PREFILL_T,
+                          "ms_per_prompt": round(ms, 4), "prefill_tok_s": round(PREFILL_T / (ms / 1000.0), 1),
+                          "e2e_tok_s": round(PREFILL_T / wall, 1),
+                          "layer_int_gops": round(PREFILL_INT_OPS / (ms / 1000.0) / 1e9, 1),
+                          "l2": "flushed before each step", "steps": args.steps, "warmup": args.warmup}))
+        model.free()
+    ctx.close()
+    return 0
+
+
 def run_sweep(args):
     """Config 1: x ~ N(0,1) (seed 1), W ~ N(0, 0.02) quantized per format;
     GB/s of packed weight bytes per one-token GEMV, L2 flushed before each
@@ -255,9 +307,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "sweep"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "sweep", "prefill"],
                     help="decode: config 0 (the default bench line); sweep: config 1, the one-token GEMV of every "
-                         "format at every shape, one JSON line each")
+                         "format at every shape, one JSON line each; prefill: config 2, one line per format")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
@@ -266,6 +318,8 @@ def main():
         return run_reference(args)
     if args.workload == "sweep":
         return run_sweep(args)
+    if args.workload == "prefill":
+        return run_prefill(args)
 
     import torch
     import torch.distributed as dist

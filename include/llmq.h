@@ -127,6 +127,15 @@ llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h
 #define LLMQ_NOALLOC_MAX_PARTS 1920
 llmq_status llmq_head_argmax_noalloc(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev,
                                      int *argmax_dev);
+/* Which kernel runs the several-token (T > 1) A16 matmuls of llmq_linear /
+ * llmq_head (tile_i16, kernels.mojo:512-573): AUTO (the tcgen05 split-int8
+ * GEMM from 16 tokens on, where the shape allows), CUDA_CORE (dp tiles), or
+ * TCGEN05 (the GEMM whenever the shape allows). Results are identical; no
+ * counterpart in the reference, which has one CPU kernel. */
+#define LLMQ_PREFILL_AUTO 0
+#define LLMQ_PREFILL_CUDA_CORE 1
+#define LLMQ_PREFILL_TCGEN05 2
+llmq_status llmq_set_prefill_kernel(llmq_ctx *ctx, int kind);
 /* Replaces layernorm (kernels.mojo:179-197), eps 1e-5. */
 llmq_status llmq_layernorm(llmq_ctx *ctx, float *out_dev, const float *x_dev, const float *w_dev,
                            const float *b_dev, int T, int C);

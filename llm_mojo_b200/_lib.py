@@ -17,6 +17,7 @@ OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3,
 BIAS, GELU, RESID = 1, 2, 4
 KV_QUANT8, KV_INTATTN = 1, 2
 MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT = 0, 1, 2
+PREFILL_AUTO, PREFILL_CUDA_CORE, PREFILL_TCGEN05 = 0, 1, 2
 
 
 class LlmqError(RuntimeError):
@@ -45,6 +46,7 @@ SIGNATURES = {
     "llmq_linear": (I, [P, P, P, P, P, I, I, I, I]),
     "llmq_head_argmax": (I, [P, P, P, P, P]),
     "llmq_head_argmax_noalloc": (I, [P, P, P, P, P]),
+    "llmq_set_prefill_kernel": (I, [P, I]),
     "llmq_layernorm": (I, [P, P, P, P, P, I, I]),
     "llmq_quantize_rows": (I, [P, P, I, I, P, P]),
     "llmq_debug_lane_sums": (I, [P, P, P, P]),

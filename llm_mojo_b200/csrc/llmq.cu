@@ -12,6 +12,7 @@
 #include "gemv_float.cuh"
 #include "mega.cuh"
 #include "prefill_a16.cuh"
+#include "tc_gemm.cuh"
 
 using namespace llmq;
 
@@ -26,6 +27,9 @@ struct llmq_ctx {
   size_t scratch_bytes = 0;
   DecodeState *state = nullptr;  // device, for llmq_head_argmax
   int dense_parts = 4;           // gemv's parts: the reference team of 4 threads (gpt2t.mojo:281 on 4 cores)
+  int prefill_kernel = LLMQ_PREFILL_AUTO;
+  int *tc_err = nullptr;         // device error code of the tcgen05 GEMM (a wait that gave up)
+  bool tc_used = false;          // a tcgen05 GEMM ran since the last check
 };
 
 enum { WK_AFFINE = 0, WK_GGUF = 1, WK_DENSE = 2 };
@@ -41,6 +45,7 @@ struct llmq_weight {
   int rtype = 0;             // GGUF / dense: the RT_* row type
   long long row_bytes = 0;
   long long nbytes = 0;
+  mutable uint8_t *tc_b = nullptr;  // split-int8 GEMM tiles of the codes, built on first several-token use
   WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
   RowMat rowmat() const { return RowMat{codes, rows, cols, rtype, row_bytes}; }
 };
@@ -171,6 +176,18 @@ bool smem_ok(const WeightView &w) {
   return b <= kMaxSmem;
 }
 
+// Reads (and clears) the tcgen05 GEMM's error code once a GEMM ran; call
+// after the stream was synchronised.
+llmq_status tc_check(llmq_ctx *ctx) {
+  if (!ctx->tc_used) return LLMQ_OK;
+  ctx->tc_used = false;
+  int code = 0;
+  CK(cudaMemcpy(&code, ctx->tc_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (code == 0) return LLMQ_OK;
+  CK(cudaMemset(ctx->tc_err, 0, sizeof(int)));
+  return fail(ctx, LLMQ_ERR_TIMEOUT, "a tcgen05 GEMM wait gave up (code " + std::to_string(code) + ")");
+}
+
 llmq_status ensure_scratch(llmq_ctx *ctx, size_t bytes) {
   if (ctx->scratch_bytes >= bytes) return LLMQ_OK;
   if (ctx->scratch) cudaFree(ctx->scratch);
@@ -211,6 +228,12 @@ cudaError_t configure_kernels() {
   rs((const void *)row_gemv_kernel<RT_Q4_K>);
   rs((const void *)row_gemv_kernel<RT_Q5_K>);
   rs((const void *)row_gemv_kernel<RT_Q6_K>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)tc_gemm_a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(TcSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)tc_gemm_a16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(TcSmem));
   return e;
 }
 }  // namespace
@@ -260,6 +283,8 @@ llmq_status llmq_init(int device, llmq_ctx **out) {
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->own, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&ctx->state, sizeof(DecodeState));
   if (e == cudaSuccess) e = cudaMemset(ctx->state, 0, sizeof(DecodeState));
+  if (e == cudaSuccess) e = cudaMalloc(&ctx->tc_err, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(ctx->tc_err, 0, sizeof(int));
   if (e == cudaSuccess) e = configure_kernels();
   if (e != cudaSuccess) {
     delete ctx;
@@ -276,6 +301,7 @@ llmq_status llmq_destroy(llmq_ctx *ctx) {
   if (ctx->own) cudaStreamSynchronize(ctx->own);
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->state) cudaFree(ctx->state);
+  if (ctx->tc_err) cudaFree(ctx->tc_err);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
   return LLMQ_OK;
@@ -294,6 +320,12 @@ void *llmq_stream(const llmq_ctx *ctx) { return ctx ? (void *)ctx->stream : null
 llmq_status llmq_sync(llmq_ctx *ctx) {
   if (!ctx) return LLMQ_ERR_INVALID;
   CK(cudaStreamSynchronize(ctx->stream));
+  return tc_check(ctx);
+}
+
+llmq_status llmq_set_prefill_kernel(llmq_ctx *ctx, int kind) {
+  if (!ctx || kind < LLMQ_PREFILL_AUTO || kind > LLMQ_PREFILL_TCGEN05) return fail(ctx, LLMQ_ERR_INVALID, "bad kind");
+  ctx->prefill_kernel = kind;
   return LLMQ_OK;
 }
 
@@ -400,6 +432,7 @@ llmq_status llmq_weight_free(llmq_weight *w) {
   if (w->codes) cudaFree(w->codes);
   if (w->scale) cudaFree(w->scale);
   if (w->zp) cudaFree(w->zp);
+  if (w->tc_b) cudaFree(w->tc_b);
   delete w;
   return LLMQ_OK;
 }
@@ -443,6 +476,88 @@ llmq_status llmq_set_dense_parts(llmq_ctx *ctx, int nparts) {
   ctx->dense_parts = nparts;
   return LLMQ_OK;
 }
+
+}  // extern "C"
+
+namespace {
+
+// Whether the several-token A16 matmul of w runs on the tcgen05 GEMM: K in
+// whole 128-byte blocks and segments, at most TC_MAX_GROUPS groups per row,
+// and (AUTO) at least 16 tokens.
+bool tc_eligible(const llmq_ctx *ctx, const llmq_weight *w, int T) {
+  if (ctx->prefill_kernel == LLMQ_PREFILL_CUDA_CORE) return false;
+  if (ctx->prefill_kernel == LLMQ_PREFILL_AUTO && T < 16) return false;
+  const int K = w->cols, G = w->group, seg = std::min(G, 256);
+  return w->kind == WK_AFFINE && w->a16 && K % TC_KB == 0 && K % seg == 0 && seg % 32 == 0 &&
+         K / G <= TC_MAX_GROUPS && K / seg <= TC_MAX_GROUPS * 8 && w->rows >= 32;
+}
+
+size_t align256(size_t n) { return (n + 255) / 256 * 256; }
+
+// matmul_rows_a16 for T > 1 (kernels.mojo:461-507) with the tile_i16 rows
+// (the first OUT / 32 * 32 outputs) on the split-int8 tcgen05 GEMM and the
+// leftover rows (rows_i16) on rows_a16_kernel.
+llmq_status tc_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
+                      int IN, int OUT, int epi) {
+  const int K = IN, nkb = K / TC_KB, seg = std::min(w->group, 256), nseg = K / seg;
+  const int mtiles = (T + TC_M - 1) / TC_M, m_pad = mtiles * TC_M;
+  const int full = OUT / 32 * 32, ntiles = (full + TC_N - 1) / TC_N;
+  const bool zc = w->bits == 8;
+  const size_t a_bytes = align256((size_t)mtiles * nkb * TC_A_BYTES), sx_bytes = align256((size_t)m_pad * 4);
+  const size_t xs_bytes = zc ? align256((size_t)m_pad * nseg * 4) : 0;
+  const size_t xq_bytes = (OUT % 32) ? align256((size_t)T * IN * 2) : 0;
+  llmq_status st = ensure_scratch(ctx, a_bytes + sx_bytes + xs_bytes + xq_bytes);
+  if (st != LLMQ_OK) return st;
+  uint8_t *a = (uint8_t *)ctx->scratch;
+  float *sx = (float *)(a + a_bytes);
+  int *xsum = zc ? (int *)((char *)sx + sx_bytes) : nullptr;
+  int16_t *xq = xq_bytes ? (int16_t *)((char *)sx + sx_bytes + xs_bytes) : nullptr;
+  if (!w->tc_b) {
+    const int wt = (w->rows + TC_N - 1) / TC_N;
+    CK(cudaMalloc(&w->tc_b, (size_t)wt * nkb * TC_B_BYTES));
+    tc_prep_b_kernel<<<dim3(wt, nkb), 256, 0, ctx->stream>>>(w->view(), w->tc_b);
+    CKL();
+  }
+  tc_split_rows_kernel<<<m_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, a, sx, xsum, xq);
+  CKL();
+  if (ntiles > 0) {
+    TcArgs p{};
+    p.a = a;
+    p.b = w->tc_b;
+    p.sx = sx;
+    p.xsum = xsum;
+    p.w = w->view();
+    p.bias = bias;
+    p.out = out;
+    p.err = ctx->tc_err;
+    p.T = T;
+    p.OUT = OUT;
+    p.n_full = full;
+    p.K = K;
+    p.nkb = nkb;
+    p.nseg = nseg;
+    p.seg_ks = seg / 32;
+    p.seg = seg;
+    p.epi = epi;
+    dim3 grid(ntiles, mtiles);
+    if (zc)
+      tc_gemm_a16_kernel<true><<<grid, TC_THREADS, sizeof(TcSmem), ctx->stream>>>(p);
+    else
+      tc_gemm_a16_kernel<false><<<grid, TC_THREADS, sizeof(TcSmem), ctx->stream>>>(p);
+    CKL();
+    ctx->tc_used = true;
+  }
+  if (OUT % 32) {
+    int n = T * (OUT - full);
+    rows_a16_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(w->view(), xq, sx, bias, out, T, OUT, full, epi);
+    CKL();
+  }
+  return LLMQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
 
 llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
                         int IN, int OUT, int flags) {
@@ -496,6 +611,7 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     CK(launch_gemv(ctx, a, PRO_QUANT, false, ctx->stream));
     return LLMQ_OK;
   }
+  if (tc_eligible(ctx, w, T)) return tc_linear(ctx, w, x, bias, out, T, IN, OUT, epi);
   size_t need = (size_t)T * IN * 2 + (size_t)T * 4 + 256;
   llmq_status st = ensure_scratch(ctx, need);
   if (st != LLMQ_OK) return st;

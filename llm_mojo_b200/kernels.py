@@ -11,7 +11,8 @@ from __future__ import annotations
 
 import ctypes as C
 
-from ._lib import BIAS, GELU, KV_INTATTN, KV_QUANT8, RESID, check, lib
+from ._lib import (BIAS, GELU, KV_INTATTN, KV_QUANT8, PREFILL_AUTO, PREFILL_CUDA_CORE, PREFILL_TCGEN05, RESID, check,
+                   lib)
 from .tensor import Context, QuantMatrix
 
 
@@ -42,6 +43,15 @@ def head(ctx: Context, logits, h, w, T: int, V: int, C_: int):
     _pre(ctx)
     check(lib().llmq_head(ctx.h, w.h, _p(h), _p(logits), T, C_, V), ctx.h)
     ctx.sync()
+
+
+PREFILL_KERNELS = {"auto": PREFILL_AUTO, "cuda_core": PREFILL_CUDA_CORE, "tcgen05": PREFILL_TCGEN05}
+
+
+def set_prefill_kernel(ctx: Context, kind: str):
+    """The kernel of several-token A16 matmuls: 'auto' (tcgen05 from 16
+    tokens), 'cuda_core' or 'tcgen05'. Results are identical."""
+    check(lib().llmq_set_prefill_kernel(ctx.h, PREFILL_KERNELS[kind]), ctx.h)
 
 
 def set_dense_parts(ctx: Context, nparts: int):
