@@ -150,6 +150,169 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c, float *out, 
   }
 }
 
+// attend_float_one for QB consecutive query tokens of one head at once (the
+// several-token path, prefill). Keys, then values, are staged in tiles of 128
+// positions converted once to float (each converted value then serves all
+// QB queries); the scores of every query stay in shared memory for the
+// softmax. Per query the arithmetic is attend_float_one's, in the same
+// order: score lanes + halving tree, * ks, * scale; exp of (score - max); the
+// total summed in position order; acc[d] = fma(p * vs, v[d], acc) in
+// position order. grid (n_head, ceil(T / QB)), 256 threads; shared memory
+// kv8_prefill_smem(P, head_dim), P the positions the block's last query sees.
+constexpr int KV_QB = 16;
+constexpr int KV_TILE = 128;
+
+__host__ __device__ inline size_t kv8_prefill_smem(int P, int HS) {
+  // tile [128][HS + 1] floats, its scales [128], q [QB][HS], scores [QB][P], totals [QB]
+  return (size_t)KV_TILE * (HS + 1) * 4 + KV_TILE * 4 + (size_t)KV_QB * HS * 4 + (size_t)KV_QB * P * 4 + KV_QB * 4;
+}
+
+__global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c, float *out, const float *qkv, int layer, int pos0,
+                                                          int T) {
+  extern __shared__ __align__(16) float kvp_sm[];
+  const int h = blockIdx.x, t0 = blockIdx.y * KV_QB;
+  const int nq = min(KV_QB, T - t0);
+  const int HS = c.head_dim, C = c.n_head * HS, HP = HS + 1;
+  const int P = pos0 + t0 + nq;  // positions the last query of the block sees
+  float *tile = kvp_sm;                        // [128][HS + 1]
+  float *tsc = tile + KV_TILE * HP;            // [128]
+  float *qs = tsc + KV_TILE;                   // [QB][HS]
+  float *sc = qs + KV_QB * HS;                 // [QB][P]
+  float *tot = sc + (size_t)KV_QB * P;         // [QB]
+  const int tid = threadIdx.x;
+  const size_t head_stride = (size_t)c.n_head * HS;
+  const int8_t *kbase = c.k + ((size_t)layer * c.max_t * c.n_head + h) * HS;
+  const int8_t *vbase = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
+  const size_t sbase = (size_t)layer * c.max_t * c.n_head + h;
+
+  for (int i = tid; i < KV_QB * HS; i += blockDim.x) {
+    const int qi = i / HS, d = i % HS;
+    qs[i] = qi < nq ? qkv[(size_t)(t0 + qi) * 3 * C + h * HS + d] : 0.0f;
+  }
+  // a tile of 128 positions of keys (which 0) or values (1) as floats, and
+  // their scales
+  auto stage = [&](int s0, int which) {
+    const int8_t *src = which == 0 ? kbase : vbase;
+    const float *scl = which == 0 ? c.ks : c.vs;
+    const int n = min(KV_TILE, P - s0), cpr = HS / 16;
+    for (int i = tid; i < n * cpr; i += blockDim.x) {
+      const int r = i / cpr, ch = i % cpr;
+      int4 raw = *(const int4 *)(src + (size_t)(s0 + r) * head_stride + ch * 16);
+      const int8_t *b = (const int8_t *)&raw;
+      float *dst = tile + r * HP + ch * 16;
+#pragma unroll
+      for (int l = 0; l < 16; l++) dst[l] = (float)b[l];
+    }
+    for (int r = tid; r < n; r += blockDim.x) tsc[r] = scl[(sbase + (size_t)(s0 + r) * c.n_head)];
+  };
+
+  // 1. scores, a tile of keys at a time; a thread takes one position for 4
+  // queries, so each key value it loads serves 4 dot products
+  const float scale = 1.0f / sqrtf((float)HS);
+  const int ngroups = (nq + 3) / 4;
+  for (int s0 = 0; s0 < P; s0 += KV_TILE) {
+    __syncthreads();
+    stage(s0, 0);
+    __syncthreads();
+    const int n = min(KV_TILE, P - s0);
+    for (int i = tid; i < n * ngroups; i += blockDim.x) {
+      const int r = i % n, g = i / n, s = s0 + r, q0 = g * 4;
+      const float *kr = tile + r * HP;
+      float d[4][16];
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+#pragma unroll
+        for (int l = 0; l < 16; l++) d[j][l] = 0.0f;
+      for (int i0 = 0; i0 < HS; i0 += 16) {
+        float kf[16];
+#pragma unroll
+        for (int l = 0; l < 16; l++) kf[l] = kr[i0 + l];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float *q = qs + (q0 + j) * HS + i0;
+#pragma unroll
+          for (int l = 0; l < 16; l++) d[j][l] = d[j][l] + q[l] * kf[l];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int qi = q0 + j;
+        if (qi >= nq || s >= pos0 + t0 + qi + 1) continue;
+        float *e = d[j];
+#pragma unroll
+        for (int l = 0; l < 8; l++) e[l] = e[l] + e[l + 8];
+#pragma unroll
+        for (int l = 0; l < 4; l++) e[l] = e[l] + e[l + 4];
+        e[0] = e[0] + e[2];
+        e[1] = e[1] + e[3];
+        sc[(size_t)qi * P + s] = ((e[0] + e[1]) * tsc[r]) * scale;
+      }
+    }
+  }
+  __syncthreads();
+
+  // 2. per query: max and exponentials (a warp per query), the totals in
+  // position order (a thread per query), then p * vs
+  const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+  for (int qi = warp; qi < nq; qi += nwarps) {
+    const int np = pos0 + t0 + qi + 1;
+    float *row = sc + (size_t)qi * P;
+    float mx = -__int_as_float(0x7f800000);
+    for (int s = lane; s < np; s += 32) mx = fmaxf(mx, row[s]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int s = lane; s < np; s += 32) row[s] = lm_expf(row[s] - mx);
+  }
+  __syncthreads();
+  if (tid < nq) {
+    const int np = pos0 + t0 + tid + 1;
+    const float *row = sc + (size_t)tid * P;
+    float total = 0.0f;
+    int s = 0;
+    for (; s + 8 <= np; s += 8) {
+      float e[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) e[j] = row[s + j];
+#pragma unroll
+      for (int j = 0; j < 8; j++) total += e[j];
+    }
+    for (; s < np; s++) total += row[s];
+    tot[tid] = total;
+  }
+  __syncthreads();
+
+  // 3. values, a tile at a time: one chain per (query, dimension) in position
+  // order; a thread runs the chains of 4 consecutive queries for one dimension
+  const int nchains = ngroups * HS;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // chains of thread tid (nchains <= blockDim)
+  const int g = tid / HS, dd = tid % HS, q0 = g * 4;
+  for (int s0 = 0; s0 < P; s0 += KV_TILE) {
+    __syncthreads();
+    stage(s0, 1);
+    __syncthreads();
+    // p * vs for this tile's positions
+    const int n = min(KV_TILE, P - s0);
+    for (int i = tid; i < nq * n; i += blockDim.x) {
+      const int qi = i / n, r = i % n, s = s0 + r;
+      if (s < pos0 + t0 + qi + 1) sc[(size_t)qi * P + s] = (sc[(size_t)qi * P + s] / tot[qi]) * tsc[r];
+    }
+    __syncthreads();
+    if (tid < nchains) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int qi = q0 + j;
+        if (qi >= nq) break;
+        const int np = min(pos0 + t0 + qi + 1, s0 + n);  // this query's positions within the tile
+        const float *ps = sc + (size_t)qi * P;
+        float a = acc[j];
+        for (int s = s0; s < np; s++) a = fmaf(ps[s], tile[(s - s0) * HP + dd], a);
+        acc[j] = a;
+      }
+    }
+  }
+  if (tid < nchains)
+    for (int j = 0; j < 4 && q0 + j < nq; j++) out[(size_t)(t0 + q0 + j) * C + h * HS + dd] = acc[j];
+}
+
 // ---------------------------------------------------------------------------
 // IntAttnKV (int_attention.mojo:62-280, intmath.mojo:48-123)
 // ---------------------------------------------------------------------------

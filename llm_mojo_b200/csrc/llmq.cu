@@ -46,6 +46,7 @@ struct llmq_weight {
   long long row_bytes = 0;
   long long nbytes = 0;
   mutable uint8_t *tc_b = nullptr;  // split-int8 GEMM tiles of the codes, built on first several-token use
+  mutable int tc_tn = 0;            // their output tile width
   WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
   RowMat rowmat() const { return RowMat{codes, rows, cols, rtype, row_bytes}; }
 };
@@ -116,6 +117,7 @@ llmq_status fail(llmq_ctx *ctx, llmq_status st, const std::string &msg) {
     if (e_ != cudaSuccess) return fail(ctx, LLMQ_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e_)); \
   } while (0)
 
+constexpr int kMaxPrefillSmem = 225 * 1024;  // the several-token attention's staging limit
 constexpr int kR = 16, kP = 3;
 constexpr int kThreads = kR * kP * 4;
 
@@ -229,11 +231,16 @@ cudaError_t configure_kernels() {
   rs((const void *)row_gemv_kernel<RT_Q5_K>);
   rs((const void *)row_gemv_kernel<RT_Q6_K>);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute((const void *)tc_gemm_a16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(TcSmem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute((const void *)tc_gemm_a16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(TcSmem));
+    e = cudaFuncSetAttribute((const void *)kv8_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kMaxPrefillSmem);
+  auto tcs = [&](const void *k) {
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TcSmem) + 1024);
+  };
+  tcs((const void *)tc_gemm_a16_kernel<true, 64>);
+  tcs((const void *)tc_gemm_a16_kernel<true, 32>);
+  tcs((const void *)tc_gemm_a16_kernel<false, 64>);
+  tcs((const void *)tc_gemm_a16_kernel<false, 32>);
   return e;
 }
 }  // namespace
@@ -501,7 +508,10 @@ llmq_status tc_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const
                       int IN, int OUT, int epi) {
   const int K = IN, nkb = K / TC_KB, seg = std::min(w->group, 256), nseg = K / seg;
   const int mtiles = (T + TC_M - 1) / TC_M, m_pad = mtiles * TC_M;
-  const int full = OUT / 32 * 32, ntiles = (full + TC_N - 1) / TC_N;
+  // 32-wide output tiles for narrow matrices (more CTAs), 64 otherwise; the
+  // weight's prepared tiles follow the width chosen on its first use.
+  const int tn = w->tc_b ? w->tc_tn : (OUT <= 1024 ? 32 : 64);
+  const int full = OUT / 32 * 32, ntiles = (full + tn - 1) / tn;
   const bool zc = w->bits == 8;
   const size_t a_bytes = align256((size_t)mtiles * nkb * TC_A_BYTES), sx_bytes = align256((size_t)m_pad * 4);
   const size_t xs_bytes = zc ? align256((size_t)m_pad * nseg * 4) : 0;
@@ -513,9 +523,10 @@ llmq_status tc_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const
   int *xsum = zc ? (int *)((char *)sx + sx_bytes) : nullptr;
   int16_t *xq = xq_bytes ? (int16_t *)((char *)sx + sx_bytes + xs_bytes) : nullptr;
   if (!w->tc_b) {
-    const int wt = (w->rows + TC_N - 1) / TC_N;
-    CK(cudaMalloc(&w->tc_b, (size_t)wt * nkb * TC_B_BYTES));
-    tc_prep_b_kernel<<<dim3(wt, nkb), 256, 0, ctx->stream>>>(w->view(), w->tc_b);
+    const int wt = (w->rows + tn - 1) / tn;
+    CK(cudaMalloc(&w->tc_b, (size_t)wt * nkb * tn * TC_KB));
+    w->tc_tn = tn;
+    tc_prep_b_kernel<<<dim3(wt, nkb), 256, 0, ctx->stream>>>(w->view(), w->tc_b, tn);
     CKL();
   }
   tc_split_rows_kernel<<<m_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, a, sx, xsum, xq);
@@ -540,10 +551,15 @@ llmq_status tc_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const
     p.seg = seg;
     p.epi = epi;
     dim3 grid(ntiles, mtiles);
-    if (zc)
-      tc_gemm_a16_kernel<true><<<grid, TC_THREADS, sizeof(TcSmem), ctx->stream>>>(p);
+    const size_t sm = sizeof(TcSmem) + 1024;
+    if (zc && tn == 64)
+      tc_gemm_a16_kernel<true, 64><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+    else if (zc)
+      tc_gemm_a16_kernel<true, 32><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+    else if (tn == 64)
+      tc_gemm_a16_kernel<false, 64><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
     else
-      tc_gemm_a16_kernel<false><<<grid, TC_THREADS, sizeof(TcSmem), ctx->stream>>>(p);
+      tc_gemm_a16_kernel<false, 32><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
     CKL();
     ctx->tc_used = true;
   }
@@ -875,7 +891,11 @@ llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *
     return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
   CK(cudaSetDevice(ctx->device));
   dim3 grid(kv->n_head, T);
-  if (kv->kind == LLMQ_KV_QUANT8) {
+  if (kv->kind == LLMQ_KV_QUANT8 && T > 1 && kv8_prefill_smem(pos0 + T, kv->head_dim) <= (size_t)kMaxPrefillSmem) {
+    const size_t sm = kv8_prefill_smem(pos0 + T, kv->head_dim);
+    kv8_prefill_kernel<<<dim3(kv->n_head, (T + KV_QB - 1) / KV_QB), 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer,
+                                                                                            pos0, T);
+  } else if (kv->kind == LLMQ_KV_QUANT8) {
     size_t sm = (size_t)(2 * kv->max_t + kv->head_dim) * 4;
     kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
   } else {

@@ -13,19 +13,21 @@
 // order, so outputs are bit-identical.
 //
 // Operands are staged as tiles that one bulk copy each brings into shared
-// memory, already in the MMA's no-swizzle K-major layout (8-row x 16-byte core
-// matrices): for each 128-byte K block, 8 columns of 16 bytes, each column
-// the tile's rows one after the other.
+// memory, already in the MMA's K-major 128-byte swizzle layout (rows of one
+// 128-byte K block, 8-row atoms with the 16-byte chunks permuted by row, which
+// keeps the tensor core's shared-memory reads free of bank conflicts):
 //   A (activations, prepared per call by tc_split_rows_kernel):
-//     [m_tile][k_block][plane l,h][chunk 8][128 rows][16 B]
+//     [m_tile][k_block][plane l,h][128 rows x 128 B, swizzled]
 //   B (weights, prepared once per weight by tc_prep_b_kernel):
-//     [n_tile][k_block][chunk 8][64 rows][16 B], int4 as int8 (u - zp), int8
-//     as its u8 code (zero point applied in the epilogue).
+//     [n_tile][k_block][TN rows x 128 B, swizzled], int4 as int8 (u - zp),
+//     int8 as its u8 code (zero point applied in the epilogue).
 //
-// One CTA per 128 x 64 output tile: warp 8 issues the bulk copies and the
-// MMAs (one thread), warps 0-7 read the accumulators segment by segment
-// (warp w: tensor-memory lanes 32 * (w % 4), columns 32 * (w / 4)), while
-// the MMAs of the next segments run into 4 rotating accumulator pairs.
+// One CTA per 128 x TN output tile (TN 64, or 32 for narrow matrices, so
+// that more SMs take part): warp 16 issues the bulk copies and the MMAs (one
+// thread), warps 0-15 read the accumulators segment by segment (warp w:
+// tensor-memory lanes 32 * (w % 4), TN / 4 columns at (w / 4) * TN / 4),
+// loading the next segment while folding this one, while the MMAs of the
+// following segments run into rotating accumulator pairs (512 columns).
 #pragma once
 
 #include "gemv_a16.cuh"
@@ -33,27 +35,29 @@
 namespace llmq {
 
 constexpr int TC_M = 128;                                  // tokens per tile (MMA M)
-constexpr int TC_N = 64;                                   // outputs per tile (MMA N)
 constexpr int TC_KB = 128;                                 // K bytes per pipeline stage
 constexpr int TC_STAGES = 4;
-constexpr int TC_NBUF = 4;                                 // accumulator pairs: 4 * 2 * 64 = 512 columns
 constexpr int TC_A_PLANE = TC_M * TC_KB;                   // 16 KB
 constexpr int TC_A_BYTES = 2 * TC_A_PLANE;                 // 32 KB, planes l and h
-constexpr int TC_B_BYTES = TC_N * TC_KB;                   // 8 KB
-constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_BYTES;    // 40 KB
-constexpr int TC_EPI_WARPS = 8;
-constexpr int TC_THREADS = (TC_EPI_WARPS + 1) * 32;        // 288
+constexpr int TC_NMAX = 64;                                // outputs per tile (MMA N): 64, or 32 for narrow matrices
+constexpr int TC_B_MAX = TC_NMAX * TC_KB;                  // 8 KB
+constexpr int TC_STAGE_BYTES = TC_A_BYTES + TC_B_MAX;      // 40 KB
+constexpr int TC_EPI_WARPS = 16;                           // 4 lane quarters x 4 column groups
+constexpr int TC_THREADS = (TC_EPI_WARPS + 1) * 32;        // 544
 constexpr int TC_MAX_GROUPS = 96;                          // groups per row in the scale table
 constexpr int TC_TMEM_COLS = 512;
 constexpr long long TC_TIMEOUT = 4000000000LL;             // cycles a wait may take (~2 s)
 
 enum { TC_ERR_FULL = 1, TC_ERR_EMPTY = 2, TC_ERR_ACC = 3, TC_ERR_ACCEMPTY = 4 };
 
+constexpr int TC_NBUF_MAX = 8;
+
 struct TcSmem {
-  alignas(128) uint8_t stage[TC_STAGES][TC_STAGE_BYTES];
-  float scale[TC_MAX_GROUPS][TC_N];
-  uint8_t zc[TC_MAX_GROUPS][TC_N];
-  alignas(8) unsigned long long full[TC_STAGES], empty[TC_STAGES], accfull[TC_NBUF], accempty[TC_NBUF], drain;
+  alignas(1024) uint8_t stage[TC_STAGES][TC_STAGE_BYTES];
+  float scale[TC_MAX_GROUPS][TC_NMAX];
+  uint8_t zc[TC_MAX_GROUPS][TC_NMAX];
+  alignas(8) unsigned long long full[TC_STAGES], empty[TC_STAGES], accfull[TC_NBUF_MAX], accempty[TC_NBUF_MAX],
+      drain;
   unsigned tmem;
   int abort;
 };
@@ -83,12 +87,15 @@ __device__ __forceinline__ void tc_mbar_arrive(unsigned bar) {
 __device__ __forceinline__ void tc_mbar_expect_tx(unsigned bar, unsigned bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: the warp sleeps in hardware until the
+// phase completes (or ~0.1 ms pass) instead of spinning on the issue slots
+// that the working warps need.
 __device__ __forceinline__ bool tc_mbar_try(unsigned bar, unsigned parity) {
   unsigned ok;
   asm volatile(
-      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+      "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(100000u)
       : "memory");
   return ok != 0;
 }
@@ -100,17 +107,25 @@ __device__ __forceinline__ void tc_bulk_g2s(unsigned dst, const void *src, unsig
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor, no swizzle, K-major: start, LBO (between
-// the two 16-byte K columns of one MMA), SBO (between 8-row core matrices).
-__device__ __forceinline__ unsigned long long tc_desc(unsigned addr, unsigned lbo, unsigned sbo) {
-  return (unsigned long long)((addr >> 4) & 0x3FFF) | ((unsigned long long)((lbo >> 4) & 0x3FFF) << 16) |
-         ((unsigned long long)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);  // version 1, base 0, no swizzle
+// Shared-memory matrix descriptor of a K-major operand in the 128-byte
+// swizzle layout: rows of 128 bytes (one K block), 8-row atoms of 1024 bytes
+// (SBO), the 16-byte chunk c of row r stored at chunk c ^ (r % 8). LBO is
+// unused for this layout (1). The start address steps by 32 bytes per MMA K
+// step inside the row; the swizzle applies to the final addresses, so atoms
+// must be 1024-byte aligned.
+__device__ __forceinline__ unsigned long long tc_desc_sw128(unsigned addr) {
+  return (unsigned long long)((addr >> 4) & 0x3FFF) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Byte offset of the 16-byte chunk c of row r in a 128-byte-swizzled tile.
+__host__ __device__ __forceinline__ unsigned tc_sw128_off(int r, int c) {
+  return (unsigned)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
 // Instruction descriptor of kind::i8: D s32, A/B u8 (0) or s8 (1), both
-// K-major, N = 64, M = 128.
-__host__ __device__ constexpr unsigned tc_idesc(int a_signed, int b_signed) {
-  return (2u << 4) | ((unsigned)a_signed << 7) | ((unsigned)b_signed << 10) | ((unsigned)(TC_N >> 3) << 17) |
+// K-major, N = n, M = 128.
+__host__ __device__ constexpr unsigned tc_idesc(int a_signed, int b_signed, int n) {
+  return (2u << 4) | ((unsigned)a_signed << 7) | ((unsigned)b_signed << 10) | ((unsigned)(n >> 3) << 17) |
          ((unsigned)(TC_M >> 4) << 24);
 }
 
@@ -126,15 +141,25 @@ __device__ __forceinline__ void tc_commit(unsigned bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ void tc_ld32(unsigned addr, int (&r)[32]) {
+// Tensor-memory loads of 16 or 8 consecutive columns of the warp's 32 lanes
+// (asynchronous until tc_ld_wait; tc_ld_done then ties later uses to it).
+__device__ __forceinline__ void tc_ld(unsigned addr, int (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(addr));
+}
+__device__ __forceinline__ void tc_ld(unsigned addr, int (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(addr));
+}
+template <int N>
+__device__ __forceinline__ void tc_ld_done(int (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
 }
 __device__ __forceinline__ void tc_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -203,7 +228,7 @@ __global__ void __launch_bounds__(256) tc_split_rows_kernel(const float *x, int 
       }
       if (xsum) atomicAdd(&ssum[k0 / seg], part);
     }
-    uint8_t *base = a + ((size_t)mt * nkb + kb) * TC_A_BYTES + ((size_t)chunk * TC_M + r) * 16;
+    uint8_t *base = a + ((size_t)mt * nkb + kb) * TC_A_BYTES + tc_sw128_off(r, chunk);
     *(uint4 *)base = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *(uint4 *)(base + TC_A_PLANE) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
   }
@@ -213,14 +238,15 @@ __global__ void __launch_bounds__(256) tc_split_rows_kernel(const float *x, int 
     for (int i = threadIdx.x; i < nseg; i += blockDim.x) xsum[(size_t)m * nseg + i] = ssum[i];
 }
 
-// B tiles of a weight: grid (n_tiles, nkb), 256 threads; int4 codes become
-// int8 (u - zp), int8 codes stay u8. Rows >= rows are zero.
-__global__ void tc_prep_b_kernel(WeightView w, uint8_t *b) {
+// B tiles of a weight for an output tile width tn (64 or 32): grid
+// (n_tiles, nkb), 256 threads; int4 codes become int8 (u - zp), int8 codes
+// stay u8. Rows >= rows are zero.
+__global__ void tc_prep_b_kernel(WeightView w, uint8_t *b, int tn) {
   const int nt = blockIdx.x, kb = blockIdx.y, nkb = gridDim.y;
   const int gpr = w.cols / w.group;
-  uint8_t *dst = b + ((size_t)nt * nkb + kb) * TC_B_BYTES;
-  for (int ci = threadIdx.x; ci < 8 * TC_N; ci += blockDim.x) {
-    const int chunk = ci / TC_N, r = ci % TC_N, n = nt * TC_N + r, k0 = kb * TC_KB + chunk * 16;
+  uint8_t *dst = b + ((size_t)nt * nkb + kb) * tn * TC_KB;
+  for (int ci = threadIdx.x; ci < 8 * tn; ci += blockDim.x) {
+    const int chunk = ci / tn, r = ci % tn, n = nt * tn + r, k0 = kb * TC_KB + chunk * 16;
     uint32_t v[4] = {0, 0, 0, 0};
     if (n < w.rows) {
 #pragma unroll
@@ -230,18 +256,48 @@ __global__ void tc_prep_b_kernel(WeightView w, uint8_t *b) {
         v[i >> 2] |= (uint32_t)(e & 0xFF) << (8 * (i & 3));
       }
     }
-    *(uint4 *)(dst + ((size_t)chunk * TC_N + r) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
+    *(uint4 *)(dst + tc_sw128_off(r, chunk)) = make_uint4(v[0], v[1], v[2], v[3]);
   }
 }
 
 // --- the GEMM -----------------------------------------------------------------
 
-template <bool ZC>
+// Exact float of an int32 |v| < 2^22 without the conversion unit: the bits
+// of 1.5 * 2^23 + v, minus 1.5 * 2^23.
+__device__ __forceinline__ float tc_small_to_float(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
+
+// Folds one segment's accumulators into the float chains of CW columns:
+// accf = fma(f32(256 * h + l - zp * sum x), s, accf). Without a zero-point
+// term (int4 weights, whose |h|, |l| < 2^22 for every segment length) the
+// float of 256 * h + l is fma(256, f32(h), f32(l)): both exact, one rounding,
+// the same as the conversion of the int32 sum; the conversions then use the
+// FMA and ALU pipes instead of the slower conversion unit.
+template <bool ZC, int CW>
+__device__ __forceinline__ void tc_fold(float (&accf)[CW], const int (&l)[CW], const int (&h)[CW], const float *sc,
+                                        const uint8_t *zc, unsigned xs) {
+#pragma unroll
+  for (int c = 0; c < CW; c++) {
+    float v;
+    if (ZC) {
+      unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c] - (unsigned)zc[c] * xs;
+      v = (float)(int)a;
+    } else {
+      v = fmaf(256.0f, tc_small_to_float(h[c]), tc_small_to_float(l[c]));
+    }
+    accf[c] = fmaf(v, sc[c], accf[c]);
+  }
+}
+
+template <bool ZC, int TN>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_a16_kernel(TcArgs p) {
+  constexpr int NBUF = TC_TMEM_COLS / (2 * TN);  // accumulator pairs in tensor memory
+  constexpr int CW = TN / 4;                     // columns per epilogue warp
+  constexpr int BBYTES = TN * TC_KB;
   extern __shared__ __align__(128) unsigned char tc_raw[];
-  TcSmem &sm = *reinterpret_cast<TcSmem *>(tc_raw);
+  // the swizzle atoms need 1024-byte aligned stages (the launch adds 1 KB)
+  TcSmem &sm = *reinterpret_cast<TcSmem *>(tc_raw + ((1024u - (tc_u32(tc_raw) & 1023u)) & 1023u));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.x, mt = blockIdx.y, n0 = nt * TC_N, m0 = mt * TC_M;
+  const int nt = blockIdx.x, mt = blockIdx.y, n0 = nt * TN, m0 = mt * TC_M;
   const int G = p.w.group, gpr = p.w.cols / G;
 
   if (threadIdx.x == 0) {
@@ -249,7 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_a16_kernel(TcArgs p) {
       tc_mbar_init(tc_u32(&sm.full[s]), 1);
       tc_mbar_init(tc_u32(&sm.empty[s]), 1);
     }
-    for (int b = 0; b < TC_NBUF; b++) {
+    for (int b = 0; b < NBUF; b++) {
       tc_mbar_init(tc_u32(&sm.accfull[b]), 1);
       tc_mbar_init(tc_u32(&sm.accempty[b]), TC_EPI_WARPS);
     }
@@ -263,8 +319,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_a16_kernel(TcArgs p) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   } else {
     // this tile's scales (and zero points) as [group][output]
-    for (int i = threadIdx.x; i < gpr * TC_N; i += TC_EPI_WARPS * 32) {
-      const int g = i / TC_N, c = i % TC_N, n = n0 + c;
+    for (int i = threadIdx.x; i < gpr * TN; i += TC_EPI_WARPS * 32) {
+      const int g = i / TN, c = i % TN, n = n0 + c;
       const bool ok = n < p.w.rows;
       sm.scale[g][c] = ok ? half_bits_to_float(p.w.scale[(size_t)n * gpr + g]) : 0.0f;
       sm.zc[g][c] = ok ? p.w.zp[(size_t)n * gpr + g] : 0;
@@ -276,99 +332,130 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_a16_kernel(TcArgs p) {
   const unsigned tmem = sm.tmem;
 
   if (warp == TC_EPI_WARPS) {
-    if (lane == 0) {
-      const unsigned idesc_l = tc_idesc(0, ZC ? 0 : 1), idesc_h = tc_idesc(1, ZC ? 0 : 1);
+    // The whole warp runs the loop (waits included) and lane 0 issues the
+    // copies, MMAs and commits: tcgen05 issue from a converged warp.
+    const bool leader = lane == 0;
+    {
+      const unsigned idesc_l = tc_idesc(0, ZC ? 0 : 1, TN), idesc_h = tc_idesc(1, ZC ? 0 : 1, TN);
+      const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
+      const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TC_A_BYTES);
       const uint8_t *ga = p.a + (size_t)mt * p.nkb * TC_A_BYTES;
-      const uint8_t *gb = p.b + (size_t)nt * p.nkb * TC_B_BYTES;
+      const uint8_t *gb = p.b + (size_t)nt * p.nkb * BBYTES;
       int issued = 0, waited = 0, kstep = 0;
       auto issue = [&](int kb) {
         const int st = kb % TC_STAGES;
         const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
-        tc_mbar_expect_tx(bar, TC_STAGE_BYTES);
-        tc_bulk_g2s(dst, ga + (size_t)kb * TC_A_BYTES, TC_A_BYTES, bar);
-        tc_bulk_g2s(dst + TC_A_BYTES, gb + (size_t)kb * TC_B_BYTES, TC_B_BYTES, bar);
+        if (leader) {
+          tc_mbar_expect_tx(bar, TC_A_BYTES + BBYTES);
+          tc_bulk_g2s(dst, ga + (size_t)kb * TC_A_BYTES, TC_A_BYTES, bar);
+          tc_bulk_g2s(dst + TC_A_BYTES, gb + (size_t)kb * BBYTES, BBYTES, bar);
+        }
+        __syncwarp();
       };
       for (; issued < p.nkb && issued < TC_STAGES; issued++) issue(issued);
       bool ok = true;
       for (int seg = 0; seg < p.nseg && ok; seg++) {
-        const int buf = seg % TC_NBUF;
-        if (seg >= TC_NBUF)
-          ok = tc_wait(sm, tc_u32(&sm.accempty[buf]), ((seg / TC_NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+        const int buf = seg % NBUF;
+        if (seg >= NBUF) ok = tc_wait(sm, tc_u32(&sm.accempty[buf]), ((seg / NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+        ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        const unsigned dl = tmem + buf * 2 * TC_N, dh = dl + TC_N;
+        const unsigned dl = tmem + buf * 2 * TN, dh = dl + TN;
         for (int ks = 0; ks < p.seg_ks && ok; ks++, kstep++) {
           const int kb = kstep >> 2, j = kstep & 3, st = kb % TC_STAGES;
           if (j == 0) {
             ok = tc_wait(sm, tc_u32(&sm.full[st]), (kb / TC_STAGES) & 1, p.err, TC_ERR_FULL);
+            ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             waited = kb + 1;
             tc_fence_after();
           }
-          const unsigned sa = tc_u32(sm.stage[st]), sb = sa + TC_A_BYTES;
-          const unsigned long long db = tc_desc(sb + j * 2 * TC_N * 16, TC_N * 16, 128);
-          tc_mma(dl, tc_desc(sa + j * 2 * TC_M * 16, TC_M * 16, 128), db, idesc_l, ks > 0);
-          tc_mma(dh, tc_desc(sa + TC_A_PLANE + j * 2 * TC_M * 16, TC_M * 16, 128), db, idesc_h, ks > 0);
+          // descriptors: the stage-0, j-0 ones plus the start-address offset
+          const unsigned long long off = (unsigned long long)((st * TC_STAGE_BYTES) >> 4);
+          const unsigned long long db = desc_b0 + off + (unsigned long long)(2 * j);
+          const unsigned long long da = desc_a0 + off + (unsigned long long)(2 * j);
+          if (leader) {
+            tc_mma(dl, da, db, idesc_l, ks > 0);
+            tc_mma(dh, da + (TC_A_PLANE >> 4), db, idesc_h, ks > 0);
+          }
+          __syncwarp();
           if (j == 3) {
-            tc_commit(tc_u32(&sm.empty[st]));
+            if (leader) tc_commit(tc_u32(&sm.empty[st]));
+            __syncwarp();
             // refill the stage of the previous k block, whose MMAs were queued
             // ahead of these
             if (kb >= 1 && issued < p.nkb) {
               const int pkb = kb - 1;
               ok = tc_wait(sm, tc_u32(&sm.empty[pkb % TC_STAGES]), (pkb / TC_STAGES) & 1, p.err, TC_ERR_EMPTY);
+              ok = __all_sync(0xffffffffu, ok);
               if (!ok) break;
               issue(issued++);
             }
           }
         }
-        if (ok) tc_commit(tc_u32(&sm.accfull[buf]));
+        if (ok && leader) tc_commit(tc_u32(&sm.accfull[buf]));
+        __syncwarp();
       }
       if (!ok) {
         // drain: copies issued but not yet waited for, then every MMA issued
         for (int kb = waited; kb < issued; kb++)
           tc_drain_wait(tc_u32(&sm.full[kb % TC_STAGES]), (kb / TC_STAGES) & 1);
-        tc_commit(tc_u32(&sm.drain));
+        if (leader) tc_commit(tc_u32(&sm.drain));
+        __syncwarp();
         tc_drain_wait(tc_u32(&sm.drain), 0);
       }
     }
   } else {
-    const int q = warp & 3, hf = warp >> 2;
+    const int q = warp & 3, cg = warp >> 2;
     const int mrow = m0 + 32 * q + lane;
-    float accf[32];
+    const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * CW;
+    float accf[CW];
 #pragma unroll
-    for (int c = 0; c < 32; c++) accf[c] = 0.0f;
-    bool ok = true;
-    for (int seg = 0; seg < p.nseg; seg++) {
-      const int buf = seg % TC_NBUF;
-      ok = tc_wait(sm, tc_u32(&sm.accfull[buf]), (seg / TC_NBUF) & 1, p.err, TC_ERR_ACC);
-      ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads below are warp-wide
-      if (!ok) break;
+    for (int c = 0; c < CW; c++) accf[c] = 0.0f;
+    int la[CW], ha[CW], lb[CW], hb[CW];
+    // Waits for segment seg's accumulators and starts loading them.
+    auto start = [&](int seg, int (&l)[CW], int (&h)[CW]) -> bool {
+      const int buf = seg % NBUF;
+      bool ok = tc_wait(sm, tc_u32(&sm.accfull[buf]), (seg / NBUF) & 1, p.err, TC_ERR_ACC);
+      ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
+      if (!ok) return false;
       tc_fence_after();
-      const unsigned base = tmem + ((unsigned)(32 * q) << 16) + buf * 2 * TC_N + hf * 32;
-      int l[32], h[32];
-      tc_ld32(base, l);
-      tc_ld32(base + TC_N, h);
+      tc_ld(tbase + buf * 2 * TN, l);
+      tc_ld(tbase + buf * 2 * TN + TN, h);
+      return true;
+    };
+    // Completes the loads and hands the accumulator pair back to the MMAs.
+    auto finish = [&](int seg, int (&l)[CW], int (&h)[CW]) {
       tc_ld_wait();
+      tc_ld_done(l);
+      tc_ld_done(h);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[buf]));
+      if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[seg % NBUF]));
+    };
+    auto fold = [&](int seg, const int (&l)[CW], const int (&h)[CW]) {
       const int g = seg * p.seg / G;
-      const float *sc = &sm.scale[g][hf * 32];
-      const uint8_t *zc = &sm.zc[g][hf * 32];
       const unsigned xs = ZC ? (unsigned)p.xsum[(size_t)mrow * p.nseg + seg] : 0u;
-#pragma unroll
-      for (int c = 0; c < 32; c++) {
-        unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c];
-        if (ZC) a -= (unsigned)zc[c] * xs;
-        accf[c] = fmaf((float)(int)a, sc[c], accf[c]);
-      }
+      tc_fold<ZC, CW>(accf, l, h, &sm.scale[g][cg * CW], &sm.zc[g][cg * CW], xs);
+    };
+    bool ok = start(0, la, ha);
+    if (ok) finish(0, la, ha);
+    // two segments per trip: fold one while the next one's loads are in flight
+    for (int seg = 0; ok && seg < p.nseg; seg += 2) {
+      if (seg + 1 < p.nseg) ok = start(seg + 1, lb, hb);
+      fold(seg, la, ha);
+      if (!ok || seg + 1 >= p.nseg) break;
+      finish(seg + 1, lb, hb);
+      if (seg + 2 < p.nseg) ok = start(seg + 2, la, ha);
+      fold(seg + 1, lb, hb);
+      if (ok && seg + 2 < p.nseg) finish(seg + 2, la, ha);
     }
     if (ok && !*(volatile int *)&sm.abort && mrow < p.T) {
       const float sxm = p.sx[mrow];
-      const int nb = n0 + hf * 32;
+      const int nb = n0 + cg * CW;
       float *dst = p.out + (size_t)mrow * p.OUT + nb;
 #pragma unroll
-      for (int c = 0; c < 32; c++) {
+      for (int c = 0; c < CW; c++) {
         if (nb + c >= p.n_full) break;
         float r = accf[c] * sxm;
         if (p.epi & EPI_BIAS) r += p.bias[nb + c];

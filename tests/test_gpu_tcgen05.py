@@ -88,3 +88,35 @@ def test_tcgen05_epilogues_and_full_prompt(torch, ctx, fmt, epi):
 def test_tcgen05_tile_edges_match_cuda_core(torch, ctx, T):
     """Token counts at the 128-row tile edges, through the automatic choice."""
     run_case(torch, ctx, "int4-g32-a16", T, 768, 3072 + 17, "auto", T, "gelu")
+
+
+@pytest.mark.parametrize("npos0,T", [(0, 16), (0, 17), (0, 476), (300, 100), (1000, 24)])
+def test_quant8_prefill_attention_matches_one_query_kernel(torch, ctx, npos0, T):
+    """The several-token attention (queries staged in blocks of 16) against
+    the oracle's attend_float_one, bit for bit."""
+    from llm_mojo_b200.kernels import KVCache
+
+    NH, HS, CN, MAXT = 12, 64, 768, 1024
+    rng = np.random.default_rng(npos0 + 3 * T)
+    n = npos0 + T
+    qkv_all = (rng.standard_normal((n, 3 * CN)) * 2).astype(np.float32)
+    kv = KVCache(ctx, "int8", 1, MAXT, NH, HS)
+    oc = O.lib().oq_qkv8_new(1, MAXT, NH, HS)
+    try:
+        kv.store(0, 0, n, dev(torch, qkv_all))
+        for p in range(n):
+            row = qkv_all[p]
+            O.lib().oq_qkv8_store(oc, 0, p, O.ptr(np.ascontiguousarray(row[CN:2 * CN])),
+                                  O.ptr(np.ascontiguousarray(row[2 * CN:])))
+        q = np.ascontiguousarray(qkv_all[npos0:])
+        out = torch.zeros((T, CN), dtype=torch.float32, device="cuda")
+        kv.attend(out, dev(torch, q), 0, T, npos0)
+        want = np.zeros((T, CN), dtype=np.float32)
+        for t in range(T):
+            for h in range(NH):
+                O.lib().oq_qkv8_attend_one(oc, O.ptr(want), O.ptr(q), 0, t, h, npos0)
+        got = out.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"max diff {np.abs(got - want).max()}"
+    finally:
+        O.lib().oq_qkv8_free(oc)
+        kv.free()
