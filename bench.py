@@ -214,6 +214,150 @@ def run_prefill(args):
     return 0
 
 
+BATCH_SEQS, BATCH_PROMPT, BATCH_STEPS = 256, 128, 128
+
+
+def cpu_batched_baseline(seconds: float):
+    """The CPU oracle on config 3's first sequence: its 128-token prompt and
+    as many greedy tokens as fit in `seconds`; returns generated tok/s of a
+    whole sequence (prompt time + 128 x the mean decode-step time), the rate
+    of the reference, which decodes sequences one after another."""
+    from llm_mojo_b200 import synth
+    from oracle import oracle as O
+
+    t = synth.gpt2_random_init(0)
+    m = O.Model(t, max_t=BATCH_PROMPT + BATCH_STEPS)
+    prompt = synth.uniform_ids(BATCH_SEQS * BATCH_PROMPT, 3).reshape(BATCH_SEQS, BATCH_PROMPT)[0]
+    t0 = time.perf_counter()
+    logits = m.forward(prompt, 0)
+    t_prompt = time.perf_counter() - t0
+    n, pos, t1 = 0, BATCH_PROMPT, time.perf_counter()
+    while n < BATCH_STEPS - 1 and (n == 0 or time.perf_counter() - t1 < seconds):
+        nxt = int(O.lib().oq_argmax(O.ptr(logits), m.V))
+        logits = m.forward([nxt], pos)
+        pos += 1
+        n += 1
+    t_step = (time.perf_counter() - t1) / n
+    m.close()
+    per_seq = t_prompt + (BATCH_STEPS - 1) * t_step
+    threads = int(O.lib().oq_threads())
+    return {"value": BATCH_STEPS / per_seq, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"sequence 0 of config 3: its prompt forward ({t_prompt:.2f} s) and {n} decode steps "
+                      f"({t_step * 1000:.1f} ms each), extrapolated to its 128 tokens; sequences run one after "
+                      f"another; {threads}-thread team"}
+
+
+def run_batched(args):
+    """Config 3: 256 independent sequences, each a 128-token prompt ~ U[0, V)
+    (seed 3) then 128 greedy tokens, int4-g32-a16 + int8 head + int8 KV.
+    Sequences are split evenly across the ranks (strong scaling); after its
+    generation every rank joins one NCCL all-gather of the ids. value: all
+    ranks' generated tokens / the max over ranks of the device time of one
+    whole generation (prompts and ids in HBM, the gather included)."""
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from llm_mojo_b200 import build, synth
+    from llm_mojo_b200.model import Batch, Model
+    from llm_mojo_b200.tensor import Context
+
+    from llm_mojo_b200.shard import gather_blocks, shard_range
+
+    build.build()
+    b_lo, b_hi = shard_range(BATCH_SEQS, world, rank)
+    per = b_hi - b_lo
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    model = Model(ctx, synth.gpt2_random_init(0), max_t=BATCH_PROMPT + BATCH_STEPS)
+    batch = Batch(model, per, BATCH_PROMPT)
+    prompts = synth.uniform_ids(BATCH_SEQS * BATCH_PROMPT, 3).reshape(BATCH_SEQS, BATCH_PROMPT)
+    mine = np.ascontiguousarray(prompts[b_lo:b_hi])
+    prompts_dev = torch.from_numpy(mine).cuda()
+    ids_dev = torch.zeros((per, BATCH_STEPS), dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def gather():
+        return gather_blocks(ids_dev, world)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup + args.steps):
+            flush.zero_()
+            barrier()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            batch.generate_async(prompts_dev, BATCH_STEPS, ids_dev)
+            gather()
+            e0.record(stream)
+            barrier()
+            if i >= args.warmup:
+                times.append(s0.elapsed_time(e0))
+    ms = torch.tensor([statistics.mean(times)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    # e2e: host prompts and host ids through llmq_batch_generate, then the gather
+    e2e = []
+    for i in range(2):
+        barrier()
+        t0 = time.perf_counter()
+        ids = batch.generate(mine, BATCH_STEPS)
+        ids_dev.copy_(torch.from_numpy(ids))
+        host_ids = gather().cpu()
+        barrier()
+        e2e.append(time.perf_counter() - t0)
+    e2e_s = torch.tensor([min(e2e)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_s.item())
+    total = BATCH_SEQS * BATCH_STEPS
+    if rank == 0:
+        check_ids = host_ids.reshape(BATCH_SEQS, BATCH_STEPS).numpy()
+        single = model.generate(list(prompts[BATCH_SEQS - 1]), BATCH_STEPS)
+        cpu = None if args.no_cpu_baseline else cpu_batched_baseline(min(args.cpu_seconds, 15.0))
+        line = {"metric": "int4-g32-a16 batched decode tok/s (b=256/box)", "value": total / (ms / 1000.0),
+                "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int16xint4->int32",
+                "data": "synthetic",
+                "config": {"workload": "config 3: 256 sequences x (128-token prompt ~ U[0, 50257) seed 3 + 128 "
+                                       "greedy tokens), GPT-2 124M int4-g32-a16 + int8-ch head + int8 KV, "
+                                       "random-init weights (seed 0)",
+                           "global_batch": BATCH_SEQS, "seq_len": BATCH_PROMPT + BATCH_STEPS,
+                           "parallelism": f"sequences split over {world} ranks, one NCCL all-gather of the ids",
+                           "l2": "flushed between steps (256 MiB write)"},
+                "e2e": {"value": total / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": per * BATCH_PROMPT * 4,
+                        "d2h_bytes_per_step": BATCH_SEQS * BATCH_STEPS * 4},
+                "last_sequence_matches_single_decode": bool(list(check_ids[-1]) == list(single)),
+                # per generation: the prompt (embed, 12 x (2 LayerNorm + 4 x (split + GEMM) + store +
+                # attention), gather, head quantize + GEMV, argmax, state) and 127 decode-step graphs
+                # (advance, embed, 12 x (4 x (quantize + GEMV) + attention), head quantize + GEMV, argmax)
+                "gpu_launches": args.steps * ((1 + 12 * 12 + 1 + 2 + 1 + 1) + (BATCH_STEPS - 1) * (2 + 12 * 9 + 3)),
+                "cpu_baseline": cpu}
+        print(json.dumps(line))
+    batch.free()
+    model.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
 def run_sweep(args):
     """Config 1: x ~ N(0,1) (seed 1), W ~ N(0, 0.02) quantized per format;
     GB/s of packed weight bytes per one-token GEMV, L2 flushed before each
@@ -307,9 +451,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "sweep", "prefill"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "sweep", "prefill", "batched"],
                     help="decode: config 0 (the default bench line); sweep: config 1, the one-token GEMV of every "
-                         "format at every shape, one JSON line each; prefill: config 2, one line per format")
+                         "format at every shape, one JSON line each; prefill: config 2, one line per format; "
+                         "batched: config 3, sequences split over the ranks")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
@@ -320,6 +465,8 @@ def main():
         return run_sweep(args)
     if args.workload == "prefill":
         return run_prefill(args)
+    if args.workload == "batched":
+        return run_batched(args)
 
     import torch
     import torch.distributed as dist

@@ -223,6 +223,27 @@ void *llmq_stream(const llmq_ctx *ctx);
 llmq_status llmq_model_set_mode(llmq_model *m, int mode);
 int llmq_model_mode(const llmq_model *m);
 
+/* ---- batched greedy decode (independent sequences) ----------------------- */
+/* No counterpart in the reference, which decodes one sequence at a time
+ * (generate, gpt2t.mojo:942-980). State for the greedy decode of up to
+ * max_seqs independent sequences with prompts of up to max_prompt tokens,
+ * each with its own QuantKV[8] cache of the model's max_t positions. The
+ * model must use the QuantKV[8] cache. */
+typedef struct llmq_batch llmq_batch;
+llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int max_prompt, llmq_batch **out);
+llmq_status llmq_batch_free(llmq_batch *b);
+/* generate (gpt2t.mojo:942-980, without the stop at EOT) for B sequences at
+ * once: prompts [B][n_prompt] and out_ids [B][steps] on the host. Each
+ * sequence's ids are those of llmq_generate on that sequence alone: its
+ * prompt runs through the several-token path, its later tokens through the
+ * one-token arithmetic. */
+llmq_status llmq_batch_generate(llmq_ctx *ctx, llmq_batch *b, const int *prompts, int B, int n_prompt, int steps,
+                                int *out_ids);
+/* The same with device prompts and device ids, enqueued on the context's
+ * stream without synchronising (for timing with inputs already in HBM). */
+llmq_status llmq_batch_generate_async(llmq_ctx *ctx, llmq_batch *b, const int *prompts_dev, int B, int n_prompt,
+                                      int steps, int *ids_dev);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,10 @@ SIGNATURES = {
     "llmq_head_argmax": (I, [P, P, P, P, P]),
     "llmq_head_argmax_noalloc": (I, [P, P, P, P, P]),
     "llmq_set_prefill_kernel": (I, [P, I]),
+    "llmq_batch_create": (I, [P, P, I, I, P]),
+    "llmq_batch_free": (I, [P]),
+    "llmq_batch_generate": (I, [P, P, P, I, I, I, P]),
+    "llmq_batch_generate_async": (I, [P, P, P, I, I, I, P]),
     "llmq_layernorm": (I, [P, P, P, P, P, I, I]),
     "llmq_quantize_rows": (I, [P, P, I, I, P, P]),
     "llmq_debug_lane_sums": (I, [P, P, P, P]),

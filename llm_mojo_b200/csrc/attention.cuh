@@ -20,6 +20,17 @@ struct KV8View {
   int8_t *k, *v;
   float *ks, *vs;
   int n_layer, max_t, n_head, head_dim;
+  size_t seq;  // codes per sequence when the view holds several caches (blockIdx.z), else 0
+
+  // The view of sequence b's cache.
+  __device__ KV8View of(int b) const {
+    KV8View c = *this;
+    c.k += b * seq;
+    c.v += b * seq;
+    c.ks += b * (seq / head_dim);
+    c.vs += b * (seq / head_dim);
+    return c;
+  }
 };
 
 // QuantKV.quantize (kvcache.mojo:319-331) of one head's 64 values by one
@@ -40,10 +51,14 @@ __device__ __forceinline__ float quant_i8_head(float x, bool active, float *red,
 }
 
 // Stores the keys and values of T tokens at positions pos0.. of `layer`
-// (QuantKV.store, kvcache.mojo:333-342). grid (n_head, T, 2), block >= 64.
-__global__ void kv8_store_kernel(KV8View c, const float *qkv, int layer, int pos0, const int *pos_dev) {
+// (QuantKV.store, kvcache.mojo:333-342). grid (n_head, T, 2 * sequences),
+// block >= 64; sequence b's rows of qkv follow sequence b-1's T rows.
+__global__ void kv8_store_kernel(KV8View c0, const float *qkv, int layer, int pos0, const int *pos_dev) {
   __shared__ float red[32];
-  int h = blockIdx.x, t = blockIdx.y, which = blockIdx.z;  // 0 = key, 1 = value
+  int h = blockIdx.x, t = blockIdx.y, which = blockIdx.z & 1;  // 0 = key, 1 = value
+  const int sb = blockIdx.z >> 1;
+  const KV8View c = c0.of(sb);
+  qkv += (size_t)sb * gridDim.y * 3 * c.n_head * c.head_dim;
   int pos = (pos_dev ? *pos_dev : pos0) + t;
   int HS = c.head_dim, C = c.n_head * HS;
   int d = threadIdx.x;
@@ -58,13 +73,16 @@ __global__ void kv8_store_kernel(KV8View c, const float *qkv, int layer, int pos
 // attend_float_one for token t (position pos0 + t), head h. grid (n_head, T).
 // With store != 0 (decode, T == 1) the CTA first stores this token's key and
 // value for its head, which is all its own attention reads of this step.
-// Shared memory: 3 * max_t floats.
-__global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c, float *out, const float *qkv, int layer,
+// Shared memory: kv8_attend_smem(max_t, head_dim).
+__global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out, const float *qkv, int layer,
                                                          int pos0, const int *pos_dev, int store) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float red[40];
   const int h = blockIdx.x, t = blockIdx.y;
+  const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with gridDim.y rows
   const int HS = c.head_dim, C = c.n_head * HS;
+  qkv += (size_t)blockIdx.z * gridDim.y * 3 * C;
+  out += (size_t)blockIdx.z * gridDim.y * C;
   const int P0 = pos_dev ? *pos_dev : pos0;
   const int npos = P0 + t + 1;
   const float *q = qkv + (size_t)t * 3 * C + h * HS;
@@ -130,24 +148,38 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c, float *out, 
     float p = sc[s] / total;
     ps[s] = p * c.vs[sl];
   }
+  // the values of this head, staged with 16-byte loads: [npos][HS] codes
+  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * c.max_t + HS) + 15) & ~(uintptr_t)15);
+  {
+    const int cpr = HS / 16;
+    const int8_t *vb = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
+    for (int i = threadIdx.x; i < npos * cpr; i += blockDim.x) {
+      const int s = i / cpr, ch = i % cpr;
+      *(int4 *)(vst + (size_t)s * HS + ch * 16) = *(const int4 *)(vb + (size_t)s * c.n_head * HS + ch * 16);
+    }
+  }
   __syncthreads();
   // acc[d] = fma(p * vs, v[s][d], acc[d]) over positions in order.
   for (int d = threadIdx.x; d < HS; d += blockDim.x) {
     float acc = 0.0f;
-    const int8_t *vp = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS + d;
-    const size_t stride = (size_t)c.n_head * HS;
+    const int8_t *vp = vst + d;
     int s = 0;
     for (; s + 4 <= npos; s += 4) {
-      float v0 = (float)vp[(size_t)s * stride], v1 = (float)vp[(size_t)(s + 1) * stride];
-      float v2 = (float)vp[(size_t)(s + 2) * stride], v3 = (float)vp[(size_t)(s + 3) * stride];
+      float v0 = (float)vp[(size_t)s * HS], v1 = (float)vp[(size_t)(s + 1) * HS];
+      float v2 = (float)vp[(size_t)(s + 2) * HS], v3 = (float)vp[(size_t)(s + 3) * HS];
       acc = fmaf(ps[s], v0, acc);
       acc = fmaf(ps[s + 1], v1, acc);
       acc = fmaf(ps[s + 2], v2, acc);
       acc = fmaf(ps[s + 3], v3, acc);
     }
-    for (; s < npos; s++) acc = fmaf(ps[s], (float)vp[(size_t)s * stride], acc);
+    for (; s < npos; s++) acc = fmaf(ps[s], (float)vp[(size_t)s * HS], acc);
     out[(size_t)t * C + h * HS + d] = acc;
   }
+}
+
+// Dynamic shared memory of kv8_attend_kernel for a cache of max_t positions.
+__host__ __device__ inline size_t kv8_attend_smem(int max_t, int HS) {
+  return (size_t)(2 * max_t + HS) * 4 + 16 + (size_t)max_t * HS;
 }
 
 // attend_float_one for QB consecutive query tokens of one head at once (the
@@ -167,12 +199,15 @@ __host__ __device__ inline size_t kv8_prefill_smem(int P, int HS) {
   return (size_t)KV_TILE * (HS + 1) * 4 + KV_TILE * 4 + (size_t)KV_QB * HS * 4 + (size_t)KV_QB * P * 4 + KV_QB * 4;
 }
 
-__global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c, float *out, const float *qkv, int layer, int pos0,
+__global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c0, float *out, const float *qkv, int layer, int pos0,
                                                           int T) {
   extern __shared__ __align__(16) float kvp_sm[];
   const int h = blockIdx.x, t0 = blockIdx.y * KV_QB;
   const int nq = min(KV_QB, T - t0);
+  const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with T rows
   const int HS = c.head_dim, C = c.n_head * HS, HP = HS + 1;
+  qkv += (size_t)blockIdx.z * T * 3 * C;
+  out += (size_t)blockIdx.z * T * C;
   const int P = pos0 + t0 + nq;  // positions the last query of the block sees
   float *tile = kvp_sm;                        // [128][HS + 1]
   float *tsc = tile + KV_TILE * HP;            // [128]

@@ -8,6 +8,7 @@
 
 #include "../../include/llmq.h"
 #include "attention.cuh"
+#include "batch.cuh"
 #include "gemv_a16.cuh"
 #include "gemv_float.cuh"
 #include "mega.cuh"
@@ -118,6 +119,7 @@ llmq_status fail(llmq_ctx *ctx, llmq_status st, const std::string &msg) {
   } while (0)
 
 constexpr int kMaxPrefillSmem = 225 * 1024;  // the several-token attention's staging limit
+constexpr int kBgemvSmem = 200 * 1024;       // the batched GEMV's shared memory limit
 constexpr int kR = 16, kP = 3;
 constexpr int kThreads = kR * kP * 4;
 
@@ -233,6 +235,9 @@ cudaError_t configure_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)kv8_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              kMaxPrefillSmem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)kv8_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kv8_attend_smem(1024, 128));
   auto tcs = [&](const void *k) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TcSmem) + 1024);
@@ -896,7 +901,7 @@ llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *
     kv8_prefill_kernel<<<dim3(kv->n_head, (T + KV_QB - 1) / KV_QB), 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer,
                                                                                             pos0, T);
   } else if (kv->kind == LLMQ_KV_QUANT8) {
-    size_t sm = (size_t)(2 * kv->max_t + kv->head_dim) * 4;
+    size_t sm = kv8_attend_smem(kv->max_t, kv->head_dim);
     kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
   } else {
     ia_attend_kernel<<<grid, 256, ia_attend_smem(kv), ctx->stream>>>(kv->ia, out, qkv, layer, pos0, nullptr, 0,
@@ -1092,7 +1097,7 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
   const int C = m->C;
   embed_kernel<<<3, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->state);
   CKL();
-  size_t att_sm = (size_t)(2 * m->max_t + C / m->n_head) * 4;
+  size_t att_sm = kv8_attend_smem(m->max_t, C / m->n_head);
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
     GemvArgs a{};
@@ -1455,3 +1460,349 @@ llmq_status llmq_model_check(llmq_ctx *ctx, llmq_model *m) {
 }
 
 }  // extern "C"
+
+// ---- batched greedy decode of independent sequences ----------------------
+
+struct llmq_batch {
+  float *part_val = nullptr;  // [max_seqs][head row tiles] argmax partials
+  int *part_idx = nullptr;
+  llmq_ctx *ctx;
+  llmq_model *m;
+  int max_seqs, max_prompt;
+  KV8View kv{};            // [max_seqs] QuantKV[8] caches of m->max_t positions
+  float *x = nullptr, *xn = nullptr, *qkv = nullptr, *att = nullptr, *fc = nullptr;  // [max_seqs * max_prompt] rows
+  float *logits = nullptr; // [max_seqs][V]
+  int16_t *xq = nullptr;   // [max_seqs][3072]
+  float *xsf = nullptr;    // [max_seqs][3072 / 16]
+  int *xsi = nullptr;      // [max_seqs][units * 16] (units of the widest matrix)
+  float *sx = nullptr;     // [max_seqs]
+  int *tokens = nullptr;   // [max_seqs * max_prompt]
+  int *ids = nullptr;      // [max_seqs][max_t]
+  int *state = nullptr;    // [0] position, [1] step
+  int *ids_host = nullptr; // pinned [max_seqs][max_t]
+  int *prompt_host = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  int graph_B = 0, graph_steps = 0;
+};
+
+namespace {
+
+int fmt_code(const llmq_weight *w) { return fmt_of(w->view()); }
+
+// bquant + bgemv for B rows: out[B][rows] (+)= act(quantize(ln?(x)) . w).
+llmq_status batch_linear(llmq_batch *bt, const llmq_weight *w, const float *x, const float *ln_w, const float *ln_b,
+                         const float *bias, float *out, int B, int epi, cudaStream_t s) {
+  llmq_ctx *ctx = bt->ctx;
+  const WeightView v = w->view();
+  const int fmt = fmt_code(w), K = v.cols;
+  BQuantArgs q{x, ln_w, ln_b, bt->xq, bt->xsf, bt->xsi, bt->sx, v};
+  const size_t qsm = SmemPlan<FMT_BLK4>(K, v.group, 0).total > SmemPlan<FMT_GEN8>(K, v.group, 0).total
+                         ? SmemPlan<FMT_BLK4>(K, v.group, 0).total
+                         : SmemPlan<FMT_GEN8>(K, v.group, 0).total;
+  const bool ln = ln_w != nullptr;
+#define BQ(F)                                                                   \
+  if (fmt == F) {                                                               \
+    if (ln)                                                                     \
+      bquant_kernel<F, PRO_LN><<<B, 256, qsm, s>>>(q);                          \
+    else                                                                        \
+      bquant_kernel<F, PRO_QUANT><<<B, 256, qsm, s>>>(q);                       \
+  }
+  BQ(FMT_BLK4) else BQ(FMT_GEN4) else BQ(FMT_GEN8)
+#undef BQ
+  CKL();
+  // out == nullptr: the greedy head, whose argmax partials replace the logits
+  BGemvArgs g{v, bt->xq, bt->xsf, bt->xsi, bt->sx, bias, out, B, epi, out ? nullptr : bt->part_val,
+              out ? nullptr : bt->part_idx, ctx->tc_err};
+  const int gx = (v.rows + BG_ROWS - 1) / BG_ROWS;
+  // 8 sequences per CTA (registers and shared memory for 2-3 CTAs per SM);
+  // the weight rows staged in shared memory where they fit beside the
+  // activations
+  const int sb = 8;
+  const bool stage = bgemv_smem(fmt, K, v.group, sb, true) <= (size_t)kBgemvSmem;
+  const size_t sm = bgemv_smem(fmt, K, v.group, sb, stage);
+  const dim3 grid(gx, (B + sb - 1) / sb);
+#define BG(F, SB, ST) bgemv_a16_kernel<F, SB, ST><<<grid, 256, sm, s>>>(g)
+#define BG2(F)                       \
+  if (sb == 16 && stage) BG(F, 16, true); \
+  else if (sb == 16) BG(F, 16, false);    \
+  else if (stage) BG(F, 8, true);         \
+  else BG(F, 8, false);
+  if (fmt == FMT_BLK4) {
+    BG2(FMT_BLK4)
+  } else if (fmt == FMT_GEN4) {
+    BG2(FMT_GEN4)
+  } else {
+    BG2(FMT_GEN8)
+  }
+#undef BG2
+#undef BG
+  CKL();
+  return LLMQ_OK;
+}
+
+// One decode step of B sequences at position state[0], writing ids[b][state[1]]
+// and advancing both.
+__global__ void batch_advance_kernel(int *state) {
+  state[0] += 1;
+  state[1] += 1;
+}
+
+llmq_status batch_decode_step(llmq_batch *bt, int B, cudaStream_t s) {
+  llmq_model *m = bt->m;
+  llmq_ctx *ctx = bt->ctx;
+  const int C = m->C;
+  embed_batch_kernel<<<B, 256, 0, s>>>(m->head->view(), m->wpe(), bt->x, bt->tokens, bt->state);
+  CKL();
+  const size_t att_sm = kv8_attend_smem(m->max_t, C / m->n_head);
+  llmq_status st;
+  for (int l = 0; l < m->n_layer; l++) {
+    const llmq_weight *const *w = &m->mats[4 * l];
+    if ((st = batch_linear(bt, w[0], bt->x, m->vec(l, 0), m->vec(l, 1), m->vec(l, 2), bt->qkv, B, EPI_BIAS, s)))
+      return st;
+    kv8_attend_kernel<<<dim3(m->n_head, 1, B), 128, att_sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, bt->state, 1);
+    CKL();
+    if ((st = batch_linear(bt, w[1], bt->att, nullptr, nullptr, m->vec(l, 3), bt->x, B, EPI_BIAS | EPI_RESID, s)))
+      return st;
+    if ((st = batch_linear(bt, w[2], bt->x, m->vec(l, 4), m->vec(l, 5), m->vec(l, 6), bt->fc, B, EPI_BIAS | EPI_GELU, s)))
+      return st;
+    if ((st = batch_linear(bt, w[3], bt->fc, nullptr, nullptr, m->vec(l, 7), bt->x, B, EPI_BIAS | EPI_RESID, s)))
+      return st;
+  }
+  if ((st = batch_linear(bt, m->head, bt->x, m->lnf_w(), m->lnf_b(), nullptr, nullptr, B, 0, s))) return st;
+  return LLMQ_OK;
+}
+
+__global__ void embed_prompts_kernel(WeightView head, const float *wpe, float *x, const int *tokens, int P) {
+  const int r = blockIdx.x, C = head.cols, gpr = head.cols / head.group;
+  const int token = min(max(tokens[r], 0), head.rows - 1), p = r % P;  // ids were checked on the host
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const size_t gi = (size_t)token * gpr + i / head.group;
+    const float sc = half_bits_to_float(head.scale[gi]);
+    const float v = (float)(code_at(head, token, i) - (int)head.zp[gi]) * sc;
+    x[(size_t)r * C + i] = v + wpe[(size_t)p * C + i];
+  }
+}
+
+__global__ void gather_last_rows_kernel(const float *x, float *dst, int P, int C) {
+  const int b = blockIdx.x;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) dst[(size_t)b * C + i] = x[((size_t)b * P + P - 1) * C + i];
+}
+
+__global__ void batch_init_state_kernel(int *state, int pos, int step) {
+  state[0] = pos;
+  state[1] = step;
+}
+
+// The prompts of B sequences (P tokens each, ids in bt->tokens), all rows at
+// once through the several-token path; the last row of each through the
+// one-token head; ids[b][0] and tokens[b] from its argmax.
+llmq_status batch_prompt(llmq_batch *bt, int B, int P, cudaStream_t s) {
+  llmq_model *m = bt->m;
+  llmq_ctx *ctx = bt->ctx;
+  const int C = m->C, T = B * P;
+  embed_prompts_kernel<<<T, 256, 0, s>>>(m->head->view(), m->wpe(), bt->x, bt->tokens, P);
+  CKL();
+  llmq_status st;
+  for (int l = 0; l < m->n_layer; l++) {
+    const llmq_weight *const *w = &m->mats[4 * l];
+    layernorm_kernel<<<T, 256, C * 4, s>>>(bt->xn, bt->x, m->vec(l, 0), m->vec(l, 1), C);
+    CKL();
+    if ((st = llmq_linear(ctx, w[0], bt->xn, m->vec(l, 2), bt->qkv, T, C, 3 * C, LLMQ_BIAS)) != LLMQ_OK) return st;
+    kv8_store_kernel<<<dim3(m->n_head, P, 2 * B), 128, 0, s>>>(bt->kv, bt->qkv, l, 0, nullptr);
+    CKL();
+    const size_t sm = kv8_prefill_smem(P, C / m->n_head);
+    kv8_prefill_kernel<<<dim3(m->n_head, (P + KV_QB - 1) / KV_QB, B), 256, sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, P);
+    CKL();
+    if ((st = llmq_linear(ctx, w[1], bt->att, m->vec(l, 3), bt->x, T, C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK)
+      return st;
+    layernorm_kernel<<<T, 256, C * 4, s>>>(bt->xn, bt->x, m->vec(l, 4), m->vec(l, 5), C);
+    CKL();
+    if ((st = llmq_linear(ctx, w[2], bt->xn, m->vec(l, 6), bt->fc, T, C, 4 * C, LLMQ_BIAS | LLMQ_GELU)) != LLMQ_OK)
+      return st;
+    if ((st = llmq_linear(ctx, w[3], bt->fc, m->vec(l, 7), bt->x, T, 4 * C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK)
+      return st;
+  }
+  gather_last_rows_kernel<<<B, 256, 0, s>>>(bt->x, bt->xn, P, C);
+  CKL();
+  if ((st = batch_linear(bt, m->head, bt->xn, m->lnf_w(), m->lnf_b(), nullptr, nullptr, B, 0, s))) return st;
+  return LLMQ_OK;
+}
+
+// generate for B sequences whose prompts are in bt->tokens ([B][P]): ids
+// into bt->ids ([B][max_t], columns 0..steps-1), and also into ids_dev
+// ([B][steps]) when given.
+llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
+  llmq_ctx *ctx = bt->ctx;
+  llmq_model *m = bt->m;
+  cudaStream_t s = ctx->stream;
+  llmq_status st = batch_prompt(bt, B, P, s);
+  if (st != LLMQ_OK) return st;
+  ctx->tc_used = true;  // the GEMVs' copy waits report through the same flag
+  // decode step i (1..steps-1) embeds the token of column i-1 at position P+i-1
+  batch_init_state_kernel<<<1, 1, 0, s>>>(bt->state, P - 1, 0);
+  CKL();
+  const int nparts = (m->V + BG_ROWS - 1) / BG_ROWS;
+  argmax_parts_kernel<<<B, 256, 0, s>>>(bt->part_val, bt->part_idx, nparts, bt->ids, m->max_t, bt->tokens, nullptr);
+  CKL();
+  if (steps > 1) {
+    // decode steps as one CUDA graph, captured for this batch size
+    if (!bt->exec || bt->graph_B != B) {
+      if (bt->exec) cudaGraphExecDestroy(bt->exec);
+      if (bt->graph) cudaGraphDestroy(bt->graph);
+      bt->exec = nullptr;
+      bt->graph = nullptr;
+      CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+      batch_advance_kernel<<<1, 1, 0, s>>>(bt->state);
+      llmq_status cst = batch_decode_step(bt, B, s);
+      if (cst == LLMQ_OK)
+        argmax_parts_kernel<<<B, 256, 0, s>>>(bt->part_val, bt->part_idx, nparts, bt->ids, m->max_t, bt->tokens,
+                                              bt->state + 1);
+      cudaGraph_t g = nullptr;
+      cudaError_t e = cudaStreamEndCapture(s, &g);
+      if (cst != LLMQ_OK) {
+        if (g) cudaGraphDestroy(g);
+        return cst;
+      }
+      CK(e);
+      bt->graph = g;
+      CK(cudaGraphInstantiate(&bt->exec, g, 0));
+      bt->graph_B = B;
+    }
+    for (int i = 1; i < steps; i++) CK(cudaGraphLaunch(bt->exec, s));
+  }
+  if (ids_dev)
+    CK(cudaMemcpy2DAsync(ids_dev, (size_t)steps * 4, bt->ids, (size_t)m->max_t * 4, (size_t)steps * 4, B,
+                         cudaMemcpyDeviceToDevice, s));
+  return LLMQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int max_prompt, llmq_batch **out) {
+  if (!ctx || !m || !out || max_seqs <= 0 || max_prompt <= 0 || max_prompt > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad batch arguments");
+  if (m->kv->kind != LLMQ_KV_QUANT8) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "batched decode takes the QuantKV[8] cache");
+  *out = nullptr;
+  CK(cudaSetDevice(ctx->device));
+  llmq_batch *bt = new llmq_batch();
+  bt->ctx = ctx;
+  bt->m = m;
+  bt->max_seqs = max_seqs;
+  bt->max_prompt = max_prompt;
+  const int C = m->C, HS = C / m->n_head;
+  const size_t seq = (size_t)m->n_layer * m->max_t * m->n_head * HS, rows = (size_t)max_seqs * max_prompt;
+  KV8View &v = bt->kv;
+  v.n_layer = m->n_layer;
+  v.max_t = m->max_t;
+  v.n_head = m->n_head;
+  v.head_dim = HS;
+  v.seq = seq;
+  int maxu = 0;
+  for (const llmq_weight *w : m->mats) maxu = std::max(maxu, w->cols / w->group);
+  maxu = std::max(maxu, m->head->cols / m->head->group);
+  cudaError_t e = cudaMalloc(&v.k, seq * max_seqs);
+  if (e == cudaSuccess) e = cudaMalloc(&v.v, seq * max_seqs);
+  if (e == cudaSuccess) e = cudaMalloc(&v.ks, seq / HS * max_seqs * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&v.vs, seq / HS * max_seqs * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->x, rows * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->xn, rows * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->qkv, rows * 3 * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->att, rows * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->fc, rows * 4 * C * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->logits, (size_t)max_seqs * m->V * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->xq, (size_t)max_seqs * 4 * C * 2);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->xsf, (size_t)max_seqs * 4 * C / 16 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->xsi, (size_t)max_seqs * maxu * 16 * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->sx, (size_t)max_seqs * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->tokens, rows * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->ids, (size_t)max_seqs * m->max_t * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->state, 2 * sizeof(int));
+  const size_t nparts = (size_t)(m->V + BG_ROWS - 1) / BG_ROWS;
+  if (e == cudaSuccess) e = cudaMalloc(&bt->part_val, (size_t)max_seqs * nparts * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&bt->part_idx, (size_t)max_seqs * nparts * 4);
+  if (e == cudaSuccess) e = cudaMemset(v.k, 0, seq * max_seqs);
+  if (e == cudaSuccess) e = cudaMemset(v.v, 0, seq * max_seqs);
+  if (e == cudaSuccess) e = cudaMemset(v.ks, 0, seq / HS * max_seqs * 4);
+  if (e == cudaSuccess) e = cudaMemset(v.vs, 0, seq / HS * max_seqs * 4);
+  if (e == cudaSuccess) e = cudaMallocHost(&bt->ids_host, (size_t)max_seqs * m->max_t * 4);
+  if (e == cudaSuccess) e = cudaMallocHost(&bt->prompt_host, rows * 4);
+  if (e != cudaSuccess) {
+    llmq_batch_free(bt);
+    return fail(ctx, LLMQ_ERR_NOMEM, std::string("batch alloc: ") + cudaGetErrorString(e));
+  }
+  // the bgemv and several-token attention kernels' shared memory
+  auto attr = [&](const void *k, size_t n) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)n);
+  };
+#define BA(F)                                                           \
+  attr((const void *)bgemv_a16_kernel<F, 16, true>, kBgemvSmem);        \
+  attr((const void *)bgemv_a16_kernel<F, 16, false>, kBgemvSmem);       \
+  attr((const void *)bgemv_a16_kernel<F, 8, true>, kBgemvSmem);         \
+  attr((const void *)bgemv_a16_kernel<F, 8, false>, kBgemvSmem);
+  BA(FMT_BLK4)
+  BA(FMT_GEN4)
+  BA(FMT_GEN8)
+#undef BA
+  if (e != cudaSuccess) {
+    int optin = 0;
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);
+    llmq_batch_free(bt);
+    return fail(ctx, LLMQ_ERR_CUDA, std::string("batch attributes: ") + cudaGetErrorString(e) +
+                                        " (shared memory per block up to " + std::to_string(optin) + ")");
+  }
+  *out = bt;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_batch_free(llmq_batch *bt) {
+  if (!bt) return LLMQ_ERR_INVALID;
+  cudaSetDevice(bt->ctx->device);
+  if (bt->exec) cudaGraphExecDestroy(bt->exec);
+  if (bt->graph) cudaGraphDestroy(bt->graph);
+  void *ps[] = {bt->kv.k, bt->kv.v, bt->kv.ks, bt->kv.vs, bt->x, bt->xn, bt->qkv, bt->att, bt->fc, bt->logits,
+                bt->xq, bt->xsf, bt->xsi, bt->sx, bt->tokens, bt->ids, bt->state, bt->part_val, bt->part_idx};
+  for (void *p : ps)
+    if (p) cudaFree(p);
+  if (bt->ids_host) cudaFreeHost(bt->ids_host);
+  if (bt->prompt_host) cudaFreeHost(bt->prompt_host);
+  delete bt;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_batch_generate_async(llmq_ctx *ctx, llmq_batch *bt, const int *prompts_dev, int B, int n_prompt,
+                                      int steps, int *ids_dev) {
+  if (!ctx || !bt || !prompts_dev || !ids_dev || B <= 0 || B > bt->max_seqs || n_prompt <= 0 ||
+      n_prompt > bt->max_prompt || steps <= 0 || n_prompt + steps - 1 > bt->m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad batch size, prompt length or steps");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaMemcpyAsync(bt->tokens, prompts_dev, (size_t)B * n_prompt * 4, cudaMemcpyDeviceToDevice, ctx->stream));
+  return batch_run(bt, B, n_prompt, steps, ids_dev);
+}
+
+llmq_status llmq_batch_generate(llmq_ctx *ctx, llmq_batch *bt, const int *prompts, int B, int n_prompt, int steps,
+                                int *out_ids) {
+  if (!ctx || !bt || !prompts || !out_ids || B <= 0 || B > bt->max_seqs || n_prompt <= 0 ||
+      n_prompt > bt->max_prompt || steps <= 0 || n_prompt + steps - 1 > bt->m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad batch size, prompt length or steps");
+  for (long i = 0; i < (long)B * n_prompt; i++)
+    if (prompts[i] < 0 || prompts[i] >= bt->m->V) return fail(ctx, LLMQ_ERR_INVALID, "token id out of range");
+  CK(cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->stream;
+  CK(cudaStreamSynchronize(s));
+  std::memcpy(bt->prompt_host, prompts, (size_t)B * n_prompt * 4);
+  CK(cudaMemcpyAsync(bt->tokens, bt->prompt_host, (size_t)B * n_prompt * 4, cudaMemcpyHostToDevice, s));
+  llmq_status st = batch_run(bt, B, n_prompt, steps, nullptr);
+  if (st != LLMQ_OK) return st;
+  CK(cudaMemcpy2DAsync(bt->ids_host, (size_t)steps * 4, bt->ids, (size_t)bt->m->max_t * 4, (size_t)steps * 4, B,
+                       cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if ((st = tc_check(ctx)) != LLMQ_OK) return st;
+  std::memcpy(out_ids, bt->ids_host, (size_t)B * steps * 4);
+  return LLMQ_OK;
+}
+
+}  // extern "C"
+

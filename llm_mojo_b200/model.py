@@ -107,3 +107,43 @@ class Model:
             self.free()
         except Exception:
             pass
+
+
+class Batch:
+    """Greedy decode of independent sequences together (no counterpart in
+    the reference, which decodes one at a time): up to max_seqs sequences
+    with prompts of up to max_prompt tokens, each with its own QuantKV[8]
+    cache. Each sequence's ids equal Model.generate on it alone."""
+
+    def __init__(self, model: Model, max_seqs: int, max_prompt: int):
+        self.model, self.max_seqs, self.max_prompt = model, max_seqs, max_prompt
+        h = C.c_void_p()
+        check(lib().llmq_batch_create(model.ctx.h, model.h, max_seqs, max_prompt, C.byref(h)), model.ctx.h)
+        self.h = h
+
+    def generate(self, prompts, steps: int) -> np.ndarray:
+        """prompts [B, P] token ids (host); returns ids [B, steps]."""
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        B, P = p.shape
+        out = np.zeros((B, steps), dtype=np.int32)
+        check(lib().llmq_batch_generate(self.model.ctx.h, self.h, p.ctypes.data_as(C.c_void_p), B, P, steps,
+                                        out.ctypes.data_as(C.c_void_p)), self.model.ctx.h)
+        return out
+
+    def generate_async(self, prompts_dev, steps: int, ids_dev):
+        """Device prompts (int32 CUDA tensor [B, P]) and ids ([B, steps]),
+        enqueued on the context's stream."""
+        B, P = prompts_dev.shape
+        check(lib().llmq_batch_generate_async(self.model.ctx.h, self.h, C.c_void_p(prompts_dev.data_ptr()), B, P,
+                                              steps, C.c_void_p(ids_dev.data_ptr())), self.model.ctx.h)
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().llmq_batch_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
