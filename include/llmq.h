@@ -40,6 +40,8 @@ typedef struct llmq_model llmq_model;
  * int_attention.mojo IntAttnKV (integer attention). */
 #define LLMQ_KV_QUANT8 1
 #define LLMQ_KV_INTATTN 2
+#define LLMQ_KV_F32 3  /* DenseKV[float32] (kvcache.mojo:153-246) */
+#define LLMQ_KV_BF16 4 /* DenseKV[bfloat16] */
 
 /* ---- context ------------------------------------------------------------ */
 /* No reference counterpart (the reference runs in-process on the CPU). */
@@ -148,7 +150,9 @@ llmq_status llmq_quantize_rows(llmq_ctx *ctx, const float *x_dev, int T, int IN,
 llmq_status llmq_debug_lane_sums(llmq_ctx *ctx, const llmq_weight *w, const float *x_dev, int32_t *lanes_dev);
 
 /* ---- KV cache (kvcache.mojo:31-87 KVCache) ------------------------------ */
-/* KVCache.create. kind LLMQ_KV_QUANT8 or LLMQ_KV_INTATTN. */
+/* KVCache.create. kind LLMQ_KV_QUANT8, LLMQ_KV_INTATTN, LLMQ_KV_F32 or
+ * LLMQ_KV_BF16 (the dense caches attend with the several-token kernel for
+ * every token count). */
 llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int n_head, int head_dim,
                            llmq_kv **out);
 llmq_status llmq_kv_free(llmq_kv *kv);
@@ -222,6 +226,16 @@ void *llmq_stream(const llmq_ctx *ctx);
 #define LLMQ_MODE_PERSISTENT 2
 llmq_status llmq_model_set_mode(llmq_model *m, int mode);
 int llmq_model_mode(const llmq_model *m);
+
+/* ---- perplexity harness ---------------------------------------------------- */
+/* Replaces score_rows (gpt2t.mojo:1042-1097) for rows [r0, r1) of a window's
+ * logits ([rows][V], device): stats_dev[k * stride + (r - r0)] in float64 for
+ * k = 0 NLL (-log p(target), log_sum_exp as gpt2t.mojo:1030-1039), 1 NLL
+ * under base_dev (the float32 model's logits; may be NULL), 2 top-1
+ * agreement, 3 KL(base || model) in nats, 4 max and 5 sum of |logit
+ * differences|. targets_dev[r] is row r's next token. */
+llmq_status llmq_score_rows(llmq_ctx *ctx, const float *logits_dev, const float *base_dev, const int *targets_dev, int V,
+                            int r0, int r1, double *stats_dev, int stride);
 
 /* ---- batched greedy decode (independent sequences) ----------------------- */
 /* No counterpart in the reference, which decodes one sequence at a time

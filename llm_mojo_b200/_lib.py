@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(HERE, "libllmq.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
 BIAS, GELU, RESID = 1, 2, 4
-KV_QUANT8, KV_INTATTN = 1, 2
+KV_QUANT8, KV_INTATTN, KV_F32, KV_BF16 = 1, 2, 3, 4
 MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT = 0, 1, 2
 PREFILL_AUTO, PREFILL_CUDA_CORE, PREFILL_TCGEN05 = 0, 1, 2
 
@@ -48,6 +48,7 @@ SIGNATURES = {
     "llmq_head_argmax_noalloc": (I, [P, P, P, P, P]),
     "llmq_set_prefill_kernel": (I, [P, I]),
     "llmq_batch_create": (I, [P, P, I, I, P]),
+    "llmq_score_rows": (I, [P, P, P, P, I, I, I, P, I]),
     "llmq_batch_free": (I, [P]),
     "llmq_batch_generate": (I, [P, P, P, I, I, I, P]),
     "llmq_batch_generate_async": (I, [P, P, P, I, I, I, P]),

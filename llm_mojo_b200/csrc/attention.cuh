@@ -70,6 +70,25 @@ __global__ void kv8_store_kernel(KV8View c0, const float *qkv, int layer, int po
   if (threadIdx.x == 0) (which == 0 ? c.ks : c.vs)[sl] = s;
 }
 
+// DenseKV.store (kvcache.mojo:204-208): the keys and values of T tokens at
+// positions pos0.. of `layer`, as float32 (KVT 1) or bfloat16 (KVT 2, round
+// to nearest even). grid (T), block 256.
+template <int KVT>
+__global__ void dkv_store_kernel(KV8View c, const float *qkv, int layer, int pos0) {
+  const int t = blockIdx.x, C = c.n_head * c.head_dim;
+  const size_t o = ((size_t)layer * c.max_t + pos0 + t) * C;
+  for (int i = threadIdx.x; i < C; i += blockDim.x) {
+    const float k = qkv[(size_t)t * 3 * C + C + i], v = qkv[(size_t)t * 3 * C + 2 * C + i];
+    if (KVT == 1) {
+      ((float *)c.k)[o + i] = k;
+      ((float *)c.v)[o + i] = v;
+    } else {
+      ((uint16_t *)c.k)[o + i] = __bfloat16_as_ushort(__float2bfloat16_rn(k));
+      ((uint16_t *)c.v)[o + i] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
+  }
+}
+
 // attend_float_one for token t (position pos0 + t), head h. grid (n_head, T).
 // With store != 0 (decode, T == 1) the CTA first stores this token's key and
 // value for its head, which is all its own attention reads of this step.
@@ -199,8 +218,12 @@ __host__ __device__ inline size_t kv8_prefill_smem(int P, int HS) {
   return (size_t)KV_TILE * (HS + 1) * 4 + KV_TILE * 4 + (size_t)KV_QB * HS * 4 + (size_t)KV_QB * P * 4 + KV_QB * 4;
 }
 
-__global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c0, float *out, const float *qkv, int layer, int pos0,
-                                                          int T) {
+// KVT: 0 QuantKV[8] (int8 codes and per-head scales), 1 DenseKV[float32],
+// 2 DenseKV[bfloat16] (kvcache.mojo:153-246: the values widened to float32,
+// no scales: score = tree * scale, p = e / total).
+template <int KVT>
+__global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out, const float *qkv, int layer, int pos0,
+                                                         int T) {
   extern __shared__ __align__(16) float kvp_sm[];
   const int h = blockIdx.x, t0 = blockIdx.y * KV_QB;
   const int nq = min(KV_QB, T - t0);
@@ -227,18 +250,32 @@ __global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c0, float *out
   // a tile of 128 positions of keys (which 0) or values (1) as floats, and
   // their scales
   auto stage = [&](int s0, int which) {
-    const int8_t *src = which == 0 ? kbase : vbase;
-    const float *scl = which == 0 ? c.ks : c.vs;
-    const int n = min(KV_TILE, P - s0), cpr = HS / 16;
-    for (int i = tid; i < n * cpr; i += blockDim.x) {
-      const int r = i / cpr, ch = i % cpr;
-      int4 raw = *(const int4 *)(src + (size_t)(s0 + r) * head_stride + ch * 16);
-      const int8_t *b = (const int8_t *)&raw;
-      float *dst = tile + r * HP + ch * 16;
+    const int n = min(KV_TILE, P - s0);
+    if (KVT == 0) {
+      const int8_t *src = which == 0 ? kbase : vbase;
+      const float *scl = which == 0 ? c.ks : c.vs;
+      const int cpr = HS / 16;
+      for (int i = tid; i < n * cpr; i += blockDim.x) {
+        const int r = i / cpr, ch = i % cpr;
+        int4 raw = *(const int4 *)(src + (size_t)(s0 + r) * head_stride + ch * 16);
+        const int8_t *b = (const int8_t *)&raw;
+        float *dst = tile + r * HP + ch * 16;
 #pragma unroll
-      for (int l = 0; l < 16; l++) dst[l] = (float)b[l];
+        for (int l = 0; l < 16; l++) dst[l] = (float)b[l];
+      }
+      for (int r = tid; r < n; r += blockDim.x) tsc[r] = scl[(sbase + (size_t)(s0 + r) * c.n_head)];
+    } else {
+      // dense caches: element offsets like the int8 codes', 4 or 2 bytes each
+      const size_t base = ((size_t)layer * c.max_t * c.n_head + h) * HS;
+      const void *src = which == 0 ? (const void *)c.k : (const void *)c.v;
+      for (int i = tid; i < n * HS; i += blockDim.x) {
+        const int r = i / HS, d = i % HS;
+        const size_t e = base + (size_t)(s0 + r) * head_stride + d;
+        tile[r * HP + d] = KVT == 1 ? ((const float *)src)[e]
+                                    : __uint_as_float((unsigned)((const uint16_t *)src)[e] << 16);
+      }
+      for (int r = tid; r < n; r += blockDim.x) tsc[r] = 1.0f;
     }
-    for (int r = tid; r < n; r += blockDim.x) tsc[r] = scl[(sbase + (size_t)(s0 + r) * c.n_head)];
   };
 
   // 1. scores, a tile of keys at a time; a thread takes one position for 4
@@ -280,7 +317,7 @@ __global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c0, float *out
         for (int l = 0; l < 4; l++) e[l] = e[l] + e[l + 4];
         e[0] = e[0] + e[2];
         e[1] = e[1] + e[3];
-        sc[(size_t)qi * P + s] = ((e[0] + e[1]) * tsc[r]) * scale;
+        sc[(size_t)qi * P + s] = KVT == 0 ? ((e[0] + e[1]) * tsc[r]) * scale : (e[0] + e[1]) * scale;
       }
     }
   }
@@ -328,7 +365,8 @@ __global__ void __launch_bounds__(256) kv8_prefill_kernel(KV8View c0, float *out
     const int n = min(KV_TILE, P - s0);
     for (int i = tid; i < nq * n; i += blockDim.x) {
       const int qi = i / n, r = i % n, s = s0 + r;
-      if (s < pos0 + t0 + qi + 1) sc[(size_t)qi * P + s] = (sc[(size_t)qi * P + s] / tot[qi]) * tsc[r];
+      if (s < pos0 + t0 + qi + 1)
+        sc[(size_t)qi * P + s] = KVT == 0 ? (sc[(size_t)qi * P + s] / tot[qi]) * tsc[r] : sc[(size_t)qi * P + s] / tot[qi];
     }
     __syncthreads();
     if (tid < nchains) {

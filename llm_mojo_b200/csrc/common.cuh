@@ -10,6 +10,7 @@
 
 #include <climits>
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 

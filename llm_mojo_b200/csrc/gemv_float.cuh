@@ -61,24 +61,26 @@ __device__ __forceinline__ void k_sm(const uint8_t *q, int j, int &sc, int &m) {
   }
 }
 
-// Lane L's chain over one block of type T at b (in shared memory); x is the
-// block's slice of the input.
-template <int T>
-__device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, int L, float acc) {
+// The dequantized values of lane L of one block of type T at b
+// (dequant_q4_0 .. dequant_q6_k, gguf.mojo:178-297), in the reference's put
+// order: f(value, index in the block) for each. The dot (block_lane) and the
+// plain dequantization (gguf_dequant_rows_kernel) both use it.
+template <int T, class F>
+__device__ __forceinline__ void block_values(const uint8_t *b, int L, F &&f) {
   if (T == RT_Q4_0) {
     const float d = ld_f16(b);
     const int q = b[2 + L];
-    acc = fmaf(((float)(q & 0xF) - 8.0f) * d, x[L], acc);
-    acc = fmaf(((float)(q >> 4) - 8.0f) * d, x[16 + L], acc);
+    f(((float)(q & 0xF) - 8.0f) * d, L);
+    f(((float)(q >> 4) - 8.0f) * d, 16 + L);
   } else if (T == RT_Q4_1) {
     const float d = ld_f16(b), m = ld_f16(b + 2);
     const int q = b[4 + L];
-    acc = fmaf(d * (float)(q & 0xF) + m, x[L], acc);
-    acc = fmaf(d * (float)(q >> 4) + m, x[16 + L], acc);
+    f(d * (float)(q & 0xF) + m, L);
+    f(d * (float)(q >> 4) + m, 16 + L);
   } else if (T == RT_Q8_0) {
     const float d = ld_f16(b);
-    acc = fmaf(d * (float)(int8_t)b[2 + L], x[L], acc);
-    acc = fmaf(d * (float)(int8_t)b[18 + L], x[16 + L], acc);
+    f(d * (float)(int8_t)b[2 + L], L);
+    f(d * (float)(int8_t)b[18 + L], 16 + L);
   } else if (T == RT_Q4_K || T == RT_Q5_K) {
     const float d = ld_f16(b), dmin = ld_f16(b + 2);
     const uint8_t *sc = b + 4;
@@ -100,8 +102,8 @@ __device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, in
           lo = (q & 0xF) | (((qh >> (2 * j)) & 1) << 4);
           hi = (q >> 4) | (((qh >> (2 * j + 1)) & 1) << 4);
         }
-        acc = fmaf(d1 * (float)lo - m1, x[64 * j + 16 * h + L], acc);
-        acc = fmaf(d2 * (float)hi - m2, x[64 * j + 32 + 16 * h + L], acc);
+        f(d1 * (float)lo - m1, 64 * j + 16 * h + L);
+        f(d2 * (float)hi - m2, 64 * j + 32 + 16 * h + L);
       }
     }
   } else if (T == RT_Q6_K) {
@@ -120,17 +122,24 @@ __device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, in
           else if (k == 1) q = (lo1 & 0xF) | (((hi >> 2) & 3) << 4);
           else if (k == 2) q = (lo0 >> 4) | (((hi >> 4) & 3) << 4);
           else q = (lo1 >> 4) | (((hi >> 6) & 3) << 4);
-          acc = fmaf(ds * ((float)q - 32.0f), x[base + 32 * k + L], acc);
+          f(ds * ((float)q - 32.0f), base + 32 * k + L);
         }
       }
     }
   } else if (T == RT_F32) {
-    acc = fmaf(((const float *)b)[L], x[L], acc);
+    f(((const float *)b)[L], L);
   } else if (T == RT_F16) {
-    acc = fmaf(__half2float(((const __half *)b)[L]), x[L], acc);
+    f(__half2float(((const __half *)b)[L]), L);
   } else if (T == RT_BF16) {
-    acc = fmaf(__uint_as_float((unsigned)((const uint16_t *)b)[L] << 16), x[L], acc);
+    f(__uint_as_float((unsigned)((const uint16_t *)b)[L] << 16), L);
   }
+}
+
+// Lane L's chain over one block of type T at b (in shared memory); x is the
+// block's slice of the input.
+template <int T>
+__device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, int L, float acc) {
+  block_values<T>(b, L, [&](float v, int i) { acc = fmaf(v, x[i], acc); });
   return acc;
 }
 

@@ -9,6 +9,7 @@
 #include "../../include/llmq.h"
 #include "attention.cuh"
 #include "batch.cuh"
+#include "dense.cuh"
 #include "gemv_a16.cuh"
 #include "gemv_float.cuh"
 #include "mega.cuh"
@@ -88,6 +89,7 @@ struct llmq_model {
   unsigned long long *mega_ll = nullptr;
   int *mega_err = nullptr;
   unsigned mega_flag = 1;
+  bool float_only = false;  // float-activation formats: forward_all only
   long long *prof = nullptr;  // [2][MK_PROF] when profiling
   const float *vec(int l, int which) const {
     static const int mult[8] = {0, 1, 2, 5, 6, 7, 8, 12};
@@ -232,9 +234,9 @@ cudaError_t configure_kernels() {
   rs((const void *)row_gemv_kernel<RT_Q4_K>);
   rs((const void *)row_gemv_kernel<RT_Q5_K>);
   rs((const void *)row_gemv_kernel<RT_Q6_K>);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute((const void *)kv8_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kMaxPrefillSmem);
+  for (const void *k : {(const void *)kv_prefill_kernel<0>, (const void *)kv_prefill_kernel<1>,
+                        (const void *)kv_prefill_kernel<2>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxPrefillSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)kv8_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kv8_attend_smem(1024, 128));
@@ -506,6 +508,47 @@ bool tc_eligible(const llmq_ctx *ctx, const llmq_weight *w, int T) {
 
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
+llmq_status dequant_rows(llmq_ctx *ctx, const llmq_weight *w, int r0, int nrows, float *dst) {
+  const int grid = (nrows + 15) / 16;
+  const RowMat rm = w->rowmat();
+#define DQ(T) \
+  case T:     \
+    gguf_dequant_rows_kernel<T><<<grid, 256, 0, ctx->stream>>>(rm, r0, nrows, dst); \
+    break;
+  switch (w->rtype) {
+    DQ(RT_F32) DQ(RT_F16) DQ(RT_BF16) DQ(RT_Q4_0) DQ(RT_Q4_1) DQ(RT_Q8_0) DQ(RT_Q4_K) DQ(RT_Q5_K) DQ(RT_Q6_K)
+    default:
+      return fail(ctx, LLMQ_ERR_UNSUPPORTED, "GGUF type");
+  }
+#undef DQ
+  CKL();
+  return LLMQ_OK;
+}
+
+// matmul_rows for T > 1 (kernels.mojo:325-358): rows of 32 outputs
+// dequantized to float32 and run through the mm_tile chain; the OUT % 32
+// leftover rows through rows_dot (:361-397).
+llmq_status gguf_rows_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out,
+                             int T, int IN, int OUT, int epi) {
+  const int full = OUT / 32 * 32;
+  llmq_status st = ensure_scratch(ctx, (size_t)OUT * IN * 4);
+  if (st != LLMQ_OK) return st;
+  float *wd = (float *)ctx->scratch;
+  if ((st = dequant_rows(ctx, w, 0, OUT, wd)) != LLMQ_OK) return st;
+  if (full > 0) {
+    const dim3 grid((full + DM_N - 1) / DM_N, (T + DM_T - 1) / DM_T);
+    dense_mm_kernel<0, true><<<grid, 256, 0, ctx->stream>>>(wd, x, bias, out, T, IN, OUT, full, epi);
+    CKL();
+  }
+  if (OUT > full) {
+    const int pairs = T * (OUT - full);
+    rows_dot_kernel<<<(pairs * 16 + 255) / 256, 256, 0, ctx->stream>>>(wd + (size_t)full * IN, x, bias, out, T, IN,
+                                                                       OUT, full, epi);
+    CKL();
+  }
+  return LLMQ_OK;
+}
+
 // matmul_rows_a16 for T > 1 (kernels.mojo:461-507) with the tile_i16 rows
 // (the first OUT / 32 * 32 outputs) on the split-int8 tcgen05 GEMM and the
 // leftover rows (rows_i16) on rows_a16_kernel.
@@ -590,7 +633,18 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
   if (w->kind == WK_DENSE) {
     // DenseMatrix layer matrices are [IN, OUT] (tensor.mojo:150-227).
     if (IN != w->rows || OUT != w->cols) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the [IN, OUT] matrix");
-    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "dense matmuls with T > 1 are not built");
+    if (T > 1) {
+      // matmul / mm_tile (kernels.mojo:51-129): one fma chain per output
+      const dim3 grid((OUT + DM_N - 1) / DM_N, (T + DM_T - 1) / DM_T);
+      if (w->rtype == RT_F32)
+        dense_mm_kernel<0, false><<<grid, 256, 0, ctx->stream>>>(w->codes, x, bias, out, T, IN, OUT, OUT, epi);
+      else if (w->rtype == RT_BF16)
+        dense_mm_kernel<1, false><<<grid, 256, 0, ctx->stream>>>(w->codes, x, bias, out, T, IN, OUT, OUT, epi);
+      else
+        return fail(ctx, LLMQ_ERR_UNSUPPORTED, "several-token dense matmuls take float32 or bfloat16");
+      CKL();
+      return LLMQ_OK;
+    }
     const int np = ctx->dense_parts;
     llmq_status st = ensure_scratch(ctx, (size_t)np * OUT * 4);
     if (st != LLMQ_OK) return st;
@@ -605,9 +659,10 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     return LLMQ_OK;
   }
   if (IN != w->cols || OUT != w->rows) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the matrix");
+  if (w->kind == WK_GGUF && T > 1) return gguf_rows_linear(ctx, w, x, bias, out, T, IN, OUT, epi);
   if (w->kind == WK_GGUF || (w->kind == WK_AFFINE && !w->a16)) {
     // matmul_rows (kernels.mojo:285-349) for one token: dot_row per output.
-    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation matmuls with T > 1 are not built");
+    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation affine matmuls with T > 1 are not built");
     if (w->kind == WK_GGUF) {
       RowGemvArgs a{w->rowmat(), x, bias, out, epi};
       CK(row_gemv(ctx, a));
@@ -673,6 +728,16 @@ llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float
     return LLMQ_OK;
   }
   if (w->kind == WK_AFFINE && w->a16) return llmq_linear(ctx, w, h, nullptr, logits, T, C, V, 0);
+  if (w->kind == WK_DENSE && T > 1 && (w->rtype == RT_F32 || w->rtype == RT_BF16)) {
+    // lm_head_rows (kernels.mojo:230-271): the 16 lane chains of lm_head, per token
+    const dim3 grid((V + 15) / 16, (T + 15) / 16);
+    if (w->rtype == RT_F32)
+      dense_head_rows_kernel<0><<<grid, 256, 0, ctx->stream>>>(w->codes, h, logits, T, V, C);
+    else
+      dense_head_rows_kernel<1><<<grid, 256, 0, ctx->stream>>>(w->codes, h, logits, T, V, C);
+    CKL();
+    return LLMQ_OK;
+  }
   // lm_head / lm_head_rows (dense, kernels.mojo:213-271) and matmul_rows
   // (OUT_MAJOR formats) for one token: a 16-lane dot per vocabulary row;
   // lm_head_rows gives every token the same arithmetic as lm_head.
@@ -825,7 +890,8 @@ llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int 
                            llmq_kv **out) {
   if (!ctx || !out || n_layer <= 0 || max_t <= 0 || n_head <= 0 || head_dim <= 0 || head_dim % 16 || head_dim > 128)
     return fail(ctx, LLMQ_ERR_INVALID, "bad cache shape");
-  if (kind != LLMQ_KV_QUANT8 && kind != LLMQ_KV_INTATTN) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "unknown cache kind");
+  if (kind != LLMQ_KV_QUANT8 && kind != LLMQ_KV_INTATTN && kind != LLMQ_KV_F32 && kind != LLMQ_KV_BF16)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "unknown cache kind");
   // IntAttnKV keeps keys in blocks of 16 positions and pairs of dimensions
   // (int_attention.mojo:283-284 aborts on other shapes).
   if (kind == LLMQ_KV_INTATTN && (max_t % IA_PB || head_dim % 32))
@@ -840,16 +906,18 @@ llmq_status llmq_kv_create(llmq_ctx *ctx, int kind, int n_layer, int max_t, int 
   c->n_head = n_head;
   c->head_dim = head_dim;
   size_t n = (size_t)n_layer * max_t * n_head * head_dim, ns = (size_t)n_layer * max_t * n_head;
+  const size_t el = kind == LLMQ_KV_F32 ? 4 : kind == LLMQ_KV_BF16 ? 2 : 1;  // bytes per key or value element
+  const bool dense = el > 1;
   void *k = nullptr, *v = nullptr, *ks = nullptr, *vs = nullptr;
-  cudaError_t e = cudaMalloc(&k, n);
-  if (e == cudaSuccess) e = cudaMalloc(&v, n);
-  if (e == cudaSuccess) e = cudaMalloc(&ks, ns * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&vs, ns * 4);
-  if (e == cudaSuccess) e = cudaMemset(k, 0, n);
-  if (e == cudaSuccess) e = cudaMemset(v, 0, n);
-  if (e == cudaSuccess) e = cudaMemset(ks, 0, ns * 4);
-  if (e == cudaSuccess) e = cudaMemset(vs, 0, ns * 4);
-  if (kind == LLMQ_KV_QUANT8)
+  cudaError_t e = cudaMalloc(&k, n * el);
+  if (e == cudaSuccess) e = cudaMalloc(&v, n * el);
+  if (e == cudaSuccess && !dense) e = cudaMalloc(&ks, ns * 4);
+  if (e == cudaSuccess && !dense) e = cudaMalloc(&vs, ns * 4);
+  if (e == cudaSuccess) e = cudaMemset(k, 0, n * el);
+  if (e == cudaSuccess) e = cudaMemset(v, 0, n * el);
+  if (e == cudaSuccess && !dense) e = cudaMemset(ks, 0, ns * 4);
+  if (e == cudaSuccess && !dense) e = cudaMemset(vs, 0, ns * 4);
+  if (kind == LLMQ_KV_QUANT8 || dense)
     c->v8 = KV8View{(int8_t *)k, (int8_t *)v, (float *)ks, (float *)vs, n_layer, max_t, n_head, head_dim};
   else
     c->ia = IAView{(int8_t *)k, (int8_t *)v, (int32_t *)ks, (int32_t *)vs, n_layer, max_t, n_head, head_dim};
@@ -884,6 +952,10 @@ llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T
   dim3 grid(kv->n_head, T, 2);
   if (kv->kind == LLMQ_KV_QUANT8)
     kv8_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr);
+  else if (kv->kind == LLMQ_KV_F32)
+    dkv_store_kernel<1><<<T, 256, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0);
+  else if (kv->kind == LLMQ_KV_BF16)
+    dkv_store_kernel<2><<<T, 256, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0);
   else
     ia_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->ia, qkv, layer, pos0);
   CKL();
@@ -896,9 +968,18 @@ llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *
     return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
   CK(cudaSetDevice(ctx->device));
   dim3 grid(kv->n_head, T);
-  if (kv->kind == LLMQ_KV_QUANT8 && T > 1 && kv8_prefill_smem(pos0 + T, kv->head_dim) <= (size_t)kMaxPrefillSmem) {
+  if (kv->kind == LLMQ_KV_F32 || kv->kind == LLMQ_KV_BF16) {
+    // attend_float_one through DenseKV, every token count
     const size_t sm = kv8_prefill_smem(pos0 + T, kv->head_dim);
-    kv8_prefill_kernel<<<dim3(kv->n_head, (T + KV_QB - 1) / KV_QB), 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer,
+    if (sm > (size_t)kMaxPrefillSmem) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "context too long for the dense cache kernel");
+    const dim3 g(kv->n_head, (T + KV_QB - 1) / KV_QB);
+    if (kv->kind == LLMQ_KV_F32)
+      kv_prefill_kernel<1><<<g, 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, T);
+    else
+      kv_prefill_kernel<2><<<g, 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, T);
+  } else if (kv->kind == LLMQ_KV_QUANT8 && T > 1 && kv8_prefill_smem(pos0 + T, kv->head_dim) <= (size_t)kMaxPrefillSmem) {
+    const size_t sm = kv8_prefill_smem(pos0 + T, kv->head_dim);
+    kv_prefill_kernel<0><<<dim3(kv->n_head, (T + KV_QB - 1) / KV_QB), 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer,
                                                                                             pos0, T);
   } else if (kv->kind == LLMQ_KV_QUANT8) {
     size_t sm = kv8_attend_smem(kv->max_t, kv->head_dim);
@@ -917,13 +998,14 @@ llmq_status llmq_kv_read(llmq_ctx *ctx, const llmq_kv *kv, void *k, void *v, voi
   CK(cudaStreamSynchronize(ctx->stream));
   size_t n = (size_t)kv->n_layer * kv->max_t * kv->n_head * kv->head_dim;
   size_t ns = (size_t)kv->n_layer * kv->max_t * kv->n_head;
-  const bool q8 = kv->kind == LLMQ_KV_QUANT8;
+  const bool q8 = kv->kind != LLMQ_KV_INTATTN;  // the int8 and dense caches live in v8
+  const size_t el = kv->kind == LLMQ_KV_F32 ? 4 : kv->kind == LLMQ_KV_BF16 ? 2 : 1;
   const void *src[4] = {q8 ? (const void *)kv->v8.k : kv->ia.k, q8 ? (const void *)kv->v8.v : kv->ia.v,
                         q8 ? (const void *)kv->v8.ks : kv->ia.kq, q8 ? (const void *)kv->v8.vs : kv->ia.vq};
   void *dst[4] = {k, v, ks, vs};
-  size_t bytes[4] = {n, n, ns * 4, ns * 4};
+  size_t bytes[4] = {n * el, n * el, ns * 4, ns * 4};
   for (int i = 0; i < 4; i++)
-    if (dst[i]) CK(cudaMemcpy(dst[i], src[i], bytes[i], cudaMemcpyDeviceToHost));
+    if (dst[i] && src[i]) CK(cudaMemcpy(dst[i], src[i], bytes[i], cudaMemcpyDeviceToHost));
   return LLMQ_OK;
 }
 
@@ -1158,7 +1240,30 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
 llmq_status enqueue_blocks(llmq_model *m, int T, int pos0, cudaStream_t s) {
   llmq_ctx *ctx = m->ctx;
   const int C = m->C;
-  embed_rows_kernel<<<T, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->tokens, pos0);
+  const llmq_weight *hd = m->head;
+  if (hd->kind == WK_AFFINE) {
+    embed_rows_kernel<<<T, 256, 0, s>>>(hd->view(), m->wpe(), m->x, m->tokens, pos0);
+  } else if (hd->kind == WK_DENSE) {
+    if (hd->rtype == RT_F32)
+      embed_dense_kernel<0><<<T, 256, 0, s>>>(hd->codes, C, hd->rows, m->wpe(), m->x, m->tokens, pos0);
+    else if (hd->rtype == RT_BF16)
+      embed_dense_kernel<1><<<T, 256, 0, s>>>(hd->codes, C, hd->rows, m->wpe(), m->x, m->tokens, pos0);
+    else
+      return fail(ctx, LLMQ_ERR_UNSUPPORTED, "dense embeddings take float32 or bfloat16");
+  } else {
+    const RowMat rm = hd->rowmat();
+#define EG(T) \
+  case T:     \
+    embed_gguf_kernel<T><<<T_, 256, 0, s>>>(rm, m->wpe(), m->x, m->tokens, pos0); \
+    break;
+    const int T_ = T;
+    switch (hd->rtype) {
+      EG(RT_F32) EG(RT_F16) EG(RT_BF16) EG(RT_Q4_0) EG(RT_Q4_1) EG(RT_Q8_0) EG(RT_Q4_K) EG(RT_Q5_K) EG(RT_Q6_K)
+      default:
+        return fail(ctx, LLMQ_ERR_UNSUPPORTED, "GGUF type");
+    }
+#undef EG
+  }
   CKL();
   llmq_status st;
   for (int l = 0; l < m->n_layer; l++) {
@@ -1186,12 +1291,21 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
   if (!ctx || !mats || !head || !small_host || !out || n_layer <= 0 || max_t <= 0 || max_t > 1024)
     return fail(ctx, LLMQ_ERR_INVALID, "bad model arguments");
   const int C = 768;
+  bool a16 = head->kind == WK_AFFINE && head->a16;
   for (int i = 0; i < 4 * n_layer; i++) {
     static const int ins[4] = {C, C, C, 4 * C}, outs[4] = {3 * C, C, 4 * C, C};
-    if (!mats[i] || mats[i]->cols != ins[i % 4] || mats[i]->rows != outs[i % 4] || !mats[i]->a16)
+    const llmq_weight *w = mats[i];
+    // dense layers are [IN, OUT] (Conv1D); the others [OUT, IN]
+    const bool shape_ok = w && (w->kind == WK_DENSE ? (w->rows == ins[i % 4] && w->cols == outs[i % 4])
+                                                    : (w->cols == ins[i % 4] && w->rows == outs[i % 4]));
+    const bool fmt_ok = w && (w->kind == WK_DENSE || w->kind == WK_GGUF || (w->kind == WK_AFFINE && w->a16));
+    if (!shape_ok || !fmt_ok)
       return fail(ctx, LLMQ_ERR_INVALID, "layer matrix " + std::to_string(i) + " has an unexpected shape or format");
+    a16 = a16 && w->kind == WK_AFFINE && w->a16;
   }
-  if (head->cols != C || !head->a16) return fail(ctx, LLMQ_ERR_INVALID, "head must be an A16 [V, 768] matrix");
+  if (head->cols != C) return fail(ctx, LLMQ_ERR_INVALID, "head must be a [V, 768] matrix");
+  if (!a16 && kv_kind == LLMQ_KV_INTATTN)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-format models take the int8 or a dense cache");
   *out = nullptr;
   CK(cudaSetDevice(ctx->device));
   llmq_model *m = new llmq_model();
@@ -1203,6 +1317,7 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
   m->n_head = 12;
   m->mats.assign(mats, mats + 4 * n_layer);
   m->head = head;
+  m->float_only = !a16;
   m->max_ids = 4096;
   llmq_status st = llmq_kv_create(ctx, kv_kind, n_layer, max_t, m->n_head, C / m->n_head, &m->kv);
   if (st != LLMQ_OK) {
@@ -1210,7 +1325,7 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
     return st;
   }
   size_t small_n = (size_t)n_layer * 13 * C + (size_t)1024 * C + 2 * C;
-  int grid = gemv_grid(ctx, head->view());
+  int grid = a16 ? gemv_grid(ctx, head->view()) : 1;
   cudaError_t e = cudaMalloc(&m->small, small_n * 4);
   if (e == cudaSuccess) e = cudaMemcpy(m->small, small_host, small_n * 4, cudaMemcpyHostToDevice);
   if (e == cudaSuccess) e = cudaMalloc(&m->x, (size_t)max_t * C * 4);
@@ -1362,6 +1477,8 @@ static llmq_status check_tokens(llmq_ctx *ctx, llmq_model *m, const int *tokens,
 
 llmq_status llmq_model_forward(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T, int pos0, float *logits_dev,
                                int *argmax_host) {
+  if (m && m->float_only)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !tokens || T <= 0 || pos0 < 0 || pos0 + T > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad tokens or positions");
   llmq_status st = check_tokens(ctx, m, tokens, T);
@@ -1391,7 +1508,7 @@ llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *toke
   llmq_status st = enqueue_blocks(m, T, 0, s);
   if (st == LLMQ_OK) {
     layernorm_kernel<<<T, 256, m->C * 4, s>>>(m->xn, m->x, m->lnf_w(), m->lnf_b(), m->C);
-    st = llmq_linear(ctx, m->head, m->xn, nullptr, logits_dev, T, m->C, m->V, 0);
+    st = llmq_head(ctx, m->head, m->xn, logits_dev, T, m->C, m->V);
   }
   if (st != LLMQ_OK) return st;
   CK(cudaStreamSynchronize(s));
@@ -1399,6 +1516,8 @@ llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *toke
 }
 
 llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n_prompt, int steps, int *out_ids) {
+  if (m && m->float_only)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !prompt || !out_ids || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
       n_prompt + steps - 1 > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
@@ -1418,6 +1537,8 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n
 
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
                                 int *ids_dev) {
+  if (m && m->float_only)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !prompt_dev || !ids_dev || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
       n_prompt + steps - 1 > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
@@ -1612,7 +1733,7 @@ llmq_status batch_prompt(llmq_batch *bt, int B, int P, cudaStream_t s) {
     kv8_store_kernel<<<dim3(m->n_head, P, 2 * B), 128, 0, s>>>(bt->kv, bt->qkv, l, 0, nullptr);
     CKL();
     const size_t sm = kv8_prefill_smem(P, C / m->n_head);
-    kv8_prefill_kernel<<<dim3(m->n_head, (P + KV_QB - 1) / KV_QB, B), 256, sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, P);
+    kv_prefill_kernel<0><<<dim3(m->n_head, (P + KV_QB - 1) / KV_QB, B), 256, sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, P);
     CKL();
     if ((st = llmq_linear(ctx, w[1], bt->att, m->vec(l, 3), bt->x, T, C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK)
       return st;
@@ -1682,6 +1803,8 @@ llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
 extern "C" {
 
 llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int max_prompt, llmq_batch **out) {
+  if (m && m->float_only)
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !out || max_seqs <= 0 || max_prompt <= 0 || max_prompt > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad batch arguments");
   if (m->kv->kind != LLMQ_KV_QUANT8) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "batched decode takes the QuantKV[8] cache");
@@ -1801,6 +1924,21 @@ llmq_status llmq_batch_generate(llmq_ctx *ctx, llmq_batch *bt, const int *prompt
   CK(cudaStreamSynchronize(s));
   if ((st = tc_check(ctx)) != LLMQ_OK) return st;
   std::memcpy(out_ids, bt->ids_host, (size_t)B * steps * 4);
+  return LLMQ_OK;
+}
+
+}  // extern "C"
+
+extern "C" {
+
+llmq_status llmq_score_rows(llmq_ctx *ctx, const float *logits_dev, const float *base_dev, const int *targets_dev, int V,
+                            int r0, int r1, double *stats_dev, int stride) {
+  if (!ctx || !logits_dev || !targets_dev || !stats_dev || V <= 0 || r0 < 0 || r1 < r0 || stride < r1 - r0)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad score arguments");
+  if (r1 == r0) return LLMQ_OK;
+  CK(cudaSetDevice(ctx->device));
+  score_rows_kernel<<<r1 - r0, 256, 0, ctx->stream>>>(logits_dev, base_dev, targets_dev, V, r0, stats_dev, stride);
+  CKL();
   return LLMQ_OK;
 }
 

@@ -11,8 +11,8 @@ from __future__ import annotations
 
 import ctypes as C
 
-from ._lib import (BIAS, GELU, KV_INTATTN, KV_QUANT8, PREFILL_AUTO, PREFILL_CUDA_CORE, PREFILL_TCGEN05, RESID, check,
-                   lib)
+from ._lib import (BIAS, GELU, KV_BF16, KV_F32, KV_INTATTN, KV_QUANT8, PREFILL_AUTO, PREFILL_CUDA_CORE,
+                   PREFILL_TCGEN05, RESID, check, lib)
 from .tensor import Context, QuantMatrix
 
 
@@ -86,12 +86,13 @@ def lane_sums(ctx: Context, w: QuantMatrix, x, lanes):
 
 
 class KVCache:
-    """KVCache (kvcache.mojo:31-87): QuantKV[8] ('int8') or IntAttnKV
-    ('intattn')."""
+    """KVCache (kvcache.mojo:31-87): QuantKV[8] ('int8'), IntAttnKV
+    ('intattn'), DenseKV[float32] ('f32') or DenseKV[bfloat16] ('bf16')."""
 
     def __init__(self, ctx: Context, kind: str, n_layer: int, max_t: int, n_head: int, head_dim: int):
         self.ctx = ctx
-        self.kind = {"int8": KV_QUANT8, "intattn": KV_INTATTN}[kind]
+        self.kind = {"int8": KV_QUANT8, "intattn": KV_INTATTN, "f32": KV_F32, "bf16": KV_BF16}[kind]
+        self.elem = {KV_F32: 4, KV_BF16: 2}.get(self.kind, 1)
         self.shape = (n_layer, max_t, n_head, head_dim)
         h = C.c_void_p()
         check(lib().llmq_kv_create(ctx.h, self.kind, n_layer, max_t, n_head, head_dim, C.byref(h)), ctx.h)
@@ -108,11 +109,13 @@ class KVCache:
         self.ctx.sync()
 
     def read(self):
-        """(k, v, ks, vs) host copies of the storage."""
+        """(k, v, ks, vs) host copies of the storage: int8 codes, or float32 /
+        bfloat16 bits (uint16) for the dense caches, which have no scales."""
         import numpy as np
 
         L, T, H, D = self.shape
-        k = np.zeros(L * T * H * D, dtype=np.int8)
+        dt = {1: np.int8, 2: np.uint16, 4: np.float32}[self.elem]
+        k = np.zeros(L * T * H * D, dtype=dt)
         v = np.zeros_like(k)
         ks = np.zeros(L * T * H, dtype=np.float32)
         vs = np.zeros_like(ks)

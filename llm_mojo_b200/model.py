@@ -147,3 +147,71 @@ class Batch:
             self.free()
         except Exception:
             pass
+
+
+# Float formats of the perplexity harness (gpt2t.mojo:1180-1270): the layer
+# format, its head and the cache that default_kv picks for it.
+FLOAT_FORMATS = ("f32", "bf16", "gguf-q4_k")
+
+
+class FloatModel:
+    """Model[W, E, KV] for the float-activation formats, run through
+    forward_all (evaluation): 'f32' (DenseMatrix[float32] layers and head,
+    DenseKV[float32]), 'bf16' (DenseMatrix[bfloat16], DenseKV[bfloat16]) and
+    'gguf-q4_k' (GGUF Q4_K layers, Q6_K head, the int8 cache: the layout of a
+    Q4_K_M file). Weights are converted from float32 tensors as the
+    reference's loaders do."""
+
+    def __init__(self, ctx: Context, tensors: dict, fmt: str, n_layer: int = synth.N_LAYER,
+                 max_t: int = synth.MAX_T):
+        from . import gguf_blocks as G
+        from ._lib import KV_BF16, KV_F32
+        from .tensor import DenseMatrix, GGUFMatrix
+
+        if fmt not in FLOAT_FORMATS:
+            raise ValueError(f"unknown float format {fmt}")
+        self.ctx, self.fmt, self.n_layer = ctx, fmt, n_layer
+        self.mats = []
+        for l in range(n_layer):
+            for name in synth.MAT_NAMES:
+                w = tensors[f"h.{l}.{name}"]  # [IN, OUT]
+                if fmt == "gguf-q4_k":
+                    self.mats.append(GGUFMatrix(ctx, G.Q4_K, G.quantize(np.ascontiguousarray(w.T), G.Q4_K),
+                                                w.shape[1], w.shape[0]))
+                else:
+                    self.mats.append(DenseMatrix(ctx, fmt, w))
+        wte = tensors["wte.weight"]
+        if fmt == "gguf-q4_k":
+            self.head = GGUFMatrix(ctx, G.Q6_K, G.quantize(wte, G.Q6_K), wte.shape[0], wte.shape[1])
+            kind = KV_QUANT8
+        else:
+            self.head = DenseMatrix(ctx, fmt, wte)
+            kind = KV_F32 if fmt == "f32" else KV_BF16
+        self.small = synth.small_floats(tensors, n_layer)
+        arr = (C.c_void_p * len(self.mats))(*[m.h.value for m in self.mats])
+        h = C.c_void_p()
+        check(lib().llmq_model_create(ctx.h, n_layer, C.cast(arr, C.c_void_p), self.head.h,
+                                      self.small.ctypes.data_as(C.c_void_p), kind, max_t, C.byref(h)), ctx.h)
+        self.h = h
+        self.V = self.head.rows
+
+    def forward_all(self, tokens, logits):
+        """logits [T, V] (float32 CUDA tensor) for every position of tokens."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        check(lib().llmq_model_forward_all(self.ctx.h, self.h, t.ctypes.data_as(C.c_void_p), t.size,
+                                           C.c_void_p(logits.data_ptr())), self.ctx.h)
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().llmq_model_free(self.h)
+            self.h = None
+        for m in getattr(self, "mats", []):
+            m.free()
+        if getattr(self, "head", None) is not None:
+            self.head.free()
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass

@@ -1430,3 +1430,128 @@ OQ_EXPORT void oq_dense_gemv(int dt, const void *w, const float *x, const float 
   }
   free(scratch);
 }
+
+/* ------------------------------------------------------------------------ */
+/* Several-token float paths and the perplexity scores                      */
+/* ------------------------------------------------------------------------ */
+
+/* matmul for T > 1 (kernels.mojo:96-129) through mm_tile (:51-93): out[T,
+ * OUT] (+)= act(x[T, IN] @ w[IN, OUT] + b), each output one fma chain over i. */
+OQ_EXPORT void oq_dense_mm(int dt, const void *w, const float *x, const float *b, float *out, int T, int IN, int OUT,
+                           int resid, int gelu) {
+  for (int t = 0; t < T; t++)
+    for (int j = 0; j < OUT; j++) {
+      float acc = 0.0f;
+      for (int i = 0; i < IN; i++) acc = fmaf(x[(long)t * IN + i], dense_at(dt, w, (long)i * OUT + j), acc);
+      if (b) acc += b[j];
+      finish(out + (long)t * OUT, j, acc, resid, gelu);
+    }
+}
+
+/* lm_head_rows (kernels.mojo:230-271): logits[T, V] = h[T, C] @ w[V, C]^T, each
+ * the 16-lane dot of lm_head. */
+OQ_EXPORT void oq_dense_head_rows(int dt, const void *w, const float *h, float *logits, int T, int V, int C) {
+  for (int t = 0; t < T; t++)
+    for (int v = 0; v < V; v++) logits[(long)t * V + v] = oq_dense_dot_row(dt, w, v, C, h + (long)t * C);
+}
+
+/* matmul_rows for T > 1 (kernels.mojo:325-358) of a GGUF matrix [OUT rows of
+ * row_bytes]: rows of 32 outputs dequantized and run through mm_tile's
+ * chain; the OUT % 32 leftover rows through rows_dot (:361-397). */
+OQ_EXPORT void oq_gguf_matmul_rows(int type, const uint8_t *rows, long row_bytes, const float *x, const float *b,
+                                   float *out, int T, int IN, int OUT, int resid, int gelu) {
+  float *wd = (float *)malloc(sizeof(float) * IN);
+  int full = OUT / 32 * 32;
+  for (int o = 0; o < OUT; o++) {
+    oq_gguf_dequant_row(type, rows + (long)o * row_bytes, IN, wd);
+    for (int t = 0; t < T; t++) {
+      const float *xt = x + (long)t * IN;
+      float r;
+      if (o < full) {
+        float acc = 0.0f;
+        for (int i = 0; i < IN; i++) acc = fmaf(xt[i], wd[i], acc);
+        r = acc;
+        if (b) r += b[o];
+      } else {
+        float d[16];
+        for (int l = 0; l < 16; l++) d[l] = 0.0f;
+        for (int i = 0; i < IN; i += 16)
+          for (int l = 0; l < 16; l++) d[l] = fmaf(xt[i + l], wd[i + l], d[l]);
+        r = tree16(d) + (b ? b[o] : 0.0f);
+      }
+      finish(out + (long)t * OUT, o, r, resid, gelu);
+    }
+  }
+  free(wd);
+}
+
+/* DenseKV (kvcache.mojo:153-246) attend_float_one for token t of qkv ([T,
+ * 3C]) at position pos0 + t, head h; k and v are [max_t][C] of one layer as
+ * float32 (dt 0) or bfloat16 (dt 2) values. */
+OQ_EXPORT void oq_dkv_attend_one(int dt, const void *k, const void *v, int n_head, int HS, float *out,
+                                 const float *qkv, int t, int h, int pos0) {
+  int C = n_head * HS, npos = pos0 + t + 1;
+  float scale = 1.0f / sqrtf((float)HS);
+  const float *q = qkv + (long)t * 3 * C + h * HS;
+  float *sc = (float *)malloc(sizeof(float) * npos);
+  float mx = -INFINITY;
+  for (int s = 0; s < npos; s++) {
+    float d[16];
+    for (int l = 0; l < 16; l++) d[l] = 0.0f;
+    for (int i = 0; i < HS; i += 16)
+      for (int l = 0; l < 16; l++) d[l] = d[l] + q[i + l] * dense_at(dt, k, (long)s * C + h * HS + i + l);
+    sc[s] = tree16(d) * scale;
+    mx = fmaxf(mx, sc[s]);
+  }
+  for (int s = 0; s < npos; s++) sc[s] = lm_expf(sc[s] - mx);
+  float total = 0.0f;
+  for (int s = 0; s < npos; s++) total += sc[s];
+  float *o = out + (long)t * C + h * HS;
+  for (int i = 0; i < HS; i++) o[i] = 0.0f;
+  for (int s = 0; s < npos; s++) {
+    float p = sc[s] / total;
+    for (int i = 0; i < HS; i++) o[i] = fmaf(p, dense_at(dt, v, (long)s * C + h * HS + i), o[i]);
+  }
+  free(sc);
+}
+
+/* log_sum_exp (gpt2t.mojo:1030-1039). */
+static double oq_lse(const float *row, int V) {
+  float mx = row[0];
+  for (int v = 1; v < V; v++) mx = fmaxf(mx, row[v]);
+  double s = 0.0;
+  for (int v = 0; v < V; v++) s += (double)lm_expf(row[v] - mx);
+  return (double)mx + log(s);
+}
+
+/* score_rows (gpt2t.mojo:1042-1097) of rows [r0, r1): stats[k * stride +
+ * (r - r0)] for k = NLL, NLL_BASE, AGREE, KL, DIFF_MAX, DIFF_SUM. base may be
+ * NULL (the last five are then 0). */
+OQ_EXPORT void oq_score_rows(const float *logits, const float *base, const int *targets, int V, int r0, int r1,
+                             double *stats, int stride) {
+  for (int r = r0; r < r1; r++) {
+    const float *lm = logits + (long)r * V;
+    double lse = oq_lse(lm, V);
+    double vals[6] = {lse - (double)lm[targets[r]], 0, 0, 0, 0, 0};
+    if (base) {
+      const float *lb = base + (long)r * V;
+      double lse_b = oq_lse(lb, V), kl = 0.0, dmax = 0.0, dsum = 0.0;
+      int best = 0, best_b = 0;
+      for (int v = 0; v < V; v++) {
+        double m = lm[v], b = lb[v], lpb = b - lse_b;
+        kl += exp(lpb) * (lpb - (m - lse));
+        double d = fabs(m - b);
+        if (d > dmax) dmax = d;
+        dsum += d;
+        if (lm[v] > lm[best]) best = v;
+        if (lb[v] > lb[best_b]) best_b = v;
+      }
+      vals[1] = lse_b - (double)lb[targets[r]];
+      vals[2] = best == best_b;
+      vals[3] = kl;
+      vals[4] = dmax;
+      vals[5] = dsum;
+    }
+    for (int k = 0; k < 6; k++) stats[(long)k * stride + (r - r0)] = vals[k];
+  }
+}

@@ -85,6 +85,11 @@ def _declare(L):
         "oq_dense_dot_row": (F, [I, P, I, I, P]),
         "oq_dense_gemv": (V, [I, P, P, P, P, I, I, I, I, I]),
         "oq_threads": (I, []), "oq_set_vnni": (I, [I]),
+        "oq_dense_mm": (V, [I, P, P, P, P, I, I, I, I, I]),
+        "oq_dense_head_rows": (V, [I, P, P, P, I, I, I]),
+        "oq_gguf_matmul_rows": (V, [I, P, C.c_long, P, P, P, I, I, I, I, I]),
+        "oq_dkv_attend_one": (V, [I, P, P, I, I, P, P, I, I, I]),
+        "oq_score_rows": (V, [P, P, P, I, I, I, P, I]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
