@@ -358,6 +358,123 @@ def run_batched(args):
     return 0
 
 
+PPL_IDS, PPL_SEED = 65536, 4
+
+
+def cpu_ppl_baseline(seconds: float):
+    """The CPU oracle on config 4's first window, int4-g32-a16, cut to the
+    tokens it forwards in about `seconds` (from 64 up, doubling): windows/s
+    extrapolated linearly to the 1024-token window (optimistic: attention
+    grows faster), with its rows scored."""
+    from llm_mojo_b200 import synth
+    from oracle import oracle as O
+
+    t = synth.gpt2_random_init(0)
+    ids = synth.zipf_ids(PPL_IDS, PPL_SEED)
+    m = O.Model(t)
+    n, dt = 64, 0.0
+    while True:
+        t0 = time.perf_counter()
+        lm = m.forward_all(ids[:n])
+        st = np.zeros((6, n - 1))
+        targets = np.ascontiguousarray(ids[1:n + 1], dtype=np.int32)
+        O.lib().oq_score_rows(O.ptr(np.ascontiguousarray(lm)), None, O.ptr(targets), lm.shape[1], 0, n - 1,
+                              O.ptr(st), n - 1)
+        dt = time.perf_counter() - t0
+        if dt * 2 > seconds or n >= 1024:
+            break
+        n *= 2
+    m.close()
+    threads = int(O.lib().oq_threads())
+    return {"value": 1.0 / (dt * 1024 / n), "unit": "windows/s", "cores": threads, "kind": "port",
+            "sample": f"int4-g32-a16 forward_all + score_rows of the first {n} tokens of window 0 in {dt:.2f} s, "
+                      f"extrapolated linearly to 1024 tokens; one format, no float32 base; {threads}-thread team"}
+
+
+def run_ppl(args):
+    """Config 4: 65,536 ids ~ Zipf(1.1) over the vocabulary (seed 4), windows
+    of 1024 every 512 (127 windows, every token after the first scored once),
+    formats f32, bf16, int4-g32-a16 and GGUF Q4_K (Q6_K head), each against
+    float32 on the same windows. Windows split round-robin over the ranks;
+    the totals meet in one all-reduce. value: windows / the max over ranks of
+    the device time of all of them (the four formats and the f32 base)."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from llm_mojo_b200 import build, synth
+    from llm_mojo_b200.evaluate import Harness, schedule
+    from llm_mojo_b200.model import FloatModel, Model
+    from llm_mojo_b200.tensor import Context
+
+    build.build()
+    ctx = Context(local)
+    stream = torch.cuda.Stream(device=local)
+    ctx.set_stream(stream.cuda_stream)
+    tensors = synth.gpt2_random_init(0)
+    base = FloatModel(ctx, tensors, "f32")
+    models = {"f32": base, "bf16": FloatModel(ctx, tensors, "bf16"), "int4-g32-a16": Model(ctx, tensors),
+              "gguf-q4_k": FloatModel(ctx, tensors, "gguf-q4_k")}
+    ids = synth.zipf_ids(PPL_IDS, PPL_SEED)
+    wins = schedule(len(ids))
+    mine = wins[rank::world]
+    with torch.cuda.stream(stream):
+        warm = Harness(ctx, models, base)
+        for w in mine[:1]:
+            warm.score_window(ids, *w)
+        del warm
+        h = Harness(ctx, models, base)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        t0 = time.perf_counter()
+        for w in mine:
+            h.score_window(ids, *w)
+        e0.record(stream)
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+        ms = torch.tensor([s0.elapsed_time(e0), wall * 1000.0], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        h.reduce(world)
+    rep = h.report()
+    if rank == 0:
+        ms_dev, ms_wall = float(ms[0]), float(ms[1])
+        cpu = None if args.no_cpu_baseline else cpu_ppl_baseline(min(args.cpu_seconds, 20.0))
+        line = {"metric": "perplexity windows/s (4 formats vs f32, 1024-token windows)",
+                "value": len(wins) / (ms_dev / 1000.0), "unit": "windows/s", "n_gpus": world, "steps": 1,
+                "warmup": 1, "ms_per_step": ms_dev / max(1, len(mine)), "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "f32/bf16/int16xint4/gguf",
+                "data": "synthetic",
+                "config": {"workload": "config 4: 65,536 ids ~ Zipf(1.1) seed 4, window 1024 stride 512, 127 windows; "
+                                       "GPT-2 124M random-init (seed 0) in f32, bf16, int4-g32-a16, GGUF Q4_K "
+                                       "(Q6_K head), each vs f32",
+                           "global_batch": len(wins), "seq_len": WINDOW_T,
+                           "parallelism": f"windows round-robin over {world} ranks, one all-reduce of the totals"},
+                "e2e": {"value": len(wins) / (ms_wall / 1000.0), "unit": "windows/s",
+                        "h2d_bytes_per_step": 4 * 1024 * 4, "d2h_bytes_per_step": 0},
+                "formats": rep, "gpu_launches": None, "cpu_baseline": cpu}
+        print(json.dumps(line))
+    for m in models.values():
+        m.free()
+    ctx.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+WINDOW_T = 1024
+
+
 def run_sweep(args):
     """Config 1: x ~ N(0,1) (seed 1), W ~ N(0, 0.02) quantized per format;
     GB/s of packed weight bytes per one-token GEMV, L2 flushed before each
@@ -451,10 +568,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="decode", choices=["decode", "sweep", "prefill", "batched"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "sweep", "prefill", "batched", "ppl"],
                     help="decode: config 0 (the default bench line); sweep: config 1, the one-token GEMV of every "
                          "format at every shape, one JSON line each; prefill: config 2, one line per format; "
-                         "batched: config 3, sequences split over the ranks")
+                         "batched: config 3, sequences split over the ranks; ppl: config 4, windows split over "
+                         "the ranks")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
@@ -467,6 +585,8 @@ def main():
         return run_prefill(args)
     if args.workload == "batched":
         return run_batched(args)
+    if args.workload == "ppl":
+        return run_ppl(args)
 
     import torch
     import torch.distributed as dist

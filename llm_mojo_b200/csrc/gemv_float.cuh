@@ -334,6 +334,8 @@ __global__ void __launch_bounds__(256) gguf_head_i16_kernel(RowMat w, const floa
   __shared__ __align__(16) int16_t xq[4096];
   __shared__ float red[64];
   const int cols = w.cols;
+  h += (size_t)blockIdx.y * cols;  // grid y: the tokens
+  logits += (size_t)blockIdx.y * w.rows;
   float mx = 0.0f;
   for (int i = threadIdx.x; i < cols; i += blockDim.x) mx = fmaxf(mx, fabsf(h[i]));
   mx = block_max(mx, red);

@@ -717,14 +717,12 @@ llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float
   CK(cudaSetDevice(ctx->device));
   if (w->kind == WK_GGUF && (w->rtype == RT_Q8_0 || w->rtype == RT_Q6_K)) {
     // head_i16: the same arithmetic for one token and for several.
-    const int grid = std::min((V + 15) / 16, ctx->num_sms * 4);
-    for (int t = 0; t < T; t++) {
-      if (w->rtype == RT_Q8_0)
-        gguf_head_i16_kernel<RT_Q8_0><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h + (size_t)t * C, logits + (size_t)t * V);
-      else
-        gguf_head_i16_kernel<RT_Q6_K><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h + (size_t)t * C, logits + (size_t)t * V);
-      CKL();
-    }
+    const dim3 grid(std::min((V + 15) / 16, T > 1 ? ctx->num_sms : ctx->num_sms * 4), T);
+    if (w->rtype == RT_Q8_0)
+      gguf_head_i16_kernel<RT_Q8_0><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h, logits);
+    else
+      gguf_head_i16_kernel<RT_Q6_K><<<grid, 256, 0, ctx->stream>>>(w->rowmat(), h, logits);
+    CKL();
     return LLMQ_OK;
   }
   if (w->kind == WK_AFFINE && w->a16) return llmq_linear(ctx, w, h, nullptr, logits, T, C, V, 0);

@@ -64,3 +64,13 @@ def test_gather_blocks_two_gloo_ranks():
         assert p.exitcode == 0
     want = np.array([[u * 100 + t for t in range(5)] for u in range(8)], dtype=np.int32)
     assert np.array_equal(got[0], want) and np.array_equal(got[1], want)
+
+
+def test_schedule_scores_every_token_once():
+    from llm_mojo_b200.evaluate import schedule
+
+    n = 65536
+    seen = []
+    for begin, end, r0, r1 in schedule(n):
+        seen.extend(begin + r + 1 for r in range(r0, r1))
+    assert seen == list(range(1, n)) and len(schedule(n)) == 127
