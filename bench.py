@@ -274,17 +274,18 @@ def run_batched(args):
     from llm_mojo_b200.shard import gather_blocks, shard_range
 
     build.build()
-    b_lo, b_hi = shard_range(BATCH_SEQS, world, rank)
+    n_seqs, n_steps = args.batch_seqs, args.batch_steps
+    b_lo, b_hi = shard_range(n_seqs, world, rank)
     per = b_hi - b_lo
     ctx = Context(local)
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
-    model = Model(ctx, synth.gpt2_random_init(0), max_t=BATCH_PROMPT + BATCH_STEPS)
+    model = Model(ctx, synth.gpt2_random_init(0), max_t=BATCH_PROMPT + n_steps)
     batch = Batch(model, per, BATCH_PROMPT)
     prompts = synth.uniform_ids(BATCH_SEQS * BATCH_PROMPT, 3).reshape(BATCH_SEQS, BATCH_PROMPT)
     mine = np.ascontiguousarray(prompts[b_lo:b_hi])
     prompts_dev = torch.from_numpy(mine).cuda()
-    ids_dev = torch.zeros((per, BATCH_STEPS), dtype=torch.int32, device="cuda")
+    ids_dev = torch.zeros((per, n_steps), dtype=torch.int32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
 
     def gather():
@@ -302,7 +303,7 @@ def run_batched(args):
             barrier()
             s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s0.record(stream)
-            batch.generate_async(prompts_dev, BATCH_STEPS, ids_dev)
+            batch.generate_async(prompts_dev, n_steps, ids_dev)
             gather()
             e0.record(stream)
             barrier()
@@ -317,7 +318,7 @@ def run_batched(args):
     for i in range(2):
         barrier()
         t0 = time.perf_counter()
-        ids = batch.generate(mine, BATCH_STEPS)
+        ids = batch.generate(mine, n_steps)
         ids_dev.copy_(torch.from_numpy(ids))
         host_ids = gather().cpu()
         barrier()
@@ -326,10 +327,10 @@ def run_batched(args):
     if world > 1:
         dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
     e2e_s = float(e2e_s.item())
-    total = BATCH_SEQS * BATCH_STEPS
+    total = n_seqs * n_steps
     if rank == 0:
-        check_ids = host_ids.reshape(BATCH_SEQS, BATCH_STEPS).numpy()
-        single = model.generate(list(prompts[BATCH_SEQS - 1]), BATCH_STEPS)
+        check_ids = host_ids.reshape(n_seqs, n_steps).numpy()
+        single = model.generate(list(prompts[n_seqs - 1]), n_steps)
         cpu = None if args.no_cpu_baseline else cpu_batched_baseline(min(args.cpu_seconds, 15.0))
         line = {"metric": "int4-g32-a16 batched decode tok/s (b=256/box)", "value": total / (ms / 1000.0),
                 "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -338,16 +339,16 @@ def run_batched(args):
                 "config": {"workload": "config 3: 256 sequences x (128-token prompt ~ U[0, 50257) seed 3 + 128 "
                                        "greedy tokens), GPT-2 124M int4-g32-a16 + int8-ch head + int8 KV, "
                                        "random-init weights (seed 0)",
-                           "global_batch": BATCH_SEQS, "seq_len": BATCH_PROMPT + BATCH_STEPS,
+                           "global_batch": n_seqs, "seq_len": BATCH_PROMPT + n_steps,
                            "parallelism": f"sequences split over {world} ranks, one NCCL all-gather of the ids",
                            "l2": "flushed between steps (256 MiB write)"},
                 "e2e": {"value": total / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": per * BATCH_PROMPT * 4,
-                        "d2h_bytes_per_step": BATCH_SEQS * BATCH_STEPS * 4},
+                        "d2h_bytes_per_step": n_seqs * n_steps * 4},
                 "last_sequence_matches_single_decode": bool(list(check_ids[-1]) == list(single)),
                 # per generation: the prompt (embed, 12 x (2 LayerNorm + 4 x (split + GEMM) + store +
                 # attention), gather, head quantize + GEMV, argmax, state) and 127 decode-step graphs
                 # (advance, embed, 12 x (4 x (quantize + GEMV) + attention), head quantize + GEMV, argmax)
-                "gpu_launches": args.steps * ((1 + 12 * 12 + 1 + 2 + 1 + 1) + (BATCH_STEPS - 1) * (2 + 12 * 9 + 3)),
+                "gpu_launches": args.steps * ((1 + 12 * 12 + 1 + 2 + 1 + 1) + (n_steps - 1) * (2 + 12 * 9 + 3)),
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     batch.free()
@@ -573,6 +574,10 @@ def main():
                          "format at every shape, one JSON line each; prefill: config 2, one line per format; "
                          "batched: config 3, sequences split over the ranks; ppl: config 4, windows split over "
                          "the ranks")
+    ap.add_argument("--batch-seqs", type=int, default=256,
+                    help="batched workload: sequences (config 3 has 256; fewer for profiling captures)")
+    ap.add_argument("--batch-steps", type=int, default=128,
+                    help="batched workload: greedy tokens per sequence (config 3 has 128)")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
