@@ -227,6 +227,23 @@ void *llmq_stream(const llmq_ctx *ctx);
 llmq_status llmq_model_set_mode(llmq_model *m, int mode);
 int llmq_model_mode(const llmq_model *m);
 
+/* ---- saved weights and GGUF files ------------------------------------------ */
+/* Replaces save_model (gpt2t.mojo:617-643): writes the model's weights, as
+ * converted, to path in the reference's saved-model layout (serialize.mojo
+ * encoding: 8-byte little-endian integers, length-prefixed strings): magic,
+ * version 1, the layer and head format names, the head, the 48 layer
+ * matrices (WeightMatrix.save), then the float32 tensors. 12-layer models
+ * with affine or dense weights. */
+llmq_status llmq_model_save(llmq_ctx *ctx, const llmq_model *m, const char *path);
+/* Replaces load_saved (gpt2t.mojo:667-698): a model from a file written by
+ * llmq_model_save or by the reference's --save, with the cache kv_kind and
+ * max_t positions. The model owns its weights (freed by llmq_model_free). */
+llmq_status llmq_model_load(llmq_ctx *ctx, const char *path, int kv_kind, int max_t, llmq_model **out);
+/* Replaces load_gguf (gpt2t.mojo:728-760) with GGUFFile (gguf.mojo:519-636):
+ * a llama.cpp GGUF file of GPT-2 124M, its matrices used as stored (tied
+ * token_embd head), the small tensors float32. The model owns its weights. */
+llmq_status llmq_model_load_gguf(llmq_ctx *ctx, const char *path, int kv_kind, int max_t, llmq_model **out);
+
 /* ---- perplexity harness ---------------------------------------------------- */
 /* Replaces score_rows (gpt2t.mojo:1042-1097) for rows [r0, r1) of a window's
  * logits ([rows][V], device): stats_dev[k * stride + (r - r0)] in float64 for

@@ -49,6 +49,9 @@ SIGNATURES = {
     "llmq_set_prefill_kernel": (I, [P, I]),
     "llmq_batch_create": (I, [P, P, I, I, P]),
     "llmq_score_rows": (I, [P, P, P, P, I, I, I, P, I]),
+    "llmq_model_save": (I, [P, P, C.c_char_p]),
+    "llmq_model_load": (I, [P, C.c_char_p, I, I, P]),
+    "llmq_model_load_gguf": (I, [P, C.c_char_p, I, I, P]),
     "llmq_batch_free": (I, [P]),
     "llmq_batch_generate": (I, [P, P, P, I, I, I, P]),
     "llmq_batch_generate_async": (I, [P, P, P, I, I, I, P]),

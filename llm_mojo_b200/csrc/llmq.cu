@@ -2,6 +2,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -89,7 +90,8 @@ struct llmq_model {
   unsigned long long *mega_ll = nullptr;
   int *mega_err = nullptr;
   unsigned mega_flag = 1;
-  bool float_only = false;  // float-activation formats: forward_all only
+  bool float_only = false;  // float-activation formats: the generic eager decode
+  std::vector<llmq_weight *> owned;  // weights a loader created for this model
   long long *prof = nullptr;  // [2][MK_PROF] when profiling
   const float *vec(int l, int which) const {
     static const int mult[8] = {0, 1, 2, 5, 6, 7, 8, 12};
@@ -1373,6 +1375,7 @@ llmq_status llmq_model_free(llmq_model *m) {
   if (m->mega_ll) cudaFree(m->mega_ll);
   if (m->mega_err) cudaFree(m->mega_err);
   if (m->prof) cudaFree(m->prof);
+  for (llmq_weight *w : m->owned) llmq_weight_free(w);
   delete m;
   return LLMQ_OK;
 }
@@ -1446,9 +1449,31 @@ static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0) {
 // ids into m->ids[0, steps), the last step's logits into m->logits (always
 // in the graph and eager modes; with want_logits in the persistent mode).
 // Asynchronous on the context's stream.
+// forward + greedy decode for the float-activation formats (generate,
+// gpt2t.mojo:942-980): the blocks for the T prompt tokens, the final
+// LayerNorm of the last row, the head for it and the argmax, then one token
+// at a time through the same one-token paths (dense gemv, GGUF dot_row).
+static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps) {
+  llmq_ctx *ctx = m->ctx;
+  cudaStream_t s = ctx->stream;
+  const int C = m->C;
+  llmq_status st;
+  for (int i = 0; i < steps; i++) {
+    const int n = i == 0 ? T : 1, p = i == 0 ? pos0 : pos0 + T + i - 1;
+    if ((st = enqueue_blocks(m, n, p, s)) != LLMQ_OK) return st;
+    layernorm_kernel<<<1, 256, C * 4, s>>>(m->xn, m->x + (size_t)(n - 1) * C, m->lnf_w(), m->lnf_b(), C);
+    CKL();
+    if ((st = llmq_head(ctx, m->head, m->xn, m->logits, 1, C, m->V)) != LLMQ_OK) return st;
+    argmax_rows_kernel<<<1, 256, 0, s>>>(m->logits, m->V, m->ids + i, 0, m->tokens, nullptr);
+    CKL();
+  }
+  return LLMQ_OK;
+}
+
 static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
+  if (m->float_only) return float_generation(m, T, pos0, steps);
   const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok;
   llmq_status st;
   if (T == 1) {
@@ -1475,8 +1500,6 @@ static llmq_status check_tokens(llmq_ctx *ctx, llmq_model *m, const int *tokens,
 
 llmq_status llmq_model_forward(llmq_ctx *ctx, llmq_model *m, const int *tokens, int T, int pos0, float *logits_dev,
                                int *argmax_host) {
-  if (m && m->float_only)
-    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !tokens || T <= 0 || pos0 < 0 || pos0 + T > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad tokens or positions");
   llmq_status st = check_tokens(ctx, m, tokens, T);
@@ -1514,8 +1537,6 @@ llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *toke
 }
 
 llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n_prompt, int steps, int *out_ids) {
-  if (m && m->float_only)
-    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !prompt || !out_ids || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
       n_prompt + steps - 1 > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
@@ -1535,8 +1556,6 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n
 
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
                                 int *ids_dev) {
-  if (m && m->float_only)
-    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
   if (!ctx || !m || !prompt_dev || !ids_dev || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
       n_prompt + steps - 1 > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
@@ -1802,7 +1821,7 @@ extern "C" {
 
 llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int max_prompt, llmq_batch **out) {
   if (m && m->float_only)
-    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation models run llmq_model_forward_all only");
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "batched decode runs the A16 formats");
   if (!ctx || !m || !out || max_seqs <= 0 || max_prompt <= 0 || max_prompt > m->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad batch arguments");
   if (m->kv->kind != LLMQ_KV_QUANT8) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "batched decode takes the QuantKV[8] cache");
@@ -1937,6 +1956,397 @@ llmq_status llmq_score_rows(llmq_ctx *ctx, const float *logits_dev, const float 
   CK(cudaSetDevice(ctx->device));
   score_rows_kernel<<<r1 - r0, 256, 0, ctx->stream>>>(logits_dev, base_dev, targets_dev, V, r0, stats_dev, stride);
   CKL();
+  return LLMQ_OK;
+}
+
+}  // extern "C"
+
+// ---- saved weights (.llmm) and GGUF files --------------------------------
+
+namespace {
+
+const char kSavedMagic[] = "llm_mojo GPT-2 124M weights";  // gpt2t.mojo:621
+constexpr long long kSavedVersion = 1;
+constexpr int kSavedLayers = 12;  // the reference's N_LAYER
+
+// The reference's --dtype names of the affine formats (gpt2t.mojo:1313-1346,
+// QuantMatrix.name at tensor.mojo:325-331): int{4,8}-{ch,g32,g64,g128}
+// [-sym][-a16]. group 0 = per channel.
+bool parse_affine_name(const std::string &n, int &bits, int &group, int &sym, int &a16) {
+  size_t p = 0;
+  auto next = [&](std::string &tok) {
+    if (p > n.size()) return false;
+    size_t q = n.find('-', p);
+    tok = n.substr(p, q == std::string::npos ? std::string::npos : q - p);
+    p = q == std::string::npos ? n.size() + 1 : q + 1;
+    return true;
+  };
+  std::string t;
+  if (!next(t) || (t != "int4" && t != "int8")) return false;
+  bits = t == "int4" ? 4 : 8;
+  if (!next(t)) return false;
+  if (t == "ch")
+    group = 0;
+  else if (t == "g32" || t == "g64" || t == "g128")
+    group = std::stoi(t.substr(1));
+  else
+    return false;
+  sym = a16 = 0;
+  while (p <= n.size() && next(t)) {
+    if (t == "sym")
+      sym = 1;
+    else if (t == "a16")
+      a16 = 1;
+    else
+      return false;
+  }
+  return true;
+}
+
+std::string affine_name(const llmq_weight *w) {
+  std::string n = std::string(w->bits == 4 ? "int4" : "int8") + "-" +
+                  (w->group == w->cols ? std::string("ch") : "g" + std::to_string(w->group));
+  if (w->sym) n += "-sym";
+  if (w->a16) n += "-a16";
+  return n;
+}
+
+int dense_code(const std::string &n) { return n == "f32" ? LLMQ_DENSE_F32 : n == "f16" ? LLMQ_DENSE_F16 : n == "bf16" ? LLMQ_DENSE_BF16 : -1; }
+
+struct ByteOut {
+  FILE *f;
+  bool ok = true;
+  void bytes(const void *p, size_t n) { ok = ok && (n == 0 || fwrite(p, 1, n, f) == n); }
+  void i64(long long v) {
+    unsigned char b[8];
+    for (int i = 0; i < 8; i++) b[i] = (unsigned char)((unsigned long long)v >> (8 * i));
+    bytes(b, 8);
+  }
+  void str(const std::string &s) {
+    i64((long long)s.size());
+    bytes(s.data(), s.size());
+  }
+};
+
+struct ByteIn {
+  FILE *f;
+  bool ok = true;
+  void bytes(void *p, size_t n) { ok = ok && (n == 0 || fread(p, 1, n, f) == n); }
+  long long i64() {
+    unsigned char b[8] = {0};
+    bytes(b, 8);
+    unsigned long long v = 0;
+    for (int i = 0; i < 8; i++) v |= (unsigned long long)b[i] << (8 * i);
+    return (long long)v;
+  }
+  std::string str() {
+    long long n = i64();
+    if (!ok || n < 0 || n > (1 << 20)) {
+      ok = false;
+      return "";
+    }
+    std::string s((size_t)n, '\0');
+    bytes(&s[0], (size_t)n);
+    return s;
+  }
+};
+
+// WeightMatrix.save (tensor.mojo:634-643 affine, :215-218 dense) of one device weight.
+llmq_status save_weight(llmq_ctx *ctx, ByteOut &o, const llmq_weight *w) {
+  if (w->kind == WK_AFFINE) {
+    const size_t nc = (size_t)w->rows * w->cols * w->bits / 8, ng = (size_t)w->rows * (w->cols / w->group);
+    std::vector<uint8_t> codes(nc), zp(ng);
+    std::vector<uint16_t> scale(ng);
+    CK(cudaMemcpy(codes.data(), w->codes, nc, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(scale.data(), w->scale, ng * 2, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(zp.data(), w->zp, ng, cudaMemcpyDeviceToHost));
+    o.i64(w->rows);
+    o.i64(w->cols);
+    o.i64(w->group);
+    o.bytes(codes.data(), nc);
+    o.bytes(scale.data(), ng * 2);
+    o.bytes(zp.data(), ng);
+  } else if (w->kind == WK_DENSE) {
+    const size_t n = (size_t)w->rows * w->row_bytes;
+    std::vector<uint8_t> data(n);
+    CK(cudaMemcpy(data.data(), w->codes, n, cudaMemcpyDeviceToHost));
+    o.i64(w->rows);
+    o.i64(w->cols);
+    o.bytes(data.data(), n);
+  } else {
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "GGUF matrices are saved as GGUF files already");
+  }
+  return LLMQ_OK;
+}
+
+// WeightMatrix.restore of the format called `name`, created on the device.
+llmq_status restore_weight(llmq_ctx *ctx, ByteIn &in, const std::string &name, llmq_weight **out) {
+  int bits, group, sym, a16;
+  const long long rows = in.i64(), cols = in.i64();
+  if (!in.ok || rows <= 0 || cols <= 0 || rows > (1 << 24) || cols > (1 << 24))
+    return fail(ctx, LLMQ_ERR_INVALID, "bad matrix shape in saved file");
+  if (parse_affine_name(name, bits, group, sym, a16)) {
+    const long long g = in.i64();
+    if (!in.ok || g != (group == 0 ? cols : group)) return fail(ctx, LLMQ_ERR_INVALID, "group size does not match " + name);
+    const size_t nc = (size_t)rows * cols * bits / 8, ng = (size_t)rows * (cols / g);
+    std::vector<uint8_t> codes(nc), zp(ng);
+    std::vector<uint16_t> scale(ng);
+    in.bytes(codes.data(), nc);
+    in.bytes(scale.data(), ng * 2);
+    in.bytes(zp.data(), ng);
+    if (!in.ok) return fail(ctx, LLMQ_ERR_INVALID, "unexpected end of saved file");
+    return llmq_weight_create_affine(ctx, bits, group, sym, a16, (int)rows, (int)cols, codes.data(), scale.data(),
+                                     zp.data(), out);
+  }
+  const int dt = dense_code(name);
+  if (dt < 0) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "unknown saved format " + name);
+  const size_t n = (size_t)rows * cols * (dt == LLMQ_DENSE_F32 ? 4 : 2);
+  std::vector<uint8_t> data(n);
+  in.bytes(data.data(), n);
+  if (!in.ok) return fail(ctx, LLMQ_ERR_INVALID, "unexpected end of saved file");
+  return llmq_weight_create_dense(ctx, dt, data.data(), (int)rows, (int)cols, out);
+}
+
+std::string weight_name(const llmq_weight *w) {
+  if (w->kind == WK_AFFINE) return affine_name(w);
+  if (w->kind == WK_DENSE) return w->rtype == RT_F32 ? "f32" : w->rtype == RT_F16 ? "f16" : "bf16";
+  return "gguf";
+}
+
+// The GGUF file (gguf.mojo:519-636): header, metadata (skipped but for
+// general.alignment), tensor index, data section.
+struct GgufTensor {
+  int type;
+  long long cols, rows, offset;
+};
+
+struct GgufFile {
+  std::vector<uint8_t> buf;
+  size_t data_start = 0;
+  std::map<std::string, GgufTensor> tensors;
+  std::string err;
+
+  uint32_t u32(size_t p) const { uint32_t v; std::memcpy(&v, &buf[p], 4); return v; }
+  uint64_t u64(size_t p) const { uint64_t v; std::memcpy(&v, &buf[p], 8); return v; }
+  bool has(size_t p, size_t n) const { return p <= buf.size() && n <= buf.size() - p; }
+
+  bool skip_value(uint32_t vt, size_t &p, int depth) {
+    static const int sizes[13] = {1, 1, 2, 2, 4, 4, 4, 1, 0, 0, 8, 8, 8};
+    if (depth > 4 || vt > 12) return false;
+    if (vt == 8) {  // string
+      if (!has(p, 8)) return false;
+      const uint64_t n = u64(p);
+      if (!has(p + 8, n)) return false;
+      p += 8 + n;
+      return true;
+    }
+    if (vt == 9) {  // array: element type, count, elements
+      if (!has(p, 12)) return false;
+      const uint32_t et = u32(p);
+      const uint64_t count = u64(p + 4);
+      p += 12;
+      for (uint64_t i = 0; i < count; i++)
+        if (!skip_value(et, p, depth + 1)) return false;
+      return true;
+    }
+    if (!has(p, sizes[vt])) return false;
+    p += sizes[vt];
+    return true;
+  }
+
+  bool read(const char *path) {
+    FILE *f = fopen(path, "rb");
+    if (!f) return err = std::string("cannot open ") + path, false;
+    fseek(f, 0, SEEK_END);
+    const long size = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    buf.resize(size > 0 ? (size_t)size : 0);
+    const bool got = size > 0 && fread(buf.data(), 1, buf.size(), f) == buf.size();
+    fclose(f);
+    if (!got || !has(0, 24)) return err = "short read", false;
+    if (u32(0) != 0x46554747u) return err = std::string(path) + " is not a GGUF file", false;
+    if (u32(4) < 2) return err = "GGUF version below 2", false;
+    const uint64_t n_tensors = u64(8), n_kv = u64(16);
+    size_t p = 24;
+    uint64_t alignment = 32;
+    for (uint64_t i = 0; i < n_kv; i++) {
+      if (!has(p, 8)) return err = "truncated metadata", false;
+      const uint64_t kn = u64(p);
+      if (!has(p + 8, kn + 4)) return err = "truncated metadata", false;
+      const std::string key((const char *)&buf[p + 8], kn);
+      p += 8 + kn;
+      const uint32_t vt = u32(p);
+      p += 4;
+      if (key == "general.alignment" && vt == 4 && has(p, 4)) alignment = u32(p);
+      if (!skip_value(vt, p, 0)) return err = "bad metadata value", false;
+    }
+    for (uint64_t i = 0; i < n_tensors; i++) {
+      if (!has(p, 8)) return err = "truncated tensor index", false;
+      const uint64_t nn = u64(p);
+      if (!has(p + 8, nn + 4)) return err = "truncated tensor index", false;
+      const std::string name((const char *)&buf[p + 8], nn);
+      p += 8 + nn;
+      const uint32_t nd = u32(p);
+      p += 4;
+      if (nd < 1 || nd > 4 || !has(p, 8 * nd + 12)) return err = "bad tensor dims", false;
+      long long cols = (long long)u64(p), rows = 1;
+      for (uint32_t d = 1; d < nd; d++) rows *= (long long)u64(p + 8 * d);
+      p += 8 * nd;
+      tensors[name] = GgufTensor{(int)u32(p), cols, rows, (long long)u64(p + 4)};
+      p += 12;
+    }
+    if (alignment == 0) alignment = 32;
+    data_start = (p + alignment - 1) / alignment * alignment;
+    return true;
+  }
+
+  // bytes of tensor t, or nullptr when it lies outside the file
+  const uint8_t *data(const GgufTensor &t, size_t bytes) const {
+    const size_t off = data_start + (size_t)t.offset;
+    return has(off, bytes) ? &buf[off] : nullptr;
+  }
+};
+
+size_t gguf_tensor_bytes(const GgufTensor &t) {
+  const int bs = rt_block_size(t.type), bb = rt_block_bytes(t.type);
+  if (bs <= 0 || bb <= 0 || t.cols % bs) return 0;
+  return (size_t)t.rows * (size_t)(t.cols / bs) * bb;
+}
+
+}  // namespace
+
+extern "C" {
+
+llmq_status llmq_model_save(llmq_ctx *ctx, const llmq_model *m, const char *path) {
+  if (!ctx || !m || !path) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  if (m->n_layer != kSavedLayers) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "saved models have 12 layers");
+  CK(cudaSetDevice(ctx->device));
+  CK(cudaStreamSynchronize(ctx->stream));
+  FILE *f = fopen(path, "wb");
+  if (!f) return fail(ctx, LLMQ_ERR_INVALID, std::string("cannot write ") + path);
+  ByteOut o{f};
+  o.str(kSavedMagic);
+  o.i64(kSavedVersion);
+  o.str(weight_name(m->mats[0]));
+  o.str(weight_name(m->head));
+  llmq_status st = save_weight(ctx, o, m->head);
+  for (size_t i = 0; st == LLMQ_OK && i < m->mats.size(); i++) st = save_weight(ctx, o, m->mats[i]);
+  if (st == LLMQ_OK) {
+    const size_t n = (size_t)m->n_layer * 13 * m->C + (size_t)1024 * m->C + 2 * m->C;
+    std::vector<float> small(n);
+    cudaError_t e = cudaMemcpy(small.data(), m->small, n * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) st = fail(ctx, LLMQ_ERR_CUDA, cudaGetErrorString(e));
+    o.i64((long long)n);
+    o.bytes(small.data(), n * 4);
+  }
+  if (fclose(f) != 0) o.ok = false;
+  if (st == LLMQ_OK && !o.ok) st = fail(ctx, LLMQ_ERR_INVALID, std::string("write to ") + path + " failed");
+  return st;
+}
+
+llmq_status llmq_model_load(llmq_ctx *ctx, const char *path, int kv_kind, int max_t, llmq_model **out) {
+  if (!ctx || !path || !out) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  *out = nullptr;
+  FILE *f = fopen(path, "rb");
+  if (!f) return fail(ctx, LLMQ_ERR_INVALID, std::string("cannot open ") + path);
+  ByteIn in{f};
+  std::vector<llmq_weight *> ws;
+  auto cleanup = [&](llmq_status st) {
+    fclose(f);
+    for (llmq_weight *w : ws) llmq_weight_free(w);
+    return st;
+  };
+  const std::string magic = in.str();
+  if (!in.ok || magic != kSavedMagic) return cleanup(fail(ctx, LLMQ_ERR_INVALID, std::string(path) + " is not a saved llm_mojo model"));
+  if (in.i64() != kSavedVersion) return cleanup(fail(ctx, LLMQ_ERR_UNSUPPORTED, "unsupported saved-model version"));
+  const std::string wname = in.str(), hname = in.str();
+  if (!in.ok) return cleanup(fail(ctx, LLMQ_ERR_INVALID, "truncated header"));
+  llmq_weight *w = nullptr;
+  llmq_status st = restore_weight(ctx, in, hname, &w);
+  if (st != LLMQ_OK) return cleanup(st);
+  ws.push_back(w);
+  for (int i = 0; i < 4 * kSavedLayers; i++) {
+    if ((st = restore_weight(ctx, in, wname, &w)) != LLMQ_OK) return cleanup(st);
+    ws.push_back(w);
+  }
+  const long long n = in.i64();
+  const long long want = (long long)kSavedLayers * 13 * 768 + 1024LL * 768 + 2 * 768;
+  if (!in.ok || n != want) return cleanup(fail(ctx, LLMQ_ERR_INVALID, "unexpected size of the float32 tensors"));
+  std::vector<float> small((size_t)n);
+  in.bytes(small.data(), (size_t)n * 4);
+  if (!in.ok) return cleanup(fail(ctx, LLMQ_ERR_INVALID, "unexpected end of saved file"));
+  llmq_model *m = nullptr;
+  if ((st = llmq_model_create(ctx, kSavedLayers, ws.data() + 1, ws[0], small.data(), kv_kind, max_t, &m)) != LLMQ_OK)
+    return cleanup(st);
+  fclose(f);
+  m->owned = ws;
+  *out = m;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_model_load_gguf(llmq_ctx *ctx, const char *path, int kv_kind, int max_t, llmq_model **out) {
+  if (!ctx || !path || !out) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
+  *out = nullptr;
+  GgufFile g;
+  if (!g.read(path)) return fail(ctx, LLMQ_ERR_INVALID, g.err);
+  std::vector<llmq_weight *> ws;
+  auto cleanup = [&](llmq_status st) {
+    for (llmq_weight *w : ws) llmq_weight_free(w);
+    return st;
+  };
+  auto matrix = [&](const std::string &name, long long rows, long long cols, llmq_weight **w) -> llmq_status {
+    auto it = g.tensors.find(name);
+    if (it == g.tensors.end()) return fail(ctx, LLMQ_ERR_INVALID, "tensor not in GGUF file: " + name);
+    const GgufTensor &t = it->second;
+    if (t.rows != rows || t.cols != cols) return fail(ctx, LLMQ_ERR_INVALID, name + " has an unexpected shape");
+    const size_t bytes = gguf_tensor_bytes(t);
+    const uint8_t *d = bytes ? g.data(t, bytes) : nullptr;
+    if (!d) return fail(ctx, LLMQ_ERR_UNSUPPORTED, name + ": unsupported format or outside the file");
+    return llmq_weight_create_gguf(ctx, t.type, d, (int)rows, (int)cols, w);
+  };
+  auto f32 = [&](const std::string &name, size_t n, float *dst) -> llmq_status {
+    auto it = g.tensors.find(name);
+    if (it == g.tensors.end()) return fail(ctx, LLMQ_ERR_INVALID, "tensor not in GGUF file: " + name);
+    const GgufTensor &t = it->second;
+    const uint8_t *d = g.data(t, n * 4);
+    if (t.type != RT_F32 || (size_t)(t.rows * t.cols) != n || !d)
+      return fail(ctx, LLMQ_ERR_INVALID, name + " is not the expected float32 tensor");
+    std::memcpy(dst, d, n * 4);
+    return LLMQ_OK;
+  };
+  const int C = 768, L = 12;
+  static const char *mat_names[4] = {"attn_qkv.weight", "attn_output.weight", "ffn_up.weight", "ffn_down.weight"};
+  static const char *vec_names[8] = {"attn_norm.weight", "attn_norm.bias", "attn_qkv.bias", "attn_output.bias",
+                                     "ffn_norm.weight", "ffn_norm.bias", "ffn_up.bias", "ffn_down.bias"};
+  static const int vec_lens[8] = {1, 1, 3, 1, 1, 1, 4, 1};
+  static const long long outs[4] = {3 * C, C, 4 * C, C}, ins[4] = {C, C, C, 4 * C};
+  if (g.tensors.count("output.weight")) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "untied output heads are not supported");
+  llmq_weight *w = nullptr;
+  llmq_status st = matrix("token_embd.weight", 50257, C, &w);
+  if (st != LLMQ_OK) return cleanup(st);
+  ws.push_back(w);
+  std::vector<float> small((size_t)L * 13 * C + 1024 * C + 2 * C);
+  size_t off = 0;
+  for (int l = 0; l < L; l++) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    for (int i = 0; i < 4; i++) {
+      if ((st = matrix(pre + mat_names[i], outs[i], ins[i], &w)) != LLMQ_OK) return cleanup(st);
+      ws.push_back(w);
+    }
+    for (int i = 0; i < 8; i++) {
+      if ((st = f32(pre + vec_names[i], (size_t)vec_lens[i] * C, small.data() + off)) != LLMQ_OK) return cleanup(st);
+      off += (size_t)vec_lens[i] * C;
+    }
+  }
+  if ((st = f32("position_embd.weight", (size_t)1024 * C, small.data() + off)) != LLMQ_OK) return cleanup(st);
+  off += (size_t)1024 * C;
+  if ((st = f32("output_norm.weight", C, small.data() + off)) != LLMQ_OK) return cleanup(st);
+  if ((st = f32("output_norm.bias", C, small.data() + off + C)) != LLMQ_OK) return cleanup(st);
+  llmq_model *m = nullptr;
+  if ((st = llmq_model_create(ctx, L, ws.data() + 1, ws[0], small.data(), kv_kind, max_t, &m)) != LLMQ_OK)
+    return cleanup(st);
+  m->owned = ws;
+  *out = m;
   return LLMQ_OK;
 }
 

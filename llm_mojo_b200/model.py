@@ -201,6 +201,14 @@ class FloatModel:
         check(lib().llmq_model_forward_all(self.ctx.h, self.h, t.ctypes.data_as(C.c_void_p), t.size,
                                            C.c_void_p(logits.data_ptr())), self.ctx.h)
 
+    def forward(self, tokens, pos0: int, logits=None) -> int:
+        """The blocks for tokens at pos0.., the last token's logits and argmax
+        (the one-token paths for later tokens, as generate uses them)."""
+        return Model.forward(self, tokens, pos0, logits)
+
+    def generate(self, prompt, steps: int) -> np.ndarray:
+        return Model.generate(self, prompt, steps)
+
     def free(self):
         if getattr(self, "h", None):
             lib().llmq_model_free(self.h)
@@ -215,3 +223,49 @@ class FloatModel:
             self.free()
         except Exception:
             pass
+
+
+class LoadedModel:
+    """A model read from a saved-weights file (load_saved, gpt2t.mojo:667-698)
+    or a GGUF file (load_gguf, gpt2t.mojo:728-760); the library owns its
+    weights. kv: 'int8', 'intattn', 'f32' or 'bf16'."""
+
+    V = 50257
+
+    def __init__(self, ctx: Context, path: str, kv: str = "int8", max_t: int = synth.MAX_T, gguf: bool = False):
+        from ._lib import KV_BF16, KV_F32
+
+        kind = {"int8": KV_QUANT8, "intattn": KV_INTATTN, "f32": KV_F32, "bf16": KV_BF16}[kv]
+        self.ctx = ctx
+        h = C.c_void_p()
+        fn = lib().llmq_model_load_gguf if gguf else lib().llmq_model_load
+        check(fn(ctx.h, path.encode(), kind, max_t, C.byref(h)), ctx.h)
+        self.h = h
+
+    def forward(self, tokens, pos0: int, logits=None) -> int:
+        return Model.forward(self, tokens, pos0, logits)
+
+    def forward_all(self, tokens, logits) -> None:
+        return Model.forward_all(self, tokens, logits)
+
+    def generate(self, prompt, steps: int) -> np.ndarray:
+        return Model.generate(self, prompt, steps)
+
+    def save(self, path: str):
+        check(lib().llmq_model_save(self.ctx.h, self.h, path.encode()), self.ctx.h)
+
+    def free(self):
+        if getattr(self, "h", None):
+            lib().llmq_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+def save_model(model, path: str):
+    """save_model (gpt2t.mojo:617-643): the model's converted weights to path."""
+    check(lib().llmq_model_save(model.ctx.h, model.h, path.encode()), model.ctx.h)
