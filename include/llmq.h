@@ -198,6 +198,30 @@ llmq_status llmq_generate(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, 
  * llmq_generate. */
 llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_dev, int n_prompt, int steps,
                                 int *ids_dev);
+
+/* ---- sampling (gpt2t.mojo:775-834) ---- */
+/* Rng(seed) (gpt2t.mojo:775-781): the xorshift64* state seed *
+ * 0x9E3779B97F4A7C15 + 1, wrapping. */
+unsigned long long llmq_rng_init(long long seed);
+/* top_k (gpt2t.mojo:800-815): ids of the k largest of logits_dev[0, V) in
+ * descending order, an equal logit ordered by the lower id first; k <= 0 or
+ * k >= V gives all V. Writes min(k, V) ids (V for k <= 0) to ids_dev.
+ * Asynchronous on the context's stream. V <= 2^24. */
+llmq_status llmq_top_k(llmq_ctx *ctx, const float *logits_dev, int V, int k, int *ids_dev);
+/* sample (gpt2t.mojo:818-834): temperature <= 0 is the argmax (first index
+ * of the largest logit; *rng_dev untouched); otherwise one draw from the top
+ * k (k <= 0: all V) with weights exp((logit - max) / temperature), summed in
+ * order in float32, advancing the device Rng state *rng_dev. The id goes to
+ * *id_dev. Asynchronous on the context's stream. V <= 2^24. */
+llmq_status llmq_sample(llmq_ctx *ctx, const float *logits_dev, int V, float temperature, int k,
+                        unsigned long long *rng_dev, int *id_dev);
+/* generate (gpt2t.mojo:965-980) with sample in place of the argmax, without
+ * the stop at EOT: `steps` ids into out_ids_host; *rng_state (host) is the
+ * Rng state, read before and written back after. temperature <= 0 is
+ * llmq_generate. The draws run on the device after each head; the decode
+ * steps are CUDA graph launches (or eager in LLMQ_MODE_EAGER). */
+llmq_status llmq_generate_sampled(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, int n_prompt, int steps,
+                                  float temperature, int k, unsigned long long *rng_state, int *out_ids_host);
 /* Per-operation timers of the persistent decode kernel, as the reference's
  * --profile (gpt2t.mojo:121-142, print_profile :461-483): with profiling on,
  * CTA 0 (which also runs head 0's attention) and CTA grid/2 add the SM

@@ -68,6 +68,10 @@ SIGNATURES = {
     "llmq_model_forward": (I, [P, P, P, I, I, P, P]),
     "llmq_model_forward_all": (I, [P, P, P, I, P]),
     "llmq_generate": (I, [P, P, P, I, I, P]),
+    "llmq_rng_init": (C.c_uint64, [C.c_int64]),
+    "llmq_top_k": (I, [P, P, I, I, P]),
+    "llmq_sample": (I, [P, P, I, C.c_float, I, P, P]),
+    "llmq_generate_sampled": (I, [P, P, P, I, I, C.c_float, I, P, P]),
     "llmq_model_set_mode": (I, [P, I]),
     "llmq_model_mode": (I, [P]),
     "llmq_generate_async": (I, [P, P, P, I, I, P]),

@@ -15,6 +15,7 @@
 #include "gemv_float.cuh"
 #include "mega.cuh"
 #include "prefill_a16.cuh"
+#include "sample.cuh"
 #include "tc_gemm.cuh"
 
 using namespace llmq;
@@ -33,6 +34,13 @@ struct llmq_ctx {
   int prefill_kernel = LLMQ_PREFILL_AUTO;
   int *tc_err = nullptr;         // device error code of the tcgen05 GEMM (a wait that gave up)
   bool tc_used = false;          // a tcgen05 GEMM ran since the last check
+  // sampling scratch (device, grown on demand): sort keys, weights, chunk
+  // candidates, the Rng state of llmq_generate_sampled
+  unsigned long long *samp_keys = nullptr;
+  float *samp_p = nullptr;
+  unsigned long long *samp_cand = nullptr;
+  unsigned long long *samp_rng = nullptr;
+  int samp_n = 0;
 };
 
 enum { WK_AFFINE = 0, WK_GGUF = 1, WK_DENSE = 2 };
@@ -250,6 +258,9 @@ cudaError_t configure_kernels() {
   tcs((const void *)tc_gemm_a16_kernel<true, 32>);
   tcs((const void *)tc_gemm_a16_kernel<false, 64>);
   tcs((const void *)tc_gemm_a16_kernel<false, 32>);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)merge_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)merge_smem(kMergeCap));
   return e;
 }
 }  // namespace
@@ -318,6 +329,8 @@ llmq_status llmq_destroy(llmq_ctx *ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->state) cudaFree(ctx->state);
   if (ctx->tc_err) cudaFree(ctx->tc_err);
+  for (void *q : {(void *)ctx->samp_keys, (void *)ctx->samp_p, (void *)ctx->samp_cand, (void *)ctx->samp_rng})
+    if (q) cudaFree(q);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
   return LLMQ_OK;
@@ -1393,6 +1406,73 @@ llmq_status llmq_model_set_mode(llmq_model *m, int mode) {
 
 int llmq_model_mode(const llmq_model *m) { return m ? m->mode : -1; }
 
+// ---- sampling (gpt2t.mojo:775-834) ----
+
+static int pow2_at_least(int v) {
+  int n = 1;
+  while (n < v) n <<= 1;
+  return n;
+}
+
+constexpr int kSampleMaxV = 1 << 24;
+
+static llmq_status sample_scratch(llmq_ctx *ctx, int V) {
+  const int n = std::max(pow2_at_least(V), kSortChunk);
+  if (!ctx->samp_cand) CK(cudaMalloc(&ctx->samp_cand, sizeof(unsigned long long) * kMergeCap));
+  if (!ctx->samp_rng) CK(cudaMalloc(&ctx->samp_rng, sizeof(unsigned long long)));
+  if (n <= ctx->samp_n) return LLMQ_OK;
+  CK(cudaStreamSynchronize(ctx->stream));
+  if (ctx->samp_keys) cudaFree(ctx->samp_keys);
+  if (ctx->samp_p) cudaFree(ctx->samp_p);
+  ctx->samp_keys = nullptr;
+  ctx->samp_p = nullptr;
+  ctx->samp_n = 0;
+  CK(cudaMalloc(&ctx->samp_keys, sizeof(unsigned long long) * n));
+  CK(cudaMalloc(&ctx->samp_p, sizeof(float) * n));
+  ctx->samp_n = n;
+  return LLMQ_OK;
+}
+
+// A draw from logits[0, V) into `o` (topk_ids == nullptr), or the top-k ids
+// into topk_ids. k <= 0 or k >= V means all V (sample: `k if k > 0 else V`;
+// top_k stops at V). The scratch must hold V keys (sample_scratch).
+static llmq_status enqueue_sample(llmq_ctx *ctx, const float *logits, int V, float temperature, int k,
+                                  unsigned long long *rng, SampleOut o, int *topk_ids, cudaStream_t s) {
+  const int kk = (k > 0 && k < V) ? k : V;
+  const int chunks = (V + kSortChunk - 1) / kSortChunk;
+  if (kk <= kTopkSmall && (long long)chunks * kk <= kMergeCap) {
+    const int n_cand = chunks * kk, n_pad = std::max(pow2_at_least(n_cand), 2);
+    sort_chunk_kernel<<<chunks, kSortThreads, 0, s>>>(logits, V, nullptr, 2, kSortChunk, 1, ctx->samp_cand, kk);
+    CKL();
+    merge_draw_kernel<<<1, kSortThreads, merge_smem(n_pad), s>>>(ctx->samp_cand, n_cand, n_pad, kk, logits,
+                                                                   temperature, rng, o, topk_ids);
+    CKL();
+    return LLMQ_OK;
+  }
+  const int n = std::max(pow2_at_least(V), kSortChunk);
+  unsigned long long *keys = ctx->samp_keys;
+  sort_chunk_kernel<<<n / kSortChunk, kSortThreads, 0, s>>>(logits, V, keys, 2, kSortChunk, 0, nullptr, 0);
+  CKL();
+  for (int sz = 2 * kSortChunk; sz <= n; sz <<= 1) {
+    for (int j = sz / 2; j >= kSortChunk; j >>= 1) {
+      bitonic_global_kernel<<<std::min(n / 512, 4 * ctx->num_sms), 256, 0, s>>>(keys, n, sz, j);
+      CKL();
+    }
+    sort_chunk_kernel<<<n / kSortChunk, kSortThreads, 0, s>>>(nullptr, V, keys, sz, sz, 0, nullptr, 0);
+    CKL();
+  }
+  sorted_draw_kernel<<<1, kSortThreads, 0, s>>>(keys, kk, logits, temperature, ctx->samp_p, rng, o, topk_ids);
+  CKL();
+  return LLMQ_OK;
+}
+
+// What generate_sampled draws with: temperature > 0, k, the device Rng state.
+struct SampleSpec {
+  float temperature;
+  int k;
+  unsigned long long *rng;
+};
+
 static llmq_status run_decode_step(llmq_model *m) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
@@ -1453,7 +1533,7 @@ static llmq_status run_prompt_tail(llmq_model *m, int T, int pos0) {
 // gpt2t.mojo:942-980): the blocks for the T prompt tokens, the final
 // LayerNorm of the last row, the head for it and the argmax, then one token
 // at a time through the same one-token paths (dense gemv, GGUF dot_row).
-static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps) {
+static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps, const SampleSpec *sp) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
   const int C = m->C;
@@ -1464,31 +1544,51 @@ static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps) {
     layernorm_kernel<<<1, 256, C * 4, s>>>(m->xn, m->x + (size_t)(n - 1) * C, m->lnf_w(), m->lnf_b(), C);
     CKL();
     if ((st = llmq_head(ctx, m->head, m->xn, m->logits, 1, C, m->V)) != LLMQ_OK) return st;
+    if (sp) {
+      st = enqueue_sample(ctx, m->logits, m->V, sp->temperature, sp->k, sp->rng,
+                          SampleOut{m->ids + i, m->tokens, nullptr, nullptr, nullptr}, nullptr, s);
+      if (st != LLMQ_OK) return st;
+      continue;
+    }
     argmax_rows_kernel<<<1, 256, 0, s>>>(m->logits, m->V, m->ids + i, 0, m->tokens, nullptr);
     CKL();
   }
   return LLMQ_OK;
 }
 
-static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits) {
+// With a SampleSpec every head's argmax is replaced by a draw: the head
+// still writes the logits, the draw overwrites the id and the next token
+// (the persistent kernel, whose head reduces to the argmax in place, is not
+// used then).
+static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits,
+                                  const SampleSpec *sp = nullptr) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
-  if (m->float_only) return float_generation(m, T, pos0, steps);
-  const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok;
+  if (m->float_only) return float_generation(m, T, pos0, steps, sp);
+  const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok && !sp;
+  const SampleOut so{nullptr, nullptr, &m->state->token, &m->state->step, m->ids};
+  auto draw = [&]() -> llmq_status {
+    return sp ? enqueue_sample(ctx, m->logits, m->V, sp->temperature, sp->k, sp->rng, so, nullptr, s) : LLMQ_OK;
+  };
   llmq_status st;
   if (T == 1) {
     if (pers) return run_mega(m, m->tokens, pos0, steps, m->ids, want_logits ? m->logits : nullptr);
     init_state_kernel<<<1, 1, 0, s>>>(m->state, m->tokens, pos0);
     CKL();
-    for (int i = 0; i < steps; i++)
+    for (int i = 0; i < steps; i++) {
       if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+      if ((st = draw()) != LLMQ_OK) return st;
+    }
     return LLMQ_OK;
   }
   if ((st = run_prompt_tail(m, T, pos0)) != LLMQ_OK) return st;
+  if ((st = draw()) != LLMQ_OK) return st;
   if (steps == 1) return LLMQ_OK;
   if (pers) return run_mega(m, &m->state->token, pos0 + T, steps - 1, m->ids + 1, want_logits ? m->logits : nullptr);
-  for (int i = 1; i < steps; i++)
+  for (int i = 1; i < steps; i++) {
     if ((st = run_decode_step(m)) != LLMQ_OK) return st;
+    if ((st = draw()) != LLMQ_OK) return st;
+  }
   return LLMQ_OK;
 }
 
@@ -1565,6 +1665,58 @@ llmq_status llmq_generate_async(llmq_ctx *ctx, llmq_model *m, const int *prompt_
   llmq_status st = run_generation(m, n_prompt, 0, steps, false);
   if (st != LLMQ_OK) return st;
   CK(cudaMemcpyAsync(ids_dev, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToDevice, s));
+  return LLMQ_OK;
+}
+
+unsigned long long llmq_rng_init(long long seed) { return (unsigned long long)seed * 0x9E3779B97F4A7C15ull + 1ull; }
+
+llmq_status llmq_top_k(llmq_ctx *ctx, const float *logits_dev, int V, int k, int *ids_dev) {
+  if (!ctx || !logits_dev || !ids_dev || V <= 0 || V > kSampleMaxV) return fail(ctx, LLMQ_ERR_INVALID, "bad top_k");
+  CK(cudaSetDevice(ctx->device));
+  llmq_status st = sample_scratch(ctx, V);
+  if (st != LLMQ_OK) return st;
+  return enqueue_sample(ctx, logits_dev, V, 1.0f, k, nullptr, SampleOut{}, ids_dev, ctx->stream);
+}
+
+llmq_status llmq_sample(llmq_ctx *ctx, const float *logits_dev, int V, float temperature, int k,
+                        unsigned long long *rng_dev, int *id_dev) {
+  if (!ctx || !logits_dev || !rng_dev || !id_dev || V <= 0 || V > kSampleMaxV)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad sample arguments");
+  CK(cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->stream;
+  if (temperature <= 0) {
+    argmax_rows_kernel<<<1, 256, 0, s>>>(logits_dev, V, id_dev, 0, id_dev, nullptr);
+    CKL();
+    return LLMQ_OK;
+  }
+  llmq_status st = sample_scratch(ctx, V);
+  if (st != LLMQ_OK) return st;
+  return enqueue_sample(ctx, logits_dev, V, temperature, k, rng_dev, SampleOut{id_dev, nullptr, nullptr, nullptr,
+                                                                              nullptr}, nullptr, s);
+}
+
+llmq_status llmq_generate_sampled(llmq_ctx *ctx, llmq_model *m, const int *prompt, int n_prompt, int steps,
+                                  float temperature, int k, unsigned long long *rng_state, int *out_ids) {
+  if (!rng_state) return fail(ctx, LLMQ_ERR_INVALID, "null rng state");
+  if (temperature <= 0) return llmq_generate(ctx, m, prompt, n_prompt, steps, out_ids);
+  if (!ctx || !m || !prompt || !out_ids || n_prompt <= 0 || steps <= 0 || steps > m->max_ids ||
+      n_prompt + steps - 1 > m->max_t)
+    return fail(ctx, LLMQ_ERR_INVALID, "bad prompt or step count");
+  llmq_status st = check_tokens(ctx, m, prompt, n_prompt);
+  if (st != LLMQ_OK) return st;
+  CK(cudaSetDevice(ctx->device));
+  cudaStream_t s = ctx->stream;
+  CK(cudaStreamSynchronize(s));
+  if ((st = sample_scratch(ctx, m->V)) != LLMQ_OK) return st;
+  CK(cudaMemcpyAsync(ctx->samp_rng, rng_state, sizeof(unsigned long long), cudaMemcpyHostToDevice, s));
+  CK(cudaMemcpyAsync(m->tokens, prompt, (size_t)n_prompt * 4, cudaMemcpyHostToDevice, s));
+  const SampleSpec sp{temperature, k, ctx->samp_rng};
+  if ((st = run_generation(m, n_prompt, 0, steps, false, &sp)) != LLMQ_OK) return st;
+  CK(cudaMemcpyAsync(m->ids_host, m->ids, (size_t)steps * 4, cudaMemcpyDeviceToHost, s));
+  CK(cudaMemcpyAsync(rng_state, ctx->samp_rng, sizeof(unsigned long long), cudaMemcpyDeviceToHost, s));
+  CK(cudaStreamSynchronize(s));
+  if ((st = mega_check(m)) != LLMQ_OK) return st;
+  std::memcpy(out_ids, m->ids_host, (size_t)steps * 4);
   return LLMQ_OK;
 }
 

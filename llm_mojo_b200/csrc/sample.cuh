@@ -1,0 +1,180 @@
+// sample.cuh -- top-k / temperature sampling on the device (gpt2t.mojo:775-834).
+//
+// The reference keeps the k largest logits in descending order (an equal
+// later logit never passes an earlier one), weights them by
+// exp((logit - max) / temperature), sums the weights in that order in
+// float32, draws r = uniform() * total from a xorshift64* state and walks the
+// list subtracting weights until r <= 0.
+//
+// Here every logit becomes one 64-bit key, (descending order of the value)
+// << 32 | id, so the ascending order of the keys is the reference's order of
+// candidates and all keys differ. Sorting is a bitonic network: chunks of
+// kSortChunk keys sort in shared memory, the levels above a chunk take one
+// global compare-exchange launch per stride plus a shared-memory pass for the
+// strides inside a chunk.
+//   k <= kTopkSmall and (chunks x k) <= kMergeCap: every chunk keeps its first
+//     k keys, one CTA sorts those candidates and draws (two launches);
+//   otherwise: the whole padded key array is sorted, one CTA draws.
+// The draw is one thread: the float32 sum and the subtraction walk are
+// sequential chains in the reference's order (the weights are computed by the
+// whole CTA first).
+#pragma once
+
+#include "common.cuh"
+
+namespace llmq {
+
+constexpr int kSortChunk = 4096;    // keys one CTA sorts in shared memory (32 KB)
+constexpr int kSortThreads = 1024;
+constexpr int kTopkSmall = 1024;    // largest k of the two-launch path
+constexpr int kMergeCap = 16384;    // candidates the merging CTA sorts (128 KB)
+
+typedef unsigned long long u64;
+
+// Where a drawn id goes: *id, *id2, and with a decode state ids[step - 1] and
+// the state's next token (the head's fused argmax already advanced step).
+struct SampleOut {
+  int *id;
+  int *id2;
+  int *state_token;
+  const int *state_step;
+  int *ids;
+};
+
+__device__ __forceinline__ u64 sample_key(float v, int id) {
+  unsigned u = __float_as_uint(v);
+  if ((u & 0x7fffffffu) == 0) u = 0;  // -0 and +0 compare equal in the reference
+  const unsigned asc = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((u64)(~asc) << 32) | (unsigned)id;
+}
+
+__device__ __forceinline__ int key_id(u64 k) { return (int)(unsigned)(k & 0xffffffffull); }
+
+// Bitonic levels s = s_lo, 2 s_lo, ..., s_hi over the n keys in shared memory
+// whose first key has global index base; strides from min(s, n) / 2 down to 1.
+// Direction of a pair: ascending when (global index & s) == 0; with all_asc
+// every level s >= n sorts ascending (each chunk sorted on its own).
+__device__ void bitonic_levels(u64 *k, int n, int base, int s_lo, int s_hi, bool all_asc) {
+  for (int s = s_lo; s <= s_hi; s <<= 1) {
+    for (int j = min(s, n) >> 1; j > 0; j >>= 1) {
+      for (int p = threadIdx.x; p < n / 2; p += blockDim.x) {
+        const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1)), l = i + j;
+        const bool asc = (((base + i) & s) == 0) || (all_asc && s >= n);
+        const u64 a = k[i], b = k[l];
+        if ((a > b) == asc) {
+          k[i] = b;
+          k[l] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// One chunk of kSortChunk keys: built from the logits (logits != nullptr,
+// keys past V are all ones) or read from keys; levels [s_lo, s_hi]; written
+// back to keys, or its first kk keys to cand[chunk * kk ..].
+__global__ void __launch_bounds__(kSortThreads)
+    sort_chunk_kernel(const float *logits, int V, u64 *keys, int s_lo, int s_hi, int all_asc, u64 *cand, int kk) {
+  __shared__ u64 sk[kSortChunk];
+  const int base = blockIdx.x * kSortChunk;
+  for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) {
+    const int g = base + i;
+    sk[i] = logits ? (g < V ? sample_key(logits[g], g) : ~0ull) : keys[g];
+  }
+  __syncthreads();
+  bitonic_levels(sk, kSortChunk, base, s_lo, s_hi, all_asc != 0);
+  if (cand) {
+    for (int i = threadIdx.x; i < kk; i += blockDim.x) cand[(size_t)blockIdx.x * kk + i] = sk[i];
+  } else {
+    for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) keys[base + i] = sk[i];
+  }
+}
+
+// One stride j >= kSortChunk of level s over the n global keys.
+__global__ void bitonic_global_kernel(u64 *keys, int n, int s, int j) {
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < n / 2; p += gridDim.x * blockDim.x) {
+    const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1)), l = i + j;
+    const bool asc = (i & s) == 0;
+    const u64 a = keys[i], b = keys[l];
+    if ((a > b) == asc) {
+      keys[i] = b;
+      keys[l] = a;
+    }
+  }
+}
+
+__device__ __forceinline__ float rng_uniform(u64 *state) {
+  u64 s = *state;
+  s ^= s >> 12;
+  s ^= s << 25;
+  s ^= s >> 27;
+  *state = s;
+  return (float)((s * 0x2545F4914F6CDD1Dull) >> 40) / (float)(1 << 24);
+}
+
+// The draw over the first k sorted keys; p holds k floats (shared or global).
+__device__ void draw_sorted(const u64 *sorted, int k, const float *logits, float temperature, float *p, u64 *rng,
+                            SampleOut o) {
+  const float mx = logits[key_id(sorted[0])];
+  for (int i = threadIdx.x; i < k; i += blockDim.x) p[i] = lm_expf((logits[key_id(sorted[i])] - mx) / temperature);
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  float total = 0.0f;
+  int i = 0;
+  for (; i + 8 <= k; i += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; u++) v[u] = p[i + u];
+#pragma unroll
+    for (int u = 0; u < 8; u++) total += v[u];
+  }
+  for (; i < k; i++) total += p[i];
+  float r = rng_uniform(rng) * total;
+  int pick = k - 1;
+  for (i = 0; i < k; i++) {
+    r -= p[i];
+    if (r <= 0.0f) {
+      pick = i;
+      break;
+    }
+  }
+  const int id = key_id(sorted[pick]);
+  if (o.id) *o.id = id;
+  if (o.id2) *o.id2 = id;
+  if (o.ids) o.ids[*o.state_step - 1] = id;
+  if (o.state_token) *o.state_token = id;
+}
+
+// n_cand chunk candidates (padded to n_pad, a power of two <= kMergeCap):
+// sort, then draw from the first k.
+__global__ void __launch_bounds__(kSortThreads)
+    merge_draw_kernel(const u64 *cand, int n_cand, int n_pad, int k, const float *logits, float temperature, u64 *rng,
+                      SampleOut o, int *topk_ids) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  u64 *sk = reinterpret_cast<u64 *>(smem);
+  float *p = reinterpret_cast<float *>(sk + n_pad);
+  for (int i = threadIdx.x; i < n_pad; i += blockDim.x) sk[i] = i < n_cand ? cand[i] : ~0ull;
+  __syncthreads();
+  bitonic_levels(sk, n_pad, 0, 2, n_pad, false);
+  if (topk_ids) {
+    for (int i = threadIdx.x; i < k; i += blockDim.x) topk_ids[i] = key_id(sk[i]);
+    return;
+  }
+  draw_sorted(sk, k, logits, temperature, p, rng, o);
+}
+
+// The draw (or the top-k ids) from a fully sorted global key array.
+__global__ void __launch_bounds__(kSortThreads)
+    sorted_draw_kernel(const u64 *keys, int k, const float *logits, float temperature, float *p, u64 *rng,
+                       SampleOut o, int *topk_ids) {
+  if (topk_ids) {
+    for (int i = threadIdx.x; i < k; i += blockDim.x) topk_ids[i] = key_id(keys[i]);
+    return;
+  }
+  draw_sorted(keys, k, logits, temperature, p, rng, o);
+}
+
+inline size_t merge_smem(int n_pad) { return (size_t)n_pad * 8 + (size_t)kTopkSmall * 4; }
+
+}  // namespace llmq

@@ -66,6 +66,48 @@ def head_argmax(ctx: Context, w: QuantMatrix, h, logits, argmax):
     ctx.sync()
 
 
+class Rng:
+    """Rng (gpt2t.mojo:775-789) whose xorshift64* state lives on the device
+    (a one-element int64 CUDA tensor holding the uint64 bits), advanced by
+    every draw of sample()."""
+
+    def __init__(self, seed: int = 1337):
+        import torch
+
+        s = int(lib().llmq_rng_init(seed))
+        self.state = torch.tensor([s - (1 << 64) if s >= 1 << 63 else s], dtype=torch.int64, device="cuda")
+
+    def value(self) -> int:
+        return int(self.state.item()) & ((1 << 64) - 1)
+
+
+def top_k(ctx: Context, logits, k: int):
+    """Ids of the k largest logits in descending order, ties to the lower id
+    (gpt2t.mojo:800-815); k <= 0 gives all. Returns an int32 CUDA tensor."""
+    import torch
+
+    V = logits.numel()
+    n = min(k, V) if k > 0 else V
+    ids = torch.empty(n, dtype=torch.int32, device="cuda")
+    _pre(ctx)
+    check(lib().llmq_top_k(ctx.h, _p(logits), V, k, _p(ids)), ctx.h)
+    ctx.sync()
+    return ids
+
+
+def sample(ctx: Context, logits, temperature: float, k: int, rng: Rng, out=None):
+    """One draw of sample (gpt2t.mojo:818-834) from logits[V] on the device;
+    returns a one-element int32 CUDA tensor (out, if given)."""
+    import torch
+
+    if out is None:
+        out = torch.empty(1, dtype=torch.int32, device="cuda")
+    _pre(ctx)
+    check(lib().llmq_sample(ctx.h, _p(logits), logits.numel(), temperature, k, _p(rng.state), _p(out)), ctx.h)
+    ctx.sync()
+    return out
+
+
 def layernorm(ctx: Context, out, x, w, b, T: int, C_: int):
     _pre(ctx)
     check(lib().llmq_layernorm(ctx.h, _p(out), _p(x), _p(w), _p(b), T, C_), ctx.h)

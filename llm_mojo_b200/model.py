@@ -93,6 +93,21 @@ class Model:
                                   out.ctypes.data_as(C.c_void_p)), self.ctx.h)
         return out
 
+    def generate_sampled(self, prompt, steps: int, temperature: float = 0.8, top_k: int = 40,
+                         seed: int = 1337, state=None) -> np.ndarray:
+        """generate with sample (gpt2t.mojo:818-834, 965-980; defaults -t 0.8
+        -k 40 -s 1337) and no stop at EOT. `state`, a one-element uint64
+        numpy array, carries the Rng state across calls (seeded from `seed`
+        when None)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(steps, dtype=np.int32)
+        if state is None:
+            state = np.array([lib().llmq_rng_init(seed)], dtype=np.uint64)
+        check(lib().llmq_generate_sampled(self.ctx.h, self.h, p.ctypes.data_as(C.c_void_p), p.size, steps,
+                                          temperature, top_k, state.ctypes.data_as(C.c_void_p),
+                                          out.ctypes.data_as(C.c_void_p)), self.ctx.h)
+        return out
+
     def free(self):
         if getattr(self, "h", None):
             lib().llmq_model_free(self.h)
@@ -209,6 +224,10 @@ class FloatModel:
     def generate(self, prompt, steps: int) -> np.ndarray:
         return Model.generate(self, prompt, steps)
 
+    def generate_sampled(self, prompt, steps: int, temperature: float = 0.8, top_k: int = 40,
+                         seed: int = 1337, state=None) -> np.ndarray:
+        return Model.generate_sampled(self, prompt, steps, temperature, top_k, seed, state)
+
     def free(self):
         if getattr(self, "h", None):
             lib().llmq_model_free(self.h)
@@ -250,6 +269,10 @@ class LoadedModel:
 
     def generate(self, prompt, steps: int) -> np.ndarray:
         return Model.generate(self, prompt, steps)
+
+    def generate_sampled(self, prompt, steps: int, temperature: float = 0.8, top_k: int = 40,
+                         seed: int = 1337, state=None) -> np.ndarray:
+        return Model.generate_sampled(self, prompt, steps, temperature, top_k, seed, state)
 
     def save(self, path: str):
         check(lib().llmq_model_save(self.ctx.h, self.h, path.encode()), self.ctx.h)

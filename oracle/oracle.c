@@ -1164,6 +1164,87 @@ OQ_EXPORT void oq_generate(oq_model *m, const int32_t *prompt, int n_prompt, int
   free(logits);
 }
 
+/* Rng (gpt2t.mojo:775-789): xorshift64* seeded with seed * 0x9E3779B97F4A7C15
+ * + 1 (wrapping); uniform() takes the top 24 bits of state * 0x2545F4914F6CDD1D. */
+OQ_EXPORT uint64_t oq_rng_init(int64_t seed) { return (uint64_t)seed * 0x9E3779B97F4A7C15ull + 1ull; }
+
+OQ_EXPORT float oq_rng_uniform(uint64_t *state) {
+  uint64_t s = *state;
+  s ^= s >> 12;
+  s ^= s << 25;
+  s ^= s >> 27;
+  *state = s;
+  return (float)((s * 0x2545F4914F6CDD1Dull) >> 40) / (float)(1 << 24);
+}
+
+/* top_k (gpt2t.mojo:800-815): ids of the k largest logits in descending
+ * order, kept by insertion into a sorted list (an equal later logit never
+ * passes an earlier one). Returns the number written (min(k, V)). */
+OQ_EXPORT int oq_top_k(const float *logits, int V, int k, int32_t *ids) {
+  int n = 0;
+  for (int v = 0; v < V; v++) {
+    float lv = logits[v];
+    if (n == k && lv <= logits[ids[k - 1]]) continue;
+    /* append at slot n (slot k is the one the reference pops again) */
+    int pos = n;
+    while (pos > 0 && logits[ids[pos - 1]] < lv) {
+      if (pos < k) ids[pos] = ids[pos - 1];
+      pos--;
+    }
+    if (pos < k) ids[pos] = v;
+    if (n < k) n++;
+  }
+  return n;
+}
+
+/* sample (gpt2t.mojo:818-834): argmax when temperature <= 0 (the state is
+ * not advanced); else the top k (k <= 0: all V) with weights
+ * exp((logit - max) / temperature), summed in order in float32, and the first
+ * candidate at which r = uniform() * total minus the running weights reaches
+ * <= 0 (the last candidate if none does). */
+OQ_EXPORT int oq_sample(const float *logits, int V, float temperature, int k, uint64_t *state) {
+  if (temperature <= 0) return oq_argmax(logits, V);
+  int kk = k > 0 ? (k < V ? k : V) : V;
+  int32_t *cand = (int32_t *)malloc(sizeof(int32_t) * kk);
+  float *p = (float *)malloc(sizeof(float) * kk);
+  int n = oq_top_k(logits, V, kk, cand);
+  float mx = logits[cand[0]], total = 0.0f;
+  for (int i = 0; i < n; i++) {
+    p[i] = lm_expf((logits[cand[i]] - mx) / temperature);
+    total += p[i];
+  }
+  float r = oq_rng_uniform(state) * total;
+  int pick = cand[n - 1];
+  for (int i = 0; i < n; i++) {
+    r -= p[i];
+    if (r <= 0) {
+      pick = cand[i];
+      break;
+    }
+  }
+  free(cand);
+  free(p);
+  return pick;
+}
+
+/* generate (gpt2t.mojo:965-980) with sample() in place of argmax, without
+ * the stop on EOT; *state is the Rng state, advanced in place. */
+OQ_EXPORT void oq_generate_sampled(oq_model *m, const int32_t *prompt, int n_prompt, int steps, float temperature,
+                                   int k, uint64_t *state, int32_t *out_ids) {
+  float *logits = (float *)malloc(sizeof(float) * m->V);
+  oq_model_forward(m, prompt, n_prompt, 0, logits);
+  int pos = n_prompt;
+  for (int i = 0; i < steps; i++) {
+    int next = oq_sample(logits, m->V, temperature, k, state);
+    out_ids[i] = next;
+    if (i == steps - 1) break;
+    int32_t one = next;
+    oq_model_forward(m, &one, 1, pos, logits);
+    pos++;
+  }
+  free(logits);
+}
+
 /* ------------------------------------------------------------------------ */
 /* GGUF block formats (gguf.mojo:139-512)                                    */
 /* ------------------------------------------------------------------------ */

@@ -77,6 +77,9 @@ def _declare(L):
         "oq_model_forward_all": (V, [P, P, I, P]),
         "oq_argmax": (I, [P, I]),
         "oq_generate": (V, [P, P, I, I, P]),
+        "oq_rng_init": (C.c_uint64, [C.c_int64]), "oq_rng_uniform": (F, [P]),
+        "oq_top_k": (I, [P, I, I, P]), "oq_sample": (I, [P, I, F, I, P]),
+        "oq_generate_sampled": (V, [P, P, I, I, F, I, P, P]),
         "oq_gguf_block_size": (I, [I]), "oq_gguf_block_bytes": (I, [I]),
         "oq_gguf_dequant_row": (V, [I, P, I, P]),
         "oq_gguf_dot_row": (F, [I, P, I, P]),
@@ -223,6 +226,14 @@ class Model:
         p = np.ascontiguousarray(prompt, dtype=np.int32)
         out = np.zeros(steps, dtype=np.int32)
         lib().oq_generate(self.h, ptr(p), p.size, steps, ptr(out))
+        return out
+
+    def generate_sampled(self, prompt, steps: int, temperature: float = 0.8, top_k: int = 40,
+                         seed: int = 1337) -> np.ndarray:
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(steps, dtype=np.int32)
+        st = np.array([lib().oq_rng_init(seed)], dtype=np.uint64)
+        lib().oq_generate_sampled(self.h, ptr(p), p.size, steps, temperature, top_k, ptr(st), ptr(out))
         return out
 
     def close(self):
