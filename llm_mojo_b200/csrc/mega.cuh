@@ -45,7 +45,7 @@ constexpr int MK_LANES = 4096;     // int32 lane sums held at once
 constexpr int MK_MAX_CHUNKS = 64;  // chunks per CTA per token
 constexpr int MK_POLL = 12;        // exchange words a thread polls at once (n <= 3072)
 #ifndef MK_BACKOFF_NS
-#define MK_BACKOFF_NS 200           // pause between unsuccessful poll rounds
+#define MK_BACKOFF_NS 0             // pause between unsuccessful poll rounds (0: none; 64 and 200 ns measured slower)
 #endif
 
 enum { PH_QKV = 0, PH_PROJ = 1, PH_FC = 2, PH_FCPROJ = 3, PH_HEAD = 4 };
@@ -226,7 +226,7 @@ __device__ __noinline__ bool mk_poll(const MegaArgs &a, MkSmem &sm, const unsign
       }
     if (pending) {
       if (!mk_alive(a, sm, t0, code)) break;
-      __nanosleep(MK_BACKOFF_NS);  // spaces the rounds: less load on the L2 lines being polled
+      if (MK_BACKOFF_NS > 0) __nanosleep(MK_BACKOFF_NS);
     }
   }
   cp_async_wait_all();  // parameters prefetched before the wait are then visible after the barrier
@@ -298,72 +298,100 @@ __device__ __noinline__ float mk_layernorm(MkSmem &sm, const float *src) {
 }
 
 // This thread's max |sm.xf[i]| over its elements of [0, IN).
-__device__ __forceinline__ float mk_local_max(const MkSmem &sm, int IN) {
+template <int IN>
+__device__ __forceinline__ float mk_local_max(const MkSmem &sm) {
   float mx = 0.0f;
+#pragma unroll
   for (int i = threadIdx.x; i < IN; i += MK_THREADS) mx = fmaxf(mx, fabsf(sm.xf[i]));
   return mx;
 }
 
+// Largest of the threads' maxima (each >= 0 and not NaN, so their bit
+// patterns order like the values): one redux per warp, 8 words in shared
+// memory. Ends with the barrier that makes sm.xf's writes visible.
+__device__ __forceinline__ float mk_block_max(MkSmem &sm, float mx) {
+  const unsigned m = __reduce_max_sync(0xffffffffu, __float_as_uint(mx));
+  if ((threadIdx.x & 31) == 0) ((unsigned *)sm.red)[threadIdx.x >> 5] = m;
+  cta_sync();
+  const uint4 a = *(const uint4 *)&sm.red[0], b = *(const uint4 *)&sm.red[4];
+  const unsigned r = max(max(max(a.x, a.y), max(a.z, a.w)), max(max(b.x, b.y), max(b.z, b.w)));
+  return __uint_as_float(r);
+}
+
 // quantize_rows of sm.xf[0..IN) into sm.xq (kernels.mojo:400-416), given
 // each thread's max |x| of its elements (mk_local_max or mk_layernorm): the
-// BLOCKED lane order and lane sums when blocked (permute_x_i16,
+// BLOCKED lane order and lane sums when BLOCKED (permute_x_i16,
 // tensor.mojo:498-516), natural order and per-lane pair sums otherwise.
-// Returns sx.
-__device__ __noinline__ float mk_quantize(MkSmem &sm, int IN, bool blocked, float mx) {
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((threadIdx.x & 31) == 0) sm.red[threadIdx.x >> 5] = mx;
-  cta_sync();
-  mx = sm.red[0];
-#pragma unroll
-  for (int w = 1; w < MK_THREADS / 32; w++) mx = fmaxf(mx, sm.red[w]);
-  float s = mx / 32767.0f;
+// Thread t takes columns 4t.. 4t+3 (+ 1024 k) as one float4, so the reads are
+// conflict-free; the integer sums are exact in any order. Returns sx.
+template <int IN, bool BLOCKED>
+__device__ __noinline__ float mk_quantize(MkSmem &sm, float mx) {
+  static_assert(IN % 128 == 0 && IN <= 3072, "whole warps of 4 columns per thread");
+  float s = mk_block_max(sm, mx) / 32767.0f;
   if (s == 0.0f) s = 1.0f;
   const float inv = 1.0f / s;
-  if (blocked && IN > 768) {
-    // Thread (blk, L) owns lane L of 256-block blk: the 16 columns
-    // blk*256 + (L%8)*32 + (L/8)*16 + e. Column e sits at step e/2, half e%2
-    // of the lane's pair; the lane sum is their total.
-    int *xp32 = (int *)sm.xq;
-    for (int i = threadIdx.x; i < IN / 16; i += MK_THREADS) {
-      const int blk = i >> 4, L = i & 15;
-      const float *src = sm.xf + blk * 256 + (L & 7) * 32 + (L >> 3) * 16;
-      int sum = 0;
+  int *xp32 = (int *)sm.xq;
+  constexpr int ITER = (IN + 4 * MK_THREADS - 1) / (4 * MK_THREADS);
+  if (BLOCKED) {
+    // Column col = blk*256 + g*32 + h*16 + e is element e of lane L = g + 8h
+    // of block blk: word blk*128 + (e/2)*16 + L, half e%2. A thread's four
+    // columns are e = 4j..4j+3 of one lane; four threads make the lane sum.
+    float *xsf = (float *)sm.xs;
 #pragma unroll
-      for (int st = 0; st < 8; st++) {
-        int c0 = round_away(src[2 * st] * inv), c1 = round_away(src[2 * st + 1] * inv);
-        sum += c0 + c1;
-        xp32[blk * 128 + st * 16 + L] = (c0 & 0xFFFF) | (c1 << 16);
+    for (int k = 0; k < ITER; k++) {
+      const int c = 4 * threadIdx.x + 4 * MK_THREADS * k;
+      if (c < IN) {
+        const float4 v = *(const float4 *)(sm.xf + c);
+        const int c0 = round_away(v.x * inv), c1 = round_away(v.y * inv);
+        const int c2 = round_away(v.z * inv), c3 = round_away(v.w * inv);
+        const int blk = c >> 8, w = c & 255, L = ((w >> 5) & 7) + 8 * ((w >> 4) & 1), st = (w & 15) >> 1;
+        int *dst = xp32 + blk * 128 + st * 16 + L;
+        dst[0] = (c0 & 0xFFFF) | (c1 << 16);
+        dst[16] = (c2 & 0xFFFF) | (c3 << 16);
+        int sum = (c0 + c1) + (c2 + c3);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if ((threadIdx.x & 3) == 0) xsf[blk * 16 + L] = (float)sum;
       }
-      ((float *)sm.xs)[i] = (float)sum;
     }
-  } else if (blocked) {
-    // Element i = (blk, L, e): lane L of 256-block blk holds the 16 columns
-    // blk*256 + (L%8)*32 + (L/8)*16 + e; column e sits at step e/2, half e%2
-    // of the lane's pair. A half-warp holds one lane's 16 columns: the pair
-    // comes from the neighbouring thread and the lane sum from 4 shuffles.
-    int *xp32 = (int *)sm.xq;
-    for (int i = threadIdx.x; i < IN; i += MK_THREADS) {
-      const int e = i & 15, L = (i >> 4) & 15, blk = i >> 8;
-      const int c = round_away(sm.xf[blk * 256 + (L & 7) * 32 + (L >> 3) * 16 + e] * inv);
-      const int nb = __shfl_xor_sync(0xffffffffu, c, 1);
-      if ((e & 1) == 0) xp32[blk * 128 + (e >> 1) * 16 + L] = (c & 0xFFFF) | (nb << 16);
-      int sum = c;
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
-      if (e == 0) ((float *)sm.xs)[blk * 16 + L] = (float)sum;
-    }
+    cta_sync();
   } else {
-    for (int i = threadIdx.x; i < IN; i += MK_THREADS) sm.xq[i] = (int16_t)round_away(sm.xf[i] * inv);
+    // Natural order; xs[L] = sum over the 32-column groups of columns 2L and
+    // 2L+1: within a warp the threads t, t^8, t^16, t^24 hold the same
+    // pairs, then one partial per warp in sm.lanes and 16 threads add them.
+    int *part = sm.lanes;
+    int p0 = 0, p1 = 0;
+#pragma unroll
+    for (int k = 0; k < ITER; k++) {
+      const int c = 4 * threadIdx.x + 4 * MK_THREADS * k;
+      if (c < IN) {
+        const float4 v = *(const float4 *)(sm.xf + c);
+        const int c0 = round_away(v.x * inv), c1 = round_away(v.y * inv);
+        const int c2 = round_away(v.z * inv), c3 = round_away(v.w * inv);
+        xp32[c >> 1] = (c0 & 0xFFFF) | (c1 << 16);
+        xp32[(c >> 1) + 1] = (c2 & 0xFFFF) | (c3 << 16);
+        p0 += c0 + c1;
+        p1 += c2 + c3;
+      }
+    }
+    p0 += __shfl_xor_sync(0xffffffffu, p0, 8);
+    p1 += __shfl_xor_sync(0xffffffffu, p1, 8);
+    p0 += __shfl_xor_sync(0xffffffffu, p0, 16);
+    p1 += __shfl_xor_sync(0xffffffffu, p1, 16);
+    const int lane = threadIdx.x & 31;
+    if (lane < 8) {
+      part[(threadIdx.x >> 5) * 16 + 2 * lane] = p0;
+      part[(threadIdx.x >> 5) * 16 + 2 * lane + 1] = p1;
+    }
     cta_sync();
     if (threadIdx.x < 16) {
-      int L = threadIdx.x, sum = 0;
-      for (int k0 = 0; k0 < IN; k0 += 32) sum += (int)sm.xq[k0 + 2 * L] + (int)sm.xq[k0 + 2 * L + 1];
-      sm.xs[L] = sum;
+      int sum = 0;
+#pragma unroll
+      for (int w = 0; w < MK_THREADS / 32; w++) sum += part[w * 16 + threadIdx.x];
+      sm.xs[threadIdx.x] = sum;
     }
+    cta_sync();
   }
-  cta_sync();
   return s;
 }
 
@@ -373,15 +401,17 @@ enum { MK_GELU = 1, MK_RESID = 2 };
 // BLOCKED int4-g32 rows of the chunk in `slot` against sm.xq (dot_row_i16,
 // tensor.mojo:522-540), then v = dot * sx + bias (+ GELU) (+ sm.xfull[o]),
 // published as exchange words out[o] with `flag`.
-__device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, float sx,
-                                          int epi, unsigned long long *out, unsigned flag, long long *pacc) {
+template <int IN>
+__device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, float sx, int epi,
+                                          unsigned long long *out, unsigned flag, long long *pacc) {
   long long t0 = clock64();
-  const int R = ch.r1 - ch.r0, nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
+  constexpr int nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
+  const int R = ch.r1 - ch.r0;
   const int *xp32 = (const int *)sm.xq;
   const float *xs = (const float *)sm.xs;
   const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
   const uint8_t *zpp = slot + ch.zp_off;
-  const int pass = MK_LANES / (nblk * 16) < 64 ? MK_LANES / (nblk * 16) : 64;
+  constexpr int pass = MK_LANES / (nblk * 16) < 64 ? MK_LANES / (nblk * 16) : 64;
   for (int rbase = 0; rbase < R; rbase += pass) {
     const int rows = R - rbase < pass ? R - rbase : pass;
     // integer phase: items (row, block, q); the steps of a block are visited
@@ -424,6 +454,7 @@ __device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const
       const uint16_t *srow = scl + (rbase + rr) * gpr + (L & 7);
       const int *lrow = sm.lanes + rr * nblk * 16 + L;
       float f = 0.0f;
+#pragma unroll
       for (int b = 0; b < nblk; b++) {
         const float zp = (float)zrow[b * 8];
         const float sc = __half2float(__ushort_as_half(srow[b * 8]));
@@ -449,9 +480,11 @@ __device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const
 // Per-channel int8 head rows of the chunk in `slot` (dot_row_i16 per
 // channel, tensor.mojo:541-566): logit = dot * sx, written to logits (if
 // any) and folded into this thread's argmax candidate (sm.thr_v / thr_i).
-__device__ __noinline__ void mk_head_tile(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, int IN, float sx,
+template <int IN>
+__device__ __noinline__ void mk_head_tile(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, float sx,
                                           float *logits) {
-  const int R = ch.r1 - ch.r0, nch = IN >> 5;
+  constexpr int nch = IN >> 5, SPAN = nch / 2;
+  const int R = ch.r1 - ch.r0;
   const int *xp32 = (const int *)sm.xq;
   const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
   const uint8_t *zpp = slot + ch.zp_off;
@@ -461,9 +494,11 @@ __device__ __noinline__ void mk_head_tile(MkSmem &sm, const uint8_t *slot, const
     int acc[4] = {0, 0, 0, 0};
     if (r < R) {
       const uint8_t *rp = slot + (size_t)r * IN;
-      const int c0 = p * (nch / 2), c1 = (p + 1) * (nch / 2), span = c1 - c0;
-      for (int cc = 0; cc < span; cc++) {
-        int c = c0 + (cc + r) % span;
+      const int c0 = p * SPAN, rot = r % SPAN;
+#pragma unroll
+      for (int cc = 0; cc < SPAN; cc++) {
+        int c = cc + rot;
+        c = c0 + (c >= SPAN ? c - SPAN : c);
         uint2 v = *(const uint2 *)(rp + c * 32 + 8 * q);
         int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
         acc[0] = dp2a_lo_su(xv.x, v.x, acc[0]);
@@ -556,7 +591,7 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
         v = ld_relaxed_u64(src);
         if ((unsigned)(v >> 32) == flag) break;
         if (!mk_alive(a, sm, t0, 2)) break;
-        __nanosleep(MK_BACKOFF_NS);
+        if (MK_BACKOFF_NS > 0) __nanosleep(MK_BACKOFF_NS);
       }
       float x = __uint_as_float((unsigned)v);
       if (which == 0)
@@ -823,7 +858,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   auto gemv = [&](const MkChunk &ch, int IN, float sx, int epi, unsigned long long *out, unsigned flag) -> bool {
     const int slot = slot_wait();
     if (slot < 0) return false;
-    mk_gemv_blk4(sm, sm.ring[slot], ch, IN, sx, epi, out, flag, pp);
+    if (IN == 768)
+      mk_gemv_blk4<768>(sm, sm.ring[slot], ch, sx, epi, out, flag, pp);
+    else
+      mk_gemv_blk4<3072>(sm, sm.ring[slot], ch, sx, epi, out, flag, pp);
     slot_release();
     return true;
   };
@@ -854,7 +892,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         long long t0 = clock64();
         const float lmx = mk_layernorm(sm, sm.xfull);
         sub_tick(pp, PF_LN, t0);
-        const float sx = mk_quantize(sm, C, true, lmx);
+        const float sx = mk_quantize<768, true>(sm, lmx);
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, 0, a.ll + ll.qkv(l), flag))) break;
         tick(PF_QKV);
@@ -871,7 +909,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         if (!(ok = mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4))) break;
         tick(PF_PROJ_WAIT);
         long long t0 = clock64();
-        const float sx = mk_quantize(sm, C, true, mk_local_max(sm, C));
+        const float sx = mk_quantize<768, true>(sm, mk_local_max<768>(sm));
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, MK_RESID, a.ll + ll.xmid(l), flag))) break;
         tick(PF_PROJ);
@@ -885,7 +923,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         long long t0 = clock64();
         const float lmx = mk_layernorm(sm, sm.xfull);
         sub_tick(pp, PF_LN, t0);
-        const float sx = mk_quantize(sm, C, true, lmx);
+        const float sx = mk_quantize<768, true>(sm, lmx);
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C, sx, MK_GELU, a.ll + ll.fc(l), flag))) break;
         tick(PF_FC);
@@ -897,7 +935,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         if (!(ok = mk_poll(a, sm, a.ll + ll.fc(l), C4, flag, sm.xf, 6))) break;
         tick(PF_FCPROJ_WAIT);
         long long t0 = clock64();
-        const float sx = mk_quantize(sm, C4, true, mk_local_max(sm, C4));
+        const float sx = mk_quantize<3072, true>(sm, mk_local_max<3072>(sm));
         sub_tick(pp, PF_QUANT, t0);
         if (!(ok = gemv(ch, C4, sx, MK_RESID, a.ll + ll.xout(l), flag))) break;
         tick(PF_FCPROJ);
@@ -908,7 +946,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     mk_params_load(sm, lnf, lnf + C, nullptr, 0, 0);
     if (!(ok = mk_poll(a, sm, a.ll + ll.xout(a.n_layer - 1), C, flag, sm.xf, 7))) break;
     tick(PF_HEAD_WAIT);
-    const float sx = mk_quantize(sm, C, false, mk_layernorm(sm, sm.xf));
+    const float sx = mk_quantize<768, false>(sm, mk_layernorm(sm, sm.xf));
     sm.thr_v[tid] = -__int_as_float(0x7f800000);
     sm.thr_i[tid] = 0x7fffffff;
     for (; ci < a.nchunks; ci++) {
@@ -917,7 +955,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
         ok = false;
         break;
       }
-      mk_head_tile(sm, sm.ring[slot], sm.chunks[ci], C, sx, a.logits);
+      mk_head_tile<768>(sm, sm.ring[slot], sm.chunks[ci], sx, a.logits);
       slot_release();
     }
     if (!ok) break;
