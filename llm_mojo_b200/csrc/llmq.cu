@@ -34,10 +34,9 @@ struct llmq_ctx {
   int prefill_kernel = LLMQ_PREFILL_AUTO;
   int *tc_err = nullptr;         // device error code of the tcgen05 GEMM (a wait that gave up)
   bool tc_used = false;          // a tcgen05 GEMM ran since the last check
-  // sampling scratch (device, grown on demand): sort keys, weights, chunk
-  // candidates, the Rng state of llmq_generate_sampled
+  // sampling scratch (device, grown on demand): sort keys, chunk candidates,
+  // the Rng state of llmq_generate_sampled
   unsigned long long *samp_keys = nullptr;
-  float *samp_p = nullptr;
   unsigned long long *samp_cand = nullptr;
   unsigned long long *samp_rng = nullptr;
   int samp_n = 0;
@@ -329,7 +328,7 @@ llmq_status llmq_destroy(llmq_ctx *ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->state) cudaFree(ctx->state);
   if (ctx->tc_err) cudaFree(ctx->tc_err);
-  for (void *q : {(void *)ctx->samp_keys, (void *)ctx->samp_p, (void *)ctx->samp_cand, (void *)ctx->samp_rng})
+  for (void *q : {(void *)ctx->samp_keys, (void *)ctx->samp_cand, (void *)ctx->samp_rng})
     if (q) cudaFree(q);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
@@ -1423,12 +1422,9 @@ static llmq_status sample_scratch(llmq_ctx *ctx, int V) {
   if (n <= ctx->samp_n) return LLMQ_OK;
   CK(cudaStreamSynchronize(ctx->stream));
   if (ctx->samp_keys) cudaFree(ctx->samp_keys);
-  if (ctx->samp_p) cudaFree(ctx->samp_p);
   ctx->samp_keys = nullptr;
-  ctx->samp_p = nullptr;
   ctx->samp_n = 0;
   CK(cudaMalloc(&ctx->samp_keys, sizeof(unsigned long long) * n));
-  CK(cudaMalloc(&ctx->samp_p, sizeof(float) * n));
   ctx->samp_n = n;
   return LLMQ_OK;
 }
@@ -1461,7 +1457,7 @@ static llmq_status enqueue_sample(llmq_ctx *ctx, const float *logits, int V, flo
     sort_chunk_kernel<<<n / kSortChunk, kSortThreads, 0, s>>>(nullptr, V, keys, sz, sz, 0, nullptr, 0);
     CKL();
   }
-  sorted_draw_kernel<<<1, kSortThreads, 0, s>>>(keys, kk, logits, temperature, ctx->samp_p, rng, o, topk_ids);
+  sorted_draw_kernel<<<1, kSortThreads, 0, s>>>(keys, kk, logits, temperature, rng, o, topk_ids);
   CKL();
   return LLMQ_OK;
 }

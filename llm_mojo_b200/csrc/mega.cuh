@@ -572,20 +572,54 @@ __device__ __noinline__ void mk_kv_prefetch(const MegaArgs &a, MkSmem &sm, int l
   cp_async_commit();
 }
 
+// Order-preserving 32-bit keys of floats (not NaN): unsigned comparison of
+// the keys is float comparison of the values.
+__device__ __forceinline__ unsigned f2key(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(unsigned k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Score of one cached position: the 16-lane dot of q with the 64 key codes,
+// reduced by the halving tree, times the key scale and 1/sqrt(64).
+__device__ __forceinline__ float mk_score(const MkSmem &sm, const int8_t *kp, float ksc) {
+  float d[16];
+#pragma unroll
+  for (int k = 0; k < 16; k++) d[k] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 64; i += 16) {
+    const int4 kv4 = *(const int4 *)(kp + i);
+    const int8_t *kb = (const int8_t *)&kv4;
+#pragma unroll
+    for (int k = 0; k < 16; k++) d[k] = d[k] + sm.att_q[i + k] * (float)kb[k];
+  }
+#pragma unroll
+  for (int k = 0; k < 8; k++) d[k] = d[k] + d[k + 8];
+#pragma unroll
+  for (int k = 0; k < 4; k++) d[k] = d[k] + d[k + 4];
+  d[0] = d[0] + d[2];
+  d[1] = d[1] + d[3];
+  return ((d[0] + d[1]) * ksc) * 0.125f;
+}
+
 // Attention phase of head h (QuantKV[8]): store the token's key and value
 // (QuantKV.store, kvcache.mojo:333-342), then attend over positions 0..pos
 // (attend_float_one, kvcache.mojo:113-150) and publish att[h*64 .. +64).
-// Returns false on timeout.
+// Warps 0 and 1 quantize the key and the value (two elements per lane, one
+// redux for the max) while warps 2-7 score the cached positions; the
+// softmax sum and the value chains run in position order as in the
+// reference. Returns false on timeout.
 __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int l, int h, int pos,
                                           unsigned flag) {
-  const int HS = a.kv.head_dim, C = a.C;
-  const int tid = threadIdx.x;
-  // poll q, k, v of head h (3 x 64 words)
+  const int C = a.C, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // poll q, k, v of head h (3 x 64 words); the staged cache copies complete
   {
     long long t0 = clock64();
-    if (tid < 3 * HS) {
-      int which = tid / HS, d = tid % HS;
-      const unsigned long long *src = a.ll + ll.qkv(l) + which * C + h * HS + d;
+    if (tid < 192) {
+      const int which = tid >> 6, d = tid & 63;
+      const unsigned long long *src = a.ll + ll.qkv(l) + which * C + h * 64 + d;
       unsigned long long v;
       while (true) {
         v = ld_relaxed_u64(src);
@@ -593,91 +627,86 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
         if (!mk_alive(a, sm, t0, 2)) break;
         if (MK_BACKOFF_NS > 0) __nanosleep(MK_BACKOFF_NS);
       }
-      float x = __uint_as_float((unsigned)v);
+      const float x = __uint_as_float((unsigned)v);
       if (which == 0)
         sm.att_q[d] = x;
       else
         sm.xf[(which - 1) * 64 + d] = x;
     }
+    cp_async_wait_all();
     cta_sync();
     if (sm.abort) return false;
   }
-  // store: per-head int8 quantization of k and v (QuantKV.quantize).
-  const size_t sl = ((size_t)l * a.kv.max_t + pos) * a.kv.n_head + h;
-  if (tid < 64) {
-    for (int which = 0; which < 2; which++) {
-      float m = fabsf(sm.xf[which * 64 + tid]);
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if ((tid & 31) == 0) sm.red[48 + which * 2 + (tid >> 5)] = m;
-    }
-  }
-  cta_sync();
-  if (tid < 64) {
-    for (int which = 0; which < 2; which++) {
-      float m = fmaxf(sm.red[48 + which * 2], sm.red[49 + which * 2]);
-      float s = m / 127.0f;
-      if (s == 0.0f) s = 1.0f;
-      float inv = 1.0f / s;
-      int8_t code = (int8_t)roundf(sm.xf[which * 64 + tid] * inv);
-      if (which == 0) {
-        sm.att_k[tid] = code;
-        a.kv.k[sl * HS + tid] = code;
-        if (tid == 0) a.kv.ks[sl] = s;
-      } else {
-        sm.att_v[tid] = code;
-        a.kv.v[sl * HS + tid] = code;
-        if (tid == 0) a.kv.vs[sl] = s;
-      }
-    }
-  }
+  const size_t stride_h = a.kv.n_head, base = (size_t)l * a.kv.max_t * stride_h + h;  // slot of position 0
+  const size_t sl = base + (size_t)pos * stride_h;
   const bool staged = pos <= MK_KV_STAGE;
-  cp_async_wait_all();
-  cta_sync();
   const int npos = pos + 1;
-  const float scale = 1.0f / sqrtf((float)HS);
   float mx = -__int_as_float(0x7f800000);
-  for (int s = tid; s < npos; s += MK_THREADS) {
-    size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
-    const int8_t *kp = (s == pos) ? sm.att_k : (staged ? sm.kst[s] : a.kv.k + ss * HS);
-    float ksc = (s == pos || !staged) ? a.kv.ks[ss] : sm.kss[s];
-    float d[16];
-#pragma unroll
-    for (int k = 0; k < 16; k++) d[k] = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 64; i += 16) {
-      int4 kv4 = *(const int4 *)(kp + i);
-      const int8_t *kb = (const int8_t *)&kv4;
-#pragma unroll
-      for (int k = 0; k < 16; k++) d[k] = d[k] + sm.att_q[i + k] * (float)kb[k];
+  if (warp < 2) {
+    // store: per-head int8 quantization (QuantKV.quantize); warp 0 the key,
+    // warp 1 the value
+    const float x0 = sm.xf[warp * 64 + lane], x1 = sm.xf[warp * 64 + lane + 32];
+    const unsigned m = __reduce_max_sync(0xffffffffu, max(__float_as_uint(fabsf(x0)), __float_as_uint(fabsf(x1))));
+    float s = __uint_as_float(m) / 127.0f;
+    if (s == 0.0f) s = 1.0f;
+    const float inv = 1.0f / s;
+    const int8_t q0 = (int8_t)round_away(x0 * inv), q1 = (int8_t)round_away(x1 * inv);
+    int8_t *g = (warp == 0 ? a.kv.k : a.kv.v) + sl * 64;
+    int8_t *sh = warp == 0 ? sm.att_k : sm.att_v;
+    g[lane] = q0;
+    g[lane + 32] = q1;
+    sh[lane] = q0;
+    sh[lane + 32] = q1;
+    if (lane == 0) {
+      (warp == 0 ? a.kv.ks : a.kv.vs)[sl] = s;
+      sm.red[50 + warp] = s;
     }
-#pragma unroll
-    for (int k = 0; k < 8; k++) d[k] = d[k] + d[k + 8];
-#pragma unroll
-    for (int k = 0; k < 4; k++) d[k] = d[k] + d[k + 4];
-    d[0] = d[0] + d[2];
-    d[1] = d[1] + d[3];
-    float v = ((d[0] + d[1]) * ksc) * scale;
+    __syncwarp();
+    if (tid == 0) {
+      const float v = mk_score(sm, sm.att_k, s);
+      sm.att_sc[pos] = v;
+      mx = v;
+    }
+  }
+  // scores of the cached positions: warps 2-7 take positions 0..191 first
+  for (int s = (tid + 192) & 255; s < pos; s += MK_THREADS) {
+    const size_t ss = base + (size_t)s * stride_h;
+    const float v = staged ? mk_score(sm, sm.kst[s], sm.kss[s]) : mk_score(sm, a.kv.k + ss * 64, a.kv.ks[ss]);
     sm.att_sc[s] = v;
     mx = fmaxf(mx, v);
   }
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) sm.red[tid >> 5] = mx;
+  {
+    const unsigned k = __reduce_max_sync(0xffffffffu, f2key(mx));
+    if (lane == 0) ((unsigned *)sm.red)[warp] = k;
+  }
   cta_sync();
-  mx = sm.red[0];
-#pragma unroll
-  for (int w = 1; w < MK_THREADS / 32; w++) mx = fmaxf(mx, sm.red[w]);
+  {
+    const uint4 ka = *(const uint4 *)&sm.red[0], kb = *(const uint4 *)&sm.red[4];
+    mx = key2f(max(max(max(ka.x, ka.y), max(ka.z, ka.w)), max(max(kb.x, kb.y), max(kb.z, kb.w))));
+  }
   for (int s = tid; s < npos; s += MK_THREADS) sm.att_sc[s] = lm_expf(sm.att_sc[s] - mx);
   cta_sync();
   if (tid == 0) {
-    // sequential sum in position order, 16 values loaded ahead at a time
+    // sequential sum in position order; the next 16 values load while the
+    // current 16 add
     float total = 0.0f;
     int s = 0;
-    for (; s + 16 <= npos; s += 16) {
-      float e[16];
+    float e[16];
+    if (npos >= 16) {
 #pragma unroll
-      for (int k = 0; k < 16; k++) e[k] = sm.att_sc[s + k];
+      for (int k = 0; k < 16; k++) e[k] = sm.att_sc[k];
+      for (; s + 32 <= npos; s += 16) {
+        float nx[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) nx[k] = sm.att_sc[s + 16 + k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) total += e[k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) e[k] = nx[k];
+      }
 #pragma unroll
       for (int k = 0; k < 16; k++) total += e[k];
+      s += 16;
     }
     for (; s < npos; s++) total += sm.att_sc[s];
     sm.red[36] = total;
@@ -685,12 +714,11 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
   cta_sync();
   const float total = sm.red[36];
   for (int s = tid; s < npos; s += MK_THREADS) {
-    size_t ss = ((size_t)l * a.kv.max_t + s) * a.kv.n_head + h;
-    float p = sm.att_sc[s] / total;
-    sm.att_ps[s] = p * ((s == pos || !staged) ? a.kv.vs[ss] : sm.vss[s]);
+    const float vsc = s == pos ? sm.red[51] : (staged ? sm.vss[s] : a.kv.vs[base + (size_t)s * stride_h]);
+    sm.att_ps[s] = (sm.att_sc[s] / total) * vsc;
   }
   cta_sync();
-  if (tid < HS) {
+  if (tid < 64) {
     // acc = fma(p * vs, v, acc) over positions in order
     const int d = tid;
     float acc = 0.0f;
@@ -708,12 +736,11 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
       }
       for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
     } else {
-      const size_t stride = (size_t)a.kv.n_head * HS;
-      const int8_t *vp = a.kv.v + ((size_t)l * a.kv.max_t * a.kv.n_head + h) * HS + d;
-      for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride], acc);
+      const int8_t *vp = a.kv.v + base * 64 + d;
+      for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride_h * 64], acc);
     }
     acc = fmaf(sm.att_ps[pos], (float)sm.att_v[d], acc);
-    st_relaxed_u64(a.ll + ll.att(l) + h * HS + d, ll_pack(acc, flag));
+    st_relaxed_u64(a.ll + ll.att(l) + h * 64 + d, ll_pack(acc, flag));
   }
   return true;
 }

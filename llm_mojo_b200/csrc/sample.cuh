@@ -113,7 +113,7 @@ __device__ __forceinline__ float rng_uniform(u64 *state) {
   return (float)((s * 0x2545F4914F6CDD1Dull) >> 40) / (float)(1 << 24);
 }
 
-// The draw over the first k sorted keys; p holds k floats (shared or global).
+// The draw over the first k sorted keys; p holds k floats in shared memory.
 __device__ void draw_sorted(const u64 *sorted, int k, const float *logits, float temperature, float *p, u64 *rng,
                             SampleOut o) {
   const float mx = logits[key_id(sorted[0])];
@@ -164,15 +164,73 @@ __global__ void __launch_bounds__(kSortThreads)
   draw_sorted(sk, k, logits, temperature, p, rng, o);
 }
 
-// The draw (or the top-k ids) from a fully sorted global key array.
+constexpr int kDrawStage = 8192;  // weights of the global-key draw staged per round
+
+// The draw (or the top-k ids) from a fully sorted global key array. The
+// weights are computed a stage at a time into shared memory (twice: for the
+// sum, then for the walk) so that thread 0's sequential chains read shared
+// memory.
 __global__ void __launch_bounds__(kSortThreads)
-    sorted_draw_kernel(const u64 *keys, int k, const float *logits, float temperature, float *p, u64 *rng,
-                       SampleOut o, int *topk_ids) {
+    sorted_draw_kernel(const u64 *keys, int k, const float *logits, float temperature, u64 *rng, SampleOut o,
+                       int *topk_ids) {
   if (topk_ids) {
     for (int i = threadIdx.x; i < k; i += blockDim.x) topk_ids[i] = key_id(keys[i]);
     return;
   }
-  draw_sorted(keys, k, logits, temperature, p, rng, o);
+  __shared__ float st[kDrawStage];
+  __shared__ float r_sh;
+  __shared__ int pick_sh;
+  const float mx = logits[key_id(keys[0])];
+  float total = 0.0f;
+  for (int c0 = 0; c0 < k; c0 += kDrawStage) {
+    const int n = min(kDrawStage, k - c0);
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      st[i] = lm_expf((logits[key_id(keys[c0 + i])] - mx) / temperature);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int i = 0;
+      for (; i + 8 <= n; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) v[u] = st[i + u];
+#pragma unroll
+        for (int u = 0; u < 8; u++) total += v[u];
+      }
+      for (; i < n; i++) total += st[i];
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    r_sh = rng_uniform(rng) * total;
+    pick_sh = -1;
+  }
+  __syncthreads();
+  for (int c0 = 0; c0 < k; c0 += kDrawStage) {
+    const int n = min(kDrawStage, k - c0);
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      st[i] = lm_expf((logits[key_id(keys[c0 + i])] - mx) / temperature);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float r = r_sh;
+      for (int i = 0; i < n; i++) {
+        r -= st[i];
+        if (r <= 0.0f) {
+          pick_sh = c0 + i;
+          break;
+        }
+      }
+      r_sh = r;
+    }
+    __syncthreads();
+    if (pick_sh >= 0) break;
+  }
+  if (threadIdx.x == 0) {
+    const int id = key_id(keys[pick_sh >= 0 ? pick_sh : k - 1]);
+    if (o.id) *o.id = id;
+    if (o.id2) *o.id2 = id;
+    if (o.ids) o.ids[*o.state_step - 1] = id;
+    if (o.state_token) *o.state_token = id;
+  }
 }
 
 inline size_t merge_smem(int n_pad) { return (size_t)n_pad * 8 + (size_t)kTopkSmall * 4; }
