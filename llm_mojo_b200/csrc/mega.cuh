@@ -398,6 +398,56 @@ __device__ __noinline__ float mk_quantize(MkSmem &sm, float mx) {
 // Epilogue flags of mk_gemv_blk4 (store_out, kernels.mojo:38-48).
 enum { MK_GELU = 1, MK_RESID = 2 };
 
+// The float phase of mk_gemv_blk4 for rows [rbase, rbase + rows) of the
+// chunk: thread j of a row's TPR threads carries the chains of lanes j,
+// j+TPR, ... over the row's blocks (lane L uses group L & 7 of each block:
+// (lane - zp * lane sum of x) * scale, fused, in block order), then the 16
+// lanes add as the halving tree (i and i+8, i+4, i+2, i+1): the levels whose
+// partner is in the same thread first, then shuffles. The row's value
+// dot * sx + bias (+ GELU) (+ residual) is published as an exchange word.
+template <int TPR, int NBLK>
+__device__ __forceinline__ void mk_float_rows(MkSmem &sm, const MkChunk &ch, const uint8_t *zpp, const uint16_t *scl,
+                                              int rbase, int rows, float sx, int epi, unsigned long long *out,
+                                              unsigned flag) {
+  constexpr int M = 16 / TPR, gpr = NBLK * 8;
+  const int j = threadIdx.x % TPR, r = threadIdx.x / TPR;
+  const int rr = r < rows ? r : 0;
+  const uint8_t *zrow = zpp + (rbase + rr) * gpr;
+  const uint16_t *srow = scl + (rbase + rr) * gpr;
+  const int *lrow = sm.lanes + rr * NBLK * 16;
+  const float *xs = (const float *)sm.xs;
+  float f[M];
+#pragma unroll
+  for (int m = 0; m < M; m++) f[m] = 0.0f;
+#pragma unroll
+  for (int b = 0; b < NBLK; b++) {
+#pragma unroll
+    for (int m = 0; m < M; m++) {
+      const int L = j + TPR * m, g = b * 8 + (L & 7);
+      const float zp = (float)zrow[g];
+      const float sc = __half2float(__ushort_as_half(srow[g]));
+      f[m] = fmaf((float)lrow[b * 16 + L] - zp * xs[b * 16 + L], sc, f[m]);
+    }
+  }
+  float v;
+  if (M == 4) {
+    v = (f[0] + f[2]) + (f[1] + f[3]);  // lanes j, j+4, j+8, j+12
+  } else if (M == 2) {
+    v = f[0] + f[1];  // lanes j, j+8
+  } else {
+    v = f[0];
+  }
+#pragma unroll
+  for (int o = TPR / 2; o > 0; o >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, o);
+  if (j == 0 && r < rows) {
+    const int rl = rbase + r, o = ch.r0 + rl;
+    float y = v * sx + sm.bias[rl];
+    if (epi & MK_GELU) y = gelu(y);
+    if (epi & MK_RESID) y += sm.xfull[o];
+    st_relaxed_u64(out + o, ll_pack(y, flag));
+  }
+}
+
 // BLOCKED int4-g32 rows of the chunk in `slot` against sm.xq (dot_row_i16,
 // tensor.mojo:522-540), then v = dot * sx + bias (+ GELU) (+ sm.xfull[o]),
 // published as exchange words out[o] with `flag`.
@@ -405,13 +455,13 @@ template <int IN>
 __device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, float sx, int epi,
                                           unsigned long long *out, unsigned flag, long long *pacc) {
   long long t0 = clock64();
-  constexpr int nblk = IN >> 8, gpr = IN >> 5, row_bytes = IN >> 1;
+  constexpr int nblk = IN >> 8, row_bytes = IN >> 1;
   const int R = ch.r1 - ch.r0;
   const int *xp32 = (const int *)sm.xq;
-  const float *xs = (const float *)sm.xs;
   const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
   const uint8_t *zpp = slot + ch.zp_off;
   constexpr int pass = MK_LANES / (nblk * 16) < 64 ? MK_LANES / (nblk * 16) : 64;
+  static_assert(pass <= 64, "one float pass: at least four threads per row");
   for (int rbase = 0; rbase < R; rbase += pass) {
     const int rows = R - rbase < pass ? R - rbase : pass;
     // integer phase: items (row, block, q); the steps of a block are visited
@@ -444,106 +494,80 @@ __device__ __noinline__ void mk_gemv_blk4(MkSmem &sm, const uint8_t *slot, const
     }
     cta_sync();
     sub_tick(pacc, PF_INT, t0);
-    // float phase: 16 threads per row, thread L carries lane L's chain over
-    // the row's blocks; the 16 lanes then add as a halving tree (xor 8, 4,
-    // 2, 1 within the half-warp).
-    for (int r0 = 0; r0 < rows; r0 += MK_THREADS / 16) {
-      const int L = threadIdx.x & 15, r = r0 + (threadIdx.x >> 4);
-      const int rr = r < rows ? r : 0;
-      const uint8_t *zrow = zpp + (rbase + rr) * gpr + (L & 7);
-      const uint16_t *srow = scl + (rbase + rr) * gpr + (L & 7);
-      const int *lrow = sm.lanes + rr * nblk * 16 + L;
-      float f = 0.0f;
-#pragma unroll
-      for (int b = 0; b < nblk; b++) {
-        const float zp = (float)zrow[b * 8];
-        const float sc = __half2float(__ushort_as_half(srow[b * 8]));
-        f = fmaf((float)lrow[b * 16] - zp * xs[b * 16 + L], sc, f);
-      }
-      f = f + __shfl_xor_sync(0xffffffffu, f, 8);
-      f = f + __shfl_xor_sync(0xffffffffu, f, 4);
-      f = f + __shfl_xor_sync(0xffffffffu, f, 2);
-      f = f + __shfl_xor_sync(0xffffffffu, f, 1);
-      if (L == 0 && r < rows) {
-        const int rl = rbase + r, o = ch.r0 + rl;
-        float v = f * sx + sm.bias[rl];
-        if (epi & MK_GELU) v = gelu(v);
-        if (epi & MK_RESID) v += sm.xfull[o];
-        st_relaxed_u64(out + o, ll_pack(v, flag));
-      }
-    }
+    // float phase, one pass: TPR threads per row (16 for up to 16 rows, 8 up
+    // to 32, 4 up to 64)
+    if (rows <= 16)
+      mk_float_rows<16, nblk>(sm, ch, zpp, scl, rbase, rows, sx, epi, out, flag);
+    else if (rows <= 32)
+      mk_float_rows<8, nblk>(sm, ch, zpp, scl, rbase, rows, sx, epi, out, flag);
+    else
+      mk_float_rows<4, nblk>(sm, ch, zpp, scl, rbase, rows, sx, epi, out, flag);
     cta_sync();
     sub_tick(pacc, PF_FLOAT, t0);
   }
 }
 
-// Per-channel int8 head rows of the chunk in `slot` (dot_row_i16 per
-// channel, tensor.mojo:541-566): logit = dot * sx, written to logits (if
-// any) and folded into this thread's argmax candidate (sm.thr_v / thr_i).
+// Per-channel int8 head rows of one or two chunks (dot_row_i16 per channel,
+// tensor.mojo:541-566): threads 0-127 take the chunk in slot0, threads
+// 128-255 the one in slot1 (if any). Thread (r, q) accumulates lanes
+// 4q..4q+3 of row r over all the row's 32-column chunks (the int32 sums are
+// exact in any order), converts them, and the row's four threads add the 16
+// lanes as the halving tree. logit = dot * sx goes to logits (if any) and
+// into this thread's argmax candidate (sm.thr_v / thr_i). No barrier: the
+// caller's barrier ends the use of the slots.
 template <int IN>
-__device__ __noinline__ void mk_head_tile(MkSmem &sm, const uint8_t *slot, const MkChunk &ch, float sx,
-                                          float *logits) {
-  constexpr int nch = IN >> 5, SPAN = nch / 2;
+__device__ __noinline__ void mk_head_pair(MkSmem &sm, const uint8_t *slot0, const MkChunk &ch0, const uint8_t *slot1,
+                                          const MkChunk *ch1, float sx, float *logits) {
+  constexpr int nch = IN >> 5;
+  const int half = threadIdx.x >> 7;
+  if (half == 1 && !ch1) return;  // whole warps
+  const uint8_t *slot = half ? slot1 : slot0;
+  const MkChunk &ch = half ? *ch1 : ch0;
   const int R = ch.r1 - ch.r0;
   const int *xp32 = (const int *)sm.xq;
-  const uint16_t *scl = (const uint16_t *)(slot + ch.scale_off);
-  const uint8_t *zpp = slot + ch.zp_off;
-  // integer phase: items (row, q, part), 2 parts of nch/2 chunks, R <= 32
-  {
-    const int q = threadIdx.x & 3, r = (threadIdx.x >> 2) & 31, p = threadIdx.x >> 7;
-    int acc[4] = {0, 0, 0, 0};
-    if (r < R) {
-      const uint8_t *rp = slot + (size_t)r * IN;
-      const int c0 = p * SPAN, rot = r % SPAN;
-#pragma unroll
-      for (int cc = 0; cc < SPAN; cc++) {
-        int c = cc + rot;
-        c = c0 + (c >= SPAN ? c - SPAN : c);
-        uint2 v = *(const uint2 *)(rp + c * 32 + 8 * q);
-        int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
-        acc[0] = dp2a_lo_su(xv.x, v.x, acc[0]);
-        acc[1] = dp2a_hi_su(xv.y, v.x, acc[1]);
-        acc[2] = dp2a_lo_su(xv.z, v.y, acc[2]);
-        acc[3] = dp2a_hi_su(xv.w, v.y, acc[3]);
-      }
-    }
-    int *ln = sm.lanes + (p * 32 + r) * 16 + 4 * q;
-#pragma unroll
-    for (int j = 0; j < 4; j++) ln[j] = acc[j];
+  const int q = threadIdx.x & 3, r = (threadIdx.x >> 2) & 31;
+  const int rr = r < R ? r : 0;  // rows past R repeat row 0 (their results are dropped)
+  const uint8_t *rp = slot + (size_t)rr * IN;
+  // a row visits its chunks in an order rotated by the row, so that the
+  // rows of a warp read different banks
+  const int rot = rr % nch;
+  int acc[4] = {0, 0, 0, 0};
+#pragma unroll 8
+  for (int cc = 0; cc < nch; cc++) {
+    int c = cc + rot;
+    c = c >= nch ? c - nch : c;
+    const uint2 v = *(const uint2 *)(rp + c * 32 + 8 * q);
+    const int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
+    acc[0] = dp2a_lo_su(xv.x, v.x, acc[0]);
+    acc[1] = dp2a_hi_su(xv.y, v.x, acc[1]);
+    acc[2] = dp2a_lo_su(xv.z, v.y, acc[2]);
+    acc[3] = dp2a_hi_su(xv.w, v.y, acc[3]);
   }
-  cta_sync();
-  if (threadIdx.x < 128) {
-    const int q = threadIdx.x & 3, r = threadIdx.x >> 2;
-    const int rr = r < R ? r : 0;
-    const int zp = zpp[rr];
-    const float sc = __half2float(__ushort_as_half(scl[rr]));
-    float f[4];
+  const int zp = (slot + ch.zp_off)[rr];
+  const float sc = __half2float(__ushort_as_half(((const uint16_t *)(slot + ch.scale_off))[rr]));
+  float f[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-      int L = 4 * q + j;
-      int acc = sm.lanes[rr * 16 + L] + sm.lanes[(32 + rr) * 16 + L];
-      acc = (int)((unsigned)acc - (unsigned)(zp * sm.xs[L]));
-      f[j] = fmaf((float)acc, sc, 0.0f);
-    }
-    // halving tree (lanes 4q..4q+3 in thread q of 4)
-    float b[4];
+  for (int j = 0; j < 4; j++) {
+    const int a = (int)((unsigned)acc[j] - (unsigned)(zp * sm.xs[4 * q + j]));
+    f[j] = fmaf((float)a, sc, 0.0f);
+  }
+  // halving tree: lanes i and i+8 from thread q^2, i and i+4 from q^1
+  float b[4];
 #pragma unroll
-    for (int j = 0; j < 4; j++) b[j] = f[j] + __shfl_xor_sync(0xffffffffu, f[j], 2);
+  for (int j = 0; j < 4; j++) b[j] = f[j] + __shfl_xor_sync(0xffffffffu, f[j], 2);
 #pragma unroll
-    for (int j = 0; j < 4; j++) b[j] = b[j] + __shfl_xor_sync(0xffffffffu, b[j], 1);
-    const float dot = (b[0] + b[2]) + (b[1] + b[3]);
-    if (q == 0 && r < R) {
-      const int o = ch.r0 + r;
-      const float v = dot * sx;
-      if (logits) logits[o] = v;
-      const int t = threadIdx.x;
-      if (better(v, o, sm.thr_v[t], sm.thr_i[t])) {
-        sm.thr_v[t] = v;
-        sm.thr_i[t] = o;
-      }
+  for (int j = 0; j < 4; j++) b[j] = b[j] + __shfl_xor_sync(0xffffffffu, b[j], 1);
+  const float dot = (b[0] + b[2]) + (b[1] + b[3]);
+  if (q == 0 && r < R) {
+    const int o = ch.r0 + r;
+    const float v = dot * sx;
+    if (logits) logits[o] = v;
+    const int t = threadIdx.x;
+    if (better(v, o, sm.thr_v[t], sm.thr_i[t])) {
+      sm.thr_v[t] = v;
+      sm.thr_i[t] = o;
     }
   }
-  cta_sync();
 }
 
 // Starts copying this head's cached keys, values and their scales for
@@ -865,9 +889,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       tlast = t;
     }
   };
-  auto slot_wait = [&]() -> int {  // slot of chunk `seq`, or -1 on timeout
-    const int slot = (int)(seq % MK_NSLOT);
-    const unsigned par = (unsigned)((seq / MK_NSLOT) & 1);
+  auto slot_wait = [&](int ahead = 0) -> int {  // slot of chunk `seq + ahead`, or -1 on timeout
+    const long long q = seq + ahead;
+    const int slot = (int)(q % MK_NSLOT);
+    const unsigned par = (unsigned)((q / MK_NSLOT) & 1);
     long long t0 = clock64();
     while (!mbar_try_wait(&sm.full[slot], par)) {
       if (!mk_alive(a, sm, t0, 1)) return -1;
@@ -876,7 +901,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     return slot;
   };
   // Called after the barrier that ends the use of the slot (the last one in
-  // mk_gemv_blk4 / mk_head_tile).
+  // mk_gemv_blk4, or the one after mk_head_pair).
   auto slot_release = [&]() {
     if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
     seq++;
@@ -976,14 +1001,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     const float sx = mk_quantize<768, false>(sm, mk_layernorm(sm, sm.xf));
     sm.thr_v[tid] = -__int_as_float(0x7f800000);
     sm.thr_i[tid] = 0x7fffffff;
-    for (; ci < a.nchunks; ci++) {
-      const int slot = slot_wait();
-      if (slot < 0) {
+    for (; ci < a.nchunks; ci += 2) {  // two chunks per round
+      const bool two = ci + 1 < a.nchunks;
+      const int s0 = slot_wait(), s1 = two ? slot_wait(1) : 0;
+      if (s0 < 0 || s1 < 0) {
         ok = false;
         break;
       }
-      mk_head_tile<768>(sm, sm.ring[slot], sm.chunks[ci], sx, a.logits);
+      mk_head_pair<768>(sm, sm.ring[s0], sm.chunks[ci], sm.ring[s1], two ? &sm.chunks[ci + 1] : nullptr, sx,
+                        a.logits);
+      cta_sync();
       slot_release();
+      if (two) slot_release();
     }
     if (!ok) break;
     tick(PF_HEAD);
