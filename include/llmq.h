@@ -218,8 +218,9 @@ llmq_status llmq_sample(llmq_ctx *ctx, const float *logits_dev, int V, float tem
 /* generate (gpt2t.mojo:965-980) with sample in place of the argmax, without
  * the stop at EOT: `steps` ids into out_ids_host; *rng_state (host) is the
  * Rng state, read before and written back after. temperature <= 0 is
- * llmq_generate. The draws run on the device after each head; the decode
- * steps are CUDA graph launches (or eager in LLMQ_MODE_EAGER). */
+ * llmq_generate. The draws run on the device after each head; in
+ * LLMQ_MODE_PERSISTENT each decode step is one launch of the persistent
+ * kernel, otherwise a CUDA graph launch (or eager in LLMQ_MODE_EAGER). */
 llmq_status llmq_generate_sampled(llmq_ctx *ctx, llmq_model *m, const int *prompt_host, int n_prompt, int steps,
                                   float temperature, int k, unsigned long long *rng_state, int *out_ids_host);
 /* Per-operation timers of the persistent decode kernel, as the reference's

@@ -39,6 +39,7 @@ struct llmq_ctx {
   unsigned long long *samp_keys = nullptr;
   unsigned long long *samp_cand = nullptr;
   unsigned long long *samp_rng = nullptr;
+  int *samp_done = nullptr;  // set by topk_fast_kernel when it finished the draw
   int samp_n = 0;
 };
 
@@ -260,6 +261,9 @@ cudaError_t configure_kernels() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)merge_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)merge_smem(kMergeCap));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void *)topk_fast_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)fast_smem());
   return e;
 }
 }  // namespace
@@ -328,7 +332,7 @@ llmq_status llmq_destroy(llmq_ctx *ctx) {
   if (ctx->scratch) cudaFree(ctx->scratch);
   if (ctx->state) cudaFree(ctx->state);
   if (ctx->tc_err) cudaFree(ctx->tc_err);
-  for (void *q : {(void *)ctx->samp_keys, (void *)ctx->samp_cand, (void *)ctx->samp_rng})
+  for (void *q : {(void *)ctx->samp_keys, (void *)ctx->samp_cand, (void *)ctx->samp_rng, (void *)ctx->samp_done})
     if (q) cudaFree(q);
   if (ctx->own) cudaStreamDestroy(ctx->own);
   delete ctx;
@@ -1419,6 +1423,7 @@ static llmq_status sample_scratch(llmq_ctx *ctx, int V) {
   const int n = std::max(pow2_at_least(V), kSortChunk);
   if (!ctx->samp_cand) CK(cudaMalloc(&ctx->samp_cand, sizeof(unsigned long long) * kMergeCap));
   if (!ctx->samp_rng) CK(cudaMalloc(&ctx->samp_rng, sizeof(unsigned long long)));
+  if (!ctx->samp_done) CK(cudaMalloc(&ctx->samp_done, sizeof(int)));
   if (n <= ctx->samp_n) return LLMQ_OK;
   CK(cudaStreamSynchronize(ctx->stream));
   if (ctx->samp_keys) cudaFree(ctx->samp_keys);
@@ -1438,10 +1443,13 @@ static llmq_status enqueue_sample(llmq_ctx *ctx, const float *logits, int V, flo
   const int chunks = (V + kSortChunk - 1) / kSortChunk;
   if (kk <= kTopkSmall && (long long)chunks * kk <= kMergeCap) {
     const int n_cand = chunks * kk, n_pad = std::max(pow2_at_least(n_cand), 2);
-    sort_chunk_kernel<<<chunks, kSortThreads, 0, s>>>(logits, V, nullptr, 2, kSortChunk, 1, ctx->samp_cand, kk);
+    int *done = ctx->samp_done;
+    topk_fast_kernel<<<1, kSortThreads, fast_smem(), s>>>(logits, V, kk, temperature, rng, o, topk_ids, done);
+    CKL();
+    sort_chunk_kernel<<<chunks, kSortThreads, 0, s>>>(logits, V, nullptr, 2, kSortChunk, 1, ctx->samp_cand, kk, done);
     CKL();
     merge_draw_kernel<<<1, kSortThreads, merge_smem(n_pad), s>>>(ctx->samp_cand, n_cand, n_pad, kk, logits,
-                                                                   temperature, rng, o, topk_ids);
+                                                                   temperature, rng, o, topk_ids, done);
     CKL();
     return LLMQ_OK;
   }
@@ -1553,14 +1561,33 @@ static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps, c
 }
 
 // With a SampleSpec every head's argmax is replaced by a draw: the head
-// still writes the logits, the draw overwrites the id and the next token
-// (the persistent kernel, whose head reduces to the argmax in place, is not
-// used then).
+// still writes the logits, the draw overwrites the id and the next token. In
+// the persistent mode the kernel then runs one token per launch (it writes
+// the logits, the draw writes the token the next launch embeds).
 static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits,
                                   const SampleSpec *sp = nullptr) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
   if (m->float_only) return float_generation(m, T, pos0, steps, sp);
+  if (sp && m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok) {
+    llmq_status st;
+    int pos = pos0, i = 0;
+    if (T > 1) {
+      if ((st = run_prompt_tail(m, T, pos0)) != LLMQ_OK) return st;
+      st = enqueue_sample(ctx, m->logits, m->V, sp->temperature, sp->k, sp->rng,
+                          SampleOut{m->ids, m->tokens, nullptr, nullptr, nullptr}, nullptr, s);
+      if (st != LLMQ_OK) return st;
+      pos = pos0 + T;
+      i = 1;
+    }
+    for (; i < steps; i++, pos++) {
+      if ((st = run_mega(m, m->tokens, pos, 1, m->ids + i, m->logits)) != LLMQ_OK) return st;
+      st = enqueue_sample(ctx, m->logits, m->V, sp->temperature, sp->k, sp->rng,
+                          SampleOut{m->ids + i, m->tokens, nullptr, nullptr, nullptr}, nullptr, s);
+      if (st != LLMQ_OK) return st;
+    }
+    return LLMQ_OK;
+  }
   const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok && !sp;
   const SampleOut so{nullptr, nullptr, &m->state->token, &m->state->step, m->ids};
   auto draw = [&]() -> llmq_status {

@@ -12,8 +12,11 @@
 // kSortChunk keys sort in shared memory, the levels above a chunk take one
 // global compare-exchange launch per stride plus a shared-memory pass for the
 // strides inside a chunk.
-//   k <= kTopkSmall and (chunks x k) <= kMergeCap: every chunk keeps its first
-//     k keys, one CTA sorts those candidates and draws (two launches);
+//   k <= kTopkSmall and (chunks x k) <= kMergeCap: topk_fast_kernel (one CTA:
+//     a threshold from per-thread maxima, the logits above it sorted); when
+//     too many logits tie at the threshold, every chunk keeps its first k
+//     keys and one CTA sorts those candidates and draws (two more launches,
+//     which return at once when the first kernel succeeded);
 //   otherwise: the whole padded key array is sorted, one CTA draws.
 // The draw is one thread: the float32 sum and the subtraction walk are
 // sequential chains in the reference's order (the weights are computed by the
@@ -75,7 +78,9 @@ __device__ void bitonic_levels(u64 *k, int n, int base, int s_lo, int s_hi, bool
 // keys past V are all ones) or read from keys; levels [s_lo, s_hi]; written
 // back to keys, or its first kk keys to cand[chunk * kk ..].
 __global__ void __launch_bounds__(kSortThreads)
-    sort_chunk_kernel(const float *logits, int V, u64 *keys, int s_lo, int s_hi, int all_asc, u64 *cand, int kk) {
+    sort_chunk_kernel(const float *logits, int V, u64 *keys, int s_lo, int s_hi, int all_asc, u64 *cand, int kk,
+                      const int *done = nullptr) {
+  if (done && *done) return;  // topk_fast_kernel finished the draw
   __shared__ u64 sk[kSortChunk];
   const int base = blockIdx.x * kSortChunk;
   for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) {
@@ -150,7 +155,8 @@ __device__ void draw_sorted(const u64 *sorted, int k, const float *logits, float
 // sort, then draw from the first k.
 __global__ void __launch_bounds__(kSortThreads)
     merge_draw_kernel(const u64 *cand, int n_cand, int n_pad, int k, const float *logits, float temperature, u64 *rng,
-                      SampleOut o, int *topk_ids) {
+                      SampleOut o, int *topk_ids, const int *done = nullptr) {
+  if (done && *done) return;  // topk_fast_kernel finished the draw
   extern __shared__ __align__(16) unsigned char smem[];
   u64 *sk = reinterpret_cast<u64 *>(smem);
   float *p = reinterpret_cast<float *>(sk + n_pad);
@@ -162,6 +168,66 @@ __global__ void __launch_bounds__(kSortThreads)
     return;
   }
   draw_sorted(sk, k, logits, temperature, p, rng, o);
+}
+
+// One-CTA top-k for k <= kTopkSmall, the usual case. Each thread takes the
+// logits t, t + 1024, ... and keeps their largest value; the k-th largest of
+// those 1024 maxima, T, has at least k logits >= T (k threads each own one),
+// so the top k are among the logits >= T. Those are gathered (typically a
+// few times k of them) and sorted as 64-bit keys. When more than kFastCap
+// logits reach T (large ties), the kernel leaves *done = 0 and the two
+// chunk-sort kernels queued after it do the work; otherwise it draws (or
+// writes the ids), sets *done = 1, and they return at once.
+constexpr int kFastCap = 8192;
+
+inline size_t fast_smem() { return (size_t)kSortThreads * 8 + (size_t)kFastCap * 8 + (size_t)kTopkSmall * 4; }
+
+__device__ __forceinline__ unsigned value_key(float v) {
+  unsigned u = __float_as_uint(v);
+  if ((u & 0x7fffffffu) == 0) u = 0;
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+    topk_fast_kernel(const float *logits, int V, int k, float temperature, u64 *rng, SampleOut o, int *topk_ids,
+                     int *done) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  u64 *tmax = reinterpret_cast<u64 *>(smem);          // [1024] (~max key) << 32 | thread
+  u64 *cand = tmax + kSortThreads;                     // [kFastCap]
+  float *p = reinterpret_cast<float *>(cand + kFastCap);  // [kTopkSmall]
+  __shared__ int cnt;
+  const int t = threadIdx.x;
+  unsigned mk = 0;
+  for (int i = t; i < V; i += kSortThreads) mk = max(mk, value_key(logits[i]));
+  tmax[t] = ((u64)(~mk) << 32) | (unsigned)t;
+  if (t == 0) cnt = 0;
+  __syncthreads();
+  bitonic_levels(tmax, kSortThreads, 0, 2, kSortThreads, false);
+  const unsigned T = ~(unsigned)(tmax[k - 1] >> 32);
+  for (int i = t; i < V; i += kSortThreads) {
+    const unsigned key = value_key(logits[i]);
+    if (key >= T) {
+      const int j = atomicAdd(&cnt, 1);
+      if (j < kFastCap) cand[j] = ((u64)(~key) << 32) | (unsigned)i;
+    }
+  }
+  __syncthreads();
+  const int n = cnt;
+  if (n > kFastCap) {
+    if (t == 0) *done = 0;
+    return;
+  }
+  int n_pad = 2;
+  while (n_pad < n) n_pad <<= 1;
+  for (int i = n + t; i < n_pad; i += kSortThreads) cand[i] = ~0ull;
+  __syncthreads();
+  bitonic_levels(cand, n_pad, 0, 2, n_pad, false);
+  if (t == 0) *done = 1;
+  if (topk_ids) {
+    for (int i = t; i < k; i += kSortThreads) topk_ids[i] = key_id(cand[i]);
+    return;
+  }
+  draw_sorted(cand, k, logits, temperature, p, rng, o);
 }
 
 constexpr int kDrawStage = 8192;  // weights of the global-key draw staged per round
