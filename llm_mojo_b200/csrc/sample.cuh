@@ -74,6 +74,33 @@ __device__ void bitonic_levels(u64 *k, int n, int base, int s_lo, int s_hi, bool
   }
 }
 
+// Ascending bitonic sort of 64 keys held by one warp, key lane + 32 h in
+// a[h]: strides below 32 pair lanes (shuffles), stride 32 pairs a[0] with
+// a[1] in the same lane.
+__device__ __forceinline__ void warp_sort64(u64 a[2]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 2; s <= 64; s <<= 1) {
+#pragma unroll
+    for (int j = s >> 1; j > 0; j >>= 1) {
+      if (j == 32) {
+        // e = lane vs lane + 32; level s = 64 is ascending
+        const u64 lo = min(a[0], a[1]), hi = max(a[0], a[1]);
+        a[0] = lo;
+        a[1] = hi;
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int e = lane + 32 * h;
+          const u64 o = __shfl_xor_sync(0xffffffffu, a[h], j);
+          const bool lower = (e & j) == 0, asc = (e & s) == 0;
+          a[h] = (lower == asc) ? min(a[h], o) : max(a[h], o);
+        }
+      }
+    }
+  }
+}
+
 // One chunk of kSortChunk keys: built from the logits (logits != nullptr,
 // keys past V are all ones) or read from keys; levels [s_lo, s_hi]; written
 // back to keys, or its first kk keys to cand[chunk * kk ..].
@@ -83,8 +110,9 @@ __global__ void __launch_bounds__(kSortThreads)
   if (done && *done) return;  // topk_fast_kernel finished the draw
   __shared__ u64 sk[kSortChunk];
   const int base = blockIdx.x * kSortChunk;
-  for (int i = threadIdx.x; i < kSortChunk; i += blockDim.x) {
-    const int g = base + i;
+#pragma unroll
+  for (int u = 0; u < kSortChunk / kSortThreads; u++) {
+    const int i = threadIdx.x + u * kSortThreads, g = base + i;
     sk[i] = logits ? (g < V ? sample_key(logits[g], g) : ~0ull) : keys[g];
   }
   __syncthreads();
@@ -170,10 +198,11 @@ __global__ void __launch_bounds__(kSortThreads)
   draw_sorted(sk, k, logits, temperature, p, rng, o);
 }
 
-// One-CTA top-k for k <= kTopkSmall, the usual case. Each thread takes the
-// logits t, t + 1024, ... and keeps their largest value; the k-th largest of
-// those 1024 maxima, T, has at least k logits >= T (k threads each own one),
-// so the top k are among the logits >= T. Those are gathered (typically a
+// One-CTA top-k for k <= kTopkSmall, the usual case. Each thread takes its
+// share of the logits (for_each_logit) and keeps their largest value; the k-th largest
+// maximum of disjoint groups of them, T, has at least k logits >= T (k groups
+// each own one), so the top k are among the logits >= T. The groups are 16
+// threads for k <= 64 (a one-warp sort of 64 maxima), single threads above. Those are gathered (typically a
 // few times k of them) and sorted as 64-bit keys. When more than kFastCap
 // logits reach T (large ties), the kernel leaves *done = 0 and the two
 // chunk-sort kernels queued after it do the work; otherwise it draws (or
@@ -188,40 +217,104 @@ __device__ __forceinline__ unsigned value_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Calls f(value, index) for every logit, the elements of thread t being
+// t, t + 1024, ... in units of float4 when the array is 16-byte aligned (8
+// loads in flight per thread), single floats otherwise.
+template <class F>
+__device__ __forceinline__ void for_each_logit(const float *logits, int V, F f) {
+  const int t = threadIdx.x;
+  constexpr int U = 8;
+  if ((reinterpret_cast<uintptr_t>(logits) & 15) == 0) {
+    const float4 *l4 = reinterpret_cast<const float4 *>(logits);
+    const int V4 = V >> 2;
+    for (int i0 = t; i0 < V4; i0 += U * kSortThreads) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) v[u] = i0 + u * kSortThreads < V4 ? l4[i0 + u * kSortThreads] : float4{};
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (i0 + u * kSortThreads < V4) {
+          const int b = 4 * (i0 + u * kSortThreads);
+          f(v[u].x, b);
+          f(v[u].y, b + 1);
+          f(v[u].z, b + 2);
+          f(v[u].w, b + 3);
+        }
+    }
+    for (int i = 4 * V4 + t; i < V; i += kSortThreads) f(logits[i], i);
+  } else {
+    for (int i0 = t; i0 < V; i0 += U * kSortThreads) {
+      float v[U];
+#pragma unroll
+      for (int u = 0; u < U; u++) v[u] = i0 + u * kSortThreads < V ? logits[i0 + u * kSortThreads] : 0.0f;
+#pragma unroll
+      for (int u = 0; u < U; u++)
+        if (i0 + u * kSortThreads < V) f(v[u], i0 + u * kSortThreads);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kSortThreads)
     topk_fast_kernel(const float *logits, int V, int k, float temperature, u64 *rng, SampleOut o, int *topk_ids,
                      int *done) {
   extern __shared__ __align__(16) unsigned char smem[];
-  u64 *tmax = reinterpret_cast<u64 *>(smem);          // [1024] (~max key) << 32 | thread
-  u64 *cand = tmax + kSortThreads;                     // [kFastCap]
+  u64 *tmax = reinterpret_cast<u64 *>(smem);             // [1024] (~max key) << 32 | group
+  u64 *cand = tmax + kSortThreads;                       // [kFastCap]
   float *p = reinterpret_cast<float *>(cand + kFastCap);  // [kTopkSmall]
   __shared__ int cnt;
-  const int t = threadIdx.x;
+  __shared__ unsigned thr;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   unsigned mk = 0;
-  for (int i = t; i < V; i += kSortThreads) mk = max(mk, value_key(logits[i]));
-  tmax[t] = ((u64)(~mk) << 32) | (unsigned)t;
+  for_each_logit(logits, V, [&](float v, int) { mk = max(mk, value_key(v)); });
   if (t == 0) cnt = 0;
+  if (k <= 64) {
+    // groups of 16 threads: 64 group maxima, the k-th largest by one warp
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) mk = max(mk, __shfl_xor_sync(0xffffffffu, mk, off));
+    if ((lane & 15) == 0) tmax[warp * 2 + (lane >> 4)] = ((u64)(~mk) << 32) | (unsigned)(warp * 2 + (lane >> 4));
+    __syncthreads();
+    if (warp == 0) {
+      u64 a[2] = {tmax[lane], tmax[lane + 32]};
+      warp_sort64(a);
+      const u64 kth = __shfl_sync(0xffffffffu, (k - 1) >= 32 ? a[1] : a[0], (k - 1) & 31);
+      if (lane == 0) thr = ~(unsigned)(kth >> 32);
+    }
+  } else {
+    tmax[t] = ((u64)(~mk) << 32) | (unsigned)t;
+    __syncthreads();
+    bitonic_levels(tmax, kSortThreads, 0, 2, kSortThreads, false);
+    if (t == 0) thr = ~(unsigned)(tmax[k - 1] >> 32);
+  }
   __syncthreads();
-  bitonic_levels(tmax, kSortThreads, 0, 2, kSortThreads, false);
-  const unsigned T = ~(unsigned)(tmax[k - 1] >> 32);
-  for (int i = t; i < V; i += kSortThreads) {
-    const unsigned key = value_key(logits[i]);
+  const unsigned T = thr;
+  for_each_logit(logits, V, [&](float v, int i) {
+    const unsigned key = value_key(v);
     if (key >= T) {
       const int j = atomicAdd(&cnt, 1);
       if (j < kFastCap) cand[j] = ((u64)(~key) << 32) | (unsigned)i;
     }
-  }
+  });
   __syncthreads();
   const int n = cnt;
   if (n > kFastCap) {
     if (t == 0) *done = 0;
     return;
   }
-  int n_pad = 2;
-  while (n_pad < n) n_pad <<= 1;
-  for (int i = n + t; i < n_pad; i += kSortThreads) cand[i] = ~0ull;
-  __syncthreads();
-  bitonic_levels(cand, n_pad, 0, 2, n_pad, false);
+  if (n <= 64) {
+    if (warp == 0) {
+      u64 a[2] = {lane < n ? cand[lane] : ~0ull, lane + 32 < n ? cand[lane + 32] : ~0ull};
+      warp_sort64(a);
+      cand[lane] = a[0];
+      cand[lane + 32] = a[1];
+    }
+    __syncthreads();
+  } else {
+    int n_pad = 128;
+    while (n_pad < n) n_pad <<= 1;
+    for (int i = n + t; i < n_pad; i += kSortThreads) cand[i] = ~0ull;
+    __syncthreads();
+    bitonic_levels(cand, n_pad, 0, 2, n_pad, false);
+  }
   if (t == 0) *done = 1;
   if (topk_ids) {
     for (int i = t; i < k; i += kSortThreads) topk_ids[i] = key_id(cand[i]);
