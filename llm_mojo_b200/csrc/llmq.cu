@@ -75,6 +75,7 @@ struct llmq_model {
   int n_layer, C, V, max_t, n_head;
   std::vector<const llmq_weight *> mats;
   const llmq_weight *head;
+  const llmq_weight *embed = nullptr;  // token embeddings when they are not the head (an untied GGUF output.weight)
   llmq_kv *kv;
   float *small;  // device copy of the float32 parameters
   float *x, *xn, *qkv, *att, *fc, *logits;
@@ -1256,7 +1257,7 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
 llmq_status enqueue_blocks(llmq_model *m, int T, int pos0, cudaStream_t s) {
   llmq_ctx *ctx = m->ctx;
   const int C = m->C;
-  const llmq_weight *hd = m->head;
+  const llmq_weight *hd = m->embed ? m->embed : m->head;
   if (hd->kind == WK_AFFINE) {
     embed_rows_kernel<<<T, 256, 0, s>>>(hd->view(), m->wpe(), m->x, m->tokens, pos0);
   } else if (hd->kind == WK_DENSE) {
@@ -2395,6 +2396,7 @@ extern "C" {
 llmq_status llmq_model_save(llmq_ctx *ctx, const llmq_model *m, const char *path) {
   if (!ctx || !m || !path) return fail(ctx, LLMQ_ERR_INVALID, "null argument");
   if (m->n_layer != kSavedLayers) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "saved models have 12 layers");
+  if (m->embed) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "the saved format holds one tied embedding / head matrix");
   CK(cudaSetDevice(ctx->device));
   CK(cudaStreamSynchronize(ctx->stream));
   FILE *f = fopen(path, "wb");
@@ -2495,9 +2497,11 @@ llmq_status llmq_model_load_gguf(llmq_ctx *ctx, const char *path, int kv_kind, i
                                      "ffn_norm.weight", "ffn_norm.bias", "ffn_up.bias", "ffn_down.bias"};
   static const int vec_lens[8] = {1, 1, 3, 1, 1, 1, 4, 1};
   static const long long outs[4] = {3 * C, C, 4 * C, C}, ins[4] = {C, C, C, 4 * C};
-  if (g.tensors.count("output.weight")) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "untied output heads are not supported");
+  // ws[0] the head (output.weight, else the tied token_embd.weight), ws[1..48]
+  // the layer matrices, ws[49] token_embd.weight when the head is untied
+  const bool tied = g.tensors.count("output.weight") == 0;
   llmq_weight *w = nullptr;
-  llmq_status st = matrix("token_embd.weight", 50257, C, &w);
+  llmq_status st = matrix(tied ? "token_embd.weight" : "output.weight", 50257, C, &w);
   if (st != LLMQ_OK) return cleanup(st);
   ws.push_back(w);
   std::vector<float> small((size_t)L * 13 * C + 1024 * C + 2 * C);
@@ -2517,9 +2521,14 @@ llmq_status llmq_model_load_gguf(llmq_ctx *ctx, const char *path, int kv_kind, i
   off += (size_t)1024 * C;
   if ((st = f32("output_norm.weight", C, small.data() + off)) != LLMQ_OK) return cleanup(st);
   if ((st = f32("output_norm.bias", C, small.data() + off + C)) != LLMQ_OK) return cleanup(st);
+  if (!tied) {
+    if ((st = matrix("token_embd.weight", 50257, C, &w)) != LLMQ_OK) return cleanup(st);
+    ws.push_back(w);
+  }
   llmq_model *m = nullptr;
   if ((st = llmq_model_create(ctx, L, ws.data() + 1, ws[0], small.data(), kv_kind, max_t, &m)) != LLMQ_OK)
     return cleanup(st);
+  if (!tied) m->embed = ws.back();
   m->owned = ws;
   *out = m;
   return LLMQ_OK;

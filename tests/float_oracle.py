@@ -10,8 +10,9 @@ from oracle import oracle as O
 DT = {"f32": 0, "bf16": 2}
 
 
-def oracle_float_forward(tensors, fmt, tokens, n_layer):
-    """The float model's forward_all composed from oracle kernels."""
+def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
+    """The float model's forward_all composed from oracle kernels; head (GGUF
+    only) is an untied [V, C] output matrix, the logits' Q6_K head."""
     from llm_mojo_b200 import gguf_blocks as G
     from llm_mojo_b200 import synth
 
@@ -80,6 +81,8 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer):
     V = wte.shape[0]
     logits = np.zeros((T, V), np.float32)
     if fmt == "gguf-q4_k":
+        if head is not None:
+            hb = G.quantize(np.ascontiguousarray(head, dtype=np.float32), G.Q6_K)
         for t in range(T):
             O.lib().oq_gguf_head_i16(G.Q6_K, O.ptr(hb), V, Cn, O.ptr(np.ascontiguousarray(xn[t])), O.ptr(logits[t]))
         O.lib().oq_qkv8_free(kv8)

@@ -5,7 +5,8 @@ the gguf package's writer; the same blocks FloatModel('gguf-q4_k') packs."""
 import numpy as np
 
 
-def write_gpt2_gguf(path: str, tensors: dict, n_layer: int = 12):
+def write_gpt2_gguf(path: str, tensors: dict, n_layer: int = 12, head=None):
+    """head: an untied [V, C] output matrix, written as output.weight (Q6_K)."""
     import gguf
 
     from llm_mojo_b200 import gguf_blocks as G
@@ -30,6 +31,8 @@ def write_gpt2_gguf(path: str, tensors: dict, n_layer: int = 12):
             quant(f"blk.{l}.{g}.weight", np.ascontiguousarray(tensors[f"h.{l}.{hf}"].T), G.Q4_K, Q.Q4_K)
         for g, hf in vecs.items():
             w.add_tensor(f"blk.{l}.{g}", np.ascontiguousarray(tensors[f"h.{l}.{hf}"], dtype=np.float32))
+    if head is not None:
+        quant("output.weight", head, G.Q6_K, Q.Q6_K)
     w.add_tensor("output_norm.weight", np.ascontiguousarray(tensors["ln_f.weight"], dtype=np.float32))
     w.add_tensor("output_norm.bias", np.ascontiguousarray(tensors["ln_f.bias"], dtype=np.float32))
     w.write_header_to_file()

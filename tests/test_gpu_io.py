@@ -122,6 +122,31 @@ def test_gguf_file_load(torch, ctx, gpt2_tensors, tmp_path):
         ref.free()
 
 
+def test_gguf_untied_output_head(torch, ctx, gpt2_tensors, tmp_path):
+    """An untied output.weight (load_gguf, gpt2t.mojo:733-736): embeddings
+    come from token_embd, logits from output.weight, equal to the oracle's
+    model built the same way."""
+    from float_oracle import oracle_float_forward
+    from gguf_file import write_gpt2_gguf
+    from llm_mojo_b200._lib import LlmqError
+    from llm_mojo_b200.model import LoadedModel
+
+    head = (np.random.default_rng(17).standard_normal((50257, 768)) * 0.02).astype(np.float32)
+    path = str(tmp_path / "gpt2-q4_k-untied.gguf")
+    write_gpt2_gguf(path, gpt2_tensors, head=head)
+    lm = LoadedModel(ctx, path, kv="int8", max_t=64, gguf=True)
+    try:
+        toks = [50256, 464, 3290, 318, 257]
+        got = torch.zeros((5, 50257), dtype=torch.float32, device="cuda")
+        lm.forward_all(toks, got)
+        want = oracle_float_forward(gpt2_tensors, "gguf-q4_k", toks, 12, head=head)
+        assert np.array_equal(got.cpu().numpy().view(np.uint32), want.view(np.uint32))
+        with pytest.raises(LlmqError):
+            lm.save(str(tmp_path / "untied.llmm"))  # the saved format has one tied matrix
+    finally:
+        lm.free()
+
+
 def test_load_rejects_bad_files(ctx, tmp_path):
     from llm_mojo_b200._lib import LlmqError
     from llm_mojo_b200.model import LoadedModel
