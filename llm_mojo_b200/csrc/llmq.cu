@@ -1102,10 +1102,21 @@ llmq_status mega_setup(llmq_model *m) {
       off += ch.bytes;
       return true;
     };
+    // The QKV and PROJ rows go to the CTAs without an attention head: the
+    // attention CTAs start their head as soon as its q, k, v arrive and
+    // poll the heads' outputs without a PROJ share of their own.
+    const int nh = m->n_head;
     for (int l = 0; l < m->n_layer; l++)
       for (int j = 0; j < 4; j++) {
         const llmq_weight *w = m->mats[4 * l + j];
-        int r0 = (int)((long long)w->rows * c / G), r1 = (int)((long long)w->rows * (c + 1) / G);
+        int r0, r1;
+        if (j <= 1) {
+          r0 = c < nh ? 0 : (int)((long long)w->rows * (c - nh) / (G - nh));
+          r1 = c < nh ? 0 : (int)((long long)w->rows * (c + 1 - nh) / (G - nh));
+        } else {
+          r0 = (int)((long long)w->rows * c / G);
+          r1 = (int)((long long)w->rows * (c + 1) / G);
+        }
         if (!add(j, l, w, r0, r1)) return LLMQ_OK;
       }
     int h0 = (int)((long long)m->V * c / G), h1 = (int)((long long)m->V * (c + 1) / G);

@@ -606,6 +606,16 @@ __device__ __forceinline__ float key2f(unsigned k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+// Byte k of w (a signed 8-bit code) as a float, exactly, without an
+// int-to-float conversion: the code + 128 becomes the low byte of the float
+// 2^23 + (code + 128), from which 2^23 + 128 is subtracted.
+__device__ __forceinline__ float s8_byte_to_f(unsigned w_biased, int k) {
+  return __uint_as_float(__byte_perm(w_biased, 0x4B000000u, 0x7540u + k)) - 8388736.0f;
+}
+__device__ __forceinline__ float s8_to_f(int8_t c) {
+  return __uint_as_float(0x4B000000u | ((unsigned)(uint8_t)c ^ 0x80u)) - 8388736.0f;
+}
+
 // Score of one cached position: the 16-lane dot of q with the 64 key codes,
 // reduced by the halving tree, times the key scale and 1/sqrt(64).
 __device__ __forceinline__ float mk_score(const MkSmem &sm, const int8_t *kp, float ksc) {
@@ -614,10 +624,10 @@ __device__ __forceinline__ float mk_score(const MkSmem &sm, const int8_t *kp, fl
   for (int k = 0; k < 16; k++) d[k] = 0.0f;
 #pragma unroll
   for (int i = 0; i < 64; i += 16) {
-    const int4 kv4 = *(const int4 *)(kp + i);
-    const int8_t *kb = (const int8_t *)&kv4;
+    const uint4 kv4 = *(const uint4 *)(kp + i);
+    const unsigned w[4] = {kv4.x ^ 0x80808080u, kv4.y ^ 0x80808080u, kv4.z ^ 0x80808080u, kv4.w ^ 0x80808080u};
 #pragma unroll
-    for (int k = 0; k < 16; k++) d[k] = d[k] + sm.att_q[i + k] * (float)kb[k];
+    for (int k = 0; k < 16; k++) d[k] = d[k] + sm.att_q[i + k] * s8_byte_to_f(w[k >> 2], k & 3);
   }
 #pragma unroll
   for (int k = 0; k < 8; k++) d[k] = d[k] + d[k + 8];
@@ -685,11 +695,24 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
       (warp == 0 ? a.kv.ks : a.kv.vs)[sl] = s;
       sm.red[50 + warp] = s;
     }
-    __syncwarp();
-    if (tid == 0) {
-      const float v = mk_score(sm, sm.att_k, s);
-      sm.att_sc[pos] = v;
-      mx = v;
+    if (warp == 0) {
+      // the new position's score across the warp: lane k < 16 carries lane
+      // k's chain over elements k, 16+k, 32+k, 48+k (lane k + 16 holds the
+      // 16+k and 48+k codes), then the halving tree by shuffles
+      const float c0 = (float)q0, c1 = (float)q1;
+      const float c16 = __shfl_down_sync(0xffffffffu, c0, 16), c48 = __shfl_down_sync(0xffffffffu, c1, 16);
+      const int k = lane & 15;
+      float d = 0.0f + sm.att_q[k] * c0;
+      d = d + sm.att_q[16 + k] * c16;
+      d = d + sm.att_q[32 + k] * c1;
+      d = d + sm.att_q[48 + k] * c48;
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) d = d + __shfl_xor_sync(0xffffffffu, d, o);
+      if (lane == 0) {
+        const float v = (d * s) * 0.125f;
+        sm.att_sc[pos] = v;
+        mx = v;
+      }
     }
   }
   // scores of the cached positions: warps 2-7 take positions 0..191 first
@@ -713,23 +736,24 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
   if (tid == 0) {
     // sequential sum in position order; the next 16 values load while the
     // current 16 add
+    const float4 *e4 = reinterpret_cast<const float4 *>(sm.att_sc);
     float total = 0.0f;
     int s = 0;
-    float e[16];
     if (npos >= 16) {
+      float4 e[4];
 #pragma unroll
-      for (int k = 0; k < 16; k++) e[k] = sm.att_sc[k];
+      for (int k = 0; k < 4; k++) e[k] = e4[k];
       for (; s + 32 <= npos; s += 16) {
-        float nx[16];
+        float4 nx[4];
 #pragma unroll
-        for (int k = 0; k < 16; k++) nx[k] = sm.att_sc[s + 16 + k];
+        for (int k = 0; k < 4; k++) nx[k] = e4[(s >> 2) + 4 + k];
 #pragma unroll
-        for (int k = 0; k < 16; k++) total += e[k];
+        for (int k = 0; k < 4; k++) total = (((total + e[k].x) + e[k].y) + e[k].z) + e[k].w;
 #pragma unroll
-        for (int k = 0; k < 16; k++) e[k] = nx[k];
+        for (int k = 0; k < 4; k++) e[k] = nx[k];
       }
 #pragma unroll
-      for (int k = 0; k < 16; k++) total += e[k];
+      for (int k = 0; k < 4; k++) total = (((total + e[k].x) + e[k].y) + e[k].z) + e[k].w;
       s += 16;
     }
     for (; s < npos; s++) total += sm.att_sc[s];
@@ -747,18 +771,46 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
     const int d = tid;
     float acc = 0.0f;
     if (staged) {
+      // 16 positions at a time; the next 16 load while the current 16 add
       int s = 0;
-      for (; s + 16 <= pos; s += 16) {
+      if (pos >= 16) {
+        const float4 *p4 = reinterpret_cast<const float4 *>(sm.att_ps);
         float pv[16], vv[16];
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
-          pv[k] = sm.att_ps[s + k];
-          vv[k] = (float)sm.vst[s + k][d];
+        for (int k = 0; k < 4; k++) {
+          const float4 q = p4[k];
+          pv[4 * k] = q.x;
+          pv[4 * k + 1] = q.y;
+          pv[4 * k + 2] = q.z;
+          pv[4 * k + 3] = q.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) vv[k] = s8_to_f(sm.vst[k][d]);
+        for (; s + 32 <= pos; s += 16) {
+          float np[16], nv[16];
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const float4 q = p4[(s >> 2) + 4 + k];
+            np[4 * k] = q.x;
+            np[4 * k + 1] = q.y;
+            np[4 * k + 2] = q.z;
+            np[4 * k + 3] = q.w;
+          }
+#pragma unroll
+          for (int k = 0; k < 16; k++) nv[k] = s8_to_f(sm.vst[s + 16 + k][d]);
+#pragma unroll
+          for (int k = 0; k < 16; k++) acc = fmaf(pv[k], vv[k], acc);
+#pragma unroll
+          for (int k = 0; k < 16; k++) {
+            pv[k] = np[k];
+            vv[k] = nv[k];
+          }
         }
 #pragma unroll
         for (int k = 0; k < 16; k++) acc = fmaf(pv[k], vv[k], acc);
+        s += 16;
       }
-      for (; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)sm.vst[s][d], acc);
+      for (; s < pos; s++) acc = fmaf(sm.att_ps[s], s8_to_f(sm.vst[s][d]), acc);
     } else {
       const int8_t *vp = a.kv.v + base * 64 + d;
       for (int s = 0; s < pos; s++) acc = fmaf(sm.att_ps[s], (float)vp[(size_t)s * stride_h * 64], acc);
@@ -918,6 +970,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     return true;
   };
 
+  // A chunk without rows (the attention CTAs have no QKV and PROJ rows): its
+  // ring slot is taken and handed back, the phase is skipped.
+  auto skip_chunk = [&]() -> bool {
+    const int slot = slot_wait();
+    if (slot < 0) return false;
+    cta_sync();
+    slot_release();
+    return true;
+  };
+
   const float *lnf = a.small + (size_t)a.n_layer * 13 * C + (size_t)1024 * C;
   bool ok = true;
   for (int step = 0; ok && step < a.steps; step++) {
@@ -932,22 +994,28 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       {
         if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
         const MkChunk &ch = sm.chunks[ci++];
-        mk_params_load(sm, vec, vec + C, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
-        if (l == 0) {  // x is this CTA's embedding; only the parameters to wait for
-          cp_async_wait_all();
-          cta_sync();
-        } else if (!mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
-          ok = false;
-          break;
+        if (ch.r1 == ch.r0) {
+          if (!(ok = skip_chunk())) break;
+          tick(PF_QKV_WAIT);
+          tick(PF_QKV);
+        } else {
+          mk_params_load(sm, vec, vec + C, vec + 2 * C, ch.r0, ch.r1 - ch.r0);
+          if (l == 0) {  // x is this CTA's embedding; only the parameters to wait for
+            cp_async_wait_all();
+            cta_sync();
+          } else if (!mk_poll(a, sm, a.ll + ll.xout(l - 1), C, flag, sm.xfull, 3)) {
+            ok = false;
+            break;
+          }
+          tick(PF_QKV_WAIT);
+          long long t0 = clock64();
+          const float lmx = mk_layernorm(sm, sm.xfull);
+          sub_tick(pp, PF_LN, t0);
+          const float sx = mk_quantize<768, true>(sm, lmx);
+          sub_tick(pp, PF_QUANT, t0);
+          if (!(ok = gemv(ch, C, sx, 0, a.ll + ll.qkv(l), flag))) break;
+          tick(PF_QKV);
         }
-        tick(PF_QKV_WAIT);
-        long long t0 = clock64();
-        const float lmx = mk_layernorm(sm, sm.xfull);
-        sub_tick(pp, PF_LN, t0);
-        const float sx = mk_quantize<768, true>(sm, lmx);
-        sub_tick(pp, PF_QUANT, t0);
-        if (!(ok = gemv(ch, C, sx, 0, a.ll + ll.qkv(l), flag))) break;
-        tick(PF_QKV);
       }
       // ---- B: KV store + attention (CTA h for head h) ----
       if (cta < a.n_head) {
@@ -957,14 +1025,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       // ---- C: PROJ + residual ----
       {
         const MkChunk &ch = sm.chunks[ci++];
-        mk_params_load(sm, nullptr, nullptr, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
-        if (!(ok = mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4))) break;
-        tick(PF_PROJ_WAIT);
-        long long t0 = clock64();
-        const float sx = mk_quantize<768, true>(sm, mk_local_max<768>(sm));
-        sub_tick(pp, PF_QUANT, t0);
-        if (!(ok = gemv(ch, C, sx, MK_RESID, a.ll + ll.xmid(l), flag))) break;
-        tick(PF_PROJ);
+        if (ch.r1 == ch.r0) {
+          if (!(ok = skip_chunk())) break;
+          tick(PF_PROJ_WAIT);
+          tick(PF_PROJ);
+        } else {
+          mk_params_load(sm, nullptr, nullptr, vec + 5 * C, ch.r0, ch.r1 - ch.r0);
+          if (!(ok = mk_poll(a, sm, a.ll + ll.att(l), C, flag, sm.xf, 4))) break;
+          tick(PF_PROJ_WAIT);
+          long long t0 = clock64();
+          const float sx = mk_quantize<768, true>(sm, mk_local_max<768>(sm));
+          sub_tick(pp, PF_QUANT, t0);
+          if (!(ok = gemv(ch, C, sx, MK_RESID, a.ll + ll.xmid(l), flag))) break;
+          tick(PF_PROJ);
+        }
       }
       // ---- D: LN2 + FC + GELU ----
       {
