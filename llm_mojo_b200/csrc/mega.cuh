@@ -900,7 +900,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   const int cta = blockIdx.x, grid = gridDim.x;
   const MkLL ll(a.C, a.n_layer, grid);
   const uint8_t *stream = a.stream + a.stream_base[cta];
-  const long long total_chunks = (long long)a.nchunks * a.steps;
+  const int total_chunks = a.nchunks * a.steps;  // <= 64 x 4096
   const int C = a.C, C4 = 4 * C;
 
   for (int i = tid; i < a.nchunks; i += MK_THREADS) sm.chunks[i] = a.chunks[(size_t)cta * a.nchunks + i];
@@ -917,16 +917,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   }
   __syncthreads();
 
-  long long seq = 0;  // chunks consumed
-  // Chunk q of the whole generation into its ring slot (thread 0).
-  auto issue = [&](long long q) {
-    const int slot = (int)(q % MK_NSLOT);
-    const MkChunk &ch = sm.chunks[q % a.nchunks];
-    mbar_expect_tx(&sm.full[slot], (unsigned)ch.bytes);
-    bulk_g2s(sm.ring[slot], stream + ch.off, (unsigned)ch.bytes, &sm.full[slot]);
+  // The ring: chunk q of the whole generation goes to slot q % MK_NSLOT
+  // with mbarrier phase parity (q / MK_NSLOT) & 1. The indices advance by one
+  // per chunk (no divisions on the way).
+  int seq = 0, rslot = 0, rpar = 0;  // chunks consumed; slot and parity of chunk seq
+  int iss = 0, iss_slot = 0, iss_ci = 0;  // thread 0: chunks issued; slot and token chunk index of the next
+  auto issue = [&]() {  // the next chunk into its slot (thread 0)
+    const MkChunk &ch = sm.chunks[iss_ci];
+    mbar_expect_tx(&sm.full[iss_slot], (unsigned)ch.bytes);
+    bulk_g2s(sm.ring[iss_slot], stream + ch.off, (unsigned)ch.bytes, &sm.full[iss_slot]);
+    iss++;
+    iss_slot = iss_slot + 1 == MK_NSLOT ? 0 : iss_slot + 1;
+    iss_ci = iss_ci + 1 == a.nchunks ? 0 : iss_ci + 1;
   };
   if (tid == 0)
-    for (long long q = 0; q < MK_NSLOT && q < total_chunks; q++) issue(q);
+    while (iss < MK_NSLOT && iss < total_chunks) issue();
 
   // profiling (thread 0 of CTAs 0 and grid/2)
   const bool prof_on = a.prof && tid == 0 && (cta == 0 || cta == grid / 2);
@@ -941,10 +946,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       tlast = t;
     }
   };
-  auto slot_wait = [&](int ahead = 0) -> int {  // slot of chunk `seq + ahead`, or -1 on timeout
-    const long long q = seq + ahead;
-    const int slot = (int)(q % MK_NSLOT);
-    const unsigned par = (unsigned)((q / MK_NSLOT) & 1);
+  auto slot_wait = [&](int ahead = 0) -> int {  // slot of chunk `seq + ahead` (ahead 0 or 1), or -1 on timeout
+    int slot = rslot + ahead;
+    unsigned par = (unsigned)rpar;
+    if (slot >= MK_NSLOT) {
+      slot -= MK_NSLOT;
+      par ^= 1u;
+    }
     long long t0 = clock64();
     while (!mbar_try_wait(&sm.full[slot], par)) {
       if (!mk_alive(a, sm, t0, 1)) return -1;
@@ -955,8 +963,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
   // Called after the barrier that ends the use of the slot (the last one in
   // mk_gemv_blk4, or the one after mk_head_pair).
   auto slot_release = [&]() {
-    if (tid == 0 && seq + MK_NSLOT < total_chunks) issue(seq + MK_NSLOT);
+    if (tid == 0 && iss < total_chunks) issue();  // chunk seq + MK_NSLOT
     seq++;
+    if (++rslot == MK_NSLOT) {
+      rslot = 0;
+      rpar ^= 1;
+    }
   };
   // One GEMV phase: wait for its weights, compute, publish, release.
   auto gemv = [&](const MkChunk &ch, int IN, float sx, int epi, unsigned long long *out, unsigned flag) -> bool {
@@ -1102,11 +1114,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     // flight.
     cp_async_wait_all();
     if (tid == 0) {
-      for (long long q = seq; q < seq + MK_NSLOT && q < total_chunks; q++) {
-        const int slot = (int)(q % MK_NSLOT);
-        const unsigned par = (unsigned)((q / MK_NSLOT) & 1);
+      int slot = rslot;
+      unsigned par = (unsigned)rpar;
+      for (int q = seq; q < seq + MK_NSLOT && q < total_chunks; q++) {
         long long t1 = clock64();
         while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        }
+        if (++slot == MK_NSLOT) {
+          slot = 0;
+          par ^= 1u;
         }
       }
     }
