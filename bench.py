@@ -46,7 +46,7 @@ METRIC = "int4-g32-a16 decode tok/s (b=1)"
 # DRAM bytes (read + write) of one persistent-kernel launch of this workload,
 # from one ncu capture (profiles/mega_decode_kernel.txt): below the
 # algorithmic bytes because the weight stream stays in L2 across tokens.
-MEGA_TRAFFIC_BYTES = 4_262_806_528
+MEGA_TRAFFIC_BYTES = 4_058_159_360
 
 
 def peaks():
