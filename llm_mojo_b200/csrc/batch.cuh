@@ -78,42 +78,54 @@ constexpr int BG_ROWS = 64;  // output rows per CTA (4 threads each)
 // bytes so that the 8 rows a warp reads fall in different banks.
 __host__ __device__ inline int bgemv_wstride(int fmt, int K) { return (fmt == FMT_GEN8 ? K : K / 2) + 16; }
 
-// grid (ceil(rows / 64), ceil(B / SB)), 256 threads. Shared memory: the CTA's
-// 64 weight rows (STAGE: one bulk copy per row; otherwise they are read from
-// global memory), the SB rows' activations and their sums.
+// The batched GEMVs' shared-memory prologue: the CTA's weight rows staged by
+// bulk copies (STAGE), the SB sequences' activations regrouped so that the
+// four pairs thread q multiplies per 16-pair step are 16 contiguous bytes
+// (the int8 format's pairs 4q..4q+3 already are), their sums, and a bounded
+// wait for the rows. Returns false (every thread) when the wait gave up.
 template <int FMT, int SB, bool STAGE>
-__global__ void __launch_bounds__(256) bgemv_a16_kernel(BGemvArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ alignas(8) unsigned long long wbar;
-  const int K = a.w.cols, G = a.w.group;
-  const int units = FMT == FMT_BLK4 ? K >> 8 : K / G;
+__device__ __forceinline__ bool bgemv_prologue(const BGemvArgs &a, unsigned char *smem, unsigned long long &wbar,
+                                               int row0, int nrows, int b0, int nb) {
+  const int K = a.w.cols;
+  const int units = FMT == FMT_BLK4 ? K >> 8 : K / a.w.group;
   const int nxs = FMT == FMT_BLK4 ? K / 16 : units * 16;
-  const int b0 = blockIdx.y * SB, nb = min(SB, a.B - b0);
   const int wstride = bgemv_wstride(FMT, K), rbytes = FMT == FMT_GEN8 ? K : K / 2;
-  const int row0 = blockIdx.x * BG_ROWS, nrows = min(BG_ROWS, a.w.rows - row0);
-  uint8_t *wt = smem;                                        // [64][wstride] weight rows (STAGE)
-  int *xq = (int *)(smem + (STAGE ? (size_t)BG_ROWS * wstride : 0));  // [SB][K / 2] int16 pairs, regrouped
-  int *xs = xq + (size_t)SB * (K / 2);                       // [SB][nxs] (float bits for BLOCKED)
+  uint8_t *wt = smem;
+  int *xq = (int *)(smem + (STAGE ? (size_t)BG_ROWS * wstride : 0));
+  int *xs = xq + (size_t)SB * (K / 2);
   if (STAGE && threadIdx.x == 0) {
     tc_mbar_init(tc_u32(&wbar), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tc_mbar_expect_tx(tc_u32(&wbar), (unsigned)(nrows * rbytes));
-    for (int r = 0; r < nrows; r++)
-      tc_bulk_g2s(tc_u32(wt + (size_t)r * wstride), a.w.codes + (size_t)(row0 + r) * rbytes, rbytes, tc_u32(&wbar));
   }
   {
-    // Each 16-pair step of the int4 formats is regrouped so that the 4 pairs
-    // thread q multiplies (2q, 2q+1, 2q+8, 2q+9) are 16 contiguous bytes; the
-    // int8 format's pairs 4q..4q+3 already are.
-    const int *src = (const int *)(a.xq + (size_t)b0 * K);
-    for (int i = threadIdx.x; i < nb * (K / 2); i += blockDim.x) {
-      const int e = i & 15;
-      const int from = FMT == FMT_GEN8 ? e : (e >> 2) * 2 + (e & 1) + ((e & 2) << 2);
-      xq[i] = src[(i & ~15) + from];
+    // The activations, 16 ints (one 16-pair step) per item, read as four
+    // int4 and regrouped in registers: each 16-pair step of the int4 formats
+    // is regrouped so that the 4 pairs thread q multiplies (2q, 2q+1, 2q+8,
+    // 2q+9) are 16 contiguous bytes; the int8 format's pairs 4q..4q+3
+    // already are.
+    const int4 *src = (const int4 *)(a.xq + (size_t)b0 * K);
+    int4 *dst = (int4 *)xq;
+    const int items = nb * (K / 32);
+    for (int i = threadIdx.x; i < items; i += blockDim.x) {
+      int v[16];
+#pragma unroll
+      for (int k = 0; k < 4; k++) *(int4 *)(v + 4 * k) = src[4 * i + k];
+      int w[16];
+#pragma unroll
+      for (int e = 0; e < 16; e++) w[e] = v[FMT == FMT_GEN8 ? e : (e >> 2) * 2 + (e & 1) + ((e & 2) << 2)];
+#pragma unroll
+      for (int k = 0; k < 4; k++) dst[4 * i + k] = *(const int4 *)(w + 4 * k);
     }
     const int *s2 = FMT == FMT_BLK4 ? (const int *)(a.xsf + (size_t)b0 * nxs) : a.xsi + (size_t)b0 * nxs;
     for (int i = threadIdx.x; i < nb * nxs; i += blockDim.x) xs[i] = s2[i];
   }
+  // the weight rows, one bulk copy per row issued by thread r, after the
+  // barrier that publishes the initialised mbarrier
+  __syncthreads();
+  if (STAGE && threadIdx.x < nrows)
+    tc_bulk_g2s(tc_u32(wt + (size_t)threadIdx.x * wstride), a.w.codes + (size_t)(row0 + threadIdx.x) * rbytes, rbytes,
+                tc_u32(&wbar));
   // the weight rows' arrival: a bounded wait (all threads), after which a
   // CTA that gave up records the error and computes nothing
   __syncthreads();
@@ -132,8 +144,28 @@ __global__ void __launch_bounds__(256) bgemv_a16_kernel(BGemvArgs a) {
       atomicExch(a.err, 5);
       if (STAGE) tc_drain_wait(tc_u32(&wbar), 0);
     }
-    return;
+    return false;
   }
+  return true;
+}
+
+// grid (ceil(rows / 64), ceil(B / SB)), 256 threads. Shared memory: the CTA's
+// 64 weight rows (STAGE: one bulk copy per row; otherwise they are read from
+// global memory), the SB rows' activations and their sums.
+template <int FMT, int SB, bool STAGE>
+__global__ void __launch_bounds__(256) bgemv_a16_kernel(BGemvArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ alignas(8) unsigned long long wbar;
+  const int K = a.w.cols, G = a.w.group;
+  const int units = FMT == FMT_BLK4 ? K >> 8 : K / G;
+  const int nxs = FMT == FMT_BLK4 ? K / 16 : units * 16;
+  const int b0 = blockIdx.y * SB, nb = min(SB, a.B - b0);
+  const int wstride = bgemv_wstride(FMT, K), rbytes = FMT == FMT_GEN8 ? K : K / 2;
+  const int row0 = blockIdx.x * BG_ROWS, nrows = min(BG_ROWS, a.w.rows - row0);
+  uint8_t *wt = smem;                                        // [64][wstride] weight rows (STAGE)
+  int *xq = (int *)(smem + (STAGE ? (size_t)BG_ROWS * wstride : 0));  // [SB][K / 2] int16 pairs, regrouped
+  int *xs = xq + (size_t)SB * (K / 2);                       // [SB][nxs] (float bits for BLOCKED)
+  if (!bgemv_prologue<FMT, SB, STAGE>(a, smem, wbar, row0, nrows, b0, nb)) return;
   const int q = threadIdx.x & 3, row = blockIdx.x * BG_ROWS + (threadIdx.x >> 2);
   const bool live = row < a.w.rows;
   const int rr = live ? row : a.w.rows - 1;
@@ -287,6 +319,180 @@ __global__ void __launch_bounds__(256) bgemv_a16_kernel(BGemvArgs a) {
           }
         a.part_val[(size_t)(b0 + s) * gridDim.x + blockIdx.x] = bv;
         a.part_idx[(size_t)(b0 + s) * gridDim.x + blockIdx.x] = bi;
+      }
+      __syncthreads();
+    }
+  }
+}
+
+// The batched GEMV with the roles of weights and activations swapped, for
+// the BLOCKED int4-g32 and per-channel int8 formats: grid (ceil(rows / 64),
+// ceil(B / 8)), 256 threads; warp w takes rows 8w..8w+7 of the CTA's 64 staged
+// rows for the CTA's 8 sequences, lane = (sequence s, q). A thread keeps its
+// sequence's activations of one unit (BLOCKED: a 256-block; int8: 8 chunks of
+// 32) in registers and applies them to the warp's rows, whose weight words it
+// reads from shared memory as broadcasts (all 8 sequences of a warp read the
+// same 4 words). The arithmetic per (row, sequence) is bgemv_a16_kernel's:
+// the same int32 lane sums, float lane chains in unit order and halving tree.
+template <int FMT, int NP>
+__global__ void __launch_bounds__(256) bgemv_rows_kernel(BGemvArgs a) {
+  constexpr int SB = 8 * NP, RW = BG_ROWS / 8;  // NP passes of 8 sequences over the staged rows
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ alignas(8) unsigned long long wbar;
+  __shared__ float pbv[8][SB];
+  __shared__ int pbi[8][SB];
+  const int K = a.w.cols;
+  const int nxs = FMT == FMT_BLK4 ? K / 16 : 16;
+  const int b0 = blockIdx.y * SB, nb = min(SB, a.B - b0);
+  const int wstride = bgemv_wstride(FMT, K);
+  const int row0 = blockIdx.x * BG_ROWS, nrows = min(BG_ROWS, a.w.rows - row0);
+  const uint8_t *wt = smem;
+  const int *xq = (const int *)(smem + (size_t)BG_ROWS * wstride);
+  const int *xs = xq + (size_t)SB * (K / 2);
+  if (!bgemv_prologue<FMT, SB, true>(a, smem, wbar, row0, nrows, b0, nb)) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, sq = lane >> 2, q = lane & 3;
+  const int rbase = warp * RW;              // this warp's rows in the CTA's tile
+  const int nr = max(0, min(RW, nrows - rbase));
+  for (int pass = 0; pass < NP; pass++) {
+    const int sp = sq + 8 * pass;             // this lane's sequence in the CTA's SB
+    const bool sv = sp < nb;
+    const int se = sv ? sp : 0;               // an absent sequence computes sequence 0's values, dropped
+    float f[RW][4];
+#pragma unroll
+    for (int r = 0; r < RW; r++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) f[r][j] = 0.0f;
+    if (FMT == FMT_BLK4) {
+      const int units = K >> 8, gpr = K >> 5;
+      int L[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) L[j] = lane_of<FMT_BLK4>(q, j);
+      for (int u = 0; u < units; u++) {
+        int4 xr[8];
+#pragma unroll
+        for (int st = 0; st < 8; st++) xr[st] = *(const int4 *)(xq + (size_t)se * (K / 2) + u * 128 + st * 16 + 4 * q);
+        float xsum[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) xsum[j] = ((const float *)xs)[(size_t)se * nxs + u * 16 + L[j]];
+#pragma unroll
+        for (int r = 0; r < RW; r++) {
+          if (r < nr) {
+            const int row = row0 + rbase + r;
+            const uint32_t *wp = (const uint32_t *)(wt + (size_t)(rbase + r) * wstride + u * 128) + q;
+            int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+            for (int st = 0; st < 8; st++) {
+              const uint32_t v = wp[4 * st];
+              const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
+              a0 = dp2a_lo_su(xr[st].x, lo, a0);
+              a1 = dp2a_hi_su(xr[st].y, lo, a1);
+              a2 = dp2a_lo_su(xr[st].z, hi, a2);
+              a3 = dp2a_hi_su(xr[st].w, hi, a3);
+            }
+            const size_t g0 = (size_t)row * gpr + u * 8 + 2 * q;  // groups of lanes 2q(+8) and 2q+1(+9)
+            const float zp0 = (float)a.w.zp[g0], zp1 = (float)a.w.zp[g0 + 1];
+            const float sc0 = half_bits_to_float(a.w.scale[g0]), sc1 = half_bits_to_float(a.w.scale[g0 + 1]);
+            f[r][0] = fmaf((float)a0 - zp0 * xsum[0], sc0, f[r][0]);
+            f[r][1] = fmaf((float)a1 - zp1 * xsum[1], sc1, f[r][1]);
+            f[r][2] = fmaf((float)a2 - zp0 * xsum[2], sc0, f[r][2]);
+            f[r][3] = fmaf((float)a3 - zp1 * xsum[3], sc1, f[r][3]);
+          }
+        }
+      }
+    } else {
+      // per-channel int8: one group per row; int32 lane sums over all chunks,
+      // one conversion at the end
+      int acc[RW][4];
+#pragma unroll
+      for (int r = 0; r < RW; r++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[r][j] = 0;
+      for (int cb = 0; cb < K / 32; cb += 8) {
+        int4 xr[8];
+#pragma unroll
+        for (int c = 0; c < 8; c++) xr[c] = *(const int4 *)(xq + (size_t)se * (K / 2) + (cb + c) * 16 + 4 * q);
+#pragma unroll
+        for (int r = 0; r < RW; r++) {
+          if (r < nr) {
+            const uint8_t *rp = wt + (size_t)(rbase + r) * wstride + cb * 32 + 8 * q;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+              const uint2 v = *(const uint2 *)(rp + c * 32);
+              acc[r][0] = dp2a_lo_su(xr[c].x, v.x, acc[r][0]);
+              acc[r][1] = dp2a_hi_su(xr[c].y, v.x, acc[r][1]);
+              acc[r][2] = dp2a_lo_su(xr[c].z, v.y, acc[r][2]);
+              acc[r][3] = dp2a_hi_su(xr[c].w, v.y, acc[r][3]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < RW; r++) {
+        if (r < nr) {
+          const int row = row0 + rbase + r;
+          const int zpv = a.w.zp[row];
+          const float scv = half_bits_to_float(a.w.scale[row]);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int v = (int)((unsigned)acc[r][j] - (unsigned)(zpv * xs[(size_t)se * nxs + 4 * q + j]));
+            f[r][j] = fmaf((float)v, scv, f[r][j]);
+          }
+        }
+      }
+    }
+    // halving tree over each row's 16 lanes (the four threads of a sequence),
+    // epilogue, and for the head the best row per sequence
+    float bv = -__int_as_float(0x7f800000);
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int r = 0; r < RW; r++) {
+      float dot;
+      if (FMT == FMT_GEN8) {
+        float t[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) t[j] = f[r][j] + __shfl_xor_sync(0xffffffffu, f[r][j], 2);
+#pragma unroll
+        for (int j = 0; j < 4; j++) t[j] = t[j] + __shfl_xor_sync(0xffffffffu, t[j], 1);
+        dot = (t[0] + t[2]) + (t[1] + t[3]);
+      } else {
+        float a0 = f[r][0] + f[r][2], a1 = f[r][1] + f[r][3];
+        a0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 2);
+        a1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 2);
+        const float c0 = a0 + __shfl_xor_sync(0xffffffffu, a0, 1);
+        const float c1 = a1 + __shfl_xor_sync(0xffffffffu, a1, 1);
+        dot = c0 + c1;
+      }
+      if (r < nr && sv) {
+        const int row = row0 + rbase + r, b = b0 + sp;
+        float *dst = a.out ? a.out + (size_t)b * a.w.rows + row : nullptr;
+        float v = dot * a.sx[b];
+        if (a.epi & EPI_BIAS) v += a.bias[row];
+        if (a.epi & EPI_GELU) v = gelu(v);
+        if ((a.epi & EPI_RESID) && dst) v += *dst;
+        if (dst && q == 0) *dst = v;
+        if (better(v, row, bv, bi)) {
+          bv = v;
+          bi = row;
+        }
+      }
+    }
+    if (a.part_val) {
+      if (q == 0) {
+        pbv[warp][sq] = bv;
+        pbi[warp][sq] = bi;
+      }
+      __syncthreads();
+      if (threadIdx.x < 8 && threadIdx.x + 8 * pass < nb) {
+        const int s = threadIdx.x;
+        float v = pbv[0][s];
+        int i = pbi[0][s];
+        for (int w = 1; w < 8; w++)
+          if (better(pbv[w][s], pbi[w][s], v, i)) {
+            v = pbv[w][s];
+            i = pbi[w][s];
+          }
+        a.part_val[(size_t)(b0 + s + 8 * pass) * gridDim.x + blockIdx.x] = v;
+        a.part_idx[(size_t)(b0 + s + 8 * pass) * gridDim.x + blockIdx.x] = i;
       }
       __syncthreads();
     }

@@ -1847,6 +1847,30 @@ llmq_status batch_linear(llmq_batch *bt, const llmq_weight *w, const float *x, c
   const bool stage = bgemv_smem(fmt, K, v.group, sb, true) <= (size_t)kBgemvSmem;
   const size_t sm = bgemv_smem(fmt, K, v.group, sb, stage);
   const dim3 grid(gx, (B + sb - 1) / sb);
+  // the row-major kernel for the BLOCKED int4 and per-channel int8 formats
+  if (stage && (fmt == FMT_BLK4 || (fmt == FMT_GEN8 && v.group == K && K % 256 == 0))) {
+    // two passes of 8 sequences over the staged rows where their activations
+    // fit beside them (four passes measured slower: too few CTAs)
+    int np = 2;
+    while (np > 1 && bgemv_smem(fmt, K, v.group, 8 * np, true) > (size_t)kBgemvSmem) np >>= 1;
+    const size_t sm2 = bgemv_smem(fmt, K, v.group, 8 * np, true);
+    const dim3 grid2(gx, (B + 8 * np - 1) / (8 * np));
+#define BR(F)                                                              \
+  if (np == 4)                                                             \
+    bgemv_rows_kernel<F, 4><<<grid2, 256, sm2, s>>>(g);                    \
+  else if (np == 2)                                                        \
+    bgemv_rows_kernel<F, 2><<<grid2, 256, sm2, s>>>(g);                    \
+  else                                                                     \
+    bgemv_rows_kernel<F, 1><<<grid2, 256, sm2, s>>>(g);
+    if (fmt == FMT_BLK4) {
+      BR(FMT_BLK4)
+    } else {
+      BR(FMT_GEN8)
+    }
+#undef BR
+    CKL();
+    return LLMQ_OK;
+  }
 #define BG(F, SB, ST) bgemv_a16_kernel<F, SB, ST><<<grid, 256, sm, s>>>(g)
 #define BG2(F)                       \
   if (sb == 16 && stage) BG(F, 16, true); \
@@ -2073,6 +2097,10 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
   BA(FMT_GEN4)
   BA(FMT_GEN8)
 #undef BA
+  for (const void *k : {(const void *)bgemv_rows_kernel<FMT_BLK4, 1>, (const void *)bgemv_rows_kernel<FMT_BLK4, 2>,
+                        (const void *)bgemv_rows_kernel<FMT_BLK4, 4>, (const void *)bgemv_rows_kernel<FMT_GEN8, 1>,
+                        (const void *)bgemv_rows_kernel<FMT_GEN8, 2>, (const void *)bgemv_rows_kernel<FMT_GEN8, 4>})
+    attr(k, kBgemvSmem);
   if (e != cudaSuccess) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);
