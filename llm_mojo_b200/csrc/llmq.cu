@@ -58,6 +58,8 @@ struct llmq_weight {
   long long nbytes = 0;
   mutable uint8_t *tc_b = nullptr;  // split-int8 GEMM tiles of the codes, built on first several-token use
   mutable int tc_tn = 0;            // their output tile width
+  mutable uint8_t *tc_w = nullptr;  // the transposed GEMM's 128-row weight tiles (first use)
+  mutable int *tc_wsum = nullptr;   // and the rows' per-segment sums of the weight values
   WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
   RowMat rowmat() const { return RowMat{codes, rows, cols, rtype, row_bytes}; }
 };
@@ -259,6 +261,13 @@ cudaError_t configure_kernels() {
   tcs((const void *)tc_gemm_a16_kernel<true, 32>);
   tcs((const void *)tc_gemm_a16_kernel<false, 64>);
   tcs((const void *)tc_gemm_a16_kernel<false, 32>);
+  auto tct = [&](const void *k, size_t n) {
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)n + 1024);
+  };
+  tct((const void *)tct_gemm_kernel<true, 32>, sizeof(TcSmemT<32>));
+  tct((const void *)tct_gemm_kernel<false, 32>, sizeof(TcSmemT<32>));
+  tct((const void *)tct_gemm_kernel<true, 64>, sizeof(TcSmemT<64>));
+  tct((const void *)tct_gemm_kernel<false, 64>, sizeof(TcSmemT<64>));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)merge_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)merge_smem(kMergeCap));
@@ -466,6 +475,8 @@ llmq_status llmq_weight_free(llmq_weight *w) {
   if (w->scale) cudaFree(w->scale);
   if (w->zp) cudaFree(w->zp);
   if (w->tc_b) cudaFree(w->tc_b);
+  if (w->tc_w) cudaFree(w->tc_w);
+  if (w->tc_wsum) cudaFree(w->tc_wsum);
   delete w;
   return LLMQ_OK;
 }
@@ -568,12 +579,92 @@ llmq_status gguf_rows_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x
   return LLMQ_OK;
 }
 
+// matmul_rows_a16 for T > 1 on the transposed GEMM (tct_gemm_kernel): the
+// weight rows as the MMA's M, both activation planes of TT tokens as its N
+// (TT 32 for matrices of at most 1024 outputs, so that more CTAs take part,
+// else 64); the OUT % 32 leftover rows on rows_a16_kernel.
+llmq_status tct_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
+                       int IN, int OUT, int epi) {
+  const int K = IN, nkb = K / TC_KB, seg = std::min(w->group, 256), nseg = K / seg;
+  const int TT = OUT <= 1024 ? 32 : 64;
+  const int ttiles = (T + TT - 1) / TT, t_pad = ttiles * TT;
+  const int full = OUT / 32 * 32, ntiles = (full + TC_M - 1) / TC_M;
+  const bool zc = w->bits == 8;
+  const size_t b_bytes = align256((size_t)ttiles * nkb * 2 * TT * TC_KB), sx_bytes = align256((size_t)t_pad * 4);
+  const size_t xs_bytes = zc ? align256((size_t)t_pad * nseg * 4) : 0;
+  const size_t xq_bytes = (OUT % 32) ? align256((size_t)T * IN * 2) : 0;
+  llmq_status st = ensure_scratch(ctx, b_bytes + sx_bytes + xs_bytes + xq_bytes);
+  if (st != LLMQ_OK) return st;
+  uint8_t *b = (uint8_t *)ctx->scratch;
+  float *sx = (float *)(b + b_bytes);
+  int *xsum = zc ? (int *)((char *)sx + sx_bytes) : nullptr;
+  int16_t *xq = xq_bytes ? (int16_t *)((char *)sx + sx_bytes + xs_bytes) : nullptr;
+  if (!w->tc_w) {
+    const int wt = (w->rows + TC_M - 1) / TC_M;
+    CK(cudaMalloc(&w->tc_w, (size_t)wt * nkb * TCT_A_BYTES));
+    CK(cudaMalloc(&w->tc_wsum, (size_t)w->rows * nseg * 4));
+    tc_prep_b_kernel<<<dim3(wt, nkb), 256, 0, ctx->stream>>>(w->view(), w->tc_w, TC_M);
+    CKL();
+    tct_wsum_kernel<<<(w->rows * nseg + 255) / 256, 256, 0, ctx->stream>>>(w->view(), seg, nseg, w->tc_wsum);
+    CKL();
+  }
+  if (TT == 32)
+    tct_split_rows_kernel<32><<<t_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, b, sx, xsum, xq);
+  else
+    tct_split_rows_kernel<64><<<t_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, b, sx, xsum, xq);
+  CKL();
+  if (ntiles > 0) {
+    TcArgsT p{};
+    p.a = w->tc_w;
+    p.b = b;
+    p.sx = sx;
+    p.xsum = xsum;
+    p.wsum = w->tc_wsum;
+    p.w = w->view();
+    p.bias = bias;
+    p.out = out;
+    p.err = ctx->tc_err;
+    p.T = T;
+    p.OUT = OUT;
+    p.n_full = full;
+    p.K = K;
+    p.nkb = nkb;
+    p.nseg = nseg;
+    p.seg_ks = seg / 32;
+    p.seg = seg;
+    p.epi = epi;
+    const dim3 grid(ntiles, ttiles);
+    if (TT == 32) {
+      const size_t sm = sizeof(TcSmemT<32>) + 1024;
+      if (zc)
+        tct_gemm_kernel<true, 32><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+      else
+        tct_gemm_kernel<false, 32><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+    } else {
+      const size_t sm = sizeof(TcSmemT<64>) + 1024;
+      if (zc)
+        tct_gemm_kernel<true, 64><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+      else
+        tct_gemm_kernel<false, 64><<<grid, TC_THREADS, sm, ctx->stream>>>(p);
+    }
+    CKL();
+    ctx->tc_used = true;
+  }
+  if (OUT % 32) {
+    int n = T * (OUT - full);
+    rows_a16_kernel<<<(n + 127) / 128, 128, 0, ctx->stream>>>(w->view(), xq, sx, bias, out, T, OUT, full, epi);
+    CKL();
+  }
+  return LLMQ_OK;
+}
+
 // matmul_rows_a16 for T > 1 (kernels.mojo:461-507) with the tile_i16 rows
 // (the first OUT / 32 * 32 outputs) on the split-int8 tcgen05 GEMM and the
 // leftover rows (rows_i16) on rows_a16_kernel.
 llmq_status tc_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
                       int IN, int OUT, int epi) {
   const int K = IN, nkb = K / TC_KB, seg = std::min(w->group, 256), nseg = K / seg;
+  if (w->bits == 4 || nseg <= TC_MAX_GROUPS) return tct_linear(ctx, w, x, bias, out, T, IN, OUT, epi);
   const int mtiles = (T + TC_M - 1) / TC_M, m_pad = mtiles * TC_M;
   // 32-wide output tiles for narrow matrices (more CTAs), 64 otherwise; the
   // weight's prepared tiles follow the width chosen on its first use.

@@ -474,4 +474,318 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_a16_kernel(TcArgs p) {
   }
 }
 
+
+// --- the transposed GEMM: weights as A, both activation planes as one B -----
+//
+// The weight rows are the MMA's M (128 per tile), the tokens its N: B holds
+// the tile's TT tokens twice, as the low plane xl' = xl - 128 and the high
+// plane xh, both signed bytes (x = 256 xh + xl' + 128), so ONE kind::i8 MMA
+// per 32-element K step gives both planes' sums: D[n][t] (low) and
+// D[n][TT + t] (high). The segment sum is 256 D_h + D_l + 128 W (W: the
+// segment's sum of the weight values, u - zp for int4, u for int8), minus
+// zp * sum(x) for int8, all modulo 2^32 like the reference's int32
+// accumulator; the float folds keep the reference's order: bit-identical.
+//
+// Shared memory: 4 stages of [A: 128 rows x 128 B][B: 2 TT rows x 128 B],
+// both in the 128-byte swizzle layout. Warp 16 issues copies, MMAs and
+// commits; warps 0-15 fold (warp w: tensor-memory lanes = weight rows
+// 32 * (w % 4) + lane, tokens (w / 4) * TT / 4 .. + TT / 4).
+
+constexpr int TCT_A_BYTES = TC_M * TC_KB;  // 16 KB of weight rows per K block
+
+template <int TT>
+struct TcSmemT {
+  alignas(1024) uint8_t stage[TC_STAGES][TCT_A_BYTES + 2 * TT * TC_KB];
+  int xsum[TT][TC_MAX_GROUPS];  // int8 weights: the tile's per-token segment sums of x
+  alignas(8) unsigned long long full[TC_STAGES], empty[TC_STAGES], accfull[TC_NBUF_MAX], accempty[TC_NBUF_MAX],
+      drain;
+  unsigned tmem;
+  int abort;
+};
+
+// The bounded wait of tc_wait on a given abort flag.
+__device__ __forceinline__ bool tc_wait_flag(int *abort, unsigned bar, unsigned parity, int *err, int code) {
+  long long t0 = clock64();
+  while (!tc_mbar_try(bar, parity)) {
+    if (*(volatile int *)abort) return false;
+    if (clock64() - t0 > TC_TIMEOUT) {
+      *(volatile int *)abort = 1;
+      atomicExch(err, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+// quantize_rows of rows [0, T) into the transposed B tiles
+// [t_tile][kb][plane l' (TT rows), plane h (TT rows)], sx[m], the
+// per-segment sums of x (xsum, when non-null) and the plain int16 rows (xq,
+// when non-null). One CTA per row of the padded token count; rows >= T hold
+// codes 0 (their outputs are not stored).
+template <int TT>
+__global__ void __launch_bounds__(256) tct_split_rows_kernel(const float *x, int T, int K, int nseg, int seg,
+                                                             uint8_t *b, float *sx, int *xsum, int16_t *xq) {
+  __shared__ float red[64];
+  __shared__ int ssum[TC_MAX_GROUPS * 8];
+  const int m = blockIdx.x, nkb = K / TC_KB;
+  const bool valid = m < T;
+  const float *row = x + (size_t)m * K;
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) ssum[i] = 0;
+  float mx = 0.0f;
+  if (valid)
+    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(row[i]));
+  mx = block_max(mx, red);
+  float s = mx / 32767.0f;
+  if (s == 0.0f) s = 1.0f;
+  const float inv = 1.0f / s;
+  const int tt = m / TT, r = m % TT;
+  for (int ci = threadIdx.x; ci < K / 16; ci += blockDim.x) {
+    const int k0 = ci * 16, kb = k0 / TC_KB, chunk = (k0 % TC_KB) / 16;
+    uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
+    int part = 0;
+    if (valid) {
+      uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 16; i++) {
+        const int16_t q = (int16_t)roundf(row[k0 + i] * inv);
+        part += q;
+        qw[i >> 1] |= (uint32_t)(uint16_t)q << (16 * (i & 1));
+        lo[i >> 2] |= (uint32_t)(((uint16_t)q & 0xFF) ^ 0x80) << (8 * (i & 3));  // xl - 128
+        hi[i >> 2] |= (uint32_t)(((uint16_t)q >> 8) & 0xFF) << (8 * (i & 3));
+      }
+      if (xq) {
+        uint4 *dq = (uint4 *)(xq + (size_t)m * K + k0);
+        dq[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
+        dq[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
+      }
+      if (xsum) atomicAdd(&ssum[k0 / seg], part);
+    }
+    uint8_t *base = b + ((size_t)tt * nkb + kb) * (2 * TT * TC_KB) + tc_sw128_off(r, chunk);
+    *(uint4 *)base = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *(uint4 *)(base + TT * TC_KB) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) sx[m] = valid ? s : 0.0f;
+  if (xsum)
+    for (int i = threadIdx.x; i < nseg; i += blockDim.x) xsum[(size_t)m * nseg + i] = ssum[i];
+}
+
+// W[n][s]: the sum over segment s of row n's weight values (u - zp for int4,
+// the u8 code for int8). One thread per (row, segment).
+__global__ void tct_wsum_kernel(WeightView w, int seg, int nseg, int *wsum) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= w.rows * nseg) return;
+  const int n = i / nseg, sg = i % nseg, gpr = w.cols / w.group;
+  int t = 0;
+  for (int k = sg * seg; k < (sg + 1) * seg; k++) {
+    const int code = code_at(w, n, k);
+    t += w.bits == 4 ? code - (int)w.zp[(size_t)n * gpr + k / w.group] : code;
+  }
+  wsum[i] = t;
+}
+
+struct TcArgsT {
+  const uint8_t *a;   // weight tiles [n_tile][kb][128 rows x 128 B] (tc_prep_b_kernel, 128 rows)
+  const uint8_t *b;   // activation tiles [t_tile][kb][2 TT rows x 128 B]
+  const float *sx;    // [t_pad]
+  const int *xsum;    // [t_pad][nseg] (int8 weights)
+  const int *wsum;    // [rows][nseg]
+  WeightView w;
+  const float *bias;
+  float *out;
+  int *err;
+  int T, OUT, n_full, K, nkb, nseg, seg_ks, seg, epi;
+};
+
+template <bool ZC, int TT>
+__global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
+  constexpr int NBUF = TC_TMEM_COLS / (2 * TT);  // accumulators of 2 TT columns in tensor memory
+  constexpr int CW = TT / 4;                     // tokens per epilogue warp
+  constexpr int BB = 2 * TT * TC_KB;             // activation bytes per K block
+  constexpr int STAGE = TCT_A_BYTES + BB;
+  static_assert(CW == 16 || CW == 8, "tc_ld widths");
+  extern __shared__ __align__(128) unsigned char tc_raw[];
+  TcSmemT<TT> &sm = *reinterpret_cast<TcSmemT<TT> *>(tc_raw + ((1024u - (tc_u32(tc_raw) & 1023u)) & 1023u));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nt = blockIdx.x, tt = blockIdx.y, n0 = nt * TC_M, t0 = tt * TT;
+  const int G = p.w.group, gpr = p.w.cols / G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; s++) {
+      tc_mbar_init(tc_u32(&sm.full[s]), 1);
+      tc_mbar_init(tc_u32(&sm.empty[s]), 1);
+    }
+    for (int b = 0; b < NBUF; b++) {
+      tc_mbar_init(tc_u32(&sm.accfull[b]), 1);
+      tc_mbar_init(tc_u32(&sm.accempty[b]), TC_EPI_WARPS);
+    }
+    tc_mbar_init(tc_u32(&sm.drain), 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == TC_EPI_WARPS) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_u32(&sm.tmem)),
+                 "r"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  } else if (ZC) {
+    for (int i = threadIdx.x; i < TT * p.nseg; i += TC_EPI_WARPS * 32) {
+      const int t = i / p.nseg, sg = i % p.nseg;
+      sm.xsum[t][sg] = p.xsum[(size_t)(t0 + t) * p.nseg + sg];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const unsigned tmem = sm.tmem;
+
+  if (warp == TC_EPI_WARPS) {
+    // the whole warp runs the loop (waits included); lane 0 issues the
+    // copies, MMAs and commits
+    const bool leader = lane == 0;
+    const unsigned idesc = tc_idesc(ZC ? 0 : 1, 1, 2 * TT);
+    const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
+    const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TCT_A_BYTES);
+    const uint8_t *ga = p.a + (size_t)nt * p.nkb * TCT_A_BYTES;
+    const uint8_t *gb = p.b + (size_t)tt * p.nkb * BB;
+    int issued = 0, waited = 0, kstep = 0;
+    auto issue = [&](int kb) {
+      const int st = kb % TC_STAGES;
+      const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
+      if (leader) {
+        tc_mbar_expect_tx(bar, STAGE);
+        tc_bulk_g2s(dst, ga + (size_t)kb * TCT_A_BYTES, TCT_A_BYTES, bar);
+        tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
+      }
+      __syncwarp();
+    };
+    for (; issued < p.nkb && issued < TC_STAGES; issued++) issue(issued);
+    bool ok = true;
+    for (int seg = 0; seg < p.nseg && ok; seg++) {
+      const int buf = seg % NBUF;
+      if (seg >= NBUF)
+        ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[buf]), ((seg / NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const unsigned d = tmem + buf * 2 * TT;
+      for (int ks = 0; ks < p.seg_ks && ok; ks++, kstep++) {
+        const int kb = kstep >> 2, j = kstep & 3, st = kb % TC_STAGES;
+        if (j == 0) {
+          ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (kb / TC_STAGES) & 1, p.err, TC_ERR_FULL);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          waited = kb + 1;
+          tc_fence_after();
+        }
+        const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
+        if (leader) tc_mma(d, desc_a0 + off + (unsigned long long)(2 * j), desc_b0 + off + (unsigned long long)(2 * j),
+                           idesc, ks > 0);
+        __syncwarp();
+        if (j == 3) {
+          if (leader) tc_commit(tc_u32(&sm.empty[st]));
+          __syncwarp();
+          // refill the stage of the previous k block, whose MMA was queued
+          // ahead of these
+          if (kb >= 1 && issued < p.nkb) {
+            const int pkb = kb - 1;
+            ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[pkb % TC_STAGES]), (pkb / TC_STAGES) & 1, p.err,
+                              TC_ERR_EMPTY);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            issue(issued++);
+          }
+        }
+      }
+      if (ok && leader) tc_commit(tc_u32(&sm.accfull[buf]));
+      __syncwarp();
+    }
+    if (!ok) {
+      // drain: copies issued but not yet waited for, then every MMA issued
+      for (int kb = waited; kb < issued; kb++) tc_drain_wait(tc_u32(&sm.full[kb % TC_STAGES]), (kb / TC_STAGES) & 1);
+      if (leader) tc_commit(tc_u32(&sm.drain));
+      __syncwarp();
+      tc_drain_wait(tc_u32(&sm.drain), 0);
+    }
+  } else {
+    const int q = warp & 3, cg = warp >> 2;
+    const int n = n0 + 32 * q + lane;            // this thread's weight row
+    const int nr = n < p.w.rows ? n : p.w.rows - 1;
+    const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * CW;
+    float accf[CW];
+#pragma unroll
+    for (int c = 0; c < CW; c++) accf[c] = 0.0f;
+    int la[CW], ha[CW], lb[CW], hb[CW];
+    auto start = [&](int seg, int (&l)[CW], int (&h)[CW]) -> bool {
+      const int buf = seg % NBUF;
+      bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (seg / NBUF) & 1, p.err, TC_ERR_ACC);
+      ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
+      if (!ok) return false;
+      tc_fence_after();
+      tc_ld(tbase + buf * 2 * TT, l);
+      tc_ld(tbase + buf * 2 * TT + TT, h);
+      return true;
+    };
+    auto finish = [&](int seg, int (&l)[CW], int (&h)[CW]) {
+      tc_ld_wait();
+      tc_ld_done(l);
+      tc_ld_done(h);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[seg % NBUF]));
+    };
+    auto fold = [&](int seg, const int (&l)[CW], const int (&h)[CW]) {
+      const int g = seg * p.seg / G;
+      const float sc = half_bits_to_float(p.w.scale[(size_t)nr * gpr + g]);
+      const int w128 = p.wsum[(size_t)nr * p.nseg + seg] * 128;
+#pragma unroll
+      for (int c = 0; c < CW; c++) {
+        float v;
+        if (ZC) {
+          const unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c] + (unsigned)w128 -
+                             (unsigned)p.w.zp[(size_t)nr * gpr + g] * (unsigned)sm.xsum[cg * CW + c][seg];
+          v = (float)(int)a;
+        } else {
+          // |h|, |l + 128 W| < 2^22 for int4 weights: both exact as floats,
+          // one rounding in the fma, as the conversion of the int32 sum
+          v = fmaf(256.0f, tc_small_to_float(h[c]), tc_small_to_float(l[c] + w128));
+        }
+        accf[c] = fmaf(v, sc, accf[c]);
+      }
+    };
+    bool ok = start(0, la, ha);
+    if (ok) finish(0, la, ha);
+    // two segments per trip: fold one while the next one's loads are in flight
+    for (int seg = 0; ok && seg < p.nseg; seg += 2) {
+      if (seg + 1 < p.nseg) ok = start(seg + 1, lb, hb);
+      fold(seg, la, ha);
+      if (!ok || seg + 1 >= p.nseg) break;
+      finish(seg + 1, lb, hb);
+      if (seg + 2 < p.nseg) ok = start(seg + 2, la, ha);
+      fold(seg + 1, lb, hb);
+      if (ok && seg + 2 < p.nseg) finish(seg + 2, la, ha);
+    }
+    if (ok && !*(volatile int *)&sm.abort && n < p.n_full) {
+      const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
+#pragma unroll
+      for (int c = 0; c < CW; c++) {
+        const int m = t0 + cg * CW + c;
+        if (m >= p.T) break;
+        float *dst = p.out + (size_t)m * p.OUT + n;
+        float r = accf[c] * p.sx[m];
+        if (p.epi & EPI_BIAS) r += bn;
+        if (p.epi & EPI_GELU) r = gelu(r);
+        if (p.epi & EPI_RESID) r += *dst;
+        *dst = r;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == TC_EPI_WARPS) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+  }
+}
+
 }  // namespace llmq
