@@ -1144,7 +1144,10 @@ inline long long align16(long long x) { return (x + 15) & ~15LL; }
 llmq_status mega_setup(llmq_model *m) {
   llmq_ctx *ctx = m->ctx;
   m->mega_ok = false;
-  if (m->kv->kind != LLMQ_KV_QUANT8 || m->n_head != 12 || m->C != 768 || m->kv->v8.head_dim != 64) return LLMQ_OK;
+  if (m->n_head != 12 || m->C != 768) return LLMQ_OK;
+  if (!(m->kv->kind == LLMQ_KV_QUANT8 && m->kv->v8.head_dim == 64) &&
+      !(m->kv->kind == LLMQ_KV_INTATTN && m->kv->ia.head_dim == 64 && m->kv->max_t <= 1024))
+    return LLMQ_OK;
   for (const llmq_weight *w : m->mats)
     if (!w->blocked) return LLMQ_OK;
   const llmq_weight *hd = m->head;
@@ -1259,6 +1262,9 @@ llmq_status run_mega(llmq_model *m, const int *first_token, int pos0, int steps,
   a.small = m->small;
   a.head = m->head->view();
   a.kv = m->kv->v8;
+  a.ia = m->kv->ia;
+  a.intattn = m->kv->kind == LLMQ_KV_INTATTN;
+  a.ia_mult = ia_mult();
   a.ll = m->mega_ll;
   a.logits = logits;
   a.ids = ids;

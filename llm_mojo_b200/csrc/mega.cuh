@@ -66,7 +66,10 @@ struct MegaArgs {
   int n_layer, C, V, n_head;
   const float *small;            // float32 parameters in Model.small order
   WeightView head;               // the tied wte / head in its stored layout (embedding lookups)
-  KV8View kv;
+  KV8View kv;                    // QuantKV[8] cache (intattn == 0)
+  IAView ia;                     // IntAttnKV cache (intattn != 0)
+  int intattn;
+  long long ia_mult;             // exp2_neg's multiplier (2^40 log2(e) / 2^16)
   unsigned long long *ll;        // exchange buffers (see MkLL)
   float *logits;                 // [V] last step's logits, or null
   int *ids;                      // [steps] produced ids
@@ -821,6 +824,135 @@ __device__ __noinline__ bool mk_attention(const MegaArgs &a, MkSmem &sm, const M
   return true;
 }
 
+// Attention phase of head h with IntAttnKV (int_attention.mojo:119-269): the
+// token's key and value quantized into the cache (quantize_head), then
+// attend_one over positions 0..pos, published as att[h*64 .. +64). The
+// arithmetic is ia_attend_kernel's: integer scores and softmax, value sums
+// flushed to float per 128 pairs of positions in order. The K/V staging
+// buffers (unused by this cache) hold the reductions' scratch. Returns false
+// on timeout.
+__device__ __noinline__ bool mk_ia_attention(const MegaArgs &a, MkSmem &sm, const MkLL &ll, int l, int h, int pos,
+                                             unsigned flag) {
+  const IAView &c = a.ia;
+  const int HS = 64, C = a.C, tid = threadIdx.x;
+  {
+    long long t0 = clock64();
+    if (tid < 192) {
+      const int which = tid >> 6, d = tid & 63;
+      const unsigned long long *src = a.ll + ll.qkv(l) + which * C + h * 64 + d;
+      unsigned long long v;
+      while (true) {
+        v = ld_relaxed_u64(src);
+        if ((unsigned)(v >> 32) == flag) break;
+        if (!mk_alive(a, sm, t0, 2)) break;
+        if (MK_BACKOFF_NS > 0) __nanosleep(MK_BACKOFF_NS);
+      }
+      const float x = __uint_as_float((unsigned)v);
+      if (which == 0)
+        sm.att_q[d] = x;
+      else
+        sm.xf[(which - 1) * 64 + d] = x;
+    }
+    cta_sync();
+    if (sm.abort) return false;
+  }
+  long long *redl = reinterpret_cast<long long *>(&sm.kst[0][0]);  // 32 slots
+  int32_t *qpair = reinterpret_cast<int32_t *>(&sm.kst[4][0]);     // 32 pairs
+  int32_t *part = reinterpret_cast<int32_t *>(&sm.kst[8][0]);      // [4][64]
+  float *redf = sm.red;
+  int32_t *sc = reinterpret_cast<int32_t *>(sm.att_sc);            // [max_t]
+  int16_t *w = reinterpret_cast<int16_t *>(sm.att_ps);             // [max_t + 2]
+  // store (quantize_head) of the key and the value
+  for (int which = 0; which < 2; which++) {
+    const bool act = tid < HS;
+    ia_quantize_head(c, act ? sm.xf[which * 64 + tid] : 0.0f, act, l, h, pos, which, redf);
+  }
+  __syncthreads();  // the cache writes of this CTA are visible to it
+  const int npos = pos + 1;
+  const int nr = (npos + IA_PB - 1) / IA_PB * IA_PB;
+  // 1. the query as int16
+  const float qv = tid < HS ? sm.att_q[tid] : 0.0f;
+  const float mq = ia_block_max_f(fabsf(qv), redf);
+  float sq = mq / 32767.0f;
+  if (sq == 0.0f) sq = 1.0f;
+  const float invq = 1.0f / sq;
+  const int16_t qi = (int16_t)roundf(qv * invq);
+  const int16_t qi_next = (int16_t)__shfl_down_sync(0xffffffffu, (int)qi, 1);
+  if (tid < HS && (tid & 1) == 0) qpair[tid / 2] = (int32_t)(uint16_t)qi | ((int32_t)qi_next << 16);
+  const long long qm = llround((double)sq / sqrt((double)HS) * (double)(1LL << (IA_SF + IA_KS)));
+  __syncthreads();
+  // 2. scores of positions [0, nr)
+  const int32_t *ks = c.kq + ia_lh(c, l, h) * c.max_t;
+  long long smax = LLONG_MIN;
+  for (int p = tid; p < nr; p += MK_THREADS) {
+    const uint16_t *kp = (const uint16_t *)(c.k + ia_k_at(c, l, h, p, 0));
+    int acc = 0;
+    for (int j = 0; j < HS / 2; j++) acc = __dp2a_lo(qpair[j], (int)kp[(size_t)j * IA_PB], acc);
+    const long long t1 = ((long long)acc * (long long)ks[p] + (1LL << (IA_KS - 1))) >> IA_KS;
+    const long long sfix = (t1 * qm + (1LL << (IA_KS - 1))) >> IA_KS;
+    sc[p] = (int32_t)sfix;
+    if (p < npos && (long long)(int32_t)sfix > smax) smax = (int32_t)sfix;
+  }
+  const long long m = ia_block_max_ll(smax, redl);
+  // 3. masked_exp: e in Q30 over the valid positions, total in int64
+  long long part_total = 0;
+  for (int p = tid; p < nr; p += MK_THREADS) {
+    const long long ev = p < npos ? ia_exp2_neg(m - (long long)sc[p], a.ia_mult) : 0;
+    sc[p] = (int32_t)ev;
+    part_total += ev;
+  }
+  const long long total = ia_block_sum_ll(part_total, redl);
+  // 4. value weights and sums
+  const int32_t *vs = c.vq + ia_lh(c, l, h) * c.max_t;
+  long long vm = 0;
+  for (int p = tid; p < npos; p += MK_THREADS) vm = (long long)vs[p] > vm ? (long long)vs[p] : vm;
+  const long long vmax = ia_block_max_ll(vm, redl);
+  unsigned long long *o = a.ll + ll.att(l) + h * HS;
+  if (vmax == 0 || total == 0) {
+    if (tid < HS) st_relaxed_u64(o + tid, ll_pack(0.0f, flag));
+    return true;
+  }
+  const long long inv47 = (1LL << 47) / vmax;
+  for (int p = tid; p < nr + 2; p += MK_THREADS) {
+    long long ww = 0;
+    if (p < nr) {
+      const long long ee = sc[p];
+      const long long r16 = p < npos ? ((long long)vs[p] * inv47) >> 31 : 0;
+      ww = (ee * r16 + (1LL << 30)) >> 31;
+      if (ww > 32767) ww = 32767;
+      if (ee == 0) ww = 0;
+    }
+    w[p] = (int16_t)ww;
+  }
+  __syncthreads();
+  constexpr int nparts = MK_THREADS / 64;  // threads per dimension
+  const int d = tid % HS, pidx = tid / HS;
+  const int npairs = (npos + 1) / 2;
+  float accf = 0.0f;
+  const uint16_t *vbase = (const uint16_t *)(c.v + ia_v_at(c, l, h, 0, 0));
+  for (int sg = 0; sg < npairs; sg += 128) {
+    const int end = npairs < sg + 128 ? npairs : sg + 128;
+    int acc = 0;
+    for (int pp = sg + pidx; pp < end; pp += nparts) {
+      const int wp = (int)(uint16_t)w[2 * pp] | ((int)w[2 * pp + 1] << 16);
+      acc = __dp2a_lo(wp, (int)vbase[(size_t)pp * HS + d], acc);
+    }
+    part[pidx * HS + d] = acc;
+    __syncthreads();
+    if (pidx == 0) {
+      unsigned sum = 0;
+      for (int q = 0; q < nparts; q++) sum += (unsigned)part[q * HS + d];
+      accf += (float)(int32_t)sum;
+    }
+    __syncthreads();
+  }
+  if (pidx == 0) {
+    const float fs = (float)((double)vmax * (double)(1 << 15) / ((double)(1 << IA_KS) * (double)total));
+    st_relaxed_u64(o + d, ll_pack(accf * fs, flag));
+  }
+  return true;
+}
+
 // Embedding of `token` at `pos` (gpt2t.mojo:378-385) into sm.xfull.
 __device__ __noinline__ void mk_embed(const MegaArgs &a, MkSmem &sm, int token, int pos) {
   const int C = a.C, gpr = a.head.cols / a.head.group;
@@ -1004,7 +1136,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       const float *vec = a.small + (size_t)l * 13 * C;
       // ---- A: LN1 + QKV ----
       {
-        if (cta < a.n_head) mk_kv_prefetch(a, sm, l, cta, pos);
+        if (cta < a.n_head && !a.intattn) mk_kv_prefetch(a, sm, l, cta, pos);
         const MkChunk &ch = sm.chunks[ci++];
         if (ch.r1 == ch.r0) {
           if (!(ok = skip_chunk())) break;
@@ -1031,7 +1163,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       }
       // ---- B: KV store + attention (CTA h for head h) ----
       if (cta < a.n_head) {
-        if (!(ok = mk_attention(a, sm, ll, l, cta, pos, flag))) break;
+        ok = a.intattn ? mk_ia_attention(a, sm, ll, l, cta, pos, flag) : mk_attention(a, sm, ll, l, cta, pos, flag);
+        if (!ok) break;
         tick(PF_ATTN);
       }
       // ---- C: PROJ + residual ----
