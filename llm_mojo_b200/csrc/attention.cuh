@@ -370,15 +370,21 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
     }
     __syncthreads();
     if (tid < nchains) {
+      // the 4 queries' chains advance together (each in position order), so
+      // that each value read serves all 4 and the chains' latencies overlap
+      int npj[4];
+      int send = s0;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const int qi = q0 + j;
-        if (qi >= nq) break;
-        const int np = min(pos0 + t0 + qi + 1, s0 + n);  // this query's positions within the tile
-        const float *ps = sc + (size_t)qi * P;
-        float a = acc[j];
-        for (int s = s0; s < np; s++) a = fmaf(ps[s], tile[(s - s0) * HP + dd], a);
-        acc[j] = a;
+        npj[j] = qi < nq ? min(pos0 + t0 + qi + 1, s0 + n) : s0;  // this query's positions within the tile
+        send = max(send, npj[j]);
+      }
+      for (int s = s0; s < send; s++) {
+        const float v = tile[(s - s0) * HP + dd];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+          if (s < npj[j]) acc[j] = fmaf(sc[(size_t)(q0 + j) * P + s], v, acc[j]);
       }
     }
   }
