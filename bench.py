@@ -497,10 +497,17 @@ def run_sweep(args):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     peak, peak_kind = peaks()
     rng = np.random.default_rng(1)
+    only_fmt, only_shape = None, None
+    if args.sweep_only:
+        only_fmt, _, shp = args.sweep_only.partition(":")
+        only_shape = tuple(int(v) for v in shp.split("x")) if shp else None
     for out_, in_ in SWEEP_SHAPES:
+        x_host = rng.standard_normal(in_).astype(np.float32)  # drawn for every shape: filters keep the inputs
+        if only_shape and (out_, in_) != only_shape:
+            continue
         src = (np.random.default_rng(out_ * 7 + in_).standard_normal((in_, out_), dtype=np.float32) *
                np.float32(0.02)).astype(np.float32)  # [IN, OUT] (Hugging Face layout)
-        x = torch.from_numpy(rng.standard_normal(in_).astype(np.float32)).cuda()
+        x = torch.from_numpy(x_host).cuda()
         b = torch.zeros(out_, dtype=torch.float32, device="cuda")
         y = torch.zeros(out_, dtype=torch.float32, device="cuda")
         cases = []
@@ -517,6 +524,8 @@ def run_sweep(args):
             # layer matrices stay [IN, OUT]; the head is wte [V, C]
             cases.append((dt, lambda dt=dt: DenseMatrix(ctx, dt, src if out_ != 50257 else np.ascontiguousarray(src.T))))
         for name, make in cases:
+            if only_fmt and name != only_fmt:
+                continue
             try:
                 w = make()
             except Exception as e:  # a format the shape does not divide into
@@ -578,6 +587,9 @@ def main():
                     help="batched workload: sequences (config 3 has 256; fewer for profiling captures)")
     ap.add_argument("--batch-steps", type=int, default=128,
                     help="batched workload: greedy tokens per sequence (config 3 has 128)")
+    ap.add_argument("--sweep-only", default=None, metavar="FORMAT[:OUTxIN]",
+                    help="sweep workload: time only this format (e.g. int8-ch-a16), optionally at one shape "
+                         "(e.g. int8-ch-a16:50257x768), for profiling captures")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")

@@ -244,6 +244,33 @@ __device__ __forceinline__ void int_phase(const WeightView &w, int row, int q, i
       ln[2 * q + 8] = a2;
       ln[2 * q + 9] = a3;
     }
+  } else if (FMT == FMT_GEN8 && w.group == w.cols) {
+    // per-channel int8: one group, so the part's chunks are read 8 at a
+    // time with all loads in flight, then accumulated
+    const int nch = w.cols >> 5;
+    const uint8_t *rp = w.codes + (size_t)row * w.cols;
+    const int c0 = (nch * p) / P, c1 = (nch * (p + 1)) / P;
+    int a[4] = {0, 0, 0, 0};
+    for (int cb = c0; cb < c1; cb += 8) {
+      uint2 v[8];
+#pragma unroll
+      for (int k = 0; k < 8; k++)
+        if (cb + k < c1) v[k] = __ldg((const uint2 *)(rp + (cb + k) * 32) + q);
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        if (cb + k < c1) {
+          const int *xs = xp32 + (cb + k) * 16;
+          a[0] = dp2a_lo_su(xs[4 * q], v[k].x, a[0]);
+          a[1] = dp2a_hi_su(xs[4 * q + 1], v[k].x, a[1]);
+          a[2] = dp2a_lo_su(xs[4 * q + 2], v[k].y, a[2]);
+          a[3] = dp2a_hi_su(xs[4 * q + 3], v[k].y, a[3]);
+        }
+      }
+    }
+    if (c0 < c1) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) atomicAdd(&lanes[lane_of<FMT>(q, j)], a[j]);
+    }
   } else {
     const int G = w.group, nch = w.cols >> 5;
     const int bits = FMT == FMT_GEN8 ? 8 : 4;
@@ -284,6 +311,9 @@ __device__ __forceinline__ void int_phase(const WeightView &w, int row, int q, i
   }
 }
 
+template <int FMT>
+__device__ __forceinline__ float tree_lanes(const float f[4]);
+
 // Float phase: the 4 lane chains of thread q over the row's units, then the
 // halving tree across the 4 threads of the row. Returns dot_row_i16.
 template <int FMT>
@@ -318,7 +348,13 @@ __device__ __forceinline__ float float_phase(const WeightView &w, int row, int q
       }
     }
   }
-  // halving tree over the 16 lanes (4 per thread, 4 consecutive threads).
+  return tree_lanes<FMT>(f);
+}
+
+// Halving tree over a row's 16 lane chains, 4 per thread in 4 consecutive
+// threads (thread q holds lanes lane_of(q, 0..3)).
+template <int FMT>
+__device__ __forceinline__ float tree_lanes(const float f[4]) {
   if (FMT == FMT_GEN8) {
     // lanes 4q..4q+3: level 1 pairs thread q with q^2, level 2 q with q^1.
     float a[4];
@@ -344,6 +380,8 @@ __device__ __forceinline__ float float_phase(const WeightView &w, int row, int q
 __device__ __forceinline__ bool better(float v, int i, float bv, int bi) {
   return v > bv || (v == bv && i < bi);
 }
+
+__device__ __forceinline__ void block_argmax_finish(const GemvArgs &a, float best_v, int best_i, float *red);
 
 // One-token GEMV. CTA = R rows x P parts x 4 threads; the CTA loops over
 // row tiles with a grid stride.
@@ -382,8 +420,223 @@ __global__ void __launch_bounds__(R * P * 4) gemv_a16_kernel(GemvArgs a) {
     __syncthreads();
   }
 
-  if (ARGMAX) {
-    float *red = (float *)(smem + pl.red);
+  if (ARGMAX) block_argmax_finish(a, best_v, best_i, (float *)(smem + pl.red));
+}
+
+// ---------------------------------------------------------------------------
+// Tall matrices (the vocabulary head): whole rows per 4 threads
+// ---------------------------------------------------------------------------
+// Thread q of a row holds lanes lane_of(q, 0..3) over the WHOLE row, so the
+// integer lane sums, the float chains over the row's units (groups or
+// 256-blocks, in the reference's order) and the halving tree all stay in
+// registers and no warp waits for another after the prologue. A warp takes
+// 8 rows at a time. Rows are read in slabs of 256 columns (8 chunks of 32):
+// the next slab's codes, scales and zero points are in flight while the
+// current slab is summed, and the first slab is requested before the
+// prologue so that its latency hides behind it. Group ends are tracked by a
+// cursor (no division per chunk). Same sums in the same order as
+// gemv_a16_kernel, so the outputs are identical.
+
+constexpr int kTallWarps = 8;
+constexpr int kTallMinBlocks = 3;
+
+template <int FMT>
+struct TallSlab {
+  uint32_t c[FMT == FMT_GEN8 ? 16 : 8];  // codes: chunk k in c[2k], c[2k+1] (int8) or c[k] (int4)
+  uint32_t sc[4];                        // f16 bits of entry k at bits 16 * (k % 2) of sc[k / 2]
+  uint32_t zp[2];                        // zero point of entry k at bits 8 * (k % 4) of zp[k / 4]
+  uint32_t ends;                         // GEN: bit k set when chunk k of the slab ends a group
+  int g;                                 // GEN: group of the slab's first chunk
+};
+// Entries: BLK4, the groups 2q and 2q + 1 of the 256-block; GEN, the group
+// that ends at chunk k of the slab (if one does).
+
+struct TallGeo {
+  int nch, cpg, gpr;  // 32-column chunks per row, chunks per group, groups per row
+};
+
+// Loads slab s of a row; cg / crem: the loader's group cursor (group index
+// and chunks of it seen so far), reset at the row's first slab.
+template <int FMT>
+__device__ __forceinline__ void tall_load(const WeightView &w, const TallGeo &geo, int row, int s, int q, int &cg,
+                                          int &crem, TallSlab<FMT> &d) {
+  if (FMT == FMT_BLK4) {
+    const uint32_t *wp = (const uint32_t *)(w.codes + (size_t)row * (w.cols >> 1) + s * 128) + q;
+#pragma unroll
+    for (int k = 0; k < 8; k++) d.c[k] = __ldg(wp + 4 * k);
+    const size_t g0 = (size_t)row * geo.gpr + s * 8 + 2 * q;
+    d.sc[0] = __ldg((const uint32_t *)(w.scale + g0));
+    d.zp[0] = __ldg((const uint16_t *)(w.zp + g0));
+  } else {
+    const int cb = FMT == FMT_GEN8 ? 32 : 16;
+    const uint8_t *rp = w.codes + ((size_t)row * geo.nch + s * 8) * cb;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      if (s * 8 + k < geo.nch) {
+        if (FMT == FMT_GEN8) {
+          const uint2 v = __ldg((const uint2 *)(rp + k * 32) + q);
+          d.c[2 * k] = v.x;
+          d.c[2 * k + 1] = v.y;
+        } else {
+          d.c[k] = __ldg((const uint32_t *)(rp + k * 16) + q);
+        }
+      }
+    }
+    if (s == 0) {
+      cg = 0;
+      crem = 0;
+    }
+    d.g = cg;
+    d.ends = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k++) d.sc[k] = 0;
+    d.zp[0] = d.zp[1] = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      if (s * 8 + k < geo.nch && ++crem == geo.cpg) {
+        const size_t gi = (size_t)row * geo.gpr + cg;
+        d.sc[k >> 1] |= (uint32_t)__ldg(w.scale + gi) << (16 * (k & 1));
+        d.zp[k >> 2] |= (uint32_t)__ldg(w.zp + gi) << (8 * (k & 3));
+        d.ends |= 1u << k;
+        cg++;
+        crem = 0;
+      }
+    }
+  }
+}
+
+// Sums slab s of this thread's row into the integer lanes acc (GEN: the open
+// group) and folds finished units into the float chains f.
+template <int FMT>
+__device__ __forceinline__ void tall_sum(const TallGeo &geo, int s, int q, const TallSlab<FMT> &d, const int *xp32,
+                                         const unsigned char *smem, const SmemPlan<FMT> &pl, int acc[4], float f[4]) {
+  if (FMT == FMT_BLK4) {
+    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const uint32_t lo = d.c[k] & 0x0F0F0F0Fu, hi = (d.c[k] >> 4) & 0x0F0F0F0Fu;
+      const int2 xa = *(const int2 *)(xp32 + s * 128 + k * 16 + 2 * q);
+      const int2 xb = *(const int2 *)(xp32 + s * 128 + k * 16 + 2 * q + 8);
+      a0 = dp2a_lo_su(xa.x, lo, a0);
+      a1 = dp2a_hi_su(xa.y, lo, a1);
+      a2 = dp2a_lo_su(xb.x, hi, a2);
+      a3 = dp2a_hi_su(xb.y, hi, a3);
+    }
+    // lanes 2q, 2q + 1, 2q + 8, 2q + 9 belong to groups 2q, 2q + 1, 2q, 2q + 1
+    const float *xsf = (const float *)(smem + pl.xs) + s * 16;
+    const float zp0 = (float)(d.zp[0] & 0xFFu), zp1 = (float)((d.zp[0] >> 8) & 0xFFu);
+    const float sc0 = half_bits_to_float((uint16_t)(d.sc[0] & 0xFFFFu));
+    const float sc1 = half_bits_to_float((uint16_t)(d.sc[0] >> 16));
+    f[0] = fmaf((float)a0 - zp0 * xsf[2 * q], sc0, f[0]);
+    f[1] = fmaf((float)a1 - zp1 * xsf[2 * q + 1], sc1, f[1]);
+    f[2] = fmaf((float)a2 - zp0 * xsf[2 * q + 8], sc0, f[2]);
+    f[3] = fmaf((float)a3 - zp1 * xsf[2 * q + 9], sc1, f[3]);
+  } else {
+    const int *xsum = (const int *)(smem + pl.xs);
+    int g = d.g;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+      const int c = s * 8 + k;
+      if (c < geo.nch) {
+        if (FMT == FMT_GEN8) {
+          const int4 xv = *(const int4 *)(xp32 + c * 16 + 4 * q);
+          acc[0] = dp2a_lo_su(xv.x, d.c[2 * k], acc[0]);
+          acc[1] = dp2a_hi_su(xv.y, d.c[2 * k], acc[1]);
+          acc[2] = dp2a_lo_su(xv.z, d.c[2 * k + 1], acc[2]);
+          acc[3] = dp2a_hi_su(xv.w, d.c[2 * k + 1], acc[3]);
+        } else {
+          const uint32_t lo = d.c[k] & 0x0F0F0F0Fu, hi = (d.c[k] >> 4) & 0x0F0F0F0Fu;
+          const int2 xa = *(const int2 *)(xp32 + c * 16 + 2 * q);
+          const int2 xb = *(const int2 *)(xp32 + c * 16 + 2 * q + 8);
+          acc[0] = dp2a_lo_su(xa.x, lo, acc[0]);
+          acc[1] = dp2a_hi_su(xa.y, lo, acc[1]);
+          acc[2] = dp2a_lo_su(xb.x, hi, acc[2]);
+          acc[3] = dp2a_hi_su(xb.y, hi, acc[3]);
+        }
+        if ((d.ends >> k) & 1u) {  // the group ends with this chunk: fold it into the lane chains
+          const int zp = (int)((d.zp[k >> 2] >> (8 * (k & 3))) & 0xFFu);
+          const float sc = half_bits_to_float((uint16_t)((d.sc[k >> 1] >> (16 * (k & 1))) & 0xFFFFu));
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            const int v = (int)((unsigned)acc[j] - (unsigned)(zp * xsum[g * 16 + lane_of<FMT>(q, j)]));
+            f[j] = fmaf((float)v, sc, f[j]);
+            acc[j] = 0;
+          }
+          g++;
+        }
+      }
+    }
+  }
+}
+
+template <int FMT, int PRO, bool ARGMAX>
+__global__ void __launch_bounds__(kTallWarps * 32, kTallMinBlocks) gemv_tall_kernel(GemvArgs a) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  SmemPlan<FMT> pl(a.w.cols, a.w.group, 0);
+  const int t = threadIdx.x, q = t & 3, rw = (t & 31) >> 2;
+  const int rows = a.w.rows;
+  TallGeo geo;
+  geo.nch = a.w.cols >> 5;
+  geo.cpg = FMT == FMT_BLK4 ? 1 : a.w.group >> 5;
+  geo.gpr = FMT == FMT_BLK4 ? a.w.cols >> 5 : a.w.cols / a.w.group;
+  const int nslab = FMT == FMT_BLK4 ? a.w.cols >> 8 : (geo.nch + 7) >> 3;
+  const int n8 = (rows + 7) >> 3, stride = gridDim.x * kTallWarps;
+  int rg = blockIdx.x * kTallWarps + (t >> 5), s = 0, cg = 0, crem = 0;
+  TallSlab<FMT> A, B;
+  if (rg < n8) tall_load<FMT>(a.w, geo, min(rg * 8 + rw, rows - 1), 0, q, cg, crem, A);
+  const float sx = prologue<FMT, PRO>(a, smem, pl);
+  const int *xp32 = (const int *)(smem + pl.xq);
+  float best_v = -__int_as_float(0x7f800000);
+  int best_i = 0x7fffffff;
+  float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int acc[4] = {0, 0, 0, 0};
+  // one slab: request the next position's slab into nx, sum cur, finish the
+  // row after its last slab
+  auto step = [&](const TallSlab<FMT> &cur, TallSlab<FMT> &nx) {
+    int ns = s + 1, nrg = rg;
+    if (ns == nslab) {
+      ns = 0;
+      nrg += stride;
+    }
+    if (nrg < n8) tall_load<FMT>(a.w, geo, min(nrg * 8 + rw, rows - 1), ns, q, cg, crem, nx);
+    tall_sum<FMT>(geo, s, q, cur, xp32, smem, pl, acc, f);
+    if (ns == 0) {
+      const float dot = tree_lanes<FMT>(f);
+      const int row = rg * 8 + rw;
+      if (q == 0 && row < rows) {
+        float v = dot * sx;
+        if (a.epi & EPI_BIAS) v += a.bias[row];
+        if (a.epi & EPI_GELU) v = gelu(v);
+        if (a.epi & EPI_RESID) v += a.out[row];
+        if (a.out) a.out[row] = v;
+        if (ARGMAX && better(v, row, best_v, best_i)) {
+          best_v = v;
+          best_i = row;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        f[j] = 0.0f;
+        acc[j] = 0;
+      }
+    }
+    s = ns;
+    rg = nrg;
+  };
+  while (rg < n8) {
+    step(A, B);
+    if (rg >= n8) break;
+    step(B, A);
+  }
+  if (ARGMAX) block_argmax_finish(a, best_v, best_i, (float *)(smem + pl.red));
+}
+
+// The fused greedy head's argmax: block reduction of the threads'
+// candidates, one partial per CTA, and the last CTA to finish reduces the
+// partials in CTA order and advances the decode state.
+__device__ __forceinline__ void block_argmax_finish(const GemvArgs &a, float best_v, int best_i, float *red) {
+  const int t = threadIdx.x;
+  {
     int *redi = (int *)(red + 32);
     // warp reduce
     for (int o = 16; o > 0; o >>= 1) {

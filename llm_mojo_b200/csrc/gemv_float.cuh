@@ -313,6 +313,61 @@ __global__ void dense_gemv_parts_kernel(const void *w, const float *x, int IN, i
   scratch[(size_t)p * OUT + j] = acc;
 }
 
+// The same parts, staged: a CTA takes one part x 32 columns. Its threads
+// copy the strip (the part's rows x 32 columns, 128 or 64 bytes a row) into
+// shared memory with 16-byte cp.async copies, all of them in flight at
+// once; warp 0 then runs the 32 chains in row order from shared memory.
+// Needs OUT * element size to be a multiple of 16 bytes.
+constexpr int DS_THREADS = 256;
+constexpr int DS_SMEM = 200 * 1024;
+
+__host__ __device__ inline int ds_rows(int IN, int nparts) { return (IN + nparts - 1) / nparts; }
+__host__ __device__ inline int ds_smem(int IN, int nparts, int es) {
+  const int rows = ds_rows(IN, nparts);
+  return ((rows * 4 + 15) & ~15) + rows * 32 * es;
+}
+
+template <int DT>
+__global__ void __launch_bounds__(DS_THREADS) dense_strip_kernel(const void *w, const float *x, int IN, int OUT,
+                                                                int nparts, float *scratch) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  constexpr int es = DT == 0 ? 4 : 2;
+  const int j0 = blockIdx.x * 32, p = blockIdx.y;
+  const int rows = ds_rows(IN, nparts);
+  const int i0 = p * rows, n = max(0, min(IN, i0 + rows) - i0);
+  float *xs = (float *)smem;
+  uint8_t *tiles = smem + ((rows * 4 + 15) & ~15);
+  const int ppr = min(32, OUT - j0) * es / 16;  // 16-byte pieces per row
+  const uint8_t *src = (const uint8_t *)w + ((size_t)i0 * OUT + j0) * es;
+  const size_t rstride = (size_t)OUT * es;
+  for (int k = threadIdx.x; k < n * ppr; k += DS_THREADS) {
+    const int r = k / ppr, c = k - r * ppr;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(rf_smem_u32(tiles + r * 32 * es + c * 16)),
+                 "l"(src + r * rstride + c * 16)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int k = threadIdx.x; k < n; k += DS_THREADS) xs[k] = x[i0 + k];
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  auto wv = [&](int r) {
+    if (DT == 0) return ((const float *)tiles)[r * 32 + lane];
+    const uint16_t h = ((const uint16_t *)tiles)[r * 32 + lane];
+    if (DT == 1) return __half2float(__ushort_as_half(h));
+    return __uint_as_float((unsigned)h << 16);
+  };
+  float acc = 0.0f;
+  int r = 0;
+  for (; r + 8 <= n; r += 8) {
+#pragma unroll
+    for (int k = 0; k < 8; k++) acc = fmaf(xs[r + k], wv(r + k), acc);
+  }
+  for (; r < n; r++) acc = fmaf(xs[r], wv(r), acc);
+  if (j0 + lane < OUT) scratch[(size_t)p * OUT + j0 + lane] = acc;
+}
+
 __global__ void dense_gemv_combine_kernel(const float *scratch, const float *bias, float *out, int OUT, int nparts,
                                           int epi) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;

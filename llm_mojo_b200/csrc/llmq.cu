@@ -146,9 +146,17 @@ int smem_bytes(const WeightView &w) {
 
 constexpr int kMaxSmem = 200 * 1024;
 
+// From this many rows on, the whole-row kernel (4 threads per row, no split
+// along the row) has enough rows to fill the GPU and wins.
+constexpr int kTallRows = 8192;
+bool use_tall(const WeightView &w) { return w.rows >= kTallRows; }
+
 template <int FMT, int PRO, bool ARG>
 cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s) {
-  gemv_a16_kernel<FMT, PRO, kR, kP, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
+  if (use_tall(a.w))
+    gemv_tall_kernel<FMT, PRO, ARG><<<grid, kTallWarps * 32, SmemPlan<FMT>(a.w.cols, a.w.group, 0).total, s>>>(a);
+  else
+    gemv_a16_kernel<FMT, PRO, kR, kP, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
   return cudaGetLastError();
 }
 
@@ -162,12 +170,28 @@ cudaError_t configure_fmt() {
   set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR, kP, false>);
   set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, true>);
   set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, false>);
+  set((const void *)gemv_tall_kernel<FMT, PRO_LN, true>);
+  set((const void *)gemv_tall_kernel<FMT, PRO_LN, false>);
+  set((const void *)gemv_tall_kernel<FMT, PRO_QUANT, true>);
+  set((const void *)gemv_tall_kernel<FMT, PRO_QUANT, false>);
+  if (FMT == FMT_BLK4) {  // once: the dense strips
+    auto set_ds = [&](const void *k) {
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, DS_SMEM);
+    };
+    set_ds((const void *)dense_strip_kernel<0>);
+    set_ds((const void *)dense_strip_kernel<1>);
+    set_ds((const void *)dense_strip_kernel<2>);
+  }
   return e;
 }
 
 int fmt_of(const WeightView &w) { return w.blocked ? FMT_BLK4 : (w.bits == 4 ? FMT_GEN4 : FMT_GEN8); }
 
 int gemv_grid(const llmq_ctx *ctx, const WeightView &w) {
+  if (use_tall(w)) {
+    const int ctas = ((w.rows + 7) / 8 + kTallWarps - 1) / kTallWarps;
+    return std::min(ctas, ctx->num_sms * kTallMinBlocks);
+  }
   int tiles = (w.rows + kR - 1) / kR;
   int cap = ctx->num_sms * 8;
   return tiles < cap ? tiles : cap;
@@ -759,6 +783,21 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     llmq_status st = ensure_scratch(ctx, (size_t)np * OUT * 4);
     if (st != LLMQ_OK) return st;
     float *scratch = (float *)ctx->scratch;
+    const int es = w->rtype == RT_F32 ? 4 : 2;
+    if ((OUT * es) % 16 == 0 && ds_smem(IN, np, es) <= DS_SMEM) {
+      const dim3 sgrid((OUT + 31) / 32, np);
+      const int sm = ds_smem(IN, np, es);
+      if (w->rtype == RT_F32)
+        dense_strip_kernel<0><<<sgrid, DS_THREADS, sm, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+      else if (w->rtype == RT_F16)
+        dense_strip_kernel<1><<<sgrid, DS_THREADS, sm, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+      else
+        dense_strip_kernel<2><<<sgrid, DS_THREADS, sm, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
+      CKL();
+      dense_gemv_combine_kernel<<<(OUT + 255) / 256, 256, 0, ctx->stream>>>(scratch, bias, out, OUT, np, epi);
+      CKL();
+      return LLMQ_OK;
+    }
     dim3 grid((OUT + 255) / 256, np);
     if (w->rtype == RT_F32) dense_gemv_parts_kernel<0><<<grid, 256, 0, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);
     else if (w->rtype == RT_F16) dense_gemv_parts_kernel<1><<<grid, 256, 0, ctx->stream>>>(w->codes, x, IN, OUT, np, scratch);

@@ -87,6 +87,27 @@ def test_affine_float_rows(torch, ctx, fmt, IN, OUT):
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("IN,OUT", SHAPES)
 def test_dense_gemv_parts(torch, ctx, dt, IN, OUT):
+    check_dense_gemv(torch, ctx, dt, IN, OUT, 4)
+
+
+@pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("IN,OUT,parts", [(770, 72, 4), (3072, 2304, 3), (768, 768, 1), (3072, 768, 1), (100, 40, 8)])
+def test_dense_gemv_strips(torch, ctx, dt, IN, OUT, parts):
+    """The staged strips (32 columns x one part per CTA): a ragged last strip
+    (72 and 40 columns), parts that do not divide the inputs (770 / 4,
+    100 / 8), other part counts, and a part too long to stage (3072 rows of
+    f32 in one part), which keeps the unstaged kernel. Same bits as the
+    oracle."""
+    from llm_mojo_b200 import kernels
+
+    kernels.set_dense_parts(ctx, parts)
+    try:
+        check_dense_gemv(torch, ctx, dt, IN, OUT, parts)
+    finally:
+        kernels.set_dense_parts(ctx, 4)
+
+
+def check_dense_gemv(torch, ctx, dt, IN, OUT, parts):
     from llm_mojo_b200 import kernels
     from llm_mojo_b200.tensor import DenseMatrix
 
@@ -99,7 +120,7 @@ def test_dense_gemv_parts(torch, ctx, dt, IN, OUT):
     kernels.linear(ctx, out, dev(torch, x), gw, dev(torch, b), 1, IN, OUT, gelu=True)
     want = np.zeros(OUT, dtype=np.float32)
     O.lib().oq_dense_gemv({"f32": 0, "f16": 1, "bf16": 2}[dt], O.ptr(gw.data), O.ptr(x), O.ptr(b), O.ptr(want), IN,
-                          OUT, 4, 0, 1)
+                          OUT, parts, 0, 1)
     assert np.array_equal(bits(out.cpu().numpy()), bits(want))
     gw.free()
 
