@@ -631,6 +631,192 @@ __global__ void __launch_bounds__(kTallWarps * 32, kTallMinBlocks) gemv_tall_ker
   if (ARGMAX) block_argmax_finish(a, best_v, best_i, (float *)(smem + pl.red));
 }
 
+// ---------------------------------------------------------------------------
+// Tall matrices in the head formats: per-warp cp.async rings
+// ---------------------------------------------------------------------------
+// For per-channel int8 (the head of config 0) and BLOCKED int4-g32 with
+// whole 256-column slabs: the same whole-row threads as gemv_tall_kernel,
+// but each warp streams its units (8 rows x one slab) through a private
+// ring of NSTG shared-memory stages filled by 16-byte cp.async copies, so
+// NSTG - 1 units are in flight per warp without holding registers. Each
+// warp waits only for its own copies (cp.async.wait_group + __syncwarp);
+// there are no mbarriers and no block-wide waits after the prologue. Rows
+// in a stage are padded so that a warp's 8 rows fall in different banks.
+// Same sums in the same order as gemv_a16_kernel.
+
+constexpr int kRingWarps = 8;
+constexpr int kRingBlocks = 2;  // CTAs per SM that the rings are sized for
+
+template <int FMT>
+struct Ring {
+  static constexpr int RB = FMT == FMT_GEN8 ? 256 : 128;            // code bytes per row and slab
+  static constexpr int RS = RB + (FMT == FMT_GEN8 ? 32 : 16);       // padded row stride in a stage
+  static constexpr int SCO = 8 * RS;                                // scales: BLK4 16 B per row; int8-ch 8 halves
+  static constexpr int ZPO = SCO + (FMT == FMT_BLK4 ? 8 * 16 : 16);  // zero points: BLK4 8 B per row; int8-ch 8 B
+  static constexpr int STAGE = (ZPO + (FMT == FMT_BLK4 ? 8 * 8 : 8) + 15) & ~15;
+  static constexpr int NSTG = FMT == FMT_GEN8 ? 5 : 8;
+};
+
+template <int FMT>
+__host__ __device__ inline int ring_smem(int in, int group) {
+  return ((SmemPlan<FMT>(in, group, 0).total + 15) & ~15) + kRingWarps * Ring<FMT>::NSTG * Ring<FMT>::STAGE;
+}
+
+__device__ __forceinline__ void cp16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp8(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
+template <int FMT, int PRO, bool ARGMAX>
+__global__ void __launch_bounds__(kRingWarps * 32, kRingBlocks) gemv_ring_kernel(GemvArgs a) {
+  using R = Ring<FMT>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  SmemPlan<FMT> pl(a.w.cols, a.w.group, 0);
+  const int t = threadIdx.x, q = t & 3, rw = (t & 31) >> 2, lane = t & 31, warp = t >> 5;
+  const int rows = a.w.rows, in = a.w.cols, gpr = in >> 5;
+  const int nslab = in >> 8, n8 = (rows + 7) >> 3;
+  const int gw = blockIdx.x * kRingWarps + warp, nw = gridDim.x * kRingWarps;
+  const int units = gw < n8 ? ((n8 - 1 - gw) / nw + 1) * nslab : 0;
+  uint8_t *ring = smem + ((pl.total + 15) & ~15) + (size_t)warp * R::NSTG * R::STAGE;
+
+  // copies unit (row group rg, slab s) into stage st
+  auto issue = [&](int rg, int s, uint8_t *st) {
+    const int row0 = rg * 8;
+    if (FMT == FMT_GEN8) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const int pc = lane + 32 * i, r = pc >> 4, c = pc & 15;
+        const int row = min(row0 + r, rows - 1);
+        cp16(st + r * R::RS + c * 16, a.w.codes + (size_t)row * in + s * 256 + c * 16);
+      }
+      if (row0 + 8 <= rows) {
+        if (lane == 0) cp16(st + R::SCO, a.w.scale + row0);
+        if (lane == 1) cp8(st + R::ZPO, a.w.zp + row0);
+      } else if (lane < 8) {  // the last, partial row group: plain loads of the rows that exist
+        const int row = min(row0 + lane, rows - 1);
+        ((uint16_t *)(st + R::SCO))[lane] = a.w.scale[row];
+        st[R::ZPO + lane] = a.w.zp[row];
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; i++) {
+        const int pc = lane + 32 * i, r = pc >> 3, c = pc & 7;
+        const int row = min(row0 + r, rows - 1);
+        cp16(st + r * R::RS + c * 16, a.w.codes + (size_t)row * (in >> 1) + s * 128 + c * 16);
+      }
+      if (lane < 16) {
+        const int r = lane & 7, row = min(row0 + r, rows - 1);
+        const size_t g0 = (size_t)row * gpr + s * 8;
+        if (lane < 8)
+          cp16(st + R::SCO + r * 16, a.w.scale + g0);
+        else
+          cp8(st + R::ZPO + r * 8, a.w.zp + g0);
+      }
+    }
+  };
+  int irg = gw, is = 0;  // next unit to issue
+  auto issue_next = [&](int k) {
+    if (k < units) {
+      issue(irg, is, ring + (k % R::NSTG) * R::STAGE);
+      if (++is == nslab) {
+        is = 0;
+        irg += nw;
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  for (int k = 0; k < R::NSTG - 1; k++) issue_next(k);
+  const float sx = prologue<FMT, PRO>(a, smem, pl);
+  const int *xp32 = (const int *)(smem + pl.xq);
+  float best_v = -__int_as_float(0x7f800000);
+  int best_i = 0x7fffffff;
+  float f[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int acc[4] = {0, 0, 0, 0};
+  int rg = gw, s = 0;
+  for (int u = 0; u < units; u++) {
+    issue_next(u + R::NSTG - 1);
+    asm volatile("cp.async.wait_group %0;" ::"n"(R::NSTG - 1) : "memory");
+    __syncwarp();
+    const uint8_t *st = ring + (u % R::NSTG) * R::STAGE;
+    const uint8_t *rp = st + rw * R::RS;
+    if (FMT == FMT_GEN8) {
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const uint2 v = *(const uint2 *)(rp + k * 32 + q * 8);
+        const int4 xv = *(const int4 *)(xp32 + (s * 8 + k) * 16 + 4 * q);
+        acc[0] = dp2a_lo_su(xv.x, v.x, acc[0]);
+        acc[1] = dp2a_hi_su(xv.y, v.x, acc[1]);
+        acc[2] = dp2a_lo_su(xv.z, v.y, acc[2]);
+        acc[3] = dp2a_hi_su(xv.w, v.y, acc[3]);
+      }
+      if (s == nslab - 1) {  // one group per row: fold it
+        const int *xsum = (const int *)(smem + pl.xs);
+        const int zp = (int)st[R::ZPO + rw];
+        const float sc = half_bits_to_float(((const uint16_t *)(st + R::SCO))[rw]);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const int v = (int)((unsigned)acc[j] - (unsigned)(zp * xsum[lane_of<FMT>(q, j)]));
+          f[j] = fmaf((float)v, sc, f[j]);
+        }
+      }
+    } else {
+      int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
+#pragma unroll
+      for (int k = 0; k < 8; k++) {
+        const uint32_t v = *(const uint32_t *)(rp + k * 16 + q * 4);
+        const uint32_t lo = v & 0x0F0F0F0Fu, hi = (v >> 4) & 0x0F0F0F0Fu;
+        const int2 xa = *(const int2 *)(xp32 + s * 128 + k * 16 + 2 * q);
+        const int2 xb = *(const int2 *)(xp32 + s * 128 + k * 16 + 2 * q + 8);
+        a0 = dp2a_lo_su(xa.x, lo, a0);
+        a1 = dp2a_hi_su(xa.y, lo, a1);
+        a2 = dp2a_lo_su(xb.x, hi, a2);
+        a3 = dp2a_hi_su(xb.y, hi, a3);
+      }
+      // lanes 2q, 2q + 1, 2q + 8, 2q + 9 belong to groups 2q, 2q + 1, 2q, 2q + 1
+      const uint32_t scw = *(const uint32_t *)(st + R::SCO + rw * 16 + 4 * q);
+      const uint32_t zpw = *(const uint16_t *)(st + R::ZPO + rw * 8 + 2 * q);
+      const float zp0 = (float)(zpw & 0xFFu), zp1 = (float)(zpw >> 8);
+      const float sc0 = half_bits_to_float((uint16_t)(scw & 0xFFFFu)), sc1 = half_bits_to_float((uint16_t)(scw >> 16));
+      const float *xs = (const float *)(smem + pl.xs) + s * 16;
+      f[0] = fmaf((float)a0 - zp0 * xs[2 * q], sc0, f[0]);
+      f[1] = fmaf((float)a1 - zp1 * xs[2 * q + 1], sc1, f[1]);
+      f[2] = fmaf((float)a2 - zp0 * xs[2 * q + 8], sc0, f[2]);
+      f[3] = fmaf((float)a3 - zp1 * xs[2 * q + 9], sc1, f[3]);
+    }
+    if (s == nslab - 1) {
+      const float dot = tree_lanes<FMT>(f);
+      const int row = rg * 8 + rw;
+      if (q == 0 && row < rows) {
+        float v = dot * sx;
+        if (a.epi & EPI_BIAS) v += a.bias[row];
+        if (a.epi & EPI_GELU) v = gelu(v);
+        if (a.epi & EPI_RESID) v += a.out[row];
+        if (a.out) a.out[row] = v;
+        if (ARGMAX && better(v, row, best_v, best_i)) {
+          best_v = v;
+          best_i = row;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        f[j] = 0.0f;
+        acc[j] = 0;
+      }
+      s = 0;
+      rg += nw;
+    } else {
+      s++;
+    }
+    __syncwarp();  // the stage is read: it may be refilled
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  if (ARGMAX) block_argmax_finish(a, best_v, best_i, (float *)(smem + pl.red));
+}
+
 // The fused greedy head's argmax: block reduction of the threads'
 // candidates, one partial per CTA, and the last CTA to finish reduces the
 // partials in CTA order and advances the decode state.

@@ -150,10 +150,20 @@ constexpr int kMaxSmem = 200 * 1024;
 // along the row) has enough rows to fill the GPU and wins.
 constexpr int kTallRows = 8192;
 bool use_tall(const WeightView &w) { return w.rows >= kTallRows; }
+// The head formats with whole 256-column slabs stream through per-warp
+// cp.async rings instead of register slabs.
+bool use_ring(const WeightView &w) {
+  if (!use_tall(w) || w.cols % 256) return false;
+  if (w.blocked) return ring_smem<FMT_BLK4>(w.cols, w.group) <= kMaxSmem;
+  return w.bits == 8 && w.group == w.cols && ring_smem<FMT_GEN8>(w.cols, w.group) <= kMaxSmem;
+}
 
 template <int FMT, int PRO, bool ARG>
 cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s) {
-  if (use_tall(a.w))
+  if ((FMT == FMT_BLK4 || FMT == FMT_GEN8) && use_ring(a.w))
+    gemv_ring_kernel<FMT == FMT_BLK4 ? FMT_BLK4 : FMT_GEN8, PRO, ARG>
+        <<<grid, kRingWarps * 32, ring_smem<FMT == FMT_BLK4 ? FMT_BLK4 : FMT_GEN8>(a.w.cols, a.w.group), s>>>(a);
+  else if (use_tall(a.w))
     gemv_tall_kernel<FMT, PRO, ARG><<<grid, kTallWarps * 32, SmemPlan<FMT>(a.w.cols, a.w.group, 0).total, s>>>(a);
   else
     gemv_a16_kernel<FMT, PRO, kR, kP, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
@@ -174,6 +184,13 @@ cudaError_t configure_fmt() {
   set((const void *)gemv_tall_kernel<FMT, PRO_LN, false>);
   set((const void *)gemv_tall_kernel<FMT, PRO_QUANT, true>);
   set((const void *)gemv_tall_kernel<FMT, PRO_QUANT, false>);
+  if (FMT != FMT_GEN4) {
+    constexpr int RF = FMT == FMT_BLK4 ? FMT_BLK4 : FMT_GEN8;
+    set((const void *)gemv_ring_kernel<RF, PRO_LN, true>);
+    set((const void *)gemv_ring_kernel<RF, PRO_LN, false>);
+    set((const void *)gemv_ring_kernel<RF, PRO_QUANT, true>);
+    set((const void *)gemv_ring_kernel<RF, PRO_QUANT, false>);
+  }
   if (FMT == FMT_BLK4) {  // once: the dense strips
     auto set_ds = [&](const void *k) {
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, DS_SMEM);
@@ -188,6 +205,7 @@ cudaError_t configure_fmt() {
 int fmt_of(const WeightView &w) { return w.blocked ? FMT_BLK4 : (w.bits == 4 ? FMT_GEN4 : FMT_GEN8); }
 
 int gemv_grid(const llmq_ctx *ctx, const WeightView &w) {
+  if (use_ring(w)) return ctx->num_sms * kRingBlocks;
   if (use_tall(w)) {
     const int ctas = ((w.rows + 7) / 8 + kTallWarps - 1) / kTallWarps;
     return std::min(ctas, ctx->num_sms * kTallMinBlocks);
