@@ -138,10 +138,21 @@ constexpr int kBgemvSmem = 200 * 1024;       // the batched GEMV's shared memory
 constexpr int kR = 16, kP = 3;
 constexpr int kThreads = kR * kP * 4;
 
+// Matrices with fewer rows than this use tiles of 4 rows x 12 parts (the
+// same 192 threads), so that the grid still covers every SM.
+constexpr int kR2 = 4, kP2 = 12;
+constexpr int kShortRows = 2048;
+static_assert(kR2 * kP2 == kR * kP, "both tile shapes launch kThreads threads");
+bool use_short(const WeightView &w) { return w.rows < kShortRows; }
+
+template <int FMT>
+int smem_bytes_r(const WeightView &w, int R) {
+  SmemPlan<FMT> pl(w.cols, w.group, R);
+  return pl.total;
+}
 template <int FMT>
 int smem_bytes(const WeightView &w) {
-  SmemPlan<FMT> pl(w.cols, w.group, kR);
-  return pl.total;
+  return smem_bytes_r<FMT>(w, use_short(w) ? kR2 : kR);
 }
 
 constexpr int kMaxSmem = 200 * 1024;
@@ -165,6 +176,8 @@ cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t s) {
         <<<grid, kRingWarps * 32, ring_smem<FMT == FMT_BLK4 ? FMT_BLK4 : FMT_GEN8>(a.w.cols, a.w.group), s>>>(a);
   else if (use_tall(a.w))
     gemv_tall_kernel<FMT, PRO, ARG><<<grid, kTallWarps * 32, SmemPlan<FMT>(a.w.cols, a.w.group, 0).total, s>>>(a);
+  else if (use_short(a.w))
+    gemv_a16_kernel<FMT, PRO, kR2, kP2, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
   else
     gemv_a16_kernel<FMT, PRO, kR, kP, ARG><<<grid, kThreads, smem_bytes<FMT>(a.w), s>>>(a);
   return cudaGetLastError();
@@ -180,6 +193,10 @@ cudaError_t configure_fmt() {
   set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR, kP, false>);
   set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, true>);
   set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR, kP, false>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR2, kP2, true>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_LN, kR2, kP2, false>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR2, kP2, true>);
+  set((const void *)gemv_a16_kernel<FMT, PRO_QUANT, kR2, kP2, false>);
   set((const void *)gemv_tall_kernel<FMT, PRO_LN, true>);
   set((const void *)gemv_tall_kernel<FMT, PRO_LN, false>);
   set((const void *)gemv_tall_kernel<FMT, PRO_QUANT, true>);
@@ -210,7 +227,8 @@ int gemv_grid(const llmq_ctx *ctx, const WeightView &w) {
     const int ctas = ((w.rows + 7) / 8 + kTallWarps - 1) / kTallWarps;
     return std::min(ctas, ctx->num_sms * kTallMinBlocks);
   }
-  int tiles = (w.rows + kR - 1) / kR;
+  const int r = use_short(w) ? kR2 : kR;
+  int tiles = (w.rows + r - 1) / r;
   int cap = ctx->num_sms * 8;
   return tiles < cap ? tiles : cap;
 }
@@ -233,7 +251,8 @@ cudaError_t launch_gemv(const llmq_ctx *ctx, const GemvArgs &a, int pro, bool ar
 
 bool smem_ok(const WeightView &w) {
   int fmt = fmt_of(w);
-  int b = fmt == FMT_BLK4 ? smem_bytes<FMT_BLK4>(w) : (fmt == FMT_GEN4 ? smem_bytes<FMT_GEN4>(w) : smem_bytes<FMT_GEN8>(w));
+  int b = fmt == FMT_BLK4 ? smem_bytes_r<FMT_BLK4>(w, kR)
+                          : (fmt == FMT_GEN4 ? smem_bytes_r<FMT_GEN4>(w, kR) : smem_bytes_r<FMT_GEN8>(w, kR));
   return b <= kMaxSmem;
 }
 
@@ -1039,11 +1058,11 @@ llmq_status llmq_debug_lane_sums(llmq_ctx *ctx, const llmq_weight *w, const floa
   int grid = gemv_grid(ctx, a.w);
   int fmt = fmt_of(a.w);
   if (fmt == FMT_BLK4) {
-    lane_sums_kernel<FMT_BLK4><<<grid, kThreads, smem_bytes<FMT_BLK4>(a.w), ctx->stream>>>(a, lanes);
+    lane_sums_kernel<FMT_BLK4><<<grid, kThreads, smem_bytes_r<FMT_BLK4>(a.w, kR), ctx->stream>>>(a, lanes);
   } else if (fmt == FMT_GEN4) {
-    lane_sums_kernel<FMT_GEN4><<<grid, kThreads, smem_bytes<FMT_GEN4>(a.w), ctx->stream>>>(a, lanes);
+    lane_sums_kernel<FMT_GEN4><<<grid, kThreads, smem_bytes_r<FMT_GEN4>(a.w, kR), ctx->stream>>>(a, lanes);
   } else {
-    lane_sums_kernel<FMT_GEN8><<<grid, kThreads, smem_bytes<FMT_GEN8>(a.w), ctx->stream>>>(a, lanes);
+    lane_sums_kernel<FMT_GEN8><<<grid, kThreads, smem_bytes_r<FMT_GEN8>(a.w, kR), ctx->stream>>>(a, lanes);
   }
   CKL();
   return LLMQ_OK;

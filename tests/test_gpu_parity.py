@@ -50,7 +50,7 @@ def dev(torch, a):
 
 
 @pytest.mark.parametrize("fmt", FORMATS)
-@pytest.mark.parametrize("IN,OUT", [(768, 2304), (3072, 768), (768, 70)])
+@pytest.mark.parametrize("IN,OUT", [(768, 2304), (3072, 768), (768, 70), (768, 5000)])
 def test_decode_gemv_bit_exact(torch, ctx, fmt, IN, OUT):
     check_decode_gemv(torch, ctx, fmt, IN, OUT)
 
