@@ -145,6 +145,15 @@ __device__ __forceinline__ float block_lane(const uint8_t *b, const float *x, in
 
 constexpr int RF_THREADS = 256;
 constexpr int RF_TILE_BYTES = 32 * 1024;  // bytes of rows per stage
+constexpr int RF_STAGES = 2;              // stages per CTA (4 stages of 24 KB measured no faster)
+constexpr int RF_MAX_ROWS = 16;           // rows per tile: one per half-warp
+
+// Rows per tile for rows of rb bytes (the copied span is 16-byte rounded
+// at both ends, hence the 32 bytes of slack).
+__host__ __device__ inline int rf_rows(int rb) {
+  const int r = (RF_TILE_BYTES - 32) / rb;
+  return r < 1 ? 1 : (r > RF_MAX_ROWS ? RF_MAX_ROWS : r);
+}
 
 struct RowGemvArgs {
   RowMat w;
@@ -157,20 +166,21 @@ struct RowGemvArgs {
 __device__ __forceinline__ unsigned rf_smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 
 // Row-major float GEMV: CTA tiles of R rows (R * row_bytes <= RF_TILE_BYTES,
-// R <= 16), two shared-memory stages filled by cp.async.bulk.
+// R <= RF_MAX_ROWS), RF_STAGES shared-memory stages filled by
+// cp.async.bulk: thread 0 arms a stage's mbarrier and issues the tile's one
+// contiguous copy; tile it + RF_STAGES - 1 is requested as tile it is summed.
 template <int T>
 __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int cols = a.w.cols, rb = (int)a.w.row_bytes;
-  const int R = min(16, max(1, (RF_TILE_BYTES - 32) / rb));
+  const int R = rf_rows(rb);
   float *xs = (float *)smem;                                         // [cols]
-  unsigned long long *bar = (unsigned long long *)(smem + cols * 4);  // [2]
-  uint8_t *stage[2] = {smem + cols * 4 + 128, smem + cols * 4 + 128 + RF_TILE_BYTES};
+  unsigned long long *bar = (unsigned long long *)(smem + cols * 4);  // [RF_STAGES]
+  uint8_t *stages = smem + cols * 4 + 128;                            // [RF_STAGES][RF_TILE_BYTES]
   const int ntiles = (a.w.rows + R - 1) / R;
   for (int i = threadIdx.x; i < cols; i += RF_THREADS) xs[i] = a.x[i];
   if (threadIdx.x == 0) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rf_smem_u32(&bar[0])));
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rf_smem_u32(&bar[1])));
+    for (int k = 0; k < RF_STAGES; k++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(rf_smem_u32(&bar[k])));
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -186,36 +196,51 @@ __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
                  : "memory");
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            rf_smem_u32(stage[s])),
+            rf_smem_u32(stages + (size_t)s * RF_TILE_BYTES)),
         "l"(a.w.data + lo), "r"(bytes), "r"(rf_smem_u32(&bar[s]))
         : "memory");
   };
+  if (threadIdx.x == 0)
+    for (int k = 0; k < RF_STAGES - 1; k++) {
+      const int tile = blockIdx.x + k * gridDim.x;
+      if (tile < ntiles) issue(tile, k);
+    }
   int it = 0;
-  if (threadIdx.x == 0 && (int)blockIdx.x < ntiles) issue(blockIdx.x, 0);
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, it++) {
-    const int s = it & 1;
-    const int next = tile + gridDim.x;
-    if (threadIdx.x == 0 && next < ntiles) issue(next, s ^ 1);
-    // wait for this tile (phase it / 2 of stage s)
-    {
-      const unsigned par = (unsigned)((it >> 1) & 1);
+    const int s = it % RF_STAGES;
+    const int ahead = tile + (RF_STAGES - 1) * gridDim.x;
+    if (threadIdx.x == 0 && ahead < ntiles) issue(ahead, (it + RF_STAGES - 1) % RF_STAGES);
+    // wait for this tile (phase it / RF_STAGES of stage s); the decision to
+    // give up is taken by the whole CTA, so every thread meets the same barriers
+    auto wait_stage = [&](int k) {
+      const unsigned par = (unsigned)((k / RF_STAGES) & 1);
       unsigned ok = 0;
-      long long t0 = clock64();
-      while (!ok) {
+      const long long t0 = clock64();
+      while (!ok && clock64() - t0 < 4000000000LL)
         asm volatile(
             "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(rf_smem_u32(&bar[s])), "r"(par)
+            : "r"(rf_smem_u32(&bar[k % RF_STAGES])), "r"(par)
             : "memory");
-        if (!ok && clock64() - t0 > 4000000000LL) return;  // a copy never landed: give up (bounded)
-      }
+      return ok != 0;
+    };
+    if (__syncthreads_or(!wait_stage(it))) {
+      // a copy never landed: wait (bounded) for the tiles still in flight, then give up
+      if (threadIdx.x == 0)
+        for (int k = it + 1; k < it + RF_STAGES && tile + (k - it) * gridDim.x < ntiles; k++) wait_stage(k);
+      __syncthreads();
+      return;
     }
     const int r0 = tile * R, n = min(R, a.w.rows - r0);
     const int shift = (int)(((long long)r0 * rb) & 15);
+    const uint8_t *stage = stages + (size_t)s * RF_TILE_BYTES;
     const int L = threadIdx.x & 15, g = threadIdx.x >> 4;
-    for (int rr = g; rr < 16; rr += RF_THREADS / 16) {  // rows of the tile handled by this half-warp
+    // rows of the tile handled by this half-warp: every half-warp runs the
+    // same number of rounds (the shuffles below take the full warp)
+    for (int rr0 = 0; rr0 < R; rr0 += RF_THREADS / 16) {
+      const int rr = rr0 + g;
       const bool live = rr < n;
-      const uint8_t *row = stage[s] + shift + (size_t)(live ? rr : 0) * rb;
+      const uint8_t *row = stage + shift + (size_t)(live ? rr : 0) * rb;
       float acc = 0.0f;
       const int bs = rt_block_size(T), bb = rt_block_bytes(T);
       for (int blk = 0; blk < cols / bs; blk++) acc = block_lane<T>(row + blk * bb, xs + blk * bs, L, acc);
@@ -232,7 +257,7 @@ __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
         a.out[o] = v;
       }
     }
-    __syncthreads();  // the stage is free for the tile after next
+    __syncthreads();  // the stage is free for the tile RF_STAGES - 1 ahead
   }
 }
 

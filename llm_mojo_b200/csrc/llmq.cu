@@ -295,7 +295,7 @@ cudaError_t configure_kernels() {
   if (e == cudaSuccess) e = cudaFuncSetAttribute((const void *)lane_sums_kernel<FMT_GEN8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)mega_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(MkSmem));
-  const int rsm = 4096 * 4 + 128 + 2 * RF_TILE_BYTES;
+  const int rsm = 4096 * 4 + 128 + RF_STAGES * RF_TILE_BYTES;
   auto rs = [&](const void *k) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, rsm);
   };
@@ -550,10 +550,10 @@ namespace {
 template <int T>
 cudaError_t launch_row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
   const int rb = (int)a.w.row_bytes;
-  const int R = std::min(16, std::max(1, (RF_TILE_BYTES - 32) / rb));
+  const int R = rf_rows(rb);
   const int ntiles = (a.w.rows + R - 1) / R;
   const int grid = std::min(ntiles, ctx->num_sms * 2);
-  const int sm = a.w.cols * 4 + 128 + 2 * RF_TILE_BYTES;
+  const int sm = a.w.cols * 4 + 128 + RF_STAGES * RF_TILE_BYTES;
   row_gemv_kernel<T><<<grid, RF_THREADS, sm, ctx->stream>>>(a);
   return cudaGetLastError();
 }
