@@ -279,7 +279,11 @@ __global__ void __launch_bounds__(256) affine_float_gemv_kernel(AffFloatArgs a) 
   for (int i = threadIdx.x; i < cols; i += blockDim.x) xsh[i] = a.x[i];
   __syncthreads();
   const int L = threadIdx.x & 15;
-  for (int row = blockIdx.x * 16 + (threadIdx.x >> 4); row < a.w.rows; row += gridDim.x * 16) {
+  // the loop bound is the CTA's: every half-warp runs every round, so the
+  // full-warp shuffles below always have the whole warp
+  for (int base = blockIdx.x * 16; base < a.w.rows; base += gridDim.x * 16) {
+    const bool live = base + (threadIdx.x >> 4) < a.w.rows;
+    const int row = live ? base + (threadIdx.x >> 4) : a.w.rows - 1;
     const uint8_t *p = a.w.codes + (size_t)row * cols * BITS / 8;
     float acc = 0.0f;
     for (int g = 0; g < gpr; g++) {
@@ -306,7 +310,7 @@ __global__ void __launch_bounds__(256) affine_float_gemv_kernel(AffFloatArgs a) 
     acc = acc + __shfl_xor_sync(0xffffffffu, acc, 4);
     acc = acc + __shfl_xor_sync(0xffffffffu, acc, 2);
     acc = acc + __shfl_xor_sync(0xffffffffu, acc, 1);
-    if (L == 0) {
+    if (live && L == 0) {
       float v = acc;
       if (a.epi & EPI_BIAS) v += a.bias[row];
       if (a.epi & EPI_GELU) v = gelu(v);
@@ -425,7 +429,10 @@ __global__ void __launch_bounds__(256) gguf_head_i16_kernel(RowMat w, const floa
   for (int i = threadIdx.x; i < cols; i += blockDim.x) xq[i] = (int16_t)round_away(h[i] * inv);
   __syncthreads();
   const int L = threadIdx.x & 15;
-  for (int row = blockIdx.x * 16 + (threadIdx.x >> 4); row < w.rows; row += gridDim.x * 16) {
+  // CTA-uniform rounds: the full-warp shuffles below always have the whole warp
+  for (int base = blockIdx.x * 16; base < w.rows; base += gridDim.x * 16) {
+    const bool live = base + (threadIdx.x >> 4) < w.rows;
+    const int row = live ? base + (threadIdx.x >> 4) : w.rows - 1;
     const uint8_t *p = w.data + (size_t)row * w.row_bytes;
     float accf = 0.0f;
     if (T == RT_Q8_0) {
@@ -460,7 +467,7 @@ __global__ void __launch_bounds__(256) gguf_head_i16_kernel(RowMat w, const floa
     accf = accf + __shfl_xor_sync(0xffffffffu, accf, 4);
     accf = accf + __shfl_xor_sync(0xffffffffu, accf, 2);
     accf = accf + __shfl_xor_sync(0xffffffffu, accf, 1);
-    if (L == 0) logits[row] = accf * s;
+    if (live && L == 0) logits[row] = accf * s;
   }
 }
 
