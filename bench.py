@@ -590,6 +590,8 @@ def main():
     ap.add_argument("--sweep-only", default=None, metavar="FORMAT[:OUTxIN]",
                     help="sweep workload: time only this format (e.g. int8-ch-a16), optionally at one shape "
                          "(e.g. int8-ch-a16:50257x768), for profiling captures")
+    ap.add_argument("--mode", default=None, choices=["cluster", "persistent", "graph", "eager"],
+                    help="decode mode of the config-0 model (default: the library's default for its formats)")
     ap.add_argument("--profile", action="store_true",
                     help="after the timed region, run one generation with the persistent kernel's per-phase "
                          "timers and print them (microseconds per token) to stderr")
@@ -627,6 +629,8 @@ def main():
     stream = torch.cuda.Stream(device=local)
     ctx.set_stream(stream.cuda_stream)
     model = Model(ctx, synth.gpt2_random_init(0))
+    if args.mode:
+        model.set_mode(args.mode)
     prompt_dev = torch.tensor(PROMPT, dtype=torch.int32, device="cuda")
     ids_dev = torch.zeros(STEPS_PER_GEN, dtype=torch.int32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -680,7 +684,7 @@ def main():
         for i, d in enumerate(model.profile_read()):
             steps = max(1, d.pop("steps"))
             us = {k: v / steps / mhz for k, v in d.items()}
-            tot = sum(v for k, v in us.items() if k != "ring waits")
+            tot = sum(v for k, v in us.items() if k != "ring waits" and not k.startswith("in: "))
             print(f"[profile] CTA {'0' if i == 0 else 'grid/2'}: {tot:.1f} us/token at {mhz:.0f} MHz: " +
                   ", ".join(f"{k} {v:.2f}" for k, v in us.items()), file=sys.stderr)
         model.profile(False)

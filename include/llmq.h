@@ -242,13 +242,19 @@ void *llmq_stream(const llmq_ctx *ctx);
 /* How decode steps run (replacing the reference's per-token thread team,
  * team.mojo:36-82, and gpt2t.mojo:350-447's single parallel region):
  * LLMQ_MODE_PERSISTENT (default when the formats allow it: int4-g32 A16
- * layers, per-channel int8 A16 head, QuantKV[8]) runs a whole generation as
- * one persistent kernel; LLMQ_MODE_GRAPH replays each step as a captured
- * CUDA graph of one-token kernels; LLMQ_MODE_EAGER launches those kernels
- * one by one. Returns LLMQ_ERR_UNSUPPORTED if the model cannot run `mode`. */
+ * layers, a per-channel int8 A16 head, QuantKV[8] or IntAttnKV) runs a whole
+ * generation as one persistent kernel over all SMs that exchange activations
+ * through global memory; LLMQ_MODE_CLUSTER (768-wide, 12-head models with
+ * QuantKV[8]) runs it as one launch of 16-CTA thread-block clusters, the
+ * layers inside one cluster exchanging through distributed shared memory;
+ * LLMQ_MODE_GRAPH replays each step as a captured CUDA graph of one-token
+ * kernels; LLMQ_MODE_EAGER launches those kernels one by one. All give the
+ * same ids and logits. Returns LLMQ_ERR_UNSUPPORTED if the model cannot run
+ * `mode`. */
 #define LLMQ_MODE_EAGER 0
 #define LLMQ_MODE_GRAPH 1
 #define LLMQ_MODE_PERSISTENT 2
+#define LLMQ_MODE_CLUSTER 3
 llmq_status llmq_model_set_mode(llmq_model *m, int mode);
 int llmq_model_mode(const llmq_model *m);
 

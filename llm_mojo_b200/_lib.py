@@ -16,7 +16,7 @@ LIB_PATH = os.path.join(HERE, "libllmq.so")
 OK, ERR_INVALID, ERR_CUDA, ERR_NOMEM, ERR_TIMEOUT, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
 BIAS, GELU, RESID = 1, 2, 4
 KV_QUANT8, KV_INTATTN, KV_F32, KV_BF16 = 1, 2, 3, 4
-MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT = 0, 1, 2
+MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT, MODE_CLUSTER = 0, 1, 2, 3
 PREFILL_AUTO, PREFILL_CUDA_CORE, PREFILL_TCGEN05 = 0, 1, 2
 
 

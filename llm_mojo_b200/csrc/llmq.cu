@@ -14,6 +14,7 @@
 #include "gemv_a16.cuh"
 #include "gemv_float.cuh"
 #include "mega.cuh"
+#include "cluster.cuh"
 #include "prefill_a16.cuh"
 #include "sample.cuh"
 #include "tc_gemm.cuh"
@@ -101,6 +102,15 @@ struct llmq_model {
   unsigned long long *mega_ll = nullptr;
   int *mega_err = nullptr;
   unsigned mega_flag = 1;
+  // cluster decode kernel (cluster.cuh); shares mega_err
+  bool cd_ok = false;
+  int cd_grid = 0, cd_nhcta = 0;
+  uint8_t *cd_lstream = nullptr, *cd_hstream = nullptr;
+  long long *cd_lbase = nullptr, *cd_lbytes = nullptr, *cd_hbase = nullptr;
+  CdChunk *cd_lchunks = nullptr;
+  int *cd_lnch = nullptr;
+  unsigned long long *cd_ll = nullptr;
+  unsigned cd_flag = 1;
   bool float_only = false;  // float-activation formats: the generic eager decode
   std::vector<llmq_weight *> owned;  // weights a loader created for this model
   long long *prof = nullptr;  // [2][MK_PROF] when profiling
@@ -1323,8 +1333,215 @@ llmq_status mega_setup(llmq_model *m) {
   return LLMQ_OK;
 }
 
+// Builds the cluster decode kernel's streams (cluster.cuh) when the model's
+// formats are the ones it runs (those of the persistent kernel with the
+// QuantKV[8] cache) and the device holds at least two 16-CTA clusters:
+//   layer rank r (cluster 0): per layer, [q, k, v rows of head r (r < 12)],
+//   PROJ rows [48r, 48r + 48), FC rows [192r, 192r + 192) in three chunks,
+//   FCPROJ rows [48r, 48r + 48) in four chunks of three 256-column blocks;
+//   head CTA j (clusters 1..): head rows [V j / H, V (j + 1) / H) in 32-row
+//   chunks. Chunk layouts are in cluster.cuh. Returns LLMQ_OK without
+//   enabling the kernel otherwise.
+llmq_status cd_setup(llmq_model *m) {
+  llmq_ctx *ctx = m->ctx;
+  m->cd_ok = false;
+  if (!m->mega_ok || m->kv->kind != LLMQ_KV_QUANT8 || m->C != 768 || m->n_head != 12) return LLMQ_OK;
+  const size_t smem = cd_smem_bytes();
+  CK(cudaFuncSetAttribute((const void *)cluster_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  CK(cudaFuncSetAttribute((const void *)cluster_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CD_CLUSTER;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeCooperative;
+  at[1].val.cooperative = 1;
+  cfg.gridDim = dim3(CD_CLUSTER * 2);
+  cfg.blockDim = dim3(CD_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  int ncl = 0;
+  if (cudaOccupancyMaxActiveClusters(&ncl, (const void *)cluster_decode_kernel, &cfg) != cudaSuccess || ncl < 2) {
+    cudaGetLastError();
+    return LLMQ_OK;
+  }
+  const int C = m->C, L = m->n_layer, V = m->V;
+  const int grid = ncl * CD_CLUSTER, nh = grid - CD_CLUSTER;
+  // the weights as stored, on the host
+  auto fetch = [&](const llmq_weight *w, std::vector<uint8_t> &codes, std::vector<uint16_t> &sc,
+                   std::vector<uint8_t> &zp) -> cudaError_t {
+    const size_t gpr = (size_t)w->cols / w->group;
+    codes.resize((size_t)w->rows * w->cols * w->bits / 8);
+    sc.resize((size_t)w->rows * gpr);
+    zp.resize((size_t)w->rows * gpr);
+    cudaError_t e = cudaMemcpy(codes.data(), w->codes, codes.size(), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(sc.data(), w->scale, sc.size() * 2, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(zp.data(), w->zp, zp.size(), cudaMemcpyDeviceToHost);
+    return e;
+  };
+  // per-layer chunk templates of each rank
+  std::vector<CdChunk> tmpl((size_t)CD_CLUSTER * CD_MAX_CHUNKS);
+  std::vector<int> nch(CD_CLUSTER);
+  std::vector<long long> lbytes(CD_CLUSTER), lbase(CD_CLUSTER);
+  long long ltotal = 0;
+  for (int r = 0; r < CD_CLUSTER; r++) {
+    int k = 0, off = 0;
+    auto add = [&](int kind, int r0, int n, int b0, int nb) {
+      CdChunk c{};
+      c.kind = kind;
+      c.r0 = r0;
+      c.n = n;
+      c.rp = (n + 7) & ~7;
+      c.b0 = b0;
+      c.nb = nb;
+      c.off = off;
+      c.scale_off = nb * c.rp * 128;
+      c.zp_off = c.scale_off + nb * c.rp * 16;
+      c.bytes = c.zp_off + nb * c.rp * 8;
+      off += c.bytes;
+      tmpl[(size_t)r * CD_MAX_CHUNKS + k++] = c;
+    };
+    if (r < m->n_head)
+      for (int c = 0; c < 3; c++) add(CD_QKV, c * C + 64 * r, 64, 0, 3);
+    add(CD_PROJ, 48 * r, 48, 0, 3);
+    for (int c = 0; c < 3; c++) add(CD_FC, 192 * r + 64 * c, 64, 0, 3);
+    for (int c = 0; c < 4; c++) add(CD_FCPROJ, 48 * r, 48, 3 * c, 3);
+    nch[r] = k;
+    lbytes[r] = off;
+    lbase[r] = ltotal;
+    ltotal += (long long)off * L;
+  }
+  for (const CdChunk &c : tmpl)
+    if (c.bytes > CD_SLOT) return fail(ctx, LLMQ_ERR_INVALID, "cluster decode: a chunk exceeds its ring slot");
+  std::vector<uint8_t> lh((size_t)ltotal, 0);
+  std::vector<uint8_t> codes, zp;
+  std::vector<uint16_t> sc;
+  for (int l = 0; l < L; l++)
+    for (int kind = 0; kind < 4; kind++) {
+      const llmq_weight *w = m->mats[4 * l + kind];
+      CK(fetch(w, codes, sc, zp));
+      const long long rb = (long long)w->cols / 2, gpr = w->cols / w->group;
+      for (int r = 0; r < CD_CLUSTER; r++)
+        for (int k = 0; k < nch[r]; k++) {
+          const CdChunk &c = tmpl[(size_t)r * CD_MAX_CHUNKS + k];
+          if (c.kind != kind) continue;
+          uint8_t *dst = lh.data() + lbase[r] + (long long)l * lbytes[r] + c.off;
+          for (int bb = 0; bb < c.nb; bb++)
+            for (int i = 0; i < c.n; i++) {
+              const long long row = c.r0 + i;
+              const int b = c.b0 + bb;
+              for (int h = 0; h < 2; h++)
+                for (int q = 0; q < 4; q++)
+                  for (int j = 0; j < 4; j++)
+                    std::memcpy(dst + ((size_t)(bb * 2 + h) * c.rp + i) * 64 + q * 16 + j * 4,
+                                codes.data() + row * rb + b * 128 + (4 * h + j) * 16 + q * 4, 4);
+              for (int g = 0; g < 8; g++) {
+                std::memcpy(dst + c.scale_off + ((size_t)(bb * c.rp + i) * 8 + g) * 2, &sc[row * gpr + b * 8 + g], 2);
+                dst[c.zp_off + (size_t)(bb * c.rp + i) * 8 + g] = zp[row * gpr + b * 8 + g];
+              }
+            }
+        }
+    }
+  // head CTAs
+  const llmq_weight *hd = m->head;
+  CK(fetch(hd, codes, sc, zp));
+  std::vector<long long> hbase(nh);
+  long long htotal = 0;
+  for (int j = 0; j < nh; j++) {
+    hbase[j] = htotal;
+    const int r0 = (int)((long long)V * j / nh), r1 = (int)((long long)V * (j + 1) / nh);
+    htotal += (long long)((r1 - r0 + CD_HROWS - 1) / CD_HROWS) * CD_HSLOT;
+  }
+  std::vector<uint8_t> hh((size_t)htotal, 0);
+  for (int j = 0; j < nh; j++) {
+    const int r0 = (int)((long long)V * j / nh), r1 = (int)((long long)V * (j + 1) / nh);
+    for (int row = r0; row < r1; row++) {
+      const int ck = (row - r0) / CD_HROWS, r = (row - r0) % CD_HROWS;
+      uint8_t *dst = hh.data() + hbase[j] + (long long)ck * CD_HSLOT;
+      for (int c = 0; c < 24; c++)
+        for (int q = 0; q < 4; q++)
+          std::memcpy(dst + ((size_t)(c * 32 + r) * 4 + q) * 8, codes.data() + (size_t)row * C + c * 32 + q * 8, 8);
+      std::memcpy(dst + CD_HROWS * 768 + r * 2, &sc[row], 2);
+      dst[CD_HROWS * 768 + CD_HROWS * 2 + r] = zp[row];
+    }
+  }
+  CK(cudaMalloc(&m->cd_lstream, lh.size()));
+  CK(cudaMemcpy(m->cd_lstream, lh.data(), lh.size(), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_hstream, hh.size()));
+  CK(cudaMemcpy(m->cd_hstream, hh.data(), hh.size(), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_lbase, sizeof(long long) * CD_CLUSTER));
+  CK(cudaMemcpy(m->cd_lbase, lbase.data(), sizeof(long long) * CD_CLUSTER, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_lbytes, sizeof(long long) * CD_CLUSTER));
+  CK(cudaMemcpy(m->cd_lbytes, lbytes.data(), sizeof(long long) * CD_CLUSTER, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_lnch, sizeof(int) * CD_CLUSTER));
+  CK(cudaMemcpy(m->cd_lnch, nch.data(), sizeof(int) * CD_CLUSTER, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_lchunks, sizeof(CdChunk) * tmpl.size()));
+  CK(cudaMemcpy(m->cd_lchunks, tmpl.data(), sizeof(CdChunk) * tmpl.size(), cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_hbase, sizeof(long long) * nh));
+  CK(cudaMemcpy(m->cd_hbase, hbase.data(), sizeof(long long) * nh, cudaMemcpyHostToDevice));
+  CK(cudaMalloc(&m->cd_ll, sizeof(unsigned long long) * (C + 2 * nh)));
+  CK(cudaMemset(m->cd_ll, 0, sizeof(unsigned long long) * (C + 2 * nh)));
+  m->cd_grid = grid;
+  m->cd_nhcta = nh;
+  m->cd_flag = 1;
+  m->cd_ok = true;  // selectable; the persistent kernel stays the default (it is faster on B200)
+  return LLMQ_OK;
+}
+
+// One cooperative launch of the cluster decode kernel: `steps` greedy steps
+// from *first_token at pos0.
+llmq_status run_cluster(llmq_model *m, const int *first_token, int pos0, int steps, int *ids, float *logits) {
+  llmq_ctx *ctx = m->ctx;
+  CdArgs a{};
+  a.lstream = m->cd_lstream;
+  a.lbase = m->cd_lbase;
+  a.lchunks = m->cd_lchunks;
+  a.lnch = m->cd_lnch;
+  a.lbytes = m->cd_lbytes;
+  a.hstream = m->cd_hstream;
+  a.hbase = m->cd_hbase;
+  a.n_hcta = m->cd_nhcta;
+  a.n_layer = m->n_layer;
+  a.C = m->C;
+  a.V = m->V;
+  a.n_head = m->n_head;
+  a.small = m->small;
+  a.head = m->head->view();
+  a.kv = m->kv->v8;
+  a.ll = m->cd_ll;
+  a.logits = logits;
+  a.ids = ids;
+  a.first_token = first_token;
+  a.pos0 = pos0;
+  a.steps = steps;
+  a.flag0 = m->cd_flag;
+  a.err = m->mega_err;
+  a.timeout_cycles = 4000000000LL;  // ~2 s at 2 GHz per wait
+  a.prof = m->prof;
+  m->cd_flag += (unsigned)steps;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CD_CLUSTER;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeCooperative;
+  at[1].val.cooperative = 1;
+  cfg.gridDim = dim3(m->cd_grid);
+  cfg.blockDim = dim3(CD_THREADS);
+  cfg.dynamicSmemBytes = cd_smem_bytes();
+  cfg.stream = ctx->stream;
+  cfg.attrs = at;
+  cfg.numAttrs = 2;
+  CK(cudaLaunchKernelEx(&cfg, cluster_decode_kernel, a));
+  return LLMQ_OK;
+}
+
 // One cooperative launch: `steps` greedy steps from *first_token at pos0.
 llmq_status run_mega(llmq_model *m, const int *first_token, int pos0, int steps, int *ids, float *logits) {
+  if (m->mode == LLMQ_MODE_CLUSTER && m->cd_ok) return run_cluster(m, first_token, pos0, steps, ids, logits);
   llmq_ctx *ctx = m->ctx;
   MegaArgs a{};
   a.stream = m->mega_stream;
@@ -1547,7 +1764,7 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
     llmq_model_free(m);
     return fail(ctx, LLMQ_ERR_CUDA, std::string("model alloc: ") + cudaGetErrorString(e));
   }
-  if ((st = mega_setup(m)) != LLMQ_OK) {
+  if ((st = mega_setup(m)) != LLMQ_OK || (st = cd_setup(m)) != LLMQ_OK) {
     llmq_model_free(m);
     return st;
   }
@@ -1575,6 +1792,10 @@ llmq_status llmq_model_free(llmq_model *m) {
   if (m->mega_chunks) cudaFree(m->mega_chunks);
   if (m->mega_ll) cudaFree(m->mega_ll);
   if (m->mega_err) cudaFree(m->mega_err);
+  void *cds[] = {m->cd_lstream, m->cd_hstream, m->cd_lbase, m->cd_lbytes, m->cd_hbase, m->cd_lchunks, m->cd_lnch,
+                 m->cd_ll};
+  for (void *p : cds)
+    if (p) cudaFree(p);
   if (m->prof) cudaFree(m->prof);
   for (llmq_weight *w : m->owned) llmq_weight_free(w);
   delete m;
@@ -1583,11 +1804,15 @@ llmq_status llmq_model_free(llmq_model *m) {
 
 llmq_status llmq_model_set_mode(llmq_model *m, int mode) {
   if (!m) return LLMQ_ERR_INVALID;
-  if (mode != LLMQ_MODE_EAGER && mode != LLMQ_MODE_GRAPH && mode != LLMQ_MODE_PERSISTENT)
+  if (mode != LLMQ_MODE_EAGER && mode != LLMQ_MODE_GRAPH && mode != LLMQ_MODE_PERSISTENT && mode != LLMQ_MODE_CLUSTER)
     return fail(m->ctx, LLMQ_ERR_INVALID, "unknown mode");
   if (mode == LLMQ_MODE_PERSISTENT && !m->mega_ok)
     return fail(m->ctx, LLMQ_ERR_UNSUPPORTED, "the persistent decode kernel runs int4-g32 A16 layers, a per-channel "
-                                              "int8 A16 head and the QuantKV[8] cache");
+                                              "int8 A16 head and the QuantKV[8] or IntAttnKV cache");
+  if (mode == LLMQ_MODE_CLUSTER && !m->cd_ok)
+    return fail(m->ctx, LLMQ_ERR_UNSUPPORTED, "the cluster decode kernel runs int4-g32 A16 layers, a per-channel int8 "
+                                              "A16 head and the QuantKV[8] cache of a 768-wide, 12-head model, on a "
+                                              "device with room for two 16-CTA clusters");
   m->mode = mode;
   return LLMQ_OK;
 }
@@ -1749,12 +1974,17 @@ static llmq_status float_generation(llmq_model *m, int T, int pos0, int steps, c
 // still writes the logits, the draw overwrites the id and the next token. In
 // the persistent mode the kernel then runs one token per launch (it writes
 // the logits, the draw writes the token the next launch embeds).
+// Whether decode steps run as one launch of a persistent kernel per generation.
+static bool persistent_mode(const llmq_model *m) {
+  return (m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok) || (m->mode == LLMQ_MODE_CLUSTER && m->cd_ok);
+}
+
 static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, bool want_logits,
                                   const SampleSpec *sp = nullptr) {
   llmq_ctx *ctx = m->ctx;
   cudaStream_t s = ctx->stream;
   if (m->float_only) return float_generation(m, T, pos0, steps, sp);
-  if (sp && m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok) {
+  if (sp && persistent_mode(m)) {
     llmq_status st;
     int pos = pos0, i = 0;
     if (T > 1) {
@@ -1773,7 +2003,7 @@ static llmq_status run_generation(llmq_model *m, int T, int pos0, int steps, boo
     }
     return LLMQ_OK;
   }
-  const bool pers = m->mode == LLMQ_MODE_PERSISTENT && m->mega_ok && !sp;
+  const bool pers = persistent_mode(m) && !sp;
   const SampleOut so{nullptr, nullptr, &m->state->token, &m->state->step, m->ids};
   auto draw = [&]() -> llmq_status {
     return sp ? enqueue_sample(ctx, m->logits, m->V, sp->temperature, sp->k, sp->rng, so, nullptr, s) : LLMQ_OK;

@@ -10,7 +10,7 @@ import ctypes as C
 import numpy as np
 
 from . import synth
-from ._lib import KV_INTATTN, KV_QUANT8, MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT, check, lib
+from ._lib import KV_INTATTN, KV_QUANT8, MODE_CLUSTER, MODE_EAGER, MODE_GRAPH, MODE_PERSISTENT, check, lib
 from .tensor import Context, QuantMatrix, parse_dtype
 
 # HEAD8_A16 (gpt2t.mojo:1231-1235): int8 per vocabulary row, integer path.
@@ -45,11 +45,13 @@ class Model:
         """Model.weight_bytes (gpt2t.mojo:312-319)."""
         return self.head.nbytes() + sum(m.nbytes() for m in self.mats) + self.small.size * 4
 
-    MODES = {"eager": MODE_EAGER, "graph": MODE_GRAPH, "persistent": MODE_PERSISTENT}
+    MODES = {"eager": MODE_EAGER, "graph": MODE_GRAPH, "persistent": MODE_PERSISTENT, "cluster": MODE_CLUSTER}
 
     def set_mode(self, mode: str):
-        """'persistent' (one kernel per generation), 'graph' (a CUDA graph per
-        decode step) or 'eager' (one launch per operation)."""
+        """'cluster' (one launch of 16-CTA clusters per generation, the layers
+        in one cluster), 'persistent' (one kernel over all SMs per
+        generation), 'graph' (a CUDA graph per decode step) or 'eager' (one
+        launch per operation)."""
         check(lib().llmq_model_set_mode(self.h, self.MODES[mode]), self.ctx.h)
 
     def mode(self) -> str:
@@ -64,11 +66,23 @@ class Model:
         """Per-phase cycle counters of the persistent kernel (--profile)."""
         check(lib().llmq_model_profile(self.ctx.h, self.h, int(enable)), self.ctx.h)
 
+    # the cluster kernel's counters: layer rank 0, then head CTA 0
+    CLUSTER_PROFILE_NAMES = (("embed", "ln1 + quantize", "qkv", "attention", "att all-gather", "proj",
+                              "xmid all-gather", "ln2 + quantize", "fc", "fc all-gather", "fcproj",
+                              "xout all-gather", "argmax wait", "ring waits", "steps", "in: gemv", "in: ln/quantize",
+                              "in: push", "in: attention"),
+                             ("hidden-state wait", "ln_f + quantize", "head rows", "ring waits", "steps"))
+
     def profile_read(self, reset: bool = True) -> list[dict]:
-        """Counters of CTA 0 and CTA grid/2: {category: cycles}."""
+        """Counters of two CTAs, {category: cycles}: CTA 0 and CTA grid/2 of
+        the persistent kernel, or layer rank 0 and head CTA 0 of the cluster
+        kernel."""
         n = len(self.PROFILE_NAMES) + 1
         buf = (C.c_longlong * (2 * n))()
         check(lib().llmq_model_profile_read(self.ctx.h, self.h, buf, 2 * n, int(reset)), self.ctx.h)
+        if self.mode() == "cluster":
+            return [dict(zip(names, buf[n * i:n * i + len(names)]))
+                    for i, names in enumerate(self.CLUSTER_PROFILE_NAMES)]
         return [dict(zip(self.PROFILE_NAMES, buf[n * i:n * i + n - 1])) for i in range(2)]
 
     def forward(self, tokens, pos0: int, logits=None) -> int:

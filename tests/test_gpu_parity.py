@@ -262,9 +262,9 @@ def test_forward_all_bit_exact(torch, gpu_model, oracle_a16, golden):
     assert np.array_equal(logits.cpu().numpy().view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("mode", ["eager", "graph", "persistent"])
+@pytest.mark.parametrize("mode", ["eager", "graph", "persistent", "cluster"])
 def test_decode_modes_agree_with_oracle(gpu_model, oracle_a16, mode):
-    """The three ways a decode step runs give the oracle's ids (and the
+    """The four ways a decode step runs give the oracle's ids (and the
     persistent kernel is the default for these formats)."""
     assert gpu_model.mode() == "persistent"
     want = oracle_a16.generate([50256], 24)
@@ -274,3 +274,29 @@ def test_decode_modes_agree_with_oracle(gpu_model, oracle_a16, mode):
     finally:
         gpu_model.set_mode("persistent")
     assert list(got) == list(want)
+
+
+@pytest.mark.parametrize("mode", ["persistent", "cluster"])
+def test_decode_logits_every_step_bit_exact(torch, gpu_model, oracle_a16, golden, mode):
+    """Logits of every decode step, not only the greedy ids (which settle on
+    a fixed point after a few tokens of a random-init model): 40 steps after
+    the 24-token prompt, one launch per step, each step's logits equal to the
+    oracle's bit for bit."""
+    prompt = list(golden["prompt24"])
+    logits = torch.zeros(50257, dtype=torch.float32, device="cuda")
+    gpu_model.set_mode(mode)
+    try:
+        am = gpu_model.forward(prompt, 0, logits)
+        want = oracle_a16.forward(prompt, 0)
+        tok = int(np.argmax(want))
+        assert am == tok
+        for i in range(40):
+            pos = len(prompt) + i
+            am = gpu_model.forward([tok], pos, logits)
+            want = oracle_a16.forward([tok], pos)
+            got = logits.cpu().numpy()
+            assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), (i, float(np.abs(got - want).max()))
+            tok = int(np.argmax(want))
+            assert am == tok
+    finally:
+        gpu_model.set_mode("persistent")
