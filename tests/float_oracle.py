@@ -8,6 +8,13 @@ import numpy as np
 from oracle import oracle as O
 
 DT = {"f32": 0, "bf16": 2}
+_PREP = {}  # (format, id(array), kind) -> converted weights, reused across calls
+
+
+def _prep(key, make):
+    if key not in _PREP:
+        _PREP[key] = make()
+    return _PREP[key]
 
 
 def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
@@ -30,15 +37,22 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
     def wdata(a):
         return np.ascontiguousarray(a, dtype=np.float32) if fmt == "f32" else bf16(a)
 
+    def wdata_cached(a):
+        return _prep((fmt, id(a), "w"), lambda: (a, wdata(a)))[1]
+
+    def q_cached(a, t, transpose):
+        return _prep((t, id(a), transpose), lambda: (a, G.quantize(np.ascontiguousarray(a.T if transpose else a,
+                                                                                       dtype=np.float32), t)))[1]
+
     wte = tensors["wte.weight"]
     dt = DT.get(fmt, 0)
     if fmt == "gguf-q4_k":
-        hb = G.quantize(wte, G.Q6_K)
+        hb = q_cached(wte, G.Q6_K, False)
         emb = np.zeros((T, Cn), np.float32)
         for i, tok in enumerate(tokens):
             O.lib().oq_gguf_dequant_row(G.Q6_K, O.ptr(np.ascontiguousarray(hb[tok])), Cn, O.ptr(emb[i]))
     else:
-        wd = wdata(wte)
+        wd = wdata_cached(wte)
         emb = (wd.astype(np.float32) if fmt == "f32" else (wd.astype(np.uint32) << 16).view(np.float32))[tokens]
     x = (emb + wpe[:T]).astype(np.float32)
     kv8 = O.lib().oq_qkv8_new(n_layer, 1024, NH, HS) if fmt == "gguf-q4_k" else None
@@ -47,12 +61,12 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
         Tn, IN = xin.shape
         out = resid.copy() if resid is not None else np.zeros((Tn, OUT), np.float32)
         if fmt == "gguf-q4_k":
-            blocks = G.quantize(np.ascontiguousarray(w.T), G.Q4_K)
+            blocks = q_cached(w, G.Q4_K, True)
             O.lib().oq_gguf_matmul_rows(G.Q4_K, O.ptr(blocks), G.row_bytes(G.Q4_K, IN), O.ptr(xin),
                                         O.ptr(np.ascontiguousarray(b)), O.ptr(out), Tn, IN, OUT,
                                         int(resid is not None), int(gelu))
         else:
-            O.lib().oq_dense_mm(dt, O.ptr(wdata(w)), O.ptr(xin), O.ptr(np.ascontiguousarray(b)), O.ptr(out), Tn, IN,
+            O.lib().oq_dense_mm(dt, O.ptr(wdata_cached(w)), O.ptr(xin), O.ptr(np.ascontiguousarray(b)), O.ptr(out), Tn, IN,
                                 OUT, int(resid is not None), int(gelu))
         return out
 
@@ -87,5 +101,5 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
             O.lib().oq_gguf_head_i16(G.Q6_K, O.ptr(hb), V, Cn, O.ptr(np.ascontiguousarray(xn[t])), O.ptr(logits[t]))
         O.lib().oq_qkv8_free(kv8)
     else:
-        O.lib().oq_dense_head_rows(dt, O.ptr(wdata(wte)), O.ptr(xn), O.ptr(logits), T, V, Cn)
+        O.lib().oq_dense_head_rows(dt, O.ptr(wdata_cached(wte)), O.ptr(xn), O.ptr(logits), T, V, Cn)
     return logits

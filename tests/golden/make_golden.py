@@ -50,9 +50,48 @@ def load_reference(ref_root: str, tmp: str, tensors: dict):
     return mod
 
 
-def configure(ref, quant=None, quant_head=None, act16=False, kv=None):
+def configure(ref, quant=None, quant_head=None, act16=False, kv=None, gguf_path=None):
     ref.QUANT, ref.QUANT_HEAD, ref.ACT16, ref.KV = quant, quant_head, act16, kv
+    if gguf_path is None:
+        ref.GGUF = None
+    else:
+        from gguf import GGUFReader
+
+        ref.GGUF = GGUFReader(gguf_path)
     ref._cache.clear()
+
+
+def bf16_weights(t: dict) -> dict:
+    """The seed-0 weights with the matrices gpt2t's bf16 format stores as
+    bfloat16 (the four per-layer matrices and wte) rounded to bfloat16, as
+    DenseMatrix[bf16] holds them; the small tensors stay float32."""
+    t = dict(t)
+    for name in list(t):
+        if name == "wte.weight" or any(name.endswith(m) for m in synth.MAT_NAMES):
+            b = np.ascontiguousarray(t[name], dtype=np.float32).view(np.uint32).astype(np.uint64)
+            b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16
+            t[name] = b.astype(np.uint32).view(np.float32)
+    return t
+
+
+def model_goldens(ref, out: dict, tag: str, prompt) -> None:
+    """Logits after [EOT], after the 24-token prompt, at all positions of its
+    first 16 tokens, and 8 greedy ids from [EOT]: top ids / values and the
+    largest |logit| (the tolerance's scale)."""
+    lg = ref.forward([synth.EOT]).astype(np.float32)
+    out[f"{tag}_eot_top_ids"], out[f"{tag}_eot_top_vals"] = topk(lg)
+    out[f"{tag}_eot_max"] = np.float32(np.abs(lg).max())
+    toks = [synth.EOT]
+    for _ in range(8):
+        toks.append(int(np.argmax(ref.forward(toks))))
+    out[f"{tag}_greedy8"] = np.array(toks[1:], dtype=np.int32)
+    lg = ref.forward(list(prompt)).astype(np.float32)
+    out[f"{tag}_p24_top_ids"], out[f"{tag}_p24_top_vals"] = topk(lg)
+    out[f"{tag}_p24_max"] = np.float32(np.abs(lg).max())
+    allp = ref.forward(list(prompt[:16]), all_positions=True).astype(np.float32)
+    out[f"{tag}_all16_top_ids"] = np.stack([topk(r, 8)[0] for r in allp])
+    out[f"{tag}_all16_top_vals"] = np.stack([topk(r, 8)[1] for r in allp])
+    out[f"{tag}_all16_max"] = np.float32(np.abs(allp).max())
 
 
 def topk(logits, k=32):
@@ -101,23 +140,30 @@ def main(ref_root: str):
         for tag, cfg in [("f32", {}),
                          ("a16", dict(quant=(4, 32, False), quant_head=(8, 0, False), act16=True, kv="int8"))]:
             configure(ref, **cfg)
-            lg = ref.forward([synth.EOT]).astype(np.float32)
-            out[f"{tag}_eot_top_ids"], out[f"{tag}_eot_top_vals"] = topk(lg)
-            out[f"{tag}_eot_max"] = np.float32(np.abs(lg).max())
-            toks = [synth.EOT]
-            for _ in range(8):
-                toks.append(int(np.argmax(ref.forward(toks))))
-            out[f"{tag}_greedy8"] = np.array(toks[1:], dtype=np.int32)
-            lg = ref.forward(list(prompt)).astype(np.float32)
-            out[f"{tag}_p24_top_ids"], out[f"{tag}_p24_top_vals"] = topk(lg)
-            out[f"{tag}_p24_max"] = np.float32(np.abs(lg).max())
-            allp = ref.forward(list(prompt[:16]), all_positions=True).astype(np.float32)
-            out[f"{tag}_all16_top_ids"] = np.stack([topk(r, 8)[0] for r in allp])
-            out[f"{tag}_all16_top_vals"] = np.stack([topk(r, 8)[1] for r in allp])
-            out[f"{tag}_all16_max"] = np.float32(np.abs(allp).max())
-        np.savez_compressed(os.path.join(HERE, "reference_py.npz"), **out)
-        print("wrote", os.path.join(HERE, "reference_py.npz"))
+            model_goldens(ref, out, tag, prompt)
+
+        # 4. A GGUF file of the same weights (Q4_K layers, Q6_K tied head,
+        # float32 small tensors; the layout of GPT-2's Q4_K_M files), read
+        # by reference.py's --gguf path (gguf-py dequantization, int16 head
+        # input), with the int8 KV cache gpt2t uses for GGUF models.
+        sys.path.insert(0, os.path.join(os.path.dirname(HERE)))
+        from gguf_file import write_gpt2_gguf
+
+        gpath = os.path.join(tmp, "gpt2_q4_k.gguf")
+        write_gpt2_gguf(gpath, synth.gpt2_random_init(0))
+        configure(ref, kv="int8", gguf_path=gpath)
+        model_goldens(ref, out, "gguf", prompt)
+    # 5. bf16: the reference model on bfloat16-rounded matrices with the
+    # bfloat16 KV cache (kvcache.mojo DenseKV[bf16]).
+    with tempfile.TemporaryDirectory() as tmp:
+        ref = load_reference(ref_root, tmp, bf16_weights(synth.gpt2_random_init(0)))
+        configure(ref, kv="bf16")
+        model_goldens(ref, out, "bf16", prompt)
+    np.savez_compressed(os.path.join(HERE, "reference_py.npz"), **out)
+    print("wrote", os.path.join(HERE, "reference_py.npz"))
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/llm_mojo")
+    main(sys.argv[1])

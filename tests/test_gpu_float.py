@@ -168,3 +168,29 @@ def test_score_rows_match_oracle(torch, ctx):
     got = stats.cpu().numpy()
     # float64 sums over the vocabulary in another order: agreement to ~1e-12
     np.testing.assert_allclose(got, want, rtol=1e-11, atol=1e-12)
+
+
+@pytest.mark.parametrize("fmt,tag", [("f32", "f32"), ("bf16", "bf16"), ("gguf-q4_k", "gguf")])
+def test_float_model_matches_reference_goldens(torch, ctx, gpt2_tensors, golden, fmt, tag):
+    """The whole 12-layer device model against the reference's own NumPy
+    GPT-2 (golden/reference_py.npz): logits at all 24 prompt positions and
+    the 8 greedy ids after [EOT], within north_star's float tolerance
+    max |logit - reference| <= 1e-3 * max |logit|, same argmax."""
+    from llm_mojo_b200.model import FloatModel
+
+    prompt = np.ascontiguousarray(golden["prompt24"], dtype=np.int32)
+    m = FloatModel(ctx, gpt2_tensors, fmt, max_t=64)
+    try:
+        logits = torch.zeros((24, m.V), dtype=torch.float32, device="cuda")
+        m.forward_all(prompt, logits)
+        lg = logits.cpu().numpy()
+        ids = list(m.generate([50256], 8))
+    finally:
+        m.free()
+    for rows, key in ((lg[23:24], "p24"), (lg[:16], "all16")):
+        top = np.atleast_2d(golden[f"{tag}_{key}_top_ids"]).astype(np.int64)
+        vals = np.atleast_2d(golden[f"{tag}_{key}_top_vals"])
+        got = np.take_along_axis(rows, top, axis=1)
+        assert np.abs(got - vals).max() <= 1e-3 * float(golden[f"{tag}_{key}_max"])
+        assert np.array_equal(rows.argmax(axis=1), top[:, 0])
+    assert ids == [int(v) for v in golden[f"{tag}_greedy8"]]
