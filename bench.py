@@ -113,27 +113,33 @@ class Clocks:
                 "samples": len(sm)}
 
 
-def cpu_baseline(seconds: float = 20.0):
-    """The CPU oracle's greedy decode of config 0, sampled for about
-    `seconds`: tokens per second over the tokens it finished."""
+def cpu_baseline(seconds: float = 20.0, samples: int = 5):
+    """The CPU oracle's greedy decode of config 0: `samples` runs (the prompt
+    forward, then decode steps up to the 100-token generation or
+    seconds / samples), tokens per second over the decode steps each
+    finished; the median of the runs (BASELINE.md's median of 5)."""
     from llm_mojo_b200 import synth
     from oracle import oracle as O
 
     t = synth.gpt2_random_init(0)
     m = O.Model(t)
-    logits = m.forward(PROMPT, 0)
-    n, pos, t0 = 1, 1, time.perf_counter()
-    while time.perf_counter() - t0 < seconds and n < STEPS_PER_GEN:
-        nxt = int(O.lib().oq_argmax(O.ptr(logits), m.V))
-        logits = m.forward([nxt], pos)
-        pos += 1
-        n += 1
-    dt = time.perf_counter() - t0
+    rates, steps = [], []
+    for _ in range(samples):
+        logits = m.forward(PROMPT, 0)
+        n, pos, t0 = 1, 1, time.perf_counter()
+        while time.perf_counter() - t0 < seconds / samples and n < STEPS_PER_GEN:
+            nxt = int(O.lib().oq_argmax(O.ptr(logits), m.V))
+            logits = m.forward([nxt], pos)
+            pos += 1
+            n += 1
+        rates.append((n - 1) / (time.perf_counter() - t0))
+        steps.append(n - 1)
     m.close()
     threads = int(O.lib().oq_threads())
     vnni = bool(O.lib().oq_set_vnni(1))
-    return {"value": (n - 1) / dt, "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{n - 1} decode steps of config 0 (after the prompt forward), {threads}-thread team "
+    return {"value": statistics.median(rates), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"median of {samples} runs of {min(steps)}-{max(steps)} decode steps of config 0 (after the "
+                      f"prompt forward; runs {', '.join(f'{r:.0f}' for r in rates)} tok/s), {threads}-thread team "
                       f"(one per physical core), {'AVX-512 VNNI' if vnni else 'scalar'} integer dots, "
                       f"{os.cpu_count()} logical CPUs"}
 
@@ -359,6 +365,61 @@ def run_batched(args):
     return 0
 
 
+def batched_sub(model, stream, flush, world, rank, reps=2, warmup=1):
+    """Config 3 inside the default bench line: 256 sequences x (128-token
+    prompt ~ U[0, V) seed 3 + 128 greedy tokens) split evenly over the ranks
+    (strong scaling), then one NCCL all-gather of the ids, on the config-0
+    model's weights. Device time by CUDA events around one whole generation
+    (prompts and ids in HBM, the gather included), L2 flushed before each;
+    the max over ranks of the mean of `reps` timed generations."""
+    import torch
+    import torch.distributed as dist
+
+    from llm_mojo_b200 import synth
+    from llm_mojo_b200.model import Batch
+    from llm_mojo_b200.shard import gather_blocks, shard_range
+
+    b_lo, b_hi = shard_range(BATCH_SEQS, world, rank)
+    per = b_hi - b_lo
+    batch = Batch(model, per, BATCH_PROMPT)
+    prompts = synth.uniform_ids(BATCH_SEQS * BATCH_PROMPT, 3).reshape(BATCH_SEQS, BATCH_PROMPT)
+    prompts_dev = torch.from_numpy(np.ascontiguousarray(prompts[b_lo:b_hi])).cuda()
+    ids_dev = torch.zeros((per, BATCH_STEPS), dtype=torch.int32, device="cuda")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    times = []
+    with torch.cuda.stream(stream):
+        for i in range(warmup + reps):
+            flush.zero_()
+            barrier()
+            s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            batch.generate_async(prompts_dev, BATCH_STEPS, ids_dev)
+            all_ids = gather_blocks(ids_dev, world)
+            e0.record(stream)
+            barrier()
+            if i >= warmup:
+                times.append(s0.elapsed_time(e0))
+    ms = torch.tensor([statistics.mean(times)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    head = [int(v) for v in all_ids.reshape(BATCH_SEQS, BATCH_STEPS)[-1, :4].cpu()]
+    batch.free()
+    return {"metric": "int4-g32-a16 batched decode tok/s (b=256/box)",
+            "value": BATCH_SEQS * BATCH_STEPS / (ms / 1000.0), "unit": "tok/s", "n_gpus": world,
+            "scaling": "strong", "seqs": BATCH_SEQS, "prompt_len": BATCH_PROMPT, "gen_tokens": BATCH_STEPS,
+            "ms_per_generation": ms, "steps": reps, "warmup": warmup,
+            "parallelism": f"sequences split over {world} ranks, one NCCL all-gather of the ids",
+            "workload": "config 3: 256 sequences x (128-token prompt ~ U[0, 50257) seed 3 + 128 greedy tokens), "
+                        "GPT-2 124M int4-g32-a16 + int8-ch head + int8 KV, random-init weights (seed 0)",
+            "l2": "flushed between generations (256 MiB write)", "last_seq_ids_head": head}
+
+
 PPL_IDS, PPL_SEED = 65536, 4
 
 
@@ -411,7 +472,7 @@ def run_ppl(args):
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
     from llm_mojo_b200 import build, synth
-    from llm_mojo_b200.evaluate import Harness, schedule
+    from llm_mojo_b200.evaluate import Harness, rank_windows, schedule
     from llm_mojo_b200.model import FloatModel, Model
     from llm_mojo_b200.tensor import Context
 
@@ -425,7 +486,7 @@ def run_ppl(args):
               "gguf-q4_k": FloatModel(ctx, tensors, "gguf-q4_k")}
     ids = synth.zipf_ids(PPL_IDS, PPL_SEED)
     wins = schedule(len(ids))
-    mine = wins[rank::world]
+    mine = rank_windows(wins, world, rank)
     with torch.cuda.stream(stream):
         warm = Harness(ctx, models, base)
         for w in mine[:1]:
@@ -590,6 +651,8 @@ def main():
     ap.add_argument("--sweep-only", default=None, metavar="FORMAT[:OUTxIN]",
                     help="sweep workload: time only this format (e.g. int8-ch-a16), optionally at one shape "
                          "(e.g. int8-ch-a16:50257x768), for profiling captures")
+    ap.add_argument("--no-batched", action="store_true",
+                    help="leave out the config-3 batched decode sub-object of the default line")
     ap.add_argument("--mode", default=None, choices=["cluster", "persistent", "graph", "eager"],
                     help="decode mode of the config-0 model (default: the library's default for its formats)")
     ap.add_argument("--profile", action="store_true",
@@ -676,6 +739,8 @@ def main():
             e2e_ms.append(s0.elapsed_time(e0))
         assert list(out) == list(ids)
 
+    batched = None if args.no_batched else batched_sub(model, stream, flush, world, rank)
+
     if args.profile:
         model.profile(True)
         model.generate(PROMPT, STEPS_PER_GEN)
@@ -716,7 +781,8 @@ def main():
             "vs_baseline": None, "dtype": "int16xint4->int32", "data": "synthetic", "config": config_dict(args),
             "e2e": {"value": world * STEPS_PER_GEN / (e2e_avg / 1000.0), "unit": "tok/s",
                     "h2d_bytes_per_step": 4 * len(PROMPT), "d2h_bytes_per_step": 4 * STEPS_PER_GEN},
-            "roofline": {"bound": "hbm", "kernel": "mega_decode_kernel (one launch = the 100-token generation)",
+            "roofline": {"bound": "hbm", "kernel": ("cluster_decode_kernel" if model.mode() == "cluster" else
+                                                     "mega_decode_kernel") + " (one launch = the 100-token generation)",
                          "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                          "frac": achieved / peak,
                          "traffic": MEGA_TRAFFIC_BYTES if model.mode() == "persistent" else None,
@@ -725,12 +791,13 @@ def main():
                          "algorithmic_bytes_per_launch": launch_bytes, "avg_launch_ms": launch_ms},
             "weight_bytes_per_token": TOKEN_BYTES,
             "effective_weight_gbs": TOKEN_BYTES * STEPS_PER_GEN * args.steps / (total_ms / 1000.0) / 1e9,
-            "gpu_launches": args.steps * (1 if model.mode() == "persistent" else
+            "gpu_launches": args.steps * (1 if model.mode() in ("persistent", "cluster") else
                                           1 + STEPS_PER_GEN * launches_per_token),
             "decode_mode": model.mode(),
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "ids_head": [int(i) for i in ids[:8]],
+            "batched": batched,
         }
         print(json.dumps(line))
     model.free()

@@ -129,6 +129,14 @@ llmq_status llmq_head_argmax(llmq_ctx *ctx, const llmq_weight *w, const float *h
 #define LLMQ_NOALLOC_MAX_PARTS 1920
 llmq_status llmq_head_argmax_noalloc(llmq_ctx *ctx, const llmq_weight *w, const float *h_dev, float *logits_dev,
                                      int *argmax_dev);
+/* Limit, in SM clock cycles, of each device-side wait of the persistent and
+ * cluster decode kernels and of the row GEMVs (GGUF and dense formats);
+ * 0 restores the default (4e9 cycles, about 2 s). A wait that runs out
+ * makes the kernel record an error, wait for its own copies in flight (a
+ * separate, long bound) and return; the call that synchronises next
+ * reports LLMQ_ERR_TIMEOUT. No counterpart in the reference (its waits are
+ * host spin loops); this is the hook the timeout tests use. */
+llmq_status llmq_set_wait_limit(llmq_ctx *ctx, long long cycles);
 /* Which kernel runs the several-token (T > 1) A16 matmuls of llmq_linear /
  * llmq_head (tile_i16, kernels.mojo:512-573): AUTO (the tcgen05 split-int8
  * GEMM from 16 tokens on, where the shape allows), CUDA_CORE (dp tiles), or

@@ -47,6 +47,7 @@ SIGNATURES = {
     "llmq_head_argmax": (I, [P, P, P, P, P]),
     "llmq_head_argmax_noalloc": (I, [P, P, P, P, P]),
     "llmq_set_prefill_kernel": (I, [P, I]),
+    "llmq_set_wait_limit": (I, [P, LL]),
     "llmq_batch_create": (I, [P, P, I, I, P]),
     "llmq_score_rows": (I, [P, P, P, P, I, I, I, P, I]),
     "llmq_model_save": (I, [P, P, C.c_char_p]),

@@ -145,6 +145,7 @@ struct CdLSmem {  // a layer rank
   unsigned long long rbar[4];         // receive buffers: att, xmid, fc, xout
   volatile int abort;
   int token;
+  unsigned rph_left;                  // parities of the receive phases open when the rank gave up
   alignas(16) float red[64];
   alignas(16) float b_att[768];       // attention output (all heads), pushed by ranks 0..11
   alignas(16) float b_xmid[768];      // x after attention + PROJ + residual
@@ -724,6 +725,7 @@ __device__ __noinline__ void cd_layer_rank(const CdArgs &a, CdLSmem &sm, const i
     for (int i = 0; i < CD_NSLOT; i++) mbar_init(&sm.full[i], 1);
     for (int i = 0; i < 4; i++) mbar_init(&sm.rbar[i], 1);
     sm.abort = 0;
+    sm.rph_left = 0;
     int t0 = *a.first_token;
     if (t0 < 0 || t0 >= a.V) {
       atomicCAS(a.err, 0, 9);
@@ -975,7 +977,7 @@ __device__ __noinline__ void cd_layer_rank(const CdArgs &a, CdLSmem &sm, const i
       unsigned par = (unsigned)rpar;
       for (int q = seq; q < iss; q++) {
         const long long t1 = clock64();
-        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < kDrainCycles) {
         }
         if (++slot == CD_NSLOT) {
           slot = 0;
@@ -983,11 +985,7 @@ __device__ __noinline__ void cd_layer_rank(const CdArgs &a, CdLSmem &sm, const i
         }
       }
     }
-    for (int i = 0; i < 4; i++) {
-      const long long t1 = clock64();
-      while (!cd_try_wait_cluster(&sm.rbar[i], (rph >> i) & 1u) && clock64() - t1 < a.timeout_cycles / 16) {
-      }
-    }
+    sm.rph_left = rph;  // the receive phases still open, drained at the kernel's end
   } else if (prof_on) {
     for (int k = 0; k < MK_PROF; k++) a.prof[k] += pacc[k];
   }
@@ -1161,7 +1159,7 @@ __device__ __noinline__ void cd_head_cta(const CdArgs &a, CdHSmem &sm, const int
       unsigned par = (unsigned)rpar;
       for (int q = seq; q < iss; q++) {
         const long long t1 = clock64();
-        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < kDrainCycles) {
         }
         if (++slot == CD_HNSLOT) {
           slot = 0;
@@ -1181,8 +1179,23 @@ __global__ void __launch_bounds__(CD_THREADS, 1) cluster_decode_kernel(CdArgs a)
     cd_layer_rank(a, *reinterpret_cast<CdLSmem *>(cd_smem_raw), (int)rank);
   else
     cd_head_cta(a, *reinterpret_cast<CdHSmem *>(cd_smem_raw), (int)((cl - 1) * CD_CLUSTER + rank));
-  // no CTA leaves while a peer may still write into its shared memory
   __syncthreads();
+  // every CTA of the cluster has stopped pushing ...
+  cd_cluster_sync();
+  if (cl == 0) {
+    // ... a layer rank that gave up waits (bounded) for the pushes it was
+    // expecting that were already in flight (after a normal run every push
+    // has been waited for) ...
+    CdLSmem &sm = *reinterpret_cast<CdLSmem *>(cd_smem_raw);
+    if (sm.abort && threadIdx.x == 0)
+      for (int i = 0; i < 4; i++) {
+        const long long t1 = clock64();
+        while (!cd_try_wait_cluster(&sm.rbar[i], (sm.rph_left >> i) & 1u) && clock64() - t1 < kDrainCycles / 16) {
+        }
+      }
+    __syncthreads();
+  }
+  // ... and no CTA leaves while a peer may still write into its shared memory
   cd_cluster_sync();
 }
 

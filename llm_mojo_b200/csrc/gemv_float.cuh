@@ -161,7 +161,14 @@ struct RowGemvArgs {
   const float *bias;  // [rows] or null
   float *out;         // [rows]
   int epi;            // EPI_BIAS / EPI_GELU / EPI_RESID
+  int *err;           // device error word: set to 6 when a tile's copy wait gives up
+  long long timeout;  // cycles a tile's copy wait may take
 };
+
+// Bound of the waits for copies still in flight when a kernel gives up
+// (independent of the settable wait limit, so that no CTA leaves while a
+// copy may still write its shared memory).
+constexpr long long kDrainCycles = 4000000000LL;
 
 __device__ __forceinline__ unsigned rf_smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
 
@@ -212,11 +219,11 @@ __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
     if (threadIdx.x == 0 && ahead < ntiles) issue(ahead, (it + RF_STAGES - 1) % RF_STAGES);
     // wait for this tile (phase it / RF_STAGES of stage s); the decision to
     // give up is taken by the whole CTA, so every thread meets the same barriers
-    auto wait_stage = [&](int k) {
+    auto wait_stage = [&](int k, long long limit) {
       const unsigned par = (unsigned)((k / RF_STAGES) & 1);
       unsigned ok = 0;
       const long long t0 = clock64();
-      while (!ok && clock64() - t0 < 4000000000LL)
+      while (!ok && clock64() - t0 < limit)
         asm volatile(
             "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
@@ -224,10 +231,13 @@ __global__ void __launch_bounds__(RF_THREADS) row_gemv_kernel(RowGemvArgs a) {
             : "memory");
       return ok != 0;
     };
-    if (__syncthreads_or(!wait_stage(it))) {
-      // a copy never landed: wait (bounded) for the tiles still in flight, then give up
-      if (threadIdx.x == 0)
-        for (int k = it + 1; k < it + RF_STAGES && tile + (k - it) * gridDim.x < ntiles; k++) wait_stage(k);
+    if (__syncthreads_or(!wait_stage(it, a.timeout))) {
+      // a copy did not land in time: record it, wait (bounded) for this
+      // tile's copy and the ones issued after it, then give up
+      if (threadIdx.x == 0) {
+        atomicCAS(a.err, 0, 6);
+        for (int k = it; k < it + RF_STAGES && tile + (k - it) * gridDim.x < ntiles; k++) wait_stage(k, kDrainCycles);
+      }
       __syncthreads();
       return;
     }

@@ -33,6 +33,7 @@ struct llmq_ctx {
   DecodeState *state = nullptr;  // device, for llmq_head_argmax
   int dense_parts = 4;           // gemv's parts: the reference team of 4 threads (gpt2t.mojo:281 on 4 cores)
   int prefill_kernel = LLMQ_PREFILL_AUTO;
+  long long wait_cycles = 4000000000LL;  // limit of a persistent kernel's or a row GEMV's device-side wait
   int *tc_err = nullptr;         // device error code of the tcgen05 GEMM (a wait that gave up)
   bool tc_used = false;          // a tcgen05 GEMM ran since the last check
   // sampling scratch (device, grown on demand): sort keys, chunk candidates,
@@ -382,6 +383,18 @@ __global__ void __launch_bounds__(kThreads) lane_sums_kernel(GemvArgs a, int32_t
   }
 }
 
+namespace {
+// Contexts alive per device, and the device address of the no-allocation
+// entry point's scratch array (g_head_argmax_scratch) on each device, looked
+// up by its first call there. The address belongs to the device's context:
+// when the last llmq context of a device is destroyed it is dropped, so a
+// context created after cudaDeviceReset looks it up again.
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+int g_dev_contexts[kNoallocMaxDevices] = {};
+void *g_noalloc_ptr[kNoallocMaxDevices] = {};
+}  // namespace
+
 extern "C" {
 
 llmq_status llmq_init(int device, llmq_ctx **out) {
@@ -402,12 +415,20 @@ llmq_status llmq_init(int device, llmq_ctx **out) {
     return LLMQ_ERR_CUDA;
   }
   ctx->stream = ctx->own;
+  if (device >= 0 && device < kNoallocMaxDevices) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    g_dev_contexts[device]++;
+  }
   *out = ctx;
   return LLMQ_OK;
 }
 
 llmq_status llmq_destroy(llmq_ctx *ctx) {
   if (!ctx) return LLMQ_ERR_INVALID;
+  if (ctx->device >= 0 && ctx->device < kNoallocMaxDevices) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (--g_dev_contexts[ctx->device] == 0) g_noalloc_ptr[ctx->device] = nullptr;
+  }
   cudaSetDevice(ctx->device);
   if (ctx->own) cudaStreamSynchronize(ctx->own);
   if (ctx->scratch) cudaFree(ctx->scratch);
@@ -434,6 +455,12 @@ llmq_status llmq_sync(llmq_ctx *ctx) {
   if (!ctx) return LLMQ_ERR_INVALID;
   CK(cudaStreamSynchronize(ctx->stream));
   return tc_check(ctx);
+}
+
+llmq_status llmq_set_wait_limit(llmq_ctx *ctx, long long cycles) {
+  if (!ctx || cycles < 0) return fail(ctx, LLMQ_ERR_INVALID, "bad wait limit");
+  ctx->wait_cycles = cycles == 0 ? 4000000000LL : cycles;
+  return LLMQ_OK;
 }
 
 llmq_status llmq_set_prefill_kernel(llmq_ctx *ctx, int kind) {
@@ -558,7 +585,7 @@ long long llmq_weight_nbytes(const llmq_weight *w) { return w ? w->nbytes : -1; 
 
 namespace {
 template <int T>
-cudaError_t launch_row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
+cudaError_t launch_row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {  // a.err / a.timeout set by row_gemv
   const int rb = (int)a.w.row_bytes;
   const int R = rf_rows(rb);
   const int ntiles = (a.w.rows + R - 1) / R;
@@ -568,7 +595,13 @@ cudaError_t launch_row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
   return cudaGetLastError();
 }
 
-cudaError_t row_gemv(const llmq_ctx *ctx, const RowGemvArgs &a) {
+// Launches the row GEMV with the context's wait limit and error word; a wait
+// that gives up is reported by the next tc_check (llmq_sync and the calls
+// that synchronise).
+cudaError_t row_gemv(llmq_ctx *ctx, RowGemvArgs a) {
+  a.err = ctx->tc_err;
+  a.timeout = ctx->wait_cycles;
+  ctx->tc_used = true;
   switch (a.w.type) {
     case RT_F32: return launch_row_gemv<RT_F32>(ctx, a);
     case RT_F16: return launch_row_gemv<RT_F16>(ctx, a);
@@ -860,7 +893,7 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     // matmul_rows (kernels.mojo:285-349) for one token: dot_row per output.
     if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation affine matmuls with T > 1 are not built");
     if (w->kind == WK_GGUF) {
-      RowGemvArgs a{w->rowmat(), x, bias, out, epi};
+      RowGemvArgs a{w->rowmat(), x, bias, out, epi, nullptr, 0};
       CK(row_gemv(ctx, a));
     } else {
       AffFloatArgs a{w->view(), x, bias, out, epi};
@@ -937,7 +970,7 @@ llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float
   // lm_head_rows gives every token the same arithmetic as lm_head.
   for (int t = 0; t < T; t++) {
     if (w->kind == WK_DENSE) {
-      RowGemvArgs a{w->rowmat(), h + (size_t)t * C, nullptr, logits + (size_t)t * V, 0};
+      RowGemvArgs a{w->rowmat(), h + (size_t)t * C, nullptr, logits + (size_t)t * V, 0, nullptr, 0};
       CK(row_gemv(ctx, a));
     } else {
       llmq_status st = llmq_linear(ctx, w, h + (size_t)t * C, nullptr, logits + (size_t)t * V, 1, C, V, 0);
@@ -992,13 +1025,10 @@ static_assert(LLMQ_NOALLOC_MAX_PARTS == kNoallocMaxParts, "header limit matches 
 static __device__ __align__(256) unsigned char g_head_argmax_scratch[kNoallocBytes];
 
 namespace {
-constexpr int kNoallocMaxDevices = 64;
-std::mutex g_noalloc_mu;
-void *g_noalloc_ptr[kNoallocMaxDevices] = {};
-
 // The device address of g_head_argmax_scratch on ctx's device, looked up once
-// per device with that device current. The lookup may load the module on the
-// device, so the first call should come before any stream capture.
+// per device (again after the device's last context was destroyed) with that
+// device current. The lookup may load the module on the device, so the first
+// call should come before any stream capture.
 llmq_status noalloc_scratch(llmq_ctx *ctx, unsigned char **out) {
   if (ctx->device < 0 || ctx->device >= kNoallocMaxDevices)
     return fail(ctx, LLMQ_ERR_INVALID, "llmq_head_argmax_noalloc: device index beyond 63");
@@ -1518,7 +1548,7 @@ llmq_status run_cluster(llmq_model *m, const int *first_token, int pos0, int ste
   a.steps = steps;
   a.flag0 = m->cd_flag;
   a.err = m->mega_err;
-  a.timeout_cycles = 4000000000LL;  // ~2 s at 2 GHz per wait
+  a.timeout_cycles = ctx->wait_cycles;
   a.prof = m->prof;
   m->cd_flag += (unsigned)steps;
   cudaLaunchConfig_t cfg{};
@@ -1566,7 +1596,7 @@ llmq_status run_mega(llmq_model *m, const int *first_token, int pos0, int steps,
   a.steps = steps;
   a.flag0 = m->mega_flag;
   a.err = m->mega_err;
-  a.timeout_cycles = 4000000000LL;  // ~2 s at 2 GHz per wait
+  a.timeout_cycles = ctx->wait_cycles;
   a.prof = m->prof;
   m->mega_flag += (unsigned)steps;
   void *args[] = {&a};

@@ -33,6 +33,7 @@
 
 #include "attention.cuh"
 #include "gemv_a16.cuh"
+#include "gemv_float.cuh"
 
 namespace llmq {
 
@@ -1078,7 +1079,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       tlast = t;
     }
   };
-  auto slot_wait = [&](int ahead = 0) -> int {  // slot of chunk `seq + ahead` (ahead 0 or 1), or -1 on timeout
+  // Slot of chunk `seq + ahead` (ahead 0 or 1), or -1 on timeout. Every
+  // thread waits; the answer is the CTA's, read after a barrier, so that no
+  // thread leaves for the exit path while others enter a phase's barriers.
+  auto slot_wait = [&](int ahead = 0) -> int {
     int slot = rslot + ahead;
     unsigned par = (unsigned)rpar;
     if (slot >= MK_NSLOT) {
@@ -1087,10 +1091,11 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
     }
     long long t0 = clock64();
     while (!mbar_try_wait(&sm.full[slot], par)) {
-      if (!mk_alive(a, sm, t0, 1)) return -1;
+      if (!mk_alive(a, sm, t0, 1)) break;
     }
     if (prof_on) pacc[PF_RING_WAIT] += clock64() - t0;
-    return slot;
+    cta_sync();
+    return sm.abort ? -1 : slot;
   };
   // Called after the barrier that ends the use of the slot (the last one in
   // mk_gemv_blk4, or the one after mk_head_pair).
@@ -1251,7 +1256,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mega_decode_kernel(MegaArgs a) 
       unsigned par = (unsigned)rpar;
       for (int q = seq; q < seq + MK_NSLOT && q < total_chunks; q++) {
         long long t1 = clock64();
-        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < a.timeout_cycles) {
+        while (!mbar_try_wait(&sm.full[slot], par) && clock64() - t1 < kDrainCycles) {
         }
         if (++slot == MK_NSLOT) {
           slot = 0;

@@ -32,6 +32,58 @@ def schedule(n: int, window: int = WINDOW, stride: int = STRIDE):
         begin += stride
 
 
+def rank_windows(windows: list, world: int, rank: int) -> list:
+    """This rank's windows: round-robin over the ranks (every window scored
+    by exactly one rank; the scoring ranges depend only on the window)."""
+    return windows[rank::world]
+
+
+def accumulate(total, s, n_rows: int) -> None:
+    """Adds one window's per-row statistics s [6, n_rows] (score_rows'
+    layout) into a format's totals [7]: sums of NLL, NLL_BASE, AGREE, KL and
+    DIFF_SUM, the max of DIFF_MAX, and the row count."""
+    import torch
+
+    total[0:4] += s[[NLL, NLL_BASE, AGREE, KL]].sum(dim=1)
+    total[4] += s[DIFF_SUM].sum()
+    total[5] = torch.maximum(total[5], s[DIFF_MAX].max())
+    total[6] += n_rows
+
+
+def reduce_totals(totals: dict, world: int) -> None:
+    """Combines every rank's totals in place (eval_loop's sums over all
+    windows, gpt2t.mojo:1120-1176): one all-reduce SUM of each format's
+    totals, then one all-reduce MAX of its largest logit difference, in the
+    same order on every rank."""
+    if world <= 1:
+        return
+    import torch.distributed as dist
+
+    for name in totals:
+        t = totals[name]
+        mx = t[5:6].clone()
+        dist.all_reduce(t)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        t[5] = mx[0]
+
+
+def report_totals(totals: dict, V: int, compared: bool) -> dict:
+    """The harness's figures from the combined totals (gpt2t.mojo:1150-1176):
+    perplexity and mean NLL, and against float32 its perplexity, top-1
+    agreement, mean KL and the mean / max absolute logit difference."""
+    out = {}
+    for name, t in totals.items():
+        t = t.cpu().numpy()
+        cnt = t[6]
+        r = {"tokens_scored": int(cnt), "perplexity": math.exp(t[0] / cnt), "mean_nll": t[0] / cnt}
+        if compared:
+            r.update({"f32_perplexity": math.exp(t[1] / cnt), "top1_agreement": t[2] / cnt,
+                      "mean_kl": t[3] / cnt, "mean_abs_logit_diff": t[4] / (cnt * V),
+                      "max_abs_logit_diff": float(t[5])})
+        out[name] = r
+    return out
+
+
 class Harness:
     """Scores formats against a float32 base model. models: {name: model}
     with forward_all(tokens, logits) and V; base: the float32 model (or None
@@ -69,35 +121,11 @@ class Harness:
                                         C.c_void_p(self.targets.data_ptr()), self.V, r0, r1,
                                         C.c_void_p(self.stats.data_ptr()), self.window), self.ctx.h)
             self.ctx.sync()
-            s = self.stats[:, : r1 - r0]
-            t = self.totals[name]
-            t[0:4] += s[[NLL, NLL_BASE, AGREE, KL]].sum(dim=1)
-            t[4] += s[DIFF_SUM].sum()
-            t[5] = torch.maximum(t[5], s[DIFF_MAX].max())
-            t[6] += r1 - r0
+            accumulate(self.totals[name], self.stats[:, : r1 - r0], r1 - r0)
 
     def reduce(self, world: int):
-        """Sums (and the max) over the ranks: one all-reduce per statistic
-        kind, in the same order on every rank."""
-        if world > 1:
-            import torch.distributed as dist
-
-            for name in self.models:
-                t = self.totals[name]
-                mx = t[5:6].clone()
-                dist.all_reduce(t)
-                dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-                t[5] = mx[0]
+        """Sums (and the max) over the ranks (reduce_totals)."""
+        reduce_totals(self.totals, world)
 
     def report(self) -> dict:
-        out = {}
-        for name, t in self.totals.items():
-            t = t.cpu().numpy()
-            cnt = t[6]
-            r = {"tokens_scored": int(cnt), "perplexity": math.exp(t[0] / cnt), "mean_nll": t[0] / cnt}
-            if self.base is not None:
-                r.update({"f32_perplexity": math.exp(t[1] / cnt), "top1_agreement": t[2] / cnt,
-                          "mean_kl": t[3] / cnt, "mean_abs_logit_diff": t[4] / (cnt * self.V),
-                          "max_abs_logit_diff": float(t[5])})
-            out[name] = r
-        return out
+        return report_totals(self.totals, self.V, self.base is not None)

@@ -5,7 +5,11 @@ its scratch in a fixed device array, so its logits must equal the existing
 entry point's bit for bit (the tolerance of the head tests: zero) and its
 argmax must be the same index. Two calls in a row check that the state the
 array carries (the CTA ticket and the id slot) is cleared between calls.
-This file is collected last so that it also runs after every other test.
+The cases take the three head GEMV kernels: the per-warp cp.async ring
+(int8-ch, 50257 rows), the split-K tiles (int4-g32, 2304 rows) and the
+whole-row kernel of the other formats from 8192 rows (int4-g128). The first
+case is also checked against the CPU oracle. This file is collected last so
+that it also runs after every other test.
 """
 
 import ctypes as C
@@ -29,7 +33,7 @@ def _p(t):
     return C.c_void_p(t.data_ptr())
 
 
-@pytest.mark.parametrize("fmt,rows", [("int8-ch-a16", 50257), ("int4-g32-a16", 2304)])
+@pytest.mark.parametrize("fmt,rows", [("int8-ch-a16", 50257), ("int4-g32-a16", 2304), ("int4-g128-a16", 8192)])
 def test_head_argmax_noalloc_matches_head_argmax(torch, fmt, rows):
     from llm_mojo_b200 import build
     from llm_mojo_b200._lib import check, lib
@@ -59,5 +63,13 @@ def test_head_argmax_noalloc_matches_head_argmax(torch, fmt, rows):
         got = got_l[i].cpu().numpy()
         assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
         assert int(got_a[i].item()) == int(want_a[i].item()) == int(np.argmax(want))
+    if fmt == "int8-ch-a16":
+        from oracle import oracle as O
+
+        ow = O.QuantMatrix(src, bits, group, sym, a16, False)
+        for i in range(2):
+            ref = O.matmul_rows_a16(hs[i].cpu().numpy()[None, :], ow, None)[0]
+            assert np.array_equal(got_l[i].cpu().numpy().view(np.uint32), ref.view(np.uint32))
+            assert int(got_a[i].item()) == int(O.lib().oq_argmax(O.ptr(ref), rows))
     w.free()
     ctx.close()
