@@ -302,6 +302,16 @@ llmq_status llmq_score_rows(llmq_ctx *ctx, const float *logits_dev, const float 
 typedef struct llmq_batch llmq_batch;
 llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int max_prompt, llmq_batch **out);
 llmq_status llmq_batch_free(llmq_batch *b);
+/* Which kernel runs the batched one-token matmuls (the layers' BLOCKED
+ * int4-g32 rows and the per-channel int8 head; dot_row_i16 per sequence,
+ * tensor.mojo:522-566): AUTO (the lane-mode tcgen05 GEMM from 16 sequences
+ * on), CUDA_CORE (the dp2a batched GEMVs) or TCGEN05 (the GEMM for any
+ * count). Results are identical; no counterpart in the reference, which
+ * decodes one sequence at a time. */
+#define LLMQ_BATCH_AUTO 0
+#define LLMQ_BATCH_CUDA_CORE 1
+#define LLMQ_BATCH_TCGEN05 2
+llmq_status llmq_batch_set_kernel(llmq_batch *b, int kind);
 /* generate (gpt2t.mojo:942-980, without the stop at EOT) for B sequences at
  * once: prompts [B][n_prompt] and out_ids [B][steps] on the host. Each
  * sequence's ids are those of llmq_generate on that sequence alone: its

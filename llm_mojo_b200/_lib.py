@@ -54,6 +54,7 @@ SIGNATURES = {
     "llmq_model_load": (I, [P, C.c_char_p, I, I, P]),
     "llmq_model_load_gguf": (I, [P, C.c_char_p, I, I, P]),
     "llmq_batch_free": (I, [P]),
+    "llmq_batch_set_kernel": (I, [P, I]),
     "llmq_batch_generate": (I, [P, P, P, I, I, I, P]),
     "llmq_batch_generate_async": (I, [P, P, P, I, I, I, P]),
     "llmq_layernorm": (I, [P, P, P, P, P, I, I]),

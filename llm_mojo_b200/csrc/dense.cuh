@@ -157,6 +157,35 @@ __global__ void __launch_bounds__(256) gguf_dequant_rows_kernel(RowMat w, int r0
   }
 }
 
+// QuantMatrix.dequant_row (tensor.mojo:431-479, the natural layout of the
+// W4A32 / W8A32 formats): value k of row r0 + rr is (u - zp) * scale, the
+// code and the zero point as exact floats, one rounding in the product.
+// One thread per pair of bytes' worth of values (two int4 codes of a byte
+// for 4 bits, one code for 8), rows [r0, r0 + nrows) into dst[rr][cols].
+__global__ void __launch_bounds__(256) affine_dequant_rows_kernel(WeightView w, int r0, int nrows, float *dst) {
+  const int gpr = w.cols / w.group;
+  const size_t per_row = (size_t)w.cols * w.bits / 8;  // bytes
+  const size_t total = per_row * nrows;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int rr = (int)(i / per_row), j = (int)(i - (size_t)rr * per_row), row = r0 + rr;
+    const uint8_t b = w.codes[(size_t)row * per_row + j];
+    float *o = dst + (size_t)rr * w.cols;
+    if (w.bits == 8) {
+      const int g = j / w.group;
+      const float s = __half2float(__ushort_as_half(w.scale[(size_t)row * gpr + g]));
+      const float zp = (float)w.zp[(size_t)row * gpr + g];
+      o[j] = ((float)b - zp) * s;
+    } else {
+      // byte j of a 32-code run: code (j % 16) low nibble, code (j % 16) + 16 high
+      const int k0 = (j >> 4) * 32 + (j & 15), g = k0 / w.group;
+      const float s = __half2float(__ushort_as_half(w.scale[(size_t)row * gpr + g]));
+      const float zp = (float)w.zp[(size_t)row * gpr + g];
+      o[k0] = ((float)(b & 0xF) - zp) * s;
+      o[k0 + 16] = ((float)(b >> 4) - zp) * s;
+    }
+  }
+}
+
 // rows_dot (kernels.mojo:361-397): output rows [o_start, OUT) from float32
 // rows wd[o - o_start][IN]: 16-lane chains, the halving tree, + bias, finish.
 // One warp per (token, row) pair half: lanes 0-15 and 16-31 take two pairs.

@@ -18,6 +18,7 @@
 #include "prefill_a16.cuh"
 #include "sample.cuh"
 #include "tc_gemm.cuh"
+#include "tcl_gemm.cuh"
 
 using namespace llmq;
 
@@ -62,6 +63,7 @@ struct llmq_weight {
   mutable int tc_tn = 0;            // their output tile width
   mutable uint8_t *tc_w = nullptr;  // the transposed GEMM's 128-row weight tiles (first use)
   mutable int *tc_wsum = nullptr;   // and the rows' per-segment sums of the weight values
+  mutable uint8_t *tcl_a = nullptr; // the lane-mode GEMM's weight tiles (batched decode)
   WeightView view() const { return WeightView{codes, scale, zp, rows, cols, group, bits, blocked}; }
   RowMat rowmat() const { return RowMat{codes, rows, cols, rtype, row_bytes}; }
 };
@@ -575,6 +577,7 @@ llmq_status llmq_weight_free(llmq_weight *w) {
   if (w->tc_b) cudaFree(w->tc_b);
   if (w->tc_w) cudaFree(w->tc_w);
   if (w->tc_wsum) cudaFree(w->tc_wsum);
+  if (w->tcl_a) cudaFree(w->tcl_a);
   delete w;
   return LLMQ_OK;
 }
@@ -643,6 +646,14 @@ bool tc_eligible(const llmq_ctx *ctx, const llmq_weight *w, int T) {
 size_t align256(size_t n) { return (n + 255) / 256 * 256; }
 
 llmq_status dequant_rows(llmq_ctx *ctx, const llmq_weight *w, int r0, int nrows, float *dst) {
+  if (w->kind == WK_AFFINE) {
+    if (w->a16 || w->blocked) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "dequant_rows takes the natural layouts");
+    const size_t bytes = (size_t)nrows * w->cols * w->bits / 8;
+    const int grid = (int)std::min<size_t>((bytes + 255) / 256, (size_t)ctx->num_sms * 16);
+    affine_dequant_rows_kernel<<<grid, 256, 0, ctx->stream>>>(w->view(), r0, nrows, dst);
+    CKL();
+    return LLMQ_OK;
+  }
   const int grid = (nrows + 15) / 16;
   const RowMat rm = w->rowmat();
 #define DQ(T) \
@@ -659,10 +670,11 @@ llmq_status dequant_rows(llmq_ctx *ctx, const llmq_weight *w, int r0, int nrows,
   return LLMQ_OK;
 }
 
-// matmul_rows for T > 1 (kernels.mojo:325-358): rows of 32 outputs
-// dequantized to float32 and run through the mm_tile chain; the OUT % 32
-// leftover rows through rows_dot (:361-397).
-llmq_status gguf_rows_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out,
+// matmul_rows for T > 1 (kernels.mojo:325-358) of the OUT_MAJOR formats
+// (GGUF rows, affine W4A32 / W8A32): rows of 32 outputs dequantized to
+// float32 and run through the mm_tile chain; the OUT % 32 leftover rows
+// through rows_dot (:361-397).
+llmq_status rows_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out,
                              int T, int IN, int OUT, int epi) {
   const int full = OUT / 32 * 32;
   llmq_status st = ensure_scratch(ctx, (size_t)OUT * IN * 4);
@@ -888,10 +900,9 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
     return LLMQ_OK;
   }
   if (IN != w->cols || OUT != w->rows) return fail(ctx, LLMQ_ERR_INVALID, "IN/OUT do not match the matrix");
-  if (w->kind == WK_GGUF && T > 1) return gguf_rows_linear(ctx, w, x, bias, out, T, IN, OUT, epi);
   if (w->kind == WK_GGUF || (w->kind == WK_AFFINE && !w->a16)) {
+    if (T > 1) return rows_linear(ctx, w, x, bias, out, T, IN, OUT, epi);
     // matmul_rows (kernels.mojo:285-349) for one token: dot_row per output.
-    if (T != 1) return fail(ctx, LLMQ_ERR_UNSUPPORTED, "float-activation affine matmuls with T > 1 are not built");
     if (w->kind == WK_GGUF) {
       RowGemvArgs a{w->rowmat(), x, bias, out, epi, nullptr, 0};
       CK(row_gemv(ctx, a));
@@ -955,6 +966,10 @@ llmq_status llmq_head(llmq_ctx *ctx, const llmq_weight *w, const float *h, float
     return LLMQ_OK;
   }
   if (w->kind == WK_AFFINE && w->a16) return llmq_linear(ctx, w, h, nullptr, logits, T, C, V, 0);
+  // head (kernels.mojo:677-689): an OUT_MAJOR head (GGUF rows without the
+  // integer kernel, affine W4A32 / W8A32) runs matmul_rows for all T tokens,
+  // so T > 1 takes the dequantized tiles, not T one-token dots
+  if (T > 1 && (w->kind == WK_GGUF || w->kind == WK_AFFINE)) return llmq_linear(ctx, w, h, nullptr, logits, T, C, V, 0);
   if (w->kind == WK_DENSE && T > 1 && (w->rtype == RT_F32 || w->rtype == RT_BF16)) {
     // lm_head_rows (kernels.mojo:230-271): the 16 lane chains of lm_head, per token
     const dim3 grid((V + 15) / 16, (T + 15) / 16);
@@ -1746,7 +1761,7 @@ llmq_status llmq_model_create(llmq_ctx *ctx, int n_layer, llmq_weight *const *ma
     // dense layers are [IN, OUT] (Conv1D); the others [OUT, IN]
     const bool shape_ok = w && (w->kind == WK_DENSE ? (w->rows == ins[i % 4] && w->cols == outs[i % 4])
                                                     : (w->cols == ins[i % 4] && w->rows == outs[i % 4]));
-    const bool fmt_ok = w && (w->kind == WK_DENSE || w->kind == WK_GGUF || (w->kind == WK_AFFINE && w->a16));
+    const bool fmt_ok = w && (w->kind == WK_DENSE || w->kind == WK_GGUF || w->kind == WK_AFFINE);
     if (!shape_ok || !fmt_ok)
       return fail(ctx, LLMQ_ERR_INVALID, "layer matrix " + std::to_string(i) + " has an unexpected shape or format");
     a16 = a16 && w->kind == WK_AFFINE && w->a16;
@@ -2242,15 +2257,96 @@ struct llmq_batch {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   int graph_B = 0, graph_steps = 0;
+  int graph_kernel = -1;      // the kernel choice the decode-step graph was captured with
+  uint8_t *tcl_b = nullptr;  // the lane-mode GEMM's sequence tiles [max_seqs padded to TCL_TT][widest K x 4]
+  int kernel = LLMQ_BATCH_AUTO;
 };
 
 namespace {
 
 int fmt_code(const llmq_weight *w) { return fmt_of(w->view()); }
 
+constexpr int TCL_TT = 32;          // sequences per lane-mode GEMM tile
+constexpr int TCL_MIN_SEQS = 16;    // AUTO: the lane-mode GEMM from this many sequences
+
+// Whether batch_linear runs w for B sequences as the lane-mode tcgen05 GEMM.
+bool batch_uses_tcl(const llmq_batch *bt, const llmq_weight *w, int B) {
+  if (!w->tcl_a || bt->kernel == LLMQ_BATCH_CUDA_CORE) return false;
+  return bt->kernel == LLMQ_BATCH_TCGEN05 || B >= TCL_MIN_SEQS;
+}
+
+// The argmax partials per sequence of the batched head (row tiles of the
+// kernel that runs it).
+int batch_head_parts(const llmq_batch *bt, int B) {
+  const llmq_model *m = bt->m;
+  return batch_uses_tcl(bt, m->head, B) ? (m->V + TC_M - 1) / TC_M : (m->V + BG_ROWS - 1) / BG_ROWS;
+}
+
+// quantize_rows (+ LayerNorm) of B rows into the lane-mode GEMM's sequence
+// tiles (with sx and, for the int8 head, the lane sums of x), then the GEMM.
+llmq_status batch_linear_tcl(llmq_batch *bt, const llmq_weight *w, const float *x, const float *ln_w,
+                             const float *ln_b, const float *bias, float *out, int B, int epi, cudaStream_t s) {
+  llmq_ctx *ctx = bt->ctx;
+  const WeightView v = w->view();
+  const int K = v.cols, mode = v.bits == 4 ? TCL_BLK4 : TCL_CH8;
+  const int bpad = (B + TCL_TT - 1) / TCL_TT * TCL_TT;
+  const size_t qsm = SmemPlan<FMT_GEN8>(K, K, 0).total;
+  if (ln_w)
+    tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad, 256, qsm, s>>>(x, ln_w, ln_b, B, K, mode, bt->tcl_b, bt->sx,
+                                                                 bt->xsi);
+  else
+    tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad, 256, qsm, s>>>(x, nullptr, nullptr, B, K, mode, bt->tcl_b,
+                                                                    bt->sx, bt->xsi);
+  CKL();
+  TcArgsL a{};
+  a.a = w->tcl_a;
+  a.b = bt->tcl_b;
+  a.sx = bt->sx;
+  a.xsl = bt->xsi;
+  a.w = v;
+  a.bias = bias;
+  a.out = out;
+  a.part_val = out ? nullptr : bt->part_val;
+  a.part_idx = out ? nullptr : bt->part_idx;
+  a.err = ctx->tc_err;
+  a.B = B;
+  a.OUT = v.rows;
+  a.K = K;
+  a.nkb = K / TC_KB;
+  a.nseg = K / 32;
+  a.epi = epi;
+  const dim3 grid(bpad / TCL_TT, (v.rows + TC_M - 1) / TC_M);
+  const size_t sm = sizeof(TcSmemL<TCL_TT>) + 1024;
+  if (mode == TCL_BLK4)
+    tcl_gemm_kernel<TCL_BLK4, TCL_TT><<<grid, TC_THREADS, sm, s>>>(a);
+  else
+    tcl_gemm_kernel<TCL_CH8, TCL_TT><<<grid, TC_THREADS, sm, s>>>(a);
+  CKL();
+  return LLMQ_OK;
+}
+
+// The lane-mode GEMM's weight tiles of every matrix it takes (the layers'
+// and the head), built once per weight.
+llmq_status batch_prepare_tcl(llmq_batch *bt) {
+  llmq_ctx *ctx = bt->ctx;
+  std::vector<const llmq_weight *> ws(bt->m->mats.begin(), bt->m->mats.end());
+  ws.push_back(bt->m->head);
+  for (const llmq_weight *w : ws) {
+    const WeightView v = w->view();
+    if (w->tcl_a || w->kind != WK_AFFINE || !w->a16 || !tcl_supported(v)) continue;
+    const int nt = (v.rows + TC_M - 1) / TC_M, nkb = v.cols / TC_KB;
+    CK(cudaMalloc(&w->tcl_a, (size_t)nt * nkb * TCT_A_BYTES));
+    tcl_prep_a_kernel<<<dim3(nt, nkb), 256, 0, ctx->stream>>>(v, v.bits == 4 ? TCL_BLK4 : TCL_CH8, w->tcl_a);
+    CKL();
+  }
+  CK(cudaStreamSynchronize(ctx->stream));
+  return LLMQ_OK;
+}
+
 // bquant + bgemv for B rows: out[B][rows] (+)= act(quantize(ln?(x)) . w).
 llmq_status batch_linear(llmq_batch *bt, const llmq_weight *w, const float *x, const float *ln_w, const float *ln_b,
                          const float *bias, float *out, int B, int epi, cudaStream_t s) {
+  if (batch_uses_tcl(bt, w, B)) return batch_linear_tcl(bt, w, x, ln_w, ln_b, bias, out, B, epi, s);
   llmq_ctx *ctx = bt->ctx;
   const WeightView v = w->view();
   const int fmt = fmt_code(w), K = v.cols;
@@ -2424,12 +2520,12 @@ llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
   // decode step i (1..steps-1) embeds the token of column i-1 at position P+i-1
   batch_init_state_kernel<<<1, 1, 0, s>>>(bt->state, P - 1, 0);
   CKL();
-  const int nparts = (m->V + BG_ROWS - 1) / BG_ROWS;
+  const int nparts = batch_head_parts(bt, B);
   argmax_parts_kernel<<<B, 256, 0, s>>>(bt->part_val, bt->part_idx, nparts, bt->ids, m->max_t, bt->tokens, nullptr);
   CKL();
   if (steps > 1) {
     // decode steps as one CUDA graph, captured for this batch size
-    if (!bt->exec || bt->graph_B != B) {
+    if (!bt->exec || bt->graph_B != B || bt->graph_kernel != bt->kernel) {
       if (bt->exec) cudaGraphExecDestroy(bt->exec);
       if (bt->graph) cudaGraphDestroy(bt->graph);
       bt->exec = nullptr;
@@ -2450,6 +2546,7 @@ llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
       bt->graph = g;
       CK(cudaGraphInstantiate(&bt->exec, g, 0));
       bt->graph_B = B;
+      bt->graph_kernel = bt->kernel;
     }
     for (int i = 1; i < steps; i++) CK(cudaGraphLaunch(bt->exec, s));
   }
@@ -2513,6 +2610,8 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
   if (e == cudaSuccess) e = cudaMemset(v.vs, 0, seq / HS * max_seqs * 4);
   if (e == cudaSuccess) e = cudaMallocHost(&bt->ids_host, (size_t)max_seqs * m->max_t * 4);
   if (e == cudaSuccess) e = cudaMallocHost(&bt->prompt_host, rows * 4);
+  const int tcl_seqs = (max_seqs + TCL_TT - 1) / TCL_TT * TCL_TT;
+  if (e == cudaSuccess) e = cudaMalloc(&bt->tcl_b, (size_t)tcl_seqs * 4 * C * 4);
   if (e != cudaSuccess) {
     llmq_batch_free(bt);
     return fail(ctx, LLMQ_ERR_NOMEM, std::string("batch alloc: ") + cudaGetErrorString(e));
@@ -2534,6 +2633,8 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
                         (const void *)bgemv_rows_kernel<FMT_BLK4, 4>, (const void *)bgemv_rows_kernel<FMT_GEN8, 1>,
                         (const void *)bgemv_rows_kernel<FMT_GEN8, 2>, (const void *)bgemv_rows_kernel<FMT_GEN8, 4>})
     attr(k, kBgemvSmem);
+  attr((const void *)tcl_gemm_kernel<TCL_BLK4, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
+  attr((const void *)tcl_gemm_kernel<TCL_CH8, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
   if (e != cudaSuccess) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);
@@ -2541,7 +2642,18 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
     return fail(ctx, LLMQ_ERR_CUDA, std::string("batch attributes: ") + cudaGetErrorString(e) +
                                         " (shared memory per block up to " + std::to_string(optin) + ")");
   }
+  llmq_status pst = batch_prepare_tcl(bt);
+  if (pst != LLMQ_OK) {
+    llmq_batch_free(bt);
+    return pst;
+  }
   *out = bt;
+  return LLMQ_OK;
+}
+
+llmq_status llmq_batch_set_kernel(llmq_batch *bt, int kind) {
+  if (!bt || kind < LLMQ_BATCH_AUTO || kind > LLMQ_BATCH_TCGEN05) return LLMQ_ERR_INVALID;
+  bt->kernel = kind;
   return LLMQ_OK;
 }
 
@@ -2551,7 +2663,8 @@ llmq_status llmq_batch_free(llmq_batch *bt) {
   if (bt->exec) cudaGraphExecDestroy(bt->exec);
   if (bt->graph) cudaGraphDestroy(bt->graph);
   void *ps[] = {bt->kv.k, bt->kv.v, bt->kv.ks, bt->kv.vs, bt->x, bt->xn, bt->qkv, bt->att, bt->fc, bt->logits,
-                bt->xq, bt->xsf, bt->xsi, bt->sx, bt->tokens, bt->ids, bt->state, bt->part_val, bt->part_idx};
+                bt->xq, bt->xsf, bt->xsi, bt->sx, bt->tokens, bt->ids, bt->state, bt->part_val, bt->part_idx,
+                bt->tcl_b};
   for (void *p : ps)
     if (p) cudaFree(p);
   if (bt->ids_host) cudaFreeHost(bt->ids_host);

@@ -150,6 +150,14 @@ class Batch:
         check(lib().llmq_batch_create(model.ctx.h, model.h, max_seqs, max_prompt, C.byref(h)), model.ctx.h)
         self.h = h
 
+    KERNELS = {"auto": 0, "cuda_core": 1, "tcgen05": 2}
+
+    def set_kernel(self, kind: str):
+        """Which kernel runs the batched one-token matmuls: 'auto' (the
+        lane-mode tcgen05 GEMM from 16 sequences on), 'cuda_core' (dp2a
+        batched GEMVs) or 'tcgen05' (the GEMM at any count)."""
+        check(lib().llmq_batch_set_kernel(self.h, self.KERNELS[kind]), self.model.ctx.h)
+
     def generate(self, prompts, steps: int) -> np.ndarray:
         """prompts [B, P] token ids (host); returns ids [B, steps]."""
         p = np.ascontiguousarray(prompts, dtype=np.int32)
@@ -179,38 +187,60 @@ class Batch:
 
 
 # Float formats of the perplexity harness (gpt2t.mojo:1180-1270): the layer
-# format, its head and the cache that default_kv picks for it.
+# format, its head and the cache that default_kv picks for it. The affine
+# W4A32 / W8A32 formats (an int --dtype without -a16, e.g. 'int4-g32') are
+# accepted besides these.
 FLOAT_FORMATS = ("f32", "bf16", "gguf-q4_k")
+
+
+def affine_float_format(fmt: str):
+    """(bits, group, sym) of an affine dtype without -a16, else None."""
+    try:
+        bits, group, sym, a16 = parse_dtype(fmt)
+    except ValueError:
+        return None
+    return None if a16 else (bits, group, sym)
 
 
 class FloatModel:
     """Model[W, E, KV] for the float-activation formats, run through
     forward_all (evaluation): 'f32' (DenseMatrix[float32] layers and head,
-    DenseKV[float32]), 'bf16' (DenseMatrix[bfloat16], DenseKV[bfloat16]) and
+    DenseKV[float32]), 'bf16' (DenseMatrix[bfloat16], DenseKV[bfloat16]),
     'gguf-q4_k' (GGUF Q4_K layers, Q6_K head, the int8 cache: the layout of a
-    Q4_K_M file). Weights are converted from float32 tensors as the
+    Q4_K_M file), and the affine W4A32 / W8A32 formats such as 'int4-g32'
+    (QuantMatrix layers without -a16, the int8 cache, and head='int8' for
+    HEAD8 = QuantMatrix[8, 0] or 'same' for the layer format: run_quantized,
+    gpt2t.mojo:1280-1292). Weights are converted from float32 tensors as the
     reference's loaders do."""
 
     def __init__(self, ctx: Context, tensors: dict, fmt: str, n_layer: int = synth.N_LAYER,
-                 max_t: int = synth.MAX_T):
+                 max_t: int = synth.MAX_T, head: str = "int8", kv: str = "auto"):
         from . import gguf_blocks as G
         from ._lib import KV_BF16, KV_F32
         from .tensor import DenseMatrix, GGUFMatrix
 
-        if fmt not in FLOAT_FORMATS:
+        aff = affine_float_format(fmt)
+        if fmt not in FLOAT_FORMATS and aff is None:
             raise ValueError(f"unknown float format {fmt}")
         self.ctx, self.fmt, self.n_layer = ctx, fmt, n_layer
         self.mats = []
         for l in range(n_layer):
             for name in synth.MAT_NAMES:
                 w = tensors[f"h.{l}.{name}"]  # [IN, OUT]
-                if fmt == "gguf-q4_k":
+                if aff is not None:
+                    self.mats.append(QuantMatrix.from_f32(ctx, w, *aff, False, True))
+                elif fmt == "gguf-q4_k":
                     self.mats.append(GGUFMatrix(ctx, G.Q4_K, G.quantize(np.ascontiguousarray(w.T), G.Q4_K),
                                                 w.shape[1], w.shape[0]))
                 else:
                     self.mats.append(DenseMatrix(ctx, fmt, w))
         wte = tensors["wte.weight"]
-        if fmt == "gguf-q4_k":
+        if aff is not None:
+            hfmt = (8, 0, False) if head == "int8" else aff
+            self.head = QuantMatrix.from_f32(ctx, wte, *hfmt, False, False)
+            # default_kv of a quantized format is int8; --kv f32 / bf16 also run
+            kind = {"auto": KV_QUANT8, "int8": KV_QUANT8, "f32": KV_F32, "bf16": KV_BF16}[kv]
+        elif fmt == "gguf-q4_k":
             self.head = GGUFMatrix(ctx, G.Q6_K, G.quantize(wte, G.Q6_K), wte.shape[0], wte.shape[1])
             kind = KV_QUANT8
         else:

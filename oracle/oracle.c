@@ -1539,12 +1539,71 @@ OQ_EXPORT void oq_dense_head_rows(int dt, const void *w, const float *h, float *
 /* matmul_rows for T > 1 (kernels.mojo:325-358) of a GGUF matrix [OUT rows of
  * row_bytes]: rows of 32 outputs dequantized and run through mm_tile's
  * chain; the OUT % 32 leftover rows through rows_dot (:361-397). */
+typedef void (*oq_row_dequant)(const void *w, int row, int IN, float *dst);
+typedef float (*oq_row_dot)(const void *w, int row, int IN, const float *x);
+
+static void rows_matmul(oq_row_dequant deq, oq_row_dot dot, const void *w, const float *x, const float *b, float *out,
+                        int T, int IN, int OUT, int resid, int gelu);
+
+struct gguf_rows {
+  int type;
+  const uint8_t *rows;
+  long row_bytes;
+};
+
+static void gguf_row_deq(const void *w, int row, int IN, float *dst) {
+  const struct gguf_rows *g = (const struct gguf_rows *)w;
+  oq_gguf_dequant_row(g->type, g->rows + (long)row * g->row_bytes, IN, dst);
+}
+
+static float gguf_row_dot(const void *w, int row, int IN, const float *x) {
+  const struct gguf_rows *g = (const struct gguf_rows *)w;
+  return oq_gguf_dot_row(g->type, g->rows + (long)row * g->row_bytes, IN, x);
+}
+
+static void affine_row_deq(const void *w, int row, int IN, float *dst) {
+  (void)IN;
+  oq_dequant_row((const oq_qmat *)w, row, dst);
+}
+
+static float affine_row_dot(const void *w, int row, int IN, const float *x) {
+  (void)IN;
+  return oq_dot_row((const oq_qmat *)w, row, x);
+}
+
 OQ_EXPORT void oq_gguf_matmul_rows(int type, const uint8_t *rows, long row_bytes, const float *x, const float *b,
                                    float *out, int T, int IN, int OUT, int resid, int gelu) {
+  struct gguf_rows g = {type, rows, row_bytes};
+  rows_matmul(gguf_row_deq, gguf_row_dot, &g, x, b, out, T, IN, OUT, resid, gelu);
+}
+
+/* matmul_rows for T > 1 (kernels.mojo:325-358) of an affine W4A32 / W8A32
+ * QuantMatrix (OUT_MAJOR, not A16): each row dequantized by dequant_row
+ * (tensor.mojo:431-479, (u - zp) * scale per value), then the same mm_tile
+ * chain and rows_dot leftovers as the GGUF matrices. The output head of such
+ * a model for T > 1 (kernels.mojo:677-689 head) is this with no bias. */
+OQ_EXPORT void oq_affine_matmul_rows(const oq_qmat *w, const float *x, const float *b, float *out, int T, int IN,
+                                     int OUT, int resid, int gelu) {
+  rows_matmul(affine_row_deq, affine_row_dot, w, x, b, out, T, IN, OUT, resid, gelu);
+}
+
+/* matmul_rows (kernels.mojo:285-358): one token takes each row's dot_row
+ * (+ bias); several take the dequantized rows through mm_tile's chain, the
+ * OUT % 32 leftover rows through rows_dot. */
+static void rows_matmul(oq_row_dequant deq, oq_row_dot dot, const void *w, const float *x, const float *b, float *out,
+                        int T, int IN, int OUT, int resid, int gelu) {
+  if (T == 1) {
+    for (int o = 0; o < OUT; o++) {
+      float r = dot(w, o, IN, x);
+      if (b) r += b[o];
+      finish(out, o, r, resid, gelu);
+    }
+    return;
+  }
   float *wd = (float *)malloc(sizeof(float) * IN);
   int full = OUT / 32 * 32;
   for (int o = 0; o < OUT; o++) {
-    oq_gguf_dequant_row(type, rows + (long)o * row_bytes, IN, wd);
+    deq(w, o, IN, wd);
     for (int t = 0; t < T; t++) {
       const float *xt = x + (long)t * IN;
       float r;

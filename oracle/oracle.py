@@ -91,6 +91,7 @@ def _declare(L):
         "oq_dense_mm": (V, [I, P, P, P, P, I, I, I, I, I]),
         "oq_dense_head_rows": (V, [I, P, P, P, I, I, I]),
         "oq_gguf_matmul_rows": (V, [I, P, C.c_long, P, P, P, I, I, I, I, I]),
+        "oq_affine_matmul_rows": (V, [P, P, P, P, I, I, I, I, I]),
         "oq_dkv_attend_one": (V, [I, P, P, I, I, P, P, I, I, I]),
         "oq_score_rows": (V, [P, P, P, I, I, I, P, I]),
     }

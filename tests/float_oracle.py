@@ -17,11 +17,16 @@ def _prep(key, make):
     return _PREP[key]
 
 
-def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
+def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None, head_fmt="int8", kv="auto"):
     """The float model's forward_all composed from oracle kernels; head (GGUF
-    only) is an untied [V, C] output matrix, the logits' Q6_K head."""
+    only) is an untied [V, C] output matrix, the logits' Q6_K head. fmt may
+    also be an affine W4A32 / W8A32 dtype ('int4-g32', 'int8-ch', ...): its
+    layers and head (head_fmt 'int8' = QuantMatrix[8, 0], or 'same') through
+    QuantMatrix.dequant_row / dot_row and matmul_rows, the int8 cache (kv
+    'auto') or DenseKV[float32] (kv 'f32')."""
     from llm_mojo_b200 import gguf_blocks as G
     from llm_mojo_b200 import synth
+    from llm_mojo_b200.model import affine_float_format
 
     T, Cn, NH, HS = len(tokens), 768, 12, 64
     small = synth.small_floats(tensors, n_layer)
@@ -34,8 +39,8 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
         b = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
         return ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)
 
-    def wdata(a):
-        return np.ascontiguousarray(a, dtype=np.float32) if fmt == "f32" else bf16(a)
+    def wdata(a):  # dense weights and DenseKV entries: float32 (dt 0) or bfloat16 (dt 2)
+        return np.ascontiguousarray(a, dtype=np.float32) if dt == 0 else bf16(a)
 
     def wdata_cached(a):
         return _prep((fmt, id(a), "w"), lambda: (a, wdata(a)))[1]
@@ -44,9 +49,21 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
         return _prep((t, id(a), transpose), lambda: (a, G.quantize(np.ascontiguousarray(a.T if transpose else a,
                                                                                        dtype=np.float32), t)))[1]
 
+    aff = affine_float_format(fmt)
+    if aff is not None and kv not in ("auto", "f32"):
+        raise ValueError("the oracle's affine model takes the int8 (auto) or float32 cache")
+
+    def aq_cached(a, spec, reduce_rows):
+        return _prep((spec, id(a), reduce_rows), lambda: (a, O.QuantMatrix(a, *spec, False, reduce_rows)))[1]
+
     wte = tensors["wte.weight"]
     dt = DT.get(fmt, 0)
-    if fmt == "gguf-q4_k":
+    if aff is not None:
+        hq = aq_cached(wte, (8, 0, False) if head_fmt == "int8" else aff, False)
+        emb = np.zeros((T, Cn), np.float32)
+        for i, tok in enumerate(tokens):
+            O.lib().oq_dequant_row(O.C.byref(hq.q), int(tok), O.ptr(emb[i]))
+    elif fmt == "gguf-q4_k":
         hb = q_cached(wte, G.Q6_K, False)
         emb = np.zeros((T, Cn), np.float32)
         for i, tok in enumerate(tokens):
@@ -55,12 +72,17 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
         wd = wdata_cached(wte)
         emb = (wd.astype(np.float32) if fmt == "f32" else (wd.astype(np.uint32) << 16).view(np.float32))[tokens]
     x = (emb + wpe[:T]).astype(np.float32)
-    kv8 = O.lib().oq_qkv8_new(n_layer, 1024, NH, HS) if fmt == "gguf-q4_k" else None
+    kv8 = O.lib().oq_qkv8_new(n_layer, 1024, NH, HS) if fmt == "gguf-q4_k" or (aff is not None and kv == "auto") \
+        else None
 
     def mm(w, xin, b, OUT, resid=None, gelu=False):
         Tn, IN = xin.shape
         out = resid.copy() if resid is not None else np.zeros((Tn, OUT), np.float32)
-        if fmt == "gguf-q4_k":
+        if aff is not None:
+            O.lib().oq_affine_matmul_rows(O.C.byref(aq_cached(w, aff, True).q), O.ptr(xin),
+                                          O.ptr(np.ascontiguousarray(b)), O.ptr(out), Tn, IN, OUT,
+                                          int(resid is not None), int(gelu))
+        elif fmt == "gguf-q4_k":
             blocks = q_cached(w, G.Q4_K, True)
             O.lib().oq_gguf_matmul_rows(G.Q4_K, O.ptr(blocks), G.row_bytes(G.Q4_K, IN), O.ptr(xin),
                                         O.ptr(np.ascontiguousarray(b)), O.ptr(out), Tn, IN, OUT,
@@ -94,7 +116,12 @@ def oracle_float_forward(tensors, fmt, tokens, n_layer, head=None):
     xn = O.layernorm(x, lnf_w, lnf_b)
     V = wte.shape[0]
     logits = np.zeros((T, V), np.float32)
-    if fmt == "gguf-q4_k":
+    if aff is not None:
+        O.lib().oq_affine_matmul_rows(O.C.byref(hq.q), O.ptr(np.ascontiguousarray(xn)), None, O.ptr(logits), T, Cn, V,
+                                      0, 0)
+        if kv8 is not None:
+            O.lib().oq_qkv8_free(kv8)
+    elif fmt == "gguf-q4_k":
         if head is not None:
             hb = G.quantize(np.ascontiguousarray(head, dtype=np.float32), G.Q6_K)
         for t in range(T):

@@ -133,12 +133,16 @@ def main(ref_root: str):
         configure(ref, kv="int8")
         out["kvq_int8"] = ref.kvq(kv)
 
-        # 3. Whole-model logits and greedy ids: f32, and int4-g32-a16 with an
-        # int8 head and int8 KV cache (gpt2t --dtype int4-g32-a16 defaults).
+        # 3. Whole-model logits and greedy ids: f32; int4-g32-a16 with an
+        # int8 head and int8 KV cache (gpt2t --dtype int4-g32-a16 defaults);
+        # int4-g32 (W4A32: the same weights, float activations, the int8
+        # head, and the float32 cache of gpt2t --dtype int4-g32 --kv f32, so
+        # that no int8 KV rounding flips enter the float comparison).
         prompt = np.random.default_rng(2).integers(0, synth.V, size=24).astype(np.int64)
         out["prompt24"] = prompt.astype(np.int32)
         for tag, cfg in [("f32", {}),
-                         ("a16", dict(quant=(4, 32, False), quant_head=(8, 0, False), act16=True, kv="int8"))]:
+                         ("a16", dict(quant=(4, 32, False), quant_head=(8, 0, False), act16=True, kv="int8")),
+                         ("wa32", dict(quant=(4, 32, False), quant_head=(8, 0, False), act16=False, kv="f32"))]:
             configure(ref, **cfg)
             model_goldens(ref, out, tag, prompt)
 

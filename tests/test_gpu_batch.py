@@ -67,3 +67,49 @@ def test_batch_rejects_oversized_calls(gpu_model):
             bt.generate(np.full((2, 4), 50257, dtype=np.int32), 2)
     finally:
         bt.free()
+
+
+@pytest.mark.parametrize("B,P,steps", [(40, 12, 10), (1, 3, 6), (33, 7, 5)])
+def test_batch_tcgen05_matches_cuda_core_and_single_decode(gpu_model, B, P, steps):
+    """The lane-mode tcgen05 GEMM (the layers' BLOCKED int4-g32 rows and the
+    int8 head as MMAs with one lane per K-step half) and the dp2a batched
+    GEMVs give the same ids, equal to each sequence's single decode; counts
+    below, at and past one 32-sequence tile."""
+    from llm_mojo_b200 import synth
+    from llm_mojo_b200.model import Batch
+
+    prompts = synth.uniform_ids(B * P, 11 + B).reshape(B, P)
+    bt = Batch(gpu_model, 48, 16)
+    try:
+        bt.set_kernel("tcgen05")
+        tc = bt.generate(prompts, steps)
+        bt.set_kernel("cuda_core")
+        cc = bt.generate(prompts, steps)
+        bt.set_kernel("auto")
+        auto = bt.generate(prompts, steps)
+    finally:
+        bt.free()
+    assert np.array_equal(tc, cc)
+    assert np.array_equal(auto, tc)
+    for b in sorted({0, B // 2, B - 1}):
+        assert list(tc[b]) == list(gpu_model.generate(list(prompts[b]), steps)), f"sequence {b}"
+
+
+def test_config3_shape_batch_matches_oracle(gpu_model, oracle_a16):
+    """Config 3's sequence shape: 32 sequences of a 128-token uniform prompt
+    (seed 3, the bench's first 32) and 128 greedy tokens through the default
+    kernels: every sequence equals its single decode, three equal the CPU
+    oracle's."""
+    from llm_mojo_b200 import synth
+    from llm_mojo_b200.model import Batch
+
+    prompts = synth.uniform_ids(256 * 128, 3).reshape(256, 128)[:32]
+    bt = Batch(gpu_model, 32, 128)
+    try:
+        got = bt.generate(prompts, 128)
+    finally:
+        bt.free()
+    for b in range(32):
+        assert list(got[b]) == list(gpu_model.generate(list(prompts[b]), 128)), f"sequence {b}"
+    for b in (0, 15, 31):
+        assert list(got[b]) == list(oracle_a16.generate(list(prompts[b]), 128)), f"sequence {b} (oracle)"

@@ -1,7 +1,8 @@
 """Float-activation several-token paths (the perplexity harness's formats)
 against the CPU oracle, bit for bit: the dense matmul tile (f32 / bf16), the
-dense head for every position, GGUF rows for several tokens, the dense KV
-caches, a whole float model's forward_all, and the scores."""
+dense head for every position, GGUF and affine W4A32 / W8A32 rows for
+several tokens, the dense KV caches, a whole float model's forward_all, and
+the scores."""
 
 import ctypes as C
 
@@ -132,20 +133,85 @@ def test_dense_kv_attention_bit_exact(torch, ctx, dt, npos0, T):
         kv.free()
 
 
-@pytest.mark.parametrize("fmt", ["f32", "bf16", "gguf-q4_k"])
-def test_float_model_forward_all_bit_exact(torch, ctx, gpt2_tensors, fmt):
+@pytest.mark.parametrize("fmt", ["int4-g32", "int4-g128-sym", "int4-ch", "int8-ch", "int8-g64"])
+@pytest.mark.parametrize("T,OUT,epi", [(9, 70, "gelu"), (33, 2304, "resid"), (2, 768, "plain")])
+def test_affine_rows_several_tokens_bit_exact(torch, ctx, fmt, T, OUT, epi):
+    """matmul_rows for T > 1 of the W4A32 / W8A32 formats (kernels.mojo:
+    325-397): dequantized rows through the mm_tile chain, the OUT % 32
+    leftover rows through rows_dot; the same bits as the oracle."""
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix, parse_dtype
+
+    bits_, group, sym, _ = parse_dtype(fmt)
+    IN = 768
+    rng = np.random.default_rng(OUT * 5 + T)
+    src = (rng.standard_normal((IN, OUT)) * 0.02).astype(np.float32)  # [IN, OUT]
+    ow = O.QuantMatrix(src, bits_, group, sym, False, True)
+    gw = QuantMatrix.from_f32(ctx, src, bits_, group, sym, False, True)
+    x = rng.standard_normal((T, IN)).astype(np.float32)
+    b = rng.standard_normal(OUT).astype(np.float32)
+    resid = rng.standard_normal((T, OUT)).astype(np.float32)
+    want = resid.copy() if epi == "resid" else np.zeros((T, OUT), np.float32)
+    O.lib().oq_affine_matmul_rows(C.byref(ow.q), O.ptr(x), O.ptr(b), O.ptr(want), T, IN, OUT, int(epi == "resid"),
+                                  int(epi == "gelu"))
+    out = dev(torch, resid) if epi == "resid" else torch.zeros((T, OUT), dtype=torch.float32, device="cuda")
+    try:
+        kernels.linear(ctx, out, dev(torch, x), gw, dev(torch, b), T, IN, OUT, resid=epi == "resid",
+                       gelu=epi == "gelu")
+        same(out.cpu().numpy(), want)
+    finally:
+        gw.free()
+
+
+@pytest.mark.parametrize("fmt", ["int8-ch", "int4-g32"])
+def test_affine_head_several_tokens_bit_exact(torch, ctx, fmt):
+    """head (kernels.mojo:677-689) of an OUT_MAJOR affine matrix for T > 1:
+    matmul_rows with no bias (4113 rows: 17 leftover rows on rows_dot), not
+    T one-token dots; T = 1 stays the dot_row path."""
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix, parse_dtype
+
+    bits_, group, sym, _ = parse_dtype(fmt)
+    V, Cn, T = 4113, 768, 3
+    rng = np.random.default_rng(21)
+    w = (rng.standard_normal((V, Cn)) * 0.02).astype(np.float32)
+    ow = O.QuantMatrix(w, bits_, group, sym, False, False)
+    gw = QuantMatrix.from_f32(ctx, w, bits_, group, sym, False, False)
+    h = rng.standard_normal((T, Cn)).astype(np.float32)
+    try:
+        for n in (T, 1):
+            want = np.zeros((n, V), np.float32)
+            O.lib().oq_affine_matmul_rows(C.byref(ow.q), O.ptr(h[:n]), None, O.ptr(want), n, Cn, V, 0, 0)
+            logits = torch.zeros((n, V), dtype=torch.float32, device="cuda")
+            kernels.head(ctx, logits, dev(torch, h[:n]), gw, n, V, Cn)
+            same(logits.cpu().numpy(), want)
+    finally:
+        gw.free()
+
+
+@pytest.mark.parametrize("fmt,kv,T", [("f32", "auto", 20), ("bf16", "auto", 20), ("gguf-q4_k", "auto", 20),
+                                      ("int4-g32", "auto", 20), ("int4-g32", "f32", 20), ("int8-ch", "auto", 20),
+                                      ("int4-g128-sym", "auto", 20), ("gguf-q4_k", "auto", 1),
+                                      ("int4-g32", "auto", 1), ("int8-ch", "f32", 1)])
+def test_float_model_forward_all_bit_exact(torch, ctx, gpt2_tensors, fmt, kv, T):
+    """forward_all of a 2-layer model, bit for bit with the oracle's; the
+    affine W4A32 / W8A32 models with the int8 (auto) or float32 cache. One
+    token takes every OUT_MAJOR matrix's one-token path (dot_row), as the
+    reference's matmul_rows does for T = 1 (the dense formats' T = 1 gemv is
+    tested on its own, test_gpu_formats.py)."""
     from llm_mojo_b200.model import FloatModel
 
-    n_layer, T = 2, 20
+    n_layer = 2
     tokens = np.random.default_rng(8).integers(0, 50257, T).astype(np.int32)
-    m = FloatModel(ctx, gpt2_tensors, fmt, n_layer=n_layer, max_t=64)
+    kw = {} if kv == "auto" else {"kv": kv}
+    m = FloatModel(ctx, gpt2_tensors, fmt, n_layer=n_layer, max_t=64, **kw)
     try:
         logits = torch.zeros((T, m.V), dtype=torch.float32, device="cuda")
         m.forward_all(tokens, logits)
         got = logits.cpu().numpy()
     finally:
         m.free()
-    same(got, oracle_float_forward(gpt2_tensors, fmt, list(tokens), n_layer))
+    same(got, oracle_float_forward(gpt2_tensors, fmt, list(tokens), n_layer, **kw))
 
 
 def test_score_rows_match_oracle(torch, ctx):
@@ -170,7 +236,7 @@ def test_score_rows_match_oracle(torch, ctx):
     np.testing.assert_allclose(got, want, rtol=1e-11, atol=1e-12)
 
 
-@pytest.mark.parametrize("fmt,tag", [("f32", "f32"), ("bf16", "bf16"), ("gguf-q4_k", "gguf")])
+@pytest.mark.parametrize("fmt,tag", [("f32", "f32"), ("bf16", "bf16"), ("gguf-q4_k", "gguf"), ("int4-g32", "wa32")])
 def test_float_model_matches_reference_goldens(torch, ctx, gpt2_tensors, golden, fmt, tag):
     """The whole 12-layer device model against the reference's own NumPy
     GPT-2 (golden/reference_py.npz): logits at all 24 prompt positions and
@@ -179,7 +245,7 @@ def test_float_model_matches_reference_goldens(torch, ctx, gpt2_tensors, golden,
     from llm_mojo_b200.model import FloatModel
 
     prompt = np.ascontiguousarray(golden["prompt24"], dtype=np.int32)
-    m = FloatModel(ctx, gpt2_tensors, fmt, max_t=64)
+    m = FloatModel(ctx, gpt2_tensors, fmt, max_t=64, **({"kv": "f32"} if tag == "wa32" else {}))
     try:
         logits = torch.zeros((24, m.V), dtype=torch.float32, device="cuda")
         m.forward_all(prompt, logits)

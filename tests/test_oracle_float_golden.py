@@ -7,7 +7,11 @@ made by golden/make_golden.py):
   (reference.py on bfloat16-rounded weights with --kv bf16);
 - gguf: a GGUF file of the weights, Q4_K layers and a Q6_K tied head,
   int8 KV cache (reference.py --gguf, which dequantizes with gguf-py and
-  gives the Q6_K head int16 inputs, as gpt2t computes it).
+  gives the Q6_K head int16 inputs, as gpt2t computes it);
+- wa32: int4-g32 W4A32 (reference.py's fake-quantized int4-g32 layers and
+  int8-ch head with float activations, float32 KV cache: gpt2t --dtype
+  int4-g32 --kv f32; with the int8 cache, rounding flips of single cache
+  entries move the first positions' logits by up to 2e-3 of the largest).
 
 The tolerance is north_star's for float formats: max |logit - reference| <=
 1e-3 * max |logit| (checked at the reference's top logits), and the same
@@ -21,7 +25,8 @@ import pytest
 from float_oracle import oracle_float_forward
 
 TOL = 1e-3
-FORMATS = [("f32", "f32"), ("bf16", "bf16"), ("gguf-q4_k", "gguf")]
+FORMATS = [("f32", "f32"), ("bf16", "bf16"), ("gguf-q4_k", "gguf"), ("int4-g32", "wa32")]
+KW = {"int4-g32": {"kv": "f32"}}  # the cache the golden was made with
 
 
 @pytest.fixture(scope="module")
@@ -30,7 +35,7 @@ def p24_logits(gpt2_tensors, golden):
     all-positions logits of the prompt's first 16 tokens: the model is
     causal and every row's arithmetic is independent of later rows)."""
     prompt = [int(v) for v in golden["prompt24"]]
-    return {fmt: oracle_float_forward(gpt2_tensors, fmt, prompt, 12) for fmt, _ in FORMATS}
+    return {fmt: oracle_float_forward(gpt2_tensors, fmt, prompt, 12, **KW.get(fmt, {})) for fmt, _ in FORMATS}
 
 
 def _check_rows(logits, ids, vals, scale):
@@ -55,7 +60,7 @@ def test_float_model_greedy_ids_match_reference(gpt2_tensors, golden, fmt, tag):
     against the reference's at the tolerance."""
     toks = [50256]
     for i in range(8):
-        lg = oracle_float_forward(gpt2_tensors, fmt, toks, 12)[-1]
+        lg = oracle_float_forward(gpt2_tensors, fmt, toks, 12, **KW.get(fmt, {}))[-1]
         if i == 0:
             _check_rows(lg, golden[f"{tag}_eot_top_ids"], golden[f"{tag}_eot_top_vals"], golden[f"{tag}_eot_max"])
         toks.append(int(np.argmax(lg)))
