@@ -2266,7 +2266,7 @@ namespace {
 
 int fmt_code(const llmq_weight *w) { return fmt_of(w->view()); }
 
-constexpr int TCL_TT = 32;          // sequences per lane-mode GEMM tile
+constexpr int TCL_TT = 16;          // sequences per lane-mode GEMM tile
 constexpr int TCL_MIN_SEQS = 16;    // AUTO: the lane-mode GEMM from this many sequences
 
 // Whether batch_linear runs w for B sequences as the lane-mode tcgen05 GEMM.
@@ -2279,7 +2279,7 @@ bool batch_uses_tcl(const llmq_batch *bt, const llmq_weight *w, int B) {
 // kernel that runs it).
 int batch_head_parts(const llmq_batch *bt, int B) {
   const llmq_model *m = bt->m;
-  return batch_uses_tcl(bt, m->head, B) ? (m->V + TC_M - 1) / TC_M : (m->V + BG_ROWS - 1) / BG_ROWS;
+  return batch_uses_tcl(bt, m->head, B) ? 4 * ((m->V + TC_M - 1) / TC_M) : (m->V + BG_ROWS - 1) / BG_ROWS;
 }
 
 // quantize_rows (+ LayerNorm) of B rows into the lane-mode GEMM's sequence
@@ -2315,12 +2315,17 @@ llmq_status batch_linear_tcl(llmq_batch *bt, const llmq_weight *w, const float *
   a.nkb = K / TC_KB;
   a.nseg = K / 32;
   a.epi = epi;
-  const dim3 grid(bpad / TCL_TT, (v.rows + TC_M - 1) / TC_M);
+  a.ntiles = (v.rows + TC_M - 1) / TC_M;
+  a.nparts = 4 * a.ntiles;
+  // one CTA per SM: the sequence tiles times as many row-tile columns as
+  // fit, each CTA looping over its column's row tiles
+  const int stiles = bpad / TCL_TT;
+  const dim3 grid(stiles, std::min(a.ntiles, std::max(1, ctx->num_sms / stiles)));
   const size_t sm = sizeof(TcSmemL<TCL_TT>) + 1024;
   if (mode == TCL_BLK4)
-    tcl_gemm_kernel<TCL_BLK4, TCL_TT><<<grid, TC_THREADS, sm, s>>>(a);
+    tcl_gemm_kernel<TCL_BLK4, TCL_TT><<<grid, TCL_THREADS, sm, s>>>(a);
   else
-    tcl_gemm_kernel<TCL_CH8, TCL_TT><<<grid, TC_THREADS, sm, s>>>(a);
+    tcl_gemm_kernel<TCL_CH8, TCL_TT><<<grid, TCL_THREADS, sm, s>>>(a);
   CKL();
   return LLMQ_OK;
 }
@@ -2601,7 +2606,9 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
   if (e == cudaSuccess) e = cudaMalloc(&bt->tokens, rows * 4);
   if (e == cudaSuccess) e = cudaMalloc(&bt->ids, (size_t)max_seqs * m->max_t * 4);
   if (e == cudaSuccess) e = cudaMalloc(&bt->state, 2 * sizeof(int));
-  const size_t nparts = (size_t)(m->V + BG_ROWS - 1) / BG_ROWS;
+  // argmax partials per sequence: the CUDA-core head's row tiles or the
+  // lane-mode GEMM's four lane quarters per row tile
+  const size_t nparts = std::max((size_t)(m->V + BG_ROWS - 1) / BG_ROWS, (size_t)4 * ((m->V + TC_M - 1) / TC_M));
   if (e == cudaSuccess) e = cudaMalloc(&bt->part_val, (size_t)max_seqs * nparts * 4);
   if (e == cudaSuccess) e = cudaMalloc(&bt->part_idx, (size_t)max_seqs * nparts * 4);
   if (e == cudaSuccess) e = cudaMemset(v.k, 0, seq * max_seqs);

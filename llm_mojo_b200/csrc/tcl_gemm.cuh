@@ -30,13 +30,17 @@
 // zp * sum(x). The folds keep the reference's order, so each sequence's
 // outputs equal its one-token outputs bit for bit.
 //
-// The pipeline is the transposed GEMM's (tc_gemm.cuh): 4 stages of
-// [A: 128 rows x 128 B][B: 4 TT rows x 128 B] in the 128-byte swizzle
-// layout, warp 16 issuing copies, MMAs and commits, warps 0-15 folding (warp
-// w: tensor-memory lanes = weight rows 32 * (w % 4) + lane, sequences
-// (w / 4) * TT / 4 .. + TT / 4), accumulators in rotating buffers of 4 TT
-// columns. The epilogue keeps 5 floats per (row, sequence): the pair's two
-// lane chains and the tree's partial sums.
+// The kernel is persistent over row tiles: CTA (sequence tile, column c)
+// takes row tiles c, c + gridDim.y, ... and streams their K blocks as units
+// of 4 K steps. Two producer warps (16, 17) take alternate units: each
+// copies its units' [A: 128 rows x 128 B][B: 4 TT rows x 128 B] tiles (the
+// 128-byte swizzle layout) through its own 3 stages, issues the unit's 8 MMAs
+// into its own tensor-memory buffer (4 K steps x 4 TT columns) and commits
+// once per unit, so one producer's waits and issue latency overlap the
+// other's. Warps 0-15 fold (warp w: tensor-memory lanes = weight rows
+// 32 * (w % 4) + lane, sequences (w / 4) * TT / 4 .. + TT / 4). The int4
+// rows' accumulators start at a float-magic bias so that reading them as
+// floats needs one subtraction, and the pair arithmetic runs on f32x2.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -65,7 +69,7 @@ __host__ __device__ __forceinline__ int tcl_col(int mode, int k, int K) {
 // Whether the lane-mode GEMM takes the matrix: BLOCKED int4-g32 A16 rows or
 // per-channel int8 A16 rows, 256-column multiples.
 __host__ __device__ inline bool tcl_supported(const WeightView &w) {
-  if (w.cols % 256 != 0) return false;
+  if (w.cols % 256 != 0 || w.cols > 4096) return false;
   if (w.bits == 4 && w.blocked && w.group == 32) return true;
   return w.bits == 8 && w.group == w.cols;
 }
@@ -95,9 +99,9 @@ __global__ void tcl_prep_a_kernel(WeightView w, int mode, uint8_t *a) {
 // quantize_rows (+ LayerNorm) of each sequence's row (kernels.mojo:400-416,
 // the one-token prologue's arithmetic in natural column order) into the B
 // tiles [sequence tile][K block][4 TT rows x 128 B]: row (plane p, half h)
-// at (2p + h) * TT + t holds, in the K step's half h, the low byte xl (p = 0)
-// or the high byte xh (p = 1) of x at column tcl_col(k), and zero in the
-// other half. Also sx[m] and, for the int8 rows, the 16 lane sums of x
+// of sequence t at p * 2 TT + 2 t + h holds, in the K step's half h, the low
+// byte xl (p = 0) or the high byte xh (p = 1) of x at column tcl_col(k), and
+// zero in the other half. Also sx[m] and, for the int8 rows, the 16 lane sums of x
 // (columns 2L, 2L + 1 of every 32-column chunk). One CTA per sequence of the
 // padded count; padding sequences get zero tiles.
 template <int TT, int PRO>
@@ -135,10 +139,10 @@ __global__ void __launch_bounds__(256) tcl_quant_pack_kernel(const float *x, con
     }
     uint8_t *kbase = tile + (size_t)kb * (4 * TT * TC_KB);
     const uint4 zero = make_uint4(0, 0, 0, 0);
-    *(uint4 *)(kbase + tc_sw128_off(half * TT + r, chunk)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *(uint4 *)(kbase + tc_sw128_off(2 * TT + half * TT + r, chunk)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *(uint4 *)(kbase + tc_sw128_off((1 - half) * TT + r, chunk)) = zero;
-    *(uint4 *)(kbase + tc_sw128_off(2 * TT + (1 - half) * TT + r, chunk)) = zero;
+    *(uint4 *)(kbase + tc_sw128_off(2 * r + half, chunk)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *(uint4 *)(kbase + tc_sw128_off(2 * TT + 2 * r + half, chunk)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *(uint4 *)(kbase + tc_sw128_off(2 * r + 1 - half, chunk)) = zero;
+    *(uint4 *)(kbase + tc_sw128_off(2 * TT + 2 * r + 1 - half, chunk)) = zero;
   }
 }
 
@@ -150,350 +154,477 @@ struct TcArgsL {
   WeightView w;
   const float *bias;  // int4 rows: [rows] or null
   float *out;         // int4 rows: [sequences][rows]
-  float *part_val;    // int8 rows: [sequences][row tiles] argmax candidates
+  float *part_val;    // int8 rows: [sequences][nparts] argmax candidates, 4 per row tile
   int *part_idx;
   int *err;
-  int B, OUT, K, nkb, nseg, epi;
+  int B, OUT, K, nkb, nseg, epi, ntiles, nparts;
 };
+
+// A CTA's units: K blocks (4 segments, one 128-byte K block of the A and B
+// tiles) of its row tiles blockIdx.y, blockIdx.y + gridDim.y, ... in order.
+// Unit u's accumulators fill tensor-memory buffer u % 2 (4 segments x 4 TT
+// columns); producer warp u % 2 issues its copies, MMAs and commits, so the
+// two producers' instruction latencies overlap and each buffer has its own
+// producer. Its copies use the producer's own stages (TCL_SPP of them).
+constexpr int TCL_NPROD = 2;
+constexpr int TCL_SPP = 3;                                       // copy stages per producer
+constexpr int TCL_STAGES = TCL_NPROD * TCL_SPP;
+constexpr int TCL_EPI = 16;                                      // epilogue warps: 4 per lane quarter
+constexpr int TCL_CG = TCL_EPI / 4;                              // sequence groups among them
+constexpr int TCL_THREADS = (TCL_EPI + TCL_NPROD) * 32;          // 192
+constexpr int TCL_MAX_SEG = 128;                                 // K steps per row: K <= 4096
+
+// What the epilogue does at K step s of a row, packed once per CTA so that
+// the loop needs no divisions: int4 rows: the scale column b * 8 + g (bits
+// 0-6), whether the pair closes (bit 7), the pair gp (bits 8-10); int8 rows:
+// the lane g (bits 0-2), whether the pair closes (bit 7), gp (bits 8-10),
+// whether each half belongs to lane g (bits 11, 12; else to lane g + 8).
+__device__ __forceinline__ int tcl_seg_entry(int mode, int s, int K) {
+  if (mode == TCL_BLK4) {
+    const int nblk = K >> 8, gp = s / nblk, b = s - gp * nblk;
+    return (b * 8 + tcl_pair_lane(gp)) | ((b == nblk - 1) << 7) | (gp << 8);
+  }
+  const int spp = K >> 8, gp = s / spp, s3 = s - gp * spp, h0 = 2 * s3;
+  return tcl_pair_lane(gp) | ((s3 == spp - 1) << 7) | (gp << 8) | ((h0 < spp) << 11) | ((h0 + 1 < spp) << 12);
+}
 
 template <int TT>
 struct TcSmemL {
-  alignas(1024) uint8_t stage[TC_STAGES][TCT_A_BYTES + 4 * TT * TC_KB];
+  alignas(1024) uint8_t stage[TCL_STAGES][TCT_A_BYTES + 4 * TT * TC_KB];
   int xsl[TT][16];
-  uint16_t scl[TC_MAX_GROUPS][TC_M];  // int4 rows: the tile's float16 scales, [group][row]
-  float cand_v[4][TT];
-  int cand_i[4][TT];
-  alignas(8) unsigned long long full[TC_STAGES], empty[TC_STAGES], accfull[TC_NBUF_MAX], accempty[TC_NBUF_MAX],
-      drain;
+  alignas(16) int seg[TCL_MAX_SEG];           // the K steps' schedule (tcl_seg_entry)
+  float tree[3][TT / TCL_CG][TCL_EPI * 32];  // the epilogue's halving-tree partial sums
+  alignas(8) unsigned long long full[TCL_STAGES], empty[TCL_STAGES], accfull[TCL_NPROD], accempty[TCL_NPROD],
+      drain[TCL_NPROD];
   unsigned tmem;
   int abort;
 };
 
-// The halving tree, fed one lane pair at a time in tcl_pair_lane order:
+
+// The halving tree is fed one lane pair at a time in tcl_pair_lane order:
 // s8 = lane g + lane g + 8; pairs (0, 4), (2, 6), (1, 5), (3, 7) make
 // s4[0], s4[2], s4[1], s4[3]; s2[0] = s4[0] + s4[2], s2[1] = s4[1] + s4[3],
-// dot = s2[0] + s2[1], left in r2 after the last pair (returns true then).
-__device__ __forceinline__ bool tcl_tree(int gp, float s8, float &p8, float &q4, float &r2) {
-  if ((gp & 1) == 0) {
-    p8 = s8;
-    return false;
-  }
-  const float s4 = p8 + s8;
-  if (gp == 1 || gp == 5) {
-    q4 = s4;
-    return false;
-  }
-  const float s2 = q4 + s4;
-  if (gp == 3) {
-    r2 = s2;
-    return false;
-  }
-  r2 = r2 + s2;
-  return true;
+// dot = s2[0] + s2[1].
+
+// Packed float pairs: the f32x2 operations of sm_100 are two independent
+// IEEE operations, each rounded to nearest once, the same as their scalar
+// forms, at one instruction per pair.
+__device__ __forceinline__ unsigned long long f2_bits(int a, int b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_pair(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(unsigned long long v, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
 }
 
-// Warps 0-15: per K step (segment) of the permuted order, the accumulators of
-// this thread's weight row and CW sequences: groups (plane p, half h) at
-// columns (2p + h) * TT. int4 rows fold lanes g and g + 8 of block b into
-// their chains and close the pair after the row's last block; int8 rows add
-// the halves into the pair's two int32 lane sums and close the pair after its
-// third K step. The row value then goes to out (int4) or to the tile's
-// argmax candidates (int8). The next segment's tensor-memory loads are in
-// flight while this one folds.
+// The int4 rows' accumulators start at TCL_MAGIC = the bits of 1.5 * 2^23:
+// the MMAs add a lane's exact int32 sum v (|v| < 2^16 per K step), and the
+// bits then read as the float 1.5 * 2^23 + v, so one float subtraction gives
+// f32(v) exactly, without a conversion.
+constexpr int TCL_MAGIC = 0x4B400000;
+constexpr float TCL_MAGIC_F = 12582912.0f;
+
+// Every column of the warp's 32 lanes in [addr, addr + W) set to v.
+template <int W>
+__device__ __forceinline__ void tc_fill(unsigned addr, int v) {
+  static_assert(W == 8 || W == 16 || W == 32, "fill widths");
+  if (W == 32)
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(addr),
+        "r"(v)
+        : "memory");
+  else if (W == 16)
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+        "%1};" ::"r"(addr),
+        "r"(v)
+        : "memory");
+  else
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(addr), "r"(v)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Warps 0-15: per segment g of the CTA's units (u = g / 4, K step g % 4),
+// the accumulators of this thread's weight row and CW sequences. Column
+// 2t + h of a plane holds sequence t's half h, so one 2 CW-column load per
+// plane gives each sequence's two lanes as an adjacent pair, and the pair's
+// arithmetic runs as f32x2. int4 rows fold lanes g and g + 8 of block b
+// into their chains and close the pair after the row's last block; int8
+// rows add the halves into the pair's two int32 lane sums and close the pair
+// after its third K step. The tree's partial sums wait in shared memory
+// (touched once per pair). After a row tile's last segment its values go to
+// out (int4) or to the argmax candidates of its four lane quarters (int8).
+// The next segment's tensor-memory loads (and int4 scale) are in flight
+// while this one folds.
 template <int MODE, int TT>
 __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, unsigned tmem, int warp, int lane,
-                                             int n0, int t0) {
-  constexpr int N = 4 * TT, NBUF = TC_TMEM_COLS / N, CW = TT / 4;
-  const int q = warp & 3, cg = warp >> 2, rl = 32 * q + lane;
-  const int n = n0 + rl;  // this thread's weight row
-  const int nr = n < p.w.rows ? n : p.w.rows - 1;
-  const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * CW;
-  float ca[CW], cb[CW], p8[CW], q4[CW], r2[CW];  // r2 ends as the row's dot
-  int ia[CW], ib[CW];  // int8 rows: the pair's lane sums
+                                             int t0, int nunits) {
+  constexpr int N = 4 * TT, KBN = 4 * N, CW = TT / TCL_CG, W = 2 * CW;
+  const int q = warp & 3, cg = warp >> 2, rl = 32 * q + lane, tid = threadIdx.x;
+  const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * W;  // low plane; the high plane at + 2 TT
+  const int nkb = p.nkb, gpr = p.K / p.w.group;
+  unsigned long long cab[CW];  // int4 rows: the pair's two lane chains
+  int ia[CW], ib[CW];          // int8 rows: the pair's two lane sums
 #pragma unroll
   for (int c = 0; c < CW; c++) {
-    ca[c] = cb[c] = p8[c] = q4[c] = r2[c] = 0.0f;
+    cab[c] = 0ull;
     ia[c] = ib[c] = 0;
   }
-  const int nblk = p.K >> 8;  // int4 rows: K steps per lane pair
-  const int spp = p.K / 256;  // int8 rows: K steps per lane pair (3 for 768 columns: 2 lanes x 48)
-  float sc8 = 0.0f;
+  float sc8 = 0.0f;  // int8 rows: the row's scale and zero point
   int zp8 = 0;
-  if (MODE == TCL_CH8) {
-    sc8 = half_bits_to_float(p.w.scale[nr]);
-    zp8 = p.w.zp[nr];
-  }
-  int d[4][CW];  // the next segment's accumulators, loads in flight while this one folds
-  // the segment being folded, its halves combined: int4 rows as floats
-  // (256 high + low), int8 rows as unsigned lane-sum increments
-  float fa[CW], fb[CW];
-  unsigned ua[CW], ub[CW];
-  auto start = [&](int seg) -> bool {
-    const int buf = seg % NBUF;
-    bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (seg / NBUF) & 1, p.err, TC_ERR_ACC);
-    ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
-    if (!ok) return false;
-    tc_fence_after();
-#pragma unroll
-    for (int g4 = 0; g4 < 4; g4++) tc_ld(tbase + buf * N + g4 * TT, d[g4]);
-    return true;
+  const unsigned long long neg_magic = f2_pair(-TCL_MAGIC_F, -TCL_MAGIC_F), k256 = f2_pair(256.0f, 256.0f);
+  auto row_of = [&](int it) {
+    const int n = (blockIdx.y + it * gridDim.y) * TC_M + rl;
+    return n < p.w.rows ? n : p.w.rows - 1;
   };
-  auto finish = [&](int seg) {
-    tc_ld_wait();
+  // int4 rows: the scales of the next unit's four K steps, loaded a unit ahead
+  unsigned scn[4] = {0, 0, 0, 0};
+  auto fetch_scales = [&](int it, int kb) {
+    const int4 e = *reinterpret_cast<const int4 *>(&sm.seg[kb * 4]);
+    const uint16_t *rs = p.w.scale + (size_t)row_of(it) * gpr;
+    scn[0] = rs[e.x & 127];
+    scn[1] = rs[e.y & 127];
+    scn[2] = rs[e.z & 127];
+    scn[3] = rs[e.w & 127];
+  };
+  // the halving tree of sequence c (the order above), its partial sums in
+  // shared memory: tree[0] the pending s8, tree[1] the pending s4, tree[2]
+  // s2[0] and then the dot
+  auto tree = [&](int gp, int c, float s8) {
+    if ((gp & 1) == 0) {
+      sm.tree[0][c][tid] = s8;
+      return;
+    }
+    const float s4 = sm.tree[0][c][tid] + s8;
+    if (gp == 1 || gp == 5) {
+      sm.tree[1][c][tid] = s4;
+      return;
+    }
+    const float s2 = sm.tree[1][c][tid] + s4;
+    if (gp == 3) {
+      sm.tree[2][c][tid] = s2;
+      return;
+    }
+    sm.tree[2][c][tid] = sm.tree[2][c][tid] + s2;
+  };
+  // the row tile's values (its last K step folded)
+  auto emit = [&](int it) {
+    const int nt = blockIdx.y + it * gridDim.y, n = nt * TC_M + rl;
+    if (MODE == TCL_BLK4) {
+      if (n >= p.OUT) return;
+      const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
 #pragma unroll
-    for (int g4 = 0; g4 < 4; g4++) tc_ld_done(d[g4]);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[seg % NBUF]));
+      for (int c = 0; c < CW; c++) {
+        const int m = t0 + cg * CW + c;
+        if (m >= p.B) break;
+        float *dst = p.out + (size_t)m * p.OUT + n;
+        float r = sm.tree[2][c][tid] * p.sx[m];
+        if (p.epi & EPI_BIAS) r += bn;
+        if (p.epi & EPI_GELU) r = gelu(r);
+        if (p.epi & EPI_RESID) r += *dst;
+        *dst = r;
+      }
+    } else {
+      // the best of the warp's 32 rows per sequence, one candidate per lane
+      // quarter and row tile
 #pragma unroll
-    for (int c = 0; c < CW; c++) {
-      if (MODE == TCL_BLK4) {
-        // |high| < 2^15, |low| < 2^16: exact floats, one rounding in the fma,
-        // as the reference's f32(lane) - zp * f32(lane sum of x)
-        fa[c] = fmaf(256.0f, tc_small_to_float(d[2][c]), tc_small_to_float(d[0][c]));
-        fb[c] = fmaf(256.0f, tc_small_to_float(d[3][c]), tc_small_to_float(d[1][c]));
-      } else {
-        ua[c] = ((unsigned)d[2][c] << 8) + (unsigned)d[0][c];
-        ub[c] = ((unsigned)d[3][c] << 8) + (unsigned)d[1][c];
+      for (int c = 0; c < CW; c++) {
+        const int m = t0 + cg * CW + c;
+        float bv = -__int_as_float(0x7f800000);
+        int bi = 0x7fffffff;
+        if (n < p.w.rows && m < p.B) {
+          bv = sm.tree[2][c][tid] * p.sx[m];
+          bi = n;
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+        if (lane == 0 && m < p.B) {
+          p.part_val[(size_t)m * p.nparts + nt * 4 + q] = bv;
+          p.part_idx[(size_t)m * p.nparts + nt * 4 + q] = bi;
+        }
       }
     }
   };
-  auto fold = [&](int seg) {
+  // one K step: its accumulators (dl, dh) and schedule entry e
+  auto step = [&](const int (&dl)[W], const int (&dh)[W], int e, unsigned sc16) {
+    const int gp = e >> 8;
     if (MODE == TCL_BLK4) {
-      const int gp = seg / nblk, b = seg - gp * nblk, g = tcl_pair_lane(gp);
-      const float sc = half_bits_to_float(sm.scl[b * 8 + g][rl]);
+      const float sc = half_bits_to_float((uint16_t)sc16);
+      const unsigned long long sc2 = f2_pair(sc, sc);
 #pragma unroll
       for (int c = 0; c < CW; c++) {
-        ca[c] = fmaf(fa[c], sc, ca[c]);
-        cb[c] = fmaf(fb[c], sc, cb[c]);
+        // |high| < 2^15, |low| < 2^16: exact floats, one rounding in the fma,
+        // as the reference's f32(lane) - zp * f32(lane sum of x)
+        const unsigned long long lo = f2_add(f2_bits(dl[2 * c], dl[2 * c + 1]), neg_magic);
+        const unsigned long long hi = f2_add(f2_bits(dh[2 * c], dh[2 * c + 1]), neg_magic);
+        cab[c] = f2_fma(f2_fma(k256, hi, lo), sc2, cab[c]);
       }
-      if (b == nblk - 1) {
+      if (e & 128) {
 #pragma unroll
         for (int c = 0; c < CW; c++) {
-          tcl_tree(gp, ca[c] + cb[c], p8[c], q4[c], r2[c]);
-          ca[c] = cb[c] = 0.0f;
+          float ca, cb;
+          f2_split(cab[c], ca, cb);
+          tree(gp, c, ca + cb);
+          cab[c] = 0ull;
         }
       }
     } else {
-      const int gp = seg / spp, s3 = seg - gp * spp, g = tcl_pair_lane(gp);
-      const int h0 = 2 * s3;  // halves [0, spp) are lane g, [spp, 2 spp) lane g + 8
+      const bool a_lo = (e >> 11) & 1, b_lo = (e >> 12) & 1;  // each half's lane: g (true) or g + 8
 #pragma unroll
       for (int c = 0; c < CW; c++) {
-        if (h0 < spp) ia[c] = (int)((unsigned)ia[c] + ua[c]);
-        else ib[c] = (int)((unsigned)ib[c] + ua[c]);
-        if (h0 + 1 < spp) ia[c] = (int)((unsigned)ia[c] + ub[c]);
-        else ib[c] = (int)((unsigned)ib[c] + ub[c]);
+        const unsigned ua = ((unsigned)dh[2 * c] << 8) + (unsigned)dl[2 * c];
+        const unsigned ub = ((unsigned)dh[2 * c + 1] << 8) + (unsigned)dl[2 * c + 1];
+        if (a_lo) ia[c] = (int)((unsigned)ia[c] + ua);
+        else ib[c] = (int)((unsigned)ib[c] + ua);
+        if (b_lo) ia[c] = (int)((unsigned)ia[c] + ub);
+        else ib[c] = (int)((unsigned)ib[c] + ub);
       }
-      if (s3 == spp - 1) {
+      if (e & 128) {
+        const int gg = e & 7;
 #pragma unroll
         for (int c = 0; c < CW; c++) {
           const int t = cg * CW + c;
-          const int a0 = (int)((unsigned)ia[c] - (unsigned)(zp8 * sm.xsl[t][g]));
-          const int a1 = (int)((unsigned)ib[c] - (unsigned)(zp8 * sm.xsl[t][g + 8]));
+          const int a0 = (int)((unsigned)ia[c] - (unsigned)(zp8 * sm.xsl[t][gg]));
+          const int a1 = (int)((unsigned)ib[c] - (unsigned)(zp8 * sm.xsl[t][gg + 8]));
           const float fx = fmaf((float)a0, sc8, 0.0f), fy = fmaf((float)a1, sc8, 0.0f);
-          tcl_tree(gp, fx + fy, p8[c], q4[c], r2[c]);
+          tree(gp, c, fx + fy);
           ia[c] = ib[c] = 0;
         }
       }
     }
   };
-  bool ok = start(0);
-  if (ok) finish(0);
-  for (int seg = 0; ok && seg < p.nseg; seg++) {
-    const bool more = seg + 1 < p.nseg;
-    if (more) ok = start(seg + 1);
-    fold(seg);
-    if (!ok || !more) break;
-    finish(seg + 1);
-  }
-  if (!ok || *(volatile int *)&sm.abort) return;
-  if (MODE == TCL_BLK4) {
-    if (n >= p.OUT) return;
-    const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
-#pragma unroll
-    for (int c = 0; c < CW; c++) {
-      const int m = t0 + cg * CW + c;
-      if (m >= p.B) break;
-      float *dst = p.out + (size_t)m * p.OUT + n;
-      float r = r2[c] * p.sx[m];
-      if (p.epi & EPI_BIAS) r += bn;
-      if (p.epi & EPI_GELU) r = gelu(r);
-      if (p.epi & EPI_RESID) r += *dst;
-      *dst = r;
+  int it = 0, kb = 0;  // the unit's row-tile iteration and K block
+  if (MODE == TCL_BLK4 && nunits > 0) fetch_scales(0, 0);
+  for (int u = 0; u < nunits; u++) {
+    const int buf = u & 1;
+    bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (u >> 1) & 1, p.err, TC_ERR_ACC);
+    ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
+    if (!ok) return;
+    tc_fence_after();
+    int dl0[W], dh0[W], dl1[W], dh1[W], dl2[W], dh2[W], dl3[W], dh3[W];
+    const unsigned tb = tbase + buf * KBN;
+    tc_ld(tb, dl0);
+    tc_ld(tb + 2 * TT, dh0);
+    tc_ld(tb + N, dl1);
+    tc_ld(tb + N + 2 * TT, dh1);
+    tc_ld(tb + 2 * N, dl2);
+    tc_ld(tb + 2 * N + 2 * TT, dh2);
+    tc_ld(tb + 3 * N, dl3);
+    tc_ld(tb + 3 * N + 2 * TT, dh3);
+    const int4 e = *reinterpret_cast<const int4 *>(&sm.seg[kb * 4]);
+    const unsigned s0 = scn[0], s1 = scn[1], s2 = scn[2], s3 = scn[3];
+    if (MODE == TCL_CH8 && kb == 0) {
+      const int nr = row_of(it);
+      sc8 = half_bits_to_float(p.w.scale[nr]);
+      zp8 = p.w.zp[nr];
     }
-  } else {
-    // the tile's argmax candidate per sequence: the best of the warp's 32
-    // rows by shuffles, then of the four warps of the sequence group
-#pragma unroll
-    for (int c = 0; c < CW; c++) {
-      const int m = t0 + cg * CW + c;
-      float bv = -__int_as_float(0x7f800000);
-      int bi = 0x7fffffff;
-      if (n < p.w.rows && m < p.B) {
-        const float v = r2[c] * p.sx[m];
-        if (better(v, n, bv, bi)) {
-          bv = v;
-          bi = n;
-        }
-      }
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (better(ov, oi, bv, bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      if (lane == 0) {
-        sm.cand_v[q][cg * CW + c] = bv;
-        sm.cand_i[q][cg * CW + c] = bi;
-      }
+    // the next unit's cursor and (int4 rows) its scales
+    int it2 = it, kb2 = kb + 1;
+    if (kb2 == nkb) {
+      kb2 = 0;
+      ++it2;
     }
+    if (MODE == TCL_BLK4 && u + 1 < nunits) fetch_scales(it2, kb2);
+    tc_ld_wait();
+    tc_ld_done(dl0);
+    tc_ld_done(dh0);
+    tc_ld_done(dl1);
+    tc_ld_done(dh1);
+    tc_ld_done(dl2);
+    tc_ld_done(dh2);
+    tc_ld_done(dl3);
+    tc_ld_done(dh3);
+    if (MODE == TCL_BLK4) {
+      // the next MMAs into this buffer accumulate onto the magic again
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        tc_fill<W>(tb + j * N, TCL_MAGIC);
+        tc_fill<W>(tb + j * N + 2 * TT, TCL_MAGIC);
+      }
+      tc_st_wait();
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[buf]));
+    step(dl0, dh0, e.x, s0);
+    step(dl1, dh1, e.y, s1);
+    step(dl2, dh2, e.z, s2);
+    step(dl3, dh3, e.w, s3);
+    if (kb == nkb - 1) emit(it);
+    it = it2;
+    kb = kb2;
   }
 }
 
-// The int8 rows' candidates of the four lane quarters, per sequence, to
-// part_val / part_idx[sequence][row tile] (after the epilogue's barrier).
-template <int TT>
-__device__ __forceinline__ void tcl_store_candidates(const TcArgsL &p, TcSmemL<TT> &sm, int t0, int nt, int ntiles) {
-  const int t = threadIdx.x;
-  if (t >= TT || t0 + t >= p.B || *(volatile int *)&sm.abort) return;
-  float bv = sm.cand_v[0][t];
-  int bi = sm.cand_i[0][t];
-  for (int k = 1; k < 4; k++)
-    if (better(sm.cand_v[k][t], sm.cand_i[k][t], bv, bi)) {
-      bv = sm.cand_v[k][t];
-      bi = sm.cand_i[k][t];
+// Producer warp pr (lane 0 issues): its units u = pr, pr + 2, ... (local
+// index k = u / 2): the copies of unit k into stage pr * TCL_SPP + k %
+// TCL_SPP, then, once buffer pr is free again and the copies landed, the
+// unit's 8 MMAs (4 K steps x the low and high rows) into buffer pr, one
+// commit for the epilogue and one for the stage; then the stage of unit k - 1
+// is refilled with unit k - 1 + TCL_SPP.
+template <int MODE, int TT>
+__device__ __forceinline__ void tcl_producer(const TcArgsL &p, TcSmemL<TT> &sm, unsigned tmem, int pr, int lane,
+                                             int nunits) {
+  constexpr int N = 4 * TT, KBN = 4 * N, BB = N * TC_KB, STAGE = TCT_A_BYTES + BB;
+  constexpr unsigned ACC = MODE == TCL_BLK4 ? 1u : 0u;  // int4 rows accumulate onto the magic
+  const bool leader = lane == 0;
+  // low rows (u8) and high rows (s8), N = 2 TT each
+  const unsigned idesc_l = tc_idesc(MODE == TCL_BLK4 ? 1 : 0, 0, 2 * TT);
+  const unsigned idesc_h = tc_idesc(MODE == TCL_BLK4 ? 1 : 0, 1, 2 * TT);
+  constexpr unsigned long long HIGH = (2 * TT * TC_KB) >> 4;  // descriptor start of the high rows
+  const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
+  const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TCT_A_BYTES);
+  const int nk = nunits > pr ? (nunits - pr + 1) / 2 : 0;
+  const uint8_t *gb = p.b + (size_t)blockIdx.x * p.nkb * BB;
+  auto stage_of = [&](int k) { return pr * TCL_SPP + k % TCL_SPP; };
+  int it_ld = 0, kb_ld = pr;  // the next load's unit 2 k + pr as (row-tile iteration, K block)
+  auto load = [&](int k) {
+    const int nt = blockIdx.y + it_ld * gridDim.y, kb = kb_ld;
+    kb_ld += 2;
+    while (kb_ld >= p.nkb) {
+      kb_ld -= p.nkb;
+      ++it_ld;
     }
-  p.part_val[(size_t)(t0 + t) * ntiles + nt] = bv;
-  p.part_idx[(size_t)(t0 + t) * ntiles + nt] = bi;
+    const int st = stage_of(k);
+    const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
+    if (leader) {
+      tc_mbar_expect_tx(bar, STAGE);
+      tc_bulk_g2s(dst, p.a + ((size_t)nt * p.nkb + kb) * TCT_A_BYTES, TCT_A_BYTES, bar);
+      tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
+    }
+    __syncwarp();
+  };
+  int issued = 0, waited = 0;
+  for (; issued < nk && issued < TCL_SPP; issued++) load(issued);
+  bool ok = true;
+  for (int k = 0; k < nk && ok; k++) {
+    const int st = stage_of(k);
+    if (k >= 1) ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[pr]), (k - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (k / TCL_SPP) & 1, p.err, TC_ERR_FULL);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    waited = k + 1;
+    tc_fence_after();
+    if (leader) {
+      const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const unsigned long long da = desc_a0 + off + (unsigned long long)(2 * j);
+        const unsigned long long db = desc_b0 + off + (unsigned long long)(2 * j);
+        const unsigned d = tmem + pr * KBN + j * N;
+        tc_mma(d, da, db, idesc_l, ACC);
+        tc_mma(d + 2 * TT, da, db + HIGH, idesc_h, ACC);
+      }
+      tc_commit(tc_u32(&sm.accfull[pr]));
+      tc_commit(tc_u32(&sm.empty[st]));
+    }
+    __syncwarp();
+    // refill the stage of unit k - 1, whose MMAs were queued ahead of these
+    if (k >= 1 && issued < nk) {
+      ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[stage_of(k - 1)]), ((k - 1) / TCL_SPP) & 1, p.err,
+                        TC_ERR_EMPTY);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      load(issued++);
+    }
+  }
+  if (!ok) {
+    // drain: copies issued but not yet waited for, then every MMA issued
+    for (int k = waited; k < issued; k++) tc_drain_wait(tc_u32(&sm.full[stage_of(k)]), (k / TCL_SPP) & 1);
+    if (leader) tc_commit(tc_u32(&sm.drain[pr]));
+    __syncwarp();
+    tc_drain_wait(tc_u32(&sm.drain[pr]), 0);
+  }
 }
 
 template <int MODE, int TT>
-__global__ void __launch_bounds__(TC_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
-  constexpr int N = 4 * TT;                  // MMA N: 4 rows per sequence
-  constexpr int NBUF = TC_TMEM_COLS / N;     // accumulator buffers in tensor memory
-  constexpr int CW = TT / 4;                 // sequences per epilogue warp
-  constexpr int BB = N * TC_KB;              // sequence-tile bytes per K block
-  constexpr int STAGE = TCT_A_BYTES + BB;
-  static_assert(CW == 8 || CW == 16, "tc_ld widths");
+__global__ void __launch_bounds__(TCL_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
+  constexpr int N = 4 * TT, KBN = 4 * N, CW = TT / TCL_CG;
+  static_assert(TCL_NPROD * KBN <= TC_TMEM_COLS, "two unit buffers of tensor memory");
+  static_assert(CW == 4 || CW == 8 || CW == 16, "tc_ld widths");
   extern __shared__ __align__(128) unsigned char tc_raw[];
   TcSmemL<TT> &sm = *reinterpret_cast<TcSmemL<TT> *>(tc_raw + ((1024u - (tc_u32(tc_raw) & 1023u)) & 1023u));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.y, tt = blockIdx.x, n0 = nt * TC_M, t0 = tt * TT;
+  const int t0 = blockIdx.x * TT;
+  const int iters = (int)blockIdx.y < p.ntiles ? (p.ntiles - 1 - (int)blockIdx.y) / (int)gridDim.y + 1 : 0;
+  const int nunits = iters * p.nkb;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < TC_STAGES; s++) {
+    for (int s = 0; s < TCL_STAGES; s++) {
       tc_mbar_init(tc_u32(&sm.full[s]), 1);
       tc_mbar_init(tc_u32(&sm.empty[s]), 1);
     }
-    for (int b = 0; b < NBUF; b++) {
+    for (int b = 0; b < TCL_NPROD; b++) {
       tc_mbar_init(tc_u32(&sm.accfull[b]), 1);
-      tc_mbar_init(tc_u32(&sm.accempty[b]), TC_EPI_WARPS);
+      tc_mbar_init(tc_u32(&sm.accempty[b]), TCL_EPI);
+      tc_mbar_init(tc_u32(&sm.drain[b]), 1);
     }
-    tc_mbar_init(tc_u32(&sm.drain), 1);
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == TC_EPI_WARPS) {
+  if (warp == TCL_EPI) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_u32(&sm.tmem)),
                  "r"(TC_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  } else if (MODE == TCL_CH8) {
-    for (int i = threadIdx.x; i < TT * 16; i += TC_EPI_WARPS * 32) {
-      const int t = t0 + i / 16;
-      sm.xsl[i / 16][i % 16] = t < p.B ? p.xsl[(size_t)t * 16 + i % 16] : 0;
-    }
-  } else {
-    // the tile's scales as [group][row] (rows past the matrix: 0)
-    const int gpr = p.K / p.w.group;
-    for (int i = threadIdx.x; i < gpr * TC_M; i += TC_EPI_WARPS * 32) {
-      const int r = i / gpr, g = i - r * gpr, row = n0 + r;
-      sm.scl[g][r] = row < p.w.rows ? p.w.scale[(size_t)row * gpr + g] : (uint16_t)0;
-    }
+  } else if (warp < TCL_EPI) {
+    if (threadIdx.x < p.nseg) sm.seg[threadIdx.x] = tcl_seg_entry(MODE, threadIdx.x, p.K);
+    if (MODE == TCL_CH8)
+      for (int i = threadIdx.x; i < TT * 16; i += TCL_EPI * 32) {
+        const int t = t0 + i / 16;
+        sm.xsl[i / 16][i % 16] = t < p.B ? p.xsl[(size_t)t * 16 + i % 16] : 0;
+      }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = sm.tmem;
-
-  if (warp == TC_EPI_WARPS) {
-    // the whole warp runs the loop (waits included); lane 0 issues the
-    // copies, MMAs and commits. One MMA per K step: each K step is a whole
-    // segment (two lanes), its accumulators a fresh buffer.
-    const bool leader = lane == 0;
-    // low rows (u8) and high rows (s8), N = 2 TT each
-    const unsigned idesc_l = tc_idesc(MODE == TCL_BLK4 ? 1 : 0, 0, 2 * TT);
-    const unsigned idesc_h = tc_idesc(MODE == TCL_BLK4 ? 1 : 0, 1, 2 * TT);
-    constexpr unsigned long long HIGH = (2 * TT * TC_KB) >> 4;  // descriptor start of the high rows
-    const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
-    const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TCT_A_BYTES);
-    const uint8_t *ga = p.a + (size_t)nt * p.nkb * TCT_A_BYTES;
-    const uint8_t *gb = p.b + (size_t)tt * p.nkb * BB;
-    int issued = 0, waited = 0;
-    auto issue = [&](int kb) {
-      const int st = kb % TC_STAGES;
-      const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
-      if (leader) {
-        tc_mbar_expect_tx(bar, STAGE);
-        tc_bulk_g2s(dst, ga + (size_t)kb * TCT_A_BYTES, TCT_A_BYTES, bar);
-        tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
+  if (MODE == TCL_BLK4) {
+    // every accumulator column of the epilogue warps starts at the magic
+    if (warp < TCL_EPI) {
+      const unsigned tb = tmem + ((unsigned)(32 * (warp & 3)) << 16) + (warp >> 2) * (2 * CW);
+      for (int c = 0; c < TCL_NPROD * 4; c++) {
+        tc_fill<2 * CW>(tb + c * N, TCL_MAGIC);
+        tc_fill<2 * CW>(tb + c * N + 2 * TT, TCL_MAGIC);
       }
-      __syncwarp();
-    };
-    for (; issued < p.nkb && issued < TC_STAGES; issued++) issue(issued);
-    bool ok = true;
-    for (int seg = 0; seg < p.nseg && ok; seg++) {
-      const int buf = seg % NBUF, kb = seg >> 2, j = seg & 3, st = kb % TC_STAGES;
-      if (seg >= NBUF)
-        ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[buf]), ((seg / NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      if (j == 0) {
-        ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (kb / TC_STAGES) & 1, p.err, TC_ERR_FULL);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        waited = kb + 1;
-      }
-      tc_fence_after();
-      const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
-      if (leader) {
-        const unsigned long long da = desc_a0 + off + (unsigned long long)(2 * j);
-        const unsigned long long db = desc_b0 + off + (unsigned long long)(2 * j);
-        tc_mma(tmem + buf * N, da, db, idesc_l, 0);
-        tc_mma(tmem + buf * N + 2 * TT, da, db + HIGH, idesc_h, 0);
-        tc_commit(tc_u32(&sm.accfull[buf]));
-      }
-      __syncwarp();
-      if (j == 3) {
-        if (leader) tc_commit(tc_u32(&sm.empty[st]));
-        __syncwarp();
-        // refill the stage of the previous K block, whose MMAs were queued
-        // ahead of these
-        if (kb >= 1 && issued < p.nkb) {
-          const int pkb = kb - 1;
-          ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[pkb % TC_STAGES]), (pkb / TC_STAGES) & 1, p.err,
-                            TC_ERR_EMPTY);
-          ok = __all_sync(0xffffffffu, ok);
-          if (!ok) break;
-          issue(issued++);
-        }
-      }
+      tc_st_wait();
     }
-    if (!ok) {
-      // drain: copies issued but not yet waited for, then every MMA issued
-      for (int kb = waited; kb < issued; kb++) tc_drain_wait(tc_u32(&sm.full[kb % TC_STAGES]), (kb / TC_STAGES) & 1);
-      if (leader) tc_commit(tc_u32(&sm.drain));
-      __syncwarp();
-      tc_drain_wait(tc_u32(&sm.drain), 0);
-    }
-  } else {
-    tcl_epilogue<MODE, TT>(p, sm, tmem, warp, lane, n0, t0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
   }
+
+  if (warp >= TCL_EPI) tcl_producer<MODE, TT>(p, sm, tmem, warp - TCL_EPI, lane, nunits);
+  else tcl_epilogue<MODE, TT>(p, sm, tmem, warp, lane, t0, nunits);
   tc_fence_before();
   __syncthreads();
-  if (MODE == TCL_CH8) tcl_store_candidates<TT>(p, sm, t0, nt, gridDim.y);
-  if (warp == TC_EPI_WARPS) {
+  if (warp == TCL_EPI) {
     __syncwarp();
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
