@@ -2290,13 +2290,13 @@ llmq_status batch_linear_tcl(llmq_batch *bt, const llmq_weight *w, const float *
   const WeightView v = w->view();
   const int K = v.cols, mode = v.bits == 4 ? TCL_BLK4 : TCL_CH8;
   const int bpad = (B + TCL_TT - 1) / TCL_TT * TCL_TT;
-  const size_t qsm = SmemPlan<FMT_GEN8>(K, K, 0).total;
+  const size_t qsm = (size_t)8 * K * 4;
   if (ln_w)
-    tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad, 256, qsm, s>>>(x, ln_w, ln_b, B, K, mode, bt->tcl_b, bt->sx,
-                                                                 bt->xsi);
+    tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad / 8, 256, qsm, s>>>(x, ln_w, ln_b, B, bpad, K, mode, bt->tcl_b,
+                                                                     bt->sx, bt->xsi);
   else
-    tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad, 256, qsm, s>>>(x, nullptr, nullptr, B, K, mode, bt->tcl_b,
-                                                                    bt->sx, bt->xsi);
+    tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad / 8, 256, qsm, s>>>(x, nullptr, nullptr, B, bpad, K, mode,
+                                                                        bt->tcl_b, bt->sx, bt->xsi);
   CKL();
   TcArgsL a{};
   a.a = w->tcl_a;
@@ -2641,6 +2641,8 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
                         (const void *)bgemv_rows_kernel<FMT_GEN8, 2>, (const void *)bgemv_rows_kernel<FMT_GEN8, 4>})
     attr(k, kBgemvSmem);
   attr((const void *)tcl_gemm_kernel<TCL_BLK4, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
+  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_LN>, 8 * 4096 * 4);
+  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_QUANT>, 8 * 4096 * 4);
   attr((const void *)tcl_gemm_kernel<TCL_CH8, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
   if (e != cudaSuccess) {
     int optin = 0;

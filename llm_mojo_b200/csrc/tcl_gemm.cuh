@@ -96,49 +96,87 @@ __global__ void tcl_prep_a_kernel(WeightView w, int mode, uint8_t *a) {
   }
 }
 
-// quantize_rows (+ LayerNorm) of each sequence's row (kernels.mojo:400-416,
-// the one-token prologue's arithmetic in natural column order) into the B
-// tiles [sequence tile][K block][4 TT rows x 128 B]: row (plane p, half h)
-// of sequence t at p * 2 TT + 2 t + h holds, in the K step's half h, the low
-// byte xl (p = 0) or the high byte xh (p = 1) of x at column tcl_col(k), and
-// zero in the other half. Also sx[m] and, for the int8 rows, the 16 lane sums of x
-// (columns 2L, 2L + 1 of every 32-column chunk). One CTA per sequence of the
-// padded count; padding sequences get zero tiles.
+// quantize_rows (+ LayerNorm) of each sequence's row (kernels.mojo:179-197,
+// 400-416: the one-token prologue's arithmetic, in natural column order)
+// into the B tiles [sequence tile][K block][4 TT rows x 128 B]: row (plane
+// p, half h) of sequence t at p * 2 TT + 2 t + h holds, in the K step's half
+// h, the low byte xl (p = 0) or the high byte xh (p = 1) of x at column
+// tcl_col(k), and zero in the other half. Also sx[m] and, for the int8 rows,
+// the 16 lane sums of x (columns 2L, 2L + 1 of every 32-column chunk). One
+// warp per sequence of the padded count (8 per CTA, the row staged in shared
+// memory), no block-wide waits; padding sequences get zero tiles.
 template <int TT, int PRO>
 __global__ void __launch_bounds__(256) tcl_quant_pack_kernel(const float *x, const float *ln_w, const float *ln_b,
-                                                             int B, int K, int mode, uint8_t *b, float *sx,
+                                                             int B, int bpad, int K, int mode, uint8_t *b, float *sx,
                                                              int *xsl) {
-  extern __shared__ __align__(16) unsigned char qsm[];
-  const int m = blockIdx.x, nkb = K / TC_KB, tt = m / TT, r = m % TT;
+  extern __shared__ __align__(16) float qsm[];  // [8][K]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp;
+  if (m >= bpad) return;
+  float *xf = qsm + (size_t)warp * K;
   const bool valid = m < B;
-  SmemPlan<FMT_GEN8> pl(K, K, 0);
-  const int16_t *xq = (const int16_t *)(qsm + pl.xq);
+  const int nkb = K / TC_KB, r = m % TT;
+  uint8_t *tile = b + (size_t)(m / TT) * nkb * (4 * TT * TC_KB);
+  float inv = 0.0f;
   if (valid) {
-    GemvArgs g{};
-    g.w.cols = K;
-    g.w.group = K;
-    g.w.bits = 8;
-    g.x = x + (size_t)m * K;
-    g.ln_w = ln_w;
-    g.ln_b = ln_b;
-    const float s = prologue<FMT_GEN8, PRO>(g, qsm, pl);
-    if (threadIdx.x == 0) sx[m] = s;
-    if (mode == TCL_CH8 && threadIdx.x < 16) xsl[(size_t)m * 16 + threadIdx.x] = ((const int *)(qsm + pl.xs))[threadIdx.x];
+    const float *row = x + (size_t)m * K;
+    for (int i = lane * 4; i < K; i += 128) *(float4 *)(xf + i) = *(const float4 *)(row + i);
+    __syncwarp();
+    if (PRO == PRO_LN) {
+      // 16 lane sums, each sequential over the row's 16-float chunks, the
+      // halving tree (every lane ends with the same mean and variance)
+      const int l = lane & 15;
+      float s = 0.0f;
+      for (int i = 0; i < K; i += 16) s = s + xf[i + l];
+      const float mean = tree16_warp(s) / (float)K;
+      float sq = 0.0f;
+      for (int i = 0; i < K; i += 16) {
+        const float d = xf[i + l] - mean;
+        sq = sq + d * d;
+      }
+      const float var = tree16_warp(sq) / (float)K;
+      const float rstd = 1.0f / sqrtf(var + 1e-5f);
+      __syncwarp();
+      for (int i = lane; i < K; i += 32) {
+        const float n = (xf[i] - mean) * rstd;
+        xf[i] = n * ln_w[i] + ln_b[i];
+      }
+      __syncwarp();
+    }
+    float mx = 0.0f;
+    for (int i = lane; i < K; i += 32) mx = fmaxf(mx, fabsf(xf[i]));
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float s = mx / 32767.0f;
+    if (s == 0.0f) s = 1.0f;
+    inv = 1.0f / s;
+    if (lane == 0) sx[m] = s;
+    if (mode == TCL_CH8) {
+      // lane L's sum over the 32-column chunks, chunks split by parity
+      const int L = lane & 15;
+      int acc = 0;
+      for (int c = lane >> 4; c < K / 32; c += 2)
+        acc += (int)roundf(xf[c * 32 + 2 * L] * inv) + (int)roundf(xf[c * 32 + 2 * L + 1] * inv);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+      if (lane < 16) xsl[(size_t)m * 16 + lane] = acc;
+    }
   }
-  uint8_t *tile = b + (size_t)tt * nkb * (4 * TT * TC_KB);
-  for (int ci = threadIdx.x; ci < K / 16; ci += blockDim.x) {
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int ci = lane; ci < K / 16; ci += 32) {
     const int k0 = ci * 16, kb = k0 / TC_KB, chunk = (k0 % TC_KB) / 16, half = (k0 >> 4) & 1;
     uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
     if (valid) {
+      // the chunk's 16 columns: contiguous for int4 rows; for int8 rows the
+      // column pairs (2L, 2L + 1) of 8 consecutive 32-column chunks
+      const int c0 = tcl_col(mode, k0, K);
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        const unsigned q = (uint16_t)xq[tcl_col(mode, k0 + i, K)];
+        const int col = mode == TCL_BLK4 ? c0 + i : c0 + (i >> 1) * 32 + (i & 1);
+        const unsigned q = (uint16_t)(int16_t)roundf(xf[col] * inv);
         lo[i >> 2] |= (q & 0xFFu) << (8 * (i & 3));
         hi[i >> 2] |= ((q >> 8) & 0xFFu) << (8 * (i & 3));
       }
     }
     uint8_t *kbase = tile + (size_t)kb * (4 * TT * TC_KB);
-    const uint4 zero = make_uint4(0, 0, 0, 0);
     *(uint4 *)(kbase + tc_sw128_off(2 * r + half, chunk)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *(uint4 *)(kbase + tc_sw128_off(2 * TT + 2 * r + half, chunk)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *(uint4 *)(kbase + tc_sw128_off(2 * r + 1 - half, chunk)) = zero;
