@@ -92,9 +92,10 @@ __global__ void dkv_store_kernel(KV8View c, const float *qkv, int layer, int pos
 // attend_float_one for token t (position pos0 + t), head h. grid (n_head, T).
 // With store != 0 (decode, T == 1) the CTA first stores this token's key and
 // value for its head, which is all its own attention reads of this step.
-// Shared memory: kv8_attend_smem(max_t, head_dim).
+// Shared memory: kv8_attend_smem(cap, head_dim), cap >= the positions any
+// query of the launch sees (at most max_t).
 __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out, const float *qkv, int layer,
-                                                         int pos0, const int *pos_dev, int store) {
+                                                         int pos0, const int *pos_dev, int store, int cap) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float red[40];
   const int h = blockIdx.x, t = blockIdx.y;
@@ -106,8 +107,8 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
   const int npos = P0 + t + 1;
   const float *q = qkv + (size_t)t * 3 * C + h * HS;
   float *sc = sm;               // [npos] scores, then exponentials
-  float *ps = sm + c.max_t;     // [npos] p * vs
-  float *qs = sm + 2 * c.max_t; // [HS] query
+  float *ps = sm + cap;         // [npos] p * vs
+  float *qs = sm + 2 * cap;     // [HS] query
 
   if (store) {
     int d = threadIdx.x;
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     ps[s] = p * c.vs[sl];
   }
   // the values of this head, staged with 16-byte loads: [npos][HS] codes
-  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * c.max_t + HS) + 15) & ~(uintptr_t)15);
+  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * cap + HS) + 15) & ~(uintptr_t)15);
   {
     const int cpr = HS / 16;
     const int8_t *vb = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
@@ -196,9 +197,10 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
   }
 }
 
-// Dynamic shared memory of kv8_attend_kernel for a cache of max_t positions.
-__host__ __device__ inline size_t kv8_attend_smem(int max_t, int HS) {
-  return (size_t)(2 * max_t + HS) * 4 + 16 + (size_t)max_t * HS;
+// Dynamic shared memory of kv8_attend_kernel for queries that see at most
+// cap positions.
+__host__ __device__ inline size_t kv8_attend_smem(int cap, int HS) {
+  return (size_t)(2 * cap + HS) * 4 + 16 + (size_t)cap * HS;
 }
 
 // attend_float_one for QB consecutive query tokens of one head at once (the

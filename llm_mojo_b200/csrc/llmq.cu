@@ -1221,8 +1221,9 @@ llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *
     kv_prefill_kernel<0><<<dim3(kv->n_head, (T + KV_QB - 1) / KV_QB), 256, sm, ctx->stream>>>(kv->v8, out, qkv, layer,
                                                                                             pos0, T);
   } else if (kv->kind == LLMQ_KV_QUANT8) {
-    size_t sm = kv8_attend_smem(kv->max_t, kv->head_dim);
-    kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0);
+    // the last query sees pos0 + T positions
+    size_t sm = kv8_attend_smem(pos0 + T, kv->head_dim);
+    kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0, pos0 + T);
   } else {
     ia_attend_kernel<<<grid, 256, ia_attend_smem(kv), ctx->stream>>>(kv->ia, out, qkv, layer, pos0, nullptr, 0,
                                                                      ia_mult());
@@ -1655,7 +1656,8 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
     a.epi = EPI_BIAS;
     CK(launch_gemv(ctx, a, PRO_LN, false, s));
     if (m->kv->kind == LLMQ_KV_QUANT8)
-      kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1);
+      kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1,
+                                                                 m->max_t);
     else
       ia_attend_kernel<<<dim3(m->n_head, 1), 256, ia_attend_smem(m->kv), s>>>(m->kv->ia, m->att, m->qkv, l, 0,
                                                                                &m->state->pos, 1, ia_mult());
@@ -2258,6 +2260,7 @@ struct llmq_batch {
   cudaGraphExec_t exec = nullptr;
   int graph_B = 0, graph_steps = 0;
   int graph_kernel = -1;      // the kernel choice the decode-step graph was captured with
+  int graph_cap = 0;          // and the attention context it was sized for
   uint8_t *tcl_b = nullptr;  // the lane-mode GEMM's sequence tiles [max_seqs padded to TCL_TT][widest K x 4]
   int kernel = LLMQ_BATCH_AUTO;
 };
@@ -2431,19 +2434,20 @@ __global__ void batch_advance_kernel(int *state) {
   state[1] += 1;
 }
 
-llmq_status batch_decode_step(llmq_batch *bt, int B, cudaStream_t s) {
+// cap: the positions the step's attention may see (its shared memory).
+llmq_status batch_decode_step(llmq_batch *bt, int B, int cap, cudaStream_t s) {
   llmq_model *m = bt->m;
   llmq_ctx *ctx = bt->ctx;
   const int C = m->C;
   embed_batch_kernel<<<B, 256, 0, s>>>(m->head->view(), m->wpe(), bt->x, bt->tokens, bt->state);
   CKL();
-  const size_t att_sm = kv8_attend_smem(m->max_t, C / m->n_head);
+  const size_t att_sm = kv8_attend_smem(cap, C / m->n_head);
   llmq_status st;
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
     if ((st = batch_linear(bt, w[0], bt->x, m->vec(l, 0), m->vec(l, 1), m->vec(l, 2), bt->qkv, B, EPI_BIAS, s)))
       return st;
-    kv8_attend_kernel<<<dim3(m->n_head, 1, B), 128, att_sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, bt->state, 1);
+    kv8_attend_kernel<<<dim3(m->n_head, 1, B), 128, att_sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, bt->state, 1, cap);
     CKL();
     if ((st = batch_linear(bt, w[1], bt->att, nullptr, nullptr, m->vec(l, 3), bt->x, B, EPI_BIAS | EPI_RESID, s)))
       return st;
@@ -2529,15 +2533,18 @@ llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
   argmax_parts_kernel<<<B, 256, 0, s>>>(bt->part_val, bt->part_idx, nparts, bt->ids, m->max_t, bt->tokens, nullptr);
   CKL();
   if (steps > 1) {
-    // decode steps as one CUDA graph, captured for this batch size
-    if (!bt->exec || bt->graph_B != B || bt->graph_kernel != bt->kernel) {
+    // decode steps as one CUDA graph, captured for this batch size, kernel
+    // choice and attention context: the last step's queries see P + steps - 1
+    // positions; the shared memory is sized for that, rounded up to 64
+    const int cap = std::min(m->max_t, (P + steps - 1 + 63) / 64 * 64);
+    if (!bt->exec || bt->graph_B != B || bt->graph_kernel != bt->kernel || bt->graph_cap != cap) {
       if (bt->exec) cudaGraphExecDestroy(bt->exec);
       if (bt->graph) cudaGraphDestroy(bt->graph);
       bt->exec = nullptr;
       bt->graph = nullptr;
       CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
       batch_advance_kernel<<<1, 1, 0, s>>>(bt->state);
-      llmq_status cst = batch_decode_step(bt, B, s);
+      llmq_status cst = batch_decode_step(bt, B, cap, s);
       if (cst == LLMQ_OK)
         argmax_parts_kernel<<<B, 256, 0, s>>>(bt->part_val, bt->part_idx, nparts, bt->ids, m->max_t, bt->tokens,
                                               bt->state + 1);
@@ -2552,6 +2559,7 @@ llmq_status batch_run(llmq_batch *bt, int B, int P, int steps, int *ids_dev) {
       CK(cudaGraphInstantiate(&bt->exec, g, 0));
       bt->graph_B = B;
       bt->graph_kernel = bt->kernel;
+      bt->graph_cap = cap;
     }
     for (int i = 1; i < steps; i++) CK(cudaGraphLaunch(bt->exec, s));
   }
