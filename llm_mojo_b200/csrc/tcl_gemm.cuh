@@ -464,16 +464,15 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
     ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
     if (!ok) return;
     tc_fence_after();
-    int dl0[W], dh0[W], dl1[W], dh1[W], dl2[W], dh2[W], dl3[W], dh3[W];
+    // the unit's K steps in two halves of two (32 registers of loads in
+    // flight, no spills); the buffer is released once the second half's
+    // loads have landed and its columns are refilled
+    int dla[W], dha[W], dlb[W], dhb[W];
     const unsigned tb = tbase + buf * KBN;
-    tc_ld(tb, dl0);
-    tc_ld(tb + 2 * TT, dh0);
-    tc_ld(tb + N, dl1);
-    tc_ld(tb + N + 2 * TT, dh1);
-    tc_ld(tb + 2 * N, dl2);
-    tc_ld(tb + 2 * N + 2 * TT, dh2);
-    tc_ld(tb + 3 * N, dl3);
-    tc_ld(tb + 3 * N + 2 * TT, dh3);
+    tc_ld(tb, dla);
+    tc_ld(tb + 2 * TT, dha);
+    tc_ld(tb + N, dlb);
+    tc_ld(tb + N + 2 * TT, dhb);
     const int4 e = *reinterpret_cast<const int4 *>(&sm.seg[kb * 4]);
     const unsigned s0 = scn[0], s1 = scn[1], s2 = scn[2], s3 = scn[3];
     if (MODE == TCL_CH8 && kb == 0) {
@@ -489,14 +488,21 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
     }
     if (MODE == TCL_BLK4 && u + 1 < nunits) fetch_scales(it2, kb2);
     tc_ld_wait();
-    tc_ld_done(dl0);
-    tc_ld_done(dh0);
-    tc_ld_done(dl1);
-    tc_ld_done(dh1);
-    tc_ld_done(dl2);
-    tc_ld_done(dh2);
-    tc_ld_done(dl3);
-    tc_ld_done(dh3);
+    tc_ld_done(dla);
+    tc_ld_done(dha);
+    tc_ld_done(dlb);
+    tc_ld_done(dhb);
+    step(dla, dha, e.x, s0);
+    step(dlb, dhb, e.y, s1);
+    tc_ld(tb + 2 * N, dla);
+    tc_ld(tb + 2 * N + 2 * TT, dha);
+    tc_ld(tb + 3 * N, dlb);
+    tc_ld(tb + 3 * N + 2 * TT, dhb);
+    tc_ld_wait();
+    tc_ld_done(dla);
+    tc_ld_done(dha);
+    tc_ld_done(dlb);
+    tc_ld_done(dhb);
     if (MODE == TCL_BLK4) {
       // the next MMAs into this buffer accumulate onto the magic again
 #pragma unroll
@@ -509,10 +515,8 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
     tc_fence_before();
     __syncwarp();
     if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[buf]));
-    step(dl0, dh0, e.x, s0);
-    step(dl1, dh1, e.y, s1);
-    step(dl2, dh2, e.z, s2);
-    step(dl3, dh3, e.w, s3);
+    step(dla, dha, e.z, s2);
+    step(dlb, dhb, e.w, s3);
     if (kb == nkb - 1) emit(it);
     it = it2;
     kb = kb2;
