@@ -724,8 +724,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
     float accf[CW];
 #pragma unroll
     for (int c = 0; c < CW; c++) accf[c] = 0.0f;
-    int la[CW], ha[CW], lb[CW], hb[CW];
-    auto start = [&](int seg, int (&l)[CW], int (&h)[CW]) -> bool {
+    // one segment's loads in flight (l, h) while the previous one, already
+    // converted to its CW floats v, folds into the chains
+    int l[CW], h[CW];
+    float v[CW];
+    unsigned short sc_nxt = 0;  // the next segment's scale, weight sum and zero point,
+    int ws_nxt = 0, zp_nxt = 0;  // loaded with its accumulators
+    float sc_cur = 0.0f;
+    auto start = [&](int seg) -> bool {
       const int buf = seg % NBUF;
       bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (seg / NBUF) & 1, p.err, TC_ERR_ACC);
       ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
@@ -733,46 +739,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
       tc_fence_after();
       tc_ld(tbase + buf * 2 * TT, l);
       tc_ld(tbase + buf * 2 * TT + TT, h);
+      const int g = seg * p.seg / G;
+      sc_nxt = p.w.scale[(size_t)nr * gpr + g];
+      ws_nxt = p.wsum[(size_t)nr * p.nseg + seg];
+      if (ZC) zp_nxt = p.w.zp[(size_t)nr * gpr + g];
       return true;
     };
-    auto finish = [&](int seg, int (&l)[CW], int (&h)[CW]) {
+    // completes the loads, hands the accumulators back to the MMAs and
+    // converts the segment's sums: f32(256 h + l + 128 W - zp sum(x))
+    auto finish = [&](int seg) {
       tc_ld_wait();
       tc_ld_done(l);
       tc_ld_done(h);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[seg % NBUF]));
-    };
-    auto fold = [&](int seg, const int (&l)[CW], const int (&h)[CW]) {
-      const int g = seg * p.seg / G;
-      const float sc = half_bits_to_float(p.w.scale[(size_t)nr * gpr + g]);
-      const int w128 = p.wsum[(size_t)nr * p.nseg + seg] * 128;
+      const int w128 = ws_nxt * 128;
 #pragma unroll
       for (int c = 0; c < CW; c++) {
-        float v;
         if (ZC) {
           const unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c] + (unsigned)w128 -
-                             (unsigned)p.w.zp[(size_t)nr * gpr + g] * (unsigned)sm.xsum[cg * CW + c][seg];
-          v = (float)(int)a;
+                             (unsigned)zp_nxt * (unsigned)sm.xsum[cg * CW + c][seg];
+          v[c] = (float)(int)a;
         } else {
           // |h|, |l + 128 W| < 2^22 for int4 weights: both exact as floats,
           // one rounding in the fma, as the conversion of the int32 sum
-          v = fmaf(256.0f, tc_small_to_float(h[c]), tc_small_to_float(l[c] + w128));
+          v[c] = fmaf(256.0f, tc_small_to_float(h[c]), tc_small_to_float(l[c] + w128));
         }
-        accf[c] = fmaf(v, sc, accf[c]);
       }
+      sc_cur = half_bits_to_float(sc_nxt);
     };
-    bool ok = start(0, la, ha);
-    if (ok) finish(0, la, ha);
-    // two segments per trip: fold one while the next one's loads are in flight
-    for (int seg = 0; ok && seg < p.nseg; seg += 2) {
-      if (seg + 1 < p.nseg) ok = start(seg + 1, lb, hb);
-      fold(seg, la, ha);
-      if (!ok || seg + 1 >= p.nseg) break;
-      finish(seg + 1, lb, hb);
-      if (seg + 2 < p.nseg) ok = start(seg + 2, la, ha);
-      fold(seg + 1, lb, hb);
-      if (ok && seg + 2 < p.nseg) finish(seg + 2, la, ha);
+    bool ok = start(0);
+    if (ok) finish(0);
+    for (int seg = 0; ok && seg < p.nseg; seg++) {
+      const bool more = seg + 1 < p.nseg;
+      if (more) ok = start(seg + 1);
+#pragma unroll
+      for (int c = 0; c < CW; c++) accf[c] = fmaf(v[c], sc_cur, accf[c]);
+      if (!ok || !more) break;
+      finish(seg + 1);
     }
     if (ok && !*(volatile int *)&sm.abort && n < p.n_full) {
       const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
