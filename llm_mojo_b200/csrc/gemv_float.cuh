@@ -330,6 +330,103 @@ __global__ void __launch_bounds__(256) affine_float_gemv_kernel(AffFloatArgs a) 
   }
 }
 
+// The same rows for group sizes 32, 64 and 128, with the work split so that
+// small matrices still fill the GPU: a row's group sums accg[g][L] (lane L's
+// chain over the group's 32-chunks) are independent of each other, and only
+// the fold acc = fma(accg, s, acc) is sequential over the groups. Phase 1:
+// thread (row, g) computes the 16 lane sums of one group from one 16-byte (int4)
+// or two (int8) loads per 32-chunk, into shared memory; phase 2: one thread per
+// (row, lanes L, L + 8) folds them over the groups in order, and one thread per
+// row adds the halving tree. AFG_ROWS rows per CTA (more CTAs than the
+// 16-lanes-per-row kernel for layer shapes). x sits in shared memory padded by
+// one float per 32, so threads of different groups read different banks.
+__host__ __device__ inline size_t afg_smem(int cols, int gpr, int rows_per_cta) {
+  return (size_t)(cols + cols / 32) * 4 + (size_t)16 * (gpr * rows_per_cta + 1) * 4 + (size_t)gpr * rows_per_cta * 4 +
+         8 * rows_per_cta * 4;
+}
+
+template <int BITS, int AFG_ROWS>
+__global__ void __launch_bounds__(256) affine_float_group_kernel(AffFloatArgs a) {
+  extern __shared__ __align__(16) float afg[];
+  const int cols = a.w.cols, G = a.w.group, gpr = cols / G, cpg = G / 32, LS = gpr * AFG_ROWS + 1;
+  float *xsh = afg;                              // [cols + cols / 32], x[k] at k + k / 32
+  float *acc_s = xsh + cols + cols / 32;         // [16][LS]: lane L, group g, row r at L * LS + g * ROWS + r
+  float *scl = acc_s + 16 * LS;                  // [gpr][ROWS]
+  float *tsum = scl + gpr * AFG_ROWS;            // [8][ROWS]: the tree's first level
+  const int tid = threadIdx.x;
+  for (int i = tid; i < cols; i += blockDim.x) xsh[i + (i >> 5)] = a.x[i];
+  for (int base = blockIdx.x * AFG_ROWS; base < a.w.rows; base += gridDim.x * AFG_ROWS) {
+    __syncthreads();  // x staged; the previous rows' sums consumed
+    // phase 1: thread (row r, group g) for items i = r + ROWS * g
+    for (int i = tid; i < gpr * AFG_ROWS; i += blockDim.x) {
+      const int r = i % AFG_ROWS, g = i / AFG_ROWS;
+      const int row = min(base + r, a.w.rows - 1);
+      const uint8_t *p = a.w.codes + (size_t)row * cols * BITS / 8;
+      const float zp = (float)a.w.zp[(size_t)row * gpr + g];
+      scl[g * AFG_ROWS + r] = __half2float(__ushort_as_half(a.w.scale[(size_t)row * gpr + g]));
+      float acc[16];
+#pragma unroll
+      for (int L = 0; L < 16; L++) acc[L] = 0.0f;
+      for (int c = 0; c < cpg; c++) {
+        const int k0 = g * G + 32 * c;
+        const float *x0 = xsh + k0 + (k0 >> 5), *x1 = x0 + 16;  // columns k0 .. k0 + 31 (one 32-chunk)
+        uint32_t wlo[4], whi[4];
+        if (BITS == 4) {
+          const uint4 w = __ldg((const uint4 *)(p + k0 / 2));
+          wlo[0] = w.x, wlo[1] = w.y, wlo[2] = w.z, wlo[3] = w.w;
+        } else {
+          const uint4 w0 = __ldg((const uint4 *)(p + k0)), w1 = __ldg((const uint4 *)(p + k0 + 16));
+          wlo[0] = w0.x, wlo[1] = w0.y, wlo[2] = w0.z, wlo[3] = w0.w;
+          whi[0] = w1.x, whi[1] = w1.y, whi[2] = w1.z, whi[3] = w1.w;
+        }
+#pragma unroll
+        for (int L = 0; L < 16; L++) {
+          const unsigned b = (wlo[L >> 2] >> (8 * (L & 3))) & 0xFFu;
+          float v0, v1;
+          if (BITS == 4) {
+            v0 = (float)(b & 0xFu) - zp;
+            v1 = (float)(b >> 4) - zp;
+          } else {
+            v0 = (float)b - zp;
+            v1 = (float)((whi[L >> 2] >> (8 * (L & 3))) & 0xFFu) - zp;
+          }
+          acc[L] = fmaf(v0, x0[L], acc[L]);
+          acc[L] = fmaf(v1, x1[L], acc[L]);
+        }
+      }
+#pragma unroll
+      for (int L = 0; L < 16; L++) acc_s[L * LS + g * AFG_ROWS + r] = acc[L];
+    }
+    __syncthreads();
+    // phase 2: thread (row r, lanes L and L + 8): acc = fma(accg, s, acc) over
+    // the groups in order, then the tree's first level acc_L + acc_{L+8}
+    if (tid < 8 * AFG_ROWS) {
+      const int r = tid % AFG_ROWS, L = tid / AFG_ROWS;
+      const float *a0 = acc_s + L * LS + r, *a1 = acc_s + (L + 8) * LS + r;
+      float c0 = 0.0f, c1 = 0.0f;
+#pragma unroll 8
+      for (int g = 0; g < gpr; g++) {
+        const float s = scl[g * AFG_ROWS + r];
+        c0 = fmaf(a0[g * AFG_ROWS], s, c0);
+        c1 = fmaf(a1[g * AFG_ROWS], s, c1);
+      }
+      tsum[L * AFG_ROWS + r] = c0 + c1;
+    }
+    __syncthreads();
+    if (tid < AFG_ROWS && base + tid < a.w.rows) {
+      const int r = tid, row = base + r;
+      const float *t = tsum + r;  // t[i * ROWS] = acc_i + acc_{i+8}
+      const float u0 = t[0] + t[4 * AFG_ROWS], u1 = t[1 * AFG_ROWS] + t[5 * AFG_ROWS];
+      const float u2 = t[2 * AFG_ROWS] + t[6 * AFG_ROWS], u3 = t[3 * AFG_ROWS] + t[7 * AFG_ROWS];
+      float v = (u0 + u2) + (u1 + u3);
+      if (a.epi & EPI_BIAS) v += a.bias[row];
+      if (a.epi & EPI_GELU) v = gelu(v);
+      if (a.epi & EPI_RESID) v += a.out[row];
+      a.out[row] = v;
+    }
+  }
+}
+
 // Dense [IN, OUT] split-K GEMV (kernels.mojo:132-176 gemv, :828-865
 // linear_team): part p accumulates rows [p*rows, min(IN, (p+1)*rows)),
 // rows = ceil(IN / nparts), as one sequential fma chain per output; the

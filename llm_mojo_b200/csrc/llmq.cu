@@ -908,11 +908,32 @@ llmq_status llmq_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
       CK(row_gemv(ctx, a));
     } else {
       AffFloatArgs a{w->view(), x, bias, out, epi};
-      const int grid = std::min((w->rows + 15) / 16, ctx->num_sms * 4);
-      if (w->bits == 4)
-        affine_float_gemv_kernel<4><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
-      else
-        affine_float_gemv_kernel<8><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
+      const bool tall = w->rows >= 8192;
+      const int rpc = tall ? 16 : 4;
+      const size_t sm = afg_smem(w->cols, w->cols / w->group, rpc);
+      if (w->group <= 128 && sm <= (size_t)kMaxSmem) {
+        // grouped rows: the group sums in parallel, the folds per row
+        const int grid = std::min((w->rows + rpc - 1) / rpc, ctx->num_sms * 8);
+        const void *k = w->bits == 4 ? (tall ? (const void *)affine_float_group_kernel<4, 16>
+                                             : (const void *)affine_float_group_kernel<4, 4>)
+                                     : (tall ? (const void *)affine_float_group_kernel<8, 16>
+                                             : (const void *)affine_float_group_kernel<8, 4>);
+        if (sm > 48 * 1024) CK(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        if (w->bits == 4 && tall)
+          affine_float_group_kernel<4, 16><<<grid, 256, sm, ctx->stream>>>(a);
+        else if (w->bits == 4)
+          affine_float_group_kernel<4, 4><<<grid, 256, sm, ctx->stream>>>(a);
+        else if (tall)
+          affine_float_group_kernel<8, 16><<<grid, 256, sm, ctx->stream>>>(a);
+        else
+          affine_float_group_kernel<8, 4><<<grid, 256, sm, ctx->stream>>>(a);
+      } else {
+        const int grid = std::min((w->rows + 15) / 16, ctx->num_sms * 4);
+        if (w->bits == 4)
+          affine_float_gemv_kernel<4><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
+        else
+          affine_float_gemv_kernel<8><<<grid, 256, w->cols * 4, ctx->stream>>>(a);
+      }
       CKL();
     }
     return LLMQ_OK;
