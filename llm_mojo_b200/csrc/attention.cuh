@@ -33,6 +33,15 @@ struct KV8View {
   }
 };
 
+// The exact float of an int8 code without the conversion unit (the bits of
+// 1.5 * 2^23 + v, minus 1.5 * 2^23; exact for |v| < 2^22).
+__device__ __forceinline__ float i8_to_float(int v) { return __int_as_float(0x4B400000 + v) - 12582912.0f; }
+
+__device__ __forceinline__ void kv_cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
+
 // QuantKV.quantize (kvcache.mojo:319-331) of one head's 64 values by one
 // warp... any block of >= head_dim threads: threads [0, head_dim) hold x.
 __device__ __forceinline__ float quant_i8_head(float x, bool active, float *red, int8_t *dst, int d) {
@@ -109,6 +118,20 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
   float *sc = sm;               // [npos] scores, then exponentials
   float *ps = sm + cap;         // [npos] p * vs
   float *qs = sm + 2 * cap;     // [HS] query
+  // the values of this head, [npos][HS] codes: copied into shared memory
+  // while the scores are computed; the positions before this token's now,
+  // this token's row (which the store below writes) after the store
+  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * cap + HS) + 15) & ~(uintptr_t)15);
+  const int cpr = HS / 16;
+  const int8_t *vb = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
+  {
+    const int npre = store ? npos - 1 : npos;
+    for (int i = threadIdx.x; i < npre * cpr; i += blockDim.x) {
+      const int s = i / cpr, ch = i % cpr;
+      kv_cp_async16(vst + (size_t)s * HS + ch * 16, vb + (size_t)s * c.n_head * HS + ch * 16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  }
 
   if (store) {
     int d = threadIdx.x;
@@ -120,6 +143,9 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
       if (threadIdx.x == 0) (which == 0 ? c.ks : c.vs)[sl] = s;
     }
     __syncthreads();
+    if (threadIdx.x < cpr)
+      *(int4 *)(vst + (size_t)(npos - 1) * HS + threadIdx.x * 16) =
+          __ldcg((const int4 *)(vb + (size_t)(npos - 1) * c.n_head * HS + threadIdx.x * 16));
   }
   for (int i = threadIdx.x; i < HS; i += blockDim.x) qs[i] = q[i];
   __syncthreads();
@@ -137,7 +163,7 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
       int4 kv = *(const int4 *)(kp + i);
       const int8_t *kb = (const int8_t *)&kv;
 #pragma unroll
-      for (int l = 0; l < 16; l++) d[l] = d[l] + qs[i + l] * (float)kb[l];
+      for (int l = 0; l < 16; l++) d[l] = d[l] + qs[i + l] * i8_to_float(kb[l]);
     }
 #pragma unroll
     for (int l = 0; l < 8; l++) d[l] = d[l] + d[l + 8];
@@ -168,16 +194,7 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     float p = sc[s] / total;
     ps[s] = p * c.vs[sl];
   }
-  // the values of this head, staged with 16-byte loads: [npos][HS] codes
-  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * cap + HS) + 15) & ~(uintptr_t)15);
-  {
-    const int cpr = HS / 16;
-    const int8_t *vb = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
-    for (int i = threadIdx.x; i < npos * cpr; i += blockDim.x) {
-      const int s = i / cpr, ch = i % cpr;
-      *(int4 *)(vst + (size_t)s * HS + ch * 16) = *(const int4 *)(vb + (size_t)s * c.n_head * HS + ch * 16);
-    }
-  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   // acc[d] = fma(p * vs, v[s][d], acc[d]) over positions in order.
   for (int d = threadIdx.x; d < HS; d += blockDim.x) {
@@ -185,14 +202,14 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     const int8_t *vp = vst + d;
     int s = 0;
     for (; s + 4 <= npos; s += 4) {
-      float v0 = (float)vp[(size_t)s * HS], v1 = (float)vp[(size_t)(s + 1) * HS];
-      float v2 = (float)vp[(size_t)(s + 2) * HS], v3 = (float)vp[(size_t)(s + 3) * HS];
+      float v0 = i8_to_float(vp[(size_t)s * HS]), v1 = i8_to_float(vp[(size_t)(s + 1) * HS]);
+      float v2 = i8_to_float(vp[(size_t)(s + 2) * HS]), v3 = i8_to_float(vp[(size_t)(s + 3) * HS]);
       acc = fmaf(ps[s], v0, acc);
       acc = fmaf(ps[s + 1], v1, acc);
       acc = fmaf(ps[s + 2], v2, acc);
       acc = fmaf(ps[s + 3], v3, acc);
     }
-    for (; s < npos; s++) acc = fmaf(ps[s], (float)vp[(size_t)s * HS], acc);
+    for (; s < npos; s++) acc = fmaf(ps[s], i8_to_float(vp[(size_t)s * HS]), acc);
     out[(size_t)t * C + h * HS + d] = acc;
   }
 }
