@@ -749,7 +749,9 @@ llmq_status tct_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, cons
     p.seg_ks = seg / 32;
     p.seg = seg;
     p.epi = epi;
-    const dim3 grid(ntiles, ttiles);
+    // one CTA per SM: the weight tiles times as many token-tile columns as
+    // fit, each CTA looping over its column's token tiles
+    const dim3 grid(ntiles, std::min(ttiles, std::max(1, ctx->num_sms / ntiles)));
     if (TT == 32) {
       const size_t sm = sizeof(TcSmemT<32>) + 1024;
       if (zc)

@@ -506,7 +506,6 @@ constexpr int TCT_A_BYTES = TC_M * TC_KB;  // 16 KB of weight rows per K block
 template <int TT>
 struct TcSmemT {
   alignas(1024) uint8_t stage[TC_STAGES][TCT_A_BYTES + 2 * TT * TC_KB];
-  int xsum[TT][TC_MAX_GROUPS];  // int8 weights: the tile's per-token segment sums of x
   alignas(8) unsigned long long full[TC_STAGES], empty[TC_STAGES], accfull[TC_NBUF_MAX], accempty[TC_NBUF_MAX],
       drain;
   unsigned tmem;
@@ -617,7 +616,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
   extern __shared__ __align__(128) unsigned char tc_raw[];
   TcSmemT<TT> &sm = *reinterpret_cast<TcSmemT<TT> *>(tc_raw + ((1024u - (tc_u32(tc_raw) & 1023u)) & 1023u));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nt = blockIdx.x, tt = blockIdx.y, n0 = nt * TC_M, t0 = tt * TT;
+  // persistent over token tiles: CTA (nt, c) takes token tiles c, c + gridDim.y, ...;
+  // the copy pipeline and the accumulator rotation run on across them
+  const int nt = blockIdx.x, n0 = nt * TC_M;
+  const int ttiles = (p.T + TT - 1) / TT;
+  const int iters = (int)blockIdx.y < ttiles ? (ttiles - 1 - (int)blockIdx.y) / (int)gridDim.y + 1 : 0;
   const int G = p.w.group, gpr = p.w.cols / G;
 
   if (threadIdx.x == 0) {
@@ -637,11 +640,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_u32(&sm.tmem)),
                  "r"(TC_TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  } else if (ZC) {
-    for (int i = threadIdx.x; i < TT * p.nseg; i += TC_EPI_WARPS * 32) {
-      const int t = i / p.nseg, sg = i % p.nseg;
-      sm.xsum[t][sg] = p.xsum[(size_t)(t0 + t) * p.nseg + sg];
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -650,41 +648,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
 
   if (warp == TC_EPI_WARPS) {
     // the whole warp runs the loop (waits included); lane 0 issues the
-    // copies, MMAs and commits
+    // copies, MMAs and commits. K blocks and segments are counted across
+    // the CTA's token tiles: K block kg = it * nkb + kb, segment sg.
     const bool leader = lane == 0;
     const unsigned idesc = tc_idesc(ZC ? 0 : 1, 1, 2 * TT);
     const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
     const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TCT_A_BYTES);
     const uint8_t *ga = p.a + (size_t)nt * p.nkb * TCT_A_BYTES;
-    const uint8_t *gb = p.b + (size_t)tt * p.nkb * BB;
+    const int nkg = iters * p.nkb, nsg = iters * p.nseg;
     int issued = 0, waited = 0, kstep = 0;
-    auto issue = [&](int kb) {
-      const int st = kb % TC_STAGES;
+    auto issue = [&](int kg) {
+      const int st = kg % TC_STAGES, it = kg / p.nkb, kb = kg - it * p.nkb;
+      const int tt = blockIdx.y + it * gridDim.y;
       const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
       if (leader) {
         tc_mbar_expect_tx(bar, STAGE);
         tc_bulk_g2s(dst, ga + (size_t)kb * TCT_A_BYTES, TCT_A_BYTES, bar);
-        tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
+        tc_bulk_g2s(dst + TCT_A_BYTES, p.b + ((size_t)tt * p.nkb + kb) * BB, BB, bar);
       }
       __syncwarp();
     };
-    for (; issued < p.nkb && issued < TC_STAGES; issued++) issue(issued);
+    for (; issued < nkg && issued < TC_STAGES; issued++) issue(issued);
     bool ok = true;
-    for (int seg = 0; seg < p.nseg && ok; seg++) {
-      const int buf = seg % NBUF;
-      if (seg >= NBUF)
-        ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[buf]), ((seg / NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+    for (int sg = 0; sg < nsg && ok; sg++) {
+      const int buf = sg % NBUF;
+      if (sg >= NBUF)
+        ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[buf]), ((sg / NBUF) - 1) & 1, p.err, TC_ERR_ACCEMPTY);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const unsigned d = tmem + buf * 2 * TT;
       for (int ks = 0; ks < p.seg_ks && ok; ks++, kstep++) {
-        const int kb = kstep >> 2, j = kstep & 3, st = kb % TC_STAGES;
+        const int kg = kstep >> 2, j = kstep & 3, st = kg % TC_STAGES;
         if (j == 0) {
-          ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (kb / TC_STAGES) & 1, p.err, TC_ERR_FULL);
+          ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (kg / TC_STAGES) & 1, p.err, TC_ERR_FULL);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
-          waited = kb + 1;
+          waited = kg + 1;
           tc_fence_after();
         }
         const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
@@ -694,11 +694,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
         if (j == 3) {
           if (leader) tc_commit(tc_u32(&sm.empty[st]));
           __syncwarp();
-          // refill the stage of the previous k block, whose MMA was queued
+          // refill the stage of the previous K block, whose MMA was queued
           // ahead of these
-          if (kb >= 1 && issued < p.nkb) {
-            const int pkb = kb - 1;
-            ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[pkb % TC_STAGES]), (pkb / TC_STAGES) & 1, p.err,
+          if (kg >= 1 && issued < nkg) {
+            const int pkg = kg - 1;
+            ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[pkg % TC_STAGES]), (pkg / TC_STAGES) & 1, p.err,
                               TC_ERR_EMPTY);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -711,7 +711,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
     }
     if (!ok) {
       // drain: copies issued but not yet waited for, then every MMA issued
-      for (int kb = waited; kb < issued; kb++) tc_drain_wait(tc_u32(&sm.full[kb % TC_STAGES]), (kb / TC_STAGES) & 1);
+      for (int kg = waited; kg < issued; kg++) tc_drain_wait(tc_u32(&sm.full[kg % TC_STAGES]), (kg / TC_STAGES) & 1);
       if (leader) tc_commit(tc_u32(&sm.drain));
       __syncwarp();
       tc_drain_wait(tc_u32(&sm.drain), 0);
@@ -721,6 +721,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
     const int n = n0 + 32 * q + lane;            // this thread's weight row
     const int nr = n < p.w.rows ? n : p.w.rows - 1;
     const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * CW;
+    const int nseg = p.nseg, nsg = iters * nseg;
     float accf[CW];
 #pragma unroll
     for (int c = 0; c < CW; c++) accf[c] = 0.0f;
@@ -731,35 +732,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
     unsigned short sc_nxt = 0;  // the next segment's scale, weight sum and zero point,
     int ws_nxt = 0, zp_nxt = 0;  // loaded with its accumulators
     float sc_cur = 0.0f;
-    auto start = [&](int seg) -> bool {
-      const int buf = seg % NBUF;
-      bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (seg / NBUF) & 1, p.err, TC_ERR_ACC);
+    int seg_l = 0, it_l = 0;  // the loads' (segment, token-tile iteration); the fold's below
+    auto start = [&](int sg) -> bool {
+      const int buf = sg % NBUF;
+      bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (sg / NBUF) & 1, p.err, TC_ERR_ACC);
       ok = __all_sync(0xffffffffu, ok);  // the tensor-memory loads are warp-wide
       if (!ok) return false;
       tc_fence_after();
       tc_ld(tbase + buf * 2 * TT, l);
       tc_ld(tbase + buf * 2 * TT + TT, h);
-      const int g = seg * p.seg / G;
+      const int g = seg_l * p.seg / G;
       sc_nxt = p.w.scale[(size_t)nr * gpr + g];
-      ws_nxt = p.wsum[(size_t)nr * p.nseg + seg];
+      ws_nxt = p.wsum[(size_t)nr * nseg + seg_l];
       if (ZC) zp_nxt = p.w.zp[(size_t)nr * gpr + g];
       return true;
     };
     // completes the loads, hands the accumulators back to the MMAs and
     // converts the segment's sums: f32(256 h + l + 128 W - zp sum(x))
-    auto finish = [&](int seg) {
+    auto finish = [&](int sg) {
       tc_ld_wait();
       tc_ld_done(l);
       tc_ld_done(h);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[seg % NBUF]));
+      if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[sg % NBUF]));
       const int w128 = ws_nxt * 128;
+      const int t0 = (blockIdx.y + it_l * gridDim.y) * TT + cg * CW;
 #pragma unroll
       for (int c = 0; c < CW; c++) {
         if (ZC) {
-          const unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c] + (unsigned)w128 -
-                             (unsigned)zp_nxt * (unsigned)sm.xsum[cg * CW + c][seg];
+          const unsigned xs = (unsigned)p.xsum[(size_t)(t0 + c) * nseg + seg_l];
+          const unsigned a = ((unsigned)h[c] << 8) + (unsigned)l[c] + (unsigned)w128 - (unsigned)zp_nxt * xs;
           v[c] = (float)(int)a;
         } else {
           // |h|, |l + 128 W| < 2^22 for int4 weights: both exact as floats,
@@ -768,22 +771,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
         }
       }
       sc_cur = half_bits_to_float(sc_nxt);
+      if (++seg_l == nseg) {
+        seg_l = 0;
+        ++it_l;
+      }
     };
-    bool ok = start(0);
-    if (ok) finish(0);
-    for (int seg = 0; ok && seg < p.nseg; seg++) {
-      const bool more = seg + 1 < p.nseg;
-      if (more) ok = start(seg + 1);
-#pragma unroll
-      for (int c = 0; c < CW; c++) accf[c] = fmaf(v[c], sc_cur, accf[c]);
-      if (!ok || !more) break;
-      finish(seg + 1);
-    }
-    if (ok && !*(volatile int *)&sm.abort && n < p.n_full) {
+    // the outputs of token tile it (its last segment folded)
+    auto emit = [&](int it) {
+      if (n >= p.n_full) return;
       const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
+      const int t0 = (blockIdx.y + it * gridDim.y) * TT + cg * CW;
 #pragma unroll
       for (int c = 0; c < CW; c++) {
-        const int m = t0 + cg * CW + c;
+        const int m = t0 + c;
         if (m >= p.T) break;
         float *dst = p.out + (size_t)m * p.OUT + n;
         float r = accf[c] * p.sx[m];
@@ -792,6 +792,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tct_gemm_kernel(TcArgsT p) {
         if (p.epi & EPI_RESID) r += *dst;
         *dst = r;
       }
+    };
+    bool ok = nsg > 0 && start(0);
+    if (ok) finish(0);
+    int seg_f = 0, it_f = 0;  // the fold's segment and token-tile iteration
+    for (int sg = 0; ok && sg < nsg; sg++) {
+      const bool more = sg + 1 < nsg;
+      if (more) ok = start(sg + 1);
+#pragma unroll
+      for (int c = 0; c < CW; c++) accf[c] = fmaf(v[c], sc_cur, accf[c]);
+      if (++seg_f == nseg) {
+        if (!*(volatile int *)&sm.abort) emit(it_f);
+#pragma unroll
+        for (int c = 0; c < CW; c++) accf[c] = 0.0f;
+        seg_f = 0;
+        ++it_f;
+      }
+      if (!ok || !more) break;
+      finish(sg + 1);
     }
   }
   tc_fence_before();
