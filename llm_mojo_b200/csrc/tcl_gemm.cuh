@@ -39,8 +39,8 @@
 // once per unit, so one producer's waits and issue latency overlap the
 // other's. Warps 0-15 fold (warp w: tensor-memory lanes = weight rows
 // 32 * (w % 4) + lane, sequences (w / 4) * TT / 4 .. + TT / 4). The int4
-// rows' accumulators start at a float-magic bias so that reading them as
-// floats needs one subtraction, and the pair arithmetic runs on f32x2.
+// rows' lane sums become floats through a float-magic bias (an integer add and
+// a float subtraction), and the pair arithmetic runs on f32x2.
 #pragma once
 
 #include "tc_gemm.cuh"
@@ -272,34 +272,13 @@ __device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsig
   return r;
 }
 
-// The int4 rows' accumulators start at TCL_MAGIC = the bits of 1.5 * 2^23:
-// the MMAs add a lane's exact int32 sum v (|v| < 2^16 per K step), and the
-// bits then read as the float 1.5 * 2^23 + v, so one float subtraction gives
-// f32(v) exactly, without a conversion.
+// A lane's exact int32 sum v (|v| < 2^16 per K step) becomes a float without
+// the conversion unit: the bits of TCL_MAGIC + v (TCL_MAGIC = the bits of
+// 1.5 * 2^23) read as the float 1.5 * 2^23 + v, and one float subtraction
+// (paired as f32x2) gives f32(v) exactly.
 constexpr int TCL_MAGIC = 0x4B400000;
 constexpr float TCL_MAGIC_F = 12582912.0f;
 
-// Every column of the warp's 32 lanes in [addr, addr + W) set to v.
-template <int W>
-__device__ __forceinline__ void tc_fill(unsigned addr, int v) {
-  static_assert(W == 8 || W == 16 || W == 32, "fill widths");
-  if (W == 32)
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(addr),
-        "r"(v)
-        : "memory");
-  else if (W == 16)
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1};" ::"r"(addr),
-        "r"(v)
-        : "memory");
-  else
-    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(addr), "r"(v)
-                 : "memory");
-}
-__device__ __forceinline__ void tc_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Warps 0-15: per segment g of the CTA's units (u = g / 4, K step g % 4),
 // the accumulators of this thread's weight row and CW sequences. Column
@@ -418,8 +397,10 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
       for (int c = 0; c < CW; c++) {
         // |high| < 2^15, |low| < 2^16: exact floats, one rounding in the fma,
         // as the reference's f32(lane) - zp * f32(lane sum of x)
-        const unsigned long long lo = f2_add(f2_bits(dl[2 * c], dl[2 * c + 1]), neg_magic);
-        const unsigned long long hi = f2_add(f2_bits(dh[2 * c], dh[2 * c + 1]), neg_magic);
+        const unsigned long long lo =
+            f2_add(f2_bits(dl[2 * c] + TCL_MAGIC, dl[2 * c + 1] + TCL_MAGIC), neg_magic);
+        const unsigned long long hi =
+            f2_add(f2_bits(dh[2 * c] + TCL_MAGIC, dh[2 * c + 1] + TCL_MAGIC), neg_magic);
         cab[c] = f2_fma(f2_fma(k256, hi, lo), sc2, cab[c]);
       }
       if (e & 128) {
@@ -503,15 +484,6 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
     tc_ld_done(dha);
     tc_ld_done(dlb);
     tc_ld_done(dhb);
-    if (MODE == TCL_BLK4) {
-      // the next MMAs into this buffer accumulate onto the magic again
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        tc_fill<W>(tb + j * N, TCL_MAGIC);
-        tc_fill<W>(tb + j * N + 2 * TT, TCL_MAGIC);
-      }
-      tc_st_wait();
-    }
     tc_fence_before();
     __syncwarp();
     if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[buf]));
@@ -533,7 +505,7 @@ template <int MODE, int TT>
 __device__ __forceinline__ void tcl_producer(const TcArgsL &p, TcSmemL<TT> &sm, unsigned tmem, int pr, int lane,
                                              int nunits) {
   constexpr int N = 4 * TT, KBN = 4 * N, BB = N * TC_KB, STAGE = TCT_A_BYTES + BB;
-  constexpr unsigned ACC = MODE == TCL_BLK4 ? 1u : 0u;  // int4 rows accumulate onto the magic
+  constexpr unsigned ACC = 0u;  // every K step into fresh accumulators
   const bool leader = lane == 0;
   // low rows (u8) and high rows (s8), N = 2 TT each
   const unsigned idesc_l = tc_idesc(MODE == TCL_BLK4 ? 1 : 0, 0, 2 * TT);
@@ -647,21 +619,6 @@ __global__ void __launch_bounds__(TCL_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = sm.tmem;
-  if (MODE == TCL_BLK4) {
-    // every accumulator column of the epilogue warps starts at the magic
-    if (warp < TCL_EPI) {
-      const unsigned tb = tmem + ((unsigned)(32 * (warp & 3)) << 16) + (warp >> 2) * (2 * CW);
-      for (int c = 0; c < TCL_NPROD * 4; c++) {
-        tc_fill<2 * CW>(tb + c * N, TCL_MAGIC);
-        tc_fill<2 * CW>(tb + c * N + 2 * TT, TCL_MAGIC);
-      }
-      tc_st_wait();
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-  }
-
   if (warp >= TCL_EPI) tcl_producer<MODE, TT>(p, sm, tmem, warp - TCL_EPI, lane, nunits);
   else tcl_epilogue<MODE, TT>(p, sm, tmem, warp, lane, t0, nunits);
   tc_fence_before();
