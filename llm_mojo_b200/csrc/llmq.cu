@@ -342,6 +342,7 @@ cudaError_t configure_kernels() {
   tct((const void *)tct_gemm_kernel<false, 32>, sizeof(TcSmemT<32>));
   tct((const void *)tct_gemm_kernel<true, 64>, sizeof(TcSmemT<64>));
   tct((const void *)tct_gemm_kernel<false, 64>, sizeof(TcSmemT<64>));
+  tct((const void *)tcp_gemm_kernel, sizeof(TcpSmem));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void *)merge_draw_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)merge_smem(kMergeCap));
@@ -702,7 +703,10 @@ llmq_status rows_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, con
 llmq_status tct_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, const float *bias, float *out, int T,
                        int IN, int OUT, int epi) {
   const int K = IN, nkb = K / TC_KB, seg = std::min(w->group, 256), nseg = K / seg;
-  const int TT = OUT <= 1024 ? 32 : 64;
+  // int4 rows with 32-column groups (one K step per segment) take the
+  // two-producer kernel on tiles of 32 tokens
+  const bool tcp = w->bits == 4 && w->group == 32;
+  const int TT = tcp || OUT <= 1024 ? 32 : 64;
   const int ttiles = (T + TT - 1) / TT, t_pad = ttiles * TT;
   const int full = OUT / 32 * 32, ntiles = (full + TC_M - 1) / TC_M;
   const bool zc = w->bits == 8;
@@ -752,7 +756,9 @@ llmq_status tct_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, cons
     // one CTA per SM: the weight tiles times as many token-tile columns as
     // fit, each CTA looping over its column's token tiles
     const dim3 grid(ntiles, std::min(ttiles, std::max(1, ctx->num_sms / ntiles)));
-    if (TT == 32) {
+    if (tcp) {
+      tcp_gemm_kernel<<<grid, TCL_THREADS, sizeof(TcpSmem) + 1024, ctx->stream>>>(p);
+    } else if (TT == 32) {
       const size_t sm = sizeof(TcSmemT<32>) + 1024;
       if (zc)
         tct_gemm_kernel<true, 32><<<grid, TC_THREADS, sm, ctx->stream>>>(p);

@@ -630,4 +630,243 @@ __global__ void __launch_bounds__(TCL_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// The prefill GEMM (tile_i16, kernels.mojo:512-573) for int4 rows with
+// 32-column groups: every segment is one 32-column K step, so a K block holds
+// 4 segments. The arithmetic is tct_gemm_kernel's (weights as the MMA's M,
+// both activation planes of TT = 32 tokens in one N = 64 operand, the
+// segment sum 256 D_h + D_l + 128 W, the float folds in order); the
+// pipeline is the lane-mode GEMM's: units of one K block alternate between
+// two producer warps, each with its own copy stages and a tensor-memory
+// buffer of 4 segments, one commit per unit; 16 epilogue warps (8 tokens
+// each) read a unit in two halves and fold token pairs as f32x2. Persistent
+// over token tiles.
+// ---------------------------------------------------------------------------
+constexpr int TCP_TT = 32;
+
+struct TcpSmem {
+  alignas(1024) uint8_t stage[TCL_STAGES][TCT_A_BYTES + 2 * TCP_TT * TC_KB];
+  alignas(8) unsigned long long full[TCL_STAGES], empty[TCL_STAGES], accfull[TCL_NPROD], accempty[TCL_NPROD],
+      drain[TCL_NPROD];
+  unsigned tmem;
+  int abort;
+};
+
+// Producer warp pr: its units u = pr, pr + 2, ... (local index k), as
+// tcl_producer: copies through its own stages, 4 MMAs into buffer pr, one
+// commit for the epilogue and one for the stage.
+__device__ __forceinline__ void tcp_producer(const TcArgsT &p, TcpSmem &sm, unsigned tmem, int pr, int lane,
+                                             int nunits) {
+  constexpr int TT = TCP_TT, N = 2 * TT, KBN = 4 * N, BB = 2 * TT * TC_KB, STAGE = TCT_A_BYTES + BB;
+  const bool leader = lane == 0;
+  const unsigned idesc = tc_idesc(1, 1, N);
+  const unsigned long long desc_a0 = tc_desc_sw128(tc_u32(sm.stage[0]));
+  const unsigned long long desc_b0 = tc_desc_sw128(tc_u32(sm.stage[0]) + TCT_A_BYTES);
+  const int nk = nunits > pr ? (nunits - pr + 1) / 2 : 0;
+  const uint8_t *ga = p.a + (size_t)blockIdx.x * p.nkb * TCT_A_BYTES;
+  auto stage_of = [&](int k) { return pr * TCL_SPP + k % TCL_SPP; };
+  int it_ld = 0, kb_ld = pr;  // the next load's unit as (token-tile iteration, K block)
+  auto load = [&](int k) {
+    const int tt = blockIdx.y + it_ld * gridDim.y, kb = kb_ld;
+    kb_ld += 2;
+    while (kb_ld >= p.nkb) {
+      kb_ld -= p.nkb;
+      ++it_ld;
+    }
+    const int st = stage_of(k);
+    const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
+    if (leader) {
+      tc_mbar_expect_tx(bar, STAGE);
+      tc_bulk_g2s(dst, ga + (size_t)kb * TCT_A_BYTES, TCT_A_BYTES, bar);
+      tc_bulk_g2s(dst + TCT_A_BYTES, p.b + ((size_t)tt * p.nkb + kb) * BB, BB, bar);
+    }
+    __syncwarp();
+  };
+  int issued = 0, waited = 0;
+  for (; issued < nk && issued < TCL_SPP; issued++) load(issued);
+  bool ok = true;
+  for (int k = 0; k < nk && ok; k++) {
+    const int st = stage_of(k);
+    if (k >= 1) ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[pr]), (k - 1) & 1, p.err, TC_ERR_ACCEMPTY);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    ok = tc_wait_flag(&sm.abort, tc_u32(&sm.full[st]), (k / TCL_SPP) & 1, p.err, TC_ERR_FULL);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) break;
+    waited = k + 1;
+    tc_fence_after();
+    if (leader) {
+      const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
+#pragma unroll
+      for (int j = 0; j < 4; j++)
+        tc_mma(tmem + pr * KBN + j * N, desc_a0 + off + (unsigned long long)(2 * j),
+               desc_b0 + off + (unsigned long long)(2 * j), idesc, 0);
+      tc_commit(tc_u32(&sm.accfull[pr]));
+      tc_commit(tc_u32(&sm.empty[st]));
+    }
+    __syncwarp();
+    if (k >= 1 && issued < nk) {
+      ok = tc_wait_flag(&sm.abort, tc_u32(&sm.empty[stage_of(k - 1)]), ((k - 1) / TCL_SPP) & 1, p.err,
+                        TC_ERR_EMPTY);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      load(issued++);
+    }
+  }
+  if (!ok) {
+    for (int k = waited; k < issued; k++) tc_drain_wait(tc_u32(&sm.full[stage_of(k)]), (k / TCL_SPP) & 1);
+    if (leader) tc_commit(tc_u32(&sm.drain[pr]));
+    __syncwarp();
+    tc_drain_wait(tc_u32(&sm.drain[pr]), 0);
+  }
+}
+
+// Epilogue warp (lane quarter q, token group cg): row n0 + 32 q + lane, tokens
+// cg * 8 .. + 8 of each token tile; segment s of a row is group s.
+__device__ __forceinline__ void tcp_epilogue(const TcArgsT &p, TcpSmem &sm, unsigned tmem, int warp, int lane,
+                                             int nunits) {
+  constexpr int TT = TCP_TT, N = 2 * TT, KBN = 4 * N, CW = TT / 4;
+  const int q = warp & 3, cg = warp >> 2;
+  const int n = blockIdx.x * TC_M + 32 * q + lane;
+  const int nr = n < p.w.rows ? n : p.w.rows - 1;
+  const unsigned tbase = tmem + ((unsigned)(32 * q) << 16) + cg * CW;  // low plane; the high plane at + TT
+  const int nkb = p.nkb, gpr = p.w.cols / p.w.group;
+  const unsigned long long neg_magic = f2_pair(-TCL_MAGIC_F, -TCL_MAGIC_F), k256 = f2_pair(256.0f, 256.0f);
+  unsigned long long acc[CW / 2];  // token pairs' float chains
+#pragma unroll
+  for (int c = 0; c < CW / 2; c++) acc[c] = 0ull;
+  // the next unit's 4 scales (float16 bits) and weight sums, loaded a unit ahead
+  uint2 scn = make_uint2(0, 0);
+  int4 wsn = make_int4(0, 0, 0, 0);
+  auto fetch = [&](int kb) {
+    scn = *reinterpret_cast<const uint2 *>(p.w.scale + (size_t)nr * gpr + kb * 4);
+    wsn = *reinterpret_cast<const int4 *>(p.wsum + (size_t)nr * p.nseg + kb * 4);
+  };
+  auto step = [&](const int (&l)[CW], const int (&h)[CW], unsigned sc16, int ws) {
+    const float sc = half_bits_to_float((uint16_t)sc16);
+    const unsigned long long sc2 = f2_pair(sc, sc);
+    const int lb = ws * 128 + TCL_MAGIC;  // 128 W, with the float magic
+#pragma unroll
+    for (int c = 0; c < CW / 2; c++) {
+      // |h|, |l + 128 W| < 2^22: exact floats, one rounding in the fma, as
+      // the conversion of the int32 sum 256 h + l + 128 W
+      const unsigned long long lo = f2_add(f2_bits(l[2 * c] + lb, l[2 * c + 1] + lb), neg_magic);
+      const unsigned long long hi = f2_add(f2_bits(h[2 * c] + TCL_MAGIC, h[2 * c + 1] + TCL_MAGIC), neg_magic);
+      acc[c] = f2_fma(f2_fma(k256, hi, lo), sc2, acc[c]);
+    }
+  };
+  auto emit = [&](int it) {
+    if (n >= p.n_full) return;
+    const float bn = (p.epi & EPI_BIAS) ? p.bias[n] : 0.0f;
+    const int t0 = (blockIdx.y + it * gridDim.y) * TT + cg * CW;
+#pragma unroll
+    for (int c = 0; c < CW; c++) {
+      const int m = t0 + c;
+      if (m >= p.T) break;
+      float a0, a1;
+      f2_split(acc[c / 2], a0, a1);
+      float *dst = p.out + (size_t)m * p.OUT + n;
+      float r = ((c & 1) ? a1 : a0) * p.sx[m];
+      if (p.epi & EPI_BIAS) r += bn;
+      if (p.epi & EPI_GELU) r = gelu(r);
+      if (p.epi & EPI_RESID) r += *dst;
+      *dst = r;
+    }
+  };
+  int it = 0, kb = 0;
+  if (nunits > 0) fetch(0);
+  for (int u = 0; u < nunits; u++) {
+    const int buf = u & 1;
+    bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accfull[buf]), (u >> 1) & 1, p.err, TC_ERR_ACC);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok) return;
+    tc_fence_after();
+    int la[CW], ha[CW], lb[CW], hb[CW];
+    const unsigned tb = tbase + buf * KBN;
+    tc_ld(tb, la);
+    tc_ld(tb + TT, ha);
+    tc_ld(tb + N, lb);
+    tc_ld(tb + N + TT, hb);
+    const uint2 sc = scn;
+    const int4 ws = wsn;
+    int it2 = it, kb2 = kb + 1;
+    if (kb2 == nkb) {
+      kb2 = 0;
+      ++it2;
+    }
+    if (u + 1 < nunits) fetch(kb2);
+    tc_ld_wait();
+    tc_ld_done(la);
+    tc_ld_done(ha);
+    tc_ld_done(lb);
+    tc_ld_done(hb);
+    step(la, ha, sc.x & 0xFFFFu, ws.x);
+    step(lb, hb, sc.x >> 16, ws.y);
+    tc_ld(tb + 2 * N, la);
+    tc_ld(tb + 2 * N + TT, ha);
+    tc_ld(tb + 3 * N, lb);
+    tc_ld(tb + 3 * N + TT, hb);
+    tc_ld_wait();
+    tc_ld_done(la);
+    tc_ld_done(ha);
+    tc_ld_done(lb);
+    tc_ld_done(hb);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) tc_mbar_arrive(tc_u32(&sm.accempty[buf]));
+    step(la, ha, sc.y & 0xFFFFu, ws.z);
+    step(lb, hb, sc.y >> 16, ws.w);
+    if (kb == nkb - 1) {
+      if (!*(volatile int *)&sm.abort) emit(it);
+#pragma unroll
+      for (int c = 0; c < CW / 2; c++) acc[c] = 0ull;
+    }
+    it = it2;
+    kb = kb2;
+  }
+}
+
+__global__ void __launch_bounds__(TCL_THREADS, 1) tcp_gemm_kernel(TcArgsT p) {
+  constexpr int KBN = 4 * 2 * TCP_TT;
+  static_assert(TCL_NPROD * KBN <= TC_TMEM_COLS, "two unit buffers of tensor memory");
+  static_assert(TCL_EPI == 16, "4 token groups of 8 per lane quarter");
+  extern __shared__ __align__(128) unsigned char tc_raw[];
+  TcpSmem &sm = *reinterpret_cast<TcpSmem *>(tc_raw + ((1024u - (tc_u32(tc_raw) & 1023u)) & 1023u));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ttiles = (p.T + TCP_TT - 1) / TCP_TT;
+  const int iters = (int)blockIdx.y < ttiles ? (ttiles - 1 - (int)blockIdx.y) / (int)gridDim.y + 1 : 0;
+  const int nunits = iters * p.nkb;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TCL_STAGES; s++) {
+      tc_mbar_init(tc_u32(&sm.full[s]), 1);
+      tc_mbar_init(tc_u32(&sm.empty[s]), 1);
+    }
+    for (int b = 0; b < TCL_NPROD; b++) {
+      tc_mbar_init(tc_u32(&sm.accfull[b]), 1);
+      tc_mbar_init(tc_u32(&sm.accempty[b]), TCL_EPI);
+      tc_mbar_init(tc_u32(&sm.drain[b]), 1);
+    }
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == TCL_EPI) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_u32(&sm.tmem)),
+                 "r"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const unsigned tmem = sm.tmem;
+  if (warp >= TCL_EPI) tcp_producer(p, sm, tmem, warp - TCL_EPI, lane, nunits);
+  else tcp_epilogue(p, sm, tmem, warp, lane, nunits);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == TCL_EPI) {
+    __syncwarp();
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
+  }
+}
+
 }  // namespace llmq
