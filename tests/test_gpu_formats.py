@@ -84,6 +84,30 @@ def test_affine_float_rows(torch, ctx, fmt, IN, OUT):
     gw.free()
 
 
+@pytest.mark.parametrize("fmt", ["int4-g32", "int8-g64", "int4-g128", "int8-ch"])
+def test_affine_float_head_rows(torch, ctx, fmt):
+    """The one-token W4A32 / W8A32 head shape (16 rows per CTA of the grouped
+    kernel from 8192 rows; the per-channel kernel for int8-ch): 12,000 rows of
+    768, every row against the oracle's dot_row, bit for bit."""
+    from llm_mojo_b200 import kernels
+    from llm_mojo_b200.tensor import QuantMatrix, parse_dtype
+
+    bits_, group, sym, _ = parse_dtype(fmt)
+    V, Cn = 12000, 768
+    rng = np.random.default_rng(V + bits_)
+    w = (rng.standard_normal((V, Cn)) * 0.02).astype(np.float32)
+    ow = O.QuantMatrix(w, bits_, group, sym, False, False)
+    gw = QuantMatrix.from_f32(ctx, w, bits_, group, sym, False, False)
+    h = rng.standard_normal(Cn).astype(np.float32)
+    logits = torch.zeros((1, V), dtype=torch.float32, device="cuda")
+    try:
+        kernels.head(ctx, logits, dev(torch, h), gw, 1, V, Cn)
+        want = np.array([O.lib().oq_dot_row(O.C.byref(ow.q), o, O.ptr(h)) for o in range(V)], dtype=np.float32)
+        assert np.array_equal(bits(logits.cpu().numpy()[0]), bits(want))
+    finally:
+        gw.free()
+
+
 @pytest.mark.parametrize("dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("IN,OUT", SHAPES)
 def test_dense_gemv_parts(torch, ctx, dt, IN, OUT):
