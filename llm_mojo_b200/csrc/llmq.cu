@@ -2314,27 +2314,36 @@ int batch_head_parts(const llmq_batch *bt, int B) {
   return batch_uses_tcl(bt, m->head, B) ? 4 * ((m->V + TC_M - 1) / TC_M) : (m->V + BG_ROWS - 1) / BG_ROWS;
 }
 
-// quantize_rows (+ LayerNorm) of B rows into the lane-mode GEMM's sequence
-// tiles (with sx and, for the int8 head, the lane sums of x), then the GEMM.
+// The lane-mode GEMM of B rows: up to TCL_PACK_K columns each CTA quantizes
+// (+ LayerNorm) its sequences' rows into shared memory itself; wider rows
+// are quantized into the sequence tiles first (tcl_quant_pack_kernel, with
+// sx and, for the int8 head, the lane sums of x).
 llmq_status batch_linear_tcl(llmq_batch *bt, const llmq_weight *w, const float *x, const float *ln_w,
                              const float *ln_b, const float *bias, float *out, int B, int epi, cudaStream_t s) {
   llmq_ctx *ctx = bt->ctx;
   const WeightView v = w->view();
   const int K = v.cols, mode = v.bits == 4 ? TCL_BLK4 : TCL_CH8;
   const int bpad = (B + TCL_TT - 1) / TCL_TT * TCL_TT;
-  const size_t qsm = (size_t)8 * K * 4;
-  if (ln_w)
-    tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad / 8, 256, qsm, s>>>(x, ln_w, ln_b, B, bpad, K, mode, bt->tcl_b,
-                                                                     bt->sx, bt->xsi);
-  else
-    tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad / 8, 256, qsm, s>>>(x, nullptr, nullptr, B, bpad, K, mode,
-                                                                        bt->tcl_b, bt->sx, bt->xsi);
-  CKL();
   TcArgsL a{};
   a.a = w->tcl_a;
-  a.b = bt->tcl_b;
-  a.sx = bt->sx;
-  a.xsl = bt->xsi;
+  a.res = K <= TCL_PACK_K && K / TC_KB <= TCL_STAGES;
+  if (a.res) {
+    a.x = x;
+    a.ln_w = ln_w;
+    a.ln_b = ln_b;
+  } else {
+    const size_t qsm = (size_t)8 * K * 4;
+    if (ln_w)
+      tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad / 8, 256, qsm, s>>>(x, ln_w, ln_b, B, bpad, K, mode, bt->tcl_b,
+                                                                       bt->sx, bt->xsi);
+    else
+      tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad / 8, 256, qsm, s>>>(x, nullptr, nullptr, B, bpad, K, mode,
+                                                                          bt->tcl_b, bt->sx, bt->xsi);
+    CKL();
+    a.b = bt->tcl_b;
+    a.sx = bt->sx;
+    a.xsl = bt->xsi;
+  }
   a.w = v;
   a.bias = bias;
   a.out = out;
@@ -2678,9 +2687,9 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
                         (const void *)bgemv_rows_kernel<FMT_GEN8, 2>, (const void *)bgemv_rows_kernel<FMT_GEN8, 4>})
     attr(k, kBgemvSmem);
   attr((const void *)tcl_gemm_kernel<TCL_BLK4, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
+  attr((const void *)tcl_gemm_kernel<TCL_CH8, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
   attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_LN>, 8 * 4096 * 4);
   attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_QUANT>, 8 * 4096 * 4);
-  attr((const void *)tcl_gemm_kernel<TCL_CH8, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
   if (e != cudaSuccess) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);

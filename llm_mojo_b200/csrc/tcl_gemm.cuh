@@ -184,11 +184,122 @@ __global__ void __launch_bounds__(256) tcl_quant_pack_kernel(const float *x, con
   }
 }
 
+// Registers per lane of a row in tcl_pack_seq: lane L holds columns L + 32 j.
+constexpr int TCL_PJ = 24;
+constexpr int TCL_PACK_K = 32 * TCL_PJ;  // the widest row packed inside the GEMM
+
+// tcl_quant_pack_kernel's arithmetic for one sequence of a K <= TCL_PACK_K
+// row, by one warp, into B tiles in shared memory (K block kb at tiles + kb
+// * kbs): the codes' positions only (the other halves are zeroed by the
+// caller). Returns sx; for the int8 rows also writes the 16 lane sums of x
+// to xsl. Lane L holds columns L + 32 j in registers (one coalesced read).
+// The LayerNorm sums keep their order: lane sum l adds columns l + 16 i for
+// i = 0, 1, ..., i.e. the registers j of lanes l and l + 16 in turn, which
+// every lane reads with two shuffles (no divergence). Each lane stores the
+// two bytes of its own codes. With ln_stage, the nthr threads 0 ... nthr - 1
+// (each packing one sequence) first copy the LayerNorm weights there
+// together. A padding sequence (valid false) stores zero codes.
+template <int TT>
+__device__ float tcl_pack_seq(const float *row, const float *ln_w, const float *ln_b, int K, int mode, bool valid,
+                              int t, uint8_t *tiles, int kbs, int *xsl, float *ln_stage, int nthr, int lane) {
+  constexpr unsigned HI = (2 * TT / 8) * 1024;  // tc_sw128_off(r + 2 TT, c) - tc_sw128_off(r, c)
+  const bool ln = ln_w != nullptr;
+  const int n = K >> 5, l = lane & 15;
+  float xr[TCL_PJ];
+#pragma unroll
+  for (int j = 0; j < TCL_PJ; j++) xr[j] = (valid && j < n) ? __ldg(row + lane + 32 * j) : 0.0f;
+  if (ln && ln_stage) {
+    for (int i = threadIdx.x; i < K; i += nthr) {
+      ln_stage[i] = __ldg(ln_w + i);
+      ln_stage[K + i] = __ldg(ln_b + i);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(nthr) : "memory");
+    ln_w = ln_stage;
+    ln_b = ln_stage + K;
+  }
+  if (ln && valid) {
+    float a = 0.0f;
+#pragma unroll
+    for (int j = 0; j < TCL_PJ; j++)
+      if (j < n) {
+        const float u0 = __shfl_sync(0xffffffffu, xr[j], l), u1 = __shfl_sync(0xffffffffu, xr[j], l + 16);
+        a = a + u0;
+        a = a + u1;
+      }
+    const float mean = tree16_warp(a) / (float)K;
+    float sq = 0.0f;
+#pragma unroll
+    for (int j = 0; j < TCL_PJ; j++)
+      if (j < n) {
+        const float d0 = __shfl_sync(0xffffffffu, xr[j], l) - mean;
+        const float d1 = __shfl_sync(0xffffffffu, xr[j], l + 16) - mean;
+        sq = sq + d0 * d0;
+        sq = sq + d1 * d1;
+      }
+    const float rstd = 1.0f / sqrtf(tree16_warp(sq) / (float)K + 1e-5f);
+#pragma unroll
+    for (int j = 0; j < TCL_PJ; j++)
+      if (j < n) {
+        const int c = lane + 32 * j;
+        const float v = (xr[j] - mean) * rstd;
+        xr[j] = v * ln_w[c] + ln_b[c];
+      }
+  }
+  float mx = 0.0f;
+#pragma unroll
+  for (int j = 0; j < TCL_PJ; j++) mx = fmaxf(mx, fabsf(xr[j]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float s = mx / 32767.0f;
+  if (s == 0.0f) s = 1.0f;
+  const float inv = valid ? 1.0f / s : 0.0f;
+  int qsum = 0;
+  if (mode == TCL_BLK4) {
+    // register j: the 32-column group j (block b = j / 8, lane group g =
+    // j % 8) is K step st = gp * nblk + b with tcl_pair_lane(gp) = g; lane
+    // L is its byte L % 16 of half L / 16
+    const int nblk = K >> 8, half = lane >> 4;
+    uint8_t *base = tiles + (lane & 15);
+#pragma unroll
+    for (int j = 0; j < TCL_PJ; j++)
+      if (j < n) {
+        const unsigned q = (uint16_t)(int16_t)roundf(xr[j] * inv);
+        const int st = tcl_pair_lane(j & 7) * nblk + (j >> 3);
+        uint8_t *dst = base + (size_t)(st >> 2) * kbs + tc_sw128_off(2 * t + half, (st & 3) * 2 + half);
+        dst[0] = (uint8_t)q;
+        dst[HI] = (uint8_t)(q >> 8);
+      }
+  } else {
+    // lane L = 2 lp + e holds, in register j, position 2 j + e of lane
+    // position lp (columns 2 lp, 2 lp + 1 of every 32-column chunk), i.e. K
+    // position gp * 2 lw + (lp >= 8 ? lw : 0) + 2 j + e, tcl_pair_lane(gp) = lp % 8
+    const int lw = K >> 4, lp = lane >> 1;
+    const int k00 = tcl_pair_lane(lp & 7) * 2 * lw + (lp >= 8 ? lw : 0) + (lane & 1);
+#pragma unroll
+    for (int j = 0; j < TCL_PJ; j++)
+      if (j < n) {
+        const float f = roundf(xr[j] * inv);
+        const unsigned q = (uint16_t)(int16_t)f;
+        qsum += (int)f;
+        const int k = k00 + 2 * j, half = (k >> 4) & 1;
+        uint8_t *dst = tiles + (size_t)(k >> 7) * kbs + tc_sw128_off(2 * t + half, (k & 127) >> 4) + (k & 15);
+        dst[0] = (uint8_t)q;
+        dst[HI] = (uint8_t)(q >> 8);
+      }
+    // lane 2L's and lane 2L + 1's sums of their codes: columns 2L, 2L + 1
+    qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+    if ((lane & 1) == 0) xsl[lane >> 1] = qsum;
+  }
+  return s;
+}
+
 struct TcArgsL {
   const uint8_t *a;   // weight tiles (tcl_prep_a_kernel)
-  const uint8_t *b;   // sequence tiles (tcl_quant_pack_kernel)
-  const float *sx;    // [sequences] activation scales
-  const int *xsl;     // int8 rows: [sequences][16] lane sums of x
+  const float *x;     // K <= TCL_PACK_K: [sequences][K] rows, packed by the CTA (tcl_pack_seq)
+  const float *ln_w;  //   LayerNorm applied first when non-null
+  const float *ln_b;
+  const uint8_t *b;   // else: sequence tiles (tcl_quant_pack_kernel)
+  const float *sx;    //   [sequences] activation scales
+  const int *xsl;     //   int8 rows: [sequences][16] lane sums of x
   WeightView w;
   const float *bias;  // int4 rows: [rows] or null
   float *out;         // int4 rows: [sequences][rows]
@@ -196,6 +307,7 @@ struct TcArgsL {
   int *part_idx;
   int *err;
   int B, OUT, K, nkb, nseg, epi, ntiles, nparts;
+  int res;            // x given: B tile kb stays in stage kb's B slot (nkb <= TCL_STAGES)
 };
 
 // A CTA's units: K blocks (4 segments, one 128-byte K block of the A and B
@@ -230,10 +342,11 @@ template <int TT>
 struct TcSmemL {
   alignas(1024) uint8_t stage[TCL_STAGES][TCT_A_BYTES + 4 * TT * TC_KB];
   int xsl[TT][16];
+  float sx[TT];                               // the sequences' activation scales
   alignas(16) int seg[TCL_MAX_SEG];           // the K steps' schedule (tcl_seg_entry)
   float tree[3][TT / TCL_CG][TCL_EPI * 32];  // the epilogue's halving-tree partial sums
   alignas(8) unsigned long long full[TCL_STAGES], empty[TCL_STAGES], accfull[TCL_NPROD], accempty[TCL_NPROD],
-      drain[TCL_NPROD];
+      drain[TCL_NPROD], packed;
   unsigned tmem;
   int abort;
 };
@@ -326,7 +439,7 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
         const int m = t0 + cg * CW + c;
         if (m >= p.B) break;
         float *dst = p.out + (size_t)m * p.OUT + n;
-        float r = sm.tree[2][c][tid] * p.sx[m];
+        float r = sm.tree[2][c][tid] * sm.sx[cg * CW + c];
         if (p.epi & EPI_BIAS) r += bn;
         if (p.epi & EPI_GELU) r = gelu(r);
         if (p.epi & EPI_RESID) r += *dst;
@@ -341,7 +454,7 @@ __device__ __forceinline__ void tcl_epilogue(const TcArgsL &p, TcSmemL<TT> &sm, 
         float bv = -__int_as_float(0x7f800000);
         int bi = 0x7fffffff;
         if (n < p.w.rows && m < p.B) {
-          bv = sm.tree[2][c][tid] * p.sx[m];
+          bv = sm.tree[2][c][tid] * sm.sx[cg * CW + c];
           bi = n;
         }
         for (int o = 16; o > 0; o >>= 1) {
@@ -488,26 +601,29 @@ __device__ __forceinline__ void tcl_producer(const TcArgsL &p, TcSmemL<TT> &sm, 
   const int nk = nunits > pr ? (nunits - pr + 1) / 2 : 0;
   const uint8_t *gb = p.b + (size_t)blockIdx.x * p.nkb * BB;
   auto stage_of = [&](int k) { return pr * TCL_SPP + k % TCL_SPP; };
-  int it_ld = 0, kb_ld = pr;  // the next load's unit 2 k + pr as (row-tile iteration, K block)
-  auto load = [&](int k) {
-    const int nt = blockIdx.y + it_ld * gridDim.y, kb = kb_ld;
-    kb_ld += 2;
-    while (kb_ld >= p.nkb) {
-      kb_ld -= p.nkb;
-      ++it_ld;
-    }
+  // the copies of unit k (2 k + pr overall): its weight tile (wa) and its
+  // B tile (wb); one expected-bytes count covers both
+  auto load = [&](int k, bool wa, bool wb) {
+    const int u = 2 * k + pr, it = u / p.nkb, kb = u - it * p.nkb, nt = blockIdx.y + it * gridDim.y;
     const int st = stage_of(k);
     const unsigned dst = tc_u32(sm.stage[st]), bar = tc_u32(&sm.full[st]);
     if (leader) {
-      tc_mbar_expect_tx(bar, STAGE);
-      tc_bulk_g2s(dst, p.a + ((size_t)nt * p.nkb + kb) * TCT_A_BYTES, TCT_A_BYTES, bar);
-      tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
+      if (wa) {
+        tc_mbar_expect_tx(bar, p.res ? TCT_A_BYTES : STAGE);
+        tc_bulk_g2s(dst, p.a + ((size_t)nt * p.nkb + kb) * TCT_A_BYTES, TCT_A_BYTES, bar);
+      }
+      if (wb && !p.res) tc_bulk_g2s(dst + TCT_A_BYTES, gb + (size_t)kb * BB, BB, bar);
     }
     __syncwarp();
   };
+  // the first stages' weight tiles while the epilogue warps pack B (or copy
+  // sx), then their B tiles (issued even after a failed wait, so that every
+  // stage's count completes before the drain)
   int issued = 0, waited = 0;
-  for (; issued < nk && issued < TCL_SPP; issued++) load(issued);
-  bool ok = true;
+  for (; issued < nk && issued < TCL_SPP; issued++) load(issued, true, false);
+  bool ok = tc_wait_flag(&sm.abort, tc_u32(&sm.packed), 0, p.err, TC_ERR_FULL);
+  ok = __all_sync(0xffffffffu, ok);
+  for (int k = 0; k < issued; k++) load(k, false, true);
   for (int k = 0; k < nk && ok; k++) {
     const int st = stage_of(k);
     if (k >= 1) ok = tc_wait_flag(&sm.abort, tc_u32(&sm.accempty[pr]), (k - 1) & 1, p.err, TC_ERR_ACCEMPTY);
@@ -520,10 +636,12 @@ __device__ __forceinline__ void tcl_producer(const TcArgsL &p, TcSmemL<TT> &sm, 
     tc_fence_after();
     if (leader) {
       const unsigned long long off = (unsigned long long)((st * STAGE) >> 4);
+      const int u = 2 * k + pr, kb = u - (u / p.nkb) * p.nkb;
+      const unsigned long long offb = p.res ? (unsigned long long)((kb * STAGE) >> 4) : off;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const unsigned long long da = desc_a0 + off + (unsigned long long)(2 * j);
-        const unsigned long long db = desc_b0 + off + (unsigned long long)(2 * j);
+        const unsigned long long db = desc_b0 + offb + (unsigned long long)(2 * j);
         const unsigned d = tmem + pr * KBN + j * N;
         tc_mma(d, da, db, idesc_l, ACC);
         tc_mma(d + 2 * TT, da, db + HIGH, idesc_h, ACC);
@@ -538,7 +656,7 @@ __device__ __forceinline__ void tcl_producer(const TcArgsL &p, TcSmemL<TT> &sm, 
                         TC_ERR_EMPTY);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
-      load(issued++);
+      load(issued++, true, true);
     }
   }
   if (!ok) {
@@ -572,6 +690,7 @@ __global__ void __launch_bounds__(TCL_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
       tc_mbar_init(tc_u32(&sm.accempty[b]), TCL_EPI);
       tc_mbar_init(tc_u32(&sm.drain[b]), 1);
     }
+    tc_mbar_init(tc_u32(&sm.packed), TCL_EPI * 32);
     sm.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -581,18 +700,44 @@ __global__ void __launch_bounds__(TCL_THREADS, 1) tcl_gemm_kernel(TcArgsL p) {
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   } else if (warp < TCL_EPI) {
     if (threadIdx.x < p.nseg) sm.seg[threadIdx.x] = tcl_seg_entry(MODE, threadIdx.x, p.K);
-    if (MODE == TCL_CH8)
-      for (int i = threadIdx.x; i < TT * 16; i += TCL_EPI * 32) {
-        const int t = t0 + i / 16;
-        sm.xsl[i / 16][i % 16] = t < p.B ? p.xsl[(size_t)t * 16 + i % 16] : 0;
-      }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = sm.tmem;
-  if (warp >= TCL_EPI) tcl_producer<MODE, TT>(p, sm, tmem, warp - TCL_EPI, lane, nunits);
-  else tcl_epilogue<MODE, TT>(p, sm, tmem, warp, lane, t0, nunits);
+  if (warp >= TCL_EPI) {
+    tcl_producer<MODE, TT>(p, sm, tmem, warp - TCL_EPI, lane, nunits);
+  } else {
+    // the CTA's sequences into its B tiles (the producers copy their first
+    // weight tiles meanwhile), made visible to the MMAs (async proxy) before
+    // each thread's arrival on sm.packed; or their scales and lane sums
+    static_assert(TT == TCL_EPI, "one sequence per epilogue warp");
+    const int m = t0 + warp;
+    if (p.res) {
+      constexpr int STAGE = TCT_A_BYTES + 4 * TT * TC_KB;
+      uint8_t *tiles = &sm.stage[0][TCT_A_BYTES];
+      // the other halves of the warp's rows (row 2 t + h holds codes in
+      // chunks of parity h only): zero
+      for (int i = lane; i < 16 * p.nkb; i += 32) {
+        const int kb = i >> 4, rr = (i >> 2) & 3, row = (rr & 2) * TT + 2 * warp + (rr & 1);
+        const int chunk = 2 * (i & 3) + 1 - (rr & 1);
+        *(uint4 *)(tiles + (size_t)kb * STAGE + tc_sw128_off(row, chunk)) = make_uint4(0, 0, 0, 0);
+      }
+      const bool stage_ln = p.ln_w != nullptr && (size_t)p.K * 8 <= sizeof(sm.tree);
+      const float sxm = tcl_pack_seq<TT>(p.x + (size_t)m * p.K, p.ln_w, p.ln_b, p.K, MODE, m < p.B, warp, tiles,
+                                         STAGE, sm.xsl[warp], stage_ln ? &sm.tree[0][0][0] : nullptr, TCL_EPI * 32,
+                                         lane);
+      if (lane == 0) sm.sx[warp] = sxm;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    } else {
+      if (lane == 0) sm.sx[warp] = m < p.B ? p.sx[m] : 1.0f;
+      if (MODE == TCL_CH8 && lane < 16) sm.xsl[warp][lane] = m < p.B ? p.xsl[(size_t)m * 16 + lane] : 0;
+    }
+    tc_mbar_arrive(tc_u32(&sm.packed));
+    // sm.sx and sm.xsl of every sequence before the epilogue reads them
+    asm volatile("bar.sync 1, %0;" ::"r"(TCL_EPI * 32) : "memory");
+    tcl_epilogue<MODE, TT>(p, sm, tmem, warp, lane, t0, nunits);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == TCL_EPI) {
