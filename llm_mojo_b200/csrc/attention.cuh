@@ -41,6 +41,10 @@ __device__ __forceinline__ void kv_cp_async16(void *dst, const void *src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
                : "memory");
 }
+__device__ __forceinline__ void kv_cp_async4(void *dst, const void *src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((unsigned)__cvta_generic_to_shared(dst)), "l"(src)
+               : "memory");
+}
 
 // QuantKV.quantize (kvcache.mojo:319-331) of one head's 64 values by one
 // warp... any block of >= head_dim threads: threads [0, head_dim) hold x.
@@ -101,69 +105,105 @@ __global__ void dkv_store_kernel(KV8View c, const float *qkv, int layer, int pos
 // attend_float_one for token t (position pos0 + t), head h. grid (n_head, T).
 // With store != 0 (decode, T == 1) the CTA first stores this token's key and
 // value for its head, which is all its own attention reads of this step.
-// Shared memory: kv8_attend_smem(cap, head_dim), cap >= the positions any
-// query of the launch sees (at most max_t).
+// Every read the CTA makes of the cache is issued at its start: the value
+// codes, both scale columns, the query and (KST) the key codes are copied
+// into shared memory (cp.async) while the token's key and value are
+// quantized, and this token's codes and scales are written to the shared
+// copies as well as to the cache, so the CTA waits for memory once. The
+// arithmetic and its order are attend_float_one's: 16 score lanes of q * k
+// over 4 chunks, halving tree, * ks, * scale; exp of (score - max); the total
+// summed in position order; acc[d] = fma(p * vs, v[s][d], acc) in position
+// order. Key rows in shared memory hold their 16-byte chunks in the order ch
+// ^ ((s >> 1) & 3), so that the 8 rows of each quarter warp's 16-byte loads
+// fall in distinct banks. Shared memory: kv8_attend_smem(cap, head_dim, KST),
+// cap >= the positions any query of the launch sees (at most max_t).
+template <bool KST>
 __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out, const float *qkv, int layer,
                                                          int pos0, const int *pos_dev, int store, int cap) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float red[40];
   const int h = blockIdx.x, t = blockIdx.y;
   const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with gridDim.y rows
-  const int HS = c.head_dim, C = c.n_head * HS;
+  const int HS = c.head_dim, C = c.n_head * HS, cpr = HS / 16;
   qkv += (size_t)blockIdx.z * gridDim.y * 3 * C;
   out += (size_t)blockIdx.z * gridDim.y * C;
   const int P0 = pos_dev ? *pos_dev : pos0;
   const int npos = P0 + t + 1;
   const float *q = qkv + (size_t)t * 3 * C + h * HS;
-  float *sc = sm;               // [npos] scores, then exponentials
-  float *ps = sm + cap;         // [npos] p * vs
-  float *qs = sm + 2 * cap;     // [HS] query
-  // the values of this head, [npos][HS] codes: copied into shared memory
-  // while the scores are computed; the positions before this token's now,
-  // this token's row (which the store below writes) after the store
-  int8_t *vst = (int8_t *)(((uintptr_t)(sm + 2 * cap + HS) + 15) & ~(uintptr_t)15);
-  const int cpr = HS / 16;
-  const int8_t *vb = c.v + ((size_t)layer * c.max_t * c.n_head + h) * HS;
-  {
-    const int npre = store ? npos - 1 : npos;
-    for (int i = threadIdx.x; i < npre * cpr; i += blockDim.x) {
-      const int s = i / cpr, ch = i % cpr;
-      kv_cp_async16(vst + (size_t)s * HS + ch * 16, vb + (size_t)s * c.n_head * HS + ch * 16);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+  float *sc = sm;              // [cap] scores, then exponentials
+  float *ps = sm + cap;        // [cap] p * vs
+  float *kss = sm + 2 * cap;   // [cap] key scales
+  float *vss = sm + 3 * cap;   // [cap] value scales
+  float *qs = sm + 4 * cap;    // [HS] query
+  int8_t *vst = (int8_t *)(((uintptr_t)(qs + HS) + 15) & ~(uintptr_t)15);  // [cap][HS] value codes
+  int8_t *kst = vst + (size_t)cap * HS;                                   // [cap][HS] key codes (KST)
+  const size_t slot0 = (size_t)layer * c.max_t * c.n_head + h;  // cache slot of position s: slot0 + s * n_head
+  const int8_t *vb = c.v + slot0 * HS, *kb = c.k + slot0 * HS;
+  const size_t rs = (size_t)c.n_head * HS;
+  const int npre = store ? npos - 1 : npos;
+  for (int i = threadIdx.x; i < npre * cpr; i += blockDim.x) {
+    const int s = i / cpr, ch = i - s * cpr;
+    kv_cp_async16(vst + (size_t)s * HS + ch * 16, vb + (size_t)s * rs + ch * 16);
+    if (KST) kv_cp_async16(kst + (size_t)s * HS + ((ch ^ ((s >> 1) & 3)) * 16), kb + (size_t)s * rs + ch * 16);
   }
+  for (int s = threadIdx.x; s < npre; s += blockDim.x) {
+    kv_cp_async4(kss + s, c.ks + slot0 + (size_t)s * c.n_head);
+    kv_cp_async4(vss + s, c.vs + slot0 + (size_t)s * c.n_head);
+  }
+  if (((uintptr_t)q & 15) == 0)
+    for (int i = threadIdx.x; i < HS / 4; i += blockDim.x) kv_cp_async16(qs + 4 * i, q + 4 * i);
+  else
+    for (int i = threadIdx.x; i < HS; i += blockDim.x) qs[i] = q[i];
+  asm volatile("cp.async.commit_group;" ::: "memory");
 
   if (store) {
-    int d = threadIdx.x;
-    size_t sl = ((size_t)layer * c.max_t + (P0 + t)) * c.n_head + h;
+    // QuantKV.quantize of this token's key and value (quant_i8_head's
+    // arithmetic), into the cache and the shared copies
+    const int d = threadIdx.x, s = npos - 1;
+    const size_t sl = slot0 + (size_t)(P0 + t) * c.n_head;
     for (int which = 0; which < 2; which++) {
-      bool act = d < HS;
-      float x = act ? qkv[(size_t)t * 3 * C + (1 + which) * C + h * HS + d] : 0.0f;
-      float s = quant_i8_head(x, act, red, (which == 0 ? c.k : c.v) + sl * HS, d);
-      if (threadIdx.x == 0) (which == 0 ? c.ks : c.vs)[sl] = s;
+      const bool act = d < HS;
+      const float x = act ? qkv[(size_t)t * 3 * C + (1 + which) * C + h * HS + d] : 0.0f;
+      float a = act ? fabsf(x) : 0.0f;
+      for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = a;
+      __syncthreads();
+      float mx = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); w++) mx = fmaxf(mx, red[w]);
+      __syncthreads();
+      float sv = mx / 127.0f;
+      if (sv == 0.0f) sv = 1.0f;
+      const float inv = 1.0f / sv;
+      if (act) {
+        const int8_t code = (int8_t)roundf(x * inv);
+        (which == 0 ? c.k : c.v)[sl * HS + d] = code;
+        if (which == 1)
+          vst[(size_t)s * HS + d] = code;
+        else if (KST)
+          kst[(size_t)s * HS + (((d >> 4) ^ ((s >> 1) & 3)) << 4) + (d & 15)] = code;
+      }
+      if (threadIdx.x == 0) {
+        (which == 0 ? c.ks : c.vs)[sl] = sv;
+        (which == 0 ? kss : vss)[s] = sv;
+      }
     }
-    __syncthreads();
-    if (threadIdx.x < cpr)
-      *(int4 *)(vst + (size_t)(npos - 1) * HS + threadIdx.x * 16) =
-          __ldcg((const int4 *)(vb + (size_t)(npos - 1) * c.n_head * HS + threadIdx.x * 16));
   }
-  for (int i = threadIdx.x; i < HS; i += blockDim.x) qs[i] = q[i];
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
 
-  // scores: 16 lanes of q*k, 4 chunks each, halving tree, * ks, * scale.
   const float scale = 1.0f / sqrtf((float)HS);
   float mx = -__int_as_float(0x7f800000);
   for (int s = threadIdx.x; s < npos; s += blockDim.x) {
-    size_t sl = ((size_t)layer * c.max_t + s) * c.n_head + h;
-    const int8_t *kp = c.k + sl * HS;
+    const int8_t *kp = KST ? kst + (size_t)s * HS : c.k + (slot0 + (size_t)s * c.n_head) * HS;
+    const int sw = KST ? ((s >> 1) & 3) : 0;
     float d[16];
 #pragma unroll
     for (int l = 0; l < 16; l++) d[l] = 0.0f;
     for (int i = 0; i < HS; i += 16) {
-      int4 kv = *(const int4 *)(kp + i);
-      const int8_t *kb = (const int8_t *)&kv;
+      const int4 kv = *(const int4 *)(kp + (((i >> 4) ^ sw) << 4));
+      const int8_t *kc = (const int8_t *)&kv;
 #pragma unroll
-      for (int l = 0; l < 16; l++) d[l] = d[l] + qs[i + l] * i8_to_float(kb[l]);
+      for (int l = 0; l < 16; l++) d[l] = d[l] + qs[i + l] * i8_to_float(kc[l]);
     }
 #pragma unroll
     for (int l = 0; l < 8; l++) d[l] = d[l] + d[l + 8];
@@ -171,7 +211,7 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     for (int l = 0; l < 4; l++) d[l] = d[l] + d[l + 4];
     d[0] = d[0] + d[2];
     d[1] = d[1] + d[3];
-    float v = ((d[0] + d[1]) * c.ks[sl]) * scale;
+    const float v = ((d[0] + d[1]) * kss[s]) * scale;
     sc[s] = v;
     mx = fmaxf(mx, v);
   }
@@ -189,12 +229,7 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
   }
   __syncthreads();
   const float total = red[36];
-  for (int s = threadIdx.x; s < npos; s += blockDim.x) {
-    size_t sl = ((size_t)layer * c.max_t + s) * c.n_head + h;
-    float p = sc[s] / total;
-    ps[s] = p * c.vs[sl];
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
+  for (int s = threadIdx.x; s < npos; s += blockDim.x) ps[s] = (sc[s] / total) * vss[s];
   __syncthreads();
   // acc[d] = fma(p * vs, v[s][d], acc[d]) over positions in order.
   for (int d = threadIdx.x; d < HS; d += blockDim.x) {
@@ -214,10 +249,10 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
   }
 }
 
-// Dynamic shared memory of kv8_attend_kernel for queries that see at most
-// cap positions.
-__host__ __device__ inline size_t kv8_attend_smem(int cap, int HS) {
-  return (size_t)(2 * cap + HS) * 4 + 16 + (size_t)cap * HS;
+// Dynamic shared memory of kv8_attend_kernel<kst> for queries that see at
+// most cap positions.
+__host__ __device__ inline size_t kv8_attend_smem(int cap, int HS, bool kst) {
+  return (size_t)(4 * cap + HS) * 4 + 16 + (size_t)cap * HS * (kst ? 2 : 1);
 }
 
 // attend_float_one for QB consecutive query tokens of one head at once (the

@@ -324,9 +324,8 @@ cudaError_t configure_kernels() {
   for (const void *k : {(const void *)kv_prefill_kernel<0>, (const void *)kv_prefill_kernel<1>,
                         (const void *)kv_prefill_kernel<2>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxPrefillSmem);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute((const void *)kv8_attend_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kv8_attend_smem(1024, 128));
+  for (const void *k : {(const void *)kv8_attend_kernel<false>, (const void *)kv8_attend_kernel<true>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   auto tcs = [&](const void *k) {
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(TcSmem) + 1024);
@@ -1230,6 +1229,23 @@ llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T
   return LLMQ_OK;
 }
 
+// kv8_attend_kernel with the key codes staged in shared memory where they
+// fit beside the values (the launch's queries see at most cap positions).
+llmq_status kv8_attend(llmq_ctx *ctx, const KV8View &v, float *out, const float *qkv, int layer, int pos0,
+                       const int *pos_dev, int store, int cap, dim3 grid, cudaStream_t s) {
+  const int HS = v.head_dim;
+  if (kv8_attend_smem(cap, HS, true) <= (size_t)kMaxSmem)
+    kv8_attend_kernel<true><<<grid, 128, kv8_attend_smem(cap, HS, true), s>>>(v, out, qkv, layer, pos0, pos_dev,
+                                                                              store, cap);
+  else if (kv8_attend_smem(cap, HS, false) <= (size_t)kMaxSmem)
+    kv8_attend_kernel<false><<<grid, 128, kv8_attend_smem(cap, HS, false), s>>>(v, out, qkv, layer, pos0, pos_dev,
+                                                                                store, cap);
+  else
+    return fail(ctx, LLMQ_ERR_UNSUPPORTED, "context too long for the int8 cache kernel");
+  CKL();
+  return LLMQ_OK;
+}
+
 llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *qkv, int layer, int T, int pos0) {
   if (!ctx || !kv || !qkv || !out || T <= 0 || layer < 0 || layer >= kv->n_layer || pos0 < 0 ||
       pos0 + T > kv->max_t)
@@ -1251,8 +1267,8 @@ llmq_status llmq_kv_attend(llmq_ctx *ctx, llmq_kv *kv, float *out, const float *
                                                                                             pos0, T);
   } else if (kv->kind == LLMQ_KV_QUANT8) {
     // the last query sees pos0 + T positions
-    size_t sm = kv8_attend_smem(pos0 + T, kv->head_dim);
-    kv8_attend_kernel<<<grid, 128, sm, ctx->stream>>>(kv->v8, out, qkv, layer, pos0, nullptr, 0, pos0 + T);
+    const llmq_status st = kv8_attend(ctx, kv->v8, out, qkv, layer, pos0, nullptr, 0, pos0 + T, grid, ctx->stream);
+    if (st) return st;
   } else {
     ia_attend_kernel<<<grid, 256, ia_attend_smem(kv), ctx->stream>>>(kv->ia, out, qkv, layer, pos0, nullptr, 0,
                                                                      ia_mult());
@@ -1672,7 +1688,6 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
   const int C = m->C;
   embed_kernel<<<3, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->state);
   CKL();
-  size_t att_sm = kv8_attend_smem(m->max_t, C / m->n_head);
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
     GemvArgs a{};
@@ -1684,10 +1699,11 @@ llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
     a.out = m->qkv;
     a.epi = EPI_BIAS;
     CK(launch_gemv(ctx, a, PRO_LN, false, s));
-    if (m->kv->kind == LLMQ_KV_QUANT8)
-      kv8_attend_kernel<<<dim3(m->n_head, 1), 128, att_sm, s>>>(m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1,
-                                                                 m->max_t);
-    else
+    if (m->kv->kind == LLMQ_KV_QUANT8) {
+      const llmq_status st = kv8_attend(ctx, m->kv->v8, m->att, m->qkv, l, 0, &m->state->pos, 1, m->max_t,
+                                        dim3(m->n_head, 1), s);
+      if (st) return st;
+    } else
       ia_attend_kernel<<<dim3(m->n_head, 1), 256, ia_attend_smem(m->kv), s>>>(m->kv->ia, m->att, m->qkv, l, 0,
                                                                                &m->state->pos, 1, ia_mult());
     CKL();
@@ -2479,14 +2495,13 @@ llmq_status batch_decode_step(llmq_batch *bt, int B, int cap, cudaStream_t s) {
   const int C = m->C;
   embed_batch_kernel<<<B, 256, 0, s>>>(m->head->view(), m->wpe(), bt->x, bt->tokens, bt->state);
   CKL();
-  const size_t att_sm = kv8_attend_smem(cap, C / m->n_head);
   llmq_status st;
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
     if ((st = batch_linear(bt, w[0], bt->x, m->vec(l, 0), m->vec(l, 1), m->vec(l, 2), bt->qkv, B, EPI_BIAS, s)))
       return st;
-    kv8_attend_kernel<<<dim3(m->n_head, 1, B), 128, att_sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, bt->state, 1, cap);
-    CKL();
+    if ((st = kv8_attend(ctx, bt->kv, bt->att, bt->qkv, l, 0, bt->state, 1, cap, dim3(m->n_head, 1, B), s)))
+      return st;
     if ((st = batch_linear(bt, w[1], bt->att, nullptr, nullptr, m->vec(l, 3), bt->x, B, EPI_BIAS | EPI_RESID, s)))
       return st;
     if ((st = batch_linear(bt, w[2], bt->x, m->vec(l, 4), m->vec(l, 5), m->vec(l, 6), bt->fc, B, EPI_BIAS | EPI_GELU, s)))
