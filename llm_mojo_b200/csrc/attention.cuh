@@ -115,27 +115,29 @@ __global__ void dkv_store_kernel(KV8View c, const float *qkv, int layer, int pos
 // summed in position order; acc[d] = fma(p * vs, v[s][d], acc) in position
 // order. Key rows in shared memory hold their 16-byte chunks in the order ch
 // ^ ((s >> 1) & 3), so that the 8 rows of each quarter warp's 16-byte loads
-// fall in distinct banks. Shared memory: kv8_attend_smem(cap, head_dim, KST),
-// cap >= the positions any query of the launch sees (at most max_t).
-template <bool KST>
+// fall in distinct banks. HSC: the head size when fixed at compile time (64),
+// else 0. Shared memory: kv8_attend_smem(cap, head_dim, KST), cap >= the
+// positions any query of the launch sees (at most max_t).
+template <bool KST, int HSC>
 __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out, const float *qkv, int layer,
                                                          int pos0, const int *pos_dev, int store, int cap) {
   extern __shared__ __align__(16) float sm[];
   __shared__ float red[40];
   const int h = blockIdx.x, t = blockIdx.y;
   const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with gridDim.y rows
-  const int HS = c.head_dim, C = c.n_head * HS, cpr = HS / 16;
+  const int HS = HSC ? HSC : c.head_dim, C = c.n_head * HS, cpr = HS / 16;
+  cap = (cap + 3) & ~3;
   qkv += (size_t)blockIdx.z * gridDim.y * 3 * C;
   out += (size_t)blockIdx.z * gridDim.y * C;
   const int P0 = pos_dev ? *pos_dev : pos0;
   const int npos = P0 + t + 1;
   const float *q = qkv + (size_t)t * 3 * C + h * HS;
-  float *sc = sm;              // [cap] scores, then exponentials
-  float *ps = sm + cap;        // [cap] p * vs
-  float *kss = sm + 2 * cap;   // [cap] key scales
-  float *vss = sm + 3 * cap;   // [cap] value scales
-  float *qs = sm + 4 * cap;    // [HS] query
-  int8_t *vst = (int8_t *)(((uintptr_t)(qs + HS) + 15) & ~(uintptr_t)15);  // [cap][HS] value codes
+  float *qs = sm;              // [HS] query
+  float *sc = sm + HS;         // [cap] scores, then exponentials
+  float *ps = sc + cap;        // [cap] p * vs
+  float *kss = ps + cap;       // [cap] key scales
+  float *vss = kss + cap;      // [cap] value scales
+  int8_t *vst = (int8_t *)(((uintptr_t)(vss + cap) + 15) & ~(uintptr_t)15);  // [cap][HS] value codes
   int8_t *kst = vst + (size_t)cap * HS;                                   // [cap][HS] key codes (KST)
   const size_t slot0 = (size_t)layer * c.max_t * c.n_head + h;  // cache slot of position s: slot0 + s * n_head
   const int8_t *vb = c.v + slot0 * HS, *kb = c.k + slot0 * HS;
@@ -199,11 +201,18 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     float d[16];
 #pragma unroll
     for (int l = 0; l < 16; l++) d[l] = 0.0f;
-    for (int i = 0; i < HS; i += 16) {
-      const int4 kv = *(const int4 *)(kp + (((i >> 4) ^ sw) << 4));
-      const int8_t *kc = (const int8_t *)&kv;
 #pragma unroll
-      for (int l = 0; l < 16; l++) d[l] = d[l] + qs[i + l] * i8_to_float(kc[l]);
+    for (int i = 0; i < HS; i += 16) {
+      // code b as a float: the byte b + 128 in the low mantissa bits of
+      // 1.5 * 2^23 (one byte permute), minus 1.5 * 2^23 + 128; exact
+      const int4 kv = *(const int4 *)(kp + (((i >> 4) ^ sw) << 4));
+      const unsigned w[4] = {(unsigned)kv.x ^ 0x80808080u, (unsigned)kv.y ^ 0x80808080u,
+                             (unsigned)kv.z ^ 0x80808080u, (unsigned)kv.w ^ 0x80808080u};
+#pragma unroll
+      for (int l = 0; l < 16; l++) {
+        const float kf = __int_as_float((int)__byte_perm(w[l >> 2], 0x4B400000u, 0x7640u | (l & 3))) - 12583040.0f;
+        d[l] = d[l] + qs[i + l] * kf;
+      }
     }
 #pragma unroll
     for (int l = 0; l < 8; l++) d[l] = d[l] + d[l + 8];
@@ -236,22 +245,24 @@ __global__ void __launch_bounds__(128) kv8_attend_kernel(KV8View c0, float *out,
     float acc = 0.0f;
     const int8_t *vp = vst + d;
     int s = 0;
-    for (; s + 4 <= npos; s += 4) {
-      float v0 = i8_to_float(vp[(size_t)s * HS]), v1 = i8_to_float(vp[(size_t)(s + 1) * HS]);
-      float v2 = i8_to_float(vp[(size_t)(s + 2) * HS]), v3 = i8_to_float(vp[(size_t)(s + 3) * HS]);
-      acc = fmaf(ps[s], v0, acc);
-      acc = fmaf(ps[s + 1], v1, acc);
-      acc = fmaf(ps[s + 2], v2, acc);
-      acc = fmaf(ps[s + 3], v3, acc);
+    for (; s + 4 <= npos; s += 4, vp += 4 * HS) {
+      const float4 p4 = *(const float4 *)(ps + s);
+      const float v0 = i8_to_float(vp[0]), v1 = i8_to_float(vp[HS]);
+      const float v2 = i8_to_float(vp[2 * HS]), v3 = i8_to_float(vp[3 * HS]);
+      acc = fmaf(p4.x, v0, acc);
+      acc = fmaf(p4.y, v1, acc);
+      acc = fmaf(p4.z, v2, acc);
+      acc = fmaf(p4.w, v3, acc);
     }
-    for (; s < npos; s++) acc = fmaf(ps[s], i8_to_float(vp[(size_t)s * HS]), acc);
+    for (; s < npos; s++, vp += HS) acc = fmaf(ps[s], i8_to_float(vp[0]), acc);
     out[(size_t)t * C + h * HS + d] = acc;
   }
 }
 
-// Dynamic shared memory of kv8_attend_kernel<kst> for queries that see at
+// Dynamic shared memory of kv8_attend_kernel<kst, *> for queries that see at
 // most cap positions.
 __host__ __device__ inline size_t kv8_attend_smem(int cap, int HS, bool kst) {
+  cap = (cap + 3) & ~3;
   return (size_t)(4 * cap + HS) * 4 + 16 + (size_t)cap * HS * (kst ? 2 : 1);
 }
 

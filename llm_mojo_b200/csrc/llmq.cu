@@ -324,7 +324,8 @@ cudaError_t configure_kernels() {
   for (const void *k : {(const void *)kv_prefill_kernel<0>, (const void *)kv_prefill_kernel<1>,
                         (const void *)kv_prefill_kernel<2>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxPrefillSmem);
-  for (const void *k : {(const void *)kv8_attend_kernel<false>, (const void *)kv8_attend_kernel<true>})
+  for (const void *k : {(const void *)kv8_attend_kernel<false, 0>, (const void *)kv8_attend_kernel<true, 0>,
+                        (const void *)kv8_attend_kernel<true, 64>})
     if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
   auto tcs = [&](const void *k) {
     if (e == cudaSuccess)
@@ -1234,12 +1235,15 @@ llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T
 llmq_status kv8_attend(llmq_ctx *ctx, const KV8View &v, float *out, const float *qkv, int layer, int pos0,
                        const int *pos_dev, int store, int cap, dim3 grid, cudaStream_t s) {
   const int HS = v.head_dim;
-  if (kv8_attend_smem(cap, HS, true) <= (size_t)kMaxSmem)
-    kv8_attend_kernel<true><<<grid, 128, kv8_attend_smem(cap, HS, true), s>>>(v, out, qkv, layer, pos0, pos_dev,
-                                                                              store, cap);
+  if (HS == 64 && kv8_attend_smem(cap, HS, true) <= (size_t)kMaxSmem)
+    kv8_attend_kernel<true, 64><<<grid, 128, kv8_attend_smem(cap, HS, true), s>>>(v, out, qkv, layer, pos0, pos_dev,
+                                                                                  store, cap);
+  else if (kv8_attend_smem(cap, HS, true) <= (size_t)kMaxSmem)
+    kv8_attend_kernel<true, 0><<<grid, 128, kv8_attend_smem(cap, HS, true), s>>>(v, out, qkv, layer, pos0, pos_dev,
+                                                                                 store, cap);
   else if (kv8_attend_smem(cap, HS, false) <= (size_t)kMaxSmem)
-    kv8_attend_kernel<false><<<grid, 128, kv8_attend_smem(cap, HS, false), s>>>(v, out, qkv, layer, pos0, pos_dev,
-                                                                                store, cap);
+    kv8_attend_kernel<false, 0><<<grid, 128, kv8_attend_smem(cap, HS, false), s>>>(v, out, qkv, layer, pos0,
+                                                                                   pos_dev, store, cap);
   else
     return fail(ctx, LLMQ_ERR_UNSUPPORTED, "context too long for the int8 cache kernel");
   CKL();
