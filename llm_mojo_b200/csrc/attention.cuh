@@ -64,23 +64,40 @@ __device__ __forceinline__ float quant_i8_head(float x, bool active, float *red,
 }
 
 // Stores the keys and values of T tokens at positions pos0.. of `layer`
-// (QuantKV.store, kvcache.mojo:333-342). grid (n_head, T, 2 * sequences),
-// block >= 64; sequence b's rows of qkv follow sequence b-1's T rows.
-__global__ void kv8_store_kernel(KV8View c0, const float *qkv, int layer, int pos0, const int *pos_dev) {
-  __shared__ float red[32];
-  int h = blockIdx.x, t = blockIdx.y, which = blockIdx.z & 1;  // 0 = key, 1 = value
-  const int sb = blockIdx.z >> 1;
+// (QuantKV.store, kvcache.mojo:333-342) for nseq sequences, sequence b's T
+// rows of qkv after sequence b - 1's. One warp per (sequence, token, head,
+// key or value): lane L holds elements L + 32 j (head_dim <= 128); the
+// maximum of |x| (exact in any order), s = max / 127 (1 when 0) and the codes
+// round(x / s) are quant_i8_head's. grid ceil(warps / 8), 256 threads.
+__global__ void __launch_bounds__(256) kv8_store_kernel(KV8View c0, const float *qkv, int layer, int pos0,
+                                                        const int *pos_dev, int T, int nseq) {
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int nh = c0.n_head;
+  if (gw >= nseq * T * nh * 2) return;
+  const int which = gw & 1, h = (gw >> 1) % nh, rest = (gw >> 1) / nh, t = rest % T, sb = rest / T;
   const KV8View c = c0.of(sb);
-  qkv += (size_t)sb * gridDim.y * 3 * c.n_head * c.head_dim;
-  int pos = (pos_dev ? *pos_dev : pos0) + t;
-  int HS = c.head_dim, C = c.n_head * HS;
-  int d = threadIdx.x;
-  bool act = d < HS;
-  float x = act ? qkv[(size_t)t * 3 * C + (1 + which) * C + h * HS + d] : 0.0f;
-  size_t sl = ((size_t)layer * c.max_t + pos) * c.n_head + h;
+  const int HS = c.head_dim, C = nh * HS;
+  const float *src = qkv + ((size_t)sb * T + t) * 3 * C + (1 + which) * C + h * HS;
+  const size_t sl = ((size_t)layer * c.max_t + (pos_dev ? *pos_dev : pos0) + t) * nh + h;
   int8_t *dst = (which == 0 ? c.k : c.v) + sl * HS;
-  float s = quant_i8_head(x, act, red, dst, d);
-  if (threadIdx.x == 0) (which == 0 ? c.ks : c.vs)[sl] = s;
+  float xv[4];
+  float a = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int d = lane + 32 * j;
+    xv[j] = d < HS ? src[d] : 0.0f;
+    a = fmaxf(a, fabsf(xv[j]));
+  }
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  float sv = a / 127.0f;
+  if (sv == 0.0f) sv = 1.0f;
+  const float inv = 1.0f / sv;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int d = lane + 32 * j;
+    if (d < HS) dst[d] = (int8_t)roundf(xv[j] * inv);
+  }
+  if (lane == 0) (which == 0 ? c.ks : c.vs)[sl] = sv;
 }
 
 // DenseKV.store (kvcache.mojo:204-208): the keys and values of T tokens at

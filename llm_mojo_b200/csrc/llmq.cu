@@ -729,9 +729,9 @@ llmq_status tct_linear(llmq_ctx *ctx, const llmq_weight *w, const float *x, cons
     CKL();
   }
   if (TT == 32)
-    tct_split_rows_kernel<32><<<t_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, b, sx, xsum, xq);
+    tct_split_rows_kernel<32><<<(t_pad + 7) / 8, 256, 0, ctx->stream>>>(x, T, t_pad, K, nseg, seg, b, sx, xsum, xq);
   else
-    tct_split_rows_kernel<64><<<t_pad, 256, 0, ctx->stream>>>(x, T, K, nseg, seg, b, sx, xsum, xq);
+    tct_split_rows_kernel<64><<<(t_pad + 7) / 8, 256, 0, ctx->stream>>>(x, T, t_pad, K, nseg, seg, b, sx, xsum, xq);
   CKL();
   if (ntiles > 0) {
     TcArgsT p{};
@@ -1217,15 +1217,14 @@ llmq_status llmq_kv_store(llmq_ctx *ctx, llmq_kv *kv, int layer, int pos0, int T
   if (!ctx || !kv || !qkv || T <= 0 || layer < 0 || layer >= kv->n_layer || pos0 < 0 || pos0 + T > kv->max_t)
     return fail(ctx, LLMQ_ERR_INVALID, "bad layer or positions");
   CK(cudaSetDevice(ctx->device));
-  dim3 grid(kv->n_head, T, 2);
   if (kv->kind == LLMQ_KV_QUANT8)
-    kv8_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr);
+    kv8_store_kernel<<<(kv->n_head * T * 2 + 7) / 8, 256, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0, nullptr, T, 1);
   else if (kv->kind == LLMQ_KV_F32)
     dkv_store_kernel<1><<<T, 256, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0);
   else if (kv->kind == LLMQ_KV_BF16)
     dkv_store_kernel<2><<<T, 256, 0, ctx->stream>>>(kv->v8, qkv, layer, pos0);
   else
-    ia_store_kernel<<<grid, 128, 0, ctx->stream>>>(kv->ia, qkv, layer, pos0);
+    ia_store_kernel<<<dim3(kv->n_head, T, 2), 128, 0, ctx->stream>>>(kv->ia, qkv, layer, pos0);
   CKL();
   return LLMQ_OK;
 }
@@ -2553,7 +2552,7 @@ llmq_status batch_prompt(llmq_batch *bt, int B, int P, cudaStream_t s) {
     layernorm_kernel<<<T, 256, C * 4, s>>>(bt->xn, bt->x, m->vec(l, 0), m->vec(l, 1), C);
     CKL();
     if ((st = llmq_linear(ctx, w[0], bt->xn, m->vec(l, 2), bt->qkv, T, C, 3 * C, LLMQ_BIAS)) != LLMQ_OK) return st;
-    kv8_store_kernel<<<dim3(m->n_head, P, 2 * B), 128, 0, s>>>(bt->kv, bt->qkv, l, 0, nullptr);
+    kv8_store_kernel<<<(m->n_head * P * 2 * B + 7) / 8, 256, 0, s>>>(bt->kv, bt->qkv, l, 0, nullptr, P, B);
     CKL();
     const size_t sm = kv8_prefill_smem(P, C / m->n_head);
     kv_prefill_kernel<0><<<dim3(m->n_head, (P + KV_QB - 1) / KV_QB, B), 256, sm, s>>>(bt->kv, bt->att, bt->qkv, l, 0, P);

@@ -529,34 +529,54 @@ __device__ __forceinline__ bool tc_wait_flag(int *abort, unsigned bar, unsigned 
 // quantize_rows of rows [0, T) into the transposed B tiles
 // [t_tile][kb][plane l' (TT rows), plane h (TT rows)], sx[m], the
 // per-segment sums of x (xsum, when non-null) and the plain int16 rows (xq,
-// when non-null). One CTA per row of the padded token count; rows >= T hold
-// codes 0 (their outputs are not stored).
+// when non-null). One warp per row of the padded token count t_pad (8 per
+// CTA; the max of |x| is exact in any order, the codes and segment sums are
+// integers); rows >= T hold codes 0 (their outputs are not stored).
 template <int TT>
-__global__ void __launch_bounds__(256) tct_split_rows_kernel(const float *x, int T, int K, int nseg, int seg,
-                                                             uint8_t *b, float *sx, int *xsum, int16_t *xq) {
-  __shared__ float red[64];
-  __shared__ int ssum[TC_MAX_GROUPS * 8];
-  const int m = blockIdx.x, nkb = K / TC_KB;
+__global__ void __launch_bounds__(256) tct_split_rows_kernel(const float *x, int T, int t_pad, int K, int nseg,
+                                                             int seg, uint8_t *b, float *sx, int *xsum, int16_t *xq) {
+  __shared__ int ssum[8][TC_MAX_GROUPS * 8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * 8 + warp, nkb = K / TC_KB;
+  if (m >= t_pad) return;
   const bool valid = m < T;
   const float *row = x + (size_t)m * K;
-  for (int i = threadIdx.x; i < nseg; i += blockDim.x) ssum[i] = 0;
+  const bool vec = ((uintptr_t)row & 15) == 0;
+  int *ss = ssum[warp];
+  if (xsum)
+    for (int i = lane; i < nseg; i += 32) ss[i] = 0;
+  __syncwarp();
   float mx = 0.0f;
   if (valid)
-    for (int i = threadIdx.x; i < K; i += blockDim.x) mx = fmaxf(mx, fabsf(row[i]));
-  mx = block_max(mx, red);
+    for (int i = lane; i < K; i += 32) mx = fmaxf(mx, fabsf(row[i]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   float s = mx / 32767.0f;
   if (s == 0.0f) s = 1.0f;
   const float inv = 1.0f / s;
   const int tt = m / TT, r = m % TT;
-  for (int ci = threadIdx.x; ci < K / 16; ci += blockDim.x) {
+  for (int ci = lane; ci < K / 16; ci += 32) {
     const int k0 = ci * 16, kb = k0 / TC_KB, chunk = (k0 % TC_KB) / 16;
     uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
     int part = 0;
     if (valid) {
+      float v[16];
+      if (vec) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 f = *(const float4 *)(row + k0 + 4 * j);
+          v[4 * j] = f.x;
+          v[4 * j + 1] = f.y;
+          v[4 * j + 2] = f.z;
+          v[4 * j + 3] = f.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = row[k0 + i];
+      }
       uint32_t qw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
       for (int i = 0; i < 16; i++) {
-        const int16_t q = (int16_t)roundf(row[k0 + i] * inv);
+        const int16_t q = (int16_t)roundf(v[i] * inv);
         part += q;
         qw[i >> 1] |= (uint32_t)(uint16_t)q << (16 * (i & 1));
         lo[i >> 2] |= (uint32_t)(((uint16_t)q & 0xFF) ^ 0x80) << (8 * (i & 3));  // xl - 128
@@ -567,16 +587,16 @@ __global__ void __launch_bounds__(256) tct_split_rows_kernel(const float *x, int
         dq[0] = make_uint4(qw[0], qw[1], qw[2], qw[3]);
         dq[1] = make_uint4(qw[4], qw[5], qw[6], qw[7]);
       }
-      if (xsum) atomicAdd(&ssum[k0 / seg], part);
+      if (xsum) atomicAdd(&ss[k0 / seg], part);
     }
     uint8_t *base = b + ((size_t)tt * nkb + kb) * (2 * TT * TC_KB) + tc_sw128_off(r, chunk);
     *(uint4 *)base = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     *(uint4 *)(base + TT * TC_KB) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) sx[m] = valid ? s : 0.0f;
+  __syncwarp();
+  if (lane == 0) sx[m] = valid ? s : 0.0f;
   if (xsum)
-    for (int i = threadIdx.x; i < nseg; i += blockDim.x) xsum[(size_t)m * nseg + i] = ssum[i];
+    for (int i = lane; i < nseg; i += 32) xsum[(size_t)m * nseg + i] = ss[i];
 }
 
 // W[n][s]: the sum over segment s of row n's weight values (u - zp for int4,
