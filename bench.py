@@ -352,9 +352,10 @@ def run_batched(args):
                         "d2h_bytes_per_step": n_seqs * n_steps * 4},
                 "last_sequence_matches_single_decode": bool(list(check_ids[-1]) == list(single)),
                 # per generation: the prompt (embed, 12 x (2 LayerNorm + 4 x (split + GEMM) + store +
-                # attention), gather, head quantize + GEMV, argmax, state) and 127 decode-step graphs
-                # (advance, embed, 12 x (4 x (quantize + GEMV) + attention), head quantize + GEMV, argmax)
-                "gpu_launches": args.steps * ((1 + 12 * 12 + 1 + 2 + 1 + 1) + (n_steps - 1) * (2 + 12 * 9 + 3)),
+                # attention), gather, head GEMM (quantizing inside), argmax, state) and 127 decode-step
+                # graphs (advance, embed, 12 x (3 GEMMs quantizing inside + quantize + GEMM for the
+                # 3072-column rows + attention), head GEMM, argmax)
+                "gpu_launches": args.steps * ((1 + 12 * 12 + 1 + 1 + 1 + 1) + (n_steps - 1) * (2 + 12 * 6 + 2)),
                 "cpu_baseline": cpu}
         print(json.dumps(line))
     batch.free()
