@@ -292,12 +292,16 @@ __host__ __device__ inline size_t kv8_attend_smem(int cap, int HS, bool kst) {
 // total summed in position order; acc[d] = fma(p * vs, v[d], acc) in
 // position order. grid (n_head, ceil(T / QB)), 256 threads; shared memory
 // kv8_prefill_smem(P, head_dim), P the positions the block's last query sees.
+// Tile rows are HS + 4 floats (16-byte loads along a row, and the 8 rows of
+// a quarter warp's loads in distinct banks); score rows are padded to a
+// multiple of 4 positions (16-byte loads of 4 consecutive positions).
 constexpr int KV_QB = 16;
 constexpr int KV_TILE = 128;
 
 __host__ __device__ inline size_t kv8_prefill_smem(int P, int HS) {
-  // tile [128][HS + 1] floats, its scales [128], q [QB][HS], scores [QB][P], totals [QB]
-  return (size_t)KV_TILE * (HS + 1) * 4 + KV_TILE * 4 + (size_t)KV_QB * HS * 4 + (size_t)KV_QB * P * 4 + KV_QB * 4;
+  // tile [128][HS + 4] floats, its scales [128], q [QB][HS], scores [QB][P padded], totals [QB]
+  const int Pp = (P + 3) & ~3;
+  return (size_t)KV_TILE * (HS + 4) * 4 + KV_TILE * 4 + (size_t)KV_QB * HS * 4 + (size_t)KV_QB * Pp * 4 + KV_QB * 4;
 }
 
 // KVT: 0 QuantKV[8] (int8 codes and per-head scales), 1 DenseKV[float32],
@@ -310,15 +314,16 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
   const int h = blockIdx.x, t0 = blockIdx.y * KV_QB;
   const int nq = min(KV_QB, T - t0);
   const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with T rows
-  const int HS = c.head_dim, C = c.n_head * HS, HP = HS + 1;
+  const int HS = c.head_dim, C = c.n_head * HS, HP = HS + 4;
   qkv += (size_t)blockIdx.z * T * 3 * C;
   out += (size_t)blockIdx.z * T * C;
   const int P = pos0 + t0 + nq;  // positions the last query of the block sees
-  float *tile = kvp_sm;                        // [128][HS + 1]
+  const int Pp = (P + 3) & ~3;   // score row stride
+  float *tile = kvp_sm;                        // [128][HS + 4]
   float *tsc = tile + KV_TILE * HP;            // [128]
   float *qs = tsc + KV_TILE;                   // [QB][HS]
-  float *sc = qs + KV_QB * HS;                 // [QB][P]
-  float *tot = sc + (size_t)KV_QB * P;         // [QB]
+  float *sc = qs + KV_QB * HS;                 // [QB][Pp]
+  float *tot = sc + (size_t)KV_QB * Pp;        // [QB]
   const int tid = threadIdx.x;
   const size_t head_stride = (size_t)c.n_head * HS;
   const int8_t *kbase = c.k + ((size_t)layer * c.max_t * c.n_head + h) * HS;
@@ -341,9 +346,10 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
         const int r = i / cpr, ch = i % cpr;
         int4 raw = *(const int4 *)(src + (size_t)(s0 + r) * head_stride + ch * 16);
         const int8_t *b = (const int8_t *)&raw;
-        float *dst = tile + r * HP + ch * 16;
+        float4 *dst = (float4 *)(tile + r * HP + ch * 16);
 #pragma unroll
-        for (int l = 0; l < 16; l++) dst[l] = (float)b[l];
+        for (int l = 0; l < 4; l++)
+          dst[l] = make_float4((float)b[4 * l], (float)b[4 * l + 1], (float)b[4 * l + 2], (float)b[4 * l + 3]);
       }
       for (int r = tid; r < n; r += blockDim.x) tsc[r] = scl[(sbase + (size_t)(s0 + r) * c.n_head)];
     } else {
@@ -380,12 +386,24 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
       for (int i0 = 0; i0 < HS; i0 += 16) {
         float kf[16];
 #pragma unroll
-        for (int l = 0; l < 16; l++) kf[l] = kr[i0 + l];
+        for (int l = 0; l < 4; l++) {
+          const float4 k4 = *(const float4 *)(kr + i0 + 4 * l);
+          kf[4 * l] = k4.x;
+          kf[4 * l + 1] = k4.y;
+          kf[4 * l + 2] = k4.z;
+          kf[4 * l + 3] = k4.w;
+        }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          const float *q = qs + (q0 + j) * HS + i0;
+          const float4 *q4 = (const float4 *)(qs + (q0 + j) * HS + i0);
 #pragma unroll
-          for (int l = 0; l < 16; l++) d[j][l] = d[j][l] + q[l] * kf[l];
+          for (int l = 0; l < 4; l++) {
+            const float4 q = q4[l];
+            d[j][4 * l] = d[j][4 * l] + q.x * kf[4 * l];
+            d[j][4 * l + 1] = d[j][4 * l + 1] + q.y * kf[4 * l + 1];
+            d[j][4 * l + 2] = d[j][4 * l + 2] + q.z * kf[4 * l + 2];
+            d[j][4 * l + 3] = d[j][4 * l + 3] + q.w * kf[4 * l + 3];
+          }
         }
       }
 #pragma unroll
@@ -399,7 +417,7 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
         for (int l = 0; l < 4; l++) e[l] = e[l] + e[l + 4];
         e[0] = e[0] + e[2];
         e[1] = e[1] + e[3];
-        sc[(size_t)qi * P + s] = KVT == 0 ? ((e[0] + e[1]) * tsc[r]) * scale : (e[0] + e[1]) * scale;
+        sc[(size_t)qi * Pp + s] = KVT == 0 ? ((e[0] + e[1]) * tsc[r]) * scale : (e[0] + e[1]) * scale;
       }
     }
   }
@@ -410,7 +428,7 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
   const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
   for (int qi = warp; qi < nq; qi += nwarps) {
     const int np = pos0 + t0 + qi + 1;
-    float *row = sc + (size_t)qi * P;
+    float *row = sc + (size_t)qi * Pp;
     float mx = -__int_as_float(0x7f800000);
     for (int s = lane; s < np; s += 32) mx = fmaxf(mx, row[s]);
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -419,7 +437,7 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
   __syncthreads();
   if (tid < nq) {
     const int np = pos0 + t0 + tid + 1;
-    const float *row = sc + (size_t)tid * P;
+    const float *row = sc + (size_t)tid * Pp;
     float total = 0.0f;
     int s = 0;
     for (; s + 8 <= np; s += 8) {
@@ -445,10 +463,11 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
     __syncthreads();
     // p * vs for this tile's positions
     const int n = min(KV_TILE, P - s0);
-    for (int i = tid; i < nq * n; i += blockDim.x) {
-      const int qi = i / n, r = i % n, s = s0 + r;
-      if (s < pos0 + t0 + qi + 1)
-        sc[(size_t)qi * P + s] = KVT == 0 ? (sc[(size_t)qi * P + s] / tot[qi]) * tsc[r] : sc[(size_t)qi * P + s] / tot[qi];
+    for (int qi = warp; qi < nq; qi += nwarps) {
+      float *row = sc + (size_t)qi * Pp;
+      const int end = min(n, pos0 + t0 + qi + 1 - s0);
+      for (int r = lane; r < end; r += 32)
+        row[s0 + r] = KVT == 0 ? (row[s0 + r] / tot[qi]) * tsc[r] : row[s0 + r] / tot[qi];
     }
     __syncthreads();
     if (tid < nchains) {
@@ -462,11 +481,39 @@ __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out,
         npj[j] = qi < nq ? min(pos0 + t0 + qi + 1, s0 + n) : s0;  // this query's positions within the tile
         send = max(send, npj[j]);
       }
-      for (int s = s0; s < send; s++) {
-        const float v = tile[(s - s0) * HP + dd];
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-          if (s < npj[j]) acc[j] = fmaf(sc[(size_t)(q0 + j) * P + s], v, acc[j]);
+      // positions every one of the 4 queries sees (4 at a time, no
+      // compares), then the ragged end
+      const int lo = min(min(npj[0], npj[1]), min(npj[2], npj[3]));
+      const float *vp = tile + dd;
+      const float *sr0 = sc + (size_t)q0 * Pp, *sr1 = sr0 + Pp, *sr2 = sr1 + Pp, *sr3 = sr2 + Pp;
+      int s = s0;
+      for (; s + 4 <= lo; s += 4, vp += 4 * HP) {
+        const float v0 = vp[0], v1 = vp[HP], v2 = vp[2 * HP], v3 = vp[3 * HP];
+        const float4 p0 = *(const float4 *)(sr0 + s), p1 = *(const float4 *)(sr1 + s);
+        const float4 p2 = *(const float4 *)(sr2 + s), p3 = *(const float4 *)(sr3 + s);
+        acc[0] = fmaf(p0.x, v0, acc[0]);
+        acc[1] = fmaf(p1.x, v0, acc[1]);
+        acc[2] = fmaf(p2.x, v0, acc[2]);
+        acc[3] = fmaf(p3.x, v0, acc[3]);
+        acc[0] = fmaf(p0.y, v1, acc[0]);
+        acc[1] = fmaf(p1.y, v1, acc[1]);
+        acc[2] = fmaf(p2.y, v1, acc[2]);
+        acc[3] = fmaf(p3.y, v1, acc[3]);
+        acc[0] = fmaf(p0.z, v2, acc[0]);
+        acc[1] = fmaf(p1.z, v2, acc[1]);
+        acc[2] = fmaf(p2.z, v2, acc[2]);
+        acc[3] = fmaf(p3.z, v2, acc[3]);
+        acc[0] = fmaf(p0.w, v3, acc[0]);
+        acc[1] = fmaf(p1.w, v3, acc[1]);
+        acc[2] = fmaf(p2.w, v3, acc[2]);
+        acc[3] = fmaf(p3.w, v3, acc[3]);
+      }
+      for (; s < send; s++, vp += HP) {
+        const float v = vp[0];
+        if (s < npj[0]) acc[0] = fmaf(sr0[s], v, acc[0]);
+        if (s < npj[1]) acc[1] = fmaf(sr1[s], v, acc[1]);
+        if (s < npj[2]) acc[2] = fmaf(sr2[s], v, acc[2]);
+        if (s < npj[3]) acc[3] = fmaf(sr3[s], v, acc[3]);
       }
     }
   }
