@@ -2351,13 +2351,13 @@ llmq_status batch_linear_tcl(llmq_batch *bt, const llmq_weight *w, const float *
     a.ln_w = ln_w;
     a.ln_b = ln_b;
   } else {
-    const size_t qsm = (size_t)8 * K * 4;
+    const size_t qsm = (size_t)K * 4;
     if (ln_w)
-      tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad / 8, 256, qsm, s>>>(x, ln_w, ln_b, B, bpad, K, mode, bt->tcl_b,
-                                                                       bt->sx, bt->xsi);
+      tcl_quant_pack_kernel<TCL_TT, PRO_LN><<<bpad, 256, qsm, s>>>(x, ln_w, ln_b, B, bpad, K, mode, bt->tcl_b,
+                                                                   bt->sx, bt->xsi);
     else
-      tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad / 8, 256, qsm, s>>>(x, nullptr, nullptr, B, bpad, K, mode,
-                                                                          bt->tcl_b, bt->sx, bt->xsi);
+      tcl_quant_pack_kernel<TCL_TT, PRO_QUANT><<<bpad, 256, qsm, s>>>(x, nullptr, nullptr, B, bpad, K, mode,
+                                                                      bt->tcl_b, bt->sx, bt->xsi);
     CKL();
     a.b = bt->tcl_b;
     a.sx = bt->sx;
@@ -2706,8 +2706,8 @@ llmq_status llmq_batch_create(llmq_ctx *ctx, llmq_model *m, int max_seqs, int ma
     attr(k, kBgemvSmem);
   attr((const void *)tcl_gemm_kernel<TCL_BLK4, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
   attr((const void *)tcl_gemm_kernel<TCL_CH8, TCL_TT>, sizeof(TcSmemL<TCL_TT>) + 1024);
-  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_LN>, 8 * 4096 * 4);
-  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_QUANT>, 8 * 4096 * 4);
+  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_LN>, 4096 * 4);
+  attr((const void *)tcl_quant_pack_kernel<TCL_TT, PRO_QUANT>, 4096 * 4);
   if (e != cudaSuccess) {
     int optin = 0;
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device);

@@ -103,65 +103,79 @@ __global__ void tcl_prep_a_kernel(WeightView w, int mode, uint8_t *a) {
 // h, the low byte xl (p = 0) or the high byte xh (p = 1) of x at column
 // tcl_col(k), and zero in the other half. Also sx[m] and, for the int8 rows,
 // the 16 lane sums of x (columns 2L, 2L + 1 of every 32-column chunk). One
-// warp per sequence of the padded count (8 per CTA, the row staged in shared
-// memory), no block-wide waits; padding sequences get zero tiles.
+// CTA of 256 threads per sequence of the padded count, the row staged in
+// shared memory: warp 0 takes the LayerNorm sums (16 lane sums, each
+// sequential over the row's 16-float chunks, then the halving tree), every
+// thread a share of the columns for the max of |x| (exact in any order), the
+// integer lane sums and the packing; padding sequences get zero tiles.
 template <int TT, int PRO>
 __global__ void __launch_bounds__(256) tcl_quant_pack_kernel(const float *x, const float *ln_w, const float *ln_b,
                                                              int B, int bpad, int K, int mode, uint8_t *b, float *sx,
                                                              int *xsl) {
-  extern __shared__ __align__(16) float qsm[];  // [8][K]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * 8 + warp;
-  if (m >= bpad) return;
-  float *xf = qsm + (size_t)warp * K;
+  extern __shared__ __align__(16) float xf[];  // [K]
+  __shared__ float red[8], stat[2];
+  __shared__ int lsum[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int m = blockIdx.x;
   const bool valid = m < B;
   const int nkb = K / TC_KB, r = m % TT;
   uint8_t *tile = b + (size_t)(m / TT) * nkb * (4 * TT * TC_KB);
+  if (tid < 16) lsum[tid] = 0;
   float inv = 0.0f;
   if (valid) {
     const float *row = x + (size_t)m * K;
-    for (int i = lane * 4; i < K; i += 128) *(float4 *)(xf + i) = *(const float4 *)(row + i);
-    __syncwarp();
+    for (int i = tid * 4; i < K; i += 1024) *(float4 *)(xf + i) = *(const float4 *)(row + i);
+    __syncthreads();
     if (PRO == PRO_LN) {
-      // 16 lane sums, each sequential over the row's 16-float chunks, the
-      // halving tree (every lane ends with the same mean and variance)
-      const int l = lane & 15;
-      float s = 0.0f;
-      for (int i = 0; i < K; i += 16) s = s + xf[i + l];
-      const float mean = tree16_warp(s) / (float)K;
-      float sq = 0.0f;
-      for (int i = 0; i < K; i += 16) {
-        const float d = xf[i + l] - mean;
-        sq = sq + d * d;
+      if (warp == 0) {
+        const int l = lane & 15;
+        float s = 0.0f;
+        for (int i = 0; i < K; i += 16) s = s + xf[i + l];
+        const float mean = tree16_warp(s) / (float)K;
+        float sq = 0.0f;
+        for (int i = 0; i < K; i += 16) {
+          const float d = xf[i + l] - mean;
+          sq = sq + d * d;
+        }
+        const float var = tree16_warp(sq) / (float)K;
+        if (lane == 0) {
+          stat[0] = mean;
+          stat[1] = 1.0f / sqrtf(var + 1e-5f);
+        }
       }
-      const float var = tree16_warp(sq) / (float)K;
-      const float rstd = 1.0f / sqrtf(var + 1e-5f);
-      __syncwarp();
-      for (int i = lane; i < K; i += 32) {
+      __syncthreads();
+      const float mean = stat[0], rstd = stat[1];
+      for (int i = tid; i < K; i += 256) {
         const float n = (xf[i] - mean) * rstd;
         xf[i] = n * ln_w[i] + ln_b[i];
       }
-      __syncwarp();
+      __syncthreads();
     }
     float mx = 0.0f;
-    for (int i = lane; i < K; i += 32) mx = fmaxf(mx, fabsf(xf[i]));
+    for (int i = tid; i < K; i += 256) mx = fmaxf(mx, fabsf(xf[i]));
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < 8; w++) mx = fmaxf(mx, red[w]);
     float s = mx / 32767.0f;
     if (s == 0.0f) s = 1.0f;
     inv = 1.0f / s;
-    if (lane == 0) sx[m] = s;
+    if (tid == 0) sx[m] = s;
     if (mode == TCL_CH8) {
-      // lane L's sum over the 32-column chunks, chunks split by parity
-      const int L = lane & 15;
+      // lane L's sum over the 32-column chunks: thread tid takes lane tid % 16
+      // of chunks tid / 16, tid / 16 + 16, ...
+      const int L = tid & 15;
       int acc = 0;
-      for (int c = lane >> 4; c < K / 32; c += 2)
+      for (int c = tid >> 4; c < K / 32; c += 16)
         acc += (int)roundf(xf[c * 32 + 2 * L] * inv) + (int)roundf(xf[c * 32 + 2 * L + 1] * inv);
-      acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-      if (lane < 16) xsl[(size_t)m * 16 + lane] = acc;
+      atomicAdd(&lsum[L], acc);
     }
   }
+  __syncthreads();
+  if (mode == TCL_CH8 && tid < 16) xsl[(size_t)m * 16 + tid] = valid ? lsum[tid] : 0;
   const uint4 zero = make_uint4(0, 0, 0, 0);
-  for (int ci = lane; ci < K / 16; ci += 32) {
+  for (int ci = tid; ci < K / 16; ci += 256) {
     const int k0 = ci * 16, kb = k0 / TC_KB, chunk = (k0 % TC_KB) / 16, half = (k0 >> 4) & 1;
     uint32_t lo[4] = {0, 0, 0, 0}, hi[4] = {0, 0, 0, 0};
     if (valid) {
