@@ -1120,7 +1120,7 @@ llmq_status llmq_head_argmax_noalloc(llmq_ctx *ctx, const llmq_weight *w, const 
 llmq_status llmq_layernorm(llmq_ctx *ctx, float *out, const float *x, const float *w, const float *b, int T, int C) {
   if (!ctx || !out || !x || !w || !b || T <= 0 || C <= 0 || C % 16) return fail(ctx, LLMQ_ERR_INVALID, "bad argument");
   CK(cudaSetDevice(ctx->device));
-  layernorm_kernel<<<T, 256, C * 4, ctx->stream>>>(out, x, w, b, C);
+  launch_layernorm(out, x, w, b, T, C, ctx->stream);
   CKL();
   return LLMQ_OK;
 }
@@ -1781,13 +1781,13 @@ llmq_status enqueue_blocks(llmq_model *m, int T, int pos0, cudaStream_t s) {
   llmq_status st;
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
-    layernorm_kernel<<<T, 256, C * 4, s>>>(m->xn, m->x, m->vec(l, 0), m->vec(l, 1), C);
+    launch_layernorm(m->xn, m->x, m->vec(l, 0), m->vec(l, 1), T, C, s);
     CKL();
     if ((st = llmq_linear(ctx, w[0], m->xn, m->vec(l, 2), m->qkv, T, C, 3 * C, LLMQ_BIAS)) != LLMQ_OK) return st;
     if ((st = llmq_kv_store(ctx, m->kv, l, pos0, T, m->qkv)) != LLMQ_OK) return st;
     if ((st = llmq_kv_attend(ctx, m->kv, m->att, m->qkv, l, T, pos0)) != LLMQ_OK) return st;
     if ((st = llmq_linear(ctx, w[1], m->att, m->vec(l, 3), m->x, T, C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK) return st;
-    layernorm_kernel<<<T, 256, C * 4, s>>>(m->xn, m->x, m->vec(l, 4), m->vec(l, 5), C);
+    launch_layernorm(m->xn, m->x, m->vec(l, 4), m->vec(l, 5), T, C, s);
     CKL();
     if ((st = llmq_linear(ctx, w[2], m->xn, m->vec(l, 6), m->fc, T, C, 4 * C, LLMQ_BIAS | LLMQ_GELU)) != LLMQ_OK) return st;
     if ((st = llmq_linear(ctx, w[3], m->fc, m->vec(l, 7), m->x, T, 4 * C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK) return st;
@@ -2161,7 +2161,7 @@ llmq_status llmq_model_forward_all(llmq_ctx *ctx, llmq_model *m, const int *toke
   CK(cudaMemcpyAsync(m->tokens, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, s));
   llmq_status st = enqueue_blocks(m, T, 0, s);
   if (st == LLMQ_OK) {
-    layernorm_kernel<<<T, 256, m->C * 4, s>>>(m->xn, m->x, m->lnf_w(), m->lnf_b(), m->C);
+    launch_layernorm(m->xn, m->x, m->lnf_w(), m->lnf_b(), T, m->C, s);
     st = llmq_head(ctx, m->head, m->xn, logits_dev, T, m->C, m->V);
   }
   if (st != LLMQ_OK) return st;
@@ -2549,7 +2549,7 @@ llmq_status batch_prompt(llmq_batch *bt, int B, int P, cudaStream_t s) {
   llmq_status st;
   for (int l = 0; l < m->n_layer; l++) {
     const llmq_weight *const *w = &m->mats[4 * l];
-    layernorm_kernel<<<T, 256, C * 4, s>>>(bt->xn, bt->x, m->vec(l, 0), m->vec(l, 1), C);
+    launch_layernorm(bt->xn, bt->x, m->vec(l, 0), m->vec(l, 1), T, C, s);
     CKL();
     if ((st = llmq_linear(ctx, w[0], bt->xn, m->vec(l, 2), bt->qkv, T, C, 3 * C, LLMQ_BIAS)) != LLMQ_OK) return st;
     kv8_store_kernel<<<(m->n_head * P * 2 * B + 7) / 8, 256, 0, s>>>(bt->kv, bt->qkv, l, 0, nullptr, P, B);
@@ -2559,7 +2559,7 @@ llmq_status batch_prompt(llmq_batch *bt, int B, int P, cudaStream_t s) {
     CKL();
     if ((st = llmq_linear(ctx, w[1], bt->att, m->vec(l, 3), bt->x, T, C, C, LLMQ_BIAS | LLMQ_RESID)) != LLMQ_OK)
       return st;
-    layernorm_kernel<<<T, 256, C * 4, s>>>(bt->xn, bt->x, m->vec(l, 4), m->vec(l, 5), C);
+    launch_layernorm(bt->xn, bt->x, m->vec(l, 4), m->vec(l, 5), T, C, s);
     CKL();
     if ((st = llmq_linear(ctx, w[2], bt->xn, m->vec(l, 6), bt->fc, T, C, 4 * C, LLMQ_BIAS | LLMQ_GELU)) != LLMQ_OK)
       return st;

@@ -38,6 +38,61 @@ __global__ void layernorm_kernel(float *out, const float *x, const float *w, con
   for (int i = threadIdx.x; i < C; i += blockDim.x) out[(size_t)blockIdx.x * C + i] = xf[i];
 }
 
+// layernorm_kernel's arithmetic with one warp per row (8 rows per CTA of 256
+// threads), for C % 32 == 0 and C <= 1024: lane L holds columns L + 32 j in
+// registers; lane sum l adds columns l + 16 i for i = 0, 1, ... in turn,
+// i.e. the registers j of lanes l and l + 16 alternately, read through two
+// shuffles per step, so the sums, the tree and every result equal
+// ln_inplace's. out may alias x.
+__global__ void __launch_bounds__(256) layernorm_rows_kernel(float *out, const float *x, const float *w,
+                                                             const float *b, int T, int C) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31, l = lane & 15;
+  if (row >= T) return;
+  const int n = C >> 5;
+  const float *xr = x + (size_t)row * C;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) v[j] = j < n ? xr[lane + 32 * j] : 0.0f;
+  float a = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j < n) {
+      const float u0 = __shfl_sync(0xffffffffu, v[j], l), u1 = __shfl_sync(0xffffffffu, v[j], l + 16);
+      a = a + u0;
+      a = a + u1;
+    }
+  const float mean = tree16_warp(a) / (float)C;
+  float sq = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j < n) {
+      const float d0 = __shfl_sync(0xffffffffu, v[j], l) - mean, d1 = __shfl_sync(0xffffffffu, v[j], l + 16) - mean;
+      sq = sq + d0 * d0;
+      sq = sq + d1 * d1;
+    }
+  const float rstd = 1.0f / sqrtf(tree16_warp(sq) / (float)C + 1e-5f);
+  float *orow = out + (size_t)row * C;
+#pragma unroll
+  for (int j = 0; j < 32; j++)
+    if (j < n) {
+      const int c = lane + 32 * j;
+      const float t = (v[j] - mean) * rstd;
+      orow[c] = t * w[c] + b[c];
+    }
+}
+
+// LayerNorm of T rows of C: one warp per row where the row fits in registers
+// and there are enough rows to fill the GPU many times over (for a prompt of
+// a few hundred tokens the CTA per row is faster: measured 2.69 vs 2.46 ms
+// per 476-token config 2 prompt).
+inline void launch_layernorm(float *out, const float *x, const float *w, const float *b, int T, int C,
+                             cudaStream_t s) {
+  if (C % 32 == 0 && C <= 1024 && T >= 4096)
+    layernorm_rows_kernel<<<(T + 7) / 8, 256, 0, s>>>(out, x, w, b, T, C);
+  else
+    layernorm_kernel<<<T, 256, C * 4, s>>>(out, x, w, b, C);
+}
+
 // Tile kernel: 32 tokens x 32 outputs per CTA, 256 threads, each thread 2
 // tokens x 2 outputs. Only output rows below full = OUT / 32 * 32.
 __global__ void __launch_bounds__(256) tile_a16_kernel(WeightView w, const int16_t *xq, const float *sx,
