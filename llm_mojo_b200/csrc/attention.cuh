@@ -311,7 +311,9 @@ template <int KVT>
 __global__ void __launch_bounds__(256) kv_prefill_kernel(KV8View c0, float *out, const float *qkv, int layer, int pos0,
                                                          int T) {
   extern __shared__ __align__(16) float kvp_sm[];
-  const int h = blockIdx.x, t0 = blockIdx.y * KV_QB;
+  // the query blocks that see the most positions first (grid y reversed),
+  // so the longest CTAs start in the first wave
+  const int h = blockIdx.x, t0 = (gridDim.y - 1 - blockIdx.y) * KV_QB;
   const int nq = min(KV_QB, T - t0);
   const KV8View c = c0.of(blockIdx.z);  // grid z: sequences, each with T rows
   const int HS = c.head_dim, C = c.n_head * HS, HP = HS + 4;
