@@ -117,7 +117,8 @@ def cpu_baseline(seconds: float = 20.0, samples: int = 5):
     """The CPU oracle's greedy decode of config 0: `samples` runs (the prompt
     forward, then decode steps up to the 100-token generation or
     seconds / samples), tokens per second over the decode steps each
-    finished; the median of the runs (BASELINE.md's median of 5)."""
+    finished; the median of the runs (five by default, as the reference's
+    published CPU figure is a median of five)."""
     from llm_mojo_b200 import synth
     from oracle import oracle as O
 
