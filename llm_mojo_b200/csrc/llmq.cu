@@ -1688,7 +1688,6 @@ llmq_status mega_check(llmq_model *m) {
 // head + argmax. Token, position and step index come from m->state.
 llmq_status enqueue_decode_step(llmq_model *m, cudaStream_t s) {
   llmq_ctx *ctx = m->ctx;
-  const int C = m->C;
   embed_kernel<<<3, 256, 0, s>>>(m->head->view(), m->wpe(), m->x, m->state);
   CKL();
   for (int l = 0; l < m->n_layer; l++) {
@@ -2495,7 +2494,6 @@ __global__ void batch_advance_kernel(int *state) {
 llmq_status batch_decode_step(llmq_batch *bt, int B, int cap, cudaStream_t s) {
   llmq_model *m = bt->m;
   llmq_ctx *ctx = bt->ctx;
-  const int C = m->C;
   embed_batch_kernel<<<B, 256, 0, s>>>(m->head->view(), m->wpe(), bt->x, bt->tokens, bt->state);
   CKL();
   llmq_status st;
